@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""bench.py — MoE decode throughput at the Kimi-Linear-48B shape on B200.
+
+Workload (extended to a whole decode step's MoE work):
+one step is ONE token through the 26 MoE layers of a Kimi-Linear-48B-shaped
+model (27 layers, layer 0 dense), each layer = router (256 experts, F32) ->
+sigmoid top-8 with renorm and routed scale 2.446 -> 8 routed experts whose
+gate/up/down weights are 3-bit residual VQ (3 x 256-entry codebooks over
+8-dim vectors) -> router-order reduce -> + one Q8G shared expert. hidden
+2304, expert intermediate 1024. All 26 layers' 256 experts are resident in
+HBM (26 x 683 MB); inputs are seeded synthetic activations (bf16-valued
+N(0,1)). A step touches ~803 MB, far more than the 126 MB L2, so no L2 flush
+is needed between steps.
+
+Also measured: the config-1 VQ3R matvec (4096 x 4096) as a batched launch
+over 32 distinct matrices (203 MB of indices), in HBM GB/s.
+
+`--impl reference` times the reference engine's own moe_layer (compiled
+from the reference sources into oracle/_ref) on this host's cores, same
+metric and config.
+
+Multi-GPU (torchrun): replicas — each rank decodes its own token stream
+against its own resident copy of the experts (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE decode tok/s (26 VQ3R MoE layers, Kimi-Linear-48B shape, batch 1)"
+UNIT = "tok/s"
+HIDDEN, INTER, EXPERTS, TOPK, SHARED = 2304, 1024, 256, 8, 1024
+MOE_LAYERS = 26
+SEED = 1234
+
+
+def layer_bytes():
+    """Algorithmic bytes one token reads in one layer."""
+    from warp_b200 import synth
+    idx = 2 * synth.index_bytes(INTER, HIDDEN, 3) + synth.index_bytes(HIDDEN, INTER, 3)
+    scales = 2 * (2 * INTER + HIDDEN)
+    routed = TOPK * (idx + scales)
+    ng_h, ng_s = (HIDDEN + 127) // 128, (SHARED + 127) // 128
+    shared = 2 * SHARED * ng_h * 128 + HIDDEN * ng_s * 128 + 2 * (2 * SHARED * ng_h + HIDDEN * ng_s)
+    router = EXPERTS * HIDDEN * 4
+    books = 9 * 256 * 8 * 4
+    return routed + shared + router + books + 2 * HIDDEN * 4
+
+
+def gateup_bytes():
+    """Algorithmic bytes of one gate/up launch (K experts, one token)."""
+    from warp_b200 import synth
+    return 2 * TOPK * synth.index_bytes(INTER, HIDDEN, 3) + HIDDEN * 4 + 2 * 3 * 256 * 8 * 4
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (200 ms period)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+# ---------------------------------------------------------------- reference
+
+def run_reference(args):
+    import oracle as O
+    from warp_b200 import synth
+    rank, world, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return 0
+    ncores = os.cpu_count() or 1
+    base = synth.moe_layer(SEED)
+    xs = synth.activations(SEED + 1, HIDDEN, T=64)
+    if O.ref_available():
+        layers = [O.RefMoe(base, max_tokens=1, threads=0),
+                  O.RefMoe(synth.derive_layer(base, 2, SEED + 2), max_tokens=1, threads=0)]
+        kind, cores = "reference", O.ref().refh_pool_threads()
+        backend = layers[0].backend.decode()
+        step_layer = lambda L, x: layers[L % 2].layer(x)
+    else:
+        ders = [base, synth.derive_layer(base, 2, SEED + 2)]
+        kind, cores, backend = "port", 1, "restatement"
+        step_layer = lambda L, x: O.moe_layer(ders[L % 2], x)
+
+    def step(k):
+        for L in range(MOE_LAYERS):
+            step_layer(L, xs[(k * MOE_LAYERS + L) % 64])
+
+    for k in range(args.warmup):
+        step(k)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        step(args.warmup + k)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    sample = (f"{args.steps} tokens x {MOE_LAYERS} layers through the reference moe_layer "
+              f"({backend}, {cores} threads); banks alternate between 2 resident layers "
+              f"(683 MB each, larger than the host caches)")
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "kimi_linear_48b_moe_decode", "hidden": HIDDEN,
+                       "moe_inter": INTER, "experts": EXPERTS, "top_k": TOPK,
+                       "moe_layers": MOE_LAYERS, "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    for L in (layers if kind == "reference" else []):
+        L.close()
+    return 0
+
+
+def cpu_baseline(budget_s=10.0):
+    """The reference CPU path on this host, bounded sample (rank 0, N=1)."""
+    import oracle as O
+    from warp_b200 import synth
+    base = synth.moe_layer(SEED)
+    xs = synth.activations(SEED + 1, HIDDEN, T=16)
+    if O.ref_available():
+        rm = O.RefMoe(base, max_tokens=1, threads=0)
+        run, kind, cores = rm.layer, "reference", O.ref().refh_pool_threads()
+    else:
+        rm, kind, cores = None, "port", 1
+        run = lambda x: O.moe_layer(base, x)
+    run(xs[0])
+    t0 = time.perf_counter()
+    run(xs[1])
+    per = max(time.perf_counter() - t0, 1e-4)
+    n = max(2, min(400, int(budget_s / per)))
+    t0 = time.perf_counter()
+    for i in range(n):
+        run(xs[i % 16])
+    dt = (time.perf_counter() - t0) / n
+    if rm is not None:
+        rm.close()
+    return {"value": 1.0 / (dt * MOE_LAYERS), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} single-token MoE layer calls ({dt * 1e3:.2f} ms each) at the "
+                      f"Kimi-Linear shape, scaled to {MOE_LAYERS} layers per token"}
+
+
+# ---------------------------------------------------------------- this repo
+
+def run_warp(args):
+    import torch
+    import warp_b200 as wb
+    from warp_b200 import synth
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    wb.init(local)
+    dev = torch.device("cuda", local)
+
+    # ---- resident layers
+    base = synth.moe_layer(SEED)
+    nL = args.layers
+    for L in range(1, nL + 1):
+        lay = base if L == 1 else synth.derive_layer(base, L, SEED + L)
+        wb.vq_bank_free(L)
+        if L == 1:
+            wb.codebooks_load_f16(base.books_raw)
+        wb.vq_bank_load(L, lay.n_experts, lay.rec_bytes, 0, lay.n_experts, lay.bank,
+                        lay.inter, lay.hidden, lay.stages)
+        wb.moe_trunk_load(L, lay.n_experts, lay.hidden, lay.top_k, lay.renorm,
+                          lay.routed_scale, lay.router, lay.bias, lay.shared_inter, lay.sh)
+        del lay
+    ntok = 4
+    xs_h = synth.activations(SEED + 100 + rank, HIDDEN, T=ntok * nL).reshape(ntok, nL, HIDDEN)
+    xs = torch.from_numpy(xs_h).to(dev)
+    out = torch.empty((nL, HIDDEN), dtype=torch.float32, device=dev)
+    idx = torch.empty((nL, TOPK), dtype=torch.int32, device=dev)
+    w = torch.empty((nL, TOPK), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(device=dev)
+
+    def step_direct(t):
+        for L in range(nL):
+            wb.moe_layer_dev(L + 1, xs[t, L].data_ptr(), out[L].data_ptr(), idx[L].data_ptr(),
+                             w[L].data_ptr(), s.cuda_stream)
+
+    with torch.cuda.stream(s):
+        for k in range(max(args.warmup, 1)):
+            step_direct(k % ntok)
+    torch.cuda.synchronize()
+
+    # ---- one CUDA graph per token slot
+    graphs = []
+    launches_per_step = None
+    try:
+        for t in range(ntok):
+            g = torch.cuda.CUDAGraph()
+            c0 = wb.launch_count()
+            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                step_direct(t)
+            launches_per_step = wb.launch_count() - c0
+            graphs.append(g)
+        use_graphs = True
+    except Exception as e:  # direct launches still measure the same kernels
+        print(f"graph capture unavailable: {e}", file=sys.stderr)
+        graphs, use_graphs = [], False
+        launches_per_step = 5 * nL
+
+    def step(k):
+        if use_graphs:
+            graphs[k % ntok].replay()
+        else:
+            step_direct(k % ntok)
+
+    clocks = Clocks(local)
+    clocks.start()
+    with torch.cuda.stream(s):
+        for k in range(args.warmup):
+            step(k)
+        t_settle = time.perf_counter()
+        k = 0
+        while time.perf_counter() - t_settle < 0.5:      # let clocks settle
+            step(k)
+            k += 1
+            if k % 64 == 0:
+                s.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for k in range(args.steps):
+            step(k)
+    e1.record(s)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ck = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- end to end through the host-buffer entry point (H2D x, D2H out)
+    x_host = [[np.ascontiguousarray(xs_h[t, L]) for L in range(nL)] for t in range(ntok)]
+    for L in range(nL):
+        wb.moe_layer(L + 1, x_host[0][L], TOPK, HIDDEN)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        for L in range(nL):
+            wb.moe_layer(L + 1, x_host[k % ntok][L], TOPK, HIDDEN)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * args.steps / e2e_s, "unit": UNIT,
+           "h2d_bytes_per_step": nL * HIDDEN * 4,
+           "d2h_bytes_per_step": nL * (HIDDEN * 4 + 2 * TOPK * 4)}
+
+    # ---- per-kernel times (phase timers) over K direct steps
+    wb.profile(True)
+    with torch.cuda.stream(s):
+        for k in range(args.steps):
+            step_direct(k % ntok)
+    torch.cuda.synchronize()
+    ph = wb.profile_read()
+    wb.profile(False)
+    gu_ms, gu_n = ph["gateup"]
+    gu_avg = gu_ms / max(gu_n, 1)
+    peak, peak_src = peaks()
+    achieved = gateup_bytes() / (gu_avg / 1e3) / 1e9
+    tot = sum(v[0] for v in ph.values())
+    kernels = {k: {"avg_us": (v[0] / max(v[1], 1)) * 1e3, "launches": v[1],
+                   "share": v[0] / tot if tot else None} for k, v in ph.items() if v[1]}
+
+    # ---- config 1: VQ3R matvec 4096 x 4096, 32 distinct matrices per launch
+    G, M, N = 32, 4096, 4096
+    rng = np.random.default_rng(SEED + 7)
+    raw = synth.codebooks(rng, 3)
+    wb.codebooks_load_f16(raw)
+    mats = [synth.random_matrix(rng, M, N) for _ in range(G)]
+    d_idx = torch.from_numpy(np.stack([m[0] for m in mats])).to(dev)
+    d_sc = torch.from_numpy(np.stack([m[1].view(np.int16) for m in mats])).to(dev)
+    d_x = torch.from_numpy(synth.activations(SEED + 8, N, T=G)).to(dev)
+    d_y = torch.empty((G, M), dtype=torch.float32, device=dev)
+    ptrs = ([d_idx[g].data_ptr() for g in range(G)], [d_sc[g].data_ptr() for g in range(G)],
+            [d_x[g].data_ptr() for g in range(G)], [d_y[g].data_ptr() for g in range(G)])
+    mv_iters = max(args.steps, 10)
+    for _ in range(3):
+        wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
+    torch.cuda.synchronize()
+    wb.profile(True)
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0.record(s)
+    for _ in range(mv_iters):
+        wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
+    m1.record(s)
+    torch.cuda.synchronize()
+    mph = wb.profile_read()
+    wb.profile(False)
+    mv_ms = m0.elapsed_time(m1) / mv_iters
+    mv_bytes = G * (synth.index_bytes(M, N, 3) + 2 * M + 4 * N + 4 * M) + 3 * 256 * 8 * 4
+    mv_tiles_avg = mph["matvec"][0] / max(mph["matvec"][1], 1)
+    matvec = {"workload": "vq3r_matvec_4096x4096_x32", "GBps": mv_bytes / (mv_ms / 1e3) / 1e9,
+              "frac": mv_bytes / (mv_ms / 1e3) / 1e9 / peak, "ms_per_launch": mv_ms,
+              "gather_kernel_GBps": G * synth.index_bytes(M, N, 3) / (mv_tiles_avg / 1e3) / 1e9,
+              "bytes_per_launch": mv_bytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; bf16-valued N(0,1) activations, N(0,0.02^2) codebooks, "
+                    "uniform indices, random-init router/shared expert)",
+            "config": {"workload": "kimi_linear_48b_moe_decode", "hidden": HIDDEN,
+                       "moe_inter": INTER, "experts": EXPERTS, "top_k": TOPK,
+                       "shared_experts": 1, "moe_layers": nL, "global_batch": world,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (~803 MB touched per step)",
+                       "cuda_graphs": use_graphs},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": ck,
+            "e2e": e2e,
+            "roofline": {"bound": "hbm", "kernel": "gateup_kernel",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_src,
+                         "traffic": None,
+                         "bytes_per_launch": gateup_bytes(), "avg_launch_us": gu_avg * 1e3,
+                         "layer_GBps": layer_bytes() / (ms_step / nL / 1e3) / 1e9,
+                         "layer_frac": layer_bytes() / (ms_step / nL / 1e3) / 1e9 / peak},
+            "kernels": kernels,
+            "matvec": matvec,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        del graphs
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("warp", "reference"), default="warp")
+    ap.add_argument("--layers", type=int, default=MOE_LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_warp(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

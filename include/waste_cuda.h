@@ -1,0 +1,217 @@
+/*
+ * waste_cuda.h — C ABI of the B200 (sm_100a) backend for WARP's routed-expert
+ * FFN: 3-bit residual-VQ ("VQ3R") expert weights held resident in HBM, the
+ * fused LUT matvec, and the MoE expert loop, behind the reference engine's
+ * backend plugin interface (sqliteai/warp src/waste_backend.h).
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, returns
+ * an int status (0 = done; negative = the caller falls back or reports, as
+ * the reference's slot contract asks) and never allocates on the caller's
+ * behalf. Host-pointer entry points are synchronous: inputs are read and
+ * outputs written before they return. `_dev` entry points take device
+ * pointers and a cudaStream_t (as void*), and are ordered on that stream.
+ *
+ * Reference interfaces replaced (paths in the sqliteai/warp tree):
+ *   waste_register_cuda          src/backend.c:57-59 (decl), :202-204 (call)
+ *   waste_cuda_vq_bank_load      the expert cache: src/ecache.c:596
+ *                                waste_ecache_get + src/model.c:1767 bank_fetch
+ *   waste_cuda_codebooks_load*   src/model.c:1269-1304 codebook decode/transpose
+ *   waste_cuda_lutb              src/model.c:1911-1923 vq_build_lut
+ *                                (slot lutb_range, src/waste_backend.h:82)
+ *   waste_cuda_vq_matvec(_dev)   src/model.c:2282-2289 vq_matvec
+ *   waste_cuda_vq_dequant        tools/verify_container.py:73-84 (dequantised W)
+ *   waste_cuda_moe_experts       src/model.c:2873-2911 moe_layer's expert loop
+ *   waste_cuda_moe_chunk_experts src/model.c:3585-3659 moe_chunk's expert loop
+ *   waste_cuda_moe_layer(_dev)   src/model.c:2713-2939 moe_layer (router,
+ *                                experts, shared expert) for a device-resident
+ *                                hidden state
+ */
+#ifndef WASTE_CUDA_H
+#define WASTE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define WASTE_CUDA_OK          0
+#define WASTE_CUDA_E_ARG      -1  /* shape or argument outside what is supported */
+#define WASTE_CUDA_E_DEVICE   -2  /* a CUDA call failed; see waste_cuda_last_error */
+#define WASTE_CUDA_E_RECORD   -3  /* an expert record header failed its check      */
+#define WASTE_CUDA_E_NOBANK   -4  /* the layer's bank (or trunk) is not loaded     */
+#define WASTE_CUDA_E_NOMEM    -5  /* device memory exhausted                       */
+#define WASTE_CUDA_E_NODEV    -6  /* no usable sm_100 device                       */
+
+/* ---- plugin registration ----------------------------------------------
+ * Replaces the missing src/cuda.cu that src/backend.c:57-59 declares and
+ * src/backend.c:202-204 calls, once, under g_init_mu. Probes for an sm_100
+ * device (WASTE_CUDA=0 declines; WASTE_CUDA_DEVICE picks one) and returns
+ * the backend name, or NULL to decline so the previous backend stays
+ * (src/waste_backend.h:116-120). It writes no slot of the reference's
+ * waste_kernels table — the expert path has no slot there — so the table
+ * pointer is taken as void* and left untouched. */
+const char *waste_register_cuda(void *waste_kernels_table);
+
+/* The expert-path slots the integration patch adds next to waste_kernels
+ * (INTEGRATION.md). Filled by waste_register_cuda_vq; a NULL slot means the
+ * engine keeps its CPU loop. */
+typedef struct waste_moe_call waste_moe_call;
+typedef struct waste_moe_chunk_call waste_moe_chunk_call;
+typedef struct {
+    int  (*codebooks_load)(const float *books, int n_books, int entries, int vec_dim);
+    int  (*vq_bank_load)(int layer, int n_experts, size_t rec_bytes, int first,
+                         int count, const void *records, int inter, int lat,
+                         int stages);
+    void (*vq_bank_free)(int layer);
+    int  (*moe_experts)(const waste_moe_call *c);
+    int  (*moe_chunk_experts)(const waste_moe_chunk_call *c);
+} waste_vq_slots;
+
+/* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */
+int waste_register_cuda_vq(waste_vq_slots *s);
+
+/* ---- device and lifetime ------------------------------------------------ */
+/* Binds the calling process to `device` (-1: WASTE_CUDA_DEVICE or 0) and
+ * allocates the workspace. Idempotent for the same device. */
+int         waste_cuda_init(int device);
+void        waste_cuda_shutdown(void);
+int         waste_cuda_device(void);
+const char *waste_cuda_last_error(void);
+/* "CUDA sm_100a (<device name>)" once initialised, else NULL. */
+const char *waste_cuda_backend_name(void);
+
+/* ---- codebooks ---------------------------------------------------------
+ * books: [n_books][entries][vec_dim] fp32, as the engine holds them after
+ * load (m->codebooks, src/model.c:1275-1288 — subnormals already flushed).
+ * The _f16 form takes the raw codebooks.bin entries and decodes them the
+ * way the engine's loader does (src/model.c:1278-1287: f16 -> f32 with
+ * subnormals flushed to signed zero). Only entries == 256, vec_dim == 8. */
+int waste_cuda_codebooks_load(const float *books, int n_books, int entries,
+                              int vec_dim);
+int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries,
+                                  int vec_dim);
+
+/* ---- expert banks resident in HBM ---------------------------------------
+ * Uploads records [first, first+count) of layer `layer`'s bank (records are
+ * the on-disk waste_expert_hdr + payload, src/waste_format.h:98-132, each
+ * rec_bytes long). Every header is checked the way src/model.c:1698-1745
+ * record_check does (magic, identity, size, fmt, lowrank, codebook range,
+ * offset order, room for the scales) before anything is copied. The first
+ * call for a layer sizes its bank for n_experts records; the shapes are
+ * gate/up [inter][lat] and down [lat][inter]. With expert parallelism a
+ * rank loads only the records it owns (waste_cuda_ep_*). */
+int  waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes,
+                             int first, int count, const void *records,
+                             int inter, int lat, int stages);
+void waste_cuda_vq_bank_free(int layer);
+
+/* Trunk tensors of one MoE layer for the device-resident layer path:
+ * router [n_experts][hidden] fp32 (F32 per docs/FORMAT.md), its score
+ * correction bias (NULL = none), the routing constants, and the shared
+ * expert as Q8G rows (group 128, rows padded to whole groups, one f16 scale
+ * per group; src/model.c:265-320 layout). sh_inter 0 = no shared expert. */
+int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
+                              int renorm, float routed_scale,
+                              const float *router, const float *bias,
+                              int sh_inter, const int8_t *sh_gate,
+                              const uint16_t *sh_gate_s, const int8_t *sh_up,
+                              const uint16_t *sh_up_s, const int8_t *sh_down,
+                              const uint16_t *sh_down_s);
+
+/* ---- the expert loop (decode) ------------------------------------------
+ * What moe_layer's serial loop computes (src/model.c:2873-2911) for one
+ * token: gate/up tables built once from x, then per routed expert j in
+ * router order gate, up, SiLU(g)*u, down, and ysum = sum_j w[j]*acc_j
+ * accumulated in j order. idx/w/x/ysum are host pointers owned by the
+ * caller (m->... in the engine). act 0 = SiLU; SiTU (K3) returns
+ * WASTE_CUDA_E_ARG so the engine keeps its CPU loop. */
+struct waste_moe_call {
+    int layer, K;
+    const int *idx;
+    const float *w;
+    const float *x;      /* [lat]  */
+    float *ysum;         /* [lat]  */
+    int lat, inter;
+    int act;
+    float situ_beta, situ_linear_beta;
+};
+int waste_cuda_moe_experts(const waste_moe_call *c);
+
+/* ---- the expert loop (prefill chunk) ------------------------------------
+ * moe_chunk's loop (src/model.c:3585-3659): nT tokens, route/rw [nT][K]
+ * (router order per token), x and ysum [nT][lat]. Per token the expert
+ * contributions are added in ascending expert id, as the reference does. */
+struct waste_moe_chunk_call {
+    int layer, nT, K;
+    const int *route;
+    const float *rw;
+    const float *x;      /* [nT][lat] */
+    float *ysum;         /* [nT][lat] */
+    int lat, inter;
+    int act;
+    float situ_beta, situ_linear_beta;
+};
+int waste_cuda_moe_chunk_experts(const waste_moe_chunk_call *c);
+
+/* ---- the whole MoE layer -------------------------------------------------
+ * moe_layer (src/model.c:2713-2939) for a Kimi-Linear-shaped layer: router
+ * matvec, sigmoid + bias top-K (strict >, lowest index wins ties), renorm
+ * (+1e-20) and routed scale, the routed experts, and the shared expert.
+ * Host form: x/out [hidden] and optional routed idx / weights [K] are host
+ * pointers. _dev form: device pointers, ordered on `stream`, nothing copied. */
+int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed,
+                         float *weights);
+int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
+                             int *d_idx, float *d_w, void *stream);
+
+/* ---- single VQ3R kernels ---------------------------------------------------
+ * lutb: lut[nv][stages][entries] = sum_d x[8v+d] * C_{cb_base+s}[c][d], an
+ * FMA chain from 0 in d order — bit-identical to the reference's AVX2 and
+ * AVX-512 lutb_range (src/simd_avx2.c:100-133, src/simd_avx512.c:90-123).
+ * vq_matvec: y[M] = f16(scale[r]) * sum_v (L0[i0]+L1[i1]+L2[i2]) over the
+ * blocked index layout [M/64][N/8][64][stages] (src/model.c:1956-2024).
+ * vq_dequant: W[M][N] = (((0 + C0[i0]) + C1[i1]) + C2[i2]) * f16(scale[r]). */
+int waste_cuda_lutb(float *lut, const float *x, int cb_base, int nv, int stages);
+int waste_cuda_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
+                         const float *x, int M, int N, int cb_base, int stages);
+int waste_cuda_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale,
+                          int M, int N, int cb_base, int stages);
+
+/* Batched independent matvecs on device pointers: for g < G,
+ * y[g][M] = VQ(idx[g], scale[g]) . x[g][N]. idx/scale/x/y are arrays of G
+ * device pointers held in HOST memory. One launch for all G. */
+int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
+                             const uint16_t *const *scale,
+                             const float *const *x, float *const *y, int M,
+                             int N, int cb_base, int stages, void *stream);
+
+/* Kernels this library launched since load (a running count, for
+ * benchmarks that report how many of their launches were this library's). */
+uint64_t waste_cuda_launch_count(void);
+
+/* Phase timers: the device counterpart of the reference's WASTE_PROFILE
+ * buckets (src/model.c:37-52, printed by tests/test_forward.c:118-134).
+ * While on, each kernel is bracketed by CUDA events on its stream;
+ * waste_cuda_profile_read waits for them, writes the summed milliseconds
+ * and launch counts of up to nphase phases (order below), and resets. Not
+ * for use while a stream is being captured into a CUDA graph. */
+enum {
+    WASTE_CUDA_PH_ROUTER = 0,   /* router logits + shared gate/up       */
+    WASTE_CUDA_PH_ROUTE,        /* top-K selection                      */
+    WASTE_CUDA_PH_GATEUP,       /* routed gate/up gathers               */
+    WASTE_CUDA_PH_DOWN,         /* SiLU(g)*u, down gathers, shared down */
+    WASTE_CUDA_PH_COMBINE,      /* router-order reduce (+ shared)       */
+    WASTE_CUDA_PH_MATVEC,       /* batched matvec gathers               */
+    WASTE_CUDA_PH_MATVEC_REDUCE,
+    WASTE_CUDA_PH_COUNT
+};
+int waste_cuda_profile(int on);
+int waste_cuda_profile_read(double *ms, uint64_t *launches, int nphase);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WASTE_CUDA_H */

@@ -1,0 +1,293 @@
+"""ctypes bindings for the parity checker. TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by oracle/Makefile:
+
+* ``_build/liboracle.so`` — the CPU restatement (vq3r_oracle.c), built from
+  this repository's sources; it exists on every machine the tests run on.
+* ``_ref/libwaste_ref.so`` — the reference engine compiled from its own
+  sources plus ref_harness.c; built only where the reference tree is
+  present, and carried to GPU machines with the working copy.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+module; the product (warp_b200, libwaste_cuda.so) never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libwaste_ref.so")
+REF_TREE = os.environ.get("WARP_REFERENCE", "/root/reference")
+
+P = C.c_void_p
+
+
+def build(ref: bool | None = None):
+    """make -C oracle (and `ref` when the reference tree is present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if ref is None:
+        ref = os.path.isdir(os.path.join(REF_TREE, "src"))
+    if ref:
+        subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
+
+
+class OrcMoe(C.Structure):
+    """orc_moe (vq3r_oracle.h)."""
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_experts", C.c_int),
+                ("top_k", C.c_int), ("renorm", C.c_int), ("routed_scale", C.c_float),
+                ("stages", C.c_int), ("entries", C.c_int), ("vec_dim", C.c_int),
+                ("index_block", C.c_int), ("router", P), ("bias", P), ("books", P),
+                ("n_books", C.c_int), ("bank", P), ("rec_bytes", C.c_size_t),
+                ("shared_inter", C.c_int), ("sh_gate", P), ("sh_up", P), ("sh_down", P),
+                ("sh_gate_s", P), ("sh_up_s", P), ("sh_down_s", P), ("sh_bits", C.c_int),
+                ("sh_group", C.c_int)]
+
+
+_orc = None
+_ref = None
+
+
+def _p(a):
+    return C.c_void_p(a.ctypes.data) if a is not None else None
+
+
+def lib() -> C.CDLL:
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORACLE_SO):
+            build(ref=False)
+        L = C.CDLL(ORACLE_SO)
+        L.orc_f16_flush.restype = C.c_float
+        L.orc_f16_flush.argtypes = [C.c_uint16]
+        L.orc_f16.restype = C.c_float
+        L.orc_f16.argtypes = [C.c_uint16]
+        L.orc_lut_build.argtypes = [P, P, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.orc_vq_rows.argtypes = [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.orc_vq_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, P, C.c_int]
+        L.orc_dequant.argtypes = [P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_int]
+        L.orc_dotf.restype = C.c_float
+        L.orc_dotf.argtypes = [P, P, C.c_int]
+        L.orc_route.argtypes = [P, P, C.c_int, C.c_int, C.c_int, C.c_float, P, P]
+        L.orc_mvq_rows.argtypes = [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_size_t]
+        L.orc_record_check.argtypes = [C.POINTER(OrcMoe), C.c_int, C.c_int]
+        L.orc_moe_layer.argtypes = [C.POINTER(OrcMoe), C.c_int, P, P, P, P, C.c_int]
+        L.orc_moe_experts.argtypes = [C.POINTER(OrcMoe), P, P, C.c_int, P, P, C.c_int]
+        L.orc_moe_chunk.argtypes = [C.POINTER(OrcMoe), C.c_int, P, C.c_int, P, P, P, C.c_int]
+        _orc = L
+    return _orc
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref() -> C.CDLL | None:
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_SO):
+            return None
+        R = C.CDLL(REF_SO)
+        R.refh_set_backend.restype = C.c_char_p
+        R.refh_set_backend.argtypes = [C.c_int]
+        R.refh_best_backend.restype = C.c_int
+        R.refh_pool_init.argtypes = [C.c_int]
+        R.refh_pool_threads.restype = C.c_int
+        R.refh_version.restype = C.c_char_p
+        R.refh_lutb.argtypes = [P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int]
+        R.refh_vq_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.c_int]
+        R.refh_mv_open.restype = P
+        R.refh_mv_open.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        R.refh_mv_run.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int]
+        R.refh_mv_close.argtypes = [P]
+        R.refh_moe_open.restype = P
+        R.refh_moe_open.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    C.c_float, P, P, P, C.c_int, C.c_int, P, C.c_size_t,
+                                    C.c_int, P, P, P, P, P, P, C.c_int]
+        R.refh_moe_layer.restype = C.c_int
+        R.refh_moe_layer.argtypes = [P, P, P, P]
+        R.refh_moe_chunk.restype = C.c_int
+        R.refh_moe_chunk.argtypes = [P, P, C.c_int, P, P, P]
+        R.refh_moe_close.argtypes = [P]
+        R.refh_load.restype = P
+        R.refh_load.argtypes = [C.c_char_p]
+        R.refh_codebooks.restype = C.POINTER(C.c_float)
+        R.refh_codebooks.argtypes = [P, C.POINTER(C.c_int)]
+        R.refh_free.argtypes = [P]
+        _ref = R
+    return _ref
+
+
+# ---- restatement ----------------------------------------------------------
+
+def f16_flush(raw: np.ndarray) -> np.ndarray:
+    L = lib()
+    r = np.asarray(raw, dtype=np.uint16).ravel()
+    return np.array([L.orc_f16_flush(int(v)) for v in r], dtype=np.float32).reshape(np.shape(raw))
+
+
+def lut_build(books, cb_base, x, stages=3, fma=1):
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    nv = xx.size // 8
+    lut = np.empty((nv, stages, 256), dtype=np.float32)
+    lib().orc_lut_build(_p(lut), _p(b), cb_base, _p(xx), nv, stages, 256, 8, fma)
+    return lut
+
+
+def vq_matvec(idx, scale, x, M, N, books, cb_base, stages=3, fma=1):
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    y = np.empty(M, dtype=np.float32)
+    lut = np.empty((N // 8) * stages * 256, dtype=np.float32)
+    lib().orc_vq_matvec(_p(y), _p(i), _p(s), _p(xx), M, N, _p(b), cb_base, stages, 256, 8,
+                        _p(lut), fma)
+    return y
+
+
+def dequant(idx, scale, M, N, books, cb_base, stages=3):
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    W = np.empty((M, N), dtype=np.float32)
+    lib().orc_dequant(_p(W), _p(i), _p(s), M, N, _p(b), cb_base, stages, 256, 8, 64)
+    return W
+
+
+def route(logits, bias, K, renorm, routed_scale):
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    b = np.ascontiguousarray(bias, dtype=np.float32) if bias is not None else None
+    idx = np.empty(K, dtype=np.int32)
+    w = np.empty(K, dtype=np.float32)
+    lib().orc_route(_p(lg), _p(b), lg.size, K, renorm, C.c_float(routed_scale), _p(idx), _p(w))
+    return idx, w
+
+
+def _moe_struct(L, keep):
+    books = np.ascontiguousarray(L.books)
+    router = np.ascontiguousarray(L.router, dtype=np.float32)
+    keep += [books, router, L.bank]
+    s = OrcMoe()
+    s.hidden, s.inter, s.n_experts, s.top_k = L.hidden, L.inter, L.n_experts, L.top_k
+    s.renorm, s.routed_scale = L.renorm, L.routed_scale
+    s.stages, s.entries, s.vec_dim, s.index_block = L.stages, 256, 8, 64
+    s.router, s.books, s.n_books = _p(router), _p(books), books.shape[0]
+    if L.bias is not None:
+        b = np.ascontiguousarray(L.bias, dtype=np.float32)
+        keep.append(b)
+        s.bias = _p(b)
+    s.bank, s.rec_bytes = _p(L.bank), L.rec_bytes
+    s.shared_inter = L.shared_inter
+    if L.shared_inter:
+        for k in ("gate", "up", "down"):
+            q, sc = L.sh[k]
+            keep += [q, sc]
+            setattr(s, "sh_" + k, _p(q))
+            setattr(s, "sh_" + k + "_s", _p(sc))
+        s.sh_bits, s.sh_group = 8, 128
+    return s
+
+
+def moe_layer(L, x, fma=1):
+    keep = []
+    s = _moe_struct(L, keep)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(L.hidden, dtype=np.float32)
+    idx = np.empty(L.top_k, dtype=np.int32)
+    w = np.empty(L.top_k, dtype=np.float32)
+    rc = lib().orc_moe_layer(C.byref(s), L.layer, _p(xx), _p(out), _p(idx), _p(w), fma)
+    if rc:
+        raise RuntimeError("oracle: record check failed")
+    return out, idx, w
+
+
+def moe_experts(L, idx, w, x, fma=1):
+    keep = []
+    s = _moe_struct(L, keep)
+    i = np.ascontiguousarray(idx, dtype=np.int32)
+    ww = np.ascontiguousarray(w, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(L.hidden, dtype=np.float32)
+    lib().orc_moe_experts(C.byref(s), _p(i), _p(ww), i.size, _p(xx), _p(y), fma)
+    return y
+
+
+def moe_chunk(L, x, fma=1):
+    keep = []
+    s = _moe_struct(L, keep)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    nT = xx.shape[0]
+    out = np.empty((nT, L.hidden), dtype=np.float32)
+    route_ = np.empty((nT, L.top_k), dtype=np.int32)
+    rw = np.empty((nT, L.top_k), dtype=np.float32)
+    rc = lib().orc_moe_chunk(C.byref(s), L.layer, _p(xx), nT, _p(out), _p(route_), _p(rw), fma)
+    if rc:
+        raise RuntimeError("oracle: record check failed")
+    return out, route_, rw
+
+
+# ---- the reference, compiled ---------------------------------------------
+
+class RefMoe:
+    """One MoE layer inside the reference engine (ref_harness.c)."""
+
+    def __init__(self, L, max_tokens=64, backend=None, threads=0):
+        R = ref()
+        if R is None:
+            raise RuntimeError("oracle/_ref/libwaste_ref.so is not built")
+        self.R = R
+        self.backend = R.refh_set_backend(R.refh_best_backend() if backend is None else backend)
+        R.refh_pool_init(threads)
+        self.keep = [np.ascontiguousarray(L.router, dtype=np.float32),
+                     np.ascontiguousarray(L.books, dtype=np.float32), L.bank]
+        bias = np.ascontiguousarray(L.bias, dtype=np.float32) if L.bias is not None else None
+        self.keep.append(bias)
+        sh = [None] * 6
+        if L.shared_inter:
+            sh = []
+            for k in ("gate", "up", "down"):
+                q, s = L.sh[k]
+                self.keep += [q, s]
+                sh += [_p(q), _p(s)]
+        self.h = R.refh_moe_open(L.layer, L.hidden, L.inter, L.n_experts, L.top_k, L.renorm,
+                                 C.c_float(L.routed_scale), _p(self.keep[0]), _p(bias),
+                                 _p(self.keep[1]), self.keep[1].shape[0], L.cb_base,
+                                 _p(L.bank), L.rec_bytes, L.shared_inter, *sh, max_tokens)
+        if not self.h:
+            raise RuntimeError("reference harness refused the layer "
+                               "(the shared width must be a multiple of inter)")
+        self.L = L
+
+    def layer(self, x):
+        xx = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(self.L.hidden, dtype=np.float32)
+        idx = np.empty(self.L.top_k, dtype=np.int32)
+        rc = self.R.refh_moe_layer(self.h, _p(xx), _p(out), _p(idx))
+        if rc:
+            raise RuntimeError(f"reference read error {rc}")
+        return out, idx
+
+    def chunk(self, x):
+        xx = np.ascontiguousarray(x, dtype=np.float32)
+        nT = xx.shape[0]
+        out = np.empty((nT, self.L.hidden), dtype=np.float32)
+        r = np.empty((nT, self.L.top_k), dtype=np.int32)
+        w = np.empty((nT, self.L.top_k), dtype=np.float32)
+        rc = self.R.refh_moe_chunk(self.h, _p(xx), nT, _p(out), _p(r), _p(w))
+        if rc:
+            raise RuntimeError(f"reference read error {rc}")
+        return out, r, w
+
+    def close(self):
+        if self.h:
+            self.R.refh_moe_close(self.h)
+            self.h = None

@@ -1,0 +1,153 @@
+"""Regenerates the golden fixtures in tests/golden/ from the REFERENCE.
+
+Run in a container that has the reference tree (default /root/reference) and
+oracle/_ref/libwaste_ref.so built from it (make -C oracle ref):
+
+    python tests/golden/make_golden.py
+
+Every output here is produced by the reference's own code:
+
+* f16_flush.npz — all 65536 f16 bit patterns through the engine's codebook
+  decode (src/model.c:1278-1287), reached by loading a container whose
+  codebooks.bin holds every pattern. The container is written by the
+  reference's tools/make_test_container.py (imported from the reference
+  tree, seed 0), and its codebooks.bin is then replaced.
+* lut_*.npz, matvec_*.npz — vq_build_lut / vq_matvec (src/model.c:1911,
+  2282) through the reference's AVX-512 slot and its portable (CPU) slot.
+* moe_*.npz — moe_layer / moe_chunk (src/model.c:2713, 3512) on seeded
+  layers built by warp_b200.synth; the inputs are regenerated from the seed
+  (numpy PCG64, which is stable across numpy versions) and pinned by a
+  sha256 of their bytes.
+
+The fixtures are small; tests compare the CPU restatement against them
+bit for bit and the CUDA backend within the stated tolerances.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import shutil
+import struct
+import sys
+import tempfile
+import zlib
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import oracle as O  # noqa: E402
+from warp_b200 import synth  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+REF_TREE = os.environ.get("WARP_REFERENCE", "/root/reference")
+
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+from golden_cases import MOE_CASES  # noqa: E402  (shared with the tests)
+
+
+def layer_sha(L) -> str:
+    h = hashlib.sha256()
+    for a in (L.books_raw, L.router, L.bank):
+        h.update(np.ascontiguousarray(a).tobytes())
+    if L.bias is not None:
+        h.update(L.bias.tobytes())
+    for k in ("gate", "up", "down"):
+        if k in L.sh:
+            h.update(L.sh[k][0].tobytes())
+            h.update(L.sh[k][1].tobytes())
+    return h.hexdigest()
+
+
+def f16_flush_fixture(R):
+    sys.path.insert(0, os.path.join(REF_TREE, "tools"))
+    import make_test_container as mtc  # the reference's own generator
+    tmp = tempfile.mkdtemp(prefix="golden_ct_")
+    try:
+        argv = sys.argv
+        sys.argv = ["make_test_container.py", tmp, "--seed", "0"]
+        try:
+            mtc.main()
+        finally:
+            sys.argv = argv
+        allpat = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+        n_books = 65536 // (256 * 8)
+        with open(os.path.join(tmp, "codebooks.bin"), "wb") as f:
+            for b in range(n_books):
+                f.write(struct.pack("<IHBBII", 0x4B424357, b, 4, 8, 256, 0))
+                f.write(allpat[b * 2048:(b + 1) * 2048].tobytes())
+        m = R.refh_load(tmp.encode())
+        if not m:
+            raise RuntimeError("reference could not load the container")
+        n = O.C.c_int(0)
+        p = R.refh_codebooks(m, O.C.byref(n))
+        got = np.ctypeslib.as_array(p, shape=(n.value * 2048,)).copy()
+        R.refh_free(m)
+        np.savez_compressed(os.path.join(OUT, "f16_flush.npz"),
+                            bits=got.view(np.uint32))
+        print("f16_flush.npz", n.value, "books")
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
+def lut_matvec_fixtures(R):
+    rng = np.random.default_rng(2024)
+    raw = synth.codebooks(rng, 12)
+    books = synth.flush_f16(raw)
+    cases = {"matvec_ragged": (100, 256, 3), "matvec_square": (256, 512, 3),
+             "matvec_vq2r": (192, 128, 2)}
+    xs = {}
+    for be, tag in ((1, "avx512"), (0, "cpu")):
+        name = R.refh_set_backend(be)
+        x = synth.activations(99, 512)[0]
+        lut = np.empty((64, 3, 256), np.float32)
+        R.refh_lutb(O._p(lut), O._p(books), 12, 3, O._p(x), 64, 3, 256, 8)
+        np.savez_compressed(os.path.join(OUT, f"lut_{tag}.npz"), books_raw=raw, x=x,
+                            cb_base=3, lut=lut, backend=name)
+        for cname, (M, N, st) in cases.items():
+            r2 = np.random.default_rng(zlib.crc32(cname.encode()))
+            idx, sc = synth.random_matrix(r2, M, N, stages=st)
+            if cname not in xs:
+                xs[cname] = synth.activations(len(cname), N)[0]
+            x = xs[cname]
+            y = np.empty(M, np.float32)
+            R.refh_vq_matvec(O._p(y), O._p(idx), O._p(sc), O._p(x), M, N, O._p(books), 12,
+                             3, st, 256, 8)
+            np.savez_compressed(os.path.join(OUT, f"{cname}_{tag}.npz"), books_raw=raw,
+                                idx=idx, scale=sc, x=x, y=y, M=M, N=N, stages=st,
+                                cb_base=3, backend=name)
+        print("lut/matvec fixtures for", name)
+
+
+def moe_fixtures():
+    for name, (seed, kw, xseed, T) in MOE_CASES.items():
+        L = synth.moe_layer(seed, **kw)
+        x = synth.activations(xseed, L.hidden, T=max(T, 2))
+        res = {"sha": layer_sha(L), "seed": seed, "xseed": xseed}
+        for be, tag in ((1, "avx512"), (0, "cpu")):
+            rm = O.RefMoe(L, max_tokens=max(T, 1), backend=be, threads=0)
+            out0, idx0 = rm.layer(x[0])
+            out1, idx1 = rm.layer(x[1])
+            res[f"out0_{tag}"], res[f"idx0_{tag}"] = out0, idx0
+            res[f"out1_{tag}"], res[f"idx1_{tag}"] = out1, idx1
+            if T:
+                c, r, w = rm.chunk(x[:T])
+                res[f"chunk_{tag}"], res[f"route_{tag}"], res[f"rw_{tag}"] = c, r, w
+            res[f"backend_{tag}"] = rm.backend
+            rm.close()
+        np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **res)
+        print(name, "written")
+
+
+def main():
+    R = O.ref()
+    if R is None:
+        raise SystemExit("build the reference first: make -C oracle ref")
+    f16_flush_fixture(R)
+    lut_matvec_fixtures(R)
+    moe_fixtures()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+"""Parity of the CUDA backend (through the C ABI) against the oracle.
+
+Tolerances, as the north star states them:
+  * the codebook table (LUT), the dequantised weights and the routing
+    indices are bit-exact;
+  * matvec and layer outputs are within 2e-5 relative L2 (fp32 accumulation,
+    different summation order over vector positions).
+The oracle is the CPU restatement pinned to the reference's golden vectors
+(tests/test_golden.py); the goldens themselves are checked here too.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from golden_cases import MATVEC_CASES, MOE_CASES, bits, load, rel_l2
+from warp_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+def test_backend_registers(cuda_lib):
+    wb = cuda_lib
+    name = wb.register_cuda()
+    assert name and "sm_100a" in name
+    slots = wb.register_cuda_vq()
+    assert slots.moe_experts and slots.moe_chunk_experts and slots.vq_bank_load
+
+
+@pytest.mark.parametrize("tag", ["avx512"])
+def test_lut_bitexact(cuda_lib, tag):
+    wb = cuda_lib
+    g = load(f"lut_{tag}")
+    wb.codebooks_load_f16(g["books_raw"])
+    lut = wb.lutb(g["x"], int(g["cb_base"]))
+    assert np.array_equal(bits(lut), bits(g["lut"]))
+    # and at a larger, freshly seeded size
+    rng = np.random.default_rng(77)
+    raw = synth.codebooks(rng, 6)
+    wb.codebooks_load_f16(raw)
+    x = synth.activations(78, 4096)[0]
+    assert np.array_equal(bits(wb.lutb(x, 3)), bits(O.lut_build(synth.flush_f16(raw), 3, x)))
+
+
+@pytest.mark.parametrize("M,N,st", [(100, 256, 3), (256, 512, 3), (64, 8, 3), (130, 96, 2),
+                                    (4096, 4096, 3)])
+def test_dequant_bitexact(cuda_lib, M, N, st):
+    wb = cuda_lib
+    rng = np.random.default_rng(M * 7 + N)
+    raw = synth.codebooks(rng, 9)
+    wb.codebooks_load_f16(raw)
+    idx, sc = synth.random_matrix(rng, M, N, stages=st)
+    W = wb.vq_dequant(idx, sc, M, N, 3, st)
+    Wo = O.dequant(idx, sc, M, N, synth.flush_f16(raw), 3, st)
+    assert np.array_equal(bits(W), bits(Wo))
+
+
+@pytest.mark.parametrize("case", MATVEC_CASES)
+def test_matvec_golden(cuda_lib, case):
+    wb = cuda_lib
+    g = load(f"{case}_avx512")
+    wb.codebooks_load_f16(g["books_raw"])
+    y = wb.vq_matvec(g["idx"], g["scale"], g["x"], int(g["M"]), int(g["N"]), int(g["cb_base"]),
+                     int(g["stages"]))
+    assert rel_l2(y, g["y"]) < TOL
+
+
+@pytest.mark.parametrize("M,N", [(4096, 4096), (1024, 2304), (2304, 1024), (7168, 2048),
+                                 (64, 8), (1, 64)])
+def test_matvec_shapes(cuda_lib, M, N):
+    """Config 1 (4096x4096) and the Kimi-Linear / K3-class expert shapes."""
+    wb = cuda_lib
+    rng = np.random.default_rng(M + N)
+    raw = synth.codebooks(rng, 3)
+    wb.codebooks_load_f16(raw)
+    idx, sc = synth.random_matrix(rng, M, N)
+    x = synth.activations(5, N)[0]
+    y = wb.vq_matvec(idx, sc, x, M, N, 0)
+    yo = O.vq_matvec(idx, sc, x, M, N, synth.flush_f16(raw), 0)
+    assert rel_l2(y, yo) < TOL
+    # deterministic: the same call twice gives the same bits
+    assert np.array_equal(bits(wb.vq_matvec(idx, sc, x, M, N, 0)), bits(y))
+
+
+def test_matvec_dev_batched(cuda_lib):
+    """The device-pointer batched entry point over G independent matrices."""
+    import torch
+    wb = cuda_lib
+    M, N, G = 1024, 2304, 5
+    rng = np.random.default_rng(9)
+    raw = synth.codebooks(rng, 3)
+    wb.codebooks_load_f16(raw)
+    mats = [synth.random_matrix(rng, M, N) for _ in range(G)]
+    xs = synth.activations(10, N, T=G)
+    d_idx = [torch.from_numpy(m[0]).cuda() for m in mats]
+    d_sc = [torch.from_numpy(m[1].view(np.int16)).cuda() for m in mats]
+    d_x = torch.from_numpy(xs).cuda()
+    d_y = torch.empty((G, M), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    wb.vq_matvec_dev([t.data_ptr() for t in d_idx], [t.data_ptr() for t in d_sc],
+                     [d_x[g].data_ptr() for g in range(G)], [d_y[g].data_ptr() for g in range(G)],
+                     M, N, 0, 3, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    y = d_y.cpu().numpy()
+    for g in range(G):
+        yo = O.vq_matvec(mats[g][0], mats[g][1], xs[g], M, N, synth.flush_f16(raw), 0)
+        assert rel_l2(y[g], yo) < TOL
+
+
+def _layer(name):
+    seed, kw, xseed, T = MOE_CASES[name]
+    L = synth.moe_layer(seed, **kw)
+    x = synth.activations(xseed, L.hidden, T=max(T, 2))
+    return L, x, load(name), T
+
+
+@pytest.mark.parametrize("name", list(MOE_CASES))
+def test_moe_layer_parity(cuda_lib, name):
+    """Router + routed experts + shared expert on the device: expert indices
+    bit-exact against the reference's golden route, output within 2e-5 of
+    the reference's (AVX-512) output."""
+    wb = cuda_lib
+    L, x, g, _ = _layer(name)
+    wb.vq_bank_free(L.layer)
+    wb.load_layer(L)
+    for t in (0, 1):
+        out, idx, w = wb.moe_layer(L.layer, x[t], L.top_k, L.hidden)
+        assert np.array_equal(idx, g[f"idx{t}_avx512"])
+        assert rel_l2(out, g[f"out{t}_avx512"]) < TOL
+        _, _, wo = O.moe_layer(L, x[t], fma=1)
+        assert rel_l2(w, wo) < 1e-6
+
+
+@pytest.mark.parametrize("name", list(MOE_CASES))
+def test_moe_experts_parity(cuda_lib, name):
+    """The drop-in slot: route given by the engine, host buffers in and out."""
+    wb = cuda_lib
+    L, x, g, _ = _layer(name)
+    wb.vq_bank_free(L.layer)
+    wb.load_layer(L, trunk=False)
+    _, idx, w = O.moe_layer(L, x[0], fma=1)
+    y = wb.moe_experts(L.layer, idx, w, x[0], L.hidden, L.inter)
+    yo = O.moe_experts(L, idx, w, x[0], fma=1)
+    assert rel_l2(y, yo) < TOL
+
+
+@pytest.mark.parametrize("name", [n for n, c in MOE_CASES.items() if c[3]])
+def test_moe_chunk_parity(cuda_lib, name):
+    """Prefill slot: per token, experts added in ascending id (moe_chunk)."""
+    import copy
+    wb = cuda_lib
+    L, x, g, T = _layer(name)
+    wb.vq_bank_free(L.layer)
+    wb.load_layer(L, trunk=False)
+    route, rw = g["route_avx512"], g["rw_avx512"]
+    y = wb.moe_chunk_experts(L.layer, route, rw, x[:T], L.hidden, L.inter)
+    L0 = copy.copy(L)
+    L0.shared_inter = 0          # the routed part alone
+    yo, r2, _ = O.moe_chunk(L0, x[:T], fma=1)
+    assert np.array_equal(r2, route)
+    assert rel_l2(y, yo) < TOL
+
+
+def test_bank_rejects_bad_record(cuda_lib):
+    wb = cuda_lib
+    L = synth.moe_layer(21, hidden=128, inter=64, n_experts=4, top_k=2, shared_inter=0, layer=7)
+    wb.vq_bank_free(7)
+    wb.codebooks_load_f16(L.books_raw)
+    bad = L.bank.copy()
+    bad[L.rec_bytes + 4] ^= 0xFF           # expert 1's layer field
+    with pytest.raises(wb.WasteCudaError) as e:
+        wb.vq_bank_load(7, 4, L.rec_bytes, 0, 4, bad, 64, 128, 3)
+    assert e.value.rc == wb.E_RECORD
+    wb.vq_bank_load(7, 4, L.rec_bytes, 0, 4, L.bank, 64, 128, 3)
+    with pytest.raises(wb.WasteCudaError) as e:
+        wb.moe_experts(7, [0, 9], [1.0, 1.0], np.zeros(128, np.float32), 128, 64)
+    assert e.value.rc == wb.E_ARG
+    with pytest.raises(wb.WasteCudaError) as e:
+        wb.moe_experts(8, [0, 1], [1.0, 1.0], np.zeros(128, np.float32), 128, 64)
+    assert e.value.rc == wb.E_NOBANK
+    wb.vq_bank_free(7)

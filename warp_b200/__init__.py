@@ -1,0 +1,310 @@
+"""warp_b200 — B200 (sm_100a) backend for WARP's VQ3R routed-expert FFN.
+
+The product is the C-ABI library ``warp_b200/lib/libwaste_cuda.so``
+(include/waste_cuda.h). This module binds it with ctypes so tests and the
+benchmark call exactly the entry points the reference engine's integration
+calls. There is no fallback: if the library is missing or no sm_100 device is
+present, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libwaste_cuda.so")
+
+# Entry points declared in include/waste_cuda.h, in header order.
+EXPORTS = (
+    "waste_register_cuda", "waste_register_cuda_vq",
+    "waste_cuda_init", "waste_cuda_shutdown", "waste_cuda_device",
+    "waste_cuda_last_error", "waste_cuda_backend_name",
+    "waste_cuda_codebooks_load", "waste_cuda_codebooks_load_f16",
+    "waste_cuda_vq_bank_load", "waste_cuda_vq_bank_free",
+    "waste_cuda_moe_trunk_load", "waste_cuda_moe_experts",
+    "waste_cuda_moe_chunk_experts", "waste_cuda_moe_layer",
+    "waste_cuda_moe_layer_dev", "waste_cuda_lutb", "waste_cuda_vq_matvec",
+    "waste_cuda_vq_dequant", "waste_cuda_vq_matvec_dev",
+    "waste_cuda_launch_count", "waste_cuda_profile", "waste_cuda_profile_read",
+)
+
+PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
+
+OK, E_ARG, E_DEVICE, E_RECORD, E_NOBANK, E_NOMEM, E_NODEV = 0, -1, -2, -3, -4, -5, -6
+
+
+class WasteCudaError(RuntimeError):
+    def __init__(self, rc: int, msg: str):
+        super().__init__(f"waste_cuda status {rc}: {msg}")
+        self.rc = rc
+
+
+class MoeCall(C.Structure):
+    """struct waste_moe_call (include/waste_cuda.h)."""
+    _fields_ = [("layer", C.c_int), ("K", C.c_int),
+                ("idx", C.POINTER(C.c_int)), ("w", C.POINTER(C.c_float)),
+                ("x", C.POINTER(C.c_float)), ("ysum", C.POINTER(C.c_float)),
+                ("lat", C.c_int), ("inter", C.c_int), ("act", C.c_int),
+                ("situ_beta", C.c_float), ("situ_linear_beta", C.c_float)]
+
+
+class MoeChunkCall(C.Structure):
+    """struct waste_moe_chunk_call (include/waste_cuda.h)."""
+    _fields_ = [("layer", C.c_int), ("nT", C.c_int), ("K", C.c_int),
+                ("route", C.POINTER(C.c_int)), ("rw", C.POINTER(C.c_float)),
+                ("x", C.POINTER(C.c_float)), ("ysum", C.POINTER(C.c_float)),
+                ("lat", C.c_int), ("inter", C.c_int), ("act", C.c_int),
+                ("situ_beta", C.c_float), ("situ_linear_beta", C.c_float)]
+
+
+class VqSlots(C.Structure):
+    """waste_vq_slots: the expert-path slots next to waste_kernels."""
+    _fields_ = [("codebooks_load", C.c_void_p), ("vq_bank_load", C.c_void_p),
+                ("vq_bank_free", C.c_void_p), ("moe_experts", C.c_void_p),
+                ("moe_chunk_experts", C.c_void_p)]
+
+
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def load_library() -> C.CDLL:
+    """Load libwaste_cuda.so (built in-tree by warp_b200.build)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(
+            f"{LIB_PATH} is missing: run `python -c 'import __graft_entry__ as g; g.build()'`")
+    lib = C.CDLL(LIB_PATH)
+    P = C.c_void_p
+    f32p, i32p = C.POINTER(C.c_float), C.POINTER(C.c_int)
+    sig = {
+        "waste_register_cuda": (C.c_char_p, [P]),
+        "waste_register_cuda_vq": (C.c_int, [C.POINTER(VqSlots)]),
+        "waste_cuda_init": (C.c_int, [C.c_int]),
+        "waste_cuda_shutdown": (None, []),
+        "waste_cuda_device": (C.c_int, []),
+        "waste_cuda_last_error": (C.c_char_p, []),
+        "waste_cuda_backend_name": (C.c_char_p, []),
+        "waste_cuda_codebooks_load": (C.c_int, [P, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_codebooks_load_f16": (C.c_int, [P, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_bank_load": (C.c_int, [C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_int,
+                                              P, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_bank_free": (None, [C.c_int]),
+        "waste_cuda_moe_trunk_load": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                C.c_float, P, P, C.c_int, P, P, P, P, P, P]),
+        "waste_cuda_moe_experts": (C.c_int, [C.POINTER(MoeCall)]),
+        "waste_cuda_moe_chunk_experts": (C.c_int, [C.POINTER(MoeChunkCall)]),
+        "waste_cuda_moe_layer": (C.c_int, [C.c_int, P, P, P, P]),
+        "waste_cuda_moe_layer_dev": (C.c_int, [C.c_int, P, P, P, P, P]),
+        "waste_cuda_lutb": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_matvec": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_dequant": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_matvec_dev": (C.c_int, [C.c_int, P, P, P, P, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, P]),
+        "waste_cuda_launch_count": (C.c_uint64, []),
+        "waste_cuda_profile": (C.c_int, [C.c_int]),
+        "waste_cuda_profile_read": (C.c_int, [P, P, C.c_int]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    del f32p, i32p
+    _lib = lib
+    return lib
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def _check(rc: int):
+    if rc != 0:
+        msg = load_library().waste_cuda_last_error()
+        raise WasteCudaError(rc, msg.decode() if msg else "(no message)")
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def init(device: int = -1) -> str:
+    lib = load_library()
+    _check(lib.waste_cuda_init(device))
+    return lib.waste_cuda_backend_name().decode()
+
+
+def shutdown():
+    load_library().waste_cuda_shutdown()
+
+
+def register_cuda() -> str | None:
+    """waste_register_cuda: the backend name, or None when it declines."""
+    n = load_library().waste_register_cuda(None)
+    return n.decode() if n else None
+
+
+def register_cuda_vq() -> VqSlots:
+    s = VqSlots()
+    _check(load_library().waste_register_cuda_vq(C.byref(s)))
+    return s
+
+
+def launch_count() -> int:
+    return int(load_library().waste_cuda_launch_count())
+
+
+def profile(on: bool):
+    """Phase timers on/off (CUDA events around every kernel launch)."""
+    _check(load_library().waste_cuda_profile(1 if on else 0))
+
+
+def profile_read() -> dict:
+    """{phase: (total ms, launches)} since the last read; resets."""
+    n = len(PHASES)
+    ms = np.zeros(n, dtype=np.float64)
+    cnt = np.zeros(n, dtype=np.uint64)
+    _check(load_library().waste_cuda_profile_read(_ptr(ms), _ptr(cnt), n))
+    return {p: (float(ms[i]), int(cnt[i])) for i, p in enumerate(PHASES)}
+
+
+def codebooks_load(books: np.ndarray):
+    b = _f32(books)
+    _check(load_library().waste_cuda_codebooks_load(_ptr(b), b.shape[0], b.shape[1], b.shape[2]))
+
+
+def codebooks_load_f16(raw: np.ndarray):
+    r = np.ascontiguousarray(raw, dtype=np.uint16)
+    _check(load_library().waste_cuda_codebooks_load_f16(_ptr(r), r.shape[0], r.shape[1],
+                                                        r.shape[2]))
+
+
+def vq_bank_load(layer: int, n_experts: int, rec_bytes: int, first: int, count: int,
+                 records: np.ndarray, inter: int, lat: int, stages: int = 3):
+    r = np.ascontiguousarray(records, dtype=np.uint8)
+    if r.size < count * rec_bytes:
+        raise ValueError("records buffer shorter than count * rec_bytes")
+    _check(load_library().waste_cuda_vq_bank_load(layer, n_experts, rec_bytes, first, count,
+                                                  _ptr(r), inter, lat, stages))
+
+
+def vq_bank_free(layer: int):
+    load_library().waste_cuda_vq_bank_free(layer)
+
+
+def moe_trunk_load(layer: int, n_experts: int, hidden: int, top_k: int, renorm: int,
+                   routed_scale: float, router: np.ndarray, bias: np.ndarray | None,
+                   sh_inter: int = 0, sh: dict | None = None):
+    rt = _f32(router)
+    b = _f32(bias) if bias is not None else None
+    keep = [rt, b]
+    ptrs = []
+    if sh_inter:
+        for k in ("gate", "up", "down"):
+            q = np.ascontiguousarray(sh[k][0], dtype=np.int8)
+            s = np.ascontiguousarray(sh[k][1], dtype=np.uint16)
+            keep += [q, s]
+            ptrs += [_ptr(q), _ptr(s)]
+    else:
+        ptrs = [None] * 6
+    _check(load_library().waste_cuda_moe_trunk_load(
+        layer, n_experts, hidden, top_k, renorm, C.c_float(routed_scale), _ptr(rt),
+        _ptr(b) if b is not None else None, sh_inter, *ptrs))
+    del keep
+
+
+def load_layer(L, trunk: bool = True):
+    """Codebooks, the whole bank and (optionally) the trunk of a synth.MoELayer."""
+    codebooks_load_f16(L.books_raw)
+    vq_bank_load(L.layer, L.n_experts, L.rec_bytes, 0, L.n_experts, L.bank, L.inter,
+                 L.hidden, L.stages)
+    if trunk:
+        moe_trunk_load(L.layer, L.n_experts, L.hidden, L.top_k, L.renorm, L.routed_scale,
+                       L.router, L.bias, L.shared_inter, L.sh)
+
+
+def moe_experts(layer: int, idx, w, x, lat: int, inter: int) -> np.ndarray:
+    """The expert loop for one token (waste_moe_call): ysum[lat]."""
+    i = np.ascontiguousarray(idx, dtype=np.int32)
+    ww = _f32(w)
+    xx = _f32(x)
+    y = np.empty(lat, dtype=np.float32)
+    c = MoeCall(layer, i.size, i.ctypes.data_as(C.POINTER(C.c_int)),
+                ww.ctypes.data_as(C.POINTER(C.c_float)), xx.ctypes.data_as(C.POINTER(C.c_float)),
+                y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, 0, 0.0, 0.0)
+    _check(load_library().waste_cuda_moe_experts(C.byref(c)))
+    return y
+
+
+def moe_chunk_experts(layer: int, route, rw, x, lat: int, inter: int) -> np.ndarray:
+    """The prefill expert loop (waste_moe_chunk_call): ysum[nT][lat]."""
+    r = np.ascontiguousarray(route, dtype=np.int32)
+    ww = _f32(rw)
+    xx = _f32(x)
+    nT, K = r.shape
+    y = np.empty((nT, lat), dtype=np.float32)
+    c = MoeChunkCall(layer, nT, K, r.ctypes.data_as(C.POINTER(C.c_int)),
+                     ww.ctypes.data_as(C.POINTER(C.c_float)),
+                     xx.ctypes.data_as(C.POINTER(C.c_float)),
+                     y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, 0, 0.0, 0.0)
+    _check(load_library().waste_cuda_moe_chunk_experts(C.byref(c)))
+    return y
+
+
+def moe_layer(layer: int, x, K: int, hidden: int):
+    """Whole layer on host buffers: (out[hidden], idx[K], w[K])."""
+    xx = _f32(x)
+    out = np.empty(hidden, dtype=np.float32)
+    idx = np.empty(K, dtype=np.int32)
+    w = np.empty(K, dtype=np.float32)
+    _check(load_library().waste_cuda_moe_layer(layer, _ptr(xx), _ptr(out), _ptr(idx), _ptr(w)))
+    return out, idx, w
+
+
+def moe_layer_dev(layer: int, d_x: int, d_out: int, d_idx: int, d_w: int, stream: int = 0):
+    _check(load_library().waste_cuda_moe_layer_dev(layer, C.c_void_p(d_x), C.c_void_p(d_out),
+                                                   C.c_void_p(d_idx), C.c_void_p(d_w),
+                                                   C.c_void_p(stream or None)))
+
+
+def lutb(x, cb_base: int, stages: int = 3) -> np.ndarray:
+    xx = _f32(x)
+    nv = xx.size // 8
+    lut = np.empty((nv, stages, 256), dtype=np.float32)
+    _check(load_library().waste_cuda_lutb(_ptr(lut), _ptr(xx), cb_base, nv, stages))
+    return lut
+
+
+def vq_matvec(idx, scale, x, M: int, N: int, cb_base: int, stages: int = 3) -> np.ndarray:
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    xx = _f32(x)
+    y = np.empty(M, dtype=np.float32)
+    _check(load_library().waste_cuda_vq_matvec(_ptr(y), _ptr(i), _ptr(s), _ptr(xx), M, N,
+                                               cb_base, stages))
+    return y
+
+
+def vq_dequant(idx, scale, M: int, N: int, cb_base: int, stages: int = 3) -> np.ndarray:
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    W = np.empty((M, N), dtype=np.float32)
+    _check(load_library().waste_cuda_vq_dequant(_ptr(W), _ptr(i), _ptr(s), M, N, cb_base,
+                                                stages))
+    return W
+
+
+def vq_matvec_dev(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base: int,
+                  stages: int = 3, stream: int = 0):
+    G = len(idx_ptrs)
+    arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
+    _check(load_library().waste_cuda_vq_matvec_dev(
+        G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base, stages,
+        C.c_void_p(stream or None)))

@@ -1,0 +1,130 @@
+/*
+ * vq3r_common.cuh — device helpers shared by the VQ3R kernels (sm_100a).
+ *
+ * Index layout (the reference's blocked layout, docs/FORMAT.md:194-208,
+ * tools/convert.py:297-312): [M/64][N/8][64][stages] bytes, one byte per
+ * stage. For a fixed (row block, vector position) the 64 rows' indices are
+ * 64*stages contiguous bytes, so a quarter of a block (16 rows) is exactly
+ * `stages` 16-byte words — one LDG.128 per stage.
+ */
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wc {
+
+constexpr int kVecDim = 8;      /* docs/FORMAT.md expert_quant.vec_dim */
+constexpr int kEntries = 256;   /* entries per stage codebook          */
+constexpr int kBlock = 64;      /* index_block == VQ_TILE              */
+constexpr int kRowsPerThread = 16;
+
+/* f16 -> f32 exactly as src/simd.h:49-67 (subnormals kept, exponent 31 not
+ * special-cased). Used for row scales and Q8G group scales. */
+__device__ __forceinline__ float f16_keep(uint16_t h)
+{
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t e = (h >> 10) & 0x1f, mn = h & 0x3ff;
+    if (e == 0) {
+        const float f = (float)mn * 5.9604644775390625e-08f;
+        return sign ? -f : f;
+    }
+    return __uint_as_float(sign | ((e + 112u) << 23) | (mn << 13));
+}
+
+/* Byte `p` (compile-time) of a little-endian run of 32-bit words. */
+template <int P>
+__device__ __forceinline__ uint32_t byte_at(const uint32_t *w)
+{
+    return (w[P >> 2] >> (8 * (P & 3))) & 0xffu;
+}
+
+/* 16-byte global load through the read-only path. */
+__device__ __forceinline__ uint4 ldg16(const void *p)
+{
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+/* Builds the table slice for vector positions [v0, v0+nvs) of one matrix
+ * family into shared memory:
+ *   lut[(v - v0)*ST*256 + s*256 + c] = fma chain over d of x[8v+d]*C[cb+s][c][d]
+ * from 0, d ascending — bit-identical to src/simd_avx512.c:104-112.
+ * xs: nvs*8 floats already in shared memory. books: [n_books][256][8]. */
+template <int ST>
+__device__ __forceinline__ void build_lut_slice(float *lut, const float *xs,
+                                                const float *__restrict__ books,
+                                                int cb, int nvs)
+{
+    for (int i = threadIdx.x; i < ST * kEntries; i += blockDim.x) {
+        const int s = i / kEntries, c = i % kEntries;
+        const float4 *src = reinterpret_cast<const float4 *>(
+            books + ((size_t)(cb + s) * kEntries + c) * kVecDim);
+        const float4 a = __ldg(src), b = __ldg(src + 1);
+        const float C[8] = { a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w };
+        for (int v = 0; v < nvs; v++) {
+            const float *xv = xs + v * kVecDim;
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < kVecDim; d++) acc = __fmaf_rn(xv[d], C[d], acc);
+            lut[(v * ST + s) * kEntries + c] = acc;
+        }
+    }
+}
+
+/* One vector position for 16 rows: add sum_s L_s[idx] to acc[k]. The 16*ST
+ * index bytes of this quarter-block are in w[0 .. 4*ST). */
+template <int ST, int K>
+struct RowStep {
+    static __device__ __forceinline__ void run(float *acc, const uint32_t *w,
+                                               const float *L)
+    {
+        float t = L[byte_at<K * ST>(w)];
+        if (ST > 1) t += L[kEntries + byte_at<K * ST + (ST > 1 ? 1 : 0)>(w)];
+        if (ST > 2) t += L[2 * kEntries + byte_at<K * ST + (ST > 2 ? 2 : 0)>(w)];
+        acc[K] += t;
+        RowStep<ST, K + 1>::run(acc, w, L);
+    }
+};
+template <int ST>
+struct RowStep<ST, kRowsPerThread> {
+    static __device__ __forceinline__ void run(float *, const uint32_t *, const float *) {}
+};
+
+/* Gathers nvv consecutive vector positions for one quarter-block (16 rows).
+ * p: the quarter's 16*ST bytes at the first position; consecutive positions
+ * are 64*ST bytes apart. L: the table at the first position (ST*256 floats
+ * per position). Loads run one position ahead of the arithmetic. */
+template <int ST>
+__device__ __forceinline__ void gather16(float *acc, const uint8_t *p,
+                                         const float *L, int nvv)
+{
+    constexpr int W = 4 * ST;              /* 32-bit words per position */
+    const size_t stride = (size_t)kBlock * ST;
+    uint32_t cur[W], nxt[W];
+    if (nvv <= 0) return;
+#pragma unroll
+    for (int i = 0; i < ST; i++) {
+        const uint4 q = ldg16(p + 16 * i);
+        cur[4 * i] = q.x; cur[4 * i + 1] = q.y; cur[4 * i + 2] = q.z; cur[4 * i + 3] = q.w;
+    }
+    for (int v = 0; v < nvv; v++) {
+        if (v + 1 < nvv) {
+            const uint8_t *pn = p + (size_t)(v + 1) * stride;
+#pragma unroll
+            for (int i = 0; i < ST; i++) {
+                const uint4 q = ldg16(pn + 16 * i);
+                nxt[4 * i] = q.x; nxt[4 * i + 1] = q.y; nxt[4 * i + 2] = q.z; nxt[4 * i + 3] = q.w;
+            }
+        }
+        RowStep<ST, 0>::run(acc, cur, L + (size_t)v * ST * kEntries);
+#pragma unroll
+        for (int i = 0; i < W; i++) cur[i] = nxt[i];
+    }
+}
+
+__device__ __forceinline__ float silu_ref(float v)
+{
+    /* src/model.c:501: v / (1 + expf(-v)). */
+    return v / (1.0f + expf(-v));
+}
+
+} /* namespace wc */

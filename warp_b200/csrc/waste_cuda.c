@@ -1,0 +1,791 @@
+/*
+ * waste_cuda.c — host side of the B200 backend, plain C over the CUDA
+ * runtime. Implements include/waste_cuda.h: device selection and the plugin
+ * registration (src/backend.c:57-59,202-204 in the reference), codebooks and
+ * expert banks resident in HBM (what src/ecache.c does for RAM), and the
+ * expert-loop slots, which copy the engine's host buffers in and out around
+ * the kernels in vq3r_kernels.cu.
+ *
+ * State is per process: one device, one stream, one set of layers — the
+ * reference's dispatch table is a process global too (src/backend.c:38).
+ * Calls are serialised by a mutex; the engine calls the slots from the
+ * thread running waste_model_step.
+ */
+#include "../../include/waste_cuda.h"
+#include "wc_launch.h"
+
+#include <cuda_runtime_api.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define WC_MAX_LAYERS 128          /* WASTE_MAX_LAYERS, src/model.h:44 */
+#define WC_MAX_TOPK 64             /* src/model.c:814-815 bounds top_k */
+#define WC_CHUNK_MAX 64            /* WASTE_CHUNK_MAX, src/model.h:285 */
+
+/* Expert record header, the reference's waste_expert_hdr
+ * (src/waste_format.h:98-132): an on-disk format, kept field for field. */
+typedef struct {
+    uint32_t magic;
+    uint16_t layer, expert_id;
+    uint8_t fmt, flags;
+    uint16_t codebook_id, lowrank_id, reserved0;
+    uint32_t rec_4k_blocks;
+    uint32_t gate_off, up_off, down_off, chan_corr_off;
+    uint32_t crc32;
+    uint32_t reserved1[2];
+} wc_hdr;
+
+#define WC_MAGIC_EXPERT 0x50584557u   /* src/waste_format.h:33 */
+#define WC_WQ_VQ3R 4                  /* src/waste_format.h:51 */
+#define WC_WQ_VQ2R 5                  /* src/waste_format.h:52 */
+#define WC_ALIGN 4096u                /* src/waste_format.h:42 */
+
+typedef struct {
+    int loaded;
+    wc_bank kb;                  /* device view                              */
+    uint8_t *d_base;
+    int n_total;                 /* experts in the layer                      */
+    int have_hdr;                /* offsets/codebook fixed by the first record */
+    /* trunk */
+    int trunk;
+    float *d_router, *d_bias;
+    int E, hidden, top_k, renorm;
+    float routed_scale;
+    int si;
+    int8_t *d_shg, *d_shu, *d_shd;
+    uint16_t *d_shg_s, *d_shu_s, *d_shd_s;
+} wc_layer;
+
+static struct {
+    int inited, device;
+    cudaStream_t stream;
+    char name[300];
+    float *d_books;
+    int n_books;
+    wc_layer layer[WC_MAX_LAYERS];
+    /* workspace for one launch of up to WC_CHUNK_MAX tokens */
+    float *d_ws;
+    size_t ws_floats;
+    float *d_x, *d_out;
+    int *d_idx;
+    float *d_w;
+    size_t io_floats;
+    /* pinned staging */
+    float *h_x, *h_out;
+    int *h_idx;
+    float *h_w;
+    /* single-kernel parity APIs */
+    void *d_tmp;
+    size_t tmp_bytes;
+} S;
+
+static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
+static _Thread_local char g_err[256];
+static char g_err_global[256];
+
+static int fail(int code, const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    memcpy(g_err_global, g_err, sizeof g_err);
+    return code;
+}
+
+static int cuda_fail(cudaError_t e, const char *what)
+{
+    if (e == cudaErrorMemoryAllocation)
+        return fail(WASTE_CUDA_E_NOMEM, "%s: %s", what, cudaGetErrorString(e));
+    return fail(WASTE_CUDA_E_DEVICE, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) { \
+    rc = cuda_fail(e_, what); goto out; } } while (0)
+
+const char *waste_cuda_last_error(void)
+{
+    return g_err[0] ? g_err : (g_err_global[0] ? g_err_global : NULL);
+}
+
+uint64_t waste_cuda_launch_count(void) { return wc_launches(); }
+
+int waste_cuda_profile(int on)
+{
+    pthread_mutex_lock(&g_mu);
+    const int rc = wc_prof_enable(on) ? fail(WASTE_CUDA_E_DEVICE, "profile events") : 0;
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_profile_read(double *ms, uint64_t *launches, int nphase)
+{
+    if (nphase < 0) return fail(WASTE_CUDA_E_ARG, "nphase < 0");
+    pthread_mutex_lock(&g_mu);
+    unsigned long long c[WC_PH_COUNT];
+    double t[WC_PH_COUNT];
+    wc_prof_read(t, c, WC_PH_COUNT);
+    for (int i = 0; i < nphase && i < WC_PH_COUNT; i++) {
+        if (ms) ms[i] = t[i];
+        if (launches) launches[i] = c[i];
+    }
+    pthread_mutex_unlock(&g_mu);
+    return 0;
+}
+
+static int pick_device(int requested)
+{
+    if (requested >= 0) return requested;
+    const char *e = getenv("WASTE_CUDA_DEVICE");
+    return e ? atoi(e) : 0;
+}
+
+/* Workspace for T tokens at the largest shapes loaded so far. */
+static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages)
+{
+    const size_t need = wc_moe_ws_floats(T, K, E, lat, inter, si, stages);
+    const size_t io = (size_t)T * (lat > 0 ? lat : 1);
+    if (need > S.ws_floats) {
+        if (S.d_ws) cudaFree(S.d_ws);
+        S.d_ws = NULL;
+        S.ws_floats = 0;
+        cudaError_t e = cudaMalloc((void **)&S.d_ws, need * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "workspace");
+        S.ws_floats = need;
+    }
+    if (io > S.io_floats) {
+        if (S.d_x) cudaFree(S.d_x);
+        if (S.d_out) cudaFree(S.d_out);
+        if (S.h_x) cudaFreeHost(S.h_x);
+        if (S.h_out) cudaFreeHost(S.h_out);
+        S.d_x = S.d_out = S.h_x = S.h_out = NULL;
+        S.io_floats = 0;
+        if (cudaMalloc((void **)&S.d_x, io * sizeof(float)) ||
+            cudaMalloc((void **)&S.d_out, io * sizeof(float)) ||
+            cudaMallocHost((void **)&S.h_x, io * sizeof(float)) ||
+            cudaMallocHost((void **)&S.h_out, io * sizeof(float)))
+            return fail(WASTE_CUDA_E_NOMEM, "io buffers for %d tokens", T);
+        S.io_floats = io;
+    }
+    return 0;
+}
+
+static int init_locked(int device)
+{
+    int rc = 0;
+    const int dev = pick_device(device);
+    if (S.inited) {
+        if (dev == S.device) return 0;
+        return fail(WASTE_CUDA_E_ARG, "already bound to device %d", S.device);
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0)
+        return fail(WASTE_CUDA_E_NODEV, "no CUDA device");
+    if (dev < 0 || dev >= n) return fail(WASTE_CUDA_E_NODEV, "device %d of %d", dev, n);
+    struct cudaDeviceProp p;
+    CK(cudaGetDeviceProperties(&p, dev), "cudaGetDeviceProperties");
+    if (p.major != 10) return fail(WASTE_CUDA_E_NODEV, "device %d is sm_%d%d, not sm_100", dev,
+                                   p.major, p.minor);
+    CK(cudaSetDevice(dev), "cudaSetDevice");
+    CK(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    CK(cudaMalloc((void **)&S.d_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "idx");
+    CK(cudaMalloc((void **)&S.d_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "w");
+    CK(cudaMallocHost((void **)&S.h_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "h_idx");
+    CK(cudaMallocHost((void **)&S.h_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "h_w");
+    snprintf(S.name, sizeof S.name, "CUDA sm_100a (%s)", p.name);
+    S.device = dev;
+    S.inited = 1;
+out:
+    return rc;
+}
+
+int waste_cuda_init(int device)
+{
+    pthread_mutex_lock(&g_mu);
+    const int rc = init_locked(device);
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_device(void) { return S.inited ? S.device : -1; }
+
+const char *waste_cuda_backend_name(void) { return S.inited ? S.name : NULL; }
+
+static void free_layer(wc_layer *L)
+{
+    cudaFree(L->d_base);
+    cudaFree(L->d_router); cudaFree(L->d_bias);
+    cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
+    cudaFree(L->d_shg_s); cudaFree(L->d_shu_s); cudaFree(L->d_shd_s);
+    memset(L, 0, sizeof *L);
+}
+
+void waste_cuda_shutdown(void)
+{
+    pthread_mutex_lock(&g_mu);
+    if (S.inited) {
+        cudaStreamSynchronize(S.stream);
+        for (int i = 0; i < WC_MAX_LAYERS; i++) free_layer(&S.layer[i]);
+        cudaFree(S.d_books); cudaFree(S.d_ws); cudaFree(S.d_x); cudaFree(S.d_out);
+        cudaFree(S.d_idx); cudaFree(S.d_w); cudaFree(S.d_tmp);
+        cudaFreeHost(S.h_x); cudaFreeHost(S.h_out); cudaFreeHost(S.h_idx);
+        cudaFreeHost(S.h_w);
+        cudaStreamDestroy(S.stream);
+        memset(&S, 0, sizeof S);
+    }
+    pthread_mutex_unlock(&g_mu);
+}
+
+/* ---- registration ---------------------------------------------------- */
+
+const char *waste_register_cuda(void *table)
+{
+    (void)table;
+    const char *e = getenv("WASTE_CUDA");
+    if (e && *e == '0') return NULL;
+    if (waste_cuda_init(-1) != 0) return NULL;
+    return S.name;
+}
+
+static int slot_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
+                          int count, const void *records, int inter, int lat,
+                          int stages)
+{
+    return waste_cuda_vq_bank_load(layer, n_experts, rec_bytes, first, count,
+                                   records, inter, lat, stages);
+}
+
+int waste_register_cuda_vq(waste_vq_slots *s)
+{
+    if (!s) return WASTE_CUDA_E_ARG;
+    memset(s, 0, sizeof *s);
+    if (!S.inited && waste_cuda_init(-1) != 0) return WASTE_CUDA_E_NODEV;
+    s->codebooks_load = waste_cuda_codebooks_load;
+    s->vq_bank_load = slot_bank_load;
+    s->vq_bank_free = waste_cuda_vq_bank_free;
+    s->moe_experts = waste_cuda_moe_experts;
+    s->moe_chunk_experts = waste_cuda_moe_chunk_experts;
+    return 0;
+}
+
+/* ---- codebooks --------------------------------------------------------- */
+
+static int books_upload(const float *books, int n_books)
+{
+    int rc = 0;
+    const size_t bytes = (size_t)n_books * 256 * 8 * sizeof(float);
+    if (S.d_books) { cudaFree(S.d_books); S.d_books = NULL; S.n_books = 0; }
+    CK(cudaMalloc((void **)&S.d_books, bytes), "codebooks");
+    CK(cudaMemcpy(S.d_books, books, bytes, cudaMemcpyHostToDevice), "codebooks H2D");
+    S.n_books = n_books;
+out:
+    return rc;
+}
+
+int waste_cuda_codebooks_load(const float *books, int n_books, int entries, int vec_dim)
+{
+    if (!books || n_books <= 0 || entries != 256 || vec_dim != 8)
+        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256, vec_dim 8");
+    pthread_mutex_lock(&g_mu);
+    int rc = S.inited ? 0 : init_locked(-1);
+    if (!rc) rc = books_upload(books, n_books);
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* The loader's decode, src/model.c:1278-1287: f16 -> f32 keeping the sign,
+ * with exponent 0 (zero and every subnormal) flushed to zero. */
+static float f16_flush(uint16_t v)
+{
+    const uint32_t sign = (uint32_t)(v >> 15) << 31;
+    const uint32_t e = (v >> 10) & 0x1f, man = v & 0x3ff;
+    const uint32_t bits = e ? (sign | ((e + 112u) << 23) | (man << 13)) : sign;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries, int vec_dim)
+{
+    if (!raw || n_books <= 0 || entries != 256 || vec_dim != 8)
+        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256, vec_dim 8");
+    const size_t n = (size_t)n_books * entries * vec_dim;
+    float *f = (float *)malloc(n * sizeof(float));
+    if (!f) return fail(WASTE_CUDA_E_NOMEM, "codebook staging");
+    for (size_t i = 0; i < n; i++) f[i] = f16_flush(raw[i]);
+    const int rc = waste_cuda_codebooks_load(f, n_books, entries, vec_dim);
+    free(f);
+    return rc;
+}
+
+/* ---- expert banks ------------------------------------------------------- */
+
+/* src/model.c:1698-1745 record_check, without the optional crc32. */
+static int check_record(const wc_hdr *h, int layer, int expert, size_t rec_bytes,
+                        int stages, int inter, int lat)
+{
+    if (rec_bytes < sizeof *h || h->magic != WC_MAGIC_EXPERT) return -1;
+    if (h->layer != (uint16_t)layer || h->expert_id != (uint16_t)expert) return -1;
+    if ((size_t)h->rec_4k_blocks * WC_ALIGN != rec_bytes) return -1;
+    if (h->fmt != WC_WQ_VQ3R && h->fmt != WC_WQ_VQ2R) return -1;
+    if (h->lowrank_id != 0) return -1;
+    if ((long)h->codebook_id + 3L * stages > S.n_books) return -1;
+    if (!(h->gate_off == sizeof *h && h->gate_off < h->up_off &&
+          h->up_off < h->down_off && h->down_off < h->chan_corr_off &&
+          h->chan_corr_off <= rec_bytes))
+        return -1;
+    const size_t scales = 2u * (size_t)(2 * inter + lat);
+    if (scales > rec_bytes - h->chan_corr_off) return -1;
+    /* the index streams must fit before the next section */
+    const size_t nrb_i = (size_t)(inter + 63) / 64, nrb_l = (size_t)(lat + 63) / 64;
+    const size_t gate_b = nrb_i * 64 * (lat / 8) * stages;
+    const size_t down_b = nrb_l * 64 * (inter / 8) * stages;
+    if (h->up_off - h->gate_off < gate_b || h->down_off - h->up_off < gate_b ||
+        h->chan_corr_off - h->down_off < down_b)
+        return -1;
+    /* 16-byte loads of the index streams */
+    if ((h->gate_off | h->up_off | h->down_off) & 15) return -1;
+    return 0;
+}
+
+int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
+                            int count, const void *records, int inter, int lat,
+                            int stages)
+{
+    int rc = 0;
+    if (layer < 0 || layer >= WC_MAX_LAYERS || n_experts <= 0 || first < 0 ||
+        count <= 0 || first + count > n_experts || !records || rec_bytes == 0 ||
+        rec_bytes % WC_ALIGN || inter <= 0 || lat <= 0 || inter % 8 || lat % 8 ||
+        (stages != 2 && stages != 3))
+        return fail(WASTE_CUDA_E_ARG, "vq_bank_load: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    if (!S.d_books) { rc = fail(WASTE_CUDA_E_ARG, "load codebooks before banks"); goto out; }
+    wc_layer *L = &S.layer[layer];
+    if (L->d_base && (L->n_total != n_experts || L->kb.rec_bytes != rec_bytes ||
+                      L->kb.inter != inter || L->kb.lat != lat || L->kb.stages != stages)) {
+        rc = fail(WASTE_CUDA_E_ARG, "layer %d: bank shape differs from the first load", layer);
+        goto out;
+    }
+    /* check every header before copying anything */
+    for (int i = 0; i < count; i++) {
+        const wc_hdr *h = (const wc_hdr *)((const uint8_t *)records + (size_t)i * rec_bytes);
+        if (check_record(h, layer, first + i, rec_bytes, stages, inter, lat)) {
+            rc = fail(WASTE_CUDA_E_RECORD, "layer %d expert %d: record header is not "
+                      "what the bank index describes", layer, first + i);
+            goto out;
+        }
+        const wc_hdr *h0 = L->have_hdr ? NULL : (const wc_hdr *)records;
+        const uint32_t go = h0 ? h0->gate_off : L->kb.gate_off;
+        const uint32_t uo = h0 ? h0->up_off : L->kb.up_off;
+        const uint32_t dof = h0 ? h0->down_off : L->kb.down_off;
+        const uint32_t so = h0 ? h0->chan_corr_off : L->kb.scale_off;
+        const int cb = h0 ? h0->codebook_id : L->kb.cb_base;
+        if (h->gate_off != go || h->up_off != uo || h->down_off != dof ||
+            h->chan_corr_off != so || h->codebook_id != cb) {
+            rc = fail(WASTE_CUDA_E_RECORD, "layer %d expert %d: payload offsets or "
+                      "codebook_id differ from the layer's first record", layer, first + i);
+            goto out;
+        }
+    }
+    if (!L->d_base) {
+        CK(cudaMalloc((void **)&L->d_base, rec_bytes * (size_t)n_experts), "bank");
+        L->n_total = n_experts;
+        L->kb.rec_bytes = rec_bytes;
+        L->kb.inter = inter;
+        L->kb.lat = lat;
+        L->kb.stages = stages;
+        L->kb.n_experts = n_experts;
+        L->kb.first = 0;
+    }
+    if (!L->have_hdr) {
+        const wc_hdr *h0 = (const wc_hdr *)records;
+        L->kb.gate_off = h0->gate_off;
+        L->kb.up_off = h0->up_off;
+        L->kb.down_off = h0->down_off;
+        L->kb.scale_off = h0->chan_corr_off;
+        L->kb.cb_base = h0->codebook_id;
+        L->have_hdr = 1;
+    }
+    L->kb.base = L->d_base;
+    CK(cudaMemcpy(L->d_base + (size_t)first * rec_bytes, records, rec_bytes * (size_t)count,
+                  cudaMemcpyHostToDevice), "bank H2D");
+    L->loaded = 1;
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+void waste_cuda_vq_bank_free(int layer)
+{
+    if (layer < 0 || layer >= WC_MAX_LAYERS) return;
+    pthread_mutex_lock(&g_mu);
+    if (S.inited) {
+        cudaStreamSynchronize(S.stream);
+        wc_layer *L = &S.layer[layer];
+        cudaFree(L->d_base);
+        L->d_base = NULL;
+        L->loaded = L->have_hdr = 0;
+        memset(&L->kb, 0, sizeof L->kb);
+    }
+    pthread_mutex_unlock(&g_mu);
+}
+
+int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
+                              int renorm, float routed_scale, const float *router,
+                              const float *bias, int sh_inter, const int8_t *sh_gate,
+                              const uint16_t *sh_gate_s, const int8_t *sh_up,
+                              const uint16_t *sh_up_s, const int8_t *sh_down,
+                              const uint16_t *sh_down_s)
+{
+    int rc = 0;
+    if (layer < 0 || layer >= WC_MAX_LAYERS || n_experts <= 0 || n_experts > 4096 ||
+        top_k < 1 || top_k > WC_MAX_TOPK || top_k > n_experts || hidden <= 0 ||
+        !router || sh_inter < 0 ||
+        (sh_inter > 0 && (!sh_gate || !sh_gate_s || !sh_up || !sh_up_s || !sh_down || !sh_down_s)))
+        return fail(WASTE_CUDA_E_ARG, "moe_trunk_load: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    wc_layer *L = &S.layer[layer];
+    cudaFree(L->d_router); cudaFree(L->d_bias);
+    cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
+    cudaFree(L->d_shg_s); cudaFree(L->d_shu_s); cudaFree(L->d_shd_s);
+    L->d_router = L->d_bias = NULL;
+    L->d_shg = L->d_shu = L->d_shd = NULL;
+    L->d_shg_s = L->d_shu_s = L->d_shd_s = NULL;
+    const size_t rb = (size_t)n_experts * hidden * sizeof(float);
+    CK(cudaMalloc((void **)&L->d_router, rb), "router");
+    CK(cudaMemcpy(L->d_router, router, rb, cudaMemcpyHostToDevice), "router H2D");
+    if (bias) {
+        CK(cudaMalloc((void **)&L->d_bias, (size_t)n_experts * sizeof(float)), "bias");
+        CK(cudaMemcpy(L->d_bias, bias, (size_t)n_experts * sizeof(float),
+                      cudaMemcpyHostToDevice), "bias H2D");
+    }
+    if (sh_inter > 0) {
+        const int g = 128;
+        const size_t ng_h = (size_t)(hidden + g - 1) / g, ng_s = (size_t)(sh_inter + g - 1) / g;
+        const size_t gb = (size_t)sh_inter * ng_h * g, db = (size_t)hidden * ng_s * g;
+        const size_t gs = (size_t)sh_inter * ng_h * 2, ds = (size_t)hidden * ng_s * 2;
+        CK(cudaMalloc((void **)&L->d_shg, gb), "shared gate");
+        CK(cudaMalloc((void **)&L->d_shu, gb), "shared up");
+        CK(cudaMalloc((void **)&L->d_shd, db), "shared down");
+        CK(cudaMalloc((void **)&L->d_shg_s, gs), "shared gate scales");
+        CK(cudaMalloc((void **)&L->d_shu_s, gs), "shared up scales");
+        CK(cudaMalloc((void **)&L->d_shd_s, ds), "shared down scales");
+        CK(cudaMemcpy(L->d_shg, sh_gate, gb, cudaMemcpyHostToDevice), "H2D");
+        CK(cudaMemcpy(L->d_shu, sh_up, gb, cudaMemcpyHostToDevice), "H2D");
+        CK(cudaMemcpy(L->d_shd, sh_down, db, cudaMemcpyHostToDevice), "H2D");
+        CK(cudaMemcpy(L->d_shg_s, sh_gate_s, gs, cudaMemcpyHostToDevice), "H2D");
+        CK(cudaMemcpy(L->d_shu_s, sh_up_s, gs, cudaMemcpyHostToDevice), "H2D");
+        CK(cudaMemcpy(L->d_shd_s, sh_down_s, ds, cudaMemcpyHostToDevice), "H2D");
+    }
+    L->trunk = 1;
+    L->E = n_experts;
+    L->hidden = hidden;
+    L->top_k = top_k;
+    L->renorm = renorm;
+    L->routed_scale = routed_scale;
+    L->si = sh_inter;
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- expert loop ------------------------------------------------------- */
+
+static int layer_ready(int layer, int lat, int inter, wc_layer **out)
+{
+    if (layer < 0 || layer >= WC_MAX_LAYERS || !S.layer[layer].loaded)
+        return fail(WASTE_CUDA_E_NOBANK, "layer %d has no bank in HBM", layer);
+    wc_layer *L = &S.layer[layer];
+    if (lat != L->kb.lat || inter != L->kb.inter)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: call shape %dx%d, bank %dx%d", layer,
+                    lat, inter, L->kb.lat, L->kb.inter);
+    *out = L;
+    return 0;
+}
+
+static int check_route(const wc_layer *L, const int *idx, int n)
+{
+    for (int i = 0; i < n; i++)
+        if (idx[i] < L->kb.first || idx[i] >= L->kb.first + L->kb.n_experts)
+            return fail(WASTE_CUDA_E_ARG, "expert id %d outside the bank", idx[i]);
+    return 0;
+}
+
+static void fill_args(wc_moe_args *a, const wc_layer *L, int T, int K, int E, int si)
+{
+    memset(a, 0, sizeof *a);
+    a->bank = L->kb;
+    a->books = S.d_books;
+    a->T = T;
+    a->K = K;
+    a->E = E;
+    a->si = si;
+    wc_moe_ws_carve(&a->ws, S.d_ws, T, K, E, L->kb.lat, L->kb.inter, si, L->kb.stages);
+}
+
+static int run_experts(int layer, int T, int K, const int *idx, const float *w,
+                       const float *x, float *ysum, int lat, int inter, int act,
+                       int order_by_id)
+{
+    int rc = 0;
+    wc_layer *L = NULL;
+    if (T <= 0 || T > WC_CHUNK_MAX || K <= 0 || K > WC_MAX_TOPK || !idx || !w || !x || !ysum)
+        return fail(WASTE_CUDA_E_ARG, "moe call: bad arguments");
+    if (act != 0) return fail(WASTE_CUDA_E_ARG, "SiTU is not implemented on the device");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = layer_ready(layer, lat, inter, &L))) goto out;
+    if ((rc = check_route(L, idx, T * K))) goto out;
+    if ((rc = ensure_ws(T, K, 1, lat, inter, 0, L->kb.stages))) goto out;
+    const size_t xb = (size_t)T * lat * sizeof(float);
+    memcpy(S.h_x, x, xb);
+    memcpy(S.h_idx, idx, (size_t)T * K * sizeof(int));
+    memcpy(S.h_w, w, (size_t)T * K * sizeof(float));
+    CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    CK(cudaMemcpyAsync(S.d_idx, S.h_idx, (size_t)T * K * sizeof(int), cudaMemcpyHostToDevice,
+                       S.stream), "idx H2D");
+    CK(cudaMemcpyAsync(S.d_w, S.h_w, (size_t)T * K * sizeof(float), cudaMemcpyHostToDevice,
+                       S.stream), "w H2D");
+    wc_moe_args a;
+    fill_args(&a, L, T, K, 1, 0);
+    a.x = S.d_x;
+    a.idx = S.d_idx;
+    a.w = S.d_w;
+    a.out = S.d_out;
+    a.order_by_id = order_by_id;
+    CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
+    CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "ysum D2H");
+    CK(cudaStreamSynchronize(S.stream), "expert loop");
+    memcpy(ysum, S.h_out, xb);
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_moe_experts(const waste_moe_call *c)
+{
+    if (!c) return fail(WASTE_CUDA_E_ARG, "NULL call");
+    return run_experts(c->layer, 1, c->K, c->idx, c->w, c->x, c->ysum, c->lat, c->inter,
+                       c->act, 0);
+}
+
+int waste_cuda_moe_chunk_experts(const waste_moe_chunk_call *c)
+{
+    if (!c) return fail(WASTE_CUDA_E_ARG, "NULL call");
+    return run_experts(c->layer, c->nT, c->K, c->route, c->rw, c->x, c->ysum, c->lat,
+                       c->inter, c->act, 1);
+}
+
+/* ---- whole layer ----------------------------------------------------------- */
+
+static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
+{
+    int rc;
+    if (layer < 0 || layer >= WC_MAX_LAYERS || !S.layer[layer].loaded || !S.layer[layer].trunk)
+        return fail(WASTE_CUDA_E_NOBANK, "layer %d: bank or trunk not loaded", layer);
+    wc_layer *L = &S.layer[layer];
+    if (L->hidden != L->kb.lat)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: router width %d != expert width %d", layer,
+                    L->hidden, L->kb.lat);
+    if (L->kb.first != 0 || L->kb.n_experts != L->E)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: the whole-layer path needs every expert", layer);
+    if ((rc = ensure_ws(1, L->top_k, L->E, L->kb.lat, L->kb.inter, L->si, L->kb.stages)))
+        return rc;
+    fill_args(a, L, 1, L->top_k, L->E, L->si);
+    a->router = L->d_router;
+    a->bias = L->d_bias;
+    a->renorm = L->renorm;
+    a->routed_scale = L->routed_scale;
+    a->shg = L->d_shg; a->shu = L->d_shu; a->shd = L->d_shd;
+    a->shg_s = L->d_shg_s; a->shu_s = L->d_shu_s; a->shd_s = L->d_shd_s;
+    *Lp = L;
+    return 0;
+}
+
+int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out, int *d_idx,
+                             float *d_w, void *stream)
+{
+    int rc = 0;
+    wc_moe_args a;
+    wc_layer *L = NULL;
+    if (!d_x || !d_out || !d_idx || !d_w) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = layer_args(layer, &a, &L))) goto out;
+    a.x = d_x;
+    a.out = d_out;
+    a.idx_out = d_idx;
+    a.w_out = d_w;
+    CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "layer kernels");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, float *weights)
+{
+    int rc = 0;
+    wc_moe_args a;
+    wc_layer *L = NULL;
+    if (!x || !out) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = layer_args(layer, &a, &L))) goto out;
+    const size_t xb = (size_t)L->hidden * sizeof(float);
+    memcpy(S.h_x, x, xb);
+    CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    a.x = S.d_x;
+    a.out = S.d_out;
+    a.idx_out = S.d_idx;
+    a.w_out = S.d_w;
+    CK((cudaError_t)wc_moe_launch(&a, S.stream), "layer kernels");
+    CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "out D2H");
+    if (routed || weights) {
+        CK(cudaMemcpyAsync(S.h_idx, S.d_idx, (size_t)L->top_k * sizeof(int),
+                           cudaMemcpyDeviceToHost, S.stream), "idx D2H");
+        CK(cudaMemcpyAsync(S.h_w, S.d_w, (size_t)L->top_k * sizeof(float),
+                           cudaMemcpyDeviceToHost, S.stream), "w D2H");
+    }
+    CK(cudaStreamSynchronize(S.stream), "moe layer");
+    memcpy(out, S.h_out, xb);
+    if (routed) memcpy(routed, S.h_idx, (size_t)L->top_k * sizeof(int));
+    if (weights) memcpy(weights, S.h_w, (size_t)L->top_k * sizeof(float));
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- single kernels (host buffers) -------------------------------------- */
+
+static int tmp_reserve(size_t bytes)
+{
+    if (bytes <= S.tmp_bytes) return 0;
+    cudaFree(S.d_tmp);
+    S.d_tmp = NULL;
+    S.tmp_bytes = 0;
+    cudaError_t e = cudaMalloc(&S.d_tmp, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "scratch");
+    S.tmp_bytes = bytes;
+    return 0;
+}
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+int waste_cuda_lutb(float *lut, const float *x, int cb_base, int nv, int stages)
+{
+    int rc = 0;
+    if (!lut || !x || nv <= 0 || (stages != 2 && stages != 3) || cb_base < 0)
+        return fail(WASTE_CUDA_E_ARG, "lutb: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.d_books || cb_base + stages > S.n_books) {
+        rc = fail(WASTE_CUDA_E_ARG, "lutb: codebooks not loaded or cb_base out of range");
+        goto out;
+    }
+    const size_t xb = (size_t)nv * 8 * sizeof(float), lb = (size_t)nv * stages * 256 * sizeof(float);
+    if ((rc = tmp_reserve(al256(xb) + lb))) goto out;
+    float *dx = (float *)S.d_tmp, *dl = (float *)((char *)S.d_tmp + al256(xb));
+    CK(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    CK((cudaError_t)wc_lutb_launch(dl, dx, S.d_books, cb_base, nv, stages, S.stream), "lutb");
+    CK(cudaMemcpyAsync(lut, dl, lb, cudaMemcpyDeviceToHost, S.stream), "lut D2H");
+    CK(cudaStreamSynchronize(S.stream), "lutb");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+static int check_mat(int M, int N, int cb_base, int stages)
+{
+    if (M <= 0 || N <= 0 || N % 8 || (stages != 2 && stages != 3) || cb_base < 0)
+        return fail(WASTE_CUDA_E_ARG, "matrix: bad shape");
+    if (!S.d_books || cb_base + stages > S.n_books)
+        return fail(WASTE_CUDA_E_ARG, "codebooks not loaded or cb_base out of range");
+    return 0;
+}
+
+int waste_cuda_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
+                         const float *x, int M, int N, int cb_base, int stages)
+{
+    int rc = 0;
+    if (!y || !idx || !scale || !x) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = check_mat(M, N, cb_base, stages))) goto out;
+    const size_t nrb = (size_t)(M + 63) / 64;
+    const size_t ib = nrb * 64 * (N / 8) * stages, sb = (size_t)M * 2;
+    const size_t xb = (size_t)N * 4, yb = (size_t)M * 4;
+    const size_t pb = wc_matvec_part_floats(1, M, N) * 4;
+    if ((rc = tmp_reserve(al256(ib) + al256(sb) + al256(xb) + al256(yb) + al256(pb)))) goto out;
+    char *p = (char *)S.d_tmp;
+    uint8_t *d_idx = (uint8_t *)p; p += al256(ib);
+    uint16_t *d_sc = (uint16_t *)p; p += al256(sb);
+    float *d_x = (float *)p; p += al256(xb);
+    float *d_y = (float *)p; p += al256(yb);
+    float *d_part = (float *)p;
+    CK(cudaMemcpyAsync(d_idx, idx, ib, cudaMemcpyHostToDevice, S.stream), "idx H2D");
+    CK(cudaMemcpyAsync(d_sc, scale, sb, cudaMemcpyHostToDevice, S.stream), "scale H2D");
+    CK(cudaMemcpyAsync(d_x, x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    static wc_matvec_args a;          /* 4 KiB: kept off the stack */
+    memset(&a, 0, sizeof a);
+    a.G = 1; a.M = M; a.N = N; a.stages = stages; a.cb_base = cb_base;
+    a.idx[0] = d_idx; a.scale[0] = d_sc; a.x[0] = d_x; a.y[0] = d_y;
+    a.books = S.d_books;
+    a.part = d_part;
+    CK((cudaError_t)wc_matvec_launch(&a, S.stream), "matvec");
+    CK(cudaMemcpyAsync(y, d_y, yb, cudaMemcpyDeviceToHost, S.stream), "y D2H");
+    CK(cudaStreamSynchronize(S.stream), "matvec");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx, const uint16_t *const *scale,
+                             const float *const *x, float *const *y, int M, int N,
+                             int cb_base, int stages, void *stream)
+{
+    int rc = 0;
+    if (G <= 0 || G > WC_MAX_G || !idx || !scale || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "matvec_dev: G must be 1..%d, pointers non-NULL", WC_MAX_G);
+    for (int g = 0; g < G; g++)
+        if (((uintptr_t)idx[g] & 15) || ((uintptr_t)x[g] & 15))
+            return fail(WASTE_CUDA_E_ARG, "matrix %d: index or x pointer not 16-byte aligned", g);
+    pthread_mutex_lock(&g_mu);
+    if ((rc = check_mat(M, N, cb_base, stages))) goto out;
+    if ((rc = tmp_reserve(wc_matvec_part_floats(G, M, N) * 4))) goto out;
+    static wc_matvec_args a;
+    memset(&a, 0, sizeof a);
+    a.G = G; a.M = M; a.N = N; a.stages = stages; a.cb_base = cb_base;
+    for (int g = 0; g < G; g++) {
+        a.idx[g] = idx[g]; a.scale[g] = scale[g]; a.x[g] = x[g]; a.y[g] = y[g];
+    }
+    a.books = S.d_books;
+    a.part = (float *)S.d_tmp;
+    CK((cudaError_t)wc_matvec_launch(&a, stream ? stream : (void *)S.stream), "matvec");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale, int M, int N,
+                          int cb_base, int stages)
+{
+    int rc = 0;
+    if (!W || !idx || !scale) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = check_mat(M, N, cb_base, stages))) goto out;
+    const size_t nrb = (size_t)(M + 63) / 64;
+    const size_t ib = nrb * 64 * (N / 8) * stages, sb = (size_t)M * 2, wb = (size_t)M * N * 4;
+    if ((rc = tmp_reserve(al256(ib) + al256(sb) + wb))) goto out;
+    uint8_t *d_idx = (uint8_t *)S.d_tmp;
+    uint16_t *d_sc = (uint16_t *)((char *)S.d_tmp + al256(ib));
+    float *d_W = (float *)((char *)S.d_tmp + al256(ib) + al256(sb));
+    CK(cudaMemcpyAsync(d_idx, idx, ib, cudaMemcpyHostToDevice, S.stream), "idx H2D");
+    CK(cudaMemcpyAsync(d_sc, scale, sb, cudaMemcpyHostToDevice, S.stream), "scale H2D");
+    CK((cudaError_t)wc_dequant_launch(d_W, d_idx, d_sc, M, N, S.d_books, cb_base, stages,
+                                      S.stream), "dequant");
+    CK(cudaMemcpyAsync(W, d_W, wb, cudaMemcpyDeviceToHost, S.stream), "W D2H");
+    CK(cudaStreamSynchronize(S.stream), "dequant");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}

@@ -1,0 +1,97 @@
+/*
+ * wc_launch.h — the shim between the plain-C host layer (waste_cuda.c) and
+ * the CUDA kernels (vq3r_kernels.cu). Plain C structs of device pointers and
+ * sizes; every launcher returns a cudaError_t as int (0 = launched).
+ */
+#ifndef WC_LAUNCH_H
+#define WC_LAUNCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One layer's bank as the kernels see it: E records of rec_bytes each,
+ * all with the same payload offsets (checked at load). */
+typedef struct {
+    const uint8_t *base;
+    size_t rec_bytes;
+    uint32_t gate_off, up_off, down_off, scale_off;
+    int n_experts, first;     /* records held: global ids [first, first+n) */
+    int cb_base;              /* codebook_id shared by every record         */
+    int inter, lat, stages;
+} wc_bank;
+
+/* The workspace a MoE launch writes; sized by wc_moe_ws_bytes. */
+typedef struct {
+    float *p_gu;       /* [T][2][ns_gu][K][inter] partial gate/up sums      */
+    float *p_d;        /* [T][K][ns_d][lat] partial down sums               */
+    float *logits;     /* [T][E]                                            */
+    float *sh_g, *sh_u, *sh_h, *sh_out;   /* shared expert [T][si] / [T][hid] */
+} wc_moe_ws;
+
+typedef struct {
+    wc_bank bank;
+    const float *books;       /* [n_books][256][8] fp32                      */
+    int T, K;
+    const float *x;           /* [T][lat]                                    */
+    const int *idx;           /* [T][K] global expert ids                    */
+    const float *w;           /* [T][K]                                      */
+    float *out;               /* [T][lat]                                    */
+    int order_by_id;          /* 1: per token, add experts in ascending id   */
+    /* router + shared expert; router == NULL means idx/w are given */
+    const float *router, *bias;
+    int E, renorm;
+    float routed_scale;
+    int *idx_out;             /* written by the router when router != NULL   */
+    float *w_out;
+    int si;                   /* shared intermediate; 0 = no shared expert   */
+    const int8_t *shg, *shu, *shd;
+    const uint16_t *shg_s, *shu_s, *shd_s;
+    wc_moe_ws ws;
+} wc_moe_args;
+
+size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
+                        int stages);
+void   wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E, int lat,
+                       int inter, int si, int stages);
+int    wc_moe_launch(const wc_moe_args *a, void *stream);
+
+/* Batched matvec: G <= WC_MAX_G matrices of [M][N]. The pointer tables go
+ * by value in the kernel parameters (4 KiB), so a launch needs no upload
+ * and can be captured in a CUDA graph. */
+#define WC_MAX_G 120
+typedef struct {
+    int G, M, N, stages, cb_base;
+    const uint8_t *idx[WC_MAX_G];
+    const uint16_t *scale[WC_MAX_G];
+    const float *x[WC_MAX_G];
+    float *y[WC_MAX_G];
+    const float *books;
+    float *part;              /* [G][ns][M] workspace                         */
+} wc_matvec_args;
+
+size_t wc_matvec_part_floats(int G, int M, int N);
+int    wc_matvec_launch(const wc_matvec_args *a, void *stream);
+
+int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
+                   int nv, int stages, void *stream);
+int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *scale,
+                      int M, int N, const float *books, int cb_base, int stages,
+                      void *stream);
+
+/* Kernels launched by this library since load. */
+uint64_t wc_launches(void);
+
+/* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
+enum { WC_PH_ROUTER, WC_PH_ROUTE, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
+       WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_COUNT };
+int  wc_prof_enable(int on);
+void wc_prof_read(double *ms, unsigned long long *cnt, int nphase);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,297 @@
+"""Seeded synthetic inputs in the reference's on-disk formats.
+
+Writes what the reference's converter writes, so the same bytes can be fed to
+the reference CPU engine and to this backend:
+
+* expert records — the 48-byte ``waste_expert_hdr`` then gate | up | down
+  index streams in the blocked layout ``[M/64][N/8][64][stages]`` (rows
+  zero-padded to whole blocks), then one f16 scale per output row of gate,
+  up and down, padded to 4 KiB (sqliteai/warp src/waste_format.h:98-132,
+  docs/FORMAT.md:194-208, tools/convert.py:297-312 block_indices,
+  tools/convert.py:457 write_expert_record);
+* codebooks — ``n_books`` books of 256 entries x 8 f16 (codebooks.bin
+  payload, src/waste_format.h:139-150);
+* Q8G trunk rows — int8 rows padded to whole groups of 128 plus one f16
+  scale per group (src/model.c:265-320 layout).
+
+Distributions follow the benchmark configs: codebook entries N(0, 0.02^2),
+indices uniform, x N(0, 1) rounded to bf16 and held in fp32, router rows
+N(0, 1/hidden) so logits are about N(0, 1).
+"""
+from __future__ import annotations
+
+import struct
+import zlib
+from dataclasses import dataclass, field
+
+import numpy as np
+
+MAGIC_EXPERT = 0x50584557
+FMT_VQ3R, FMT_VQ2R = 4, 5
+ALIGN = 4096
+HDR_SIZE = 48
+HDR_FMT = "<IHHBBHHHIIIIIIII"      # waste_expert_hdr, src/waste_format.h:98-132
+VEC_DIM, ENTRIES, BLOCK = 8, 256, 64
+GROUP = 128
+
+
+def f16_bits(a: np.ndarray) -> np.ndarray:
+    return np.asarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 (ties to even), returned as fp32."""
+    u = np.asarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def flush_f16(raw: np.ndarray) -> np.ndarray:
+    """The engine's codebook decode (src/model.c:1278-1287): sign kept,
+    exponent 0 flushed to zero, exponent 31 not special-cased."""
+    h = np.asarray(raw, dtype=np.uint16).astype(np.uint32)
+    sign = (h >> 15) << 31
+    e = (h >> 10) & 0x1F
+    man = h & 0x3FF
+    bits = np.where(e != 0, sign | ((e + 112) << 23) | (man << 13), sign)
+    return bits.astype(np.uint32).view(np.float32)
+
+
+def codebooks(rng: np.random.Generator, n_books: int, std: float = 0.02) -> np.ndarray:
+    """Raw f16 codebook entries [n_books][256][8] as uint16."""
+    return f16_bits(rng.normal(0.0, std, size=(n_books, ENTRIES, VEC_DIM)))
+
+
+def block_indices(idx: np.ndarray) -> np.ndarray:
+    """[M][N/8][stages] uint8 -> blocked bytes [ceil(M/64)][N/8][64][stages]."""
+    M, nv, st = idx.shape
+    nb = (M + BLOCK - 1) // BLOCK
+    pad = np.zeros((nb * BLOCK, nv, st), dtype=np.uint8)
+    pad[:M] = idx
+    return np.ascontiguousarray(pad.reshape(nb, BLOCK, nv, st).transpose(0, 2, 1, 3)).reshape(-1)
+
+
+def unblock_indices(blob: np.ndarray, M: int, N: int, stages: int) -> np.ndarray:
+    nv = N // VEC_DIM
+    nb = (M + BLOCK - 1) // BLOCK
+    a = np.asarray(blob, dtype=np.uint8)[: nb * nv * BLOCK * stages]
+    return a.reshape(nb, nv, BLOCK, stages).transpose(0, 2, 1, 3).reshape(nb * BLOCK, nv, stages)[:M]
+
+
+def random_matrix(rng: np.random.Generator, M: int, N: int, stages: int = 3,
+                  scale_lo: float = 0.5, scale_hi: float = 1.5):
+    """One VQ matrix: blocked index bytes and f16 row scales (uint16)."""
+    idx = random_bytes(rng, M * (N // VEC_DIM) * stages).reshape(M, N // VEC_DIM, stages)
+    scales = f16_bits(rng.uniform(scale_lo, scale_hi, size=M))
+    return block_indices(idx), scales
+
+
+def index_bytes(M: int, N: int, stages: int) -> int:
+    return ((M + BLOCK - 1) // BLOCK) * (N // VEC_DIM) * BLOCK * stages
+
+
+def record_bytes(inter: int, lat: int, stages: int) -> int:
+    body = 2 * index_bytes(inter, lat, stages) + index_bytes(lat, inter, stages)
+    body += 2 * (2 * inter + lat)
+    return ((HDR_SIZE + body + ALIGN - 1) // ALIGN) * ALIGN
+
+
+def expert_record(rng: np.random.Generator, layer: int, eid: int, cb_base: int,
+                  inter: int, lat: int, stages: int = 3,
+                  scale_lo: float = 0.5, scale_hi: float = 1.5) -> bytes:
+    """One expert record: header, gate | up | down indices, scales, padding."""
+    parts, offsets, off = [], [], HDR_SIZE
+    for (M, N) in ((inter, lat), (inter, lat), (lat, inter)):
+        b = random_bytes(rng, index_bytes(M, N, stages))
+        if M % BLOCK:      # padding rows stay zero, as block_indices writes them
+            b = b.reshape((M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK, stages)
+            b[-1, :, M % BLOCK:, :] = 0
+            b = b.reshape(-1)
+        offsets.append(off)
+        parts.append(b.tobytes())
+        off += b.size
+    corr_off = off
+    for M in (inter, inter, lat):
+        s = f16_bits(rng.uniform(scale_lo, scale_hi, size=M)).tobytes()
+        parts.append(s)
+        off += len(s)
+    body = b"".join(parts)
+    total = HDR_SIZE + len(body)
+    blocks = (total + ALIGN - 1) // ALIGN
+    fmt = FMT_VQ3R if stages == 3 else FMT_VQ2R
+    hdr = struct.pack(HDR_FMT, MAGIC_EXPERT, layer, eid, fmt, 0, cb_base, 0, 0, blocks,
+                      offsets[0], offsets[1], offsets[2], corr_off,
+                      zlib.crc32(body) & 0xFFFFFFFF, 0, 0)
+    return hdr + body + b"\0" * (blocks * ALIGN - total)
+
+
+def parse_header(rec: bytes | np.ndarray) -> dict:
+    h = struct.unpack(HDR_FMT, bytes(rec[:HDR_SIZE]))
+    keys = ("magic", "layer", "expert_id", "fmt", "flags", "codebook_id", "lowrank_id",
+            "reserved0", "rec_4k_blocks", "gate_off", "up_off", "down_off",
+            "chan_corr_off", "crc32", "r1", "r2")
+    return dict(zip(keys, h))
+
+
+def q8g(rng: np.random.Generator, rows: int, cols: int, s_lo: float, s_hi: float):
+    """Q8G rows (int8, padded to whole groups) and f16 group scales."""
+    ng = (cols + GROUP - 1) // GROUP
+    q = rng.integers(-127, 128, size=(rows, ng * GROUP), dtype=np.int8)
+    if cols % GROUP:
+        q[:, cols:] = 0
+    s = f16_bits(rng.uniform(s_lo, s_hi, size=(rows, ng)))
+    return q, s
+
+
+@dataclass
+class MoELayer:
+    """One Kimi-Linear-shaped MoE layer, as the engine holds it after load."""
+    layer: int
+    hidden: int
+    inter: int
+    n_experts: int
+    top_k: int
+    renorm: int
+    routed_scale: float
+    stages: int
+    cb_base: int
+    books_raw: np.ndarray            # [n_books][256][8] uint16
+    router: np.ndarray               # [E][hidden] f32
+    bias: np.ndarray | None          # [E] f32
+    bank: np.ndarray                 # E * rec_bytes uint8
+    rec_bytes: int
+    shared_inter: int
+    sh: dict = field(default_factory=dict)   # gate/up/down (q, s)
+
+    @property
+    def books(self) -> np.ndarray:
+        return flush_f16(self.books_raw)
+
+    @property
+    def n_books(self) -> int:
+        return self.books_raw.shape[0]
+
+    def record(self, e: int) -> np.ndarray:
+        return self.bank[e * self.rec_bytes:(e + 1) * self.rec_bytes]
+
+    def matrix(self, e: int, kind: int):
+        """(blocked index bytes, f16 scales, M, N) of gate(0)/up(1)/down(2)."""
+        rec = self.record(e)
+        h = parse_header(rec)
+        M, N = ((self.inter, self.hidden), (self.inter, self.hidden),
+                (self.hidden, self.inter))[kind]
+        off = (h["gate_off"], h["up_off"], h["down_off"])[kind]
+        idx = rec[off:off + index_bytes(M, N, self.stages)]
+        s0 = h["chan_corr_off"] + 2 * (0, self.inter, 2 * self.inter)[kind]
+        sc = rec[s0:s0 + 2 * M].view(np.uint16)
+        return idx, sc, M, N
+
+
+def random_bytes(rng: np.random.Generator, n: int) -> np.ndarray:
+    """n uniform bytes from the generator's raw 64-bit stream (the fastest
+    path numpy offers; PCG64 output is stable across numpy versions)."""
+    return rng.bit_generator.random_raw((n + 7) // 8).view(np.uint8)[:n].copy()
+
+
+def _finish_bank(bank: np.ndarray, rng: np.random.Generator, layer: int, cb_base: int,
+                 inter: int, lat: int, stages: int, scale_lo: float, scale_hi: float):
+    """Turns E rows of random bytes into E valid records in place: zero the
+    index padding rows, write the f16 row scales, zero the 4 KiB tail and
+    write each header with its crc32."""
+    E, rb = bank.shape
+    off = HDR_SIZE
+    offs = []
+    for (M, N) in ((inter, lat), (inter, lat), (lat, inter)):
+        n = index_bytes(M, N, stages)
+        offs.append(off)
+        if M % BLOCK:
+            v = bank[:, off:off + n].reshape(E, (M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK, stages)
+            v[:, -1, :, M % BLOCK:, :] = 0
+        off += n
+    corr = off
+    ns = 2 * inter + lat
+    bank[:, corr:corr + 2 * ns] = f16_bits(rng.uniform(scale_lo, scale_hi, size=(E, ns))).view(np.uint8)
+    end = corr + 2 * ns
+    bank[:, end:] = 0
+    fmt = FMT_VQ3R if stages == 3 else FMT_VQ2R
+    blocks = rb // ALIGN
+    for e in range(E):
+        crc = zlib.crc32(memoryview(bank[e, HDR_SIZE:end])) & 0xFFFFFFFF
+        bank[e, :HDR_SIZE] = np.frombuffer(
+            struct.pack(HDR_FMT, MAGIC_EXPERT, layer, e, fmt, 0, cb_base, 0, 0, blocks,
+                        offs[0], offs[1], offs[2], corr, crc, 0, 0), dtype=np.uint8)
+
+
+def bank(rng: np.random.Generator, layer: int, n_experts: int, cb_base: int, inter: int,
+         lat: int, stages: int = 3, scale_lo: float = 0.5, scale_hi: float = 1.5) -> np.ndarray:
+    """A whole layer's bank: n_experts records, uniform random indices."""
+    rb = record_bytes(inter, lat, stages)
+    b = random_bytes(rng, n_experts * rb).reshape(n_experts, rb)
+    _finish_bank(b, rng, layer, cb_base, inter, lat, stages, scale_lo, scale_hi)
+    return b.reshape(-1)
+
+
+def derive_layer(base: "MoELayer", layer: int, seed: int) -> "MoELayer":
+    """Another layer for benchmarks that need many resident layers: the base
+    bank's index bytes and scales under this layer's headers (the layer
+    field; the crc32 does not cover the header), plus a fresh router and
+    shared expert, so routing differs from layer to layer. Loaded, it is a
+    separate copy in HBM like any other layer."""
+    rng = np.random.default_rng(seed)
+    b = base.bank.copy().reshape(base.n_experts, base.rec_bytes)
+    b[:, 4:6] = np.frombuffer(struct.pack("<H", layer), dtype=np.uint8)
+    router = (rng.standard_normal(base.router.shape, dtype=np.float32)
+              / np.float32(np.sqrt(base.hidden))).astype(np.float32)
+    sh = {}
+    if base.shared_inter:
+        sh["gate"] = q8g(rng, base.shared_inter, base.hidden, 2e-4, 5e-4)
+        sh["up"] = q8g(rng, base.shared_inter, base.hidden, 2e-4, 5e-4)
+        sh["down"] = q8g(rng, base.hidden, base.shared_inter, 2e-4, 5e-4)
+    return MoELayer(layer, base.hidden, base.inter, base.n_experts, base.top_k, base.renorm,
+                    base.routed_scale, base.stages, base.cb_base, base.books_raw, router,
+                    base.bias, b.reshape(-1), base.rec_bytes, base.shared_inter, sh)
+
+
+def moe_layer(seed: int, hidden: int = 2304, inter: int = 1024, n_experts: int = 256,
+              top_k: int = 8, shared_inter: int = 1024, layer: int = 1,
+              routed_scale: float = 2.446, renorm: int = 1, stages: int = 3,
+              with_bias: bool = False, cb_base: int | None = None) -> MoELayer:
+    """Seeded layer at the Kimi-Linear-48B shape by default (hidden 2304,
+    expert inter 1024, 256 experts, top-8, one shared expert, routed scale
+    2.446 with renorm)."""
+    rng = np.random.default_rng(seed)
+    if cb_base is None:
+        cb_base = 3 * stages * (layer - 1) if layer >= 1 else 0
+    n_books = cb_base + 3 * stages
+    books_raw = codebooks(rng, n_books)
+    router = (rng.standard_normal((n_experts, hidden), dtype=np.float32)
+              / np.float32(np.sqrt(hidden))).astype(np.float32)
+    bias = (rng.normal(0, 0.05, size=n_experts).astype(np.float32) if with_bias else None)
+    rb = record_bytes(inter, hidden, stages)
+    bk = bank(rng, layer, n_experts, cb_base, inter, hidden, stages)
+    sh = {}
+    if shared_inter:
+        sh["gate"] = q8g(rng, shared_inter, hidden, 2e-4, 5e-4)
+        sh["up"] = q8g(rng, shared_inter, hidden, 2e-4, 5e-4)
+        sh["down"] = q8g(rng, hidden, shared_inter, 2e-4, 5e-4)
+    return MoELayer(layer, hidden, inter, n_experts, top_k, renorm, routed_scale, stages,
+                    cb_base, books_raw, router, bias, bk, rb, shared_inter, sh)
+
+
+def activations(seed: int, n: int, T: int = 1) -> np.ndarray:
+    """x ~ N(0, 1) rounded to bf16, held in fp32, shape [T][n]."""
+    rng = np.random.default_rng(seed)
+    return bf16_round(rng.standard_normal((T, n), dtype=np.float32))
+
+
+def zipf_routes(seed: int, T: int, E: int, K: int, s: float = 1.1) -> np.ndarray:
+    """[T][K] distinct expert ids per token drawn from Zipf(s) over a seeded
+    permutation of the E ids (prefill routing skew)."""
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(E)
+    p = 1.0 / np.arange(1, E + 1, dtype=np.float64) ** s
+    p /= p.sum()
+    out = np.empty((T, K), dtype=np.int32)
+    for t in range(T):
+        out[t] = perm[rng.choice(E, size=K, replace=False, p=p)]
+    return out
