@@ -89,37 +89,49 @@ struct RowStep<ST, kRowsPerThread> {
     static __device__ __forceinline__ void run(float *, const uint32_t *, const float *) {}
 };
 
-/* Gathers nvv consecutive vector positions for one quarter-block (16 rows).
- * p: the quarter's 16*ST bytes at the first position; consecutive positions
- * are 64*ST bytes apart. L: the table at the first position (ST*256 floats
- * per position). Loads run one position ahead of the arithmetic. */
+/* Streams the index words of one quarter-block (16 rows) over nvv
+ * consecutive vector positions and adds their lookups into acc[16].
+ * begin() issues the loads of the first two positions, so a kernel can call
+ * it before building its table and have the DRAM latency overlap the build;
+ * run() keeps two positions in flight ahead of the arithmetic. Positions are
+ * 64*ST bytes apart; L is the table at the first position. */
 template <int ST>
-__device__ __forceinline__ void gather16(float *acc, const uint8_t *p,
-                                         const float *L, int nvv)
-{
-    constexpr int W = 4 * ST;              /* 32-bit words per position */
-    const size_t stride = (size_t)kBlock * ST;
-    uint32_t cur[W], nxt[W];
-    if (nvv <= 0) return;
+struct Gather16 {
+    static constexpr int W = 4 * ST;       /* 32-bit words per position */
+    uint32_t b0[W], b1[W];
+    const uint8_t *p;
+    int n;
+
+    __device__ __forceinline__ static void load(uint32_t *dst, const uint8_t *src)
+    {
 #pragma unroll
-    for (int i = 0; i < ST; i++) {
-        const uint4 q = ldg16(p + 16 * i);
-        cur[4 * i] = q.x; cur[4 * i + 1] = q.y; cur[4 * i + 2] = q.z; cur[4 * i + 3] = q.w;
-    }
-    for (int v = 0; v < nvv; v++) {
-        if (v + 1 < nvv) {
-            const uint8_t *pn = p + (size_t)(v + 1) * stride;
-#pragma unroll
-            for (int i = 0; i < ST; i++) {
-                const uint4 q = ldg16(pn + 16 * i);
-                nxt[4 * i] = q.x; nxt[4 * i + 1] = q.y; nxt[4 * i + 2] = q.z; nxt[4 * i + 3] = q.w;
-            }
+        for (int i = 0; i < ST; i++) {
+            const uint4 q = ldg16(src + 16 * i);
+            dst[4 * i] = q.x; dst[4 * i + 1] = q.y; dst[4 * i + 2] = q.z; dst[4 * i + 3] = q.w;
         }
-        RowStep<ST, 0>::run(acc, cur, L + (size_t)v * ST * kEntries);
-#pragma unroll
-        for (int i = 0; i < W; i++) cur[i] = nxt[i];
     }
-}
+
+    __device__ __forceinline__ void begin(const uint8_t *p0, int nvv)
+    {
+        p = p0;
+        n = nvv;
+        if (n > 0) load(b0, p);
+        if (n > 1) load(b1, p + (size_t)kBlock * ST);
+    }
+
+    __device__ __forceinline__ void run(float *acc, const float *L)
+    {
+        const size_t stride = (size_t)kBlock * ST;
+        int v = 0;
+        for (; v + 1 < n; v += 2) {
+            RowStep<ST, 0>::run(acc, b0, L + (size_t)v * ST * kEntries);
+            if (v + 2 < n) load(b0, p + (size_t)(v + 2) * stride);
+            RowStep<ST, 0>::run(acc, b1, L + (size_t)(v + 1) * ST * kEntries);
+            if (v + 3 < n) load(b1, p + (size_t)(v + 3) * stride);
+        }
+        if (v < n) RowStep<ST, 0>::run(acc, b0, L + (size_t)v * ST * kEntries);
+    }
+};
 
 __device__ __forceinline__ float silu_ref(float v)
 {

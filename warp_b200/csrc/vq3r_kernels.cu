@@ -101,85 +101,123 @@ extern "C" void wc_prof_read(double *ms, unsigned long long *cnt, int nphase)
 
 namespace {
 
-/* ---- tile geometry ------------------------------------------------------ */
+constexpr int kMaxTopK = 64;
+
+/* ---- tile geometry ------------------------------------------------------
+ * A tile is (group of matrices that share one table slice, slice of vector
+ * positions). Every thread owns 16 rows (a quarter of a 64-row index block)
+ * of one matrix of the group and a contiguous run of the slice's positions
+ * (its lane); lanes of the same rows are summed in shared memory in lane
+ * order. */
 
 struct TileGeom {
-    int nrb;        /* 64-row blocks in the matrix                          */
-    int nrb_tile;   /* blocks per tile                                      */
-    int nchunk;     /* row chunks                                           */
-    int Q;          /* quarter-blocks (threads per lane) per tile           */
-    int nlanes;     /* lanes splitting the slice's positions                */
-    int nv, Vs, ns; /* positions, positions per slice, slices               */
+    int M, nrb;       /* rows per matrix, 64-row blocks per matrix           */
+    int EG, groups;   /* matrices per tile, tiles along the matrix axis      */
+    int nv, Vs, ns;   /* positions, positions per slice, slices              */
+    int Q;            /* quarter-blocks per tile (threads per lane)          */
+    int nlanes;
     int threads;
-    size_t smem;    /* bytes                                                */
+    size_t smem;      /* bytes: xs + max(table, lane reduction)              */
 };
 
-TileGeom make_geom(int M, int N, int Vs, int stages)
+constexpr int kMaxTileRows = 8192;
+
+TileGeom make_geom(int M, int N, int nmat, int Vs, int stages, int target_threads)
 {
     TileGeom g;
+    g.M = M;
     g.nrb = (M + kBlock - 1) / kBlock;
-    g.nrb_tile = g.nrb < 64 ? g.nrb : 64;
-    g.nchunk = (g.nrb + g.nrb_tile - 1) / g.nrb_tile;
-    g.nrb_tile = (g.nrb + g.nchunk - 1) / g.nchunk;
-    g.Q = g.nrb_tile * 4;
+    int eg = kMaxTileRows / (g.nrb * kBlock);
+    if (eg < 1) eg = 1;
+    if (eg > nmat) eg = nmat;
+    g.groups = (nmat + eg - 1) / eg;
+    g.EG = (nmat + g.groups - 1) / g.groups;     /* balance the groups */
+    g.Q = g.EG * g.nrb * 4;
     g.nv = N / kVecDim;
     g.Vs = Vs < g.nv ? Vs : g.nv;
     g.ns = (g.nv + g.Vs - 1) / g.Vs;
-    int nl = 320 / g.Q;
+    int nl = target_threads / g.Q;
     if (nl < 1) nl = 1;
     if (nl > g.Vs) nl = g.Vs;
+    while (g.Q * nl > 512 && nl > 1) nl--;
     g.nlanes = nl;
-    g.threads = g.Q * nl;
+    g.threads = ((g.Q * nl + 31) / 32) * 32;
     const size_t lut = (size_t)g.Vs * stages * kEntries;
-    const size_t red = (size_t)nl * g.nrb_tile * kBlock;
-    g.smem = ((size_t)g.Vs * kVecDim + (lut > red ? lut : red)) * sizeof(float);
+    const size_t red = (size_t)nl * g.EG * g.nrb * kBlock;
+    size_t region = lut > red ? lut : red;
+    if (region < (size_t)2 * g.threads) region = (size_t)2 * g.threads;  /* down prologue */
+    g.smem = ((size_t)g.Vs * kVecDim + region) * sizeof(float);
     return g;
 }
 
-/* The body every gather tile runs once xs (the slice's inputs, Vs*8 floats)
- * is in shared memory. Writes one partial sum per valid row to out[row]. */
+/* Per-thread part of a tile: which rows, which positions, and the index
+ * stream, whose first loads are issued at construction. */
 template <int ST>
-__device__ __forceinline__ void tile_gather(const uint8_t *__restrict__ mat,
-                                            const TileGeom &g, int chunk,
-                                            int slice, const float *xs,
-                                            float *lut, const float *books,
-                                            int cb, int M, float *out)
-{
-    const int v0 = slice * g.Vs;
-    const int nvs = min(g.Vs, g.nv - v0);
-    build_lut_slice<ST>(lut, xs, books, cb, nvs);
-    __syncthreads();
+struct TileThread {
+    int lane, m, rbl, q, vl0, vl1;
+    bool active;
+    Gather16<ST> G;
 
-    const int tid = threadIdx.x;
-    const int lane = tid / g.Q, qi = tid % g.Q;
-    const int rbl = qi >> 2, q = qi & 3;
-    const int rb = chunk * g.nrb_tile + rbl;
-    float acc[kRowsPerThread];
+    /* The matrix this thread's rows belong to (0 .. EG-1). */
+    static __device__ __forceinline__ int matrix_of_thread(const TileGeom &g)
+    {
+        return (threadIdx.x % g.Q) / (g.nrb * 4);
+    }
+
+    /* mat: the index stream of matrix matrix_of_thread(g) (may be anything
+     * when that matrix is past nm: the thread is then inactive). */
+    __device__ __forceinline__ TileThread(const TileGeom &g, int slice, int nm,
+                                          const uint8_t *mat)
+    {
+        const int tid = threadIdx.x;
+        lane = tid / g.Q;
+        const int qi = tid % g.Q;
+        m = qi / (g.nrb * 4);
+        const int rem = qi % (g.nrb * 4);
+        rbl = rem >> 2;
+        q = rem & 3;
+        const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
+        active = lane < g.nlanes && m < nm;
+        vl0 = lane * nvs / g.nlanes;
+        vl1 = (lane + 1) * nvs / g.nlanes;
+        if (active) {
+            const uint8_t *p = mat + (((size_t)rbl * g.nv + v0 + vl0) * kBlock + q * 16) * ST;
+            G.begin(p, vl1 - vl0);
+        } else {
+            G.n = 0;
+        }
+    }
+
+    /* After the table is built: gather, reduce the lanes, and write one
+     * partial sum per valid row to out[m * mstride + row]. */
+    __device__ __forceinline__ void finish(const TileGeom &g, float *lut, float *out,
+                                           size_t mstride, int nm)
+    {
+        float acc[kRowsPerThread];
 #pragma unroll
-    for (int k = 0; k < kRowsPerThread; k++) acc[k] = 0.0f;
-    const bool active = lane < g.nlanes && rbl < g.nrb_tile && rb < g.nrb;
-    if (active) {
-        const int vl0 = lane * nvs / g.nlanes, vl1 = (lane + 1) * nvs / g.nlanes;
-        const uint8_t *p = mat + (((size_t)rb * g.nv + v0 + vl0) * kBlock + q * 16) * ST;
-        gather16<ST>(acc, p, lut + (size_t)vl0 * ST * kEntries, vl1 - vl0);
-    }
-    __syncthreads();             /* the table is dead; reuse it for lanes */
-    float *red = lut;
-    const int R = g.nrb_tile * kBlock;
-    if (active) {
+        for (int k = 0; k < kRowsPerThread; k++) acc[k] = 0.0f;
+        if (active) G.run(acc, lut + (size_t)vl0 * ST * kEntries);
+        __syncthreads();                 /* the table is dead; reuse it */
+        float *red = lut;
+        const int R = g.EG * g.nrb * kBlock;
+        if (active) {
+            float *dst = red + (size_t)lane * R + (size_t)m * g.nrb * kBlock + rbl * kBlock + q * 16;
 #pragma unroll
-        for (int k = 0; k < kRowsPerThread; k++)
-            red[lane * R + rbl * kBlock + q * 16 + k] = acc[k];
+            for (int k = 0; k < kRowsPerThread; k += 4)
+                *reinterpret_cast<float4 *>(dst + k) =
+                    make_float4(acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
+        }
+        __syncthreads();
+        const int rows_pm = g.nrb * kBlock;
+        for (int r = threadIdx.x; r < nm * rows_pm; r += blockDim.x) {
+            const int mm = r / rows_pm, row = r % rows_pm;
+            if (row >= g.M) continue;
+            float s = red[r];
+            for (int l = 1; l < g.nlanes; l++) s += red[(size_t)l * R + r];
+            out[(size_t)mm * mstride + row] = s;
+        }
     }
-    __syncthreads();
-    const int row0 = chunk * g.nrb_tile * kBlock;
-    for (int r = tid; r < R; r += blockDim.x) {
-        if (row0 + r >= M) break;
-        float s = red[r];
-        for (int l = 1; l < g.nlanes; l++) s += red[l * R + r];
-        out[row0 + r] = s;
-    }
-}
+};
 
 /* ---- batched matvec (independent matrices, each with its own x) --------- */
 
@@ -187,20 +225,17 @@ template <int ST>
 __global__ void __launch_bounds__(512)
 matvec_tiles_kernel(TileGeom g, const wc_matvec_args a)
 {
-    const float *books = a.books;
-    const int cb = a.cb_base, M = a.M;
-    float *part = a.part;
     extern __shared__ float smem[];
     float *xs = smem, *lut = smem + g.Vs * kVecDim;
-    const int per_g = g.ns * g.nchunk;
-    const int gi = blockIdx.x / per_g, rem = blockIdx.x % per_g;
-    const int slice = rem / g.nchunk, chunk = rem % g.nchunk;
+    const int gi = blockIdx.x / g.ns, slice = blockIdx.x % g.ns;
+    TileThread<ST> th(g, slice, 1, a.idx[gi]);
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
     const float *xg = a.x[gi] + (size_t)v0 * kVecDim;
     for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xg[i];
     __syncthreads();
-    tile_gather<ST>(a.idx[gi], g, chunk, slice, xs, lut, books, cb, M,
-                    part + ((size_t)gi * g.ns + slice) * M);
+    build_lut_slice<ST>(lut, xs, a.books, a.cb_base, nvs);
+    __syncthreads();
+    th.finish(g, lut, a.part + ((size_t)gi * g.ns + slice) * a.M, 0, 1);
 }
 
 __global__ void matvec_reduce_kernel(int ns, const wc_matvec_args a)
@@ -257,8 +292,6 @@ __global__ void dequant_kernel(float *W, const uint8_t *idx, const uint16_t *sca
 
 /* ---- MoE layer ------------------------------------------------------------ */
 
-/* Warp-per-row dot products: the router (fp32 rows) and the shared expert's
- * gate/up (Q8G rows, src/model.c:265-320 layout), all reading x. */
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
@@ -266,272 +299,366 @@ __device__ __forceinline__ float warp_sum(float v)
     return v;
 }
 
-__device__ float dot_f32_row(const float *__restrict__ w, const float *__restrict__ x,
-                             int n, int lane)
+/* fp32 row . x (x in shared memory), all of the lane's loads issued first. */
+__device__ __forceinline__ float dot_f32_row(const float *__restrict__ w, const float *xs,
+                                             int n, int lane)
 {
+    constexpr int U = 8;
     float acc = 0.0f;
-    if ((n & 3) == 0) {
-        const float4 *w4 = reinterpret_cast<const float4 *>(w);
-        const float4 *x4 = reinterpret_cast<const float4 *>(x);
-        for (int i = lane; i < n / 4; i += 32) {
-            const float4 a = __ldg(w4 + i), b = __ldg(x4 + i);
-            acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc);
-            acc = fmaf(a.z, b.z, acc); acc = fmaf(a.w, b.w, acc);
-        }
-    } else {
-        for (int i = lane; i < n; i += 32) acc = fmaf(w[i], x[i], acc);
-    }
-    return warp_sum(acc);
-}
-
-/* Q8G row: 16-byte chunks; chunk c covers inputs [16c, 16c+16) of group
- * c*16/128. Inputs at or past n (a partly filled last group) are skipped. */
-__device__ float dot_q8g_row(const int8_t *__restrict__ row,
-                             const uint16_t *__restrict__ ws,
-                             const float *__restrict__ x, int n, int lane)
-{
-    float acc = 0.0f;
-    const int nchunk = (n + 15) / 16;
-    for (int c = lane; c < nchunk; c += 32) {
-        const uint4 q = ldg16(row + (size_t)c * 16);
-        const uint32_t wv[4] = { q.x, q.y, q.z, q.w };
-        float part = 0.0f;
-        const int base = c * 16;
+    const int n4 = n >> 2;
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    for (int base = 0; base < n4; base += 32 * U) {
+        float4 a[U];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            if (base + i < n) {
-                const int8_t b = (int8_t)((wv[i >> 2] >> (8 * (i & 3))) & 0xff);
-                part = fmaf((float)b, x[base + i], part);
+        for (int u = 0; u < U; u++) {
+            const int i = base + u * 32 + lane;
+            a[u] = i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = base + u * 32 + lane;
+            if (i < n4) {
+                const float4 b = x4[i];
+                acc = fmaf(a[u].x, b.x, acc); acc = fmaf(a[u].y, b.y, acc);
+                acc = fmaf(a[u].z, b.z, acc); acc = fmaf(a[u].w, b.w, acc);
             }
         }
-        acc = fmaf(f16_keep(ws[base / 128]), part, acc);
     }
     return warp_sum(acc);
 }
 
-__global__ void router_shared_kernel(wc_moe_args a)
+/* Q8G row (src/model.c:265-320 layout: int8 rows padded to whole groups of
+ * 128, one f16 scale per group) . x (x in shared memory). Chunk c is inputs
+ * [16c, 16c+16) of group c/8; inputs at or past n are skipped. */
+__device__ __forceinline__ float dot_q8g_row(const int8_t *__restrict__ row,
+                                             const uint16_t *__restrict__ ws,
+                                             const float *xs, int n, int lane)
 {
-    const int warps = blockDim.x / 32;
-    const int row = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x % 32;
+    constexpr int U = 6;
+    float acc = 0.0f;
+    const int nchunk = (n + 15) / 16;
+    for (int base = 0; base < nchunk; base += 32 * U) {
+        uint4 q[U];
+        float sc[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = base + u * 32 + lane;
+            q[u] = c < nchunk ? ldg16(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+            sc[u] = c < nchunk ? f16_keep(__ldg(ws + (c >> 3))) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = base + u * 32 + lane;
+            if (c >= nchunk) continue;
+            const uint32_t wv[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
+            const int b0 = c * 16;
+            float part = 0.0f;
+            if (b0 + 16 <= n) {
+                const float4 *x4 = reinterpret_cast<const float4 *>(xs + b0);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float4 xv = x4[k];
+                    const uint32_t wd = wv[k];
+                    part = fmaf((float)(int8_t)(wd & 0xff), xv.x, part);
+                    part = fmaf((float)(int8_t)((wd >> 8) & 0xff), xv.y, part);
+                    part = fmaf((float)(int8_t)((wd >> 16) & 0xff), xv.z, part);
+                    part = fmaf((float)(int8_t)(wd >> 24), xv.w, part);
+                }
+            } else {
+                for (int i = 0; b0 + i < n; i++)
+                    part = fmaf((float)(int8_t)((wv[i >> 2] >> (8 * (i & 3))) & 0xff),
+                                xs[b0 + i], part);
+            }
+            acc = fmaf(sc[u], part, acc);
+        }
+    }
+    return warp_sum(acc);
+}
+
+/* Router logits (fp32 rows) and the shared expert's gate/up (Q8G rows), one
+ * warp per output row, x staged in shared memory. */
+__global__ void __launch_bounds__(256) router_shared_kernel(wc_moe_args a)
+{
+    extern __shared__ float xs[];
     const int lat = a.bank.lat;
+    const int warps = blockDim.x / 32;
     const int per_t = a.E + 2 * a.si;
-    const int t = row / per_t, r = row % per_t;
-    if (t >= a.T) return;
+    const int t = blockIdx.y;                   /* grid: (row blocks, tokens) */
+    const int r = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x % 32;
     const float *x = a.x + (size_t)t * lat;
+    for (int i = threadIdx.x; i < lat; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    if (r >= per_t) return;
     if (r < a.E) {
-        const float v = dot_f32_row(a.router + (size_t)r * lat, x, lat, lane);
+        const float v = dot_f32_row(a.router + (size_t)r * lat, xs, lat, lane);
         if (lane == 0) a.ws.logits[(size_t)t * a.E + r] = v;
         return;
     }
     const int rr = r - a.E;
     const int kind = rr / a.si, o = rr % a.si;
     const int ng = (lat + 127) / 128;
-    const size_t rowbytes = (size_t)ng * 128;
     const int8_t *W = kind ? a.shu : a.shg;
     const uint16_t *S = kind ? a.shu_s : a.shg_s;
-    const float v = dot_q8g_row(W + (size_t)o * rowbytes, S + (size_t)o * ng, x, lat, lane);
+    const float v = dot_q8g_row(W + (size_t)o * ng * 128, S + (size_t)o * ng, xs, lat, lane);
     if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = v;
 }
 
-/* Routing, src/model.c:2724-2747: score = 1/(1+expf(-logit)); K rounds of
- * argmax over score + bias (0.0f when there is no bias) with a strict >,
- * so the lowest index wins a tie and a NaN never wins; w = score[best];
- * optional renorm by (sum + 1e-20f) in j order; times routed_scale.
- * One warp per token. Also forms the shared expert's SiLU(g)*u. */
-__global__ void route_kernel(wc_moe_args a)
+/* Routing, src/model.c:2724-2747, one block per token. Warp 0 holds the E
+ * scores in registers (score = 1/(1+expf(-logit)), plus the bias, or plus
+ * 0.0f when there is none) and runs K rounds of argmax: within a lane the
+ * ids ascend and the comparison is a strict >, across lanes the larger
+ * value wins and equal values go to the lower id — so the lowest id wins a
+ * tie and a NaN never wins, exactly as the sequential scan from -1e30f.
+ * w = score[best]; renorm by (sum + 1e-20f) in j order; times routed_scale.
+ * The other warps form the shared expert's SiLU(g)*u meanwhile. */
+constexpr int kMaxPerLane = 32;      /* E <= 1024 */
+
+__global__ void __launch_bounds__(256) route_kernel(wc_moe_args a)
 {
-    extern __shared__ float sm[];
     const int t = blockIdx.x;
-    float *score = sm;
     const int E = a.E, K = a.K;
-    const float *lg = a.ws.logits + (size_t)t * E;
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-        score[e] = 1.0f / (1.0f + expf(-lg[e]));
-    if (a.si > 0) {
-        for (int i = threadIdx.x; i < a.si; i += blockDim.x) {
+    if (threadIdx.x >= 32) {
+        for (int i = threadIdx.x - 32; i < a.si; i += blockDim.x - 32) {
             const size_t o = (size_t)t * a.si + i;
             a.ws.sh_h[o] = silu_ref(a.ws.sh_g[o]) * a.ws.sh_u[o];
         }
+        return;
     }
-    __syncthreads();
-    if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
-    __shared__ int chosen[64];
-    __shared__ float wsel[64];
-    for (int j = 0; j < K; j++) {
-        float bv = -1e30f;
-        int best = -1;
-        for (int e = lane; e < E; e += 32) {
-            bool taken = false;
-            for (int p = 0; p < j; p++) taken |= (chosen[p] == e);
-            if (taken) continue;
-            const float v = score[e] + (a.bias ? a.bias[e] : 0.0f);
-            if (v > bv) { bv = v; best = e; }   /* e ascending per lane */
+    const float *lg = a.ws.logits + (size_t)t * E;
+    float sc[kMaxPerLane], v[kMaxPerLane];
+    uint32_t live = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxPerLane; k++) {
+        const int e = lane + 32 * k;
+        sc[k] = 0.0f;
+        v[k] = 0.0f;
+        if (e < E) {
+            sc[k] = 1.0f / (1.0f + expf(-lg[e]));
+            v[k] = sc[k] + (a.bias ? a.bias[e] : 0.0f);
+            live |= 1u << k;
         }
-        /* combine lanes: larger value wins; equal values -> lower index */
+    }
+    float wsel = 0.0f, wsum = 0.0f;
+    int mine = -1;                      /* lane j keeps the j-th choice */
+    for (int j = 0; j < K; j++) {
+        float bv = -1e30f, bs = 0.0f;
+        int best = -1;
+#pragma unroll
+        for (int k = 0; k < kMaxPerLane; k++)
+            if (((live >> k) & 1) && v[k] > bv) { bv = v[k]; bs = sc[k]; best = lane + 32 * k; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
             const int oi = __shfl_xor_sync(0xffffffffu, best, o);
-            const bool take = (oi >= 0) && (best < 0 || ov > bv || (ov == bv && oi < best));
-            if (take) { bv = ov; best = oi; }
+            if (oi >= 0 && (best < 0 || ov > bv || (ov == bv && oi < best))) {
+                bv = ov; bs = os; best = oi;
+            }
         }
-        if (lane == 0) {
-            chosen[j] = best;
-            wsel[j] = best >= 0 ? score[best] : 0.0f;
-        }
-        __syncwarp();
+        if (best >= 0 && (best & 31) == lane) live &= ~(1u << (best >> 5));
+        if (lane == j) { mine = best; wsel = best >= 0 ? bs : 0.0f; }
+        wsum += best >= 0 ? bs : 0.0f;   /* same j-order sum in every lane */
     }
-    if (lane == 0) {
-        if (a.renorm && K > 1) {
-            float s = 0;
-            for (int j = 0; j < K; j++) s += wsel[j];
-            for (int j = 0; j < K; j++) wsel[j] /= (s + 1e-20f);
-        }
-        for (int j = 0; j < K; j++) {
-            a.idx_out[(size_t)t * K + j] = chosen[j];
-            a.w_out[(size_t)t * K + j] = wsel[j] * a.routed_scale;
-        }
+    if (lane < K) {
+        float w = wsel;
+        if (a.renorm && K > 1) w /= (wsum + 1e-20f);
+        a.idx_out[(size_t)t * K + lane] = mine;
+        a.w_out[(size_t)t * K + lane] = w * a.routed_scale;
     }
 }
 
-struct MoeGeom {
-    TileGeom gu, d;
-    int gu_tiles, d_tiles, sh_blocks;
-};
-
-/* gate/up tiles: (t, kind, slice, j, chunk). */
-template <int ST>
-__global__ void __launch_bounds__(512)
-gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
+/* The record of routed expert j of token t (ids are global; a bank may hold
+ * a contiguous subset starting at `first`). */
+__device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const int *idx,
+                                                     int K, int t, int j)
 {
-    extern __shared__ float smem[];
-    float *xs = smem, *lut = smem + g.Vs * kVecDim;
-    int b = blockIdx.x;
-    const int chunk = b % g.nchunk; b /= g.nchunk;
-    const int j = b % a.K; b /= a.K;
-    const int slice = b % g.ns; b /= g.ns;
-    const int kind = b % 2; const int t = b / 2;
+    return bk.base + (size_t)(idx[(size_t)t * K + j] - bk.first) * bk.rec_bytes;
+}
+
+/* The shared expert's down rows ([lat][si] Q8G) for SiLU(g)*u of token t:
+ * one warp per row, block `b` of the token's ceil(lat / warps) blocks. */
+__device__ __forceinline__ void shared_down_rows(const wc_moe_args &a, float *hs, int b)
+{
     const wc_bank &bk = a.bank;
-    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
-    const float *xt = a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim;
-    for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xt[i];
+    const int warps = blockDim.x / 32;
+    const int per_tok = (bk.lat + warps - 1) / warps;
+    const int t = b / per_tok;
+    if (t >= a.T) return;
+    for (int i = threadIdx.x; i < a.si; i += blockDim.x) hs[i] = a.ws.sh_h[(size_t)t * a.si + i];
     __syncthreads();
-    const int e = idx[(size_t)t * a.K + j] - bk.first;
-    const uint8_t *rec = bk.base + (size_t)e * bk.rec_bytes;
-    const uint8_t *mat = rec + (kind ? bk.up_off : bk.gate_off);
-    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j) * bk.inter;
-    tile_gather<ST>(mat, g, chunk, slice, xs, lut, a.books, bk.cb_base + kind * ST,
-                    bk.inter, out);
+    const int o = (b % per_tok) * warps + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (o >= bk.lat) return;
+    const int ng = (a.si + 127) / 128;
+    const float v = dot_q8g_row(a.shd + (size_t)o * ng * 128, a.shd_s + (size_t)o * ng,
+                                hs, a.si, lane);
+    if (lane == 0) a.ws.sh_out[(size_t)t * bk.lat + o] = v;
 }
 
-/* down tiles: (t, j, slice, chunk) with the SiLU(g)*u prologue; then the
- * shared expert's down rows (warp per row) in the trailing blocks. */
+/* gate/up: tile = (token, kind, slice, expert group). Every tile's table is
+ * shared by the rows of all the experts in its group. Blocks past gu_tiles
+ * run the shared expert's down rows (routing, and so SiLU(g)*u of the
+ * shared expert, is done by then). */
 template <int ST>
 __global__ void __launch_bounds__(512)
-down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, const int *idx)
+gateup_kernel(wc_moe_args a, TileGeom g, int gu_tiles, const int *idx)
 {
     extern __shared__ float smem[];
-    const wc_bank &bk = a.bank;
-    if ((int)blockIdx.x >= d_tiles) {
-        /* shared expert down: [lat][si] Q8G, input sh_h */
-        const int warps = blockDim.x / 32;
-        const int row = (blockIdx.x - d_tiles) * warps + threadIdx.x / 32;
-        const int lane = threadIdx.x % 32;
-        const int t = row / bk.lat, o = row % bk.lat;
-        if (t >= a.T) return;
-        const int ng = (a.si + 127) / 128;
-        const size_t rowbytes = (size_t)ng * 128;
-        const float v = dot_q8g_row(a.shd + (size_t)o * rowbytes, a.shd_s + (size_t)o * ng,
-                                    a.ws.sh_h + (size_t)t * a.si, a.si, lane);
-        if (lane == 0) a.ws.sh_out[(size_t)t * bk.lat + o] = v;
+    if ((int)blockIdx.x >= gu_tiles) {
+        shared_down_rows(a, smem, blockIdx.x - gu_tiles);
         return;
     }
     float *xs = smem, *lut = smem + g.Vs * kVecDim;
     int b = blockIdx.x;
-    const int chunk = b % g.nchunk; b /= g.nchunk;
+    const int grp = b % g.groups; b /= g.groups;
+    const int slice = b % g.ns; b /= g.ns;
+    const int kind = b % 2; const int t = b / 2;
+    const wc_bank &bk = a.bank;
+    const int j0 = grp * g.EG;
+    const int nm = min(g.EG, a.K - j0);
+    /* this thread's matrix, then its first index loads */
+    const int m = min(TileThread<ST>::matrix_of_thread(g), nm - 1);
+    const uint8_t *mat = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off);
+    TileThread<ST> th(g, slice, nm, mat);
+    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
+    const float *xt = a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim;
+    for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xt[i];
+    __syncthreads();
+    build_lut_slice<ST>(lut, xs, a.books, bk.cb_base + kind * ST, nvs);
+    __syncthreads();
+    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
+    th.finish(g, lut, out, bk.inter, nm);
+}
+
+/* down: tile = (token, expert j, slice), h = SiLU(g)*u formed from the
+ * gate/up partial sums for the slice's inputs; then the shared expert's down
+ * rows (warp per row) in the trailing blocks. */
+template <int ST>
+__global__ void __launch_bounds__(512, 1)
+down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, const int *idx)
+{
+    extern __shared__ float smem[];
+    const wc_bank &bk = a.bank;
+    (void)d_tiles;
+    float *xs = smem, *lut = smem + g.Vs * kVecDim;
+    int b = blockIdx.x;
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
+    const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
+    TileThread<ST> th(g, slice, 1, rec + bk.down_off);
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
-    const int e = idx[(size_t)t * a.K + j] - bk.first;
-    const uint8_t *rec = bk.base + (size_t)e * bk.rec_bytes;
     const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
     const int inter = bk.inter;
-    const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * a.K * inter + (size_t)j * inter;
-    const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * a.K * inter + (size_t)j * inter;
     const size_t sstride = (size_t)a.K * inter;
-    for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) {
+    const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * sstride + (size_t)j * inter;
+    const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * sstride + (size_t)j * inter;
+    /* Sum the gate/up slices for the slice's inputs with the whole block:
+     * part p of P adds slices p, p+P, ...; parts are then added in order. */
+    const int nin = nvs * kVecDim;
+    const int P = max(1, (int)blockDim.x / nin);
+    float *red2 = lut;                         /* [P][2][nin], before the table */
+    if ((int)threadIdx.x < P * nin) {
+        const int i = threadIdx.x % nin, p = threadIdx.x / nin;
         const int n = v0 * kVecDim + i;
         float sg = 0.0f, su = 0.0f;
-        for (int s = 0; s < gu.ns; s++) {
-            sg += pg[(size_t)s * sstride + n];
-            su += pu[(size_t)s * sstride + n];
+        for (int s2 = p; s2 < gu.ns; s2 += P) {
+            sg += pg[(size_t)s2 * sstride + n];
+            su += pu[(size_t)s2 * sstride + n];
+        }
+        red2[(p * 2 + 0) * nin + i] = sg;
+        red2[(p * 2 + 1) * nin + i] = su;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < nin) {
+        const int i = threadIdx.x, n = v0 * kVecDim + i;
+        float sg = 0.0f, su = 0.0f;
+        for (int p = 0; p < P; p++) {
+            sg += red2[(p * 2 + 0) * nin + i];
+            su += red2[(p * 2 + 1) * nin + i];
         }
         const float gv = sg * f16_keep(sc[n]);
         const float uv = su * f16_keep(sc[inter + n]);
         xs[i] = silu_ref(gv) * uv;
     }
     __syncthreads();
+    build_lut_slice<ST>(lut, xs, a.books, bk.cb_base + 2 * ST, nvs);
+    __syncthreads();
     float *out = a.ws.p_d + (((size_t)t * a.K + j) * g.ns + slice) * bk.lat;
-    tile_gather<ST>(rec + bk.down_off, g, chunk, slice, xs, lut, a.books,
-                    bk.cb_base + 2 * ST, bk.lat, out);
+    th.finish(g, lut, out, 0, 1);
 }
 
 /* out[t][i] = sum_j w[j] * (f16(scale_down_j[i]) * sum_s P_d[t][j][s][i]),
  * j in router order (src/model.c:2908-2909) — or in ascending expert id
- * when order_by_id (moe_chunk, src/model.c:3632-3656) — then + shared. */
-__global__ void combine_kernel(wc_moe_args a, TileGeom g, const int *idx,
-                               const float *w)
+ * when order_by_id (moe_chunk, src/model.c:3632-3656) — then + shared.
+ * Block: 32 outputs x 8 expert lanes. */
+__global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
+                                                      const int *idx, const float *w)
 {
+    __shared__ float accj[kMaxTopK][32];
+    __shared__ int order[kMaxTopK];
     const wc_bank &bk = a.bank;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    const int t = blockIdx.y;
-    if (i >= bk.lat) return;
-    const int K = a.K;
+    const int t = blockIdx.y, K = a.K;
+    const int il = threadIdx.x % 32, jl = threadIdx.x / 32;
+    const int i = blockIdx.x * 32 + il;
     const int *it = idx + (size_t)t * K;
+    for (int j = jl; j < K; j += blockDim.x / 32) {
+        float s = 0.0f;
+        if (i < bk.lat) {
+            const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
+            for (int k = 0; k < g.ns; k++) s += p[(size_t)k * bk.lat];
+            const uint16_t *sc = reinterpret_cast<const uint16_t *>(
+                bk.base + (size_t)(it[j] - bk.first) * bk.rec_bytes + bk.scale_off) + 2 * bk.inter;
+            s *= f16_keep(sc[i]);
+        }
+        accj[j][il] = s;
+    }
+    if (threadIdx.x == 0) {
+        int last = -1;
+        for (int n = 0; n < K; n++) {
+            int jj = n;
+            if (a.order_by_id) {          /* next larger id, first j routed to it */
+                jj = -1;
+                for (int q = 0; q < K; q++)
+                    if (it[q] > last && (jj < 0 || it[q] < it[jj])) jj = q;
+                if (jj >= 0) last = it[jj];
+            }
+            order[n] = jj;
+        }
+    }
+    __syncthreads();
+    if (jl != 0 || i >= bk.lat) return;
     const float *wt = w + (size_t)t * K;
     float y = 0.0f;
-    int last = -1;
     for (int n = 0; n < K; n++) {
-        int j = n;
-        if (a.order_by_id) {          /* next larger id after `last` */
-            int bj = -1;
-            for (int q = 0; q < K; q++)
-                if (it[q] > last && (bj < 0 || it[q] < it[bj])) bj = q;
-            if (bj < 0) break;
-            j = bj;
-            last = it[bj];
-            /* the reference takes the first j routed to this id */
-            for (int q = 0; q < bj; q++) if (it[q] == it[bj]) { j = q; break; }
-        }
+        const int j = order[n];
+        if (j < 0) break;
         const float wj = wt[j];
         if (a.order_by_id && wj == 0.0f) continue;
-        const int e = it[j] - bk.first;
-        const uint16_t *sc = reinterpret_cast<const uint16_t *>(
-            bk.base + (size_t)e * bk.rec_bytes + bk.scale_off) + 2 * bk.inter;
-        const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
-        float s = 0.0f;
-        for (int k = 0; k < g.ns; k++) s += p[(size_t)k * bk.lat];
-        const float acc = s * f16_keep(sc[i]);
-        y = __fadd_rn(y, __fmul_rn(wj, acc));
+        y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
     }
     if (a.si > 0) y = __fadd_rn(y, a.ws.sh_out[(size_t)t * bk.lat + i]);
     a.out[(size_t)t * bk.lat + i] = y;
 }
 
-constexpr int kVsGateUp = 12;
+constexpr int kVsGateUp = 4;
 constexpr int kVsDown = 8;
+
+struct MoeGeom {
+    TileGeom gu, d;
+    int gu_tiles, d_tiles, sh_blocks;
+};
 
 MoeGeom moe_geom(const wc_moe_args *a)
 {
     MoeGeom m;
     const wc_bank &b = a->bank;
-    m.gu = make_geom(b.inter, b.lat, kVsGateUp, b.stages);
-    m.d = make_geom(b.lat, b.inter, kVsDown, b.stages);
-    m.gu_tiles = a->T * 2 * m.gu.ns * a->K * m.gu.nchunk;
-    m.d_tiles = a->T * a->K * m.d.ns * m.d.nchunk;
-    const int warps = m.d.threads / 32;
-    m.sh_blocks = a->si > 0 ? (a->T * b.lat + warps - 1) / warps : 0;
+    m.gu = make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512);
+    m.d = make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 512);
+    m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
+    m.d_tiles = a->T * a->K * m.d.ns;
+    const int warps = m.gu.threads / 32;
+    m.sh_blocks = a->si > 0 ? a->T * ((b.lat + warps - 1) / warps) : 0;
     return m;
 }
 
@@ -539,34 +666,35 @@ template <int ST>
 int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
 {
     const MoeGeom m = moe_geom(a);
-    if (m.d.threads < 32 || m.d.threads % 32) { /* shared rows use whole warps */ }
     const int *idx = a->idx;
     const float *w = a->w;
     if (a->router) {
-        const int rows = a->T * (a->E + 2 * a->si);
+        const dim3 rg((a->E + 2 * a->si + 7) / 8, a->T);
         int pe = prof_begin(WC_PH_ROUTER, s);
-        router_shared_kernel<<<(rows + 7) / 8, 256, 0, s>>>(*a);
+        router_shared_kernel<<<rg, 256, (size_t)a->bank.lat * sizeof(float), s>>>(*a);
         prof_end(pe, s);
         pe = prof_begin(WC_PH_ROUTE, s);
-        route_kernel<<<a->T, 256, (size_t)a->E * sizeof(float), s>>>(*a);
+        route_kernel<<<a->T, 256, 0, s>>>(*a);
         prof_end(pe, s);
         g_launches += 2;
         idx = a->idx_out;
         w = a->w_out;
     }
+    size_t gsmem = m.gu.smem;
+    const size_t shsmem = (size_t)a->si * sizeof(float);
+    if (a->router && shsmem > gsmem) gsmem = shsmem;
     cudaFuncSetAttribute(gateup_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)m.gu.smem);
+                         (int)gsmem);
     int pe = prof_begin(WC_PH_GATEUP, s);
-    gateup_kernel<ST><<<m.gu_tiles, m.gu.threads, m.gu.smem, s>>>(*a, m.gu, idx);
+    gateup_kernel<ST><<<m.gu_tiles + (a->router ? m.sh_blocks : 0), m.gu.threads, gsmem, s>>>(
+        *a, m.gu, m.gu_tiles, idx);
     prof_end(pe, s);
     cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)m.d.smem);
-    const int dthreads = ((m.d.threads + 31) / 32) * 32;
     pe = prof_begin(WC_PH_DOWN, s);
-    down_kernel<ST><<<m.d_tiles + (a->router ? m.sh_blocks : 0), dthreads, m.d.smem, s>>>(
-        *a, m.gu, m.d, m.d_tiles, idx);
+    down_kernel<ST><<<m.d_tiles, m.d.threads, m.d.smem, s>>>(*a, m.gu, m.d, m.d_tiles, idx);
     prof_end(pe, s);
-    dim3 cg((a->bank.lat + 255) / 256, a->T);
+    dim3 cg((a->bank.lat + 31) / 32, a->T);
     wc_moe_args ca = *a;
     if (!a->router) ca.si = 0;
     pe = prof_begin(WC_PH_COMBINE, s);
@@ -581,8 +709,8 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
 extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
                                    int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, kVsGateUp, stages);
-    const TileGeom d = make_geom(lat, inter, kVsDown, stages);
+    const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
+    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 512);
     size_t n = 0;
     n += (size_t)T * 2 * gu.ns * K * inter;
     n += (size_t)T * K * d.ns * lat;
@@ -594,8 +722,8 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
                                 int lat, int inter, int si, int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, kVsGateUp, stages);
-    const TileGeom d = make_geom(lat, inter, kVsDown, stages);
+    const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
+    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 512);
     float *p = base;
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
     ws->p_d = p; p += (size_t)T * K * d.ns * lat;
@@ -620,17 +748,17 @@ static constexpr int kVsMatvec = 16;
 
 extern "C" size_t wc_matvec_part_floats(int G, int M, int N)
 {
-    const TileGeom g = make_geom(M, N, kVsMatvec, 3);
+    const TileGeom g = make_geom(M, N, 1, kVsMatvec, 3, 512);
     return (size_t)G * g.ns * M;
 }
 
 template <int ST>
 static int matvec_launch_st(const wc_matvec_args *a, cudaStream_t s)
 {
-    const TileGeom g = make_geom(a->M, a->N, kVsMatvec, ST);
+    const TileGeom g = make_geom(a->M, a->N, 1, kVsMatvec, ST, 512);
     cudaFuncSetAttribute(matvec_tiles_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)g.smem);
-    const int tiles = a->G * g.ns * g.nchunk;
+    const int tiles = a->G * g.ns;
     int pe = prof_begin(WC_PH_MATVEC, s);
     matvec_tiles_kernel<ST><<<tiles, g.threads, g.smem, s>>>(g, *a);
     prof_end(pe, s);
