@@ -336,10 +336,14 @@ def run_warp(args):
            "h2d_bytes_per_step": nL * HIDDEN * 4,
            "d2h_bytes_per_step": nL * (HIDDEN * 4 + 2 * TOPK * 4)}
 
-    # ---- per-kernel times (phase timers) over K direct steps
+    # ---- per-kernel times (phase timers): a GPU-side sleep holds the stream
+    # while the host queues the launches, so each event pair brackets kernel
+    # time rather than host launch gaps. Kept under the launch-queue depth.
+    prof_steps = max(1, min(args.steps, 700 // (12 * nL) or 1))
     wb.profile(True)
     with torch.cuda.stream(s):
-        for k in range(args.steps):
+        torch.cuda._sleep(int(2e6 * nL * prof_steps))      # ~1 ms per layer-call at 2 GHz
+        for k in range(prof_steps):
             step_direct(k % ntok)
     torch.cuda.synchronize()
     ph = wb.profile_read()
@@ -368,12 +372,17 @@ def run_warp(args):
     for _ in range(3):
         wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
     torch.cuda.synchronize()
-    wb.profile(True)
     m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     m0.record(s)
     for _ in range(mv_iters):
         wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
     m1.record(s)
+    torch.cuda.synchronize()
+    wb.profile(True)
+    with torch.cuda.stream(s):
+        torch.cuda._sleep(int(1e6))
+        for _ in range(10):
+            wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
     torch.cuda.synchronize()
     mph = wb.profile_read()
     wb.profile(False)

@@ -290,7 +290,27 @@ __global__ void dequant_kernel(float *W, const uint8_t *idx, const uint16_t *sca
                          __fmul_rn(rec[6], sc), __fmul_rn(rec[7], sc));
 }
 
-/* ---- MoE layer ------------------------------------------------------------ */
+/* ---- MoE layer ------------------------------------------------------------
+ * Four launches per layer, chained with programmatic dependent launch (PDL)
+ * so that each kernel's routing-independent prologue overlaps its
+ * predecessor:
+ *   1. router_kernel   router logits (fp32 rows, split in quarters) and the
+ *                      shared expert's gate/up (Q8G rows); the last block to
+ *                      finish runs the top-K and the shared SiLU(g)*u;
+ *   2. gateup_kernel   [before the wait] stage x and build the gate or up
+ *                      table slice — it depends on x and the codebooks only;
+ *                      [after] gather the routed experts' gate/up rows, then
+ *                      a share of the shared expert's down rows;
+ *   3. down_kernel     [before] issue the routed expert's down index loads;
+ *                      [after] SiLU(g)*u from the gate/up partials, table,
+ *                      gather;
+ *   4. combine_kernel  [before] row scales; [after] slice sums, the
+ *                      router-order weighted reduce, + shared.
+ * griddepcontrol.wait is a no-op for a kernel launched without PDL, so the
+ * same kernels run unchanged behind a host copy. */
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 __device__ __forceinline__ float warp_sum(float v)
 {
@@ -299,167 +319,144 @@ __device__ __forceinline__ float warp_sum(float v)
     return v;
 }
 
-/* fp32 row . x (x in shared memory), all of the lane's loads issued first. */
-__device__ __forceinline__ float dot_f32_row(const float *__restrict__ w, const float *xs,
-                                             int n, int lane)
+/* fp32 dot of w[0..n) with xs (shared memory), every load issued first.
+ * n4 = n/4 must be <= 32*U4. */
+template <int U4>
+__device__ __forceinline__ float dot_f32_span(const float *__restrict__ w, const float *xs,
+                                              int n4, int lane)
 {
-    constexpr int U = 8;
-    float acc = 0.0f;
-    const int n4 = n >> 2;
     const float4 *w4 = reinterpret_cast<const float4 *>(w);
     const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-    for (int base = 0; base < n4; base += 32 * U) {
-        float4 a[U];
+    float4 a[U4];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int i = base + u * 32 + lane;
-            a[u] = i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int u = 0; u < U4; u++) {
+        const int i = u * 32 + lane;
+        a[u] = i < n4 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float acc = 0.0f;
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int i = base + u * 32 + lane;
-            if (i < n4) {
-                const float4 b = x4[i];
-                acc = fmaf(a[u].x, b.x, acc); acc = fmaf(a[u].y, b.y, acc);
-                acc = fmaf(a[u].z, b.z, acc); acc = fmaf(a[u].w, b.w, acc);
-            }
+    for (int u = 0; u < U4; u++) {
+        const int i = u * 32 + lane;
+        if (i < n4) {
+            const float4 b = x4[i];
+            acc = fmaf(a[u].x, b.x, acc); acc = fmaf(a[u].y, b.y, acc);
+            acc = fmaf(a[u].z, b.z, acc); acc = fmaf(a[u].w, b.w, acc);
         }
     }
     return warp_sum(acc);
 }
 
 /* Q8G row (src/model.c:265-320 layout: int8 rows padded to whole groups of
- * 128, one f16 scale per group) . x (x in shared memory). Chunk c is inputs
- * [16c, 16c+16) of group c/8; inputs at or past n are skipped. */
+ * 128, one f16 scale per group) . xs. Chunk c is inputs [16c, 16c+16) of
+ * group c/8; inputs at or past n are skipped. All loads issued first. */
+__device__ __forceinline__ float q8g_chunk(uint4 q, float sc, const float *xs, int b0, int n)
+{
+    const uint32_t wv[4] = { q.x, q.y, q.z, q.w };
+    float part = 0.0f;
+    if (b0 + 16 <= n) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xs + b0);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float4 xv = x4[k];
+            const uint32_t wd = wv[k];
+            part = fmaf((float)(int8_t)(wd & 0xff), xv.x, part);
+            part = fmaf((float)(int8_t)((wd >> 8) & 0xff), xv.y, part);
+            part = fmaf((float)(int8_t)((wd >> 16) & 0xff), xv.z, part);
+            part = fmaf((float)(int8_t)(wd >> 24), xv.w, part);
+        }
+    } else {
+        for (int i = 0; b0 + i < n; i++)
+            part = fmaf((float)(int8_t)((wv[i >> 2] >> (8 * (i & 3))) & 0xff), xs[b0 + i], part);
+    }
+    return sc * part;
+}
+
+template <int U>
 __device__ __forceinline__ float dot_q8g_row(const int8_t *__restrict__ row,
                                              const uint16_t *__restrict__ ws,
                                              const float *xs, int n, int lane)
 {
-    constexpr int U = 6;
-    float acc = 0.0f;
     const int nchunk = (n + 15) / 16;
+    float acc = 0.0f;
     for (int base = 0; base < nchunk; base += 32 * U) {
         uint4 q[U];
-        float sc[U];
+        uint16_t sh[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int c = base + u * 32 + lane;
             q[u] = c < nchunk ? ldg16(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-            sc[u] = c < nchunk ? f16_keep(__ldg(ws + (c >> 3))) : 0.0f;
+            sh[u] = c < nchunk ? __ldg(ws + (c >> 3)) : (uint16_t)0;
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int c = base + u * 32 + lane;
-            if (c >= nchunk) continue;
-            const uint32_t wv[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
-            const int b0 = c * 16;
-            float part = 0.0f;
-            if (b0 + 16 <= n) {
-                const float4 *x4 = reinterpret_cast<const float4 *>(xs + b0);
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const float4 xv = x4[k];
-                    const uint32_t wd = wv[k];
-                    part = fmaf((float)(int8_t)(wd & 0xff), xv.x, part);
-                    part = fmaf((float)(int8_t)((wd >> 8) & 0xff), xv.y, part);
-                    part = fmaf((float)(int8_t)((wd >> 16) & 0xff), xv.z, part);
-                    part = fmaf((float)(int8_t)(wd >> 24), xv.w, part);
-                }
-            } else {
-                for (int i = 0; b0 + i < n; i++)
-                    part = fmaf((float)(int8_t)((wv[i >> 2] >> (8 * (i & 3))) & 0xff),
-                                xs[b0 + i], part);
-            }
-            acc = fmaf(sc[u], part, acc);
+            if (c < nchunk) acc += q8g_chunk(q[u], f16_keep(sh[u]), xs, c * 16, n);
         }
     }
     return warp_sum(acc);
 }
 
-/* Router logits (fp32 rows) and the shared expert's gate/up (Q8G rows), one
- * warp per output row, x staged in shared memory. */
-__global__ void __launch_bounds__(256) router_shared_kernel(wc_moe_args a)
+/* ---- 1. router (+ top-K in the last block) -------------------------------- */
+
+constexpr int kRouterBlock = 256;      /* 8 warps                           */
+constexpr int kRouterSplit = 4;        /* warps per router row              */
+constexpr int kMaxPerLane = 32;        /* E <= 1024 (one live bit per lane entry) */
+
+struct RouterGeom {
+    int rblocks;     /* blocks for the router rows (2 rows per block)        */
+    int sblocks;     /* blocks for the shared gate/up rows (8 per block)     */
+};
+
+__host__ __device__ inline RouterGeom router_geom(int E, int si)
 {
-    extern __shared__ float xs[];
-    const int lat = a.bank.lat;
-    const int warps = blockDim.x / 32;
-    const int per_t = a.E + 2 * a.si;
-    const int t = blockIdx.y;                   /* grid: (row blocks, tokens) */
-    const int r = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x % 32;
-    const float *x = a.x + (size_t)t * lat;
-    for (int i = threadIdx.x; i < lat; i += blockDim.x) xs[i] = x[i];
-    __syncthreads();
-    if (r >= per_t) return;
-    if (r < a.E) {
-        const float v = dot_f32_row(a.router + (size_t)r * lat, xs, lat, lane);
-        if (lane == 0) a.ws.logits[(size_t)t * a.E + r] = v;
-        return;
-    }
-    const int rr = r - a.E;
-    const int kind = rr / a.si, o = rr % a.si;
-    const int ng = (lat + 127) / 128;
-    const int8_t *W = kind ? a.shu : a.shg;
-    const uint16_t *S = kind ? a.shu_s : a.shg_s;
-    const float v = dot_q8g_row(W + (size_t)o * ng * 128, S + (size_t)o * ng, xs, lat, lane);
-    if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = v;
+    RouterGeom g;
+    const int rows_pb = (kRouterBlock / 32) / kRouterSplit;
+    g.rblocks = (E + rows_pb - 1) / rows_pb;
+    g.sblocks = (2 * si + (kRouterBlock / 32) - 1) / (kRouterBlock / 32);
+    return g;
 }
 
-/* Routing, src/model.c:2724-2747, one block per token. Warp 0 holds the E
- * scores in registers (score = 1/(1+expf(-logit)), plus the bias, or plus
- * 0.0f when there is none) and runs K rounds of argmax: within a lane the
- * ids ascend and the comparison is a strict >, across lanes the larger
- * value wins and equal values go to the lower id — so the lowest id wins a
- * tie and a NaN never wins, exactly as the sequential scan from -1e30f.
- * w = score[best]; renorm by (sum + 1e-20f) in j order; times routed_scale.
- * The other warps form the shared expert's SiLU(g)*u meanwhile. */
-constexpr int kMaxPerLane = 32;      /* E <= 1024 */
-
-__global__ void __launch_bounds__(256) route_kernel(wc_moe_args a)
+/* Routing, src/model.c:2724-2747, by one warp. The E scores live in
+ * registers (score = 1/(1+expf(-logit)), plus the bias, or plus 0.0f when
+ * there is none); K rounds of argmax: within a lane the ids ascend and the
+ * comparison is a strict >, across lanes the larger value wins and equal
+ * values go to the lower id — so the lowest id wins a tie and a NaN never
+ * wins, exactly as the sequential scan from -1e30f does. w = score[best];
+ * renorm by (sum + 1e-20f) accumulated in j order; times routed_scale. */
+__device__ void route_warp(const wc_moe_args &a, int t, int lane, float *sc, float *v)
 {
-    const int t = blockIdx.x;
+    /* sc, v: E floats of shared memory each */
     const int E = a.E, K = a.K;
-    if (threadIdx.x >= 32) {
-        for (int i = threadIdx.x - 32; i < a.si; i += blockDim.x - 32) {
-            const size_t o = (size_t)t * a.si + i;
-            a.ws.sh_h[o] = silu_ref(a.ws.sh_g[o]) * a.ws.sh_u[o];
-        }
-        return;
-    }
-    const int lane = threadIdx.x;
     const float *lg = a.ws.logits + (size_t)t * E;
-    float sc[kMaxPerLane], v[kMaxPerLane];
     uint32_t live = 0;
-#pragma unroll
-    for (int k = 0; k < kMaxPerLane; k++) {
+    for (int k = 0; lane + 32 * k < E; k++) {
         const int e = lane + 32 * k;
-        sc[k] = 0.0f;
-        v[k] = 0.0f;
-        if (e < E) {
-            sc[k] = 1.0f / (1.0f + expf(-lg[e]));
-            v[k] = sc[k] + (a.bias ? a.bias[e] : 0.0f);
-            live |= 1u << k;
-        }
+        const float s = 1.0f / (1.0f + expf(-__ldcg(lg + e)));
+        sc[e] = s;
+        v[e] = s + (a.bias ? __ldg(a.bias + e) : 0.0f);
+        live |= 1u << k;
     }
     float wsel = 0.0f, wsum = 0.0f;
     int mine = -1;                      /* lane j keeps the j-th choice */
     for (int j = 0; j < K; j++) {
-        float bv = -1e30f, bs = 0.0f;
+        float bv = -1e30f, bsc = 0.0f;
         int best = -1;
-#pragma unroll
-        for (int k = 0; k < kMaxPerLane; k++)
-            if (((live >> k) & 1) && v[k] > bv) { bv = v[k]; bs = sc[k]; best = lane + 32 * k; }
+        for (int k = 0; lane + 32 * k < E; k++) {
+            const int e = lane + 32 * k;
+            if (((live >> k) & 1) && v[e] > bv) { bv = v[e]; bsc = sc[e]; best = e; }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+            const float os = __shfl_xor_sync(0xffffffffu, bsc, o);
             const int oi = __shfl_xor_sync(0xffffffffu, best, o);
             if (oi >= 0 && (best < 0 || ov > bv || (ov == bv && oi < best))) {
-                bv = ov; bs = os; best = oi;
+                bv = ov; bsc = os; best = oi;
             }
         }
         if (best >= 0 && (best & 31) == lane) live &= ~(1u << (best >> 5));
-        if (lane == j) { mine = best; wsel = best >= 0 ? bs : 0.0f; }
-        wsum += best >= 0 ? bs : 0.0f;   /* same j-order sum in every lane */
+        if (lane == j) { mine = best; wsel = best >= 0 ? bsc : 0.0f; }
+        wsum += best >= 0 ? bsc : 0.0f;   /* the same j-order sum in every lane */
     }
     if (lane < K) {
         float w = wsel;
@@ -469,92 +466,148 @@ __global__ void __launch_bounds__(256) route_kernel(wc_moe_args a)
     }
 }
 
+__global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, RouterGeom rg)
+{
+    extern __shared__ float xs[];
+    __shared__ float part[kRouterBlock / 32];
+    __shared__ unsigned int ticket;
+    pdl_trigger();                   /* let gate/up start its table build */
+    const int lat = a.bank.lat;
+    const int t = blockIdx.y;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const float *x = a.x + (size_t)t * lat;
+    for (int i = threadIdx.x; i < lat; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const int b = blockIdx.x;
+    if (b < rg.rblocks) {
+        /* two router rows per block, a quarter of the row per warp */
+        const int r = b * 2 + warp / kRouterSplit, qtr = warp % kRouterSplit;
+        const int n4 = lat / 4, per = (n4 + kRouterSplit - 1) / kRouterSplit;
+        const int q0 = qtr * per, q1 = min(n4, q0 + per);
+        float v = 0.0f;
+        if (r < a.E)
+            v = dot_f32_span<6>(a.router + (size_t)r * lat + 4 * q0, xs + 4 * q0, q1 - q0, lane);
+        if (lane == 0) part[warp] = v;
+        __syncthreads();
+        if (threadIdx.x < 2) {
+            const int rr = b * 2 + threadIdx.x;
+            if (rr < a.E) {
+                const float *p = part + threadIdx.x * kRouterSplit;
+                a.ws.logits[(size_t)t * a.E + rr] = ((p[0] + p[1]) + p[2]) + p[3];
+            }
+        }
+    } else {
+        const int rr = (b - rg.rblocks) * (kRouterBlock / 32) + warp;
+        if (rr < 2 * a.si) {
+            const int kind = rr / a.si, o = rr % a.si;
+            const int ng = (lat + 127) / 128;
+            const int8_t *W = kind ? a.shu : a.shg;
+            const uint16_t *S = kind ? a.shu_s : a.shg_s;
+            const float v = dot_q8g_row<5>(W + (size_t)o * ng * 128, S + (size_t)o * ng, xs,
+                                           lat, lane);
+            if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = v;
+        }
+    }
+    /* the last block of this token routes it */
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ticket = atomicAdd(a.ws.tickets + t, 1u);
+    __syncthreads();
+    if (ticket != gridDim.x - 1) return;
+    __threadfence();
+    if (warp == 0) route_warp(a, t, lane, xs, xs + a.E);   /* x is dead by now */
+    for (int i = threadIdx.x - 32; i >= 0 && i < a.si; i += blockDim.x - 32) {
+        const size_t o = (size_t)t * a.si + i;
+        a.ws.sh_h[o] = silu_ref(__ldcg(a.ws.sh_g + o)) * __ldcg(a.ws.sh_u + o);
+    }
+    if (threadIdx.x == 0) a.ws.tickets[t] = 0;       /* ready for the next launch */
+}
+
 /* The record of routed expert j of token t (ids are global; a bank may hold
  * a contiguous subset starting at `first`). */
 __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const int *idx,
                                                      int K, int t, int j)
 {
-    return bk.base + (size_t)(idx[(size_t)t * K + j] - bk.first) * bk.rec_bytes;
+    return bk.base + (size_t)(__ldcg(idx + (size_t)t * K + j) - bk.first) * bk.rec_bytes;
 }
 
-/* The shared expert's down rows ([lat][si] Q8G) for SiLU(g)*u of token t:
- * one warp per row, block `b` of the token's ceil(lat / warps) blocks. */
-__device__ __forceinline__ void shared_down_rows(const wc_moe_args &a, float *hs, int b)
-{
-    const wc_bank &bk = a.bank;
-    const int warps = blockDim.x / 32;
-    const int per_tok = (bk.lat + warps - 1) / warps;
-    const int t = b / per_tok;
-    if (t >= a.T) return;
-    for (int i = threadIdx.x; i < a.si; i += blockDim.x) hs[i] = a.ws.sh_h[(size_t)t * a.si + i];
-    __syncthreads();
-    const int o = (b % per_tok) * warps + threadIdx.x / 32, lane = threadIdx.x % 32;
-    if (o >= bk.lat) return;
-    const int ng = (a.si + 127) / 128;
-    const float v = dot_q8g_row(a.shd + (size_t)o * ng * 128, a.shd_s + (size_t)o * ng,
-                                hs, a.si, lane);
-    if (lane == 0) a.ws.sh_out[(size_t)t * bk.lat + o] = v;
-}
-
-/* gate/up: tile = (token, kind, slice, expert group). Every tile's table is
- * shared by the rows of all the experts in its group. Blocks past gu_tiles
- * run the shared expert's down rows (routing, and so SiLU(g)*u of the
- * shared expert, is done by then). */
+/* ---- 2. gate/up ------------------------------------------------------------
+ * tile = (token, kind, slice, expert group): one table slice shared by the
+ * rows of every expert in the group. After the tile, the block runs its
+ * share of the shared expert's down rows ([lat][si] Q8G, one warp per row). */
 template <int ST>
 __global__ void __launch_bounds__(512)
-gateup_kernel(wc_moe_args a, TileGeom g, int gu_tiles, const int *idx)
+gateup_kernel(wc_moe_args a, TileGeom g, int gu_tiles, int sh_rows_pb, const int *idx)
 {
     extern __shared__ float smem[];
-    if ((int)blockIdx.x >= gu_tiles) {
-        shared_down_rows(a, smem, blockIdx.x - gu_tiles);
-        return;
-    }
     float *xs = smem, *lut = smem + g.Vs * kVecDim;
     int b = blockIdx.x;
     const int grp = b % g.groups; b /= g.groups;
     const int slice = b % g.ns; b /= g.ns;
     const int kind = b % 2; const int t = b / 2;
     const wc_bank &bk = a.bank;
-    const int j0 = grp * g.EG;
-    const int nm = min(g.EG, a.K - j0);
-    /* this thread's matrix, then its first index loads */
-    const int m = min(TileThread<ST>::matrix_of_thread(g), nm - 1);
-    const uint8_t *mat = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off);
-    TileThread<ST> th(g, slice, nm, mat);
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
+    /* routing-independent: x slice and the table */
     const float *xt = a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim;
     for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xt[i];
     __syncthreads();
     build_lut_slice<ST>(lut, xs, a.books, bk.cb_base + kind * ST, nvs);
+    pdl_wait();                      /* routing (and all earlier work) is done */
+    pdl_trigger();
+    const int j0 = grp * g.EG;
+    const int nm = min(g.EG, a.K - j0);
+    const int m = min(TileThread<ST>::matrix_of_thread(g), nm - 1);
+    const uint8_t *mat = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off);
+    TileThread<ST> th(g, slice, nm, mat);
     __syncthreads();
     float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
     th.finish(g, lut, out, bk.inter, nm);
+    if (a.si <= 0 || t != 0 || sh_rows_pb <= 0) return;
+    /* shared expert down rows for every token: rows [blk*R, blk*R + R) */
+    for (int tt = 0; tt < a.T; tt++) {
+        __syncthreads();
+        float *hs = smem;
+        for (int i = threadIdx.x; i < a.si; i += blockDim.x) hs[i] = __ldcg(a.ws.sh_h + (size_t)tt * a.si + i);
+        __syncthreads();
+        const int warps = blockDim.x / 32;
+        const int ng = (a.si + 127) / 128;
+        const int lin = ((kind * g.ns + slice) * g.groups + grp);
+        for (int rr = threadIdx.x / 32; rr < sh_rows_pb; rr += warps) {
+            const int o = lin * sh_rows_pb + rr;
+            if (o >= bk.lat) break;
+            const float v = dot_q8g_row<2>(a.shd + (size_t)o * ng * 128, a.shd_s + (size_t)o * ng,
+                                           hs, a.si, threadIdx.x % 32);
+            if (threadIdx.x % 32 == 0) a.ws.sh_out[(size_t)tt * bk.lat + o] = v;
+        }
+    }
 }
 
-/* down: tile = (token, expert j, slice), h = SiLU(g)*u formed from the
- * gate/up partial sums for the slice's inputs; then the shared expert's down
- * rows (warp per row) in the trailing blocks. */
+/* ---- 3. down ---------------------------------------------------------------
+ * tile = (token, expert j, slice). The expert's down index loads go out
+ * before the wait (the route is known by then: gate/up started after it);
+ * h = SiLU(g)*u for the slice's inputs comes from the gate/up partials. */
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
-down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, const int *idx)
+down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
 {
     extern __shared__ float smem[];
     const wc_bank &bk = a.bank;
-    (void)d_tiles;
     float *xs = smem, *lut = smem + g.Vs * kVecDim;
     int b = blockIdx.x;
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
     const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
     TileThread<ST> th(g, slice, 1, rec + bk.down_off);
+    pdl_trigger();
+    pdl_wait();                      /* gate/up partials are complete */
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
     const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
     const int inter = bk.inter;
     const size_t sstride = (size_t)a.K * inter;
     const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * sstride + (size_t)j * inter;
     const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * sstride + (size_t)j * inter;
-    /* Sum the gate/up slices for the slice's inputs with the whole block:
-     * part p of P adds slices p, p+P, ...; parts are then added in order. */
+    /* gate/up slice sums with the whole block: part p of P adds slices
+     * p, p+P, ...; parts are then added in order */
     const int nin = nvs * kVecDim;
     const int P = max(1, (int)blockDim.x / nin);
     float *red2 = lut;                         /* [P][2][nin], before the table */
@@ -562,9 +615,10 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, const int *idx)
         const int i = threadIdx.x % nin, p = threadIdx.x / nin;
         const int n = v0 * kVecDim + i;
         float sg = 0.0f, su = 0.0f;
+#pragma unroll 4
         for (int s2 = p; s2 < gu.ns; s2 += P) {
-            sg += pg[(size_t)s2 * sstride + n];
-            su += pu[(size_t)s2 * sstride + n];
+            sg += __ldcg(pg + (size_t)s2 * sstride + n);
+            su += __ldcg(pu + (size_t)s2 * sstride + n);
         }
         red2[(p * 2 + 0) * nin + i] = sg;
         red2[(p * 2 + 1) * nin + i] = su;
@@ -588,10 +642,13 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, const int *idx)
     th.finish(g, lut, out, 0, 1);
 }
 
-/* out[t][i] = sum_j w[j] * (f16(scale_down_j[i]) * sum_s P_d[t][j][s][i]),
+/* ---- 4. combine --------------------------------------------------------------
+ * out[t][i] = sum_j w[j] * (f16(scale_down_j[i]) * sum_s P_d[t][j][s][i]),
  * j in router order (src/model.c:2908-2909) — or in ascending expert id
  * when order_by_id (moe_chunk, src/model.c:3632-3656) — then + shared.
  * Block: 32 outputs x 8 expert lanes. */
+constexpr int kMaxSlicesReg = 32;
+
 __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
                                                       const int *idx, const float *w)
 {
@@ -602,14 +659,29 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     const int il = threadIdx.x % 32, jl = threadIdx.x / 32;
     const int i = blockIdx.x * 32 + il;
     const int *it = idx + (size_t)t * K;
-    for (int j = jl; j < K; j += blockDim.x / 32) {
+    /* before the wait: the row scales (the route is complete by now) */
+    float scl[kMaxTopK / 8];
+    for (int j = jl, n = 0; j < K; j += 8, n++) {
+        scl[n] = 0.0f;
+        if (i < bk.lat) {
+            const uint16_t *sc = reinterpret_cast<const uint16_t *>(
+                bk.base + (size_t)(__ldcg(it + j) - bk.first) * bk.rec_bytes + bk.scale_off) +
+                2 * bk.inter;
+            scl[n] = f16_keep(sc[i]);
+        }
+    }
+    pdl_wait();
+    for (int j = jl, n = 0; j < K; j += 8, n++) {
         float s = 0.0f;
         if (i < bk.lat) {
             const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
-            for (int k = 0; k < g.ns; k++) s += p[(size_t)k * bk.lat];
-            const uint16_t *sc = reinterpret_cast<const uint16_t *>(
-                bk.base + (size_t)(it[j] - bk.first) * bk.rec_bytes + bk.scale_off) + 2 * bk.inter;
-            s *= f16_keep(sc[i]);
+            float v[kMaxSlicesReg];
+#pragma unroll
+            for (int k = 0; k < kMaxSlicesReg; k++)
+                v[k] = k < g.ns ? __ldcg(p + (size_t)k * bk.lat) : 0.0f;
+            for (int k = 0; k < g.ns && k < kMaxSlicesReg; k++) s += v[k];
+            for (int k = kMaxSlicesReg; k < g.ns; k++) s += __ldcg(p + (size_t)k * bk.lat);
+            s *= scl[n];
         }
         accj[j][il] = s;
     }
@@ -619,9 +691,11 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
             int jj = n;
             if (a.order_by_id) {          /* next larger id, first j routed to it */
                 jj = -1;
-                for (int q = 0; q < K; q++)
-                    if (it[q] > last && (jj < 0 || it[q] < it[jj])) jj = q;
-                if (jj >= 0) last = it[jj];
+                for (int q = 0; q < K; q++) {
+                    const int e = __ldcg(it + q);
+                    if (e > last && (jj < 0 || e < __ldcg(it + jj))) jj = q;
+                }
+                if (jj >= 0) last = __ldcg(it + jj);
             }
             order[n] = jj;
         }
@@ -633,11 +707,11 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     for (int n = 0; n < K; n++) {
         const int j = order[n];
         if (j < 0) break;
-        const float wj = wt[j];
+        const float wj = __ldcg(wt + j);
         if (a.order_by_id && wj == 0.0f) continue;
         y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
     }
-    if (a.si > 0) y = __fadd_rn(y, a.ws.sh_out[(size_t)t * bk.lat + i]);
+    if (a.si > 0) y = __fadd_rn(y, __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i));
     a.out[(size_t)t * bk.lat + i] = y;
 }
 
@@ -646,7 +720,7 @@ constexpr int kVsDown = 8;
 
 struct MoeGeom {
     TileGeom gu, d;
-    int gu_tiles, d_tiles, sh_blocks;
+    int gu_tiles, d_tiles, sh_rows_pb;
 };
 
 MoeGeom moe_geom(const wc_moe_args *a)
@@ -657,9 +731,26 @@ MoeGeom moe_geom(const wc_moe_args *a)
     m.d = make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 512);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
     m.d_tiles = a->T * a->K * m.d.ns;
-    const int warps = m.gu.threads / 32;
-    m.sh_blocks = a->si > 0 ? a->T * ((b.lat + warps - 1) / warps) : 0;
+    const int per_t = 2 * m.gu.ns * m.gu.groups;      /* token-0 tiles run the shared rows */
+    m.sh_rows_pb = a->si > 0 ? (b.lat + per_t - 1) / per_t : 0;
     return m;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   bool pdl, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 template <int ST>
@@ -668,39 +759,48 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
     const MoeGeom m = moe_geom(a);
     const int *idx = a->idx;
     const float *w = a->w;
+    bool pdl = false;
+    cudaError_t e = cudaSuccess;
     if (a->router) {
-        const dim3 rg((a->E + 2 * a->si + 7) / 8, a->T);
-        int pe = prof_begin(WC_PH_ROUTER, s);
-        router_shared_kernel<<<rg, 256, (size_t)a->bank.lat * sizeof(float), s>>>(*a);
+        if (a->E > 32 * kMaxPerLane) return (int)cudaErrorInvalidValue;
+        const RouterGeom rg = router_geom(a->E, a->si);
+        const int pe = prof_begin(WC_PH_ROUTER, s);
+        const size_t rsm = (size_t)max(a->bank.lat, 2 * a->E) * sizeof(float);
+        e = launch(router_kernel, dim3(rg.rblocks + rg.sblocks, a->T), dim3(kRouterBlock),
+                   rsm, s, false, *a, rg);
         prof_end(pe, s);
-        pe = prof_begin(WC_PH_ROUTE, s);
-        route_kernel<<<a->T, 256, 0, s>>>(*a);
-        prof_end(pe, s);
-        g_launches += 2;
+        g_launches += 1;
         idx = a->idx_out;
         w = a->w_out;
+        pdl = true;
+        if (e != cudaSuccess) return (int)e;
     }
+    const int prof = P.on;             /* events between kernels defeat PDL */
     size_t gsmem = m.gu.smem;
     const size_t shsmem = (size_t)a->si * sizeof(float);
     if (a->router && shsmem > gsmem) gsmem = shsmem;
     cudaFuncSetAttribute(gateup_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)gsmem);
     int pe = prof_begin(WC_PH_GATEUP, s);
-    gateup_kernel<ST><<<m.gu_tiles + (a->router ? m.sh_blocks : 0), m.gu.threads, gsmem, s>>>(
-        *a, m.gu, m.gu_tiles, idx);
+    e = launch(gateup_kernel<ST>, dim3(m.gu_tiles), dim3(m.gu.threads), gsmem, s, pdl && !prof,
+               *a, m.gu, m.gu_tiles, a->router ? m.sh_rows_pb : 0, idx);
     prof_end(pe, s);
+    if (e != cudaSuccess) return (int)e;
     cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)m.d.smem);
     pe = prof_begin(WC_PH_DOWN, s);
-    down_kernel<ST><<<m.d_tiles, m.d.threads, m.d.smem, s>>>(*a, m.gu, m.d, m.d_tiles, idx);
+    e = launch(down_kernel<ST>, dim3(m.d_tiles), dim3(m.d.threads), m.d.smem, s, !prof,
+               *a, m.gu, m.d, idx);
     prof_end(pe, s);
-    dim3 cg((a->bank.lat + 31) / 32, a->T);
+    if (e != cudaSuccess) return (int)e;
     wc_moe_args ca = *a;
     if (!a->router) ca.si = 0;
     pe = prof_begin(WC_PH_COMBINE, s);
-    combine_kernel<<<cg, 256, 0, s>>>(ca, m.d, idx, w);
+    e = launch(combine_kernel, dim3((a->bank.lat + 31) / 32, a->T), dim3(256), 0, s, !prof,
+               ca, m.d, idx, w);
     prof_end(pe, s);
     g_launches += 3;
+    if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();
 }
 
@@ -716,6 +816,7 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
     n += (size_t)T * K * d.ns * lat;
     n += (size_t)T * E;
     n += (size_t)T * si * 3 + (size_t)T * lat;
+    n += (size_t)T;                          /* tickets */
     return n + 64;
 }
 
@@ -725,6 +826,7 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 512);
     float *p = base;
+    ws->tickets = reinterpret_cast<unsigned int *>(p); p += 64;   /* first: stays put */
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
     ws->p_d = p; p += (size_t)T * K * d.ns * lat;
     ws->logits = p; p += (size_t)T * E;

@@ -154,6 +154,9 @@ static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages
         S.ws_floats = 0;
         cudaError_t e = cudaMalloc((void **)&S.d_ws, need * sizeof(float));
         if (e != cudaSuccess) return cuda_fail(e, "workspace");
+        /* the router's ticket counters live here and must start at zero */
+        e = cudaMemset(S.d_ws, 0, need * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
         S.ws_floats = need;
     }
     if (io > S.io_floats) {

@@ -30,6 +30,7 @@ typedef struct {
     float *p_d;        /* [T][K][ns_d][lat] partial down sums               */
     float *logits;     /* [T][E]                                            */
     float *sh_g, *sh_u, *sh_h, *sh_out;   /* shared expert [T][si] / [T][hid] */
+    unsigned int *tickets;  /* [T] router blocks done; zero between launches   */
 } wc_moe_ws;
 
 typedef struct {
@@ -53,6 +54,8 @@ typedef struct {
     wc_moe_ws ws;
 } wc_moe_args;
 
+/* Floats of workspace for T tokens. The region must be zeroed once when it
+ * is allocated (the ticket counters reset themselves after every launch). */
 size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
                         int stages);
 void   wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E, int lat,
