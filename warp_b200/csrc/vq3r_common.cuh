@@ -133,6 +133,86 @@ struct Gather16 {
     }
 };
 
+/* All of a thread's positions in registers: NP positions (at most) of one
+ * quarter-block, loaded by begin() in one go — one DRAM round trip — and
+ * consumed by run(). For tiles whose lanes hold few positions. */
+template <int ST, int NP>
+struct GatherAll {
+    static constexpr int W = 4 * ST;
+    uint32_t w[NP][W];
+    int n;
+
+    __device__ __forceinline__ void begin(const uint8_t *p, int nvv)
+    {
+        n = nvv;
+#pragma unroll
+        for (int i = 0; i < NP; i++)
+            if (i < n) Gather16<ST>::load(w[i], p + (size_t)i * kBlock * ST);
+    }
+
+    __device__ __forceinline__ void run(float *acc, const float *L)
+    {
+#pragma unroll
+        for (int i = 0; i < NP; i++)
+            if (i < n) RowStep<ST, 0>::run(acc, w[i], L + (size_t)i * ST * kEntries);
+    }
+};
+
+/* Codebook rows for the table build, loaded ahead of time: entry i of the
+ * thread's share (i = threadIdx.x + k*blockDim.x, k < NE) of the ST*256
+ * (stage, code) pairs of book group cb. */
+template <int ST, int NE>
+struct BookRows {
+    float4 c[NE][2];
+    bool all;                 /* the block's NE rows per thread cover every entry */
+    const float *src_books;
+    int src_cb;
+
+    __device__ __forceinline__ void load(const float *__restrict__ books, int cb)
+    {
+        all = (int)blockDim.x * NE >= ST * kEntries;
+        src_books = books;
+        src_cb = cb;
+        if (!all) return;     /* small blocks build from global memory instead */
+#pragma unroll
+        for (int k = 0; k < NE; k++) {
+            const int i = threadIdx.x + k * blockDim.x;
+            if (i < ST * kEntries) {
+                const int s = i / kEntries, code = i % kEntries;
+                const float4 *src = reinterpret_cast<const float4 *>(
+                    books + ((size_t)(cb + s) * kEntries + code) * kVecDim);
+                c[k][0] = __ldg(src);
+                c[k][1] = __ldg(src + 1);
+            }
+        }
+    }
+
+    /* lut[(v*ST + s)*256 + code] = FMA chain over d from 0, d ascending —
+     * the same arithmetic as build_lut_slice, from the prefetched rows. */
+    __device__ __forceinline__ void build(float *lut, const float *xs, int nvs) const
+    {
+        if (!all) {
+            build_lut_slice<ST>(lut, xs, src_books, src_cb, nvs);
+            return;
+        }
+#pragma unroll
+        for (int k = 0; k < NE; k++) {
+            const int i = threadIdx.x + k * blockDim.x;
+            if (i >= ST * kEntries) continue;
+            const int s = i / kEntries, code = i % kEntries;
+            const float C[8] = { c[k][0].x, c[k][0].y, c[k][0].z, c[k][0].w,
+                                 c[k][1].x, c[k][1].y, c[k][1].z, c[k][1].w };
+            for (int v = 0; v < nvs; v++) {
+                const float *xv = xs + v * kVecDim;
+                float acc = 0.0f;
+#pragma unroll
+                for (int d = 0; d < kVecDim; d++) acc = __fmaf_rn(xv[d], C[d], acc);
+                lut[(v * ST + s) * kEntries + code] = acc;
+            }
+        }
+    }
+};
+
 __device__ __forceinline__ float silu_ref(float v)
 {
     /* src/model.c:501: v / (1 + expf(-v)). */

@@ -152,17 +152,19 @@ TileGeom make_geom(int M, int N, int nmat, int Vs, int stages, int target_thread
 
 /* Per-thread part of a tile: which rows, which positions, and the index
  * stream, whose first loads are issued at construction. */
-template <int ST>
+template <int ST, typename Gat = Gather16<ST>>
 struct TileThread {
     int lane, m, rbl, q, vl0, vl1;
     bool active;
-    Gather16<ST> G;
+    Gat G;
 
     /* The matrix this thread's rows belong to (0 .. EG-1). */
     static __device__ __forceinline__ int matrix_of_thread(const TileGeom &g)
     {
         return (threadIdx.x % g.Q) / (g.nrb * 4);
     }
+
+    TileThread() = default;
 
     /* mat: the index stream of matrix matrix_of_thread(g) (may be anything
      * when that matrix is past nm: the thread is then inactive). */
@@ -396,11 +398,18 @@ __device__ __forceinline__ float dot_q8g_row(const int8_t *__restrict__ row,
     return warp_sum(acc);
 }
 
-/* ---- 1. router (+ top-K in the last block) -------------------------------- */
-
-constexpr int kRouterBlock = 256;      /* 8 warps                           */
+/* ---- 1. router (+ top-K in the last block) --------------------------------
+ * Blocks of 8 warps: router blocks hold 2 rows, a quarter row per warp;
+ * shared blocks hold 8 shared gate/up rows, a row per warp. Each thread
+ * issues its weight loads and its share of x first, so a block costs one
+ * DRAM round trip. The last block of a token (ticket) routes it. */
+constexpr int kRouterBlock = 256;
 constexpr int kRouterSplit = 4;        /* warps per router row              */
+constexpr int kRouterU4 = 6;           /* float4 per lane: lat/4/4/32 <= 6 -> lat <= 3072 */
+constexpr int kShU = 5;                /* 16-byte chunks per lane: lat <= 2560 */
+constexpr int kXU = 3;                 /* float4 of x per thread: lat <= 3072 */
 constexpr int kMaxPerLane = 32;        /* E <= 1024 (one live bit per lane entry) */
+constexpr int kSiluU = 8;              /* shared SiLU inputs per thread: si <= 1792 */
 
 struct RouterGeom {
     int rblocks;     /* blocks for the router rows (2 rows per block)        */
@@ -416,8 +425,8 @@ __host__ __device__ inline RouterGeom router_geom(int E, int si)
     return g;
 }
 
-/* Routing, src/model.c:2724-2747, by one warp. The E scores live in
- * registers (score = 1/(1+expf(-logit)), plus the bias, or plus 0.0f when
+/* Routing, src/model.c:2724-2747, by one warp: the E scores in shared
+ * memory (score = 1/(1+expf(-logit)), plus the bias, or plus 0.0f when
  * there is none); K rounds of argmax: within a lane the ids ascend and the
  * comparison is a strict >, across lanes the larger value wins and equal
  * values go to the lower id — so the lowest id wins a tie and a NaN never
@@ -425,17 +434,27 @@ __host__ __device__ inline RouterGeom router_geom(int E, int si)
  * renorm by (sum + 1e-20f) accumulated in j order; times routed_scale. */
 __device__ void route_warp(const wc_moe_args &a, int t, int lane, float *sc, float *v)
 {
-    /* sc, v: E floats of shared memory each */
     const int E = a.E, K = a.K;
     const float *lg = a.ws.logits + (size_t)t * E;
-    uint32_t live = 0;
-    for (int k = 0; lane + 32 * k < E; k++) {
+    float lv[kMaxPerLane], bv0[kMaxPerLane];
+#pragma unroll
+    for (int k = 0; k < kMaxPerLane; k++) {
         const int e = lane + 32 * k;
-        const float s = 1.0f / (1.0f + expf(-__ldcg(lg + e)));
-        sc[e] = s;
-        v[e] = s + (a.bias ? __ldg(a.bias + e) : 0.0f);
-        live |= 1u << k;
+        lv[k] = e < E ? __ldcg(lg + e) : 0.0f;
+        bv0[k] = (e < E && a.bias) ? __ldg(a.bias + e) : 0.0f;
     }
+    uint32_t live = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxPerLane; k++) {
+        const int e = lane + 32 * k;
+        if (e < E) {
+            const float s = 1.0f / (1.0f + expf(-lv[k]));
+            sc[e] = s;
+            v[e] = s + bv0[k];
+            live |= 1u << k;
+        }
+    }
+    __syncwarp();
     float wsel = 0.0f, wsum = 0.0f;
     int mine = -1;                      /* lane j keeps the j-th choice */
     for (int j = 0; j < K; j++) {
@@ -472,22 +491,73 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     __shared__ float part[kRouterBlock / 32];
     __shared__ unsigned int ticket;
     pdl_trigger();                   /* let gate/up start its table build */
-    const int lat = a.bank.lat;
+    const int lat = a.bank.lat, n4 = lat / 4;
     const int t = blockIdx.y;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const float *x = a.x + (size_t)t * lat;
-    for (int i = threadIdx.x; i < lat; i += blockDim.x) xs[i] = x[i];
-    __syncthreads();
     const int b = blockIdx.x;
-    if (b < rg.rblocks) {
-        /* two router rows per block, a quarter of the row per warp */
-        const int r = b * 2 + warp / kRouterSplit, qtr = warp % kRouterSplit;
-        const int n4 = lat / 4, per = (n4 + kRouterSplit - 1) / kRouterSplit;
-        const int q0 = qtr * per, q1 = min(n4, q0 + per);
-        float v = 0.0f;
-        if (r < a.E)
-            v = dot_f32_span<6>(a.router + (size_t)r * lat + 4 * q0, xs + 4 * q0, q1 - q0, lane);
-        if (lane == 0) part[warp] = v;
+    const bool is_router = b < rg.rblocks;
+    /* weight loads first */
+    float4 wr[kRouterU4];
+    uint4 wq[kShU];
+    uint16_t wsq[kShU];
+    int r = 0, q0 = 0, q1 = 0, kind = 0, o = -1;
+    const int ng = (lat + 127) / 128, nchunk = (lat + 15) / 16;
+    if (is_router) {
+        r = b * 2 + warp / kRouterSplit;
+        const int qtr = warp % kRouterSplit, per = (n4 + kRouterSplit - 1) / kRouterSplit;
+        q0 = qtr * per;
+        q1 = min(n4, q0 + per);
+        const float4 *w4 = reinterpret_cast<const float4 *>(a.router + (size_t)r * lat) + q0;
+#pragma unroll
+        for (int u = 0; u < kRouterU4; u++) {
+            const int i = u * 32 + lane;
+            wr[u] = (r < a.E && i < q1 - q0) ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    } else {
+        const int rr = (b - rg.rblocks) * (kRouterBlock / 32) + warp;
+        if (rr < 2 * a.si) {
+            kind = rr / a.si;
+            o = rr % a.si;
+            const int8_t *row = (kind ? a.shu : a.shg) + (size_t)o * ng * 128;
+            const uint16_t *ws = (kind ? a.shu_s : a.shg_s) + (size_t)o * ng;
+#pragma unroll
+            for (int u = 0; u < kShU; u++) {
+                const int c = u * 32 + lane;
+                wq[u] = c < nchunk ? ldg16(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+                wsq[u] = c < nchunk ? __ldg(ws + (c >> 3)) : (uint16_t)0;
+            }
+        }
+    }
+    /* then x */
+    {
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t * lat);
+        float4 xv[kXU];
+#pragma unroll
+        for (int u = 0; u < kXU; u++) {
+            const int i = threadIdx.x + u * kRouterBlock;
+            xv[u] = i < n4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kXU; u++) {
+            const int i = threadIdx.x + u * kRouterBlock;
+            if (i < n4) reinterpret_cast<float4 *>(xs)[i] = xv[u];
+        }
+    }
+    __syncthreads();
+    if (is_router) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xs) + q0;
+        float acc = 0.0f;
+#pragma unroll
+        for (int u = 0; u < kRouterU4; u++) {
+            const int i = u * 32 + lane;
+            if (i < q1 - q0) {
+                const float4 xv = x4[i];
+                acc = fmaf(wr[u].x, xv.x, acc); acc = fmaf(wr[u].y, xv.y, acc);
+                acc = fmaf(wr[u].z, xv.z, acc); acc = fmaf(wr[u].w, xv.w, acc);
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) part[warp] = acc;
         __syncthreads();
         if (threadIdx.x < 2) {
             const int rr = b * 2 + threadIdx.x;
@@ -496,17 +566,15 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
                 a.ws.logits[(size_t)t * a.E + rr] = ((p[0] + p[1]) + p[2]) + p[3];
             }
         }
-    } else {
-        const int rr = (b - rg.rblocks) * (kRouterBlock / 32) + warp;
-        if (rr < 2 * a.si) {
-            const int kind = rr / a.si, o = rr % a.si;
-            const int ng = (lat + 127) / 128;
-            const int8_t *W = kind ? a.shu : a.shg;
-            const uint16_t *S = kind ? a.shu_s : a.shg_s;
-            const float v = dot_q8g_row<5>(W + (size_t)o * ng * 128, S + (size_t)o * ng, xs,
-                                           lat, lane);
-            if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = v;
+    } else if (o >= 0) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int u = 0; u < kShU; u++) {
+            const int c = u * 32 + lane;
+            if (c < nchunk) acc += q8g_chunk(wq[u], f16_keep(wsq[u]), xs, c * 16, lat);
         }
+        acc = warp_sum(acc);
+        if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = acc;
     }
     /* the last block of this token routes it */
     __threadfence();
@@ -515,10 +583,22 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     __syncthreads();
     if (ticket != gridDim.x - 1) return;
     __threadfence();
-    if (warp == 0) route_warp(a, t, lane, xs, xs + a.E);   /* x is dead by now */
-    for (int i = threadIdx.x - 32; i >= 0 && i < a.si; i += blockDim.x - 32) {
-        const size_t o = (size_t)t * a.si + i;
-        a.ws.sh_h[o] = silu_ref(__ldcg(a.ws.sh_g + o)) * __ldcg(a.ws.sh_u + o);
+    if (warp == 0) {
+        route_warp(a, t, lane, xs, xs + a.E);      /* x is dead by now */
+    } else {
+        float g[kSiluU], u[kSiluU];
+        const int nt = blockDim.x - 32;
+#pragma unroll
+        for (int k = 0; k < kSiluU; k++) {
+            const int i = threadIdx.x - 32 + k * nt;
+            g[k] = i < a.si ? __ldcg(a.ws.sh_g + (size_t)t * a.si + i) : 0.0f;
+            u[k] = i < a.si ? __ldcg(a.ws.sh_u + (size_t)t * a.si + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kSiluU; k++) {
+            const int i = threadIdx.x - 32 + k * nt;
+            if (i < a.si) a.ws.sh_h[(size_t)t * a.si + i] = silu_ref(g[k]) * u[k];
+        }
     }
     if (threadIdx.x == 0) a.ws.tickets[t] = 0;       /* ready for the next launch */
 }
@@ -533,11 +613,17 @@ __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const in
 
 /* ---- 2. gate/up ------------------------------------------------------------
  * tile = (token, kind, slice, expert group): one table slice shared by the
- * rows of every expert in the group. After the tile, the block runs its
- * share of the shared expert's down rows ([lat][si] Q8G, one warp per row). */
+ * rows of every expert in the group; every thread holds all its positions
+ * (kGuNP) in registers. Before the wait: x, the codebook rows and the table,
+ * plus this block's share of the shared expert's down rows (weights only).
+ * After: the routed rows, then the shared down rows with SiLU(g)*u. */
+constexpr int kGuNP = 4;               /* positions per gate/up thread      */
+constexpr int kGuBooks = 2;            /* codebook rows per thread (768/512) */
+constexpr int kShdU = 4;               /* shared down: 16-byte chunks per lane, si <= 2048 */
+
 template <int ST>
-__global__ void __launch_bounds__(512)
-gateup_kernel(wc_moe_args a, TileGeom g, int gu_tiles, int sh_rows_pb, const int *idx)
+__global__ void __launch_bounds__(512, 1)
+gateup_kernel(wc_moe_args a, TileGeom g, int sh_rows_pb, const int *idx)
 {
     extern __shared__ float smem[];
     float *xs = smem, *lut = smem + g.Vs * kVecDim;
@@ -547,45 +633,97 @@ gateup_kernel(wc_moe_args a, TileGeom g, int gu_tiles, int sh_rows_pb, const int
     const int kind = b % 2; const int t = b / 2;
     const wc_bank &bk = a.bank;
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
-    /* routing-independent: x slice and the table */
-    const float *xt = a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim;
-    for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xt[i];
+    /* routing-independent loads: x slice, codebook rows, shared down rows */
+    BookRows<ST, kGuBooks> books;
+    books.load(a.books, bk.cb_base + kind * ST);
+    float xv = 0.0f;
+    if ((int)threadIdx.x < nvs * kVecDim)
+        xv = __ldg(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
+    const int warps = blockDim.x / 32, lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    const int lin = (kind * g.ns + slice) * g.groups + grp;
+    const bool do_shared = a.si > 0 && t == 0 && sh_rows_pb > 0;
+    const int ngs = (a.si + 127) / 128, nchs = (a.si + 15) / 16;
+    /* the warp's first shared down row is prefetched; further rows (small
+     * shapes, more rows than warps) load when they are reached */
+    const int o0 = lin * sh_rows_pb + warp;
+    uint4 shq[kShdU];
+    uint16_t shs[kShdU];
+    if (do_shared && warp < sh_rows_pb && o0 < bk.lat) {
+#pragma unroll
+        for (int u = 0; u < kShdU; u++) {
+            const int c = u * 32 + lane;
+            shq[u] = c < nchs ? ldg16(a.shd + (size_t)o0 * ngs * 128 + (size_t)c * 16)
+                              : make_uint4(0, 0, 0, 0);
+            shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o0 * ngs + (c >> 3)) : (uint16_t)0;
+        }
+    }
+    if ((int)threadIdx.x < nvs * kVecDim) xs[threadIdx.x] = xv;
     __syncthreads();
-    build_lut_slice<ST>(lut, xs, a.books, bk.cb_base + kind * ST, nvs);
+    books.build(lut, xs, nvs);
     pdl_wait();                      /* routing (and all earlier work) is done */
     pdl_trigger();
     const int j0 = grp * g.EG;
     const int nm = min(g.EG, a.K - j0);
-    const int m = min(TileThread<ST>::matrix_of_thread(g), nm - 1);
+    const int m = min(TileThread<ST, GatherAll<ST, kGuNP>>::matrix_of_thread(g), nm - 1);
     const uint8_t *mat = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off);
-    TileThread<ST> th(g, slice, nm, mat);
+    TileThread<ST, GatherAll<ST, kGuNP>> th(g, slice, nm, mat);
     __syncthreads();
     float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
     th.finish(g, lut, out, bk.inter, nm);
-    if (a.si <= 0 || t != 0 || sh_rows_pb <= 0) return;
-    /* shared expert down rows for every token: rows [blk*R, blk*R + R) */
+    if (!do_shared) return;
+    /* shared expert down rows of every token (token 0's tiles do them) */
     for (int tt = 0; tt < a.T; tt++) {
         __syncthreads();
         float *hs = smem;
-        for (int i = threadIdx.x; i < a.si; i += blockDim.x) hs[i] = __ldcg(a.ws.sh_h + (size_t)tt * a.si + i);
+        for (int i = threadIdx.x; i < a.si; i += blockDim.x)
+            hs[i] = __ldcg(a.ws.sh_h + (size_t)tt * a.si + i);
         __syncthreads();
-        const int warps = blockDim.x / 32;
-        const int ng = (a.si + 127) / 128;
-        const int lin = ((kind * g.ns + slice) * g.groups + grp);
-        for (int rr = threadIdx.x / 32; rr < sh_rows_pb; rr += warps) {
+        for (int rr = warp; rr < sh_rows_pb; rr += warps) {
             const int o = lin * sh_rows_pb + rr;
             if (o >= bk.lat) break;
-            const float v = dot_q8g_row<2>(a.shd + (size_t)o * ng * 128, a.shd_s + (size_t)o * ng,
-                                           hs, a.si, threadIdx.x % 32);
-            if (threadIdx.x % 32 == 0) a.ws.sh_out[(size_t)tt * bk.lat + o] = v;
+            if (rr != warp) {
+#pragma unroll
+                for (int u = 0; u < kShdU; u++) {
+                    const int c = u * 32 + lane;
+                    shq[u] = c < nchs ? ldg16(a.shd + (size_t)o * ngs * 128 + (size_t)c * 16)
+                                      : make_uint4(0, 0, 0, 0);
+                    shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o * ngs + (c >> 3)) : (uint16_t)0;
+                }
+            }
+            float acc = 0.0f;
+#pragma unroll
+            for (int u = 0; u < kShdU; u++) {
+                const int c = u * 32 + lane;
+                if (c < nchs) acc += q8g_chunk(shq[u], f16_keep(shs[u]), hs, c * 16, a.si);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) a.ws.sh_out[(size_t)tt * bk.lat + o] = acc;
+        }
+        if (a.T > 1 && sh_rows_pb > warps) {
+            /* reload the first rows for the next token */
+            const int o = lin * sh_rows_pb + warp;
+            if (warp < sh_rows_pb && o < bk.lat) {
+#pragma unroll
+                for (int u = 0; u < kShdU; u++) {
+                    const int c = u * 32 + lane;
+                    shq[u] = c < nchs ? ldg16(a.shd + (size_t)o * ngs * 128 + (size_t)c * 16)
+                                      : make_uint4(0, 0, 0, 0);
+                    shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o * ngs + (c >> 3)) : (uint16_t)0;
+                }
+            }
         }
     }
 }
 
 /* ---- 3. down ---------------------------------------------------------------
- * tile = (token, expert j, slice). The expert's down index loads go out
- * before the wait (the route is known by then: gate/up started after it);
- * h = SiLU(g)*u for the slice's inputs comes from the gate/up partials. */
+ * tile = (token, expert j, slice). Before the wait (the route is known:
+ * gate/up started after it): the expert's down index loads, its gate/up row
+ * scales for the slice's inputs, the codebook rows. After: the gate/up
+ * slice sums (every load issued at once), SiLU(g)*u, the table, the gather. */
+constexpr int kDnNP = 3;               /* positions per down thread         */
+constexpr int kDnBooks = 2;            /* codebook rows per thread (768/432) */
+constexpr int kDnSlices = 12;          /* gate/up slices summed per thread  */
+
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
 down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
@@ -597,26 +735,42 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
     const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
-    TileThread<ST> th(g, slice, 1, rec + bk.down_off);
+    TileThread<ST, GatherAll<ST, kDnNP>> th(g, slice, 1, rec + bk.down_off);
+    BookRows<ST, kDnBooks> books;
+    books.load(a.books, bk.cb_base + 2 * ST);
+    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
+    const int nin = nvs * kVecDim;
+    const int inter = bk.inter;
+    const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
+    float sg_scale = 0.0f, su_scale = 0.0f;
+    if ((int)threadIdx.x < nin) {
+        const int n = v0 * kVecDim + threadIdx.x;
+        sg_scale = f16_keep(__ldg(sc + n));
+        su_scale = f16_keep(__ldg(sc + inter + n));
+    }
     pdl_trigger();
     pdl_wait();                      /* gate/up partials are complete */
-    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
-    const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
-    const int inter = bk.inter;
     const size_t sstride = (size_t)a.K * inter;
     const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * sstride + (size_t)j * inter;
     const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * sstride + (size_t)j * inter;
-    /* gate/up slice sums with the whole block: part p of P adds slices
-     * p, p+P, ...; parts are then added in order */
-    const int nin = nvs * kVecDim;
+    /* part p of P sums slices p, p+P, ... (at most kDnSlices of them, all
+     * loads issued at once); parts are then added in order */
     const int P = max(1, (int)blockDim.x / nin);
     float *red2 = lut;                         /* [P][2][nin], before the table */
     if ((int)threadIdx.x < P * nin) {
         const int i = threadIdx.x % nin, p = threadIdx.x / nin;
         const int n = v0 * kVecDim + i;
+        float vg[kDnSlices], vu[kDnSlices];
+#pragma unroll
+        for (int k = 0; k < kDnSlices; k++) {
+            const int s2 = p + k * P;
+            vg[k] = s2 < gu.ns ? __ldcg(pg + (size_t)s2 * sstride + n) : 0.0f;
+            vu[k] = s2 < gu.ns ? __ldcg(pu + (size_t)s2 * sstride + n) : 0.0f;
+        }
         float sg = 0.0f, su = 0.0f;
-#pragma unroll 4
-        for (int s2 = p; s2 < gu.ns; s2 += P) {
+#pragma unroll
+        for (int k = 0; k < kDnSlices; k++) { sg += vg[k]; su += vu[k]; }
+        for (int s2 = p + kDnSlices * P; s2 < gu.ns; s2 += P) {       /* not at our shapes */
             sg += __ldcg(pg + (size_t)s2 * sstride + n);
             su += __ldcg(pu + (size_t)s2 * sstride + n);
         }
@@ -625,18 +779,16 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
     }
     __syncthreads();
     if ((int)threadIdx.x < nin) {
-        const int i = threadIdx.x, n = v0 * kVecDim + i;
+        const int i = threadIdx.x;
         float sg = 0.0f, su = 0.0f;
         for (int p = 0; p < P; p++) {
             sg += red2[(p * 2 + 0) * nin + i];
             su += red2[(p * 2 + 1) * nin + i];
         }
-        const float gv = sg * f16_keep(sc[n]);
-        const float uv = su * f16_keep(sc[inter + n]);
-        xs[i] = silu_ref(gv) * uv;
+        xs[i] = silu_ref(sg * sg_scale) * (su * su_scale);
     }
     __syncthreads();
-    build_lut_slice<ST>(lut, xs, a.books, bk.cb_base + 2 * ST, nvs);
+    books.build(lut, xs, nvs);
     __syncthreads();
     float *out = a.ws.p_d + (((size_t)t * a.K + j) * g.ns + slice) * bk.lat;
     th.finish(g, lut, out, 0, 1);
@@ -646,40 +798,52 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
  * out[t][i] = sum_j w[j] * (f16(scale_down_j[i]) * sum_s P_d[t][j][s][i]),
  * j in router order (src/model.c:2908-2909) — or in ascending expert id
  * when order_by_id (moe_chunk, src/model.c:3632-3656) — then + shared.
- * Block: 32 outputs x 8 expert lanes. */
-constexpr int kMaxSlicesReg = 32;
+ * Block: 32 outputs x 8 expert lanes; every load issued up front. */
+constexpr int kMaxSlicesReg = 16;
 
 __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
                                                       const int *idx, const float *w)
 {
     __shared__ float accj[kMaxTopK][32];
     __shared__ int order[kMaxTopK];
+    __shared__ float wsm[kMaxTopK];
     const wc_bank &bk = a.bank;
     const int t = blockIdx.y, K = a.K;
     const int il = threadIdx.x % 32, jl = threadIdx.x / 32;
     const int i = blockIdx.x * 32 + il;
     const int *it = idx + (size_t)t * K;
+    const bool ok = i < bk.lat;
     /* before the wait: the row scales (the route is complete by now) */
-    float scl[kMaxTopK / 8];
-    for (int j = jl, n = 0; j < K; j += 8, n++) {
+    constexpr int kJ = kMaxTopK / 8;
+    float scl[kJ];
+#pragma unroll
+    for (int n = 0; n < kJ; n++) {
+        const int j = jl + 8 * n;
         scl[n] = 0.0f;
-        if (i < bk.lat) {
+        if (j < K && ok) {
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(
                 bk.base + (size_t)(__ldcg(it + j) - bk.first) * bk.rec_bytes + bk.scale_off) +
                 2 * bk.inter;
-            scl[n] = f16_keep(sc[i]);
+            scl[n] = f16_keep(__ldg(sc + i));
         }
     }
     pdl_wait();
-    for (int j = jl, n = 0; j < K; j += 8, n++) {
+    if (threadIdx.x < K) wsm[threadIdx.x] = __ldcg(w + (size_t)t * K + threadIdx.x);
+    const float shv = (a.si > 0 && jl == 0 && ok) ? __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i)
+                                                 : 0.0f;
+#pragma unroll
+    for (int n = 0; n < kJ; n++) {
+        const int j = jl + 8 * n;
+        if (j >= K) break;
         float s = 0.0f;
-        if (i < bk.lat) {
+        if (ok) {
             const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
             float v[kMaxSlicesReg];
 #pragma unroll
             for (int k = 0; k < kMaxSlicesReg; k++)
                 v[k] = k < g.ns ? __ldcg(p + (size_t)k * bk.lat) : 0.0f;
-            for (int k = 0; k < g.ns && k < kMaxSlicesReg; k++) s += v[k];
+#pragma unroll
+            for (int k = 0; k < kMaxSlicesReg; k++) s += v[k];
             for (int k = kMaxSlicesReg; k < g.ns; k++) s += __ldcg(p + (size_t)k * bk.lat);
             s *= scl[n];
         }
@@ -701,17 +865,16 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         }
     }
     __syncthreads();
-    if (jl != 0 || i >= bk.lat) return;
-    const float *wt = w + (size_t)t * K;
+    if (jl != 0 || !ok) return;
     float y = 0.0f;
     for (int n = 0; n < K; n++) {
         const int j = order[n];
         if (j < 0) break;
-        const float wj = __ldcg(wt + j);
+        const float wj = wsm[j];
         if (a.order_by_id && wj == 0.0f) continue;
         y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
     }
-    if (a.si > 0) y = __fadd_rn(y, __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i));
+    if (a.si > 0) y = __fadd_rn(y, shv);
     a.out[(size_t)t * bk.lat + i] = y;
 }
 
@@ -728,12 +891,32 @@ MoeGeom moe_geom(const wc_moe_args *a)
     MoeGeom m;
     const wc_bank &b = a->bank;
     m.gu = make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512);
-    m.d = make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 512);
+    m.d = make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
     m.d_tiles = a->T * a->K * m.d.ns;
     const int per_t = 2 * m.gu.ns * m.gu.groups;      /* token-0 tiles run the shared rows */
     m.sh_rows_pb = a->si > 0 ? (b.lat + per_t - 1) / per_t : 0;
     return m;
+}
+
+/* The register-resident forms hold a fixed number of positions per thread;
+ * shapes outside these bounds are refused by the host. */
+bool moe_geom_ok(const MoeGeom &m, const wc_moe_args *a)
+{
+    if (!a->router) {   /* router/shared limits only apply to the whole layer */
+        const int gu_pos = (m.gu.Vs + m.gu.nlanes - 1) / m.gu.nlanes;
+        const int d_pos = (m.d.Vs + m.d.nlanes - 1) / m.d.nlanes;
+        return gu_pos <= kGuNP && d_pos <= kDnNP && m.d.ns <= kMaxSlicesReg * 8 &&
+               a->K <= kMaxTopK;
+    }
+    const int gu_pos = (m.gu.Vs + m.gu.nlanes - 1) / m.gu.nlanes;
+    const int d_pos = (m.d.Vs + m.d.nlanes - 1) / m.d.nlanes;
+    if (gu_pos > kGuNP || d_pos > kDnNP) return false;
+    if (a->bank.lat > 4 * 32 * kRouterU4 * kRouterSplit || a->bank.lat > 16 * 32 * kShU) return false;
+    if (a->bank.lat > 4 * kRouterBlock * kXU) return false;
+    if (a->si > 16 * 32 * kShdU || a->si > (kRouterBlock - 32) * kSiluU) return false;
+    if (m.d.ns > kMaxSlicesReg * 8 || a->K > kMaxTopK) return false;
+    return true;
 }
 
 template <typename... KArgs, typename... Args>
@@ -757,6 +940,7 @@ template <int ST>
 int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
 {
     const MoeGeom m = moe_geom(a);
+    if (!moe_geom_ok(m, a)) return (int)cudaErrorInvalidValue;
     const int *idx = a->idx;
     const float *w = a->w;
     bool pdl = false;
@@ -783,7 +967,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
                          (int)gsmem);
     int pe = prof_begin(WC_PH_GATEUP, s);
     e = launch(gateup_kernel<ST>, dim3(m.gu_tiles), dim3(m.gu.threads), gsmem, s, pdl && !prof,
-               *a, m.gu, m.gu_tiles, a->router ? m.sh_rows_pb : 0, idx);
+               *a, m.gu, a->router ? m.sh_rows_pb : 0, idx);
     prof_end(pe, s);
     if (e != cudaSuccess) return (int)e;
     cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -810,7 +994,7 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
                                    int stages)
 {
     const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
-    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 512);
+    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     size_t n = 0;
     n += (size_t)T * 2 * gu.ns * K * inter;
     n += (size_t)T * K * d.ns * lat;
@@ -824,7 +1008,7 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
                                 int lat, int inter, int si, int stages)
 {
     const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
-    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 512);
+    const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     float *p = base;
     ws->tickets = reinterpret_cast<unsigned int *>(p); p += 64;   /* first: stays put */
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
@@ -834,6 +1018,12 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     ws->sh_u = p; p += (size_t)T * si;
     ws->sh_h = p; p += (size_t)T * si;
     ws->sh_out = p;
+}
+
+extern "C" int wc_moe_supported(const wc_moe_args *a)
+{
+    const MoeGeom m = moe_geom(a);
+    return moe_geom_ok(m, a) ? 0 : -1;
 }
 
 extern "C" int wc_moe_launch(const wc_moe_args *a, void *stream)

@@ -560,6 +560,7 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
     a.w = S.d_w;
     a.out = S.d_out;
     a.order_by_id = order_by_id;
+    if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
     CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
     CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "ysum D2H");
     CK(cudaStreamSynchronize(S.stream), "expert loop");
@@ -605,6 +606,9 @@ static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
     a->routed_scale = L->routed_scale;
     a->shg = L->d_shg; a->shu = L->d_shu; a->shd = L->d_shd;
     a->shg_s = L->d_shg_s; a->shu_s = L->d_shu_s; a->shd_s = L->d_shd_s;
+    if (wc_moe_supported(a))
+        return fail(WASTE_CUDA_E_ARG, "layer %d: shape outside the kernels' bounds "
+                    "(hidden <= 3072, shared inter <= 1792, experts <= 1024)", layer);
     *Lp = L;
     return 0;
 }
