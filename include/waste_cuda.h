@@ -167,6 +167,15 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed,
 int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
                              int *d_idx, float *d_w, void *stream);
 
+/* Sticky error bits raised on the device. The layer path hands the route
+ * from the router kernel to the gate/up kernel through a flag; that wait is
+ * bounded, and when it runs out it sets WASTE_CUDA_DERR_ROUTE_WAIT and the
+ * waiting kernel skips its work instead of hanging. The host form of
+ * moe_layer checks this itself; callers of the _dev form call this after
+ * synchronising. Waits for the library's stream; reading clears the bits. */
+#define WASTE_CUDA_DERR_ROUTE_WAIT 1u
+unsigned waste_cuda_device_errors(void);
+
 /* ---- single VQ3R kernels ---------------------------------------------------
  * lutb: lut[nv][stages][entries] = sum_d x[8v+d] * C_{cb_base+s}[c][d], an
  * FMA chain from 0 in d order — bit-identical to the reference's AVX2 and

@@ -28,6 +28,7 @@ EXPORTS = (
     "waste_cuda_moe_layer_dev", "waste_cuda_lutb", "waste_cuda_vq_matvec",
     "waste_cuda_vq_dequant", "waste_cuda_vq_matvec_dev",
     "waste_cuda_launch_count", "waste_cuda_profile", "waste_cuda_profile_read",
+    "waste_cuda_device_errors",
 )
 
 PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -111,6 +112,7 @@ def load_library() -> C.CDLL:
         "waste_cuda_launch_count": (C.c_uint64, []),
         "waste_cuda_profile": (C.c_int, [C.c_int]),
         "waste_cuda_profile_read": (C.c_int, [P, P, C.c_int]),
+        "waste_cuda_device_errors": (C.c_uint, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -155,6 +157,11 @@ def register_cuda_vq() -> VqSlots:
     s = VqSlots()
     _check(load_library().waste_register_cuda_vq(C.byref(s)))
     return s
+
+
+def device_errors() -> int:
+    """Sticky device error bits (WASTE_CUDA_DERR_*); reading clears them."""
+    return int(load_library().waste_cuda_device_errors())
 
 
 def launch_count() -> int:

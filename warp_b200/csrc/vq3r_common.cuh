@@ -44,6 +44,40 @@ __device__ __forceinline__ uint4 ldg16(const void *p)
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
+/* Loads that must be ISSUED where they are written: a prefetch into
+ * registers ahead of a barrier or a grid-dependency wait. A read-only (.nc)
+ * load may legally be sunk to its first use or issued again there, which
+ * turns the prefetch into a stall; a volatile coherent load is neither. */
+__device__ __forceinline__ uint4 ld_pin16(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float4 ld_pin_f4(const void *p)
+{
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint16_t ld_pin_u16(const void *p)
+{
+    unsigned short v;
+    asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float ld_pin_f32(const void *p)
+{
+    float v;
+    asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 /* Builds the table slice for vector positions [v0, v0+nvs) of one matrix
  * family into shared memory:
  *   lut[(v - v0)*ST*256 + s*256 + c] = fma chain over d of x[8v+d]*C[cb+s][c][d]
@@ -106,7 +140,7 @@ struct Gather16 {
     {
 #pragma unroll
         for (int i = 0; i < ST; i++) {
-            const uint4 q = ldg16(src + 16 * i);
+            const uint4 q = ld_pin16(src + 16 * i);
             dst[4 * i] = q.x; dst[4 * i + 1] = q.y; dst[4 * i + 2] = q.z; dst[4 * i + 3] = q.w;
         }
     }
@@ -181,8 +215,8 @@ struct BookRows {
                 const int s = i / kEntries, code = i % kEntries;
                 const float4 *src = reinterpret_cast<const float4 *>(
                     books + ((size_t)(cb + s) * kEntries + code) * kVecDim);
-                c[k][0] = __ldg(src);
-                c[k][1] = __ldg(src + 1);
+                c[k][0] = ld_pin_f4(src);
+                c[k][1] = ld_pin_f4(src + 1);
             }
         }
     }
@@ -209,6 +243,121 @@ struct BookRows {
                 for (int d = 0; d < kVecDim; d++) acc = __fmaf_rn(xv[d], C[d], acc);
                 lut[(v * ST + s) * kEntries + code] = acc;
             }
+        }
+    }
+};
+
+/* ---- TMA bulk copies into shared memory ----------------------------------
+ * cp.async.bulk (the untiled TMA form) moves a contiguous run of global
+ * memory into this CTA's shared memory and signals an mbarrier with the byte
+ * count; both addresses 16-byte aligned, the size a multiple of 16. The
+ * copy is issued where it is written and holds no registers, which is what
+ * a prefetch ahead of a grid-dependency wait needs. No multicast. */
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+/* Make the initialised barrier visible to the async (TMA) proxy. */
+__device__ __forceinline__ void mbar_fence_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+/* Bounded wait for phase `parity` of the barrier: false after kMbarLimit
+ * polls (each try_wait also suspends for a while), so a copy that never
+ * lands ends the wait instead of the kernel. */
+constexpr int kMbarLimit = 1 << 22;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+{
+    for (int i = 0; i < kMbarLimit; i++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+/* The index stream of one quarter-block staged in shared memory:
+ * base points at the quarter's 16*ST bytes of its first position,
+ * consecutive positions `pstride` bytes apart. */
+template <int ST>
+__device__ __forceinline__ void gather_smem(float *acc, const uint8_t *base, int pstride,
+                                            const float *L, int nvv)
+{
+    constexpr int W = 4 * ST;
+    for (int v = 0; v < nvv; v++) {
+        uint32_t w[W];
+        const uint4 *src = reinterpret_cast<const uint4 *>(base + (size_t)v * pstride);
+#pragma unroll
+        for (int i = 0; i < ST; i++) {
+            const uint4 q = src[i];
+            w[4 * i] = q.x; w[4 * i + 1] = q.y; w[4 * i + 2] = q.z; w[4 * i + 3] = q.w;
+        }
+        RowStep<ST, 0>::run(acc, w, L + (size_t)v * ST * kEntries);
+    }
+}
+
+/* Gather policy for index streams staged in shared memory by TMA (layout
+ * [row block][position][64][ST], i.e. positions 64*ST bytes apart). The
+ * positions before `split` land on bar0, the rest on bar1 (bar1 may be
+ * null when there is one phase); each wait is bounded and a failure is
+ * reported through `ok`. */
+template <int ST>
+struct GatherSmem {
+    const uint8_t *p;
+    int n, first;             /* positions [first, first+n) of the slice */
+    uint64_t *bar0, *bar1;
+    int split;
+    bool ok;
+
+    __device__ __forceinline__ void begin(const uint8_t *p0, int nvv)
+    {
+        p = p0;
+        n = nvv;
+        ok = true;
+    }
+
+    __device__ __forceinline__ void run(float *acc, const float *L)
+    {
+        const int stride = kBlock * ST;
+        if (bar1 == nullptr) {
+            ok = mbar_wait(bar0, 0);
+            if (ok) gather_smem<ST>(acc, p, stride, L, n);
+            return;
+        }
+        const int n0 = max(0, min(n, split - first));
+        if (n0 > 0) {
+            ok = mbar_wait(bar0, 0);
+            if (!ok) return;
+            gather_smem<ST>(acc, p, stride, L, n0);
+        }
+        if (n0 < n) {
+            ok = mbar_wait(bar1, 0);
+            if (!ok) return;
+            gather_smem<ST>(acc, p + (size_t)n0 * stride, stride, L + (size_t)n0 * ST * kEntries,
+                            n - n0);
         }
     }
 };

@@ -117,7 +117,24 @@ struct TileGeom {
     int Q;            /* quarter-blocks per tile (threads per lane)          */
     int nlanes;
     int threads;
-    size_t smem;      /* bytes: xs + max(table, lane reduction)              */
+    size_t region;    /* floats: max(table, lane reduction), 16-byte multiple */
+    size_t stage;     /* bytes of TMA-staged index streams (0: streamed)     */
+    size_t smem;      /* bytes: barriers + xs + region + stage               */
+};
+
+/* Shared-memory carve-up of a tile: two mbarriers, the slice's inputs, the
+ * table / lane-reduction region, then the staged index streams. */
+struct TileSmem {
+    uint64_t *bars;
+    float *xs, *lut;
+    uint8_t *stage;
+    __device__ __forceinline__ TileSmem(unsigned char *raw, const TileGeom &g)
+    {
+        bars = reinterpret_cast<uint64_t *>(raw);
+        xs = reinterpret_cast<float *>(raw + 16);
+        lut = xs + ((g.Vs * kVecDim + 3) & ~3);
+        stage = reinterpret_cast<uint8_t *>(lut + g.region);
+    }
 };
 
 constexpr int kMaxTileRows = 8192;
@@ -146,7 +163,19 @@ TileGeom make_geom(int M, int N, int nmat, int Vs, int stages, int target_thread
     const size_t red = (size_t)nl * g.EG * g.nrb * kBlock;
     size_t region = lut > red ? lut : red;
     if (region < (size_t)2 * g.threads) region = (size_t)2 * g.threads;  /* down prologue */
-    g.smem = ((size_t)g.Vs * kVecDim + region) * sizeof(float);
+    g.region = (region + 3) & ~(size_t)3;
+    g.stage = 0;
+    g.smem = 16 + (((size_t)g.Vs * kVecDim + 3) & ~(size_t)3) * sizeof(float) +
+             g.region * sizeof(float);
+    return g;
+}
+
+/* The same tile with its index streams staged in shared memory by TMA:
+ * every (matrix, row block) of the group, the slice's positions. */
+TileGeom with_stage(TileGeom g, int stages)
+{
+    g.stage = (size_t)g.EG * g.nrb * g.Vs * kBlock * stages;
+    g.smem += g.stage;
     return g;
 }
 
@@ -199,6 +228,22 @@ struct TileThread {
 #pragma unroll
         for (int k = 0; k < kRowsPerThread; k++) acc[k] = 0.0f;
         if (active) G.run(acc, lut + (size_t)vl0 * ST * kEntries);
+        if (g.nlanes == 1) {             /* the thread owns its rows outright */
+            if (!active) return;
+            const int row0 = rbl * kBlock + q * 16;
+            float *dst = out + (size_t)m * mstride + row0;
+            if (row0 + 16 <= g.M && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+                for (int k = 0; k < kRowsPerThread; k += 4)
+                    *reinterpret_cast<float4 *>(dst + k) =
+                        make_float4(acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < kRowsPerThread; k++)
+                    if (row0 + k < g.M) dst[k] = acc[k];
+            }
+            return;
+        }
         __syncthreads();                 /* the table is dead; reuse it */
         float *red = lut;
         const int R = g.EG * g.nrb * kBlock;
@@ -227,8 +272,9 @@ template <int ST>
 __global__ void __launch_bounds__(512)
 matvec_tiles_kernel(TileGeom g, const wc_matvec_args a)
 {
-    extern __shared__ float smem[];
-    float *xs = smem, *lut = smem + g.Vs * kVecDim;
+    extern __shared__ __align__(16) unsigned char smraw[];
+    TileSmem sm(smraw, g);
+    float *xs = sm.xs, *lut = sm.lut;
     const int gi = blockIdx.x / g.ns, slice = blockIdx.x % g.ns;
     TileThread<ST> th(g, slice, 1, a.idx[gi]);
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
@@ -314,6 +360,73 @@ __global__ void dequant_kernel(float *W, const uint8_t *idx, const uint16_t *sca
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+/* Ask L2 to fetch [p, p+bytes) from HBM (no registers, no shared memory:
+ * cp.async.bulk.prefetch.L2). p 16-byte aligned, bytes a multiple of 16. */
+__device__ __forceinline__ void l2_prefetch(const void *p, size_t bytes)
+{
+    const char *c = static_cast<const char *>(p);
+    constexpr size_t kChunk = 64 * 1024;
+    for (size_t off = 0; off < bytes; off += kChunk) {
+        const uint32_t n = (uint32_t)(bytes - off < kChunk ? bytes - off : kChunk);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c + off), "r"(n) : "memory");
+    }
+}
+
+__device__ __forceinline__ void st_release(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.gpu.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int *p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+/* Spins on a flag another CTA of an earlier kernel publishes. The kernels
+ * that wait are launched only after every CTA of the publisher has started
+ * (programmatic launch), so the publisher never waits for a slot they hold.
+ * Bounded: after kSpinLimit polls (well over a second) the wait gives up,
+ * records WC_ERR_ROUTE_WAIT and reports failure. */
+constexpr long long kSpinLimit = 1ll << 24;
+
+__device__ __forceinline__ bool wait_flag(const unsigned int *flag, unsigned int *err)
+{
+    for (long long i = 0; i < kSpinLimit; i++) {
+        if (ld_acquire(flag)) return true;
+        __nanosleep(64);
+    }
+    atomicOr(err, WC_ERR_ROUTE_WAIT);
+    return false;
+}
+
+/* fetch-and-add with acquire-release semantics at GPU scope */
+__device__ __forceinline__ unsigned int atomic_add_acq_rel(unsigned int *p, unsigned int v)
+{
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+/* dst[0..n) = src[0..n) (global, written by an earlier phase) into shared
+ * memory: every thread's loads issued before any store. n <= 8*blockDim. */
+__device__ __forceinline__ void stage_floats(float *dst, const float *src, int n)
+{
+    constexpr int U = 8;
+    float v[U];
+#pragma unroll
+    for (int k = 0; k < U; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        v[k] = i < n ? __ldcg(src + i) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < U; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n) dst[i] = v[k];
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
@@ -349,50 +462,27 @@ __device__ __forceinline__ float dot_f32_span(const float *__restrict__ w, const
 }
 
 /* Q8G row (src/model.c:265-320 layout: int8 rows padded to whole groups of
- * 128, one f16 scale per group) . xs. Chunk c is inputs [16c, 16c+16) of
- * group c/8; inputs at or past n are skipped. All loads issued first. */
-__device__ __forceinline__ float q8g_chunk(uint4 q, float sc, const float *xs, int b0, int n)
+ * 128, one f16 scale per group) . x, with the row and its group scales in
+ * shared memory. Step s
+ * covers group s: lane l takes weights [128s + 4l, 128s + 4l + 4) (one
+ * 32-bit word) and the matching float4 of x, so a warp step reads 128
+ * contiguous weight bytes and 512 contiguous x bytes — no bank conflicts.
+ * n must be a multiple of 4. */
+__device__ __forceinline__ float dot_q8g_smem(const uint8_t *row, const float *gsc,
+                                              const float *xs, int n, int lane)
 {
-    const uint32_t wv[4] = { q.x, q.y, q.z, q.w };
-    float part = 0.0f;
-    if (b0 + 16 <= n) {
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs + b0);
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float4 xv = x4[k];
-            const uint32_t wd = wv[k];
-            part = fmaf((float)(int8_t)(wd & 0xff), xv.x, part);
-            part = fmaf((float)(int8_t)((wd >> 8) & 0xff), xv.y, part);
-            part = fmaf((float)(int8_t)((wd >> 16) & 0xff), xv.z, part);
-            part = fmaf((float)(int8_t)(wd >> 24), xv.w, part);
-        }
-    } else {
-        for (int i = 0; b0 + i < n; i++)
-            part = fmaf((float)(int8_t)((wv[i >> 2] >> (8 * (i & 3))) & 0xff), xs[b0 + i], part);
-    }
-    return sc * part;
-}
-
-template <int U>
-__device__ __forceinline__ float dot_q8g_row(const int8_t *__restrict__ row,
-                                             const uint16_t *__restrict__ ws,
-                                             const float *xs, int n, int lane)
-{
-    const int nchunk = (n + 15) / 16;
+    const int ng = (n + 127) / 128;
     float acc = 0.0f;
-    for (int base = 0; base < nchunk; base += 32 * U) {
-        uint4 q[U];
-        uint16_t sh[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int c = base + u * 32 + lane;
-            q[u] = c < nchunk ? ldg16(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-            sh[u] = c < nchunk ? __ldg(ws + (c >> 3)) : (uint16_t)0;
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int c = base + u * 32 + lane;
-            if (c < nchunk) acc += q8g_chunk(q[u], f16_keep(sh[u]), xs, c * 16, n);
+    for (int s = 0; s < ng; s++) {
+        const int i = s * 128 + lane * 4;
+        if (i < n) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+            const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
+            float part = (float)(int8_t)(w & 0xff) * xv.x;
+            part = fmaf((float)(int8_t)((w >> 8) & 0xff), xv.y, part);
+            part = fmaf((float)(int8_t)((w >> 16) & 0xff), xv.z, part);
+            part = fmaf((float)(int8_t)(w >> 24), xv.w, part);
+            acc = fmaf(gsc[s], part, acc);
         }
     }
     return warp_sum(acc);
@@ -412,58 +502,61 @@ constexpr int kMaxPerLane = 32;        /* E <= 1024 (one live bit per lane entry
 constexpr int kSiluU = 8;              /* shared SiLU inputs per thread: si <= 1792 */
 
 struct RouterGeom {
-    int rblocks;     /* blocks for the router rows (2 rows per block)        */
-    int sblocks;     /* blocks for the shared gate/up rows (8 per block)     */
+    int rblocks;       /* blocks for the router rows (2 rows per block)      */
+    int sblocks;       /* blocks for the shared gate/up rows (8 per block)   */
+    int sblocks_base;  /* = rblocks                                          */
 };
 
+/* Shared rows go 8 to a block and never straddle the gate/up boundary
+ * (si % 8 == 0, checked by the host), so each block's rows are one
+ * contiguous run for TMA. */
 __host__ __device__ inline RouterGeom router_geom(int E, int si)
 {
     RouterGeom g;
     const int rows_pb = (kRouterBlock / 32) / kRouterSplit;
     g.rblocks = (E + rows_pb - 1) / rows_pb;
-    g.sblocks = (2 * si + (kRouterBlock / 32) - 1) / (kRouterBlock / 32);
+    g.sblocks = 2 * ((si + (kRouterBlock / 32) - 1) / (kRouterBlock / 32));
+    g.sblocks_base = g.rblocks;
     return g;
 }
 
-/* Routing, src/model.c:2724-2747, by one warp: the E scores in shared
- * memory (score = 1/(1+expf(-logit)), plus the bias, or plus 0.0f when
- * there is none); K rounds of argmax: within a lane the ids ascend and the
- * comparison is a strict >, across lanes the larger value wins and equal
- * values go to the lower id — so the lowest id wins a tie and a NaN never
- * wins, exactly as the sequential scan from -1e30f does. w = score[best];
- * renorm by (sum + 1e-20f) accumulated in j order; times routed_scale. */
-__device__ void route_warp(const wc_moe_args &a, int t, int lane, float *sc, float *v)
+/* Routing, src/model.c:2724-2747, by one warp, everything in registers:
+ * lane l holds ids l, l+32, ... (NK of them): score = 1/(1+expf(-logit)),
+ * v = score + bias (or + 0.0f when there is none). K rounds of argmax:
+ * within a lane the ids ascend and the comparison is a strict >, across
+ * lanes the larger value wins and equal values go to the lower id — so the
+ * lowest id wins a tie and a NaN never wins, exactly as the sequential scan
+ * from -1e30f does. w = score[best]; renorm by (sum + 1e-20f) accumulated in
+ * j order; times routed_scale. */
+template <int NK>
+__device__ void route_warp(const wc_moe_args &a, int t, int lane)
 {
     const int E = a.E, K = a.K;
     const float *lg = a.ws.logits + (size_t)t * E;
-    float lv[kMaxPerLane], bv0[kMaxPerLane];
+    float sc[NK], v[NK];
 #pragma unroll
-    for (int k = 0; k < kMaxPerLane; k++) {
+    for (int k = 0; k < NK; k++) {
         const int e = lane + 32 * k;
-        lv[k] = e < E ? __ldcg(lg + e) : 0.0f;
-        bv0[k] = (e < E && a.bias) ? __ldg(a.bias + e) : 0.0f;
+        sc[k] = e < E ? __ldcg(lg + e) : 0.0f;
+        v[k] = (e < E && a.bias) ? __ldg(a.bias + e) : 0.0f;
     }
     uint32_t live = 0;
 #pragma unroll
-    for (int k = 0; k < kMaxPerLane; k++) {
+    for (int k = 0; k < NK; k++) {
         const int e = lane + 32 * k;
-        if (e < E) {
-            const float s = 1.0f / (1.0f + expf(-lv[k]));
-            sc[e] = s;
-            v[e] = s + bv0[k];
-            live |= 1u << k;
-        }
+        sc[k] = 1.0f / (1.0f + expf(-sc[k]));
+        v[k] = sc[k] + v[k];
+        if (e < E) live |= 1u << k;
     }
-    __syncwarp();
     float wsel = 0.0f, wsum = 0.0f;
     int mine = -1;                      /* lane j keeps the j-th choice */
     for (int j = 0; j < K; j++) {
         float bv = -1e30f, bsc = 0.0f;
-        int best = -1;
-        for (int k = 0; lane + 32 * k < E; k++) {
-            const int e = lane + 32 * k;
-            if (((live >> k) & 1) && v[e] > bv) { bv = v[e]; bsc = sc[e]; best = e; }
-        }
+        int bk = -1;
+#pragma unroll
+        for (int k = 0; k < NK; k++)
+            if (((live >> k) & 1) && v[k] > bv) { bv = v[k]; bsc = sc[k]; bk = k; }
+        int best = bk >= 0 ? lane + 32 * bk : -1;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -485,9 +578,11 @@ __device__ void route_warp(const wc_moe_args &a, int t, int lane, float *sc, flo
     }
 }
 
+template <int NK>
 __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, RouterGeom rg)
 {
-    extern __shared__ float xs[];
+    /* shared memory: barrier | x [lat] | staged weight rows | staged scales */
+    extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ float part[kRouterBlock / 32];
     __shared__ unsigned int ticket;
     pdl_trigger();                   /* let gate/up start its table build */
@@ -496,95 +591,92 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int b = blockIdx.x;
     const bool is_router = b < rg.rblocks;
-    /* weight loads first */
-    float4 wr[kRouterU4];
-    uint4 wq[kShU];
-    uint16_t wsq[kShU];
-    int r = 0, q0 = 0, q1 = 0, kind = 0, o = -1;
-    const int ng = (lat + 127) / 128, nchunk = (lat + 15) / 16;
+    const int ng = (lat + 127) / 128;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smraw);
+    float *xs = reinterpret_cast<float *>(smraw + 16);
+    uint8_t *wst = reinterpret_cast<uint8_t *>(xs + lat);
+    const int rows_pb = (kRouterBlock / 32) / kRouterSplit;
+    /* this block's rows: router rows [r0, r0+nr) or shared rows of one kind */
+    int r0 = 0, nr = 0, kind = 0, o0 = 0;
+    const uint8_t *wsrc = nullptr;
+    uint32_t wbytes = 0;
     if (is_router) {
-        r = b * 2 + warp / kRouterSplit;
-        const int qtr = warp % kRouterSplit, per = (n4 + kRouterSplit - 1) / kRouterSplit;
-        q0 = qtr * per;
-        q1 = min(n4, q0 + per);
-        const float4 *w4 = reinterpret_cast<const float4 *>(a.router + (size_t)r * lat) + q0;
-#pragma unroll
-        for (int u = 0; u < kRouterU4; u++) {
-            const int i = u * 32 + lane;
-            wr[u] = (r < a.E && i < q1 - q0) ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        r0 = b * rows_pb;
+        nr = max(0, min(rows_pb, a.E - r0));
+        wsrc = reinterpret_cast<const uint8_t *>(a.router + (size_t)r0 * lat);
+        wbytes = (uint32_t)nr * lat * 4;
     } else {
-        const int rr = (b - rg.rblocks) * (kRouterBlock / 32) + warp;
-        if (rr < 2 * a.si) {
-            kind = rr / a.si;
-            o = rr % a.si;
-            const int8_t *row = (kind ? a.shu : a.shg) + (size_t)o * ng * 128;
-            const uint16_t *ws = (kind ? a.shu_s : a.shg_s) + (size_t)o * ng;
-#pragma unroll
-            for (int u = 0; u < kShU; u++) {
-                const int c = u * 32 + lane;
-                wq[u] = c < nchunk ? ldg16(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-                wsq[u] = c < nchunk ? __ldg(ws + (c >> 3)) : (uint16_t)0;
-            }
-        }
+        const int rr0 = (b - rg.sblocks_base) * (kRouterBlock / 32);
+        kind = rr0 / a.si;
+        o0 = rr0 % a.si;
+        nr = max(0, min(kRouterBlock / 32, a.si - o0));
+        wsrc = reinterpret_cast<const uint8_t *>(kind ? a.shu : a.shg) + (size_t)o0 * ng * 128;
+        wbytes = (uint32_t)nr * ng * 128;
     }
-    /* then x */
-    {
-        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t * lat);
-        float4 xv[kXU];
-#pragma unroll
-        for (int u = 0; u < kXU; u++) {
-            const int i = threadIdx.x + u * kRouterBlock;
-            xv[u] = i < n4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < kXU; u++) {
-            const int i = threadIdx.x + u * kRouterBlock;
-            if (i < n4) reinterpret_cast<float4 *>(xs)[i] = xv[u];
-        }
+    uint16_t *sst = reinterpret_cast<uint16_t *>(wst + (size_t)(kRouterBlock / 32) * ng * 128);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+        uint32_t tx = (uint32_t)lat * 4 + wbytes;
+        const uint32_t sbytes = is_router ? 0u : (uint32_t)nr * ng * 2;
+        tx += sbytes;
+        mbar_expect_tx(bar, tx);
+        bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
+        if (wbytes) bulk_g2s(wst, wsrc, wbytes, bar);
+        if (sbytes)
+            bulk_g2s(sst, (kind ? a.shu_s : a.shg_s) + (size_t)o0 * ng, sbytes, bar);
     }
     __syncthreads();
+    const bool ok = mbar_wait(bar, 0);
+    if (!ok && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
     if (is_router) {
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs) + q0;
+        const int lr = warp / kRouterSplit, qtr = warp % kRouterSplit;
+        const int per = (n4 + kRouterSplit - 1) / kRouterSplit;
+        const int q0 = qtr * per, q1 = min(n4, q0 + per);
+        const float4 *w4 = reinterpret_cast<const float4 *>(wst) + (size_t)lr * n4;
+        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
         float acc = 0.0f;
-#pragma unroll
-        for (int u = 0; u < kRouterU4; u++) {
-            const int i = u * 32 + lane;
-            if (i < q1 - q0) {
-                const float4 xv = x4[i];
-                acc = fmaf(wr[u].x, xv.x, acc); acc = fmaf(wr[u].y, xv.y, acc);
-                acc = fmaf(wr[u].z, xv.z, acc); acc = fmaf(wr[u].w, xv.w, acc);
+        if (ok && lr < nr)
+            for (int i = q0 + lane; i < q1; i += 32) {
+                const float4 w = w4[i], xv = x4[i];
+                acc = fmaf(w.x, xv.x, acc); acc = fmaf(w.y, xv.y, acc);
+                acc = fmaf(w.z, xv.z, acc); acc = fmaf(w.w, xv.w, acc);
             }
-        }
         acc = warp_sum(acc);
         if (lane == 0) part[warp] = acc;
         __syncthreads();
-        if (threadIdx.x < 2) {
-            const int rr = b * 2 + threadIdx.x;
-            if (rr < a.E) {
-                const float *p = part + threadIdx.x * kRouterSplit;
-                a.ws.logits[(size_t)t * a.E + rr] = ((p[0] + p[1]) + p[2]) + p[3];
+        if ((int)threadIdx.x < nr) {
+            const float *p = part + threadIdx.x * kRouterSplit;
+            a.ws.logits[(size_t)t * a.E + r0 + threadIdx.x] = ((p[0] + p[1]) + p[2]) + p[3];
+        }
+    } else if (ok && warp < nr) {
+        const uint8_t *row = wst + (size_t)warp * ng * 128;
+        const uint16_t *srow = sst + (size_t)warp * ng;
+        float acc = 0.0f;
+        for (int gi = 0; gi < ng; gi++) {
+            const int i = gi * 128 + lane * 4;
+            if (i < lat) {
+                const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+                const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
+                float part = (float)(int8_t)(w & 0xff) * xv.x;
+                part = fmaf((float)(int8_t)((w >> 8) & 0xff), xv.y, part);
+                part = fmaf((float)(int8_t)((w >> 16) & 0xff), xv.z, part);
+                part = fmaf((float)(int8_t)(w >> 24), xv.w, part);
+                acc = fmaf(f16_keep(srow[gi]), part, acc);
             }
         }
-    } else if (o >= 0) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int u = 0; u < kShU; u++) {
-            const int c = u * 32 + lane;
-            if (c < nchunk) acc += q8g_chunk(wq[u], f16_keep(wsq[u]), xs, c * 16, lat);
-        }
         acc = warp_sum(acc);
-        if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o] = acc;
+        if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)t * a.si + o0 + warp] = acc;
     }
-    /* the last block of this token routes it */
-    __threadfence();
+    /* the last block of this token routes it: the block's writes are
+     * ordered before thread 0's release; its acquire orders the other
+     * blocks' writes before the routing reads (all through L2) */
     __syncthreads();
-    if (threadIdx.x == 0) ticket = atomicAdd(a.ws.tickets + t, 1u);
+    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(a.ws.tickets + t, 1u);
     __syncthreads();
     if (ticket != gridDim.x - 1) return;
-    __threadfence();
     if (warp == 0) {
-        route_warp(a, t, lane, xs, xs + a.E);      /* x is dead by now */
+        route_warp<NK>(a, t, lane);
     } else {
         float g[kSiluU], u[kSiluU];
         const int nt = blockDim.x - 32;
@@ -600,7 +692,11 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
             if (i < a.si) a.ws.sh_h[(size_t)t * a.si + i] = silu_ref(g[k]) * u[k];
         }
     }
-    if (threadIdx.x == 0) a.ws.tickets[t] = 0;       /* ready for the next launch */
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        a.ws.tickets[t] = 0;                           /* ready for the next launch */
+        st_release(a.ws.route_flag + t, 1u);           /* gate/up may go */
+    }
 }
 
 /* The record of routed expert j of token t (ids are global; a bank may hold
@@ -613,140 +709,219 @@ __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const in
 
 /* ---- 2. gate/up ------------------------------------------------------------
  * tile = (token, kind, slice, expert group): one table slice shared by the
- * rows of every expert in the group; every thread holds all its positions
- * (kGuNP) in registers. Before the wait: x, the codebook rows and the table,
- * plus this block's share of the shared expert's down rows (weights only).
- * After: the routed rows, then the shared down rows with SiLU(g)*u. */
-constexpr int kGuNP = 4;               /* positions per gate/up thread      */
+ * rows of every expert in the group. Before routing is known: x, the
+ * codebook rows and the table. Then the wait — on the router's published
+ * flag when the router runs in the same chain (no kernel-completion
+ * latency), else the programmatic dependency — and the routed experts' index
+ * streams come in by TMA in two halves; the gather starts on the first half
+ * while the second lands. */
 constexpr int kGuBooks = 2;            /* codebook rows per thread (768/512) */
-constexpr int kShdU = 4;               /* shared down: 16-byte chunks per lane, si <= 2048 */
 
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
-gateup_kernel(wc_moe_args a, TileGeom g, int sh_rows_pb, const int *idx)
+gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
 {
-    extern __shared__ float smem[];
-    float *xs = smem, *lut = smem + g.Vs * kVecDim;
+    extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ int go;
+    TileSmem sm(smraw, g);
     int b = blockIdx.x;
     const int grp = b % g.groups; b /= g.groups;
     const int slice = b % g.ns; b /= g.ns;
     const int kind = b % 2; const int t = b / 2;
     const wc_bank &bk = a.bank;
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
-    /* routing-independent loads: x slice, codebook rows, shared down rows */
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.bars[0], 1);
+        mbar_init(&sm.bars[1], 1);
+        mbar_fence_init();
+    }
+    /* routing-independent: x slice, codebook rows, the table */
     BookRows<ST, kGuBooks> books;
     books.load(a.books, bk.cb_base + kind * ST);
-    float xv = 0.0f;
     if ((int)threadIdx.x < nvs * kVecDim)
-        xv = __ldg(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
-    const int warps = blockDim.x / 32, lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-    const int lin = (kind * g.ns + slice) * g.groups + grp;
-    const bool do_shared = a.si > 0 && t == 0 && sh_rows_pb > 0;
-    const int ngs = (a.si + 127) / 128, nchs = (a.si + 15) / 16;
-    /* the warp's first shared down row is prefetched; further rows (small
-     * shapes, more rows than warps) load when they are reached */
-    const int o0 = lin * sh_rows_pb + warp;
-    uint4 shq[kShdU];
-    uint16_t shs[kShdU];
-    if (do_shared && warp < sh_rows_pb && o0 < bk.lat) {
-#pragma unroll
-        for (int u = 0; u < kShdU; u++) {
-            const int c = u * 32 + lane;
-            shq[u] = c < nchs ? ldg16(a.shd + (size_t)o0 * ngs * 128 + (size_t)c * 16)
-                              : make_uint4(0, 0, 0, 0);
-            shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o0 * ngs + (c >> 3)) : (uint16_t)0;
-        }
-    }
-    if ((int)threadIdx.x < nvs * kVecDim) xs[threadIdx.x] = xv;
+        sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
     __syncthreads();
-    books.build(lut, xs, nvs);
-    pdl_wait();                      /* routing (and all earlier work) is done */
+    books.build(sm.lut, sm.xs, nvs);
+    if (a.router) {
+        if (threadIdx.x == 0) {
+            go = wait_flag(a.ws.route_flag + t, a.ws.err);
+            /* the last tile of this token to pass clears the flag */
+            const int per_t = 2 * g.ns * g.groups;
+            if (atomicAdd(a.ws.route_pass + t, 1u) == (unsigned)per_t - 1) {
+                a.ws.route_pass[t] = 0;
+                a.ws.route_flag[t] = 0;
+            }
+        }
+        __syncthreads();
+        if (!go) return;
+    } else {
+        pdl_wait();
+    }
     pdl_trigger();
     const int j0 = grp * g.EG;
     const int nm = min(g.EG, a.K - j0);
-    const int m = min(TileThread<ST, GatherAll<ST, kGuNP>>::matrix_of_thread(g), nm - 1);
-    const uint8_t *mat = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off);
-    TileThread<ST, GatherAll<ST, kGuNP>> th(g, slice, nm, mat);
+    /* stage the group's index streams for this slice: (matrix, row block)
+     * runs of nvs positions, in halves [0,h) and [h,nvs) */
+    const uint32_t psz = kBlock * ST;
+    const int h = (nvs + 1) / 2;
+    const int ncopy = nm * g.nrb;
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(&sm.bars[0], (uint32_t)ncopy * h * psz);
+        if (nvs > h) mbar_expect_tx(&sm.bars[1], (uint32_t)ncopy * (nvs - h) * psz);
+    }
     __syncthreads();
-    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
-    th.finish(g, lut, out, bk.inter, nm);
-    if (!do_shared) return;
-    /* shared expert down rows of every token (token 0's tiles do them) */
-    for (int tt = 0; tt < a.T; tt++) {
-        __syncthreads();
-        float *hs = smem;
-        for (int i = threadIdx.x; i < a.si; i += blockDim.x)
-            hs[i] = __ldcg(a.ws.sh_h + (size_t)tt * a.si + i);
-        __syncthreads();
-        for (int rr = warp; rr < sh_rows_pb; rr += warps) {
-            const int o = lin * sh_rows_pb + rr;
-            if (o >= bk.lat) break;
-            if (rr != warp) {
-#pragma unroll
-                for (int u = 0; u < kShdU; u++) {
-                    const int c = u * 32 + lane;
-                    shq[u] = c < nchs ? ldg16(a.shd + (size_t)o * ngs * 128 + (size_t)c * 16)
-                                      : make_uint4(0, 0, 0, 0);
-                    shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o * ngs + (c >> 3)) : (uint16_t)0;
-                }
-            }
-            float acc = 0.0f;
-#pragma unroll
-            for (int u = 0; u < kShdU; u++) {
-                const int c = u * 32 + lane;
-                if (c < nchs) acc += q8g_chunk(shq[u], f16_keep(shs[u]), hs, c * 16, a.si);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) a.ws.sh_out[(size_t)tt * bk.lat + o] = acc;
-        }
-        if (a.T > 1 && sh_rows_pb > warps) {
-            /* reload the first rows for the next token */
-            const int o = lin * sh_rows_pb + warp;
-            if (warp < sh_rows_pb && o < bk.lat) {
-#pragma unroll
-                for (int u = 0; u < kShdU; u++) {
-                    const int c = u * 32 + lane;
-                    shq[u] = c < nchs ? ldg16(a.shd + (size_t)o * ngs * 128 + (size_t)c * 16)
-                                      : make_uint4(0, 0, 0, 0);
-                    shs[u] = c < nchs ? __ldg(a.shd_s + (size_t)o * ngs + (c >> 3)) : (uint16_t)0;
-                }
-            }
+    for (int c = threadIdx.x; c < ncopy; c += blockDim.x) {
+        const int m = c / g.nrb, rbl = c % g.nrb;
+        const uint8_t *src = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off) +
+                             ((size_t)rbl * g.nv + v0) * psz;
+        uint8_t *dst = sm.stage + (size_t)(m * g.nrb + rbl) * nvs * psz;
+        bulk_g2s(dst, src, h * psz, &sm.bars[0]);
+        if (nvs > h) bulk_g2s(dst + (size_t)h * psz, src + (size_t)h * psz, (nvs - h) * psz, &sm.bars[1]);
+    }
+    if (threadIdx.x == 0 && t == 0 && a.prefetch_down) {
+        /* this block's share of the routed experts' down index streams:
+         * L2 fetches them while the gathers below keep HBM idle */
+        const size_t per = bk.scale_off - bk.down_off;
+        const size_t total = per * (size_t)a.K * a.T;
+        const int nb = gridDim.x;
+        const size_t share = ((total + nb - 1) / nb + 15) & ~(size_t)15;
+        size_t lo = (size_t)blockIdx.x * share, hi = min(total, lo + share);
+        while (lo < hi) {
+            const size_t jt = lo / per, off = lo % per;
+            const size_t n = min(hi - lo, per - off) & ~(size_t)15;
+            if (n == 0) break;
+            const int e = __ldcg(idx + jt) - bk.first;
+            if (e >= 0 && e < bk.n_experts)
+                l2_prefetch(bk.base + (size_t)e * bk.rec_bytes + bk.down_off + off, n);
+            lo += per - off;
         }
     }
+    TileGeom gs = g;                 /* the staged view: positions [0, nvs) */
+    gs.nv = nvs;
+    gs.Vs = nvs;
+    const int m = min(TileThread<ST, GatherSmem<ST>>::matrix_of_thread(g), nm - 1);
+    TileThread<ST, GatherSmem<ST>> th(gs, 0, nm, sm.stage + (size_t)m * g.nrb * nvs * psz);
+    th.G.first = th.vl0;
+    th.G.bar0 = &sm.bars[0];
+    th.G.bar1 = nvs > h ? &sm.bars[1] : nullptr;
+    th.G.split = h;
+    __syncthreads();                 /* the table */
+    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
+    th.finish(gs, sm.lut, out, bk.inter, nm);
+    if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
 }
 
 /* ---- 3. down ---------------------------------------------------------------
  * tile = (token, expert j, slice). Before the wait (the route is known:
- * gate/up started after it): the expert's down index loads, its gate/up row
- * scales for the slice's inputs, the codebook rows. After: the gate/up
- * slice sums (every load issued at once), SiLU(g)*u, the table, the gather. */
-constexpr int kDnNP = 3;               /* positions per down thread         */
+ * gate/up passed it before letting this kernel start): TMA stages the
+ * expert's down index stream for the slice, and the gate/up row scales for
+ * the slice's inputs and the codebook rows are loaded. After: the gate/up
+ * slice sums (every load issued at once), SiLU(g)*u, the table, the gather
+ * from shared memory. Blocks past d_tiles compute the shared expert's down
+ * rows ([lat][si] Q8G, sh_rows_pw rows per warp, weights staged by TMA
+ * before the wait). */
 constexpr int kDnBooks = 2;            /* codebook rows per thread (768/432) */
 constexpr int kDnSlices = 12;          /* gate/up slices summed per thread  */
+constexpr int kShRowsMax = 12;         /* shared down rows per warp (shared memory) */
+
+__device__ __forceinline__ void shared_down_block(const wc_moe_args &a, unsigned char *raw,
+                                                  int sb, int rows_pw)
+{
+    const wc_bank &bk = a.bank;
+    const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int ngs = (a.si + 127) / 128;
+    const size_t rowb = (size_t)ngs * 128;
+    const int row0 = sb * warps * rows_pw;
+    const int nrows = max(0, min(warps * rows_pw, bk.lat - row0));
+    uint64_t *bar = reinterpret_cast<uint64_t *>(raw);
+    float *hs = reinterpret_cast<float *>(raw + 16);
+    float *scs = hs + ((a.si + 3) & ~3);                   /* [nrows][ngs] scales */
+    uint8_t *wst = reinterpret_cast<uint8_t *>(scs + ((warps * rows_pw * ngs + 3) & ~3));
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+        if (nrows > 0) {
+            mbar_expect_tx(bar, (uint32_t)(nrows * rowb));
+            bulk_g2s(wst, a.shd + (size_t)row0 * rowb, (uint32_t)(nrows * rowb), bar);
+        }
+    }
+    /* the rows' group scales, every load issued before any store */
+    {
+        constexpr int U = 4;
+        const int n = nrows * ngs;
+        uint16_t v[U];
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const int i = threadIdx.x + k * blockDim.x;
+            v[k] = i < n ? ld_pin_u16(a.shd_s + (size_t)row0 * ngs + i) : (uint16_t)0;
+        }
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const int i = threadIdx.x + k * blockDim.x;
+            if (i < n) scs[i] = f16_keep(v[k]);
+        }
+        for (int i = threadIdx.x + U * blockDim.x; i < n; i += blockDim.x)
+            scs[i] = f16_keep(ld_pin_u16(a.shd_s + (size_t)row0 * ngs + i));
+    }
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();
+    const bool ok = nrows == 0 || mbar_wait(bar, 0);
+    if (!ok) {
+        if (threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+        return;
+    }
+    for (int tt = 0; tt < a.T; tt++) {
+        __syncthreads();
+        stage_floats(hs, a.ws.sh_h + (size_t)tt * a.si, a.si);
+        __syncthreads();
+        for (int r = 0; r < rows_pw; r++) {
+            const int lr = warp * rows_pw + r, o = row0 + lr;
+            if (o >= bk.lat) break;
+            const float acc = dot_q8g_smem(wst + (size_t)lr * rowb, scs + (size_t)lr * ngs, hs,
+                                           a.si, lane);
+            if (lane == 0) a.ws.sh_out[(size_t)tt * bk.lat + o] = acc;
+        }
+    }
+}
 
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
-down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
+down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, int sh_rows_pw, const int *idx)
 {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) unsigned char smraw[];
     const wc_bank &bk = a.bank;
-    float *xs = smem, *lut = smem + g.Vs * kVecDim;
+    if ((int)blockIdx.x >= d_tiles) {
+        shared_down_block(a, smraw, blockIdx.x - d_tiles, sh_rows_pw);
+        return;
+    }
+    TileSmem sm(smraw, g);
+    float *xs = sm.xs, *lut = sm.lut;
     int b = blockIdx.x;
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
+    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
+    const uint32_t psz = kBlock * ST;
     const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
-    TileThread<ST, GatherAll<ST, kDnNP>> th(g, slice, 1, rec + bk.down_off);
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.bars[0], 1);
+        mbar_fence_init();
+        mbar_expect_tx(&sm.bars[0], (uint32_t)g.nrb * nvs * psz);
+    }
+    __syncthreads();
+    for (int rbl = threadIdx.x; rbl < g.nrb; rbl += blockDim.x)
+        bulk_g2s(sm.stage + (size_t)rbl * nvs * psz,
+                 rec + bk.down_off + ((size_t)rbl * g.nv + v0) * psz, nvs * psz, &sm.bars[0]);
     BookRows<ST, kDnBooks> books;
     books.load(a.books, bk.cb_base + 2 * ST);
-    const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
     const int nin = nvs * kVecDim;
     const int inter = bk.inter;
     const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
     float sg_scale = 0.0f, su_scale = 0.0f;
     if ((int)threadIdx.x < nin) {
         const int n = v0 * kVecDim + threadIdx.x;
-        sg_scale = f16_keep(__ldg(sc + n));
-        su_scale = f16_keep(__ldg(sc + inter + n));
+        sg_scale = f16_keep(ld_pin_u16(sc + n));
+        su_scale = f16_keep(ld_pin_u16(sc + inter + n));
     }
     pdl_trigger();
     pdl_wait();                      /* gate/up partials are complete */
@@ -790,8 +965,17 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, const int *idx)
     __syncthreads();
     books.build(lut, xs, nvs);
     __syncthreads();
+    TileGeom gs = g;                 /* the staged view: positions [0, nvs) */
+    gs.nv = nvs;
+    gs.Vs = nvs;
+    TileThread<ST, GatherSmem<ST>> th(gs, 0, 1, sm.stage);
+    th.G.first = th.vl0;
+    th.G.bar0 = &sm.bars[0];
+    th.G.bar1 = nullptr;
+    th.G.split = nvs;
     float *out = a.ws.p_d + (((size_t)t * a.K + j) * g.ns + slice) * bk.lat;
-    th.finish(g, lut, out, 0, 1);
+    th.finish(gs, lut, out, 0, 1);
+    if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
 }
 
 /* ---- 4. combine --------------------------------------------------------------
@@ -824,7 +1008,19 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(
                 bk.base + (size_t)(__ldcg(it + j) - bk.first) * bk.rec_bytes + bk.scale_off) +
                 2 * bk.inter;
-            scl[n] = f16_keep(__ldg(sc + i));
+            scl[n] = f16_keep(ld_pin_u16(sc + i));
+        }
+    }
+    if (threadIdx.x == 0 && t == 0) {
+        /* ranges the caller wants in L2 for what follows (the next layer's
+         * router and shared expert), split over the blocks */
+        for (int r = 0; r < 4; r++) {
+            const size_t n = a.pf_bytes[r];
+            if (!a.pf_ptr[r] || n == 0) continue;
+            const size_t share = ((n + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+            const size_t lo = (size_t)blockIdx.x * share;
+            if (lo < n) l2_prefetch(static_cast<const char *>(a.pf_ptr[r]) + lo,
+                                    (min(n, lo + share) - lo) & ~(size_t)15);
         }
     }
     pdl_wait();
@@ -883,19 +1079,38 @@ constexpr int kVsDown = 8;
 
 struct MoeGeom {
     TileGeom gu, d;
-    int gu_tiles, d_tiles, sh_rows_pb;
+    int gu_tiles, d_tiles, sh_blocks, sh_rows_pw;
 };
+
+constexpr int kSMs = 148;              /* B200 */
+
+/* dynamic shared memory of a shared-down block: barrier | h | scales | rows */
+size_t shared_down_smem(int threads, int rows_pw, int si)
+{
+    const size_t rows = (size_t)(threads / 32) * rows_pw, ngs = ((size_t)si + 127) / 128;
+    return 16 + (((size_t)si + 3) & ~(size_t)3) * 4 + ((rows * ngs + 3) & ~(size_t)3) * 4 +
+           rows * ngs * 128;
+}
 
 MoeGeom moe_geom(const wc_moe_args *a)
 {
     MoeGeom m;
     const wc_bank &b = a->bank;
-    m.gu = make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512);
-    m.d = make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448);
+    m.gu = with_stage(make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512), b.stages);
+    m.d = with_stage(make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448), b.stages);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
     m.d_tiles = a->T * a->K * m.d.ns;
-    const int per_t = 2 * m.gu.ns * m.gu.groups;      /* token-0 tiles run the shared rows */
-    m.sh_rows_pb = a->si > 0 ? (b.lat + per_t - 1) / per_t : 0;
+    /* the shared expert's down rows take the SMs the down tiles leave free
+     * (one down block per SM), or a few more when there are none */
+    const int warps = m.d.threads / 32;
+    int free_sms = kSMs - m.d_tiles % kSMs;
+    if (free_sms < 8) free_sms = 8;
+    m.sh_rows_pw = (b.lat + free_sms * warps - 1) / (free_sms * warps);
+    if (m.sh_rows_pw > kShRowsMax) m.sh_rows_pw = kShRowsMax;
+    while (m.sh_rows_pw > 1 && shared_down_smem(m.d.threads, m.sh_rows_pw, a->si) > 227 * 1024)
+        m.sh_rows_pw--;
+    const int rows_pb = warps * m.sh_rows_pw;
+    m.sh_blocks = a->si > 0 ? (b.lat + rows_pb - 1) / rows_pb : 0;
     return m;
 }
 
@@ -904,17 +1119,15 @@ MoeGeom moe_geom(const wc_moe_args *a)
 bool moe_geom_ok(const MoeGeom &m, const wc_moe_args *a)
 {
     if (!a->router) {   /* router/shared limits only apply to the whole layer */
-        const int gu_pos = (m.gu.Vs + m.gu.nlanes - 1) / m.gu.nlanes;
-        const int d_pos = (m.d.Vs + m.d.nlanes - 1) / m.d.nlanes;
-        return gu_pos <= kGuNP && d_pos <= kDnNP && m.d.ns <= kMaxSlicesReg * 8 &&
-               a->K <= kMaxTopK;
+        return a->K <= kMaxTopK && m.gu.smem <= 227 * 1024 && m.d.smem <= 227 * 1024;
     }
-    const int gu_pos = (m.gu.Vs + m.gu.nlanes - 1) / m.gu.nlanes;
-    const int d_pos = (m.d.Vs + m.d.nlanes - 1) / m.d.nlanes;
-    if (gu_pos > kGuNP || d_pos > kDnNP) return false;
+
     if (a->bank.lat > 4 * 32 * kRouterU4 * kRouterSplit || a->bank.lat > 16 * 32 * kShU) return false;
     if (a->bank.lat > 4 * kRouterBlock * kXU) return false;
-    if (a->si > 16 * 32 * kShdU || a->si > (kRouterBlock - 32) * kSiluU) return false;
+    if (a->si > (kRouterBlock - 32) * kSiluU) return false;
+    if (a->si > 0 && shared_down_smem(m.d.threads, m.sh_rows_pw, a->si) > 227 * 1024) return false;
+    if (a->si % (kRouterBlock / 32) || a->bank.lat % 4 || a->si % 4) return false;
+    if (m.gu.smem > 227 * 1024 || m.d.smem > 227 * 1024) return false;
     if (m.d.ns > kMaxSlicesReg * 8 || a->K > kMaxTopK) return false;
     return true;
 }
@@ -949,9 +1162,21 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         if (a->E > 32 * kMaxPerLane) return (int)cudaErrorInvalidValue;
         const RouterGeom rg = router_geom(a->E, a->si);
         const int pe = prof_begin(WC_PH_ROUTER, s);
-        const size_t rsm = (size_t)max(a->bank.lat, 2 * a->E) * sizeof(float);
-        e = launch(router_kernel, dim3(rg.rblocks + rg.sblocks, a->T), dim3(kRouterBlock),
-                   rsm, s, false, *a, rg);
+        const int ngr = (a->bank.lat + 127) / 128;
+        size_t wmax = (size_t)((kRouterBlock / 32) / kRouterSplit) * a->bank.lat * 4;
+        const size_t wsh = (size_t)(kRouterBlock / 32) * ngr * 128;
+        if (wsh > wmax) wmax = wsh;
+        const size_t rsm = 16 + (size_t)a->bank.lat * 4 + wmax + (size_t)(kRouterBlock / 32) * ngr * 2 + 16;
+        cudaFuncSetAttribute(router_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+        cudaFuncSetAttribute(router_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+        cudaFuncSetAttribute(router_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+        const dim3 rgrid(rg.rblocks + rg.sblocks, a->T);
+        if (a->E <= 256)
+            e = launch(router_kernel<8>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
+        else if (a->E <= 512)
+            e = launch(router_kernel<16>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
+        else
+            e = launch(router_kernel<32>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
         prof_end(pe, s);
         g_launches += 1;
         idx = a->idx_out;
@@ -960,21 +1185,22 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         if (e != cudaSuccess) return (int)e;
     }
     const int prof = P.on;             /* events between kernels defeat PDL */
-    size_t gsmem = m.gu.smem;
-    const size_t shsmem = (size_t)a->si * sizeof(float);
-    if (a->router && shsmem > gsmem) gsmem = shsmem;
     cudaFuncSetAttribute(gateup_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)gsmem);
+                         (int)m.gu.smem);
     int pe = prof_begin(WC_PH_GATEUP, s);
-    e = launch(gateup_kernel<ST>, dim3(m.gu_tiles), dim3(m.gu.threads), gsmem, s, pdl && !prof,
-               *a, m.gu, a->router ? m.sh_rows_pb : 0, idx);
+    e = launch(gateup_kernel<ST>, dim3(m.gu_tiles), dim3(m.gu.threads), m.gu.smem, s,
+               pdl && !prof, *a, m.gu, idx);
     prof_end(pe, s);
     if (e != cudaSuccess) return (int)e;
-    cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)m.d.smem);
+    size_t dsm = m.d.smem;
+    if (a->router && a->si > 0) {
+        const size_t shm = shared_down_smem(m.d.threads, m.sh_rows_pw, a->si);
+        if (shm > dsm) dsm = shm;
+    }
+    cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm);
     pe = prof_begin(WC_PH_DOWN, s);
-    e = launch(down_kernel<ST>, dim3(m.d_tiles), dim3(m.d.threads), m.d.smem, s, !prof,
-               *a, m.gu, m.d, idx);
+    e = launch(down_kernel<ST>, dim3(m.d_tiles + (a->router ? m.sh_blocks : 0)),
+               dim3(m.d.threads), dsm, s, !prof, *a, m.gu, m.d, m.d_tiles, m.sh_rows_pw, idx);
     prof_end(pe, s);
     if (e != cudaSuccess) return (int)e;
     wc_moe_args ca = *a;
@@ -1000,8 +1226,7 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
     n += (size_t)T * K * d.ns * lat;
     n += (size_t)T * E;
     n += (size_t)T * si * 3 + (size_t)T * lat;
-    n += (size_t)T;                          /* tickets */
-    return n + 64;
+    return n + 256 + 64;                     /* + control words */
 }
 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
@@ -1010,7 +1235,13 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     float *p = base;
-    ws->tickets = reinterpret_cast<unsigned int *>(p); p += 64;   /* first: stays put */
+    /* control words first (zeroed once at allocation, self-resetting):
+     * tickets [0,64), route flags [64,128), pass counters [128,192), err */
+    ws->tickets = reinterpret_cast<unsigned int *>(p);
+    ws->route_flag = ws->tickets + 64;
+    ws->route_pass = ws->tickets + 128;
+    ws->err = ws->tickets + 192;
+    p += 256;
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
     ws->p_d = p; p += (size_t)T * K * d.ns * lat;
     ws->logits = p; p += (size_t)T * E;

@@ -80,6 +80,8 @@ static struct {
     /* single-kernel parity APIs */
     void *d_tmp;
     size_t tmp_bytes;
+    /* fetch layer+1's router and shared expert into L2 during layer */
+    int prefetch_next;
 } S;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
@@ -112,6 +114,25 @@ const char *waste_cuda_last_error(void)
 }
 
 uint64_t waste_cuda_launch_count(void) { return wc_launches(); }
+
+/* The workspace's control words (wc_moe_ws_carve): err sits 192 words in. */
+static unsigned read_device_errors(int clear)
+{
+    if (!S.d_ws) return 0;
+    unsigned int *err = (unsigned int *)S.d_ws + 192, v = 0;
+    if (cudaStreamSynchronize(S.stream) != cudaSuccess) return ~0u;
+    if (cudaMemcpy(&v, err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return ~0u;
+    if (v && clear) cudaMemset(err, 0, sizeof v);
+    return v;
+}
+
+unsigned waste_cuda_device_errors(void)
+{
+    pthread_mutex_lock(&g_mu);
+    const unsigned v = S.inited ? read_device_errors(1) : 0;
+    pthread_mutex_unlock(&g_mu);
+    return v;
+}
 
 int waste_cuda_profile(int on)
 {
@@ -199,6 +220,10 @@ static int init_locked(int device)
     CK(cudaMallocHost((void **)&S.h_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "h_idx");
     CK(cudaMallocHost((void **)&S.h_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "h_w");
     snprintf(S.name, sizeof S.name, "CUDA sm_100a (%s)", p.name);
+    {
+        const char *pe = getenv("WASTE_CUDA_PREFETCH");
+        S.prefetch_next = !(pe && *pe == '0');
+    }
     S.device = dev;
     S.inited = 1;
 out:
@@ -560,6 +585,7 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
     a.w = S.d_w;
     a.out = S.d_out;
     a.order_by_id = order_by_id;
+    a.prefetch_down = 1;
     if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
     CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
     CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "ysum D2H");
@@ -606,6 +632,24 @@ static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
     a->routed_scale = L->routed_scale;
     a->shg = L->d_shg; a->shu = L->d_shu; a->shd = L->d_shd;
     a->shg_s = L->d_shg_s; a->shu_s = L->d_shu_s; a->shd_s = L->d_shd_s;
+    a->prefetch_down = 1;
+    if (S.prefetch_next && layer + 1 < WC_MAX_LAYERS && S.layer[layer + 1].trunk) {
+        /* the next layer's router and shared expert, fetched into L2 while
+         * this layer's gathers keep HBM idle */
+        const wc_layer *N = &S.layer[layer + 1];
+        const int g = 128;
+        const size_t ng_h = (size_t)(N->hidden + g - 1) / g, ng_s = (size_t)(N->si + g - 1) / g;
+        a->pf_ptr[0] = N->d_router;
+        a->pf_bytes[0] = (size_t)N->E * N->hidden * sizeof(float);
+        if (N->si > 0) {
+            a->pf_ptr[1] = N->d_shg;
+            a->pf_bytes[1] = (size_t)N->si * ng_h * g;
+            a->pf_ptr[2] = N->d_shu;
+            a->pf_bytes[2] = (size_t)N->si * ng_h * g;
+            a->pf_ptr[3] = N->d_shd;
+            a->pf_bytes[3] = (size_t)N->hidden * ng_s * g;
+        }
+    }
     if (wc_moe_supported(a))
         return fail(WASTE_CUDA_E_ARG, "layer %d: shape outside the kernels' bounds "
                     "(hidden <= 3072, shared inter <= 1792, experts <= 1024)", layer);
@@ -656,6 +700,10 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
                            cudaMemcpyDeviceToHost, S.stream), "w D2H");
     }
     CK(cudaStreamSynchronize(S.stream), "moe layer");
+    if (read_device_errors(1)) {
+        rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
+        goto out;
+    }
     memcpy(out, S.h_out, xb);
     if (routed) memcpy(routed, S.h_idx, (size_t)L->top_k * sizeof(int));
     if (weights) memcpy(weights, S.h_w, (size_t)L->top_k * sizeof(float));

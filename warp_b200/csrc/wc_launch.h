@@ -31,7 +31,14 @@ typedef struct {
     float *logits;     /* [T][E]                                            */
     float *sh_g, *sh_u, *sh_h, *sh_out;   /* shared expert [T][si] / [T][hid] */
     unsigned int *tickets;  /* [T] router blocks done; zero between launches   */
+    unsigned int *route_flag;  /* [T] 1 once routing is published            */
+    unsigned int *route_pass;  /* [T] gate/up tiles that have seen the flag   */
+    unsigned int *err;         /* sticky device error bits (WC_ERR_*)         */
 } wc_moe_ws;
+
+/* Device error bits: a bounded wait that ran out. */
+#define WC_ERR_ROUTE_WAIT 1u
+#define WC_ERR_TMA_WAIT   2u
 
 typedef struct {
     wc_bank bank;
@@ -52,6 +59,11 @@ typedef struct {
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
+    /* L2 prefetching: the routed experts' down streams during gate/up, and
+     * up to four caller ranges (16-byte aligned) during combine */
+    int prefetch_down;
+    const void *pf_ptr[4];
+    size_t pf_bytes[4];
 } wc_moe_args;
 
 /* Floats of workspace for T tokens. The region must be zeroed once when it
