@@ -197,6 +197,33 @@ int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
                              const float *const *x, float *const *y, int M,
                              int N, int cb_base, int stages, void *stream);
 
+/* vq_matvec_dev for callers that cannot allocate device memory once they
+ * run: a decode loop that reserved the device's memory for weights and
+ * state at load time (a late cudaMalloc can then fail), or one that cannot
+ * take the device-wide synchronisation of cudaFree while other streams
+ * work. vq_matvec_dev grows its partial-sum scratch with cudaFree and
+ * cudaMalloc; this entry point allocates nothing and keeps the partial
+ * sums in a fixed array of WASTE_CUDA_NOALLOC_SCRATCH_BYTES (16 MiB)
+ * compiled into the library. It has no counterpart in the reference.
+ *  - Limit: G * ceil(N/128) * M * 4 bytes must fit the array (G = 32
+ *    matrices of 4096 x 4096 fill it exactly); larger calls return
+ *    WASTE_CUDA_E_ARG with the sizes in waste_cuda_last_error().
+ *  - The calling thread's current device must be the library's device.
+ *    The first call on a device looks up the array's address on it; make
+ *    that first call before capturing a stream into a CUDA graph.
+ *  - Nothing in the array has to start at zero: each call writes every
+ *    partial sum it reads back.
+ *  - There is one array per device: calls whose kernels overlap on the GPU
+ *    (different streams, or different host threads without ordering
+ *    between their streams) race on it. Order them on one stream.
+ * Arguments, alignment rules and results are those of vq_matvec_dev. */
+#define WASTE_CUDA_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
+                                     const uint16_t *const *scale,
+                                     const float *const *x, float *const *y,
+                                     int M, int N, int cb_base, int stages,
+                                     void *stream);
+
 /* Kernels this library launched since load (a running count, for
  * benchmarks that report how many of their launches were this library's). */
 uint64_t waste_cuda_launch_count(void);

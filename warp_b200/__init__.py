@@ -28,7 +28,7 @@ EXPORTS = (
     "waste_cuda_moe_layer_dev", "waste_cuda_lutb", "waste_cuda_vq_matvec",
     "waste_cuda_vq_dequant", "waste_cuda_vq_matvec_dev",
     "waste_cuda_launch_count", "waste_cuda_profile", "waste_cuda_profile_read",
-    "waste_cuda_device_errors",
+    "waste_cuda_device_errors", "waste_cuda_vq_matvec_dev_noalloc",
 )
 
 PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -109,6 +109,8 @@ def load_library() -> C.CDLL:
         "waste_cuda_vq_dequant": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int]),
         "waste_cuda_vq_matvec_dev": (C.c_int, [C.c_int, P, P, P, P, C.c_int, C.c_int,
                                                C.c_int, C.c_int, P]),
+        "waste_cuda_vq_matvec_dev_noalloc": (C.c_int, [C.c_int, P, P, P, P, C.c_int,
+                                                       C.c_int, C.c_int, C.c_int, P]),
         "waste_cuda_launch_count": (C.c_uint64, []),
         "waste_cuda_profile": (C.c_int, [C.c_int]),
         "waste_cuda_profile_read": (C.c_int, [P, P, C.c_int]),
@@ -313,5 +315,23 @@ def vq_matvec_dev(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base:
     G = len(idx_ptrs)
     arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
     _check(load_library().waste_cuda_vq_matvec_dev(
+        G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base, stages,
+        C.c_void_p(stream or None)))
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def vq_matvec_dev_noalloc(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base: int,
+                          stages: int = 3, stream: int = 0):
+    """vq_matvec_dev without any device allocation: for callers that reserved
+    the device's memory up front, or cannot take cudaFree's device-wide
+    synchronisation mid-run. Partial sums use a fixed 16 MiB array built
+    into the library (G * ceil(N/128) * M * 4 bytes at most; larger calls
+    raise). Calls overlapping on the GPU race on that array; make the first
+    call on a device before any stream capture."""
+    G = len(idx_ptrs)
+    arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
+    _check(load_library().waste_cuda_vq_matvec_dev_noalloc(
         G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base, stages,
         C.c_void_p(stream or None)))

@@ -1269,6 +1269,16 @@ extern "C" int wc_moe_launch(const wc_moe_args *a, void *stream)
 
 static constexpr int kVsMatvec = 16;
 
+/* The allocation-free matvec's partial sums live here instead of in
+ * cudaMalloc'd scratch: the array is part of this module's image, so it
+ * exists on a device as soon as the module is loaded there. */
+static __device__ __align__(256) float g_noalloc_part[WC_NOALLOC_PART_FLOATS];
+
+extern "C" int wc_noalloc_part(float **ptr)
+{
+    return (int)cudaGetSymbolAddress((void **)ptr, g_noalloc_part);
+}
+
 extern "C" size_t wc_matvec_part_floats(int G, int M, int N)
 {
     const TileGeom g = make_geom(M, N, 1, kVsMatvec, 3, 512);

@@ -821,6 +821,73 @@ out:
     return rc;
 }
 
+/* Allocation-free form of vq_matvec_dev. The partial sums go to the fixed
+ * device array behind wc_noalloc_part instead of the growable scratch, so
+ * no call makes cudaMalloc or cudaFree (whose implicit device-wide
+ * synchronisation a running decode loop cannot afford, and which can fail
+ * once the caller has reserved the device's memory). The array's address
+ * is looked up once per device ordinal and kept here, outside S, so that
+ * it survives shutdown/init: the module (and with it the array) stays
+ * loaded while the device's primary context lives. Every partial a call
+ * reads back is written earlier in the same call, so nothing has to start
+ * at zero. */
+#define WC_NOALLOC_MAX_DEV 64
+_Static_assert(WASTE_CUDA_NOALLOC_SCRATCH_BYTES == WC_NOALLOC_PART_FLOATS * sizeof(float),
+               "header and kernel disagree on the fixed scratch size");
+static float *g_noalloc_part[WC_NOALLOC_MAX_DEV];
+
+int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
+                                     const uint16_t *const *scale, const float *const *x,
+                                     float *const *y, int M, int N, int cb_base, int stages,
+                                     void *stream)
+{
+    int rc = 0;
+    if (G <= 0 || G > WC_MAX_G || !idx || !scale || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "matvec_dev_noalloc: G must be 1..%d, pointers non-NULL",
+                    WC_MAX_G);
+    for (int g = 0; g < G; g++)
+        if (((uintptr_t)idx[g] & 15) || ((uintptr_t)x[g] & 15))
+            return fail(WASTE_CUDA_E_ARG, "matrix %d: index or x pointer not 16-byte aligned", g);
+    pthread_mutex_lock(&g_mu);
+    if ((rc = check_mat(M, N, cb_base, stages))) goto out;
+    const size_t need = wc_matvec_part_floats(G, M, N) * sizeof(float);
+    if (need > WASTE_CUDA_NOALLOC_SCRATCH_BYTES) {
+        rc = fail(WASTE_CUDA_E_ARG,
+                  "matvec_dev_noalloc: G=%d of %dx%d needs %zu bytes of partial sums, more than "
+                  "the fixed %zu-byte scratch (G * ceil(N/128) * M * 4 must not exceed it)",
+                  G, M, N, need, (size_t)WASTE_CUDA_NOALLOC_SCRATCH_BYTES);
+        goto out;
+    }
+    int cur = -1;
+    CK(cudaGetDevice(&cur), "cudaGetDevice");
+    if (cur != S.device || cur < 0 || cur >= WC_NOALLOC_MAX_DEV) {
+        rc = fail(WASTE_CUDA_E_ARG, "matvec_dev_noalloc: current device %d is not the "
+                  "library's device %d", cur, S.device);
+        goto out;
+    }
+    if (!g_noalloc_part[cur]) {       /* once per device, with it current */
+        float *p = NULL;
+        CK((cudaError_t)wc_noalloc_part(&p), "fixed scratch address");
+        if (!p) {
+            rc = fail(WASTE_CUDA_E_DEVICE, "fixed scratch address: NULL");
+            goto out;
+        }
+        g_noalloc_part[cur] = p;
+    }
+    static wc_matvec_args a;
+    memset(&a, 0, sizeof a);
+    a.G = G; a.M = M; a.N = N; a.stages = stages; a.cb_base = cb_base;
+    for (int g = 0; g < G; g++) {
+        a.idx[g] = idx[g]; a.scale[g] = scale[g]; a.x[g] = x[g]; a.y[g] = y[g];
+    }
+    a.books = S.d_books;
+    a.part = g_noalloc_part[cur];
+    CK((cudaError_t)wc_matvec_launch(&a, stream ? stream : (void *)S.stream), "matvec");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
 int waste_cuda_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale, int M, int N,
                           int cb_base, int stages)
 {
