@@ -372,15 +372,20 @@ def run_warp(args):
     for _ in range(3):
         wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
     torch.cuda.synchronize()
+    # The launches are queued behind a GPU-side sleep that outlasts the host's
+    # enqueue time (the Python wrapper builds its pointer tables per call), so
+    # the events bracket back-to-back device work only.
     m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    m0.record(s)
-    for _ in range(mv_iters):
-        wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
-    m1.record(s)
+    with torch.cuda.stream(s):
+        torch.cuda._sleep(int(2e8))                  # ~0.1 s at 2 GHz
+        m0.record(s)
+        for _ in range(mv_iters):
+            wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
+        m1.record(s)
     torch.cuda.synchronize()
     wb.profile(True)
     with torch.cuda.stream(s):
-        torch.cuda._sleep(int(1e6))
+        torch.cuda._sleep(int(1e8))
         for _ in range(10):
             wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
     torch.cuda.synchronize()

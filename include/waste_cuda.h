@@ -6,8 +6,9 @@
  *
  * Every entry point is `extern "C"`, takes plain pointers and sizes, returns
  * an int status (0 = done; negative = the caller falls back or reports, as
- * the reference's slot contract asks) and never allocates on the caller's
- * behalf. Host-pointer entry points are synchronous: inputs are read and
+ * the reference's slot contract asks) and hands the caller no memory to
+ * free: what it allocates (banks, trunks, workspace, scratch) is its own and
+ * goes with vq_bank_free / shutdown. Host-pointer entry points are synchronous: inputs are read and
  * outputs written before they return. `_dev` entry points take device
  * pointers and a cudaStream_t (as void*), and are ordered on that stream.
  *
@@ -101,8 +102,9 @@ int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries,
  * record_check does (magic, identity, size, fmt, lowrank, codebook range,
  * offset order, room for the scales) before anything is copied. The first
  * call for a layer sizes its bank for n_experts records; the shapes are
- * gate/up [inter][lat] and down [lat][inter]. With expert parallelism a
- * rank loads only the records it owns (waste_cuda_ep_*). */
+ * gate/up [inter][lat] and down [lat][inter]. A caller that shards the
+ * experts loads only the records it owns (first/count); the others stay
+ * absent and a call that names one fails with WASTE_CUDA_E_ARG. */
 int  waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes,
                              int first, int count, const void *records,
                              int inter, int lat, int stages);
@@ -167,13 +169,18 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed,
 int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
                              int *d_idx, float *d_w, void *stream);
 
-/* Sticky error bits raised on the device. The layer path hands the route
- * from the router kernel to the gate/up kernel through a flag; that wait is
- * bounded, and when it runs out it sets WASTE_CUDA_DERR_ROUTE_WAIT and the
- * waiting kernel skips its work instead of hanging. The host form of
- * moe_layer checks this itself; callers of the _dev form call this after
- * synchronising. Waits for the library's stream; reading clears the bits. */
+/* Sticky error bits raised on the device. Every wait inside a kernel is
+ * bounded; when one runs out, the kernel sets a bit and skips its work
+ * instead of hanging:
+ *   WASTE_CUDA_DERR_ROUTE_WAIT  the gate/up kernel waited too long for the
+ *                               router kernel's route flag;
+ *   WASTE_CUDA_DERR_TMA_WAIT    a bulk copy into shared memory did not
+ *                               complete in time.
+ * The host forms check these themselves and return WASTE_CUDA_E_DEVICE;
+ * callers of the _dev forms call this after synchronising. Waits for the
+ * library's stream; reading clears the bits. */
 #define WASTE_CUDA_DERR_ROUTE_WAIT 1u
+#define WASTE_CUDA_DERR_TMA_WAIT   2u
 unsigned waste_cuda_device_errors(void);
 
 /* ---- single VQ3R kernels ---------------------------------------------------
@@ -182,16 +189,18 @@ unsigned waste_cuda_device_errors(void);
  * AVX-512 lutb_range (src/simd_avx2.c:100-133, src/simd_avx512.c:90-123).
  * vq_matvec: y[M] = f16(scale[r]) * sum_v (L0[i0]+L1[i1]+L2[i2]) over the
  * blocked index layout [M/64][N/8][64][stages] (src/model.c:1956-2024).
- * vq_dequant: W[M][N] = (((0 + C0[i0]) + C1[i1]) + C2[i2]) * f16(scale[r]). */
+ * vq_dequant: W[M][N] = (((0 + C0[i0]) + C1[i1]) + C2[i2]) * f16(scale[r]).
+ * Shapes: N a multiple of 8, M at most 8192 for the matvecs. */
 int waste_cuda_lutb(float *lut, const float *x, int cb_base, int nv, int stages);
 int waste_cuda_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
                          const float *x, int M, int N, int cb_base, int stages);
 int waste_cuda_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale,
                           int M, int N, int cb_base, int stages);
 
-/* Batched independent matvecs on device pointers: for g < G,
+/* Batched independent matvecs on device pointers: for g < G (1..120),
  * y[g][M] = VQ(idx[g], scale[g]) . x[g][N]. idx/scale/x/y are arrays of G
- * device pointers held in HOST memory. One launch for all G. */
+ * device pointers held in HOST memory; idx[g] and x[g] 16-byte aligned.
+ * One gather launch for all G, then one reduce launch. */
 int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
                              const uint16_t *const *scale,
                              const float *const *x, float *const *y, int M,
@@ -203,9 +212,9 @@ int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
  * take the device-wide synchronisation of cudaFree while other streams
  * work. vq_matvec_dev grows its partial-sum scratch with cudaFree and
  * cudaMalloc; this entry point allocates nothing and keeps the partial
- * sums in a fixed array of WASTE_CUDA_NOALLOC_SCRATCH_BYTES (16 MiB)
+ * sums in a fixed array of WASTE_CUDA_NOALLOC_SCRATCH_BYTES (32 MiB)
  * compiled into the library. It has no counterpart in the reference.
- *  - Limit: G * ceil(N/128) * M * 4 bytes must fit the array (G = 32
+ *  - Limit: G * ceil(N/64) * M * 4 bytes must fit the array (G = 32
  *    matrices of 4096 x 4096 fill it exactly); larger calls return
  *    WASTE_CUDA_E_ARG with the sizes in waste_cuda_last_error().
  *  - The calling thread's current device must be the library's device.
@@ -217,7 +226,7 @@ int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
  *    (different streams, or different host threads without ordering
  *    between their streams) race on it. Order them on one stream.
  * Arguments, alignment rules and results are those of vq_matvec_dev. */
-#define WASTE_CUDA_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+#define WASTE_CUDA_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
                                      const uint16_t *const *scale,
                                      const float *const *x, float *const *y,

@@ -179,3 +179,36 @@ def test_bank_rejects_bad_record(cuda_lib):
         wb.moe_experts(8, [0, 1], [1.0, 1.0], np.zeros(128, np.float32), 128, 64)
     assert e.value.rc == wb.E_NOBANK
     wb.vq_bank_free(7)
+
+
+def test_sharded_bank(cuda_lib):
+    """A rank that owns half the experts loads only their records: routes
+    over them match the oracle, a route naming an absent record is refused,
+    and the whole-layer path (which may route anywhere) refuses the layer."""
+    wb = cuda_lib
+    L = synth.moe_layer(31, hidden=256, inter=128, n_experts=16, top_k=4, shared_inter=128,
+                        layer=9)
+    x = synth.activations(32, L.hidden)[0]
+    wb.vq_bank_free(L.layer)
+    wb.codebooks_load_f16(L.books_raw)
+    half = L.n_experts // 2
+    wb.vq_bank_load(L.layer, L.n_experts, L.rec_bytes, half, half,
+                    L.bank[half * L.rec_bytes:], L.inter, L.hidden, L.stages)
+    wb.moe_trunk_load(L.layer, L.n_experts, L.hidden, L.top_k, L.renorm, L.routed_scale,
+                      L.router, L.bias, L.shared_inter, L.sh)
+    idx = np.array([9, 15, 8, 12], np.int32)
+    w = np.array([0.4, 0.3, 0.2, 0.1], np.float32)
+    y = wb.moe_experts(L.layer, idx, w, x, L.hidden, L.inter)
+    assert rel_l2(y, O.moe_experts(L, idx, w, x, fma=1)) < TOL
+    with pytest.raises(wb.WasteCudaError) as e:
+        wb.moe_experts(L.layer, [9, 3], [0.5, 0.5], x, L.hidden, L.inter)
+    assert e.value.rc == wb.E_ARG
+    with pytest.raises(wb.WasteCudaError) as e:
+        wb.moe_layer(L.layer, x, L.top_k, L.hidden)
+    assert e.value.rc == wb.E_ARG
+    wb.vq_bank_load(L.layer, L.n_experts, L.rec_bytes, 0, half, L.bank, L.inter, L.hidden,
+                    L.stages)
+    out, ridx, _ = wb.moe_layer(L.layer, x, L.top_k, L.hidden)
+    ro, rio, _ = O.moe_layer(L, x, fma=1)
+    assert np.array_equal(ridx, rio) and rel_l2(out, ro) < TOL
+    wb.vq_bank_free(L.layer)

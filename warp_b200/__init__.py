@@ -319,15 +319,15 @@ def vq_matvec_dev(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base:
         C.c_void_p(stream or None)))
 
 
-NOALLOC_SCRATCH_BYTES = 16 << 20
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 
 def vq_matvec_dev_noalloc(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base: int,
                           stages: int = 3, stream: int = 0):
     """vq_matvec_dev without any device allocation: for callers that reserved
     the device's memory up front, or cannot take cudaFree's device-wide
-    synchronisation mid-run. Partial sums use a fixed 16 MiB array built
-    into the library (G * ceil(N/128) * M * 4 bytes at most; larger calls
+    synchronisation mid-run. Partial sums use a fixed 32 MiB array built
+    into the library (G * ceil(N/64) * M * 4 bytes at most; larger calls
     raise). Calls overlapping on the GPU race on that array; make the first
     call on a device before any stream capture."""
     G = len(idx_ptrs)

@@ -71,6 +71,24 @@ __device__ __forceinline__ uint16_t ld_pin_u16(const void *p)
     return v;
 }
 
+/* Streaming 16-byte load for data read once: an L2 evict-first policy, so
+ * a long index stream does not push out what the kernel wrote (partial
+ * sums that a reduction reads back). */
+__device__ __forceinline__ uint64_t l2_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const void *ptr, uint64_t pol)
+{
+    uint4 v;
+    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(ptr), "l"(pol));
+    return v;
+}
+
 __device__ __forceinline__ float ld_pin_f32(const void *p)
 {
     float v;
@@ -82,7 +100,8 @@ __device__ __forceinline__ float ld_pin_f32(const void *p)
  * family into shared memory:
  *   lut[(v - v0)*ST*256 + s*256 + c] = fma chain over d of x[8v+d]*C[cb+s][c][d]
  * from 0, d ascending — bit-identical to src/simd_avx512.c:104-112.
- * xs: nvs*8 floats already in shared memory. books: [n_books][256][8]. */
+ * xs: nvs*8 floats already in shared memory, 16-byte aligned (read as
+ * float4 broadcasts). books: [n_books][256][8]. */
 template <int ST>
 __device__ __forceinline__ void build_lut_slice(float *lut, const float *xs,
                                                 const float *__restrict__ books,
@@ -93,12 +112,14 @@ __device__ __forceinline__ void build_lut_slice(float *lut, const float *xs,
         const float4 *src = reinterpret_cast<const float4 *>(
             books + ((size_t)(cb + s) * kEntries + c) * kVecDim);
         const float4 a = __ldg(src), b = __ldg(src + 1);
-        const float C[8] = { a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w };
         for (int v = 0; v < nvs; v++) {
-            const float *xv = xs + v * kVecDim;
+            const float4 x0 = *reinterpret_cast<const float4 *>(xs + v * kVecDim);
+            const float4 x1 = *reinterpret_cast<const float4 *>(xs + v * kVecDim + 4);
             float acc = 0.0f;
-#pragma unroll
-            for (int d = 0; d < kVecDim; d++) acc = __fmaf_rn(xv[d], C[d], acc);
+            acc = __fmaf_rn(x0.x, a.x, acc); acc = __fmaf_rn(x0.y, a.y, acc);
+            acc = __fmaf_rn(x0.z, a.z, acc); acc = __fmaf_rn(x0.w, a.w, acc);
+            acc = __fmaf_rn(x1.x, b.x, acc); acc = __fmaf_rn(x1.y, b.y, acc);
+            acc = __fmaf_rn(x1.z, b.z, acc); acc = __fmaf_rn(x1.w, b.w, acc);
             lut[(v * ST + s) * kEntries + c] = acc;
         }
     }
@@ -136,11 +157,12 @@ struct Gather16 {
     const uint8_t *p;
     int n;
 
-    __device__ __forceinline__ static void load(uint32_t *dst, const uint8_t *src)
+    __device__ __forceinline__ void load(uint32_t *dst, const uint8_t *src) const
     {
+        const uint64_t pol = l2_evict_first();   /* one instruction; not kept live */
 #pragma unroll
         for (int i = 0; i < ST; i++) {
-            const uint4 q = ld_pin16(src + 16 * i);
+            const uint4 q = ld_stream16(src + 16 * i, pol);
             dst[4 * i] = q.x; dst[4 * i + 1] = q.y; dst[4 * i + 2] = q.z; dst[4 * i + 3] = q.w;
         }
     }
@@ -157,6 +179,7 @@ struct Gather16 {
     {
         const size_t stride = (size_t)kBlock * ST;
         int v = 0;
+#pragma unroll 1
         for (; v + 1 < n; v += 2) {
             RowStep<ST, 0>::run(acc, b0, L + (size_t)v * ST * kEntries);
             if (v + 2 < n) load(b0, p + (size_t)(v + 2) * stride);
@@ -164,31 +187,6 @@ struct Gather16 {
             if (v + 3 < n) load(b1, p + (size_t)(v + 3) * stride);
         }
         if (v < n) RowStep<ST, 0>::run(acc, b0, L + (size_t)v * ST * kEntries);
-    }
-};
-
-/* All of a thread's positions in registers: NP positions (at most) of one
- * quarter-block, loaded by begin() in one go — one DRAM round trip — and
- * consumed by run(). For tiles whose lanes hold few positions. */
-template <int ST, int NP>
-struct GatherAll {
-    static constexpr int W = 4 * ST;
-    uint32_t w[NP][W];
-    int n;
-
-    __device__ __forceinline__ void begin(const uint8_t *p, int nvv)
-    {
-        n = nvv;
-#pragma unroll
-        for (int i = 0; i < NP; i++)
-            if (i < n) Gather16<ST>::load(w[i], p + (size_t)i * kBlock * ST);
-    }
-
-    __device__ __forceinline__ void run(float *acc, const float *L)
-    {
-#pragma unroll
-        for (int i = 0; i < NP; i++)
-            if (i < n) RowStep<ST, 0>::run(acc, w[i], L + (size_t)i * ST * kEntries);
     }
 };
 
@@ -222,7 +220,8 @@ struct BookRows {
     }
 
     /* lut[(v*ST + s)*256 + code] = FMA chain over d from 0, d ascending —
-     * the same arithmetic as build_lut_slice, from the prefetched rows. */
+     * the same arithmetic as build_lut_slice, from the prefetched rows.
+     * xs 16-byte aligned. */
     __device__ __forceinline__ void build(float *lut, const float *xs, int nvs) const
     {
         if (!all) {
@@ -234,13 +233,15 @@ struct BookRows {
             const int i = threadIdx.x + k * blockDim.x;
             if (i >= ST * kEntries) continue;
             const int s = i / kEntries, code = i % kEntries;
-            const float C[8] = { c[k][0].x, c[k][0].y, c[k][0].z, c[k][0].w,
-                                 c[k][1].x, c[k][1].y, c[k][1].z, c[k][1].w };
+            const float4 a = c[k][0], b = c[k][1];
             for (int v = 0; v < nvs; v++) {
-                const float *xv = xs + v * kVecDim;
+                const float4 x0 = *reinterpret_cast<const float4 *>(xs + v * kVecDim);
+                const float4 x1 = *reinterpret_cast<const float4 *>(xs + v * kVecDim + 4);
                 float acc = 0.0f;
-#pragma unroll
-                for (int d = 0; d < kVecDim; d++) acc = __fmaf_rn(xv[d], C[d], acc);
+                acc = __fmaf_rn(x0.x, a.x, acc); acc = __fmaf_rn(x0.y, a.y, acc);
+                acc = __fmaf_rn(x0.z, a.z, acc); acc = __fmaf_rn(x0.w, a.w, acc);
+                acc = __fmaf_rn(x1.x, b.x, acc); acc = __fmaf_rn(x1.y, b.y, acc);
+                acc = __fmaf_rn(x1.z, b.z, acc); acc = __fmaf_rn(x1.w, b.w, acc);
                 lut[(v * ST + s) * kEntries + code] = acc;
             }
         }

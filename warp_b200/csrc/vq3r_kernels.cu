@@ -268,8 +268,8 @@ struct TileThread {
 
 /* ---- batched matvec (independent matrices, each with its own x) --------- */
 
-template <int ST>
-__global__ void __launch_bounds__(512)
+template <int ST, int MAXT>
+__global__ void __launch_bounds__(MAXT, 2)
 matvec_tiles_kernel(TileGeom g, const wc_matvec_args a)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
@@ -284,6 +284,50 @@ matvec_tiles_kernel(TileGeom g, const wc_matvec_args a)
     build_lut_slice<ST>(lut, xs, a.books, a.cb_base, nvs);
     __syncthreads();
     th.finish(g, lut, a.part + ((size_t)gi * g.ns + slice) * a.M, 0, 1);
+}
+
+/* The same tile for matrices of more than 2048 rows, where one lane of
+ * quarter blocks covers the tile (thread t: row block t/4, quarter t%4) and
+ * no lane reduction is needed: the mapping is fixed, the index words of two
+ * positions are in flight before the table is built, and the partial sums
+ * go straight from registers to memory. Vs = kVsM positions per tile. */
+template <int ST, int MAXT, int kVsM>
+__global__ void __launch_bounds__(MAXT)
+matvec_rows_kernel(int ns, const wc_matvec_args a)
+{
+    extern __shared__ __align__(16) unsigned char smraw[];
+    float *xs = reinterpret_cast<float *>(smraw);
+    float *lut = xs + kVsM * kVecDim;
+    const int gi = blockIdx.x / ns, slice = blockIdx.x % ns;
+    const int nv = a.N / kVecDim, nrb = (a.M + kBlock - 1) / kBlock;
+    const int rb = threadIdx.x >> 2, q = threadIdx.x & 3;
+    const int v0 = slice * kVsM, nvs = min(kVsM, nv - v0);
+    const bool active = rb < nrb;
+    Gather16<ST> gat;
+    const uint8_t *p = a.idx[gi] + (((size_t)rb * nv + v0) * kBlock + q * 16) * ST;
+    if (active) gat.begin(p, nvs);
+    else gat.n = 0;
+    const float *xg = a.x[gi] + (size_t)v0 * kVecDim;
+    for (int i = threadIdx.x; i < nvs * kVecDim; i += blockDim.x) xs[i] = xg[i];
+    __syncthreads();
+    build_lut_slice<ST>(lut, xs, a.books, a.cb_base, nvs);
+    __syncthreads();
+    if (!active) return;
+    float acc[kRowsPerThread];
+#pragma unroll
+    for (int k = 0; k < kRowsPerThread; k++) acc[k] = 0.0f;
+    gat.run(acc, lut);
+    const int row0 = rb * kBlock + q * 16;
+    float *dst = a.part + ((size_t)gi * ns + slice) * a.M + row0;
+    if (row0 + 16 <= a.M && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+        for (int k = 0; k < kRowsPerThread; k += 4)
+            *reinterpret_cast<float4 *>(dst + k) = make_float4(acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < kRowsPerThread; k++)
+            if (row0 + k < a.M) dst[k] = acc[k];
+    }
 }
 
 __global__ void matvec_reduce_kernel(int ns, const wc_matvec_args a)
@@ -304,8 +348,8 @@ template <int ST>
 __global__ void lutb_kernel(float *lut, const float *x, const float *books,
                             int cb, int nv)
 {
-    /* one block per position */
-    __shared__ float xs[kVecDim];
+    /* one block per position; build_lut_slice reads xs as float4 */
+    __shared__ __align__(16) float xs[kVecDim];
     const int v = blockIdx.x;
     if (threadIdx.x < kVecDim) xs[threadIdx.x] = x[(size_t)v * kVecDim + threadIdx.x];
     __syncthreads();
@@ -1267,7 +1311,11 @@ extern "C" int wc_moe_launch(const wc_moe_args *a, void *stream)
     }
 }
 
-static constexpr int kVsMatvec = 16;
+/* 8 positions per tile and a 256-thread target (one lane per quarter
+ * block at M = 4096): four tiles per SM, each with a 24 KB table — the
+ * shape that keeps the shared-memory pipe busiest (measured against 16/32
+ * positions, 128-512 threads, and cluster-reduced slices). */
+static constexpr int kVsMatvec = 8;
 
 /* The allocation-free matvec's partial sums live here instead of in
  * cudaMalloc'd scratch: the array is part of this module's image, so it
@@ -1281,19 +1329,30 @@ extern "C" int wc_noalloc_part(float **ptr)
 
 extern "C" size_t wc_matvec_part_floats(int G, int M, int N)
 {
-    const TileGeom g = make_geom(M, N, 1, kVsMatvec, 3, 512);
+    const TileGeom g = make_geom(M, N, 1, kVsMatvec, 3, 256);
     return (size_t)G * g.ns * M;
 }
 
 template <int ST>
 static int matvec_launch_st(const wc_matvec_args *a, cudaStream_t s)
 {
-    const TileGeom g = make_geom(a->M, a->N, 1, kVsMatvec, ST, 512);
-    cudaFuncSetAttribute(matvec_tiles_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)g.smem);
+    const TileGeom g = make_geom(a->M, a->N, 1, kVsMatvec, ST, 256);
     const int tiles = a->G * g.ns;
-    int pe = prof_begin(WC_PH_MATVEC, s);
-    matvec_tiles_kernel<ST><<<tiles, g.threads, g.smem, s>>>(g, *a);
+    int pe;
+    if (g.nlanes == 1) {           /* M > 2048: one thread per quarter block */
+        const int threads = ((g.nrb * 4 + 31) / 32) * 32;
+        const size_t smem = ((size_t)kVsMatvec * kVecDim + (size_t)kVsMatvec * ST * kEntries) * 4;
+        const auto k = threads <= 256 ? matvec_rows_kernel<ST, 256, kVsMatvec>
+                                      : matvec_rows_kernel<ST, 512, kVsMatvec>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        pe = prof_begin(WC_PH_MATVEC, s);
+        k<<<tiles, threads, smem, s>>>(g.ns, *a);
+    } else {
+        const auto k = matvec_tiles_kernel<ST, 512>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+        pe = prof_begin(WC_PH_MATVEC, s);
+        k<<<tiles, g.threads, g.smem, s>>>(g, *a);
+    }
     prof_end(pe, s);
     const int n = a->G * a->M;
     pe = prof_begin(WC_PH_MATVEC_REDUCE, s);

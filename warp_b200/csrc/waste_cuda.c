@@ -48,6 +48,8 @@ typedef struct {
     wc_bank kb;                  /* device view                              */
     uint8_t *d_base;
     int n_total;                 /* experts in the layer                      */
+    uint8_t *present;            /* host: which records have been loaded      */
+    int n_present;
     int have_hdr;                /* offsets/codebook fixed by the first record */
     /* trunk */
     int trunk;
@@ -248,6 +250,7 @@ static void free_layer(wc_layer *L)
     cudaFree(L->d_router); cudaFree(L->d_bias);
     cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
     cudaFree(L->d_shg_s); cudaFree(L->d_shu_s); cudaFree(L->d_shd_s);
+    free(L->present);
     memset(L, 0, sizeof *L);
 }
 
@@ -420,6 +423,10 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
         }
     }
     if (!L->d_base) {
+        free(L->present);
+        L->present = (uint8_t *)calloc((size_t)n_experts, 1);
+        L->n_present = 0;
+        if (!L->present) { rc = fail(WASTE_CUDA_E_NOMEM, "bank index"); goto out; }
         CK(cudaMalloc((void **)&L->d_base, rec_bytes * (size_t)n_experts), "bank");
         L->n_total = n_experts;
         L->kb.rec_bytes = rec_bytes;
@@ -441,6 +448,10 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
     L->kb.base = L->d_base;
     CK(cudaMemcpy(L->d_base + (size_t)first * rec_bytes, records, rec_bytes * (size_t)count,
                   cudaMemcpyHostToDevice), "bank H2D");
+    for (int i = first; i < first + count; i++) {
+        L->n_present += !L->present[i];
+        L->present[i] = 1;
+    }
     L->loaded = 1;
 out:
     pthread_mutex_unlock(&g_mu);
@@ -456,6 +467,9 @@ void waste_cuda_vq_bank_free(int layer)
         wc_layer *L = &S.layer[layer];
         cudaFree(L->d_base);
         L->d_base = NULL;
+        free(L->present);
+        L->present = NULL;
+        L->n_present = 0;
         L->loaded = L->have_hdr = 0;
         memset(&L->kb, 0, sizeof L->kb);
     }
@@ -539,8 +553,12 @@ static int layer_ready(int layer, int lat, int inter, wc_layer **out)
 static int check_route(const wc_layer *L, const int *idx, int n)
 {
     for (int i = 0; i < n; i++)
+    {
         if (idx[i] < L->kb.first || idx[i] >= L->kb.first + L->kb.n_experts)
             return fail(WASTE_CUDA_E_ARG, "expert id %d outside the bank", idx[i]);
+        if (!L->present[idx[i]])
+            return fail(WASTE_CUDA_E_ARG, "expert %d's record was not loaded here", idx[i]);
+    }
     return 0;
 }
 
@@ -621,7 +639,7 @@ static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
     if (L->hidden != L->kb.lat)
         return fail(WASTE_CUDA_E_ARG, "layer %d: router width %d != expert width %d", layer,
                     L->hidden, L->kb.lat);
-    if (L->kb.first != 0 || L->kb.n_experts != L->E)
+    if (L->kb.first != 0 || L->kb.n_experts != L->E || L->n_present != L->E)
         return fail(WASTE_CUDA_E_ARG, "layer %d: the whole-layer path needs every expert", layer);
     if ((rc = ensure_ws(1, L->top_k, L->E, L->kb.lat, L->kb.inter, L->si, L->kb.stages)))
         return rc;
@@ -754,6 +772,8 @@ static int check_mat(int M, int N, int cb_base, int stages)
 {
     if (M <= 0 || N <= 0 || N % 8 || (stages != 2 && stages != 3) || cb_base < 0)
         return fail(WASTE_CUDA_E_ARG, "matrix: bad shape");
+    if (M > 8192)      /* one tile holds every row of its matrix: 512 threads */
+        return fail(WASTE_CUDA_E_ARG, "matrix: M = %d rows, at most 8192", M);
     if (!S.d_books || cb_base + stages > S.n_books)
         return fail(WASTE_CUDA_E_ARG, "codebooks not loaded or cb_base out of range");
     return 0;
@@ -854,7 +874,7 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
     if (need > WASTE_CUDA_NOALLOC_SCRATCH_BYTES) {
         rc = fail(WASTE_CUDA_E_ARG,
                   "matvec_dev_noalloc: G=%d of %dx%d needs %zu bytes of partial sums, more than "
-                  "the fixed %zu-byte scratch (G * ceil(N/128) * M * 4 must not exceed it)",
+                  "the fixed %zu-byte scratch (G * ceil(N/64) * M * 4 must not exceed it)",
                   G, M, N, need, (size_t)WASTE_CUDA_NOALLOC_SCRATCH_BYTES);
         goto out;
     }

@@ -95,10 +95,10 @@ size_t wc_matvec_part_floats(int G, int M, int N);
 int    wc_matvec_launch(const wc_matvec_args *a, void *stream);
 
 /* Fixed partial-sum scratch of the allocation-free matvec: a module-scope
- * device array of WC_NOALLOC_PART_FLOATS floats (16 MiB). wc_noalloc_part
+ * device array of WC_NOALLOC_PART_FLOATS floats (32 MiB). wc_noalloc_part
  * looks up its address on the current device (cudaGetSymbolAddress; the
  * return is a cudaError_t). */
-#define WC_NOALLOC_PART_FLOATS ((size_t)4 << 20)
+#define WC_NOALLOC_PART_FLOATS ((size_t)8 << 20)
 int    wc_noalloc_part(float **ptr);
 
 int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
