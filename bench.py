@@ -58,6 +58,13 @@ def layer_bytes():
     return routed + shared + router + books + 2 * HIDDEN * 4
 
 
+# DRAM traffic of one gateup_kernel launch (dram__bytes_read.sum +
+# dram__bytes_write.sum), from one ncu capture of this bench's workload
+# (profiles/gateup_kernel_kimi_linear_decode.txt): the algorithmic bytes plus
+# the deliberate L2 prefetch of the chosen experts' down streams.
+GATEUP_TRAFFIC_BYTES = 21_349_376
+
+
 def gateup_bytes():
     """Algorithmic bytes of one gate/up launch (K experts, one token)."""
     from warp_b200 import synth
@@ -422,7 +429,7 @@ def run_warp(args):
             "roofline": {"bound": "hbm", "kernel": "gateup_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
-                         "traffic": None,
+                         "traffic": GATEUP_TRAFFIC_BYTES,
                          "bytes_per_launch": gateup_bytes(), "avg_launch_us": gu_avg * 1e3,
                          "layer_GBps": layer_bytes() / (ms_step / nL / 1e3) / 1e9,
                          "layer_frac": layer_bytes() / (ms_step / nL / 1e3) / 1e9 / peak},
