@@ -212,3 +212,44 @@ def test_sharded_bank(cuda_lib):
     ro, rio, _ = O.moe_layer(L, x, fma=1)
     assert np.array_equal(ridx, rio) and rel_l2(out, ro) < TOL
     wb.vq_bank_free(L.layer)
+
+
+def test_moe_layer_k3_shape(cuda_lib):
+    """K3-class widths (hidden 7168, expert inter 2048, shared inter 2048,
+    top-16) through the whole device layer and the prefill slot: the route
+    bit-exact, outputs within 2e-5 of the oracle. 64 experts keep the bank
+    near 1 GB; the 512-expert router is covered below."""
+    wb = cuda_lib
+    L = synth.moe_layer(77, hidden=7168, inter=2048, n_experts=64, top_k=16,
+                        shared_inter=2048, layer=11, routed_scale=2.827)
+    x = synth.activations(78, L.hidden, T=3)
+    wb.vq_bank_free(L.layer)
+    wb.load_layer(L)
+    out, idx, w = wb.moe_layer(L.layer, x[0], L.top_k, L.hidden)
+    ro, ri, rw = O.moe_layer(L, x[0], fma=1)
+    assert np.array_equal(idx, ri)
+    assert rel_l2(out, ro) < TOL and rel_l2(w, rw) < 1e-6
+    import copy
+    L0 = copy.copy(L)
+    L0.shared_inter = 0
+    yo, route, rws = O.moe_chunk(L0, x, fma=1)
+    y = wb.moe_chunk_experts(L.layer, route, rws, x, L.hidden, L.inter)
+    assert rel_l2(y, yo) < TOL
+    wb.vq_bank_free(L.layer)
+
+
+def test_moe_layer_512_experts_top16(cuda_lib):
+    """The router at 512 experts and top-16 (the K3 routing shape) on small
+    experts: indices bit-exact, output within 2e-5."""
+    wb = cuda_lib
+    L = synth.moe_layer(91, hidden=256, inter=128, n_experts=512, top_k=16, shared_inter=128,
+                        layer=12, with_bias=True)
+    x = synth.activations(92, L.hidden, T=2)
+    wb.vq_bank_free(L.layer)
+    wb.load_layer(L)
+    for t in range(2):
+        out, idx, _ = wb.moe_layer(L.layer, x[t], L.top_k, L.hidden)
+        ro, ri, _ = O.moe_layer(L, x[t], fma=1)
+        assert np.array_equal(idx, ri)
+        assert rel_l2(out, ro) < TOL
+    wb.vq_bank_free(L.layer)

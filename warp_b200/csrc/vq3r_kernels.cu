@@ -539,11 +539,9 @@ __device__ __forceinline__ float dot_q8g_smem(const uint8_t *row, const float *g
  * DRAM round trip. The last block of a token (ticket) routes it. */
 constexpr int kRouterBlock = 256;
 constexpr int kRouterSplit = 4;        /* warps per router row              */
-constexpr int kRouterU4 = 6;           /* float4 per lane: lat/4/4/32 <= 6 -> lat <= 3072 */
-constexpr int kShU = 5;                /* 16-byte chunks per lane: lat <= 2560 */
-constexpr int kXU = 3;                 /* float4 of x per thread: lat <= 3072 */
 constexpr int kMaxPerLane = 32;        /* E <= 1024 (one live bit per lane entry) */
-constexpr int kSiluU = 8;              /* shared SiLU inputs per thread: si <= 1792 */
+constexpr int kRouteMaxK = 32;         /* route_warp: lane j keeps choice j */
+constexpr int kSiluU = 8;              /* shared SiLU inputs per thread held in registers */
 
 struct RouterGeom {
     int rblocks;       /* blocks for the router rows (2 rows per block)      */
@@ -735,6 +733,10 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
             const int i = threadIdx.x - 32 + k * nt;
             if (i < a.si) a.ws.sh_h[(size_t)t * a.si + i] = silu_ref(g[k]) * u[k];
         }
+        for (int i = threadIdx.x - 32 + kSiluU * nt; i < a.si; i += nt)   /* si > 1792 */
+            a.ws.sh_h[(size_t)t * a.si + i] =
+                silu_ref(__ldcg(a.ws.sh_g + (size_t)t * a.si + i)) *
+                __ldcg(a.ws.sh_u + (size_t)t * a.si + i);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1128,6 +1130,17 @@ struct MoeGeom {
 
 constexpr int kSMs = 148;              /* B200 */
 
+/* dynamic shared memory of a router block: barrier | x | the larger of two
+ * router rows (fp32) and eight shared rows (Q8G) | their group scales */
+size_t router_smem(int lat)
+{
+    const size_t ngr = ((size_t)lat + 127) / 128;
+    size_t wmax = (size_t)((kRouterBlock / 32) / kRouterSplit) * lat * 4;
+    const size_t wsh = (size_t)(kRouterBlock / 32) * ngr * 128;
+    if (wsh > wmax) wmax = wsh;
+    return 16 + (size_t)lat * 4 + wmax + (size_t)(kRouterBlock / 32) * ngr * 2 + 16;
+}
+
 /* dynamic shared memory of a shared-down block: barrier | h | scales | rows */
 size_t shared_down_smem(int threads, int rows_pw, int si)
 {
@@ -1166,9 +1179,8 @@ bool moe_geom_ok(const MoeGeom &m, const wc_moe_args *a)
         return a->K <= kMaxTopK && m.gu.smem <= 227 * 1024 && m.d.smem <= 227 * 1024;
     }
 
-    if (a->bank.lat > 4 * 32 * kRouterU4 * kRouterSplit || a->bank.lat > 16 * 32 * kShU) return false;
-    if (a->bank.lat > 4 * kRouterBlock * kXU) return false;
-    if (a->si > (kRouterBlock - 32) * kSiluU) return false;
+    if (router_smem(a->bank.lat) > 227 * 1024 || a->K > kRouteMaxK) return false;
+    if (a->E > 32 * kMaxPerLane) return false;
     if (a->si > 0 && shared_down_smem(m.d.threads, m.sh_rows_pw, a->si) > 227 * 1024) return false;
     if (a->si % (kRouterBlock / 32) || a->bank.lat % 4 || a->si % 4) return false;
     if (m.gu.smem > 227 * 1024 || m.d.smem > 227 * 1024) return false;
@@ -1206,11 +1218,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         if (a->E > 32 * kMaxPerLane) return (int)cudaErrorInvalidValue;
         const RouterGeom rg = router_geom(a->E, a->si);
         const int pe = prof_begin(WC_PH_ROUTER, s);
-        const int ngr = (a->bank.lat + 127) / 128;
-        size_t wmax = (size_t)((kRouterBlock / 32) / kRouterSplit) * a->bank.lat * 4;
-        const size_t wsh = (size_t)(kRouterBlock / 32) * ngr * 128;
-        if (wsh > wmax) wmax = wsh;
-        const size_t rsm = 16 + (size_t)a->bank.lat * 4 + wmax + (size_t)(kRouterBlock / 32) * ngr * 2 + 16;
+        const size_t rsm = router_smem(a->bank.lat);
         cudaFuncSetAttribute(router_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         cudaFuncSetAttribute(router_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         cudaFuncSetAttribute(router_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);

@@ -670,7 +670,8 @@ static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
     }
     if (wc_moe_supported(a))
         return fail(WASTE_CUDA_E_ARG, "layer %d: shape outside the kernels' bounds "
-                    "(hidden <= 3072, shared inter <= 1792, experts <= 1024)", layer);
+                    "(top-K <= 32, experts <= 1024, tiles within 227 KB of shared memory)",
+                    layer);
     *Lp = L;
     return 0;
 }

@@ -74,7 +74,8 @@ void   wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E, int lat,
                        int inter, int si, int stages);
 int    wc_moe_launch(const wc_moe_args *a, void *stream);
 /* 0 when the shapes in `a` are within the kernels' register-resident
- * bounds (hidden <= 3072 and shared inter <= 1792 for the whole layer). */
+ * bounds: every tile within 227 KB of shared memory, and for the whole layer
+ * (device router) top-K <= 32 and experts <= 1024. */
 int    wc_moe_supported(const wc_moe_args *a);
 
 /* Batched matvec: G <= WC_MAX_G matrices of [M][N]. The pointer tables go
