@@ -110,6 +110,16 @@ int  waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes,
                              int inter, int lat, int stages);
 void waste_cuda_vq_bank_free(int layer);
 
+/* Reserves HBM for records [first, first+count) of a layer of n_experts
+ * ahead of loading, for a caller that holds only part of the experts. Later
+ * loads must fall inside the range. Without it, a layer's first
+ * vq_bank_load reserves the whole layer (or, after waste_cuda_ep_init, this
+ * rank's range). No counterpart in the reference, which reads every expert
+ * from disk on one host. */
+int  waste_cuda_vq_bank_reserve(int layer, int n_experts, size_t rec_bytes,
+                                int first, int count, int inter, int lat,
+                                int stages);
+
 /* Trunk tensors of one MoE layer for the device-resident layer path:
  * router [n_experts][hidden] fp32 (F32 per docs/FORMAT.md), its score
  * correction bias (NULL = none), the routing constants, and the shared
@@ -168,6 +178,47 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed,
                          float *weights);
 int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
                              int *d_idx, float *d_w, void *stream);
+
+/* The local part of a layer whose experts are spread over several devices:
+ * T (1..64) tokens through the device router (the same routes on every
+ * device), the routed experts THIS bank holds (all of its range loaded) in
+ * router order, and the shared expert for tokens [sh_t0, sh_t1) only.
+ * d_out[T][hidden] receives these partial sums; a token's output is the sum
+ * of the partials over the devices, which hold disjoint ranges and add the
+ * shared expert once. d_idx/d_w [T][K] receive the routes. For callers
+ * that run their own exchange; waste_cuda_ep_moe_layer_dev wraps it with
+ * NCCL. Ordered on `stream`. */
+int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x,
+                                  float *d_out, int sh_t0, int sh_t1,
+                                  int *d_idx, float *d_w, void *stream);
+
+/* ---- expert parallelism (one process per GPU, NCCL over NVLink) ----------
+ * `world` processes share every MoE layer; rank r holds the contiguous
+ * expert range [r*E/world, (r+1)*E/world) (waste_cuda_ep_range), and the
+ * trunk (router, bias, shared expert) is replicated. Sequence per process:
+ * waste_cuda_init(device); rank 0 calls waste_cuda_ep_unique_id and hands
+ * the bytes to every rank over any channel; every rank calls
+ * waste_cuda_ep_init (it returns once all have joined); then codebooks,
+ * banks (each rank uploads only its own records: a layer's first
+ * vq_bank_load after ep_init reserves the rank's range; a layer call
+ * refuses a bank whose range is not the rank's) and trunks.
+ * waste_cuda_ep_moe_layer_dev: every rank passes its own T tokens (the same
+ * T everywhere, world*T <= 64). The library all-gathers them, routes all of
+ * them, runs its own experts for every token routed there, adds the shared
+ * expert for its own tokens, and reduce-scatters the partial sums so that
+ * each rank receives its own tokens' outputs d_out[T][hidden]. d_idx/d_w
+ * (optional, [T][K]) receive its tokens' routes. Ordered on `stream`;
+ * every rank must make the same calls in the same order. NCCL is loaded at
+ * run time (libnccl.so.2); without it these return WASTE_CUDA_E_NODEV. No
+ * counterpart in the reference, which runs on one host. */
+int  waste_cuda_ep_range(int n_experts, int rank, int world, int *first,
+                         int *count);
+int  waste_cuda_ep_unique_id(void *id, size_t bytes);   /* >= 128 bytes */
+int  waste_cuda_ep_init(int rank, int world, const void *id, size_t bytes);
+void waste_cuda_ep_shutdown(void);
+int  waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x,
+                                 float *d_out, int *d_idx, float *d_w,
+                                 void *stream);
 
 /* Sticky error bits raised on the device. Every wait inside a kernel is
  * bounded; when one runs out, the kernel sets a bit and skips its work

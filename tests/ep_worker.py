@@ -1,0 +1,65 @@
+"""One rank of the two-GPU expert-parallel test (launched by
+tests/test_ep_gpu.py under torchrun): each rank holds half of the experts
+of two layers, decodes its own tokens through the NCCL path, and checks
+them against the oracle on the whole layer."""
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+import oracle as O
+import warp_b200 as wb
+from golden_cases import rel_l2
+from warp_b200 import ep, synth
+
+TOL = 2e-5
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    wb.init(local)
+    ep.setup(rank, world)
+    layers = [synth.moe_layer(71 + k, hidden=768, inter=384, n_experts=64, top_k=8,
+                              shared_inter=384, layer=50 + k, with_bias=bool(k), cb_base=9 * k)
+              for k in range(2)]
+    first, count = ep.ep_range(64, rank, world)
+    wb.codebooks_load_f16(np.concatenate([layers[0].books_raw[:9], layers[1].books_raw[9:18]]))
+    for L in layers:
+        wb.vq_bank_load(L.layer, L.n_experts, L.rec_bytes, first, count,
+                        L.bank[first * L.rec_bytes:], L.inter, L.hidden, L.stages)
+        wb.moe_trunk_load(L.layer, L.n_experts, L.hidden, L.top_k, L.renorm, L.routed_scale,
+                          L.router, L.bias, L.shared_inter, L.sh)
+    T = 3
+    dev = torch.device("cuda", local)
+    for L in layers:
+        x = synth.activations(100 + 10 * rank + L.layer, L.hidden, T=T)
+        dx = torch.from_numpy(x).to(dev)
+        out = torch.empty((T, L.hidden), device=dev)
+        idx = torch.empty((T, L.top_k), dtype=torch.int32, device=dev)
+        ep.moe_layer_dev(L.layer, T, dx.data_ptr(), out.data_ptr(), idx.data_ptr())
+        torch.cuda.synchronize()
+        out, idx = out.cpu().numpy(), idx.cpu().numpy()
+        for t in range(T):
+            ro, ri, _ = O.moe_layer(L, x[t], fma=1)
+            assert np.array_equal(idx[t], ri), (rank, L.layer, t)
+            r = rel_l2(out[t], ro)
+            assert r < TOL, (rank, L.layer, t, r)
+    assert wb.device_errors() == 0
+    dist.barrier()
+    ep.shutdown()
+    dist.destroy_process_group()
+    print(f"ep_worker ok rank {rank}", flush=True)
+
+
+if __name__ == "__main__":
+    main()

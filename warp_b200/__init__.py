@@ -29,6 +29,9 @@ EXPORTS = (
     "waste_cuda_vq_dequant", "waste_cuda_vq_matvec_dev",
     "waste_cuda_launch_count", "waste_cuda_profile", "waste_cuda_profile_read",
     "waste_cuda_device_errors", "waste_cuda_vq_matvec_dev_noalloc",
+    "waste_cuda_vq_bank_reserve", "waste_cuda_moe_layer_part_dev",
+    "waste_cuda_ep_range", "waste_cuda_ep_unique_id", "waste_cuda_ep_init",
+    "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev",
 )
 
 PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -115,6 +118,15 @@ def load_library() -> C.CDLL:
         "waste_cuda_profile": (C.c_int, [C.c_int]),
         "waste_cuda_profile_read": (C.c_int, [P, P, C.c_int]),
         "waste_cuda_device_errors": (C.c_uint, []),
+        "waste_cuda_vq_bank_reserve": (C.c_int, [C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_int,
+                                                 C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_moe_layer_part_dev": (C.c_int, [C.c_int, C.c_int, P, P, C.c_int, C.c_int,
+                                                    P, P, P]),
+        "waste_cuda_ep_range": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P]),
+        "waste_cuda_ep_unique_id": (C.c_int, [P, C.c_size_t]),
+        "waste_cuda_ep_init": (C.c_int, [C.c_int, C.c_int, P, C.c_size_t]),
+        "waste_cuda_ep_shutdown": (None, []),
+        "waste_cuda_ep_moe_layer_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -208,6 +220,13 @@ def vq_bank_free(layer: int):
     load_library().waste_cuda_vq_bank_free(layer)
 
 
+def vq_bank_reserve(layer: int, n_experts: int, rec_bytes: int, first: int, count: int,
+                    inter: int, lat: int, stages: int = 3):
+    """HBM for records [first, first+count) of a layer, ahead of loading."""
+    _check(load_library().waste_cuda_vq_bank_reserve(layer, n_experts, rec_bytes, first, count,
+                                                     inter, lat, stages))
+
+
 def moe_trunk_load(layer: int, n_experts: int, hidden: int, top_k: int, renorm: int,
                    routed_scale: float, router: np.ndarray, bias: np.ndarray | None,
                    sh_inter: int = 0, sh: dict | None = None):
@@ -281,6 +300,15 @@ def moe_layer_dev(layer: int, d_x: int, d_out: int, d_idx: int, d_w: int, stream
     _check(load_library().waste_cuda_moe_layer_dev(layer, C.c_void_p(d_x), C.c_void_p(d_out),
                                                    C.c_void_p(d_idx), C.c_void_p(d_w),
                                                    C.c_void_p(stream or None)))
+
+
+def moe_layer_part_dev(layer: int, T: int, d_x: int, d_out: int, sh_t0: int, sh_t1: int,
+                       d_idx: int, d_w: int, stream: int = 0):
+    """The experts this device holds (+ the shared expert for tokens
+    [sh_t0, sh_t1)) for T tokens: partial sums to be added over devices."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_moe_layer_part_dev(layer, T, v(d_x), v(d_out), sh_t0, sh_t1,
+                                                        v(d_idx), v(d_w), v(stream)))
 
 
 def lutb(x, cb_base: int, stages: int = 3) -> np.ndarray:

@@ -74,7 +74,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) 
         objs.append(o)
     if force or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs,
-              "-lpthread"], verbose)
+              "-lpthread", "-ldl"], verbose)
     return LIB
 
 

@@ -633,6 +633,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int b = blockIdx.x;
     const bool is_router = b < rg.rblocks;
+    const bool sh_here = t >= a.sh_t0 && t < a.sh_t1;     /* this token's shared rows */
     const int ng = (lat + 127) / 128;
     uint64_t *bar = reinterpret_cast<uint64_t *>(smraw);
     float *xs = reinterpret_cast<float *>(smraw + 16);
@@ -651,7 +652,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
         const int rr0 = (b - rg.sblocks_base) * (kRouterBlock / 32);
         kind = rr0 / a.si;
         o0 = rr0 % a.si;
-        nr = max(0, min(kRouterBlock / 32, a.si - o0));
+        nr = sh_here ? max(0, min(kRouterBlock / 32, a.si - o0)) : 0;
         wsrc = reinterpret_cast<const uint8_t *>(kind ? a.shu : a.shg) + (size_t)o0 * ng * 128;
         wbytes = (uint32_t)nr * ng * 128;
     }
@@ -719,7 +720,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     if (ticket != gridDim.x - 1) return;
     if (warp == 0) {
         route_warp<NK>(a, t, lane);
-    } else {
+    } else if (sh_here) {
         float g[kSiluU], u[kSiluU];
         const int nt = blockDim.x - 32;
 #pragma unroll
@@ -751,6 +752,16 @@ __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const in
                                                      int K, int t, int j)
 {
     return bk.base + (size_t)(__ldcg(idx + (size_t)t * K + j) - bk.first) * bk.rec_bytes;
+}
+
+/* Whether routed expert j of token t is held by this bank. With expert
+ * parallelism a rank's bank holds only its own range of ids; the others'
+ * records are not in this GPU's memory, so no address is formed for them:
+ * their tiles skip, and their contributions come from the owning rank. */
+__device__ __forceinline__ bool expert_here(const wc_bank &bk, const int *idx, int K, int t, int j)
+{
+    const int e = __ldcg(idx + (size_t)t * K + j) - bk.first;
+    return e >= 0 && e < bk.n_experts;
 }
 
 /* ---- 2. gate/up ------------------------------------------------------------
@@ -807,17 +818,23 @@ gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
     const int j0 = grp * g.EG;
     const int nm = min(g.EG, a.K - j0);
     /* stage the group's index streams for this slice: (matrix, row block)
-     * runs of nvs positions, in halves [0,h) and [h,nvs) */
+     * runs of nvs positions, in halves [0,h) and [h,nvs); matrices of
+     * experts held by another rank are neither staged nor gathered */
+    uint32_t here = 0;
+    for (int mm = 0; mm < nm; mm++)
+        if (expert_here(bk, idx, a.K, t, j0 + mm)) here |= 1u << mm;
     const uint32_t psz = kBlock * ST;
     const int h = (nvs + 1) / 2;
     const int ncopy = nm * g.nrb;
+    const int nhere = __popc(here) * g.nrb;
     if (threadIdx.x == 0) {
-        mbar_expect_tx(&sm.bars[0], (uint32_t)ncopy * h * psz);
-        if (nvs > h) mbar_expect_tx(&sm.bars[1], (uint32_t)ncopy * (nvs - h) * psz);
+        if (nhere) mbar_expect_tx(&sm.bars[0], (uint32_t)nhere * h * psz);
+        if (nhere && nvs > h) mbar_expect_tx(&sm.bars[1], (uint32_t)nhere * (nvs - h) * psz);
     }
     __syncthreads();
     for (int c = threadIdx.x; c < ncopy; c += blockDim.x) {
         const int m = c / g.nrb, rbl = c % g.nrb;
+        if (!((here >> m) & 1u)) continue;
         const uint8_t *src = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off) +
                              ((size_t)rbl * g.nv + v0) * psz;
         uint8_t *dst = sm.stage + (size_t)(m * g.nrb + rbl) * nvs * psz;
@@ -847,6 +864,7 @@ gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
     gs.Vs = nvs;
     const int m = min(TileThread<ST, GatherSmem<ST>>::matrix_of_thread(g), nm - 1);
     TileThread<ST, GatherSmem<ST>> th(gs, 0, nm, sm.stage + (size_t)m * g.nrb * nvs * psz);
+    th.active = th.active && ((here >> m) & 1u);
     th.G.first = th.vl0;
     th.G.bar0 = &sm.bars[0];
     th.G.bar1 = nvs > h ? &sm.bars[1] : nullptr;
@@ -917,7 +935,7 @@ __device__ __forceinline__ void shared_down_block(const wc_moe_args &a, unsigned
         if (threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
         return;
     }
-    for (int tt = 0; tt < a.T; tt++) {
+    for (int tt = a.sh_t0; tt < a.sh_t1; tt++) {
         __syncthreads();
         stage_floats(hs, a.ws.sh_h + (size_t)tt * a.si, a.si);
         __syncthreads();
@@ -946,6 +964,7 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, int sh_rows_pw,
     int b = blockIdx.x;
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
+    if (!expert_here(bk, idx, a.K, t, j)) return;       /* another rank's expert */
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
     const uint32_t psz = kBlock * ST;
     const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
@@ -1050,7 +1069,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     for (int n = 0; n < kJ; n++) {
         const int j = jl + 8 * n;
         scl[n] = 0.0f;
-        if (j < K && ok) {
+        if (j < K && ok && expert_here(bk, it, K, 0, j)) {
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(
                 bk.base + (size_t)(__ldcg(it + j) - bk.first) * bk.rec_bytes + bk.scale_off) +
                 2 * bk.inter;
@@ -1071,14 +1090,15 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     }
     pdl_wait();
     if (threadIdx.x < K) wsm[threadIdx.x] = __ldcg(w + (size_t)t * K + threadIdx.x);
-    const float shv = (a.si > 0 && jl == 0 && ok) ? __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i)
+    const bool sh_here = a.si > 0 && t >= a.sh_t0 && t < a.sh_t1;
+    const float shv = (sh_here && jl == 0 && ok) ? __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i)
                                                  : 0.0f;
 #pragma unroll
     for (int n = 0; n < kJ; n++) {
         const int j = jl + 8 * n;
         if (j >= K) break;
         float s = 0.0f;
-        if (ok) {
+        if (ok && expert_here(bk, it, K, 0, j)) {
             const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
             float v[kMaxSlicesReg];
 #pragma unroll
@@ -1092,7 +1112,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         accj[j][il] = s;
     }
     if (threadIdx.x == 0) {
-        int last = -1;
+        int last = -1, nn = 0;
         for (int n = 0; n < K; n++) {
             int jj = n;
             if (a.order_by_id) {          /* next larger id, first j routed to it */
@@ -1103,8 +1123,10 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
                 }
                 if (jj >= 0) last = __ldcg(it + jj);
             }
-            order[n] = jj;
+            if (jj >= 0 && !expert_here(bk, it, K, 0, jj)) continue;   /* held elsewhere */
+            order[nn++] = jj;
         }
+        for (; nn < K; nn++) order[nn] = -1;
     }
     __syncthreads();
     if (jl != 0 || !ok) return;
@@ -1116,7 +1138,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         if (a.order_by_id && wj == 0.0f) continue;
         y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
     }
-    if (a.si > 0) y = __fadd_rn(y, shv);
+    if (sh_here) y = __fadd_rn(y, shv);
     a.out[(size_t)t * bk.lat + i] = y;
 }
 

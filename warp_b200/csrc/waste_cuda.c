@@ -15,6 +15,8 @@
 #include "wc_launch.h"
 
 #include <cuda_runtime_api.h>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <pthread.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -86,7 +88,28 @@ static struct {
     int prefetch_next;
 } S;
 
+/* Expert parallelism: this process's rank among `world` processes (one GPU
+ * each) that share every MoE layer, each holding a contiguous range of the
+ * experts. NCCL is resolved at run time (dlopen), so the library loads and
+ * runs single-GPU without it. Kept outside S: shutdown tears it down first. */
+static struct {
+    int active, rank, world;
+    void *lib;
+    ncclComm_t comm;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *);
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                               cudaStream_t);
+    ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                                   ncclComm_t, cudaStream_t);
+    const char *(*error_string)(ncclResult_t);
+    float *d_xall, *d_outall;     /* [world*T][hidden] gathered tokens and partials */
+    size_t all_floats;
+} EP;
+
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
+static void ep_shutdown_locked(void);
 static _Thread_local char g_err[256];
 static char g_err_global[256];
 
@@ -257,6 +280,7 @@ static void free_layer(wc_layer *L)
 void waste_cuda_shutdown(void)
 {
     pthread_mutex_lock(&g_mu);
+    ep_shutdown_locked();
     if (S.inited) {
         cudaStreamSynchronize(S.stream);
         for (int i = 0; i < WC_MAX_LAYERS; i++) free_layer(&S.layer[i]);
@@ -382,26 +406,91 @@ static int check_record(const wc_hdr *h, int layer, int expert, size_t rec_bytes
     return 0;
 }
 
+/* Contiguous split of n experts over `world` ranks: rank r holds
+ * [r*n/world, (r+1)*n/world). */
+static void split_range(int n, int rank, int world, int *first, int *count)
+{
+    const int lo = (int)((long long)rank * n / world);
+    const int hi = (int)((long long)(rank + 1) * n / world);
+    *first = lo;
+    *count = hi - lo;
+}
+
+int waste_cuda_ep_range(int n_experts, int rank, int world, int *first, int *count)
+{
+    if (n_experts <= 0 || world <= 0 || rank < 0 || rank >= world || !first || !count)
+        return fail(WASTE_CUDA_E_ARG, "ep_range: bad arguments");
+    split_range(n_experts, rank, world, first, count);
+    return 0;
+}
+
+/* HBM for records [first, first+count) of a layer of n_experts; the caller
+ * holds g_mu and has checked the shape arguments. */
+static int reserve_locked(int layer, int n_experts, size_t rec_bytes, int first, int count,
+                          int inter, int lat, int stages)
+{
+    int rc = 0;
+    wc_layer *L = &S.layer[layer];
+    if (L->d_base) {
+        if (L->n_total != n_experts || L->kb.rec_bytes != rec_bytes || L->kb.inter != inter ||
+            L->kb.lat != lat || L->kb.stages != stages || L->kb.first != first ||
+            L->kb.n_experts != count)
+            return fail(WASTE_CUDA_E_ARG, "layer %d: bank shape or range differs from the "
+                        "first reservation", layer);
+        return 0;
+    }
+    free(L->present);
+    L->present = (uint8_t *)calloc((size_t)count, 1);
+    L->n_present = 0;
+    if (!L->present) return fail(WASTE_CUDA_E_NOMEM, "bank index");
+    CK(cudaMalloc((void **)&L->d_base, rec_bytes * (size_t)count), "bank");
+    L->n_total = n_experts;
+    L->kb.rec_bytes = rec_bytes;
+    L->kb.inter = inter;
+    L->kb.lat = lat;
+    L->kb.stages = stages;
+    L->kb.n_experts = count;
+    L->kb.first = first;
+    L->kb.base = L->d_base;
+out:
+    return rc;
+}
+
+static int bank_args_ok(int layer, int n_experts, size_t rec_bytes, int first, int count,
+                        int inter, int lat, int stages)
+{
+    return layer >= 0 && layer < WC_MAX_LAYERS && n_experts > 0 && first >= 0 && count > 0 &&
+           first + count <= n_experts && rec_bytes > 0 && rec_bytes % WC_ALIGN == 0 &&
+           inter > 0 && lat > 0 && inter % 8 == 0 && lat % 8 == 0 &&
+           (stages == 2 || stages == 3);
+}
+
+int waste_cuda_vq_bank_reserve(int layer, int n_experts, size_t rec_bytes, int first,
+                               int count, int inter, int lat, int stages)
+{
+    int rc = 0;
+    if (!bank_args_ok(layer, n_experts, rec_bytes, first, count, inter, lat, stages))
+        return fail(WASTE_CUDA_E_ARG, "vq_bank_reserve: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    rc = reserve_locked(layer, n_experts, rec_bytes, first, count, inter, lat, stages);
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
 int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
                             int count, const void *records, int inter, int lat,
                             int stages)
 {
     int rc = 0;
-    if (layer < 0 || layer >= WC_MAX_LAYERS || n_experts <= 0 || first < 0 ||
-        count <= 0 || first + count > n_experts || !records || rec_bytes == 0 ||
-        rec_bytes % WC_ALIGN || inter <= 0 || lat <= 0 || inter % 8 || lat % 8 ||
-        (stages != 2 && stages != 3))
+    if (!records || !bank_args_ok(layer, n_experts, rec_bytes, first, count, inter, lat, stages))
         return fail(WASTE_CUDA_E_ARG, "vq_bank_load: bad arguments");
     pthread_mutex_lock(&g_mu);
     if (!S.inited && (rc = init_locked(-1))) goto out;
     if (!S.d_books) { rc = fail(WASTE_CUDA_E_ARG, "load codebooks before banks"); goto out; }
     wc_layer *L = &S.layer[layer];
-    if (L->d_base && (L->n_total != n_experts || L->kb.rec_bytes != rec_bytes ||
-                      L->kb.inter != inter || L->kb.lat != lat || L->kb.stages != stages)) {
-        rc = fail(WASTE_CUDA_E_ARG, "layer %d: bank shape differs from the first load", layer);
-        goto out;
-    }
-    /* check every header before copying anything */
+    /* check every header before anything is reserved or copied */
     for (int i = 0; i < count; i++) {
         const wc_hdr *h = (const wc_hdr *)((const uint8_t *)records + (size_t)i * rec_bytes);
         if (check_record(h, layer, first + i, rec_bytes, stages, inter, lat)) {
@@ -423,18 +512,21 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
         }
     }
     if (!L->d_base) {
-        free(L->present);
-        L->present = (uint8_t *)calloc((size_t)n_experts, 1);
-        L->n_present = 0;
-        if (!L->present) { rc = fail(WASTE_CUDA_E_NOMEM, "bank index"); goto out; }
-        CK(cudaMalloc((void **)&L->d_base, rec_bytes * (size_t)n_experts), "bank");
-        L->n_total = n_experts;
-        L->kb.rec_bytes = rec_bytes;
-        L->kb.inter = inter;
-        L->kb.lat = lat;
-        L->kb.stages = stages;
-        L->kb.n_experts = n_experts;
-        L->kb.first = 0;
+        /* first load of the layer: the whole layer, or this rank's range */
+        int r0 = 0, rn = n_experts;
+        if (EP.active) split_range(n_experts, EP.rank, EP.world, &r0, &rn);
+        if ((rc = reserve_locked(layer, n_experts, rec_bytes, r0, rn, inter, lat, stages)))
+            goto out;
+    } else if (L->n_total != n_experts || L->kb.rec_bytes != rec_bytes ||
+               L->kb.inter != inter || L->kb.lat != lat || L->kb.stages != stages) {
+        rc = fail(WASTE_CUDA_E_ARG, "layer %d: bank shape differs from the first load", layer);
+        goto out;
+    }
+    if (first < L->kb.first || first + count > L->kb.first + L->kb.n_experts) {
+        rc = fail(WASTE_CUDA_E_ARG, "layer %d: records [%d, %d) fall outside the experts "
+                  "this bank holds, [%d, %d)", layer, first, first + count, L->kb.first,
+                  L->kb.first + L->kb.n_experts);
+        goto out;
     }
     if (!L->have_hdr) {
         const wc_hdr *h0 = (const wc_hdr *)records;
@@ -445,10 +537,10 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
         L->kb.cb_base = h0->codebook_id;
         L->have_hdr = 1;
     }
-    L->kb.base = L->d_base;
-    CK(cudaMemcpy(L->d_base + (size_t)first * rec_bytes, records, rec_bytes * (size_t)count,
+    const int at = first - L->kb.first;
+    CK(cudaMemcpy(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
                   cudaMemcpyHostToDevice), "bank H2D");
-    for (int i = first; i < first + count; i++) {
+    for (int i = at; i < at + count; i++) {
         L->n_present += !L->present[i];
         L->present[i] = 1;
     }
@@ -556,7 +648,7 @@ static int check_route(const wc_layer *L, const int *idx, int n)
     {
         if (idx[i] < L->kb.first || idx[i] >= L->kb.first + L->kb.n_experts)
             return fail(WASTE_CUDA_E_ARG, "expert id %d outside the bank", idx[i]);
-        if (!L->present[idx[i]])
+        if (!L->present[idx[i] - L->kb.first])
             return fail(WASTE_CUDA_E_ARG, "expert %d's record was not loaded here", idx[i]);
     }
     return 0;
@@ -571,6 +663,8 @@ static void fill_args(wc_moe_args *a, const wc_layer *L, int T, int K, int E, in
     a->K = K;
     a->E = E;
     a->si = si;
+    a->sh_t0 = 0;
+    a->sh_t1 = T;
     wc_moe_ws_carve(&a->ws, S.d_ws, T, K, E, L->kb.lat, L->kb.inter, si, L->kb.stages);
 }
 
@@ -630,20 +724,31 @@ int waste_cuda_moe_chunk_experts(const waste_moe_chunk_call *c)
 
 /* ---- whole layer ----------------------------------------------------------- */
 
-static int layer_args(int layer, wc_moe_args *a, wc_layer **Lp)
+/* Arguments for T tokens through the device router. part = 0: the whole
+ * layer, every expert held here. part = 1: the experts this bank holds (all
+ * of its range loaded), the rest left to the ranks that hold them. */
+static int layer_args(int layer, int T, int part, wc_moe_args *a, wc_layer **Lp)
 {
     int rc;
     if (layer < 0 || layer >= WC_MAX_LAYERS || !S.layer[layer].loaded || !S.layer[layer].trunk)
         return fail(WASTE_CUDA_E_NOBANK, "layer %d: bank or trunk not loaded", layer);
     wc_layer *L = &S.layer[layer];
+    if (T <= 0 || T > WC_CHUNK_MAX)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: %d tokens, 1..%d per call", layer, T,
+                    WC_CHUNK_MAX);
     if (L->hidden != L->kb.lat)
         return fail(WASTE_CUDA_E_ARG, "layer %d: router width %d != expert width %d", layer,
                     L->hidden, L->kb.lat);
-    if (L->kb.first != 0 || L->kb.n_experts != L->E || L->n_present != L->E)
-        return fail(WASTE_CUDA_E_ARG, "layer %d: the whole-layer path needs every expert", layer);
-    if ((rc = ensure_ws(1, L->top_k, L->E, L->kb.lat, L->kb.inter, L->si, L->kb.stages)))
+    if (L->n_total != L->E)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: router has %d experts, bank %d", layer, L->E,
+                    L->n_total);
+    if (part ? L->n_present != L->kb.n_experts
+             : (L->kb.first != 0 || L->kb.n_experts != L->E || L->n_present != L->E))
+        return fail(WASTE_CUDA_E_ARG, part ? "layer %d: not every record of the bank's range "
+                    "is loaded" : "layer %d: the whole-layer path needs every expert", layer);
+    if ((rc = ensure_ws(T, L->top_k, L->E, L->kb.lat, L->kb.inter, L->si, L->kb.stages)))
         return rc;
-    fill_args(a, L, 1, L->top_k, L->E, L->si);
+    fill_args(a, L, T, L->top_k, L->E, L->si);
     a->router = L->d_router;
     a->bias = L->d_bias;
     a->renorm = L->renorm;
@@ -684,12 +789,176 @@ int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out, int *d_i
     wc_layer *L = NULL;
     if (!d_x || !d_out || !d_idx || !d_w) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
     pthread_mutex_lock(&g_mu);
-    if ((rc = layer_args(layer, &a, &L))) goto out;
+    if ((rc = layer_args(layer, 1, 0, &a, &L))) goto out;
     a.x = d_x;
     a.out = d_out;
     a.idx_out = d_idx;
     a.w_out = d_w;
     CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "layer kernels");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x, float *d_out,
+                                  int sh_t0, int sh_t1, int *d_idx, float *d_w, void *stream)
+{
+    int rc = 0;
+    wc_moe_args a;
+    wc_layer *L = NULL;
+    if (!d_x || !d_out || !d_idx || !d_w || sh_t0 < 0 || sh_t1 < sh_t0 || sh_t1 > T)
+        return fail(WASTE_CUDA_E_ARG, "moe_layer_part: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = layer_args(layer, T, 1, &a, &L))) goto out;
+    a.x = d_x;
+    a.out = d_out;
+    a.idx_out = d_idx;
+    a.w_out = d_w;
+    a.sh_t0 = sh_t0;
+    a.sh_t1 = sh_t1;
+    CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "layer kernels");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- expert parallelism over NCCL ------------------------------------------ */
+
+static int nccl_fail(ncclResult_t r, const char *what)
+{
+    return fail(WASTE_CUDA_E_DEVICE, "%s: %s", what,
+                EP.error_string ? EP.error_string(r) : "NCCL error");
+}
+
+static int nccl_load(void)
+{
+    if (EP.lib) return 0;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail(WASTE_CUDA_E_NODEV, "expert parallelism needs libnccl.so.2: %s",
+                        dlerror());
+    *(void **)&EP.get_unique_id = dlsym(h, "ncclGetUniqueId");
+    *(void **)&EP.comm_init_rank = dlsym(h, "ncclCommInitRank");
+    *(void **)&EP.comm_destroy = dlsym(h, "ncclCommDestroy");
+    *(void **)&EP.all_gather = dlsym(h, "ncclAllGather");
+    *(void **)&EP.reduce_scatter = dlsym(h, "ncclReduceScatter");
+    *(void **)&EP.error_string = dlsym(h, "ncclGetErrorString");
+    if (!EP.get_unique_id || !EP.comm_init_rank || !EP.comm_destroy || !EP.all_gather ||
+        !EP.reduce_scatter || !EP.error_string) {
+        dlclose(h);
+        return fail(WASTE_CUDA_E_NODEV, "libnccl.so.2 lacks an entry point this library uses");
+    }
+    EP.lib = h;
+    return 0;
+}
+
+int waste_cuda_ep_unique_id(void *id, size_t bytes)
+{
+    if (!id || bytes < sizeof(ncclUniqueId))
+        return fail(WASTE_CUDA_E_ARG, "ep_unique_id: need %zu bytes", sizeof(ncclUniqueId));
+    pthread_mutex_lock(&g_mu);
+    int rc = nccl_load();
+    if (!rc) {
+        ncclUniqueId u;
+        const ncclResult_t r = EP.get_unique_id(&u);
+        if (r != ncclSuccess) rc = nccl_fail(r, "ncclGetUniqueId");
+        else memcpy(id, &u, sizeof u);
+    }
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_ep_init(int rank, int world, const void *id, size_t bytes)
+{
+    int rc = 0;
+    if (world <= 0 || rank < 0 || rank >= world || !id || bytes < sizeof(ncclUniqueId))
+        return fail(WASTE_CUDA_E_ARG, "ep_init: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (EP.active) { rc = fail(WASTE_CUDA_E_ARG, "expert parallelism already initialised"); goto out; }
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "ep_init before waste_cuda_init"); goto out; }
+    if ((rc = nccl_load())) goto out;
+    CK(cudaSetDevice(S.device), "cudaSetDevice");
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof u);
+    const ncclResult_t r = EP.comm_init_rank(&EP.comm, world, u, rank);
+    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclCommInitRank"); goto out; }
+    EP.rank = rank;
+    EP.world = world;
+    EP.active = 1;
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+static void ep_shutdown_locked(void)
+{
+    if (!EP.active) return;
+    if (S.inited) cudaStreamSynchronize(S.stream);
+    EP.comm_destroy(EP.comm);
+    cudaFree(EP.d_xall);
+    cudaFree(EP.d_outall);
+    EP.comm = NULL;
+    EP.d_xall = EP.d_outall = NULL;
+    EP.all_floats = 0;
+    EP.active = EP.rank = EP.world = 0;
+}
+
+void waste_cuda_ep_shutdown(void)
+{
+    pthread_mutex_lock(&g_mu);
+    ep_shutdown_locked();
+    pthread_mutex_unlock(&g_mu);
+}
+
+int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out, int *d_idx,
+                                float *d_w, void *stream)
+{
+    int rc = 0;
+    wc_moe_args a;
+    wc_layer *L = NULL;
+    if (!d_x || !d_out || T <= 0) return fail(WASTE_CUDA_E_ARG, "ep_moe_layer: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!EP.active) { rc = fail(WASTE_CUDA_E_ARG, "ep_moe_layer before ep_init"); goto out; }
+    const int Ta = T * EP.world;
+    if ((rc = layer_args(layer, Ta, 1, &a, &L))) goto out;
+    {
+        int r0, rn;
+        split_range(L->E, EP.rank, EP.world, &r0, &rn);
+        if (L->kb.first != r0 || L->kb.n_experts != rn) {
+            rc = fail(WASTE_CUDA_E_ARG, "layer %d: bank holds [%d, %d), rank %d of %d owns "
+                      "[%d, %d)", layer, L->kb.first, L->kb.first + L->kb.n_experts, EP.rank,
+                      EP.world, r0, r0 + rn);
+            goto out;
+        }
+    }
+    const size_t need = (size_t)Ta * L->hidden;
+    if (need > EP.all_floats) {
+        cudaFree(EP.d_xall);
+        cudaFree(EP.d_outall);
+        EP.d_xall = EP.d_outall = NULL;
+        EP.all_floats = 0;
+        CK(cudaMalloc((void **)&EP.d_xall, need * sizeof(float)), "ep tokens");
+        CK(cudaMalloc((void **)&EP.d_outall, need * sizeof(float)), "ep partials");
+        EP.all_floats = need;
+    }
+    cudaStream_t st = stream ? (cudaStream_t)stream : S.stream;
+    const size_t per = (size_t)T * L->hidden;
+    ncclResult_t r = EP.all_gather(d_x, EP.d_xall, per, ncclFloat32, EP.comm, st);
+    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllGather"); goto out; }
+    a.x = EP.d_xall;
+    a.out = EP.d_outall;
+    a.idx_out = S.d_idx;
+    a.w_out = S.d_w;
+    a.sh_t0 = EP.rank * T;            /* the shared expert once, on the token's rank */
+    a.sh_t1 = EP.rank * T + T;
+    CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
+    r = EP.reduce_scatter(EP.d_outall, d_out, per, ncclFloat32, ncclSum, EP.comm, st);
+    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclReduceScatter"); goto out; }
+    const size_t kb = (size_t)T * L->top_k;
+    if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)EP.rank * kb, kb * sizeof(int),
+                                  cudaMemcpyDeviceToDevice, st), "route copy");
+    if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)EP.rank * kb, kb * sizeof(float),
+                                cudaMemcpyDeviceToDevice, st), "weight copy");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -702,7 +971,7 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
     wc_layer *L = NULL;
     if (!x || !out) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
     pthread_mutex_lock(&g_mu);
-    if ((rc = layer_args(layer, &a, &L))) goto out;
+    if ((rc = layer_args(layer, 1, 0, &a, &L))) goto out;
     const size_t xb = (size_t)L->hidden * sizeof(float);
     memcpy(S.h_x, x, xb);
     CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");

@@ -56,6 +56,8 @@ typedef struct {
     int *idx_out;             /* written by the router when router != NULL   */
     float *w_out;
     int si;                   /* shared intermediate; 0 = no shared expert   */
+    int sh_t0, sh_t1;         /* tokens [sh_t0, sh_t1) get the shared expert
+                                 (all of them, unless expert parallel)       */
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
