@@ -19,8 +19,13 @@ over 32 distinct matrices (203 MB of indices), in HBM GB/s.
 from the reference sources into oracle/_ref) on this host's cores, same
 metric and config.
 
-Multi-GPU (torchrun): replicas — each rank decodes its own token stream
-against its own resident copy of the experts (weak scaling).
+Multi-GPU (torchrun, --gpus N > 1): expert parallel — each rank holds a
+contiguous 1/N of every layer's experts (the router and shared expert are
+replicated) and contributes one token per step, so a step decodes N tokens;
+the routed tokens and partial sums cross NVLink inside the library (NCCL
+all-gather / reduce-scatter). Per-GPU work stays ~K expert-token pairs per
+layer (weak scaling). `--parallel replicas` instead runs N independent
+copies of the single-GPU decode.
 """
 from __future__ import annotations
 
@@ -234,8 +239,14 @@ def run_warp(args):
                                 device_id=torch.device("cuda", local))
     wb.init(local)
     dev = torch.device("cuda", local)
+    ep_mode = world > 1 and args.parallel == "ep"
+    first, count = 0, EXPERTS
+    if ep_mode:
+        from warp_b200 import ep
+        ep.setup(rank, world)
+        first, count = ep.ep_range(EXPERTS, rank, world)
 
-    # ---- resident layers
+    # ---- resident layers (this rank's experts)
     base = synth.moe_layer(SEED)
     nL = args.layers
     for L in range(1, nL + 1):
@@ -243,8 +254,8 @@ def run_warp(args):
         wb.vq_bank_free(L)
         if L == 1:
             wb.codebooks_load_f16(base.books_raw)
-        wb.vq_bank_load(L, lay.n_experts, lay.rec_bytes, 0, lay.n_experts, lay.bank,
-                        lay.inter, lay.hidden, lay.stages)
+        wb.vq_bank_load(L, lay.n_experts, lay.rec_bytes, first, count,
+                        lay.bank[first * lay.rec_bytes:], lay.inter, lay.hidden, lay.stages)
         wb.moe_trunk_load(L, lay.n_experts, lay.hidden, lay.top_k, lay.renorm,
                           lay.routed_scale, lay.router, lay.bias, lay.shared_inter, lay.sh)
         del lay
@@ -258,8 +269,12 @@ def run_warp(args):
 
     def step_direct(t):
         for L in range(nL):
-            wb.moe_layer_dev(L + 1, xs[t, L].data_ptr(), out[L].data_ptr(), idx[L].data_ptr(),
-                             w[L].data_ptr(), s.cuda_stream)
+            if ep_mode:
+                ep.moe_layer_dev(L + 1, 1, xs[t, L].data_ptr(), out[L].data_ptr(),
+                                 idx[L].data_ptr(), w[L].data_ptr(), s.cuda_stream)
+            else:
+                wb.moe_layer_dev(L + 1, xs[t, L].data_ptr(), out[L].data_ptr(),
+                                 idx[L].data_ptr(), w[L].data_ptr(), s.cuda_stream)
 
     with torch.cuda.stream(s):
         for k in range(max(args.warmup, 1)):
@@ -267,16 +282,19 @@ def run_warp(args):
     torch.cuda.synchronize()
 
     # ---- one CUDA graph per token slot
-    graphs = []
+    def capture(t):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+            step_direct(t)
+        return g
+
+    graphs = []           # the only references: released before the communicators go
     launches_per_step = None
     try:
         for t in range(ntok):
-            g = torch.cuda.CUDAGraph()
             c0 = wb.launch_count()
-            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
-                step_direct(t)
+            graphs.append(capture(t))
             launches_per_step = wb.launch_count() - c0
-            graphs.append(g)
         use_graphs = True
     except Exception as e:  # direct launches still measure the same kernels
         print(f"graph capture unavailable: {e}", file=sys.stderr)
@@ -294,12 +312,22 @@ def run_warp(args):
     with torch.cuda.stream(s):
         for k in range(args.warmup):
             step(k)
-        t_settle = time.perf_counter()
-        k = 0
-        while time.perf_counter() - t_settle < 0.5:      # let clocks settle
+    torch.cuda.synchronize()
+    # Let clocks settle for ~0.5 s. Every rank runs the SAME number of steps
+    # (an expert-parallel step holds collectives): one step is timed, the
+    # slowest rank's time sets the count.
+    t1 = time.perf_counter()
+    with torch.cuda.stream(s):
+        step(0)
+    s.synchronize()
+    t_step = torch.tensor([time.perf_counter() - t1], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
+    n_settle = max(1, min(2000, int(0.5 / max(float(t_step.item()), 1e-5))))
+    with torch.cuda.stream(s):
+        for k in range(n_settle):
             step(k)
-            k += 1
-            if k % 64 == 0:
+            if k % 64 == 63:
                 s.synchronize()
     torch.cuda.synchronize()
     if dist:
@@ -324,16 +352,33 @@ def run_warp(args):
     ms_step = ms / args.steps
     value = world * args.steps / (ms / 1e3)
 
-    # ---- end to end through the host-buffer entry point (H2D x, D2H out)
-    x_host = [[np.ascontiguousarray(xs_h[t, L]) for L in range(nL)] for t in range(ntok)]
+    # ---- end to end through the public entry points, host buffers: each
+    # layer's x copied in from pinned memory and its output copied back
+    if ep_mode:
+        x_pin = torch.from_numpy(xs_h).pin_memory()
+        o_pin = torch.empty((HIDDEN,), dtype=torch.float32).pin_memory()
+        xd = torch.empty((HIDDEN,), dtype=torch.float32, device=dev)
+
+        def e2e_layer(t, L):
+            with torch.cuda.stream(s):
+                xd.copy_(x_pin[t, L], non_blocking=True)
+                ep.moe_layer_dev(L + 1, 1, xd.data_ptr(), out[L].data_ptr(), idx[L].data_ptr(),
+                                 w[L].data_ptr(), s.cuda_stream)
+                o_pin.copy_(out[L], non_blocking=True)
+            s.synchronize()
+    else:
+        x_host = [[np.ascontiguousarray(xs_h[t, L]) for L in range(nL)] for t in range(ntok)]
+
+        def e2e_layer(t, L):
+            wb.moe_layer(L + 1, x_host[t][L], TOPK, HIDDEN)
     for L in range(nL):
-        wb.moe_layer(L + 1, x_host[0][L], TOPK, HIDDEN)
+        e2e_layer(0, L)
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for k in range(args.steps):
         for L in range(nL):
-            wb.moe_layer(L + 1, x_host[k % ntok][L], TOPK, HIDDEN)
+            e2e_layer(k % ntok, L)
     e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
@@ -420,7 +465,9 @@ def run_warp(args):
             "config": {"workload": "kimi_linear_48b_moe_decode", "hidden": HIDDEN,
                        "moe_inter": INTER, "experts": EXPERTS, "top_k": TOPK,
                        "shared_experts": 1, "moe_layers": nL, "global_batch": world,
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "parallelism": (f"ep{world}" if ep_mode else f"replicas{world}")
+                                      if world > 1 else "single",
+                       "experts_per_gpu": count,
                        "l2": "inputs larger than L2 (~803 MB touched per step)",
                        "cuda_graphs": use_graphs},
             "gpu_launches": int(launches_per_step * args.steps),
@@ -438,9 +485,17 @@ def run_warp(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    # Graphs that hold the library's NCCL calls must be gone before its
+    # communicator is destroyed, or the teardown waits for good.
+    torch.cuda.synchronize()
+    graphs.clear()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if dist:
-        del graphs
         dist.barrier()
+        if ep_mode:
+            ep.shutdown()
         dist.destroy_process_group()
     return 0
 
@@ -454,6 +509,8 @@ def main():
     ap.add_argument("--layers", type=int, default=MOE_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--parallel", choices=("ep", "replicas"), default="ep",
+                    help="with --gpus N > 1: expert parallel (default) or N replicas")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
