@@ -168,6 +168,23 @@ struct waste_moe_chunk_call {
 };
 int waste_cuda_moe_chunk_experts(const waste_moe_chunk_call *c);
 
+/* The prefill expert loop on the tensor cores, device pointers: T tokens
+ * (T*K <= 65536), route/rw [T][K] (router order), x/out [T][lat]. Computes
+ * what moe_chunk_experts does (per token, experts added in ascending id) as
+ * dense tiles: each expert's weights are dequantised into shared memory
+ * once per 128 routed tokens and multiplied on the tensor cores (tcgen05)
+ * with split-fp16 operands, within 2e-5 of the fp32 loop. Needs 3-stage
+ * codebooks that are exact in fp16 (as loaded from codebooks.bin), rows in
+ * multiples of 128, and every record of the layer's bank range loaded;
+ * experts outside the bank are skipped and flagged
+ * (WASTE_CUDA_DERR_BAD_EXPERT). moe_chunk_experts takes this path itself
+ * when a chunk has at least two routed tokens per expert on average
+ * (WASTE_CUDA_PREFILL_TC=0 keeps it on the lookup path). Ordered on
+ * `stream`. */
+int waste_cuda_moe_prefill_dev(int layer, int T, int K, const int *d_route,
+                               const float *d_rw, const float *d_x,
+                               float *d_out, void *stream);
+
 /* ---- the whole MoE layer -------------------------------------------------
  * moe_layer (src/model.c:2713-2939) for a Kimi-Linear-shaped layer: router
  * matvec, sigmoid + bias top-K (strict >, lowest index wins ties), renorm
@@ -231,7 +248,8 @@ int  waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x,
  * callers of the _dev forms call this after synchronising. Waits for the
  * library's stream; reading clears the bits. */
 #define WASTE_CUDA_DERR_ROUTE_WAIT 1u
-#define WASTE_CUDA_DERR_TMA_WAIT   2u
+#define WASTE_CUDA_DERR_TMA_WAIT   2u   /* also: a tensor-core commit that never came */
+#define WASTE_CUDA_DERR_BAD_EXPERT 4u   /* a device-side route named an expert not held */
 unsigned waste_cuda_device_errors(void);
 
 /* ---- single VQ3R kernels ---------------------------------------------------

@@ -31,7 +31,7 @@ EXPORTS = (
     "waste_cuda_device_errors", "waste_cuda_vq_matvec_dev_noalloc",
     "waste_cuda_vq_bank_reserve", "waste_cuda_moe_layer_part_dev",
     "waste_cuda_ep_range", "waste_cuda_ep_unique_id", "waste_cuda_ep_init",
-    "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev",
+    "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev", "waste_cuda_moe_prefill_dev",
 )
 
 PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -127,6 +127,7 @@ def load_library() -> C.CDLL:
         "waste_cuda_ep_init": (C.c_int, [C.c_int, C.c_int, P, C.c_size_t]),
         "waste_cuda_ep_shutdown": (None, []),
         "waste_cuda_ep_moe_layer_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_moe_prefill_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -309,6 +310,14 @@ def moe_layer_part_dev(layer: int, T: int, d_x: int, d_out: int, sh_t0: int, sh_
     v = lambda p: C.c_void_p(int(p) or None)
     _check(load_library().waste_cuda_moe_layer_part_dev(layer, T, v(d_x), v(d_out), sh_t0, sh_t1,
                                                         v(d_idx), v(d_w), v(stream)))
+
+
+def moe_prefill_dev(layer: int, T: int, K: int, d_route: int, d_rw: int, d_x: int, d_out: int,
+                    stream: int = 0):
+    """Prefill expert loop on the tensor cores (device pointers)."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_moe_prefill_dev(layer, T, K, v(d_route), v(d_rw), v(d_x),
+                                                     v(d_out), v(stream)))
 
 
 def lutb(x, cb_base: int, stages: int = 3) -> np.ndarray:

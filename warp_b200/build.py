@@ -23,7 +23,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["vq3r_kernels.cu"]
+CU_SOURCES = ["vq3r_kernels.cu", "prefill_tc.cu"]
 C_SOURCES = ["waste_cuda.c"]
 HEADERS = ["vq3r_common.cuh", "wc_launch.h"]
 
@@ -74,7 +74,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) 
         objs.append(o)
     if force or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs,
-              "-lpthread", "-ldl"], verbose)
+              "-lpthread", "-ldl", "-lm"], verbose)
     return LIB
 
 

@@ -1357,6 +1357,8 @@ extern "C" int wc_noalloc_part(float **ptr)
     return (int)cudaGetSymbolAddress((void **)ptr, g_noalloc_part);
 }
 
+extern "C" void wc_count_launches(int n) { g_launches += (uint64_t)n; }
+
 extern "C" size_t wc_matvec_part_floats(int G, int M, int N)
 {
     const TileGeom g = make_geom(M, N, 1, kVsMatvec, 3, 256);

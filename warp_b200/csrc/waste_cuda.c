@@ -18,6 +18,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 #include <pthread.h>
+#include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -69,6 +70,11 @@ static struct {
     char name[300];
     float *d_books;
     int n_books;
+    float *book_absmax;          /* host: max |entry| of each book               */
+    int books_f16;               /* every entry an fp16 normal or zero (exact in fp16) */
+    /* batched (prefill) path on the tensor cores */
+    void *d_pf;
+    size_t pf_bytes;
     wc_layer layer[WC_MAX_LAYERS];
     /* workspace for one launch of up to WC_CHUNK_MAX tokens */
     float *d_ws;
@@ -110,6 +116,8 @@ static struct {
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
+static int pf_wanted(const wc_layer *L, int T, int K);
+static int pf_args(const wc_layer *L, int T, int K, wc_pf_args *a);
 static _Thread_local char g_err[256];
 static char g_err_global[256];
 
@@ -180,6 +188,12 @@ int waste_cuda_profile_read(double *ms, uint64_t *launches, int nphase)
     }
     pthread_mutex_unlock(&g_mu);
     return 0;
+}
+
+static int getenv_flag(const char *name, int dflt)
+{
+    const char *e = getenv(name);
+    return (e && *e) ? (*e != '0') : dflt;
 }
 
 static int pick_device(int requested)
@@ -285,7 +299,8 @@ void waste_cuda_shutdown(void)
         cudaStreamSynchronize(S.stream);
         for (int i = 0; i < WC_MAX_LAYERS; i++) free_layer(&S.layer[i]);
         cudaFree(S.d_books); cudaFree(S.d_ws); cudaFree(S.d_x); cudaFree(S.d_out);
-        cudaFree(S.d_idx); cudaFree(S.d_w); cudaFree(S.d_tmp);
+        cudaFree(S.d_idx); cudaFree(S.d_w); cudaFree(S.d_tmp); cudaFree(S.d_pf);
+        free(S.book_absmax);
         cudaFreeHost(S.h_x); cudaFreeHost(S.h_out); cudaFreeHost(S.h_idx);
         cudaFreeHost(S.h_w);
         cudaStreamDestroy(S.stream);
@@ -333,6 +348,22 @@ static int books_upload(const float *books, int n_books)
     int rc = 0;
     const size_t bytes = (size_t)n_books * 256 * 8 * sizeof(float);
     if (S.d_books) { cudaFree(S.d_books); S.d_books = NULL; S.n_books = 0; }
+    free(S.book_absmax);
+    S.book_absmax = (float *)calloc((size_t)n_books, sizeof(float));
+    if (!S.book_absmax) return fail(WASTE_CUDA_E_NOMEM, "codebook maxima");
+    /* per-book maxima (the tensor-core path's weight pre-scale), and whether
+     * every entry is exact in fp16 (normal or zero), which that path needs */
+    S.books_f16 = 1;
+    for (int b = 0; b < n_books; b++)
+        for (size_t i = 0; i < 256 * 8; i++) {
+            const float v = books[(size_t)b * 256 * 8 + i];
+            uint32_t bits;
+            memcpy(&bits, &v, 4);
+            const uint32_t ex = (bits >> 23) & 0xff;
+            if (v != 0.0f && (ex < 113 || ex > 142 || (bits & 0x1fff))) S.books_f16 = 0;
+            const float m = v < 0 ? -v : v;
+            if (m > S.book_absmax[b]) S.book_absmax[b] = m;
+        }
     CK(cudaMalloc((void **)&S.d_books, bytes), "codebooks");
     CK(cudaMemcpy(S.d_books, books, bytes, cudaMemcpyHostToDevice), "codebooks H2D");
     S.n_books = n_books;
@@ -690,18 +721,33 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
                        S.stream), "idx H2D");
     CK(cudaMemcpyAsync(S.d_w, S.h_w, (size_t)T * K * sizeof(float), cudaMemcpyHostToDevice,
                        S.stream), "w H2D");
-    wc_moe_args a;
-    fill_args(&a, L, T, K, 1, 0);
-    a.x = S.d_x;
-    a.idx = S.d_idx;
-    a.w = S.d_w;
-    a.out = S.d_out;
-    a.order_by_id = order_by_id;
-    a.prefetch_down = 1;
-    if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
-    CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
+    if (order_by_id && pf_wanted(L, T, K)) {
+        /* a chunk with enough tokens per expert: dense tiles on the tensor cores */
+        wc_pf_args pa;
+        if ((rc = pf_args(L, T, K, &pa))) goto out;
+        pa.route = S.d_idx;
+        pa.rw = S.d_w;
+        pa.x = S.d_x;
+        pa.out = S.d_out;
+        CK((cudaError_t)wc_pf_launch(&pa, S.stream), "prefill kernels");
+    } else {
+        wc_moe_args a;
+        fill_args(&a, L, T, K, 1, 0);
+        a.x = S.d_x;
+        a.idx = S.d_idx;
+        a.w = S.d_w;
+        a.out = S.d_out;
+        a.order_by_id = order_by_id;
+        a.prefetch_down = 1;
+        if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
+        CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
+    }
     CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "ysum D2H");
     CK(cudaStreamSynchronize(S.stream), "expert loop");
+    if (read_device_errors(1)) {
+        rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
+        goto out;
+    }
     memcpy(ysum, S.h_out, xb);
 out:
     pthread_mutex_unlock(&g_mu);
@@ -817,6 +863,106 @@ int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x, float *d_o
     a.sh_t0 = sh_t0;
     a.sh_t1 = sh_t1;
     CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "layer kernels");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- batched (prefill) experts on the tensor cores -------------------------- */
+
+static size_t al256z(size_t n) { return (n + 255) & ~(size_t)255; }
+
+/* Carves the prefill workspace for T tokens x K experts (grown on demand). */
+static int pf_args(const wc_layer *L, int T, int K, wc_pf_args *a)
+{
+    const size_t np = (size_t)T * K, lat = L->kb.lat, inter = L->kb.inter;
+    const size_t nt = wc_pf_max_tiles(T, K, L->kb.n_experts);
+    size_t sz[13], need = 0;
+    sz[0] = np * 4;                         /* pairs            */
+    sz[1] = sz[2] = sz[3] = nt * 4;         /* tile_e, _s, _n   */
+    sz[4] = 4;                              /* ntiles           */
+    sz[5] = sz[6] = (size_t)T * lat * 2;    /* xh, xl           */
+    sz[7] = (size_t)T * 4;                  /* xinv             */
+    sz[8] = np * 2 * inter * 4;             /* gu               */
+    sz[9] = sz[10] = np * inter * 2;        /* hh, hl           */
+    sz[11] = np * 4;                        /* hinv             */
+    sz[12] = np * lat * 4;                  /* y                */
+    for (int i = 0; i < 13; i++) need += al256z(sz[i]);
+    if (need > S.pf_bytes) {
+        cudaFree(S.d_pf);
+        S.d_pf = NULL;
+        S.pf_bytes = 0;
+        const cudaError_t e = cudaMalloc(&S.d_pf, need);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill workspace");
+        S.pf_bytes = need;
+    }
+    char *p = (char *)S.d_pf;
+    void *ptr[13];
+    for (int i = 0; i < 13; i++) { ptr[i] = p; p += al256z(sz[i]); }
+    memset(a, 0, sizeof *a);
+    a->bank = L->kb;
+    a->books = S.d_books;
+    a->T = T;
+    a->K = K;
+    a->pairs = (int *)ptr[0];
+    a->tile_e = (int *)ptr[1]; a->tile_s = (int *)ptr[2]; a->tile_n = (int *)ptr[3];
+    a->ntiles = (int *)ptr[4];
+    a->xh = (uint16_t *)ptr[5]; a->xl = (uint16_t *)ptr[6]; a->xinv = (float *)ptr[7];
+    a->gu = (float *)ptr[8];
+    a->hh = (uint16_t *)ptr[9]; a->hl = (uint16_t *)ptr[10]; a->hinv = (float *)ptr[11];
+    a->y = (float *)ptr[12];
+    a->err = (unsigned int *)S.d_ws + 192;
+    for (int k = 0; k < 3; k++) {
+        float bound = 0.0f;
+        for (int st = 0; st < 3; st++) bound += S.book_absmax[L->kb.cb_base + 3 * k + st];
+        int ex = 0;
+        frexpf(bound > 0.0f ? bound : 1.0f, &ex);
+        ex = 14 - ex;                                  /* |w * scale| < 2^14 */
+        ex = ex > 40 ? 40 : (ex < -40 ? -40 : ex);
+        a->wscale[k] = ldexpf(1.0f, ex);
+    }
+    return 0;
+}
+
+/* Whether the tensor-core path takes this call: its shape bounds, fp16-exact
+ * codebooks, and enough pairs per expert for dense tiles to beat lookups. */
+static int pf_wanted(const wc_layer *L, int T, int K)
+{
+    return S.books_f16 && wc_pf_supported(&L->kb, T, K) == 0 &&
+           (long)T * K >= 2L * L->kb.n_experts && getenv_flag("WASTE_CUDA_PREFILL_TC", 1);
+}
+
+int waste_cuda_moe_prefill_dev(int layer, int T, int K, const int *d_route, const float *d_rw,
+                               const float *d_x, float *d_out, void *stream)
+{
+    int rc = 0;
+    wc_layer *L = NULL;
+    wc_pf_args a;
+    if (T <= 0 || K <= 0 || !d_route || !d_rw || !d_x || !d_out)
+        return fail(WASTE_CUDA_E_ARG, "moe_prefill: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (layer < 0 || layer >= WC_MAX_LAYERS || !S.layer[layer].loaded) {
+        rc = fail(WASTE_CUDA_E_NOBANK, "layer %d has no bank in HBM", layer);
+        goto out;
+    }
+    L = &S.layer[layer];
+    if (L->n_present != L->kb.n_experts) {
+        rc = fail(WASTE_CUDA_E_ARG, "layer %d: not every record of the bank is loaded", layer);
+        goto out;
+    }
+    if (!S.books_f16 || wc_pf_supported(&L->kb, T, K)) {
+        rc = fail(WASTE_CUDA_E_ARG, "layer %d: outside the tensor-core path's bounds (3 stages, "
+                  "rows multiples of 128, T*K <= %d, K <= 64, fp16-exact codebooks)", layer,
+                  WC_PF_MAX_PAIRS);
+        goto out;
+    }
+    if ((rc = ensure_ws(1, K, 1, L->kb.lat, L->kb.inter, 0, L->kb.stages))) goto out;
+    if ((rc = pf_args(L, T, K, &a))) goto out;
+    a.route = d_route;
+    a.rw = d_rw;
+    a.x = d_x;
+    a.out = d_out;
+    CK((cudaError_t)wc_pf_launch(&a, stream ? stream : (void *)S.stream), "prefill kernels");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;

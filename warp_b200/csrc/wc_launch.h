@@ -36,9 +36,11 @@ typedef struct {
     unsigned int *err;         /* sticky device error bits (WC_ERR_*)         */
 } wc_moe_ws;
 
-/* Device error bits: a bounded wait that ran out. */
+/* Device error bits: a bounded wait that ran out, or a route naming an
+ * expert the bank does not hold (skipped). */
 #define WC_ERR_ROUTE_WAIT 1u
 #define WC_ERR_TMA_WAIT   2u
+#define WC_ERR_BAD_EXPERT 4u
 
 typedef struct {
     wc_bank bank;
@@ -110,8 +112,37 @@ int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *scale,
                       int M, int N, const float *books, int cb_base, int stages,
                       void *stream);
 
+/* Batched (prefill) expert path on the tensor cores (prefill_tc.cu): T
+ * tokens, K routed experts each, route/rw [T][K], x/out [T][lat]; the
+ * workspace arrays are sized by the host (wc_pf_max_tiles). */
+#define WC_PF_MAX_PAIRS 65536
+typedef struct {
+    wc_bank bank;
+    const float *books;
+    int T, K;
+    const int *route;
+    const float *rw;
+    const float *x;
+    float *out;
+    float wscale[3];          /* power-of-two pre-scales of gate, up, down weights */
+    int *pairs;               /* [T*K] pair ids (t*K + j) grouped by expert      */
+    int *tile_e, *tile_s, *tile_n, *ntiles;
+    uint16_t *xh, *xl;        /* [T][lat] fp16 halves of x * 1/xinv              */
+    float *xinv;              /* [T]                                             */
+    float *gu;                /* [pairs][2][inter] gate, up (list order)         */
+    uint16_t *hh, *hl;        /* [pairs][inter] fp16 halves of h * 1/hinv        */
+    float *hinv;              /* [pairs]                                         */
+    float *y;                 /* [T*K][lat] per pair, unweighted                 */
+    unsigned int *err;
+} wc_pf_args;
+
+int    wc_pf_supported(const wc_bank *b, int T, int K);
+size_t wc_pf_max_tiles(int T, int K, int n_experts);
+int    wc_pf_launch(const wc_pf_args *a, void *stream);
+
 /* Kernels launched by this library since load. */
 uint64_t wc_launches(void);
+void     wc_count_launches(int n);
 
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
 enum { WC_PH_ROUTER, WC_PH_ROUTE, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
