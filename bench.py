@@ -451,6 +451,59 @@ def run_warp(args):
               "gather_kernel_GBps": G * synth.index_bytes(M, N, 3) / (mv_tiles_avg / 1e3) / 1e9,
               "bytes_per_launch": mv_bytes}
 
+    # ---- config 3: prefill, 512 tokens with Zipf(1.1) routes, one layer (layer
+    # 1's bank), on the tensor cores; the lookup path (8 host-slot chunks of 64
+    # tokens, copies included) timed beside it
+    prefill = None
+    if not ep_mode:
+        PT = 512
+        route = synth.zipf_routes(SEED + 9, PT, EXPERTS, TOPK).astype(np.int32)
+        rw = np.random.default_rng(SEED + 10).uniform(0.05, 0.6, size=route.shape).astype(np.float32)
+        px = synth.activations(SEED + 11, HIDDEN, T=PT)
+        d_r, d_rw = torch.from_numpy(route).to(dev), torch.from_numpy(rw).to(dev)
+        d_px = torch.from_numpy(px).to(dev)
+        d_po = torch.empty((PT, HIDDEN), dtype=torch.float32, device=dev)
+        wb.codebooks_load_f16(base.books_raw)
+        call = lambda: wb.moe_prefill_dev(1, PT, TOPK, d_r.data_ptr(), d_rw.data_ptr(),
+                                          d_px.data_ptr(), d_po.data_ptr(), s.cuda_stream)
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        p_iters = 10
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(2e7))
+            p0.record(s)
+            for _ in range(p_iters):
+                call()
+            p1.record(s)
+        torch.cuda.synchronize()
+        p_ms = p0.elapsed_time(p1) / p_iters
+        flops = 2.0 * PT * TOPK * 3 * INTER * HIDDEN
+        touched = int(np.unique(route).size)
+        os.environ["WASTE_CUDA_PREFILL_TC"] = "0"
+        wb.moe_chunk_experts(1, route[:64], rw[:64], px[:64], HIDDEN, INTER)
+        t0 = time.perf_counter()
+        for c in range(PT // 64):
+            wb.moe_chunk_experts(1, route[64 * c:64 * c + 64], rw[64 * c:64 * c + 64],
+                                 px[64 * c:64 * c + 64], HIDDEN, INTER)
+        lookup_ms = (time.perf_counter() - t0) * 1e3
+        del os.environ["WASTE_CUDA_PREFILL_TC"]
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+            os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+        tpeak = float(pk.get("bf16_tflops", 1590.0))
+        prefill = {"workload": "kimi_linear_moe_prefill_512tok_zipf1.1", "tokens": PT,
+                   "experts_touched": touched, "ms_per_layer": p_ms,
+                   "tok_per_s": PT / (p_ms / 1e3),
+                   "algorithmic_tflops": flops / (p_ms / 1e3) / 1e12,
+                   "tensor_peak_tflops": tpeak,
+                   "frac_of_tensor_peak": flops / (p_ms / 1e3) / 1e12 / tpeak,
+                   "mma_tflops_issued": 3 * flops / (p_ms / 1e3) / 1e12,
+                   "weight_bytes": touched * synth.record_bytes(INTER, HIDDEN, 3),
+                   "weight_GBps": touched * synth.record_bytes(INTER, HIDDEN, 3) / (p_ms / 1e3) / 1e9,
+                   "lookup_path_ms_per_layer": lookup_ms,
+                   "speedup_vs_lookup": lookup_ms / p_ms}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_budget)
@@ -482,6 +535,7 @@ def run_warp(args):
                          "layer_frac": layer_bytes() / (ms_step / nL / 1e3) / 1e9 / peak},
             "kernels": kernels,
             "matvec": matvec,
+            "prefill": prefill,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

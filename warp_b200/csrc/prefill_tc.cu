@@ -50,14 +50,40 @@ constexpr int kPfAcc = 4;             /* TMEM accumulators, round robin by step 
 constexpr int kPfThreads = 128;       /* one thread per weight row                */
 constexpr int kPfMaxE = 1024;
 
-/* shared memory of a GEMM tile: two stages of {A hi, A lo, B hi, B lo},
- * each [8 chunks][128 rows][16 bytes] (the K-major no-swizzle core-matrix
- * layout), then the fp16 codebooks of the kind and the staged indices */
+/* shared memory of a GEMM tile. Operands use the K-major no-swizzle
+ * core-matrix layout, [8 chunks][128 rows][16 bytes] per 64-wide K step:
+ *   A  (dequantised weights, hi and lo): 2 stages            64 KB
+ *   B  (token operand, hi and lo):       ring of 4 steps    128 KB
+ *   indices of the step's weight rows:   ring of 4 steps     12 KB
+ *   the kind's codebooks in fp16                             12 KB
+ * The B and index rings are filled by cp.async two steps ahead, so their
+ * global-memory latency hides behind the current step's dequantisation
+ * and MMAs. */
 constexpr int kPfOpBytes = 8 * 128 * 16;                      /* 16 KB */
-constexpr int kPfStageBytes = 4 * kPfOpBytes;                  /* 64 KB */
-constexpr int kPfBookBytes = 3 * 256 * 8 * 2;                  /* 12 KB */
+constexpr int kPfAOff = 0;
+constexpr int kPfBOff = kPfAOff + 2 * 2 * kPfOpBytes;
 constexpr int kPfIdxBytes = 2 * 8 * 192;                       /* 3 KB  */
-constexpr int kPfSmem = 2 * kPfStageBytes + kPfBookBytes + 2 * kPfIdxBytes;
+constexpr int kPfIdxOff = kPfBOff + 4 * 2 * kPfOpBytes;
+constexpr int kPfBookOff = kPfIdxOff + 4 * kPfIdxBytes;
+constexpr int kPfBookBytes = 3 * 256 * 8 * 2;                  /* 12 KB */
+constexpr int kPfSmem = kPfBookOff + kPfBookBytes;              /* 216 KB */
+static_assert(kPfSmem + 4096 <= 227 * 1024, "prefill tile exceeds shared memory");
+
+/* 16-byte asynchronous copy global -> shared (zero-filled when !valid) */
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ uint64_t sm_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
 {
@@ -233,9 +259,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
                              (kind == 0 ? 0 : (kind == 1 ? bk.inter : 2 * bk.inter));
     const float wsc = a.wscale[kind];
 
-    unsigned char *stage0 = smraw;
-    uint16_t *cb = reinterpret_cast<uint16_t *>(smraw + 2 * kPfStageBytes);
-    uint8_t *idxs = smraw + 2 * kPfStageBytes + kPfBookBytes;
+    uint16_t *cb = reinterpret_cast<uint16_t *>(smraw + kPfBookOff);
 
     /* TMEM: four accumulators of kPfTok fp32 columns */
     if (warp == 0) {
@@ -266,51 +290,54 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
     const uint32_t tmem = tmem_base;
     const uint32_t idesc = mma_idesc();
     const int rb0 = m0 / kBlock;
-    bool ok = true;
 
-    for (int ks = 0; ks < nks && ok; ks++) {
-        const int st = ks & 1;
-        unsigned char *sa_hi = stage0 + st * kPfStageBytes;
-        unsigned char *sa_lo = sa_hi + kPfOpBytes;
-        unsigned char *sb_hi = sa_lo + kPfOpBytes;
-        unsigned char *sb_lo = sb_hi + kPfOpBytes;
-        uint8_t *six = idxs + st * kPfIdxBytes;
-        if (ks >= 2) ok = mbar_wait(&bars[st], ((ks - 2) >> 1) & 1);   /* stage free */
-        if (!ok) break;
-        /* indices of the two row blocks, 8 positions: 2 x 1536 contiguous bytes */
-        const int v0 = ks * (kPfKs / kVecDim);
-        for (int c = tid; c < 2 * 96; c += kPfThreads) {
-            const int r = c / 96, q = c % 96;
-            const uint4 *src = reinterpret_cast<const uint4 *>(
-                mat + ((size_t)(rb0 + r) * nv + v0) * kBlock * 3);
-            reinterpret_cast<uint4 *>(six + r * 1536)[q] = __ldg(src + q);
-        }
-        /* B: the tile's operand rows (x of the pair's token, or the pair's h) */
-        {
-            const int j = tid;                                   /* one pair per thread */
-            uint4 h[8], l[8];
-            if (j < n) {
-                const size_t row = DOWN ? (size_t)(s0 + j) : (size_t)(s_pair[j] / a.K);
-                const uint16_t *ph = (DOWN ? a.hh : a.xh) + row * Kin + (size_t)ks * kPfKs;
-                const uint16_t *pl = (DOWN ? a.hl : a.xl) + row * Kin + (size_t)ks * kPfKs;
-#pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    h[c] = __ldg(reinterpret_cast<const uint4 *>(ph) + c);
-                    l[c] = __ldg(reinterpret_cast<const uint4 *>(pl) + c);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; c++) h[c] = l[c] = make_uint4(0, 0, 0, 0);
+    /* this thread's B row (pair j = tid): x of the pair's token, or its h */
+    const int jb = tid;
+    const bool jvalid = jb < n;
+    const size_t brow = !jvalid ? 0 : (DOWN ? (size_t)(s0 + jb) : (size_t)(s_pair[jb] / a.K));
+    const uint16_t *bh_src = (DOWN ? a.hh : a.xh) + brow * Kin;
+    const uint16_t *bl_src = (DOWN ? a.hl : a.xl) + brow * Kin;
+
+    /* step k's indices and B rows into ring slot k & 3 (one group per step,
+     * empty past the end so the group count stays uniform) */
+    auto issue = [&](int k) {
+        if (k < nks) {
+            const int slot = k & 3;
+            uint8_t *six = smraw + kPfIdxOff + slot * kPfIdxBytes;
+            const int v0 = k * (kPfKs / kVecDim);
+            for (int c = tid; c < 2 * 96; c += kPfThreads) {
+                const int r = c / 96, q = c % 96;
+                cp_async16(six + r * 1536 + q * 16,
+                           mat + ((size_t)(rb0 + r) * nv + v0) * kBlock * 3 + (size_t)q * 16, true);
             }
+            unsigned char *bh = smraw + kPfBOff + slot * 2 * kPfOpBytes, *bl = bh + kPfOpBytes;
 #pragma unroll
             for (int c = 0; c < 8; c++) {
-                const int o = c * (kPfTok * 16) + (j / 8) * 128 + (j % 8) * 16;
-                *reinterpret_cast<uint4 *>(sb_hi + o) = h[c];
-                *reinterpret_cast<uint4 *>(sb_lo + o) = l[c];
+                const int o = c * (kPfTok * 16) + (jb / 8) * 128 + (jb % 8) * 16;
+                cp_async16(bh + o, bh_src + (size_t)k * kPfKs + c * 8, jvalid);
+                cp_async16(bl + o, bl_src + (size_t)k * kPfKs + c * 8, jvalid);
             }
         }
-        __syncthreads();                                          /* indices staged */
-        /* A: thread r dequantises row m0 + r at the 8 positions */
+        cp_async_commit();
+    };
+
+    bool ok = true;
+    issue(0);
+    issue(1);
+    for (int ks = 0; ks < nks; ks++) {
+        const int st = ks & 1, slot = ks & 3;
+        /* A stage st and ring slot (ks+2)&3 were read by step ks-2's MMAs */
+        if (ks >= 2) ok = mbar_wait(&bars[st], ((ks - 2) >> 1) & 1);
+        if (!ok) break;
+        issue(ks + 2);
+        cp_async_wait<2>();                              /* step ks's group landed */
+        __syncthreads();
+        unsigned char *sa_hi = smraw + kPfAOff + st * 2 * kPfOpBytes;
+        unsigned char *sa_lo = sa_hi + kPfOpBytes;
+        unsigned char *sb_hi = smraw + kPfBOff + slot * 2 * kPfOpBytes;
+        unsigned char *sb_lo = sb_hi + kPfOpBytes;
+        const uint8_t *six = smraw + kPfIdxOff + slot * kPfIdxBytes;
+        /* A: thread r dequantises row m0 + r at the step's 8 positions */
         {
             const int r = tid, rbl = r / kBlock, rr = r % kBlock;
 #pragma unroll 2
@@ -356,6 +383,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
             mma_commit(&bars[st]);
         }
     }
+    cp_async_wait<0>();                                  /* no copy outlives the tile */
     /* the last step's commit covers every MMA issued before it */
     if (ok) ok = mbar_wait(&bars[(nks - 1) & 1], ((nks - 1) >> 1) & 1);
     if (!ok) {

@@ -758,10 +758,11 @@ __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const in
  * parallelism a rank's bank holds only its own range of ids; the others'
  * records are not in this GPU's memory, so no address is formed for them:
  * their tiles skip, and their contributions come from the owning rank. */
-__device__ __forceinline__ bool expert_here(const wc_bank &bk, const int *idx, int K, int t, int j)
+__device__ __forceinline__ bool expert_here(const wc_moe_args &a, const int *idx, int K, int t, int j)
 {
-    const int e = __ldcg(idx + (size_t)t * K + j) - bk.first;
-    return e >= 0 && e < bk.n_experts;
+    if (!a.partial_bank) return true;        /* every routed expert is held here */
+    const int e = __ldcg(idx + (size_t)t * K + j) - a.bank.first;
+    return e >= 0 && e < a.bank.n_experts;
 }
 
 /* ---- 2. gate/up ------------------------------------------------------------
@@ -822,7 +823,7 @@ gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
      * experts held by another rank are neither staged nor gathered */
     uint32_t here = 0;
     for (int mm = 0; mm < nm; mm++)
-        if (expert_here(bk, idx, a.K, t, j0 + mm)) here |= 1u << mm;
+        if (expert_here(a, idx, a.K, t, j0 + mm)) here |= 1u << mm;
     const uint32_t psz = kBlock * ST;
     const int h = (nvs + 1) / 2;
     const int ncopy = nm * g.nrb;
@@ -964,7 +965,7 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, int sh_rows_pw,
     int b = blockIdx.x;
     const int slice = b % g.ns; b /= g.ns;
     const int j = b % a.K; const int t = b / a.K;
-    if (!expert_here(bk, idx, a.K, t, j)) return;       /* another rank's expert */
+    if (!expert_here(a, idx, a.K, t, j)) return;        /* another rank's expert */
     const int v0 = slice * g.Vs, nvs = min(g.Vs, g.nv - v0);
     const uint32_t psz = kBlock * ST;
     const uint8_t *rec = expert_rec(bk, idx, a.K, t, j);
@@ -1069,7 +1070,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     for (int n = 0; n < kJ; n++) {
         const int j = jl + 8 * n;
         scl[n] = 0.0f;
-        if (j < K && ok && expert_here(bk, it, K, 0, j)) {
+        if (j < K && ok && expert_here(a, it, K, 0, j)) {
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(
                 bk.base + (size_t)(__ldcg(it + j) - bk.first) * bk.rec_bytes + bk.scale_off) +
                 2 * bk.inter;
@@ -1098,7 +1099,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         const int j = jl + 8 * n;
         if (j >= K) break;
         float s = 0.0f;
-        if (ok && expert_here(bk, it, K, 0, j)) {
+        if (ok && expert_here(a, it, K, 0, j)) {
             const float *p = a.ws.p_d + (((size_t)t * K + j) * g.ns) * bk.lat + i;
             float v[kMaxSlicesReg];
 #pragma unroll
@@ -1123,7 +1124,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
                 }
                 if (jj >= 0) last = __ldcg(it + jj);
             }
-            if (jj >= 0 && !expert_here(bk, it, K, 0, jj)) continue;   /* held elsewhere */
+            if (jj >= 0 && !expert_here(a, it, K, 0, jj)) continue;   /* held elsewhere */
             order[nn++] = jj;
         }
         for (; nn < K; nn++) order[nn] = -1;

@@ -696,6 +696,7 @@ static void fill_args(wc_moe_args *a, const wc_layer *L, int T, int K, int E, in
     a->si = si;
     a->sh_t0 = 0;
     a->sh_t1 = T;
+    a->partial_bank = L->kb.first != 0 || L->kb.n_experts != L->n_total;
     wc_moe_ws_carve(&a->ws, S.d_ws, T, K, E, L->kb.lat, L->kb.inter, si, L->kb.stages);
 }
 

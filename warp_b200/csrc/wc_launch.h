@@ -60,6 +60,8 @@ typedef struct {
     int si;                   /* shared intermediate; 0 = no shared expert   */
     int sh_t0, sh_t1;         /* tokens [sh_t0, sh_t1) get the shared expert
                                  (all of them, unless expert parallel)       */
+    int partial_bank;         /* 1: the bank holds only some experts; routes
+                                 to the others are skipped, not computed      */
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
