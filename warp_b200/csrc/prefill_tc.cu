@@ -47,7 +47,7 @@ constexpr int kPfRows = 128;          /* MMA M: weight rows per tile            
 constexpr int kPfTok = 128;           /* MMA N: routed pairs per tile             */
 constexpr int kPfKs = 64;             /* K elements per step (8 vector positions) */
 constexpr int kPfAcc = 4;             /* TMEM accumulators, round robin by step   */
-constexpr int kPfThreads = 128;       /* one thread per weight row                */
+constexpr int kPfThreads = 256;       /* two threads per weight row (4 positions each) */
 constexpr int kPfMaxE = 1024;
 
 /* shared memory of a GEMM tile. Operands use the K-major no-swizzle
@@ -125,6 +125,14 @@ __device__ __forceinline__ void split_f16(float v, uint16_t &hi, uint16_t &lo)
     const __half h = __float2half_rn(v);
     hi = __half_as_ushort(h);
     lo = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+}
+
+/* the same for two values at once, with packed conversions */
+__device__ __forceinline__ void split_f16x2(float a, float b, __half2 &hi, __half2 &lo)
+{
+    hi = __floats2half2_rn(a, b);
+    const float2 back = __half22float2(hi);
+    lo = __floats2half2_rn(a - back.x, b - back.y);
 }
 
 /* 2^(14 - e) for the largest |value| m = f * 2^e (0.5 <= f < 1): scaled
@@ -291,8 +299,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
     const uint32_t idesc = mma_idesc();
     const int rb0 = m0 / kBlock;
 
-    /* this thread's B row (pair j = tid): x of the pair's token, or its h */
-    const int jb = tid;
+    /* this thread's B row (pair jb) and half of its 8 chunks: x of the
+     * pair's token, or its h */
+    const int jb = tid % kPfTok, chalf = tid / kPfTok;
     const bool jvalid = jb < n;
     const size_t brow = !jvalid ? 0 : (DOWN ? (size_t)(s0 + jb) : (size_t)(s_pair[jb] / a.K));
     const uint16_t *bh_src = (DOWN ? a.hh : a.xh) + brow * Kin;
@@ -312,7 +321,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
             }
             unsigned char *bh = smraw + kPfBOff + slot * 2 * kPfOpBytes, *bl = bh + kPfOpBytes;
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
+            for (int cc = 0; cc < 4; cc++) {
+                const int c = chalf * 4 + cc;
                 const int o = c * (kPfTok * 16) + (jb / 8) * 128 + (jb % 8) * 16;
                 cp_async16(bh + o, bh_src + (size_t)k * kPfKs + c * 8, jvalid);
                 cp_async16(bl + o, bl_src + (size_t)k * kPfKs + c * 8, jvalid);
@@ -337,11 +347,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
         unsigned char *sb_hi = smraw + kPfBOff + slot * 2 * kPfOpBytes;
         unsigned char *sb_lo = sb_hi + kPfOpBytes;
         const uint8_t *six = smraw + kPfIdxOff + slot * kPfIdxBytes;
-        /* A: thread r dequantises row m0 + r at the step's 8 positions */
+        /* A: row m0 + r, positions 4*vh .. 4*vh+3 of the step's 8 */
         {
-            const int r = tid, rbl = r / kBlock, rr = r % kBlock;
+            const int r = tid % kPfRows, vh = tid / kPfRows, rbl = r / kBlock, rr = r % kBlock;
 #pragma unroll 2
-            for (int v = 0; v < 8; v++) {
+            for (int v = 4 * vh; v < 4 * vh + 4; v++) {
                 const uint8_t *ib = six + rbl * 1536 + v * 192 + rr * 3;
                 const uint4 c0 = *reinterpret_cast<const uint4 *>(cb + ((0 * 256 + ib[0]) << 3));
                 const uint4 c1 = *reinterpret_cast<const uint4 *>(cb + ((1 * 256 + ib[1]) << 3));
@@ -349,15 +359,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
                 const __half2 *h0 = reinterpret_cast<const __half2 *>(&c0);
                 const __half2 *h1 = reinterpret_cast<const __half2 *>(&c1);
                 const __half2 *h2 = reinterpret_cast<const __half2 *>(&c2);
-                __align__(16) uint16_t hi[8], lo[8];
+                __align__(16) __half2 hi[4], lo[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const float2 f0 = __half22float2(h0[q]), f1 = __half22float2(h1[q]),
                                  f2 = __half22float2(h2[q]);
                     const float wa = ((0.0f + f0.x) + f1.x) + f2.x;
                     const float wb = ((0.0f + f0.y) + f1.y) + f2.y;
-                    split_f16(wa * wsc, hi[2 * q], lo[2 * q]);
-                    split_f16(wb * wsc, hi[2 * q + 1], lo[2 * q + 1]);
+                    split_f16x2(wa * wsc, wb * wsc, hi[q], lo[q]);
                 }
                 const int o = v * (kPfRows * 16) + (r / 8) * 128 + (r % 8) * 16;
                 *reinterpret_cast<uint4 *>(sa_hi + o) = *reinterpret_cast<const uint4 *>(hi);
@@ -393,16 +402,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm(wc_pf_args a)
     }
     asm volatile("tcgen05.fence::after_thread_sync;");
     if (ok) {
-        const int r = warp * 32 + lane;                  /* TMEM lane = weight row */
+        /* warp w reads TMEM lanes 32*(w%4).. (its lane quarter) = weight rows,
+         * columns (pairs) [64*(w/4), 64*(w/4) + 64) */
+        const int quarter = warp % 4, chw = warp / 4;
+        const int r = quarter * 32 + lane;
         const float rs = f16_keep(rscale[m0 + r]) / wsc;
-        for (int c0 = 0; c0 < n; c0 += 16) {
+        const int cend = min(n, chw * (kPfTok / 2) + kPfTok / 2);
+        for (int c0 = chw * (kPfTok / 2); c0 < cend; c0 += 16) {
             float sum[16];
 #pragma unroll
             for (int j = 0; j < 16; j++) sum[j] = 0.0f;
 #pragma unroll
             for (int q = 0; q < kPfAcc; q++) {
                 uint32_t v[16];
-                const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(q * kPfTok + c0);
+                const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * kPfTok + c0);
                 asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
                              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]),
