@@ -657,6 +657,10 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
         wbytes = (uint32_t)nr * ng * 128;
     }
     uint16_t *sst = reinterpret_cast<uint16_t *>(wst + (size_t)(kRouterBlock / 32) * ng * 128);
+    /* The weight rows depend on nothing earlier in the stream: their copies
+     * are issued before the grid-dependency wait, so they overlap the end
+     * of the previous kernel. x, and every write this kernel makes, come
+     * after it. */
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         mbar_fence_init();
@@ -664,11 +668,12 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
         const uint32_t sbytes = is_router ? 0u : (uint32_t)nr * ng * 2;
         tx += sbytes;
         mbar_expect_tx(bar, tx);
-        bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
         if (wbytes) bulk_g2s(wst, wsrc, wbytes, bar);
         if (sbytes)
             bulk_g2s(sst, (kind ? a.shu_s : a.shg_s) + (size_t)o0 * ng, sbytes, bar);
     }
+    pdl_wait();
+    if (threadIdx.x == 0) bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
     __syncthreads();
     const bool ok = mbar_wait(bar, 0);
     if (!ok && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
@@ -1090,6 +1095,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         }
     }
     pdl_wait();
+    pdl_trigger();         /* down is done: the next layer's router may prefetch its rows */
     if (threadIdx.x < K) wsm[threadIdx.x] = __ldcg(w + (size_t)t * K + threadIdx.x);
     const bool sh_here = a.si > 0 && t >= a.sh_t0 && t < a.sh_t1;
     const float shv = (sh_here && jl == 0 && ok) ? __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i)
@@ -1246,12 +1252,15 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         cudaFuncSetAttribute(router_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         cudaFuncSetAttribute(router_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         const dim3 rgrid(rg.rblocks + rg.sblocks, a->T);
+        /* programmatic launch: the router's weight copies overlap whatever
+         * kernel precedes it in the stream (the previous layer's combine) */
+        const bool rpdl = !P.on;
         if (a->E <= 256)
-            e = launch(router_kernel<8>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
+            e = launch(router_kernel<8>, rgrid, dim3(kRouterBlock), rsm, s, rpdl, *a, rg);
         else if (a->E <= 512)
-            e = launch(router_kernel<16>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
+            e = launch(router_kernel<16>, rgrid, dim3(kRouterBlock), rsm, s, rpdl, *a, rg);
         else
-            e = launch(router_kernel<32>, rgrid, dim3(kRouterBlock), rsm, s, false, *a, rg);
+            e = launch(router_kernel<32>, rgrid, dim3(kRouterBlock), rsm, s, rpdl, *a, rg);
         prof_end(pe, s);
         g_launches += 1;
         idx = a->idx_out;
