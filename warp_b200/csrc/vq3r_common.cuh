@@ -8,6 +8,7 @@
  * `stages` 16-byte words — one LDG.128 per stage.
  */
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -280,6 +281,19 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+/* Tiled TMA load of a 3-D box at {x, y, z} (x in elements of the map,
+ * x * element size a multiple of 16 bytes) into shared memory (128-byte
+ * aligned), signalling `bar` with the box's bytes. The map is a kernel
+ * parameter (__grid_constant__). No multicast. */
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
+                   "r"(smem_u32(bar)) : "memory");
 }
 
 /* Bounded wait for phase `parity` of the barrier: false after kMbarLimit

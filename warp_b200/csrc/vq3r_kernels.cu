@@ -133,7 +133,9 @@ struct TileSmem {
         bars = reinterpret_cast<uint64_t *>(raw);
         xs = reinterpret_cast<float *>(raw + 16);
         lut = xs + ((g.Vs * kVecDim + 3) & ~3);
-        stage = reinterpret_cast<uint8_t *>(lut + g.region);
+        /* TMA tensor copies land on 128-byte boundaries */
+        const uintptr_t st = reinterpret_cast<uintptr_t>(lut + g.region);
+        stage = reinterpret_cast<uint8_t *>((st + 127) & ~(uintptr_t)127);
     }
 };
 
@@ -175,7 +177,7 @@ TileGeom make_geom(int M, int N, int nmat, int Vs, int stages, int target_thread
 TileGeom with_stage(TileGeom g, int stages)
 {
     g.stage = (size_t)g.EG * g.nrb * g.Vs * kBlock * stages;
-    g.smem += g.stage;
+    g.smem += g.stage + 128;       /* + the stage's 128-byte alignment */
     return g;
 }
 
@@ -782,7 +784,7 @@ constexpr int kGuBooks = 2;            /* codebook rows per thread (768/512) */
 
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
-gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
+gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ int go;
@@ -833,12 +835,32 @@ gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
     const int h = (nvs + 1) / 2;
     const int ncopy = nm * g.nrb;
     const int nhere = __popc(here) * g.nrb;
+    /* with the layer's tensor maps: two boxes per expert (the halves of its
+     * row blocks), each half on its own barrier */
+    const bool use_map = bk.tmap_ok;
     if (threadIdx.x == 0) {
-        if (nhere) mbar_expect_tx(&sm.bars[0], (uint32_t)nhere * h * psz);
-        if (nhere && nvs > h) mbar_expect_tx(&sm.bars[1], (uint32_t)nhere * (nvs - h) * psz);
+        if (use_map) {
+            const uint32_t box = (uint32_t)(g.nrb / 2) * nvs * psz;
+            if (nhere) {
+                mbar_expect_tx(&sm.bars[0], (uint32_t)__popc(here) * box);
+                mbar_expect_tx(&sm.bars[1], (uint32_t)__popc(here) * box);
+            }
+        } else {
+            if (nhere) mbar_expect_tx(&sm.bars[0], (uint32_t)nhere * h * psz);
+            if (nhere && nvs > h) mbar_expect_tx(&sm.bars[1], (uint32_t)nhere * (nvs - h) * psz);
+        }
     }
     __syncthreads();
-    for (int c = threadIdx.x; c < ncopy; c += blockDim.x) {
+    if (use_map && (int)threadIdx.x < nm && ((here >> threadIdx.x) & 1u)) {
+        /* thread m issues expert m's two boxes: the route reads run in parallel */
+        const int mm = threadIdx.x;
+        const uint32_t box = (uint32_t)(g.nrb / 2) * nvs * psz;
+        const int e = __ldcg(idx + (size_t)t * a.K + j0 + mm) - bk.first;
+        uint8_t *dst = sm.stage + (size_t)mm * g.nrb * nvs * psz;
+        tma_load_3d(dst, &bk.tmap[kind], v0 * 24, 0, e, &sm.bars[0]);
+        tma_load_3d(dst + box, &bk.tmap[kind], v0 * 24, g.nrb / 2, e, &sm.bars[1]);
+    }
+    for (int c = threadIdx.x; c < ncopy && !use_map; c += blockDim.x) {
         const int m = c / g.nrb, rbl = c % g.nrb;
         if (!((here >> m) & 1u)) continue;
         const uint8_t *src = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off) +
@@ -872,8 +894,13 @@ gateup_kernel(wc_moe_args a, TileGeom g, const int *idx)
     TileThread<ST, GatherSmem<ST>> th(gs, 0, nm, sm.stage + (size_t)m * g.nrb * nvs * psz);
     th.active = th.active && ((here >> m) & 1u);
     th.G.first = th.vl0;
-    th.G.bar0 = &sm.bars[0];
-    th.G.bar1 = nvs > h ? &sm.bars[1] : nullptr;
+    if (use_map) {                   /* this thread's rows arrive with one box */
+        th.G.bar0 = th.rbl < g.nrb / 2 ? &sm.bars[0] : &sm.bars[1];
+        th.G.bar1 = nullptr;
+    } else {
+        th.G.bar0 = &sm.bars[0];
+        th.G.bar1 = nvs > h ? &sm.bars[1] : nullptr;
+    }
     th.G.split = h;
     __syncthreads();                 /* the table */
     float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
@@ -957,7 +984,8 @@ __device__ __forceinline__ void shared_down_block(const wc_moe_args &a, unsigned
 
 template <int ST>
 __global__ void __launch_bounds__(512, 1)
-down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, int sh_rows_pw, const int *idx)
+down_kernel(const __grid_constant__ wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles,
+            int sh_rows_pw, const int *idx)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
     const wc_bank &bk = a.bank;
@@ -978,9 +1006,12 @@ down_kernel(wc_moe_args a, TileGeom gu, TileGeom g, int d_tiles, int sh_rows_pw,
         mbar_init(&sm.bars[0], 1);
         mbar_fence_init();
         mbar_expect_tx(&sm.bars[0], (uint32_t)g.nrb * nvs * psz);
+        if (bk.tmap_ok)              /* the whole slice of the stream: one box */
+            tma_load_3d(sm.stage, &bk.tmap[2], v0 * 24, 0,
+                        __ldcg(idx + (size_t)t * a.K + j) - bk.first, &sm.bars[0]);
     }
     __syncthreads();
-    for (int rbl = threadIdx.x; rbl < g.nrb; rbl += blockDim.x)
+    for (int rbl = threadIdx.x; rbl < g.nrb && !bk.tmap_ok; rbl += blockDim.x)
         bulk_g2s(sm.stage + (size_t)rbl * nvs * psz,
                  rec + bk.down_off + ((size_t)rbl * g.nv + v0) * psz, nvs * psz, &sm.bars[0]);
     BookRows<ST, kDnBooks> books;
@@ -1149,8 +1180,8 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
     a.out[(size_t)t * bk.lat + i] = y;
 }
 
-constexpr int kVsGateUp = 4;
-constexpr int kVsDown = 8;
+constexpr int kVsGateUp = WC_VS_GATEUP;
+constexpr int kVsDown = WC_VS_DOWN;
 
 struct MoeGeom {
     TileGeom gu, d;

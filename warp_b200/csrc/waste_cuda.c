@@ -455,6 +455,63 @@ int waste_cuda_ep_range(int n_experts, int rank, int world, int *first, int *cou
     return 0;
 }
 
+/* cuTensorMapEncodeTiled, reached through the runtime (no -lcuda). */
+typedef CUresult (*wc_encode_tiled_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                       const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                       const cuuint32_t *, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                       CUtensorMapFloatOOBfill);
+
+static wc_encode_tiled_fn encode_tiled(void)
+{
+    static wc_encode_tiled_fn fn;
+    static int tried;
+    if (!tried) {
+        tried = 1;
+        void *p = NULL;
+        enum cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = (wc_encode_tiled_fn)p;
+    }
+    return fn;
+}
+
+/* The bank's index streams as 3-D tensors of 8-byte elements: {positions of
+ * a row block * 24, 64-row blocks, experts held}, strides {row block,
+ * record}. Box: one decode tile's positions by half the row blocks
+ * (gate/up) or all of them (down). Leaves tmap_ok = 0 when a shape does not
+ * fit (the kernels then copy row block by row block). */
+static void bank_tensor_maps(wc_bank *kb)
+{
+    kb->tmap_ok = 0;
+    wc_encode_tiled_fn enc = encode_tiled();
+    if (!enc) return;
+    const int nv_gu = kb->lat / 8, nrb_gu = (kb->inter + 63) / 64;
+    const int nv_d = kb->inter / 8, nrb_d = (kb->lat + 63) / 64;
+    if (nv_gu % WC_VS_GATEUP || nv_d % WC_VS_DOWN || nrb_gu % 2 || nrb_gu / 2 > 256 ||
+        nrb_d > 256 || WC_VS_DOWN * 24 > 256 || kb->stages != 3)
+        return;
+    const uint32_t off[3] = { kb->gate_off, kb->up_off, kb->down_off };
+    for (int k = 0; k < 3; k++) {
+        const int nv = k < 2 ? nv_gu : nv_d, nrb = k < 2 ? nrb_gu : nrb_d;
+        const cuuint64_t dims[3] = { (cuuint64_t)nv * 24, (cuuint64_t)nrb,
+                                     (cuuint64_t)kb->n_experts };
+        const cuuint64_t strides[2] = { (cuuint64_t)nv * 192, (cuuint64_t)kb->rec_bytes };
+        const cuuint32_t box[3] = { (cuuint32_t)(k < 2 ? WC_VS_GATEUP : WC_VS_DOWN) * 24,
+                                    (cuuint32_t)(k < 2 ? nrb / 2 : nrb), 1 };
+        const cuuint32_t estr[3] = { 1, 1, 1 };
+        void *base = (void *)(kb->base + off[k]);
+        if (((uintptr_t)base & 15) ||
+            enc(&kb->tmap[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, base, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+                CUDA_SUCCESS)
+            return;
+    }
+    kb->tmap_ok = 1;
+}
+
 /* HBM for records [first, first+count) of a layer of n_experts; the caller
  * holds g_mu and has checked the shape arguments. */
 static int reserve_locked(int layer, int n_experts, size_t rec_bytes, int first, int count,
@@ -567,6 +624,7 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
         L->kb.scale_off = h0->chan_corr_off;
         L->kb.cb_base = h0->codebook_id;
         L->have_hdr = 1;
+        bank_tensor_maps(&L->kb);
     }
     const int at = first - L->kb.first;
     CK(cudaMemcpy(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,

@@ -6,6 +6,7 @@
 #ifndef WC_LAUNCH_H
 #define WC_LAUNCH_H
 
+#include <cuda.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -13,9 +14,20 @@
 extern "C" {
 #endif
 
+/* Vector positions per gate/up and per down tile of the decode kernels. */
+#define WC_VS_GATEUP 4
+#define WC_VS_DOWN   8
+
 /* One layer's bank as the kernels see it: E records of rec_bytes each,
- * all with the same payload offsets (checked at load). */
+ * all with the same payload offsets (checked at load). tmap: TMA tensor
+ * maps of the gate, up and down index streams over the bank, 8-byte
+ * elements, dims {positions * 24, 64-row blocks, experts}; boxes of one
+ * tile's positions by half the row blocks (gate/up) or all of them (down).
+ * tmap_ok = 0 when the shapes do not fit the boxes (per-row-block copies
+ * are used instead). */
 typedef struct {
+    CUtensorMap tmap[3];
+    int tmap_ok;
     const uint8_t *base;
     size_t rec_bytes;
     uint32_t gate_off, up_off, down_off, scale_off;
