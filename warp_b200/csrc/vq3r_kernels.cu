@@ -75,6 +75,8 @@ void prof_end(int i, cudaStream_t s)
 }
 } /* namespace */
 
+extern "C" int wc_profiling(void) { return P.on; }
+
 extern "C" int wc_prof_enable(int on)
 {
     if (on && !P.created) {

@@ -62,6 +62,10 @@ typedef struct {
     int si;
     int8_t *d_shg, *d_shu, *d_shd;
     uint16_t *d_shg_s, *d_shu_s, *d_shd_s;
+    /* the host-buffer layer call as one CUDA graph (copies in, kernels,
+     * copies out), rebuilt when anything it points at may have moved */
+    cudaGraphExec_t gx;
+    unsigned gx_epoch;
 } wc_layer;
 
 static struct {
@@ -92,7 +96,16 @@ static struct {
     size_t tmp_bytes;
     /* fetch layer+1's router and shared expert into L2 during layer */
     int prefetch_next;
+    /* the host layer call's results in one block, so one copy brings them
+     * back: out [res_lat] | route [WC_MAX_TOPK] | weights [WC_MAX_TOPK] | err */
+    float *d_res, *h_res;
+    int res_lat;
 } S;
+
+/* Bumped by every call that allocates, frees or reloads what a cached
+ * layer graph points at (workspace, banks, trunks, codebooks, the expert
+ * split); a graph built under another epoch is rebuilt before use. */
+static unsigned g_epoch = 1;
 
 /* Expert parallelism: this process's rank among `world` processes (one GPU
  * each) that share every MoE layer, each holding a contiguous range of the
@@ -212,6 +225,7 @@ static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages
         if (S.d_ws) cudaFree(S.d_ws);
         S.d_ws = NULL;
         S.ws_floats = 0;
+        g_epoch++;
         cudaError_t e = cudaMalloc((void **)&S.d_ws, need * sizeof(float));
         if (e != cudaSuccess) return cuda_fail(e, "workspace");
         /* the router's ticket counters live here and must start at zero */
@@ -220,6 +234,7 @@ static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages
         S.ws_floats = need;
     }
     if (io > S.io_floats) {
+        g_epoch++;
         if (S.d_x) cudaFree(S.d_x);
         if (S.d_out) cudaFree(S.d_out);
         if (S.h_x) cudaFreeHost(S.h_x);
@@ -283,6 +298,7 @@ const char *waste_cuda_backend_name(void) { return S.inited ? S.name : NULL; }
 
 static void free_layer(wc_layer *L)
 {
+    if (L->gx) cudaGraphExecDestroy(L->gx);
     cudaFree(L->d_base);
     cudaFree(L->d_router); cudaFree(L->d_bias);
     cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
@@ -303,6 +319,7 @@ void waste_cuda_shutdown(void)
         free(S.book_absmax);
         cudaFreeHost(S.h_x); cudaFreeHost(S.h_out); cudaFreeHost(S.h_idx);
         cudaFreeHost(S.h_w);
+        cudaFree(S.d_res); cudaFreeHost(S.h_res);
         cudaStreamDestroy(S.stream);
         memset(&S, 0, sizeof S);
     }
@@ -346,6 +363,7 @@ int waste_register_cuda_vq(waste_vq_slots *s)
 static int books_upload(const float *books, int n_books)
 {
     int rc = 0;
+    g_epoch++;
     const size_t bytes = (size_t)n_books * 256 * 8 * sizeof(float);
     if (S.d_books) { cudaFree(S.d_books); S.d_books = NULL; S.n_books = 0; }
     free(S.book_absmax);
@@ -518,6 +536,7 @@ static int reserve_locked(int layer, int n_experts, size_t rec_bytes, int first,
                           int inter, int lat, int stages)
 {
     int rc = 0;
+    g_epoch++;
     wc_layer *L = &S.layer[layer];
     if (L->d_base) {
         if (L->n_total != n_experts || L->kb.rec_bytes != rec_bytes || L->kb.inter != inter ||
@@ -646,6 +665,7 @@ void waste_cuda_vq_bank_free(int layer)
     if (S.inited) {
         cudaStreamSynchronize(S.stream);
         wc_layer *L = &S.layer[layer];
+        g_epoch++;
         cudaFree(L->d_base);
         L->d_base = NULL;
         free(L->present);
@@ -672,6 +692,7 @@ int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
         return fail(WASTE_CUDA_E_ARG, "moe_trunk_load: bad arguments");
     pthread_mutex_lock(&g_mu);
     if (!S.inited && (rc = init_locked(-1))) goto out;
+    g_epoch++;
     wc_layer *L = &S.layer[layer];
     cudaFree(L->d_router); cudaFree(L->d_bias);
     cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
@@ -1090,6 +1111,7 @@ int waste_cuda_ep_init(int rank, int world, const void *id, size_t bytes)
     EP.rank = rank;
     EP.world = world;
     EP.active = 1;
+    g_epoch++;
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -1106,6 +1128,7 @@ static void ep_shutdown_locked(void)
     EP.d_xall = EP.d_outall = NULL;
     EP.all_floats = 0;
     EP.active = EP.rank = EP.world = 0;
+    g_epoch++;
 }
 
 void waste_cuda_ep_shutdown(void)
@@ -1169,6 +1192,55 @@ out:
     return rc;
 }
 
+/* The host-buffer layer call captured once: H2D of x, the kernel chain,
+ * D2H of the output, route, weights and error word. Rebuilt when the
+ * epoch moved since it was made. */
+static size_t res_floats(int lat) { return (size_t)lat + 2 * WC_MAX_TOPK + 4; }
+
+static int ensure_res(int lat)
+{
+    if (lat <= S.res_lat) return 0;
+    g_epoch++;
+    cudaFree(S.d_res);
+    cudaFreeHost(S.h_res);
+    S.d_res = S.h_res = NULL;
+    S.res_lat = 0;
+    if (cudaMalloc((void **)&S.d_res, res_floats(lat) * sizeof(float)) != cudaSuccess ||
+        cudaMallocHost((void **)&S.h_res, res_floats(lat) * sizeof(float)) != cudaSuccess ||
+        cudaMemset(S.d_res, 0, res_floats(lat) * sizeof(float)) != cudaSuccess)
+        return fail(WASTE_CUDA_E_NOMEM, "layer result block");
+    S.res_lat = lat;
+    return 0;
+}
+
+static int layer_graph(wc_layer *L, const wc_moe_args *a, size_t xb)
+{
+    int rc = 0;
+    if (L->gx && L->gx_epoch == g_epoch) return 0;
+    if (L->gx) { cudaGraphExecDestroy(L->gx); L->gx = NULL; }
+    cudaGraph_t g = NULL;
+    CK(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
+    cudaError_t e = cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream);
+    if (e == cudaSuccess) e = (cudaError_t)wc_moe_launch(a, S.stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(S.h_res, S.d_res, res_floats(S.res_lat) * sizeof(float),
+                            cudaMemcpyDeviceToHost, S.stream);
+    (void)L;
+    const cudaError_t ee = cudaStreamEndCapture(S.stream, &g);   /* always end it */
+    if (e == cudaSuccess) e = ee;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&L->gx, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        L->gx = NULL;
+        cudaGetLastError();
+        rc = cuda_fail(e, "layer graph");
+        goto out;
+    }
+    L->gx_epoch = g_epoch;
+out:
+    return rc;
+}
+
 int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, float *weights)
 {
     int rc = 0;
@@ -1178,24 +1250,46 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
     pthread_mutex_lock(&g_mu);
     if ((rc = layer_args(layer, 1, 0, &a, &L))) goto out;
     const size_t xb = (size_t)L->hidden * sizeof(float);
-    memcpy(S.h_x, x, xb);
-    CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
     a.x = S.d_x;
     a.out = S.d_out;
     a.idx_out = S.d_idx;
     a.w_out = S.d_w;
-    CK((cudaError_t)wc_moe_launch(&a, S.stream), "layer kernels");
-    CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "out D2H");
-    if (routed || weights) {
+    memcpy(S.h_x, x, xb);
+    if (!wc_profiling()) {
+        /* one graph launch per call: x in, the kernel chain, and one copy of
+         * the result block (output, route, weights, error word) out */
+        if ((rc = ensure_res(L->hidden))) goto out;
+        const int lat = S.res_lat;
+        a.out = S.d_res;
+        a.idx_out = (int *)(S.d_res + lat);
+        a.w_out = S.d_res + lat + WC_MAX_TOPK;
+        a.ws.err = (unsigned int *)(S.d_res + lat + 2 * WC_MAX_TOPK);
+        if ((rc = layer_graph(L, &a, xb))) goto out;
+        CK(cudaGraphLaunch(L->gx, S.stream), "layer graph");
+        CK(cudaStreamSynchronize(S.stream), "moe layer");
+        const unsigned int err = *(const unsigned int *)(S.h_res + lat + 2 * WC_MAX_TOPK);
+        if (err) {
+            cudaMemset(S.d_res + lat + 2 * WC_MAX_TOPK, 0, sizeof(unsigned int));
+            rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
+            goto out;
+        }
+        memcpy(out, S.h_res, xb);
+        if (routed) memcpy(routed, S.h_res + lat, (size_t)L->top_k * sizeof(int));
+        if (weights) memcpy(weights, S.h_res + lat + WC_MAX_TOPK, (size_t)L->top_k * sizeof(float));
+        goto out;
+    } else {                        /* phase timers: events between the kernels */
+        CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
+        CK((cudaError_t)wc_moe_launch(&a, S.stream), "layer kernels");
+        CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "out D2H");
         CK(cudaMemcpyAsync(S.h_idx, S.d_idx, (size_t)L->top_k * sizeof(int),
                            cudaMemcpyDeviceToHost, S.stream), "idx D2H");
         CK(cudaMemcpyAsync(S.h_w, S.d_w, (size_t)L->top_k * sizeof(float),
                            cudaMemcpyDeviceToHost, S.stream), "w D2H");
-    }
-    CK(cudaStreamSynchronize(S.stream), "moe layer");
-    if (read_device_errors(1)) {
-        rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
-        goto out;
+        CK(cudaStreamSynchronize(S.stream), "moe layer");
+        if (read_device_errors(1)) {
+            rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
+            goto out;
+        }
     }
     memcpy(out, S.h_out, xb);
     if (routed) memcpy(routed, S.h_idx, (size_t)L->top_k * sizeof(int));

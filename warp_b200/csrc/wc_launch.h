@@ -162,6 +162,7 @@ void     wc_count_launches(int n);
 enum { WC_PH_ROUTER, WC_PH_ROUTE, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
        WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_COUNT };
 int  wc_prof_enable(int on);
+int  wc_profiling(void);      /* 1 while the phase timers are on */
 void wc_prof_read(double *ms, unsigned long long *cnt, int nphase);
 
 #ifdef __cplusplus
