@@ -226,7 +226,7 @@ struct TileThread {
     /* After the table is built: gather, reduce the lanes, and write one
      * partial sum per valid row to out[m * mstride + row]. */
     __device__ __forceinline__ void finish(const TileGeom &g, float *lut, float *out,
-                                           size_t mstride, int nm)
+                                           size_t mstride, int nm, const int *slots = nullptr)
     {
         float acc[kRowsPerThread];
 #pragma unroll
@@ -235,7 +235,7 @@ struct TileThread {
         if (g.nlanes == 1) {             /* the thread owns its rows outright */
             if (!active) return;
             const int row0 = rbl * kBlock + q * 16;
-            float *dst = out + (size_t)m * mstride + row0;
+            float *dst = out + (size_t)(slots ? slots[m] : m) * mstride + row0;
             if (row0 + 16 <= g.M && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
                 for (int k = 0; k < kRowsPerThread; k += 4)
@@ -265,7 +265,7 @@ struct TileThread {
             if (row >= g.M) continue;
             float s = red[r];
             for (int l = 1; l < g.nlanes; l++) s += red[(size_t)l * R + r];
-            out[(size_t)mm * mstride + row] = s;
+            out[(size_t)(slots ? slots[mm] : mm) * mstride + row] = s;
         }
     }
 };
@@ -789,7 +789,8 @@ __global__ void __launch_bounds__(512, 1)
 gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
-    __shared__ int go;
+    __shared__ int go, s_nloc;
+    __shared__ int s_slot[kMaxTopK];
     TileSmem sm(smraw, g);
     int b = blockIdx.x;
     const int grp = b % g.groups; b /= g.groups;
@@ -802,13 +803,18 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         mbar_init(&sm.bars[1], 1);
         mbar_fence_init();
     }
-    /* routing-independent: x slice, codebook rows, the table */
+    /* routing-independent: x slice, codebook rows, the table — built while
+     * the route is computed, unless this device holds so few of the experts
+     * (gu_eg > 0) that most tiles find no work: then the route comes first */
+    const bool route_first = a.partial_bank && a.gu_eg > 0;
     BookRows<ST, kGuBooks> books;
-    books.load(a.books, bk.cb_base + kind * ST);
-    if ((int)threadIdx.x < nvs * kVecDim)
-        sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
-    __syncthreads();
-    books.build(sm.lut, sm.xs, nvs);
+    if (!route_first) {
+        books.load(a.books, bk.cb_base + kind * ST);
+        if ((int)threadIdx.x < nvs * kVecDim)
+            sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
+        __syncthreads();
+        books.build(sm.lut, sm.xs, nvs);
+    }
     if (a.router) {
         if (threadIdx.x == 0) {
             go = wait_flag(a.ws.route_flag + t, a.ws.err);
@@ -825,14 +831,39 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         pdl_wait();
     }
     pdl_trigger();
+    /* the group's route slots: slots j0.. of the token, or, with a partial
+     * bank, the group's share of the slots whose experts are held here */
     const int j0 = grp * g.EG;
-    const int nm = min(g.EG, a.K - j0);
+    int nm;
+    if (route_first) {
+        if (threadIdx.x == 0) {
+            int n = 0;
+            for (int j = 0; j < a.K; j++)
+                if (expert_here(a, idx, a.K, t, j)) s_slot[n++] = j;
+            s_nloc = n;
+        }
+        __syncthreads();
+        if (j0 >= s_nloc) return;               /* uniform: no local expert left */
+        nm = min(g.EG, s_nloc - j0);
+        books.load(a.books, bk.cb_base + kind * ST);
+        if ((int)threadIdx.x < nvs * kVecDim)
+            sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
+        __syncthreads();
+        books.build(sm.lut, sm.xs, nvs);
+    } else {
+        nm = min(g.EG, a.K - j0);
+        if ((int)threadIdx.x < nm) s_slot[j0 + threadIdx.x] = j0 + threadIdx.x;
+        __syncthreads();
+    }
+    const int *slot = s_slot + j0;              /* matrix m is route slot slot[m] */
     /* stage the group's index streams for this slice: (matrix, row block)
      * runs of nvs positions, in halves [0,h) and [h,nvs); matrices of
      * experts held by another rank are neither staged nor gathered */
+    /* matrices whose experts another device holds are neither staged nor
+     * gathered (route-first groups hold only local slots) */
     uint32_t here = 0;
     for (int mm = 0; mm < nm; mm++)
-        if (expert_here(a, idx, a.K, t, j0 + mm)) here |= 1u << mm;
+        if (route_first || expert_here(a, idx, a.K, t, slot[mm])) here |= 1u << mm;
     const uint32_t psz = kBlock * ST;
     const int h = (nvs + 1) / 2;
     const int ncopy = nm * g.nrb;
@@ -857,7 +888,7 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         /* thread m issues expert m's two boxes: the route reads run in parallel */
         const int mm = threadIdx.x;
         const uint32_t box = (uint32_t)(g.nrb / 2) * nvs * psz;
-        const int e = __ldcg(idx + (size_t)t * a.K + j0 + mm) - bk.first;
+        const int e = __ldcg(idx + (size_t)t * a.K + slot[mm]) - bk.first;
         uint8_t *dst = sm.stage + (size_t)mm * g.nrb * nvs * psz;
         tma_load_3d(dst, &bk.tmap[kind], v0 * 24, 0, e, &sm.bars[0]);
         tma_load_3d(dst + box, &bk.tmap[kind], v0 * 24, g.nrb / 2, e, &sm.bars[1]);
@@ -865,7 +896,7 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
     for (int c = threadIdx.x; c < ncopy && !use_map; c += blockDim.x) {
         const int m = c / g.nrb, rbl = c % g.nrb;
         if (!((here >> m) & 1u)) continue;
-        const uint8_t *src = expert_rec(bk, idx, a.K, t, j0 + m) + (kind ? bk.up_off : bk.gate_off) +
+        const uint8_t *src = expert_rec(bk, idx, a.K, t, slot[m]) + (kind ? bk.up_off : bk.gate_off) +
                              ((size_t)rbl * g.nv + v0) * psz;
         uint8_t *dst = sm.stage + (size_t)(m * g.nrb + rbl) * nvs * psz;
         bulk_g2s(dst, src, h * psz, &sm.bars[0]);
@@ -905,8 +936,8 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
     }
     th.G.split = h;
     __syncthreads();                 /* the table */
-    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K + j0) * bk.inter;
-    th.finish(gs, sm.lut, out, bk.inter, nm);
+    float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K) * bk.inter;
+    th.finish(gs, sm.lut, out, bk.inter, nm, slot);
     if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
 }
 
@@ -1215,7 +1246,17 @@ MoeGeom moe_geom(const wc_moe_args *a)
 {
     MoeGeom m;
     const wc_bank &b = a->bank;
-    m.gu = with_stage(make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512), b.stages);
+    if (a->partial_bank && a->gu_eg > 0) {
+        /* experts spread over devices: tiles of the expected local count,
+         * enough groups for the case where every routed expert is local */
+        /* one lane per quarter block: small tiles, many per SM, and the
+         * empty ones retire right after the route */
+        const int q = a->gu_eg * ((b.inter + kBlock - 1) / kBlock) * 4;
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, kVsGateUp, b.stages, q), b.stages);
+        m.gu.groups = (a->K + m.gu.EG - 1) / m.gu.EG;
+    } else {
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512), b.stages);
+    }
     m.d = with_stage(make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448), b.stages);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
     m.d_tiles = a->T * a->K * m.d.ns;

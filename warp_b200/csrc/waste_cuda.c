@@ -776,6 +776,13 @@ static void fill_args(wc_moe_args *a, const wc_layer *L, int T, int K, int E, in
     a->sh_t0 = 0;
     a->sh_t1 = T;
     a->partial_bank = L->kb.first != 0 || L->kb.n_experts != L->n_total;
+    if (a->partial_bank && L->n_total > 0) {
+        /* routed experts of a token expected here; at two or fewer most
+         * gate/up tiles would be empty, so they become route-first tiles of
+         * that many experts */
+        const int eg = (int)(((long)K * L->kb.n_experts + L->n_total - 1) / L->n_total);
+        a->gu_eg = eg <= 4 ? eg : 0;
+    }
     wc_moe_ws_carve(&a->ws, S.d_ws, T, K, E, L->kb.lat, L->kb.inter, si, L->kb.stages);
 }
 

@@ -74,6 +74,8 @@ typedef struct {
                                  (all of them, unless expert parallel)       */
     int partial_bank;         /* 1: the bank holds only some experts; routes
                                  to the others are skipped, not computed      */
+    int gu_eg;                /* gate/up experts per tile with a partial bank
+                                 (0: all K of a token)                        */
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
