@@ -41,20 +41,30 @@ def main():
                           L.router, L.bias, L.shared_inter, L.sh)
     T = 3
     dev = torch.device("cuda", local)
-    for L in layers:
-        x = synth.activations(100 + 10 * rank + L.layer, L.hidden, T=T)
-        dx = torch.from_numpy(x).to(dev)
-        out = torch.empty((T, L.hidden), device=dev)
-        idx = torch.empty((T, L.top_k), dtype=torch.int32, device=dev)
-        ep.moe_layer_dev(L.layer, T, dx.data_ptr(), out.data_ptr(), idx.data_ptr())
-        torch.cuda.synchronize()
-        out, idx = out.cpu().numpy(), idx.cpu().numpy()
-        for t in range(T):
-            ro, ri, _ = O.moe_layer(L, x[t], fma=1)
-            assert np.array_equal(idx[t], ri), (rank, L.layer, t)
-            r = rel_l2(out[t], ro)
-            assert r < TOL, (rank, L.layer, t, r)
-    assert wb.device_errors() == 0
+
+    def check(mode):
+        for rep in range(2):                 # twice: the exchange's flags only grow
+            for L in layers:
+                x = synth.activations(100 + 10 * rank + L.layer + rep, L.hidden, T=T)
+                dx = torch.from_numpy(x).to(dev)
+                out = torch.empty((T, L.hidden), device=dev)
+                idx = torch.empty((T, L.top_k), dtype=torch.int32, device=dev)
+                ep.moe_layer_dev(L.layer, T, dx.data_ptr(), out.data_ptr(), idx.data_ptr())
+                torch.cuda.synchronize()
+                out, idx = out.cpu().numpy(), idx.cpu().numpy()
+                for t in range(T):
+                    ro, ri, _ = O.moe_layer(L, x[t], fma=1)
+                    assert np.array_equal(idx[t], ri), (mode, rank, L.layer, t)
+                    r = rel_l2(out[t], ro)
+                    assert r < TOL, (mode, rank, L.layer, t, r)
+        assert wb.device_errors() == 0, mode
+
+    check("peer memory")                     # the default exchange
+    dist.barrier()
+    ep.shutdown()
+    os.environ["WASTE_CUDA_EP_P2P"] = "0"    # the NCCL exchange, same banks
+    ep.setup(rank, world)
+    check("nccl")
     dist.barrier()
     ep.shutdown()
     dist.destroy_process_group()

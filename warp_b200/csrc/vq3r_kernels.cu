@@ -457,6 +457,102 @@ __device__ __forceinline__ unsigned int atomic_add_acq_rel(unsigned int *p, unsi
     return old;
 }
 
+/* ---- the expert-parallel exchange through peer memory --------------------
+ * Flags are written by another GPU over NVLink: release/acquire at system
+ * scope, and every wait is bounded (WC_ERR_PEER_WAIT, work skipped). */
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.sys.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned int *ep_xflags(const wc_ep_link &l, int r)
+{
+    return reinterpret_cast<unsigned int *>(l.mail[r]);
+}
+__device__ __forceinline__ unsigned int *ep_pflags(const wc_ep_link &l, int r)
+{
+    return reinterpret_cast<unsigned int *>(l.mail[r] + 256);
+}
+__device__ __forceinline__ unsigned int *ep_ticket(const wc_ep_link &l)
+{
+    return reinterpret_cast<unsigned int *>(l.mail[l.rank] + 512);
+}
+__device__ __forceinline__ unsigned int *ep_epoch(const wc_ep_link &l)
+{
+    return reinterpret_cast<unsigned int *>(l.mail[l.rank] + 640);
+}
+/* rank r's mailbox: x [world][T][hidden], then part [world][T][hidden] */
+__device__ __forceinline__ float *ep_x(const wc_ep_link &l, int r)
+{
+    return reinterpret_cast<float *>(l.mail[r] + WC_EP_MAIL_HDR);
+}
+__device__ __forceinline__ float *ep_part(const wc_ep_link &l, int r)
+{
+    return ep_x(l, r) + (size_t)l.world * l.T * l.hidden;
+}
+
+/* Until every rank's flag (in this rank's mailbox) reaches epoch e. */
+__device__ __forceinline__ bool ep_wait_all(const unsigned int *flags, int world, unsigned int e,
+                                            unsigned int *err)
+{
+    for (int r = 0; r < world; r++) {
+        long long i = 0;
+        while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
+            if (++i >= kSpinLimit) {
+                atomicOr(err, WC_ERR_PEER_WAIT);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+/* Layer start: this rank's T tokens into every rank's mailbox, then the
+ * x flag of this rank, at the new epoch, in every mailbox. One block. */
+__global__ void __launch_bounds__(256) ep_publish_kernel(wc_ep_link l, const float *x)
+{
+    __shared__ unsigned int e;
+    if (threadIdx.x == 0) e = *ep_epoch(l) + 1;
+    __syncthreads();
+    const size_t n4 = (size_t)l.T * l.hidden / 4, off = (size_t)l.rank * l.T * l.hidden;
+    const float4 *src = reinterpret_cast<const float4 *>(x);
+    for (size_t i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = src[i];
+        for (int r = 0; r < l.world; r++) reinterpret_cast<float4 *>(ep_x(l, r) + off)[i] = v;
+    }
+    __syncthreads();                 /* every thread's stores before the releases */
+    if ((int)threadIdx.x < l.world) st_release_sys(ep_xflags(l, threadIdx.x) + l.rank, e);
+    if (threadIdx.x == 0) *ep_epoch(l) = e;       /* later kernels of this call read it */
+}
+
+/* Layer end: once every rank's partial sums of this rank's tokens are in,
+ * out[t] = the sum over ranks in rank order. grid (ceil(hidden/256), T). */
+__global__ void __launch_bounds__(256) ep_finalize_kernel(wc_ep_link l, float *out,
+                                                         unsigned int *err)
+{
+    __shared__ int ok;
+    const unsigned int e = *ep_epoch(l);
+    if (threadIdx.x == 0) ok = ep_wait_all(ep_pflags(l, l.rank), l.world, e, err);
+    __syncthreads();
+    if (!ok) return;
+    for (int r = 0; r < l.world; r++) (void)ld_acquire_sys(ep_pflags(l, l.rank) + r);
+    const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= l.hidden) return;
+    const float *part = ep_part(l, l.rank);
+    float y = 0.0f;
+    for (int r = 0; r < l.world; r++)
+        y = __fadd_rn(y, __ldcv(part + ((size_t)r * l.T + t) * l.hidden + i));
+    out[(size_t)t * l.hidden + i] = y;
+}
+
 /* dst[0..n) = src[0..n) (global, written by an earlier phase) into shared
  * memory: every thread's loads issued before any store. n <= 8*blockDim. */
 __device__ __forceinline__ void stage_floats(float *dst, const float *src, int n)
@@ -631,6 +727,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ float part[kRouterBlock / 32];
     __shared__ unsigned int ticket;
+    __shared__ int ep_fail;
+    if (threadIdx.x == 0) ep_fail = 0;
     pdl_trigger();                   /* let gate/up start its table build */
     const int lat = a.bank.lat, n4 = lat / 4;
     const int t = blockIdx.y;
@@ -677,10 +775,17 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
             bulk_g2s(sst, (kind ? a.shu_s : a.shg_s) + (size_t)o0 * ng, sbytes, bar);
     }
     pdl_wait();
-    if (threadIdx.x == 0) bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
+    if (threadIdx.x == 0) {
+        if (a.ep.on) {            /* every rank's tokens are in this mailbox */
+            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err))
+                ep_fail = 1;
+            asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
+        }
+        bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
+    }
     __syncthreads();
-    const bool ok = mbar_wait(bar, 0);
-    if (!ok && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    const bool ok = mbar_wait(bar, 0) && !ep_fail;   /* a missing peer: no dot products */
+    if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
     if (is_router) {
         const int lr = warp / kRouterSplit, qtr = warp % kRouterSplit;
         const int per = (n4 + kRouterSplit - 1) / kRouterSplit;
@@ -1200,17 +1305,38 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         for (; nn < K; nn++) order[nn] = -1;
     }
     __syncthreads();
-    if (jl != 0 || !ok) return;
-    float y = 0.0f;
-    for (int n = 0; n < K; n++) {
-        const int j = order[n];
-        if (j < 0) break;
-        const float wj = wsm[j];
-        if (a.order_by_id && wj == 0.0f) continue;
-        y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
+    if (jl == 0 && ok) {
+        float y = 0.0f;
+        for (int n = 0; n < K; n++) {
+            const int j = order[n];
+            if (j < 0) break;
+            const float wj = wsm[j];
+            if (a.order_by_id && wj == 0.0f) continue;
+            y = __fadd_rn(y, __fmul_rn(wj, accj[j][il]));
+        }
+        if (sh_here) y = __fadd_rn(y, shv);
+        if (!a.ep.on) {
+            a.out[(size_t)t * bk.lat + i] = y;
+        } else {                  /* straight into the token's rank, over NVLink */
+            const int owner = t / a.ep.T, tl = t % a.ep.T;
+            ep_part(a.ep, owner)[((size_t)a.ep.rank * a.ep.T + tl) * a.ep.hidden + i] = y;
+        }
     }
-    if (sh_here) y = __fadd_rn(y, shv);
-    a.out[(size_t)t * bk.lat + i] = y;
+    if (!a.ep.on) return;
+    /* the last block of this rank's combine tells every rank its partial
+     * sums are in */
+    __shared__ unsigned int last;
+    __syncthreads();                 /* the block's stores happen before thread 0's fence */
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomic_add_acq_rel(ep_ticket(a.ep), 1u) == gridDim.x * gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) *ep_ticket(a.ep) = 0;
+    __threadfence_system();
+    if ((int)threadIdx.x < a.ep.world)
+        st_release_sys(ep_pflags(a.ep, threadIdx.x) + a.ep.rank, *ep_epoch(a.ep));
 }
 
 constexpr int kVsGateUp = WC_VS_GATEUP;
@@ -1509,6 +1635,24 @@ extern "C" int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *s
     if (stages == 3) dequant_kernel<3><<<blocks, 256, 0, s>>>(W, idx, scale, M, N, books, cb);
     else if (stages == 2) dequant_kernel<2><<<blocks, 256, 0, s>>>(W, idx, scale, M, N, books, cb);
     else return (int)cudaErrorInvalidValue;
+    g_launches += 1;
+    return (int)cudaGetLastError();
+}
+
+extern "C" int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigned int *err,
+                                    void *stream)
+{
+    (void)err;
+    ep_publish_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(*l, x);
+    g_launches += 1;
+    return (int)cudaGetLastError();
+}
+
+extern "C" int wc_ep_finalize_launch(const wc_ep_link *l, float *out, unsigned int *err,
+                                     void *stream)
+{
+    ep_finalize_kernel<<<dim3((l->hidden + 255) / 256, l->T), 256, 0, (cudaStream_t)stream>>>(
+        *l, out, err);
     g_launches += 1;
     return (int)cudaGetLastError();
 }

@@ -123,8 +123,14 @@ static struct {
     ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
                                    ncclComm_t, cudaStream_t);
     const char *(*error_string)(ncclResult_t);
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                               ncclComm_t, cudaStream_t);
     float *d_xall, *d_outall;     /* [world*T][hidden] gathered tokens and partials */
     size_t all_floats;
+    /* the exchange through peer memory: every rank's mailbox mapped here */
+    int p2p;                      /* 1 once every rank mapped every mailbox */
+    unsigned char *mail[WC_EP_MAX];
+    int mail_T, mail_hidden;
 } EP;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
@@ -1076,8 +1082,9 @@ static int nccl_load(void)
     *(void **)&EP.all_gather = dlsym(h, "ncclAllGather");
     *(void **)&EP.reduce_scatter = dlsym(h, "ncclReduceScatter");
     *(void **)&EP.error_string = dlsym(h, "ncclGetErrorString");
+    *(void **)&EP.all_reduce = dlsym(h, "ncclAllReduce");
     if (!EP.get_unique_id || !EP.comm_init_rank || !EP.comm_destroy || !EP.all_gather ||
-        !EP.reduce_scatter || !EP.error_string) {
+        !EP.reduce_scatter || !EP.error_string || !EP.all_reduce) {
         dlclose(h);
         return fail(WASTE_CUDA_E_NODEV, "libnccl.so.2 lacks an entry point this library uses");
     }
@@ -1124,10 +1131,92 @@ out:
     return rc;
 }
 
+/* Every rank's agreement on an int (min over ranks), through NCCL. */
+static int ep_agree_min(int v, int *out)
+{
+    int rc = 0;
+    int *d = NULL;
+    CK(cudaMalloc((void **)&d, sizeof(int)), "agreement word");
+    CK(cudaMemcpy(d, &v, sizeof(int), cudaMemcpyHostToDevice), "agreement H2D");
+    const ncclResult_t r = EP.all_reduce(d, d, 1, ncclInt32, ncclMin, EP.comm, S.stream);
+    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllReduce"); goto out; }
+    CK(cudaStreamSynchronize(S.stream), "agreement");
+    CK(cudaMemcpy(out, d, sizeof(int), cudaMemcpyDeviceToHost), "agreement D2H");
+out:
+    cudaFree(d);
+    return rc;
+}
+
+/* Unmaps the peers' mailboxes and, once every rank has, frees this one. */
+static void ep_mail_free(void)
+{
+    if (!EP.mail[EP.rank]) return;
+    for (int r = 0; r < EP.world; r++)
+        if (r != EP.rank && EP.mail[r]) cudaIpcCloseMemHandle(EP.mail[r]);
+    int dummy = 0;
+    ep_agree_min(0, &dummy);                 /* nobody maps this one any more */
+    cudaFree(EP.mail[EP.rank]);
+    memset(EP.mail, 0, sizeof EP.mail);
+    EP.p2p = 0;
+    EP.mail_T = EP.mail_hidden = 0;
+}
+
+/* Collective: mailboxes for T tokens per rank of `hidden` floats, mapped on
+ * every rank, or EP.p2p = 0 on every rank when any mapping fails. */
+static int ep_mail_setup(int T, int hidden)
+{
+    int rc = 0;
+    if (EP.mail[EP.rank] && T <= EP.mail_T && hidden <= EP.mail_hidden) return 0;
+    if (EP.mail[EP.rank]) ep_mail_free();
+    g_epoch++;
+    const int Tm = T > WC_CHUNK_MAX / EP.world ? T : WC_CHUNK_MAX / EP.world;
+    const size_t bytes = WC_EP_MAIL_HDR + 2 * (size_t)EP.world * Tm * hidden * sizeof(float);
+    unsigned char *mine = NULL, *dh = NULL;
+    cudaIpcMemHandle_t hs[WC_EP_MAX];
+    int ok = 1;
+    CK(cudaMalloc((void **)&mine, bytes), "mailbox");
+    CK(cudaMemset(mine, 0, bytes), "mailbox clear");
+    CK(cudaDeviceSynchronize(), "mailbox clear");
+    if (cudaIpcGetMemHandle(&hs[EP.rank], mine) != cudaSuccess) ok = 0;
+    CK(cudaMalloc((void **)&dh, sizeof hs), "handle exchange");
+    CK(cudaMemcpy(dh + EP.rank * sizeof(cudaIpcMemHandle_t), &hs[EP.rank],
+                  sizeof(cudaIpcMemHandle_t), cudaMemcpyHostToDevice), "handle H2D");
+    {
+        const ncclResult_t r = EP.all_gather(dh + EP.rank * sizeof(cudaIpcMemHandle_t), dh,
+                                             sizeof(cudaIpcMemHandle_t), ncclUint8, EP.comm,
+                                             S.stream);
+        if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllGather"); goto out; }
+    }
+    CK(cudaStreamSynchronize(S.stream), "handle exchange");
+    CK(cudaMemcpy(hs, dh, (size_t)EP.world * sizeof(cudaIpcMemHandle_t),
+                  cudaMemcpyDeviceToHost), "handles D2H");
+    EP.mail[EP.rank] = mine;
+    for (int r = 0; r < EP.world && ok; r++) {
+        if (r == EP.rank) continue;
+        void *p = NULL;
+        if (cudaIpcOpenMemHandle(&p, hs[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+        } else {
+            EP.mail[r] = (unsigned char *)p;
+        }
+    }
+    int all = 0;
+    if ((rc = ep_agree_min(ok, &all))) goto out;
+    EP.mail_T = Tm;
+    EP.mail_hidden = hidden;
+    EP.p2p = all;
+    if (!all) ep_mail_free();                /* every rank falls back to NCCL */
+out:
+    cudaFree(dh);
+    return rc;
+}
+
 static void ep_shutdown_locked(void)
 {
     if (!EP.active) return;
     if (S.inited) cudaStreamSynchronize(S.stream);
+    ep_mail_free();
     EP.comm_destroy(EP.comm);
     cudaFree(EP.d_xall);
     cudaFree(EP.d_outall);
@@ -1178,6 +1267,36 @@ int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out
     }
     cudaStream_t st = stream ? (cudaStream_t)stream : S.stream;
     const size_t per = (size_t)T * L->hidden;
+    const size_t kb = (size_t)T * L->top_k;
+    if (getenv_flag("WASTE_CUDA_EP_P2P", 1) && (rc = ep_mail_setup(T, L->hidden))) goto out;
+    if (EP.p2p && T <= EP.mail_T && L->hidden <= EP.mail_hidden) {
+        /* tokens out to every mailbox, the layer on all of them, partial
+         * sums straight into the tokens' ranks, sum in rank order */
+        wc_ep_link lk;
+        memset(&lk, 0, sizeof lk);
+        lk.on = 1;
+        lk.rank = EP.rank;
+        lk.world = EP.world;
+        lk.T = T;
+        lk.hidden = L->hidden;
+        memcpy(lk.mail, EP.mail, sizeof lk.mail);
+        CK((cudaError_t)wc_ep_publish_launch(&lk, d_x, a.ws.err, st), "ep publish");
+        a.x = (const float *)(EP.mail[EP.rank] + WC_EP_MAIL_HDR);
+        a.out = EP.d_outall;
+        a.idx_out = S.d_idx;
+        a.w_out = S.d_w;
+        a.sh_t0 = EP.rank * T;
+        a.sh_t1 = EP.rank * T + T;
+        a.ep = lk;
+        if (a.gu_eg == 0) a.gu_eg = L->top_k;   /* route-first: x arrives with the route */
+        CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
+        CK((cudaError_t)wc_ep_finalize_launch(&lk, d_out, a.ws.err, st), "ep finalize");
+        if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)EP.rank * kb, kb * sizeof(int),
+                                      cudaMemcpyDeviceToDevice, st), "route copy");
+        if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)EP.rank * kb, kb * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, st), "weight copy");
+        goto out;
+    }
     ncclResult_t r = EP.all_gather(d_x, EP.d_xall, per, ncclFloat32, EP.comm, st);
     if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllGather"); goto out; }
     a.x = EP.d_xall;
@@ -1189,7 +1308,6 @@ int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out
     CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
     r = EP.reduce_scatter(EP.d_outall, d_out, per, ncclFloat32, ncclSum, EP.comm, st);
     if (r != ncclSuccess) { rc = nccl_fail(r, "ncclReduceScatter"); goto out; }
-    const size_t kb = (size_t)T * L->top_k;
     if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)EP.rank * kb, kb * sizeof(int),
                                   cudaMemcpyDeviceToDevice, st), "route copy");
     if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)EP.rank * kb, kb * sizeof(float),

@@ -53,6 +53,28 @@ typedef struct {
 #define WC_ERR_ROUTE_WAIT 1u
 #define WC_ERR_TMA_WAIT   2u
 #define WC_ERR_BAD_EXPERT 4u
+#define WC_ERR_PEER_WAIT  8u          /* a peer's flag did not arrive in time */
+
+/* Expert-parallel exchange through peer memory (NVLink). Every rank has a
+ * mailbox of the same layout, mapped into every other rank's address
+ * space:
+ *   +0     x flags     [WC_EP_MAX] : epoch of rank r's tokens, set by r
+ *   +256   part flags  [WC_EP_MAX] : epoch of rank r's partial sums, set by r
+ *   +512   combine ticket (local use)
+ *   +640   epoch counter (local use: bumped once per layer call)
+ *   +1024  x   [world][T][hidden]  : every rank's tokens
+ *   then   part[world][T][hidden]  : every rank's partial sums of this
+ *                                    rank's tokens
+ * Flags only grow (epochs), so nothing is reset between calls. */
+#define WC_EP_MAX 8
+#define WC_EP_MAIL_HDR 1024
+typedef struct {
+    int on, rank, world, T, hidden;
+    unsigned char *mail[WC_EP_MAX];   /* every rank's mailbox as mapped here */
+} wc_ep_link;
+
+int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigned int *err, void *stream);
+int wc_ep_finalize_launch(const wc_ep_link *l, float *out, unsigned int *err, void *stream);
 
 typedef struct {
     wc_bank bank;
@@ -76,6 +98,8 @@ typedef struct {
                                  to the others are skipped, not computed      */
     int gu_eg;                /* gate/up experts per tile with a partial bank
                                  (0: all K of a token)                        */
+    wc_ep_link ep;            /* on: x comes from the mailbox, partial sums go
+                                 to the tokens' ranks through peer memory    */
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
