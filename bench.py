@@ -554,6 +554,296 @@ def run_warp(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 4
+
+K3_HIDDEN, K3_INTER, K3_EXPERTS, K3_TOPK, K3_SHARED = 7168, 2048, 512, 16, 2048
+K3_SCALE = 2.827
+K3_LAYERS = 4                 # resident layers the steps cycle over
+K3_BATCHES = (1, 16, 64)
+K3_METRIC = "K3-class MoE layer tok/s (hidden 7168, 512 VQ3R experts, top-16)"
+
+
+def k3_expert_bytes():
+    from warp_b200 import synth
+    idx = 2 * synth.index_bytes(K3_INTER, K3_HIDDEN, 3) + synth.index_bytes(K3_HIDDEN, K3_INTER, 3)
+    return idx + 2 * (2 * K3_INTER + K3_HIDDEN)
+
+
+def k3_trunk_bytes():
+    ng_h, ng_s = (K3_HIDDEN + 127) // 128, (K3_SHARED + 127) // 128
+    shared = (2 * K3_SHARED * ng_h * 128 + K3_HIDDEN * ng_s * 128
+              + 2 * (2 * K3_SHARED * ng_h + K3_HIDDEN * ng_s))
+    return K3_EXPERTS * K3_HIDDEN * 4, shared
+
+
+def k3_cpu_sample(budget_s=10.0, threads=0):
+    """The reference moe_layer at the K3-class matrix shapes on this host's
+    cores: a 32-expert bank (top-16, so every token still runs 16 experts of
+    7168 x 2048), bounded to about budget_s. Returns (s per token, cores,
+    kind, sample)."""
+    import oracle as O
+    from warp_b200 import synth
+    L = synth.moe_layer(SEED + 50, hidden=K3_HIDDEN, inter=K3_INTER, n_experts=32,
+                        top_k=K3_TOPK, shared_inter=K3_SHARED, routed_scale=K3_SCALE)
+    xs = synth.activations(SEED + 51, K3_HIDDEN, T=8)
+    if O.ref_available():
+        rm = O.RefMoe(L, max_tokens=1, threads=threads)
+        run, kind, cores = rm.layer, "reference", O.ref().refh_pool_threads()
+    else:
+        rm, kind, cores = None, "port", 1
+        run = lambda x: O.moe_layer(L, x)
+    run(xs[0])
+    t0 = time.perf_counter()
+    run(xs[1])
+    per = max(time.perf_counter() - t0, 1e-4)
+    n = max(2, min(200, int(budget_s / per)))
+    t0 = time.perf_counter()
+    for i in range(n):
+        run(xs[i % 8])
+    dt = (time.perf_counter() - t0) / n
+    if rm is not None:
+        rm.close()
+    return dt, cores, kind, (f"{n} single-token calls of the reference moe_layer at hidden "
+                             f"7168 / inter 2048 / top-16 + shared expert, on a 32-expert bank "
+                             f"(the per-token expert work of the 512-expert layer)")
+
+
+def run_k3_reference(args):
+    rank, world, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return 0
+    dt, cores, kind, sample = k3_cpu_sample(max(args.cpu_budget, 5.0))
+    v = 1.0 / dt
+    line = {"metric": K3_METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "k3_class_moe_layer_decode", "hidden": K3_HIDDEN,
+                       "moe_inter": K3_INTER, "experts": K3_EXPERTS, "top_k": K3_TOPK,
+                       "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_k3(args):
+    """Config 4: one K3-class MoE layer per step, batches 1/16/64 tokens.
+    N = 1: the whole layer on one GPU (the batched layer call). N > 1:
+    expert parallel, 512/N experts per rank; batch 1 is held by every rank
+    (replicated trunk: routes agree, partial sums all-reduced through peer
+    memory), larger batches are split B/N tokens per rank (tokens out to
+    every rank, partial sums back to the tokens' ranks)."""
+    import torch
+    import warp_b200 as wb
+    from warp_b200 import synth
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    wb.init(local)
+    E = args.k3_experts
+    first, count = 0, E
+    if world > 1:
+        from warp_b200 import ep
+        ep.setup(rank, world)
+        first, count = ep.ep_range(E, rank, world)
+    nL = args.k3_layers
+    books = synth.codebooks(np.random.default_rng(SEED + 20), 9)
+    wb.codebooks_load_f16(books)
+    rb = synth.record_bytes(K3_INTER, K3_HIDDEN, 3)
+    t_gen = time.perf_counter()
+    chunk = 16
+    for c0 in range(first, first + count, chunk):
+        n = min(chunk, first + count - c0)
+        recs = synth.bank_range(SEED + 30, 1, c0, n, 0, K3_INTER, K3_HIDDEN)
+        for L in range(1, nL + 1):
+            synth.set_layer(recs, L)
+            wb.vq_bank_load(L, E, rb, c0, n, recs.reshape(-1), K3_INTER, K3_HIDDEN, 3)
+        del recs
+    for L in range(1, nL + 1):
+        router, sh = synth.trunk(SEED + 40 + L, K3_HIDDEN, E, K3_SHARED)
+        wb.moe_trunk_load(L, E, K3_HIDDEN, K3_TOPK, 1, K3_SCALE, router, None,
+                          K3_SHARED, sh)
+    t_gen = time.perf_counter() - t_gen
+    s = torch.cuda.Stream(device=dev)
+    ntok = 4
+    results, graphs = {}, []
+    clocks = Clocks(local)
+    clocks.start()
+    expert_b = k3_expert_bytes()
+    router_b, shared_b = k3_trunk_bytes()
+    router_b = router_b * E // K3_EXPERTS
+    for B in [int(b) for b in args.batches.split(",")]:
+        if world > 1 and B > 1 and B % world:
+            continue
+        T = B if (world == 1 or B == 1) else B // world      # tokens this rank passes
+        mode = "single" if world == 1 else ("rep" if B == 1 else "split")
+        xs_h = synth.activations(SEED + 60 + B + (rank if mode == "split" else 0), K3_HIDDEN,
+                                 T=ntok * nL * T).reshape(ntok, nL, T, K3_HIDDEN)
+        xs = torch.from_numpy(xs_h).to(dev)
+        out = torch.empty((nL, T, K3_HIDDEN), dtype=torch.float32, device=dev)
+        Tr = T if mode != "split" else T          # routes returned for this rank's tokens
+        idx = torch.empty((ntok, nL, Tr, K3_TOPK), dtype=torch.int32, device=dev)
+        w = torch.empty((ntok, nL, Tr, K3_TOPK), dtype=torch.float32, device=dev)
+
+        def call(t, L):
+            xp, op = xs[t, L].data_ptr(), out[L].data_ptr()
+            ip, wp = idx[t, L].data_ptr(), w[t, L].data_ptr()
+            if mode == "single":
+                if T == 1:
+                    wb.moe_layer_dev(L + 1, xp, op, ip, wp, s.cuda_stream)
+                else:
+                    wb.moe_layer_part_dev(L + 1, T, xp, op, 0, T, ip, wp, s.cuda_stream)
+            elif mode == "rep":
+                ep.moe_layer_rep_dev(L + 1, T, xp, op, ip, wp, s.cuda_stream)
+            else:
+                ep.moe_layer_dev(L + 1, T, xp, op, ip, wp, s.cuda_stream)
+
+        def step_direct(t):
+            for L in range(nL):
+                call(t, L)
+
+        with torch.cuda.stream(s):
+            for t in range(ntok):
+                step_direct(t)
+        torch.cuda.synchronize()
+        assert wb.device_errors() == 0
+        # distinct experts each call reads on this rank, from the routes
+        ih = idx.cpu().numpy()
+        if mode == "split":           # every rank's tokens reach every rank
+            allr = torch.from_numpy(ih).to(dev)
+            gath = [torch.empty_like(allr) for _ in range(world)]
+            dist.all_gather(gath, allr)
+            ih = np.concatenate([g.cpu().numpy() for g in gath], axis=2)
+        local_e = [np.unique(ih[t, L][(ih[t, L] >= first) & (ih[t, L] < first + count)]).size
+                   for t in range(ntok) for L in range(nL)]
+        ex_rank = float(np.mean(local_e))
+        # per-rank algorithmic bytes of one layer call: local experts, the
+        # replicated router, the shared expert for this rank's share of the
+        # tokens (rounded up: one token's share is a whole read), the tokens
+        sh_tokens = T if mode != "rep" else (rank + 1) * T // world - rank * T // world
+        call_bytes = (ex_rank * expert_b + router_b + (shared_b if sh_tokens else 0)
+                      + 2 * T * K3_HIDDEN * 4)
+        gs = []
+        try:
+            for t in range(ntok):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                    step_direct(t)
+                gs.append(g)
+            graphs.extend(gs)
+            use_graphs = True
+        except Exception as e:
+            print(f"graph capture unavailable: {e}", file=sys.stderr)
+            gs, use_graphs = [], False
+
+        def step(k):
+            if use_graphs:
+                gs[k % ntok].replay()
+            else:
+                step_direct(k % ntok)
+
+        reps = max(1, args.steps // nL)
+        with torch.cuda.stream(s):
+            for k in range(max(args.warmup, 3)):
+                step(k)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        with torch.cuda.stream(s):
+            for k in range(reps):
+                step(k)
+        e1.record(s)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        ms = e0.elapsed_time(e1)
+        my_ms = ms
+        if dist:
+            tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        calls = reps * nL
+        ms_call = ms / calls
+        per_rank_GBps = call_bytes / (my_ms / calls / 1e3) / 1e9
+        # per-kernel device times: one step's launches queued behind a
+        # GPU-side sleep, so each event pair brackets kernel time only
+        wb.profile(True)
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(2e7))
+            step_direct(0)
+        torch.cuda.synchronize()
+        ph = wb.profile_read()
+        wb.profile(False)
+        if dist:
+            dist.barrier()
+        results[B] = {"tokens_per_call": B, "tokens_per_rank": T, "mode": mode,
+                      "ms_per_layer_call": ms_call, "tok_per_s": B / (ms_call / 1e3),
+                      "local_experts_per_call": ex_rank,
+                      "rank0_bytes_per_call": None, "rank0_GBps": None,
+                      "rank0_kernel_us_per_call": {k: v[0] * 1e3 / nL for k, v in ph.items()
+                                                   if v[1]}}
+        # rank 0's own figures (bytes and GB/s over its own time)
+        if rank == 0:
+            results[B]["rank0_bytes_per_call"] = call_bytes
+            results[B]["rank0_GBps"] = per_rank_GBps
+        assert wb.device_errors() == 0
+    ck = clocks.stop()
+    peak, peak_src = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, cores, kind, sample = k3_cpu_sample(args.cpu_budget)
+        cpu = {"value": 1.0 / dt, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
+    if rank == 0:
+        head = results[max(results)]
+        line = {
+            "metric": K3_METRIC, "value": head["tok_per_s"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms_per_layer_call"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded per expert; uniform indices, N(0,0.02^2) codebooks, "
+                    "router rows N(0,1/hidden), bf16-valued N(0,1) tokens)",
+            "config": {"workload": "k3_class_moe_layer_decode", "hidden": K3_HIDDEN,
+                       "moe_inter": K3_INTER, "experts": E, "top_k": K3_TOPK,
+                       "shared_experts": 1, "resident_layers": nL,
+                       "global_batch": max(results), "experts_per_gpu": count,
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "l2": f"steps cycle over {nL} resident layers and 4 token slots "
+                             "(> 126 MB of distinct weights between repeats at the "
+                             "default 4 layers x 512 experts)",
+                       "cuda_graphs": bool(graphs), "setup_s": t_gen},
+            "batches": results,
+            "roofline": {"bound": "hbm", "peak": peak, "peak_source": peak_src,
+                         "unit": "GB/s",
+                         "rank0_frac_by_batch": {b: (r["rank0_GBps"] or 0) / peak
+                                                 for b, r in results.items()}},
+            "clocks": ck,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    graphs.clear()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+        ep.shutdown()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -565,9 +855,18 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--parallel", choices=("ep", "replicas"), default="ep",
                     help="with --gpus N > 1: expert parallel (default) or N replicas")
+    ap.add_argument("--workload", choices=("kimi", "k3"), default="kimi",
+                    help="kimi: the Kimi-Linear decode step (default); k3: one K3-class "
+                         "MoE layer at batches 1/16/64")
+    ap.add_argument("--batches", default="1,16,64", help="k3: global batches")
+    ap.add_argument("--k3-experts", type=int, default=K3_EXPERTS,
+                    help="k3: experts per layer (fewer only for small profiling cases)")
+    ap.add_argument("--k3-layers", type=int, default=K3_LAYERS, help="k3: resident layers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "k3":
+        return run_k3_reference(args) if args.impl == "reference" else run_k3(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_warp(args)

@@ -236,6 +236,15 @@ void waste_cuda_ep_shutdown(void);
 int  waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x,
                                  float *d_out, int *d_idx, float *d_w,
                                  void *stream);
+/* The same layer for a batch that every rank holds (replicated trunk, e.g.
+ * a batch of one): every rank passes the SAME T tokens (1..64), runs its
+ * own experts for all of them, and every rank receives all T outputs, each
+ * the sum of the ranks' partial sums in rank order (NCCL all-reduce on the
+ * fallback path). The shared expert runs once per token, on one rank of a
+ * split of the tokens. d_idx/d_w receive all T routes. */
+int  waste_cuda_ep_moe_layer_rep_dev(int layer, int T, const float *d_x,
+                                     float *d_out, int *d_idx, float *d_w,
+                                     void *stream);
 
 /* Sticky error bits raised on the device. Every wait inside a kernel is
  * bounded; when one runs out, the kernel sets a bit and skips its work
@@ -313,8 +322,8 @@ uint64_t waste_cuda_launch_count(void);
  * and launch counts of up to nphase phases (order below), and resets. Not
  * for use while a stream is being captured into a CUDA graph. */
 enum {
-    WASTE_CUDA_PH_ROUTER = 0,   /* router logits + shared gate/up       */
-    WASTE_CUDA_PH_ROUTE,        /* top-K selection                      */
+    WASTE_CUDA_PH_ROUTER = 0,   /* router logits + shared gate/up + top-K */
+    WASTE_CUDA_PH_ACT,          /* SiLU(g)*u of batched calls            */
     WASTE_CUDA_PH_GATEUP,       /* routed gate/up gathers               */
     WASTE_CUDA_PH_DOWN,         /* SiLU(g)*u, down gathers, shared down */
     WASTE_CUDA_PH_COMBINE,      /* router-order reduce (+ shared)       */

@@ -1,7 +1,8 @@
 """One rank of the two-GPU expert-parallel test (launched by
 tests/test_ep_gpu.py under torchrun): each rank holds half of the experts
-of two layers, decodes its own tokens through the NCCL path, and checks
-them against the oracle on the whole layer."""
+of two layers, decodes its own tokens (and tokens every rank holds)
+through the peer-memory exchange and then the NCCL one, and checks them
+against the oracle on the whole layer."""
 import datetime
 import os
 import sys
@@ -57,6 +58,23 @@ def main():
                     assert np.array_equal(idx[t], ri), (mode, rank, L.layer, t)
                     r = rel_l2(out[t], ro)
                     assert r < TOL, (mode, rank, L.layer, t, r)
+                # the same layer for tokens every rank holds (a batch of one,
+                # then nine: 72 routes, the batched SiLU kernel), interleaved
+                # with the calls above
+                for Tr in (1, 9):
+                    xr = synth.activations(300 + L.layer + rep + Tr, L.hidden, T=Tr)
+                    dx = torch.from_numpy(xr).to(dev)
+                    out = torch.empty((Tr, L.hidden), device=dev)
+                    idx = torch.empty((Tr, L.top_k), dtype=torch.int32, device=dev)
+                    ep.moe_layer_rep_dev(L.layer, Tr, dx.data_ptr(), out.data_ptr(),
+                                         idx.data_ptr())
+                    torch.cuda.synchronize()
+                    out, idx = out.cpu().numpy(), idx.cpu().numpy()
+                    for t in range(Tr):
+                        ro, ri, _ = O.moe_layer(L, xr[t], fma=1)
+                        assert np.array_equal(idx[t], ri), (mode, "rep", rank, L.layer, t)
+                        r = rel_l2(out[t], ro)
+                        assert r < TOL, (mode, "rep", rank, L.layer, t, r)
         assert wb.device_errors() == 0, mode
 
     check("peer memory")                     # the default exchange

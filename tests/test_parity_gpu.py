@@ -235,7 +235,31 @@ def test_moe_layer_k3_shape(cuda_lib):
     yo, route, rws = O.moe_chunk(L0, x, fma=1)
     y = wb.moe_chunk_experts(L.layer, route, rws, x, L.hidden, L.inter)
     assert rel_l2(y, yo) < TOL
+    # five tokens in one device call: the several-token router (groups of
+    # four at this width, then one) and the batched expert tiles
+    _batched_layer_check(wb, L, synth.activations(79, L.hidden, T=5))
     wb.vq_bank_free(L.layer)
+
+
+def _batched_layer_check(wb, L, x):
+    """T tokens through moe_layer_part_dev on a whole bank (shared expert
+    for all of them): each token's route bit-exact, output within TOL."""
+    import torch
+    T = x.shape[0]
+    dev = torch.device("cuda", 0)
+    dx = torch.from_numpy(x).to(dev)
+    o = torch.empty((T, L.hidden), device=dev)
+    i = torch.empty((T, L.top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, L.top_k), device=dev)
+    wb.moe_layer_part_dev(L.layer, T, dx.data_ptr(), o.data_ptr(), 0, T, i.data_ptr(),
+                          w.data_ptr())
+    torch.cuda.synchronize()
+    assert wb.device_errors() == 0
+    o, i = o.cpu().numpy(), i.cpu().numpy()
+    for t in range(T):
+        ro, ri, _ = O.moe_layer(L, x[t], fma=1)
+        assert np.array_equal(i[t], ri), t
+        assert rel_l2(o[t], ro) < TOL, t
 
 
 def test_moe_layer_512_experts_top16(cuda_lib):
@@ -252,4 +276,6 @@ def test_moe_layer_512_experts_top16(cuda_lib):
         ro, ri, _ = O.moe_layer(L, x[t], fma=1)
         assert np.array_equal(idx, ri)
         assert rel_l2(out, ro) < TOL
+    # 17 tokens in one call: router token groups of eight, eight and one
+    _batched_layer_check(wb, L, synth.activations(93, L.hidden, T=17))
     wb.vq_bank_free(L.layer)

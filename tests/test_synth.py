@@ -65,3 +65,25 @@ def test_zipf_routes():
     assert all(len(set(row)) == 8 for row in r)
     counts = np.bincount(r.ravel(), minlength=256)
     assert counts.max() > 10 * np.median(counts[counts > 0])
+
+
+def test_bank_range_splits_agree():
+    """A rank's records are the same bytes whatever the split, carry their
+    global expert ids, and pass the engine's record check."""
+    inter, lat, E = 64, 128, 6
+    L = synth.moe_layer(3, hidden=lat, inter=inter, n_experts=E, top_k=2, shared_inter=0)
+    cb = L.cb_base
+    whole = synth.bank_range(5, L.layer, 0, E, cb, inter, lat)
+    a = synth.bank_range(5, L.layer, 0, 2, cb, inter, lat)
+    b = synth.bank_range(5, L.layer, 2, 4, cb, inter, lat)
+    assert np.array_equal(np.concatenate([a, b]), whole)
+    L.bank = whole.reshape(-1).copy()
+    keep = []
+    s = O._moe_struct(L, keep)
+    for e in range(E):
+        assert synth.parse_header(L.record(e))["expert_id"] == e
+        assert O.lib().orc_record_check(O.C.byref(s), L.layer, e) == 0
+    moved = whole.copy()
+    synth.set_layer(moved, 9)
+    assert all(synth.parse_header(r)["layer"] == 9 for r in moved)
+    assert np.array_equal(moved[:, 48:], whole[:, 48:])

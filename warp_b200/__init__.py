@@ -32,9 +32,10 @@ EXPORTS = (
     "waste_cuda_vq_bank_reserve", "waste_cuda_moe_layer_part_dev",
     "waste_cuda_ep_range", "waste_cuda_ep_unique_id", "waste_cuda_ep_init",
     "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev", "waste_cuda_moe_prefill_dev",
+    "waste_cuda_ep_moe_layer_rep_dev",
 )
 
-PHASES = ("router", "route", "gateup", "down", "combine", "matvec", "matvec_reduce")
+PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
 
 OK, E_ARG, E_DEVICE, E_RECORD, E_NOBANK, E_NOMEM, E_NODEV = 0, -1, -2, -3, -4, -5, -6
 
@@ -127,6 +128,7 @@ def load_library() -> C.CDLL:
         "waste_cuda_ep_init": (C.c_int, [C.c_int, C.c_int, P, C.c_size_t]),
         "waste_cuda_ep_shutdown": (None, []),
         "waste_cuda_ep_moe_layer_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_ep_moe_layer_rep_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_moe_prefill_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():

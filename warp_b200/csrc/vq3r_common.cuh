@@ -345,12 +345,14 @@ struct GatherSmem {
     int n, first;             /* positions [first, first+n) of the slice */
     uint64_t *bar0, *bar1;
     int split;
+    uint32_t par;             /* barrier phase parity of this staging round */
     bool ok;
 
     __device__ __forceinline__ void begin(const uint8_t *p0, int nvv)
     {
         p = p0;
         n = nvv;
+        par = 0;
         ok = true;
     }
 
@@ -358,18 +360,18 @@ struct GatherSmem {
     {
         const int stride = kBlock * ST;
         if (bar1 == nullptr) {
-            ok = mbar_wait(bar0, 0);
+            ok = mbar_wait(bar0, par);
             if (ok) gather_smem<ST>(acc, p, stride, L, n);
             return;
         }
         const int n0 = max(0, min(n, split - first));
         if (n0 > 0) {
-            ok = mbar_wait(bar0, 0);
+            ok = mbar_wait(bar0, par);
             if (!ok) return;
             gather_smem<ST>(acc, p, stride, L, n0);
         }
         if (n0 < n) {
-            ok = mbar_wait(bar1, 0);
+            ok = mbar_wait(bar1, par);
             if (!ok) return;
             gather_smem<ST>(acc, p + (size_t)n0 * stride, stride, L + (size_t)n0 * ST * kEntries,
                             n - n0);

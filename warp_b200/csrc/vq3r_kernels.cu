@@ -164,7 +164,8 @@ TileGeom make_geom(int M, int N, int nmat, int Vs, int stages, int target_thread
     g.nlanes = nl;
     g.threads = ((g.Q * nl + 31) / 32) * 32;
     const size_t lut = (size_t)g.Vs * stages * kEntries;
-    const size_t red = (size_t)nl * g.EG * g.nrb * kBlock;
+    /* the lane reduction reuses the table region; one lane needs none */
+    const size_t red = nl > 1 ? (size_t)nl * g.EG * g.nrb * kBlock : 0;
     size_t region = lut > red ? lut : red;
     if (region < (size_t)2 * g.threads) region = (size_t)2 * g.threads;  /* down prologue */
     g.region = (region + 3) & ~(size_t)3;
@@ -515,8 +516,9 @@ __device__ __forceinline__ bool ep_wait_all(const unsigned int *flags, int world
     return true;
 }
 
-/* Layer start: this rank's T tokens into every rank's mailbox, then the
- * x flag of this rank, at the new epoch, in every mailbox. One block. */
+/* Layer start: this rank's T tokens into every rank's mailbox (not with
+ * rep: every rank has them already), then the x flag of this rank, at the
+ * new epoch, in every mailbox. One block. */
 __global__ void __launch_bounds__(256) ep_publish_kernel(wc_ep_link l, const float *x)
 {
     __shared__ unsigned int e;
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(256) ep_publish_kernel(wc_ep_link l, const flo
     __syncthreads();
     const size_t n4 = (size_t)l.T * l.hidden / 4, off = (size_t)l.rank * l.T * l.hidden;
     const float4 *src = reinterpret_cast<const float4 *>(x);
-    for (size_t i = threadIdx.x; i < n4; i += blockDim.x) {
+    for (size_t i = threadIdx.x; i < (l.rep ? 0 : n4); i += blockDim.x) {
         const float4 v = src[i];
         for (int r = 0; r < l.world; r++) reinterpret_cast<float4 *>(ep_x(l, r) + off)[i] = v;
     }
@@ -860,6 +862,209 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     }
 }
 
+/* The router for several tokens (T >= 2): a block holds TB tokens' x in
+ * shared memory and streams its weight rows once for all of them (the
+ * single-token kernel re-reads every row per token). Router blocks take rw
+ * rows per warp, shared blocks 2*rw Q8G rows per warp. Each dot product
+ * keeps the single-token kernel's order (four quarter rows, lane-strided
+ * FMA chains, warp sums, then ((q0+q1)+q2)+q3; per Q8G group the scale
+ * times the group's products), so both kernels give the same logits. The
+ * last block of a token group routes its tokens, one warp each. */
+constexpr int kRouterTB = 8;           /* tokens per block, at most */
+constexpr int kRtChunk = 8;            /* router weight float4 loads in flight per lane */
+constexpr int kShChunk = 16;           /* shared-expert weight words in flight per lane */
+
+struct RouterTGeom {
+    int rblocks, sblocks, rw, TB;
+};
+
+__host__ inline RouterTGeom router_t_geom(int E, int si, int T, int lat)
+{
+    RouterTGeom g;
+    int tb = (int)((112 * 1024) / ((size_t)lat * 4));
+    tb = tb < 1 ? 1 : (tb > kRouterTB ? kRouterTB : tb);
+    g.TB = tb < T ? tb : T;
+    const int groups = (T + g.TB - 1) / g.TB;
+    const int warps = kRouterBlock / 32;
+    g.rw = 1;
+    for (int rw = 4; rw > 1; rw /= 2) {     /* fewer, longer blocks while >= 4 per SM */
+        const int rb = (E + warps * rw - 1) / (warps * rw);
+        const int sb = (2 * si + warps * 2 * rw - 1) / (warps * 2 * rw);
+        if ((rb + sb) * groups >= 4 * 148) { g.rw = rw; break; }
+    }
+    g.rblocks = (E + warps * g.rw - 1) / (warps * g.rw);
+    g.sblocks = (2 * si + warps * 2 * g.rw - 1) / (warps * 2 * g.rw);
+    return g;
+}
+
+template <int NK>
+__global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args a, RouterTGeom rg)
+{
+    extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ unsigned int ticket;
+    __shared__ int ep_fail;
+    if (threadIdx.x == 0) ep_fail = 0;
+    pdl_trigger();
+    const int lat = a.bank.lat, n4 = lat / 4, ng = (lat + 127) / 128;
+    const int t0 = blockIdx.y * rg.TB, nt = min(rg.TB, a.T - t0);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int warps = kRouterBlock / 32;
+    const int b = blockIdx.x;
+    const bool is_router = b < rg.rblocks;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smraw);
+    float *xs = reinterpret_cast<float *>(smraw + 16);
+    /* this warp's rows: router rows [r0, r1) or shared rows [r0, r1) of the
+     * 2*si gate-then-up rows */
+    const int rpw = is_router ? rg.rw : 2 * rg.rw;
+    const int nrows = is_router ? a.E : 2 * a.si;
+    const int rb0 = (is_router ? b : b - rg.rblocks) * warps * rpw;
+    const int r0 = min(nrows, rb0 + warp * rpw), r1 = min(nrows, r0 + rpw);
+    /* tokens of the group that get the shared expert here */
+    const int ts0 = max(0, a.sh_t0 - t0), ts1 = min(nt, a.sh_t1 - t0);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    /* the block's weight rows into L2 while the previous kernel finishes */
+    if (lane == 0 && r1 > r0) {
+        if (is_router) {
+            l2_prefetch(a.router + (size_t)r0 * lat, (size_t)(r1 - r0) * lat * 4);
+        } else if (ts1 > ts0) {
+            for (int r = r0; r < r1; r++)
+                l2_prefetch((r < a.si ? a.shg + (size_t)r * ng * 128
+                                      : a.shu + (size_t)(r - a.si) * ng * 128), (size_t)ng * 128);
+        }
+    }
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        if (a.ep.on) {            /* every rank's tokens are in this mailbox */
+            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err))
+                ep_fail = 1;
+            asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
+        }
+        mbar_expect_tx(bar, (uint32_t)nt * lat * 4);
+        bulk_g2s(xs, a.x + (size_t)t0 * lat, (uint32_t)nt * lat * 4, bar);
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(bar, 0) && !ep_fail;
+    if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    if (ok && is_router) {
+        const int per = (n4 + kRouterSplit - 1) / kRouterSplit;
+        for (int r = r0; r < r1; r++) {
+            const float4 *w4 = reinterpret_cast<const float4 *>(a.router + (size_t)r * lat);
+            float res[kRouterTB];
+#pragma unroll
+            for (int k = 0; k < kRouterTB; k++) res[k] = 0.0f;
+            for (int qtr = 0; qtr < kRouterSplit; qtr++) {
+                const int q0 = qtr * per, q1 = min(n4, q0 + per);
+                float acc[kRouterTB];
+#pragma unroll
+                for (int k = 0; k < kRouterTB; k++) acc[k] = 0.0f;
+                /* chunks of kRtChunk weight loads in flight at once; the
+                 * FMA chain still runs over i ascending */
+                for (int base = q0 + lane; base < q1; base += 32 * kRtChunk) {
+                    float4 wv[kRtChunk];
+#pragma unroll
+                    for (int c = 0; c < kRtChunk; c++) {
+                        const int i = base + 32 * c;
+                        wv[c] = i < q1 ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int c = 0; c < kRtChunk; c++) {
+                        const int i = base + 32 * c;
+                        if (i >= q1) break;
+                        const float4 w = wv[c];
+#pragma unroll
+                        for (int k = 0; k < kRouterTB; k++) {
+                            if (k < nt) {
+                                const float4 xv = x4[(size_t)k * n4 + i];
+                                acc[k] = fmaf(w.x, xv.x, acc[k]); acc[k] = fmaf(w.y, xv.y, acc[k]);
+                                acc[k] = fmaf(w.z, xv.z, acc[k]); acc[k] = fmaf(w.w, xv.w, acc[k]);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < kRouterTB; k++) {
+                    if (k < nt) {             /* block-uniform */
+                        const float q = warp_sum(acc[k]);
+                        res[k] = qtr == 0 ? q : res[k] + q;
+                    }
+                }
+            }
+            if (lane == 0)
+                for (int k = 0; k < nt; k++) a.ws.logits[(size_t)(t0 + k) * a.E + r] = res[k];
+        }
+    } else if (ok && ts1 > ts0) {
+        for (int r = r0; r < r1; r++) {
+            const int kind = r >= a.si, o = kind ? r - a.si : r;
+            const uint8_t *row = reinterpret_cast<const uint8_t *>(kind ? a.shu : a.shg) +
+                                 (size_t)o * ng * 128;
+            const uint16_t *srow = (kind ? a.shu_s : a.shg_s) + (size_t)o * ng;
+            float acc[kRouterTB];
+#pragma unroll
+            for (int k = 0; k < kRouterTB; k++) acc[k] = 0.0f;
+            for (int gb = 0; gb < ng; gb += kShChunk) {
+                uint32_t wv[kShChunk];
+                uint16_t sv[kShChunk];
+#pragma unroll
+                for (int c = 0; c < kShChunk; c++) {
+                    const int gi = gb + c, i = gi * 128 + lane * 4;
+                    wv[c] = (gi < ng && i < lat)
+                                ? __ldg(reinterpret_cast<const unsigned int *>(row + i)) : 0u;
+                    sv[c] = gi < ng ? __ldg(srow + gi) : (uint16_t)0;
+                }
+#pragma unroll
+                for (int c = 0; c < kShChunk; c++) {
+                    const int gi = gb + c, i = gi * 128 + lane * 4;
+                    if (gi >= ng) break;
+                    if (i >= lat) continue;
+                    const uint32_t w = wv[c];
+                    const float sc = f16_keep(sv[c]);
+                    const float w0 = (float)(int8_t)(w & 0xff), w1 = (float)(int8_t)((w >> 8) & 0xff);
+                    const float w2 = (float)(int8_t)((w >> 16) & 0xff), w3 = (float)(int8_t)(w >> 24);
+#pragma unroll
+                    for (int k = 0; k < kRouterTB; k++) {
+                        if (k >= ts0 && k < ts1) {
+                            const float4 xv = *reinterpret_cast<const float4 *>(xs + (size_t)k * lat + i);
+                            float part = w0 * xv.x;
+                            part = fmaf(w1, xv.y, part);
+                            part = fmaf(w2, xv.z, part);
+                            part = fmaf(w3, xv.w, part);
+                            acc[k] = fmaf(sc, part, acc[k]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kRouterTB; k++) {
+                if (k >= ts0 && k < ts1) {    /* block-uniform */
+                    const float v = warp_sum(acc[k]);
+                    if (lane == 0) (kind ? a.ws.sh_u : a.ws.sh_g)[(size_t)(t0 + k) * a.si + o] = v;
+                }
+            }
+        }
+    }
+    /* the last block of this token group routes it (ordering as in the
+     * single-token kernel: writes, barrier, acq_rel ticket) */
+    __syncthreads();
+    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(a.ws.tickets + t0, 1u);
+    __syncthreads();
+    if (ticket != gridDim.x - 1) return;
+    if (warp < nt) route_warp<NK>(a, t0 + warp, lane);
+    for (int k = ts0; k < ts1; k++) {
+        const size_t tb = (size_t)(t0 + k) * a.si;
+        for (int i = threadIdx.x; i < a.si; i += blockDim.x)
+            a.ws.sh_h[tb + i] = silu_ref(__ldcg(a.ws.sh_g + tb + i)) * __ldcg(a.ws.sh_u + tb + i);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        a.ws.tickets[t0] = 0;                          /* ready for the next launch */
+        for (int k = 0; k < nt; k++) st_release(a.ws.route_flag + t0 + k, 1u);
+    }
+}
+
 /* The record of routed expert j of token t (ids are global; a bank may hold
  * a contiguous subset starting at `first`). */
 __device__ __forceinline__ const uint8_t *expert_rec(const wc_bank &bk, const int *idx,
@@ -937,15 +1142,23 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
     }
     pdl_trigger();
     /* the group's route slots: slots j0.. of the token, or, with a partial
-     * bank, the group's share of the slots whose experts are held here */
-    const int j0 = grp * g.EG;
+     * bank, the token's slots whose experts are held here, compacted; then
+     * the tile takes groups grp, grp + groups, ... of them in rounds, with
+     * one table (one lane of threads: the table is never reused as the lane
+     * reduction) */
+    int j0 = grp * g.EG;
     int nm;
     if (route_first) {
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < 32) {                 /* one warp reads the routes at once */
             int n = 0;
-            for (int j = 0; j < a.K; j++)
-                if (expert_here(a, idx, a.K, t, j)) s_slot[n++] = j;
-            s_nloc = n;
+            for (int jb = 0; jb < a.K; jb += 32) {
+                const int j = jb + (int)threadIdx.x;
+                const bool hj = j < a.K && expert_here(a, idx, a.K, t, j);
+                const unsigned mk = __ballot_sync(0xffffffffu, hj);
+                if (hj) s_slot[n + __popc(mk & ((1u << threadIdx.x) - 1u))] = j;
+                n += __popc(mk);
+            }
+            if (threadIdx.x == 0) s_nloc = n;
         }
         __syncthreads();
         if (j0 >= s_nloc) return;               /* uniform: no local expert left */
@@ -960,12 +1173,12 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         if ((int)threadIdx.x < nm) s_slot[j0 + threadIdx.x] = j0 + threadIdx.x;
         __syncthreads();
     }
+    for (uint32_t round = 0;; round++) {
     const int *slot = s_slot + j0;              /* matrix m is route slot slot[m] */
     /* stage the group's index streams for this slice: (matrix, row block)
      * runs of nvs positions, in halves [0,h) and [h,nvs); matrices of
-     * experts held by another rank are neither staged nor gathered */
-    /* matrices whose experts another device holds are neither staged nor
-     * gathered (route-first groups hold only local slots) */
+     * experts held by another rank are neither staged nor gathered
+     * (route-first groups hold only local slots) */
     uint32_t here = 0;
     for (int mm = 0; mm < nm; mm++)
         if (route_first || expert_here(a, idx, a.K, t, slot[mm])) here |= 1u << mm;
@@ -1007,7 +1220,7 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         bulk_g2s(dst, src, h * psz, &sm.bars[0]);
         if (nvs > h) bulk_g2s(dst + (size_t)h * psz, src + (size_t)h * psz, (nvs - h) * psz, &sm.bars[1]);
     }
-    if (threadIdx.x == 0 && t == 0 && a.prefetch_down) {
+    if (threadIdx.x == 0 && t == 0 && round == 0 && a.prefetch_down) {
         /* this block's share of the routed experts' down index streams:
          * L2 fetches them while the gathers below keep HBM idle */
         const size_t per = bk.scale_off - bk.down_off;
@@ -1040,9 +1253,35 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         th.G.bar1 = nvs > h ? &sm.bars[1] : nullptr;
     }
     th.G.split = h;
+    th.G.par = round & 1u;
     __syncthreads();                 /* the table */
     float *out = a.ws.p_gu + ((((size_t)t * 2 + kind) * g.ns + slice) * a.K) * bk.inter;
     th.finish(gs, sm.lut, out, bk.inter, nm, slot);
+    if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    if (!route_first || g.nlanes != 1) break;
+    j0 += g.groups * g.EG;
+    if (j0 >= s_nloc) break;         /* uniform */
+    nm = min(g.EG, s_nloc - j0);
+    __syncthreads();                 /* every gather is done with the staged streams */
+    }
+}
+
+/* The down tile's gathers once its table is built: one partial sum per
+ * output row of the slice. */
+template <int ST>
+__device__ __forceinline__ void down_gather(const wc_moe_args &a, const TileGeom &g, TileSmem &sm,
+                                            int t, int j, int slice, int nvs)
+{
+    TileGeom gs = g;                 /* the staged view: positions [0, nvs) */
+    gs.nv = nvs;
+    gs.Vs = nvs;
+    TileThread<ST, GatherSmem<ST>> th(gs, 0, 1, sm.stage);
+    th.G.first = th.vl0;
+    th.G.bar0 = &sm.bars[0];
+    th.G.bar1 = nullptr;
+    th.G.split = nvs;
+    float *out = a.ws.p_d + (((size_t)t * a.K + j) * g.ns + slice) * a.bank.lat;
+    th.finish(gs, sm.lut, out, 0, 1);
     if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
 }
 
@@ -1158,13 +1397,23 @@ down_kernel(const __grid_constant__ wc_moe_args a, TileGeom gu, TileGeom g, int 
     const int inter = bk.inter;
     const uint16_t *sc = reinterpret_cast<const uint16_t *>(rec + bk.scale_off);
     float sg_scale = 0.0f, su_scale = 0.0f;
-    if ((int)threadIdx.x < nin) {
+    if ((int)threadIdx.x < nin && !a.act_pre) {
         const int n = v0 * kVecDim + threadIdx.x;
         sg_scale = f16_keep(ld_pin_u16(sc + n));
         su_scale = f16_keep(ld_pin_u16(sc + inter + n));
     }
     pdl_trigger();
-    pdl_wait();                      /* gate/up partials are complete */
+    pdl_wait();                      /* gate/up partials (or h) are complete */
+    if (a.act_pre) {                 /* SiLU(g)*u of this slice, computed once */
+        if ((int)threadIdx.x < nin)
+            xs[threadIdx.x] = __ldcg(a.ws.h + ((size_t)t * a.K + j) * inter + v0 * kVecDim +
+                                     threadIdx.x);
+        __syncthreads();
+        books.build(lut, xs, nvs);
+        __syncthreads();
+        down_gather<ST>(a, g, sm, t, j, slice, nvs);
+        return;
+    }
     const size_t sstride = (size_t)a.K * inter;
     const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * sstride + (size_t)j * inter;
     const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * sstride + (size_t)j * inter;
@@ -1205,17 +1454,55 @@ down_kernel(const __grid_constant__ wc_moe_args a, TileGeom gu, TileGeom g, int 
     __syncthreads();
     books.build(lut, xs, nvs);
     __syncthreads();
-    TileGeom gs = g;                 /* the staged view: positions [0, nvs) */
-    gs.nv = nvs;
-    gs.Vs = nvs;
-    TileThread<ST, GatherSmem<ST>> th(gs, 0, 1, sm.stage);
-    th.G.first = th.vl0;
-    th.G.bar0 = &sm.bars[0];
-    th.G.bar1 = nullptr;
-    th.G.split = nvs;
-    float *out = a.ws.p_d + (((size_t)t * a.K + j) * g.ns + slice) * bk.lat;
-    th.finish(gs, lut, out, 0, 1);
-    if (th.active && !th.G.ok) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    down_gather<ST>(a, g, sm, t, j, slice, nvs);
+}
+
+/* SiLU(g)*u for every (token, routed expert) of a batched call, once, in
+ * the down tiles' arithmetic: the gate/up slice sums in P parts (part p:
+ * slices p, p+P, ... ascending, the first kDnSlices of them padded with
+ * zeros), the parts in order, then the f16 row scales. P is what the down
+ * tile holding input n uses: its threads over its inputs. grid
+ * (ceil(inter/256), T*K). */
+template <int ST>
+__global__ void __launch_bounds__(256) act_kernel(const __grid_constant__ wc_moe_args a,
+                                                  TileGeom gu, TileGeom d, const int *idx)
+{
+    pdl_trigger();                   /* the down tiles stage their streams meanwhile */
+    const wc_bank &bk = a.bank;
+    const int pair = blockIdx.y, t = pair / a.K, j = pair % a.K;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int inter = bk.inter;
+    pdl_wait();                      /* gate/up partials are complete */
+    if (n >= inter || !expert_here(a, idx, a.K, t, j)) return;
+    const int dsl = n / (d.Vs * kVecDim);
+    const int nin = min(d.Vs, d.nv - dsl * d.Vs) * kVecDim;
+    const int P = max(1, d.threads / nin);
+    const size_t sstride = (size_t)a.K * inter;
+    const float *pg = a.ws.p_gu + (((size_t)t * 2 + 0) * gu.ns) * sstride + (size_t)j * inter + n;
+    const float *pu = a.ws.p_gu + (((size_t)t * 2 + 1) * gu.ns) * sstride + (size_t)j * inter + n;
+    float sg = 0.0f, su = 0.0f;
+    for (int p = 0; p < P; p++) {
+        float vg[kDnSlices], vu[kDnSlices];
+#pragma unroll
+        for (int k = 0; k < kDnSlices; k++) {
+            const int s2 = p + k * P;
+            vg[k] = s2 < gu.ns ? __ldcg(pg + (size_t)s2 * sstride) : 0.0f;
+            vu[k] = s2 < gu.ns ? __ldcg(pu + (size_t)s2 * sstride) : 0.0f;
+        }
+        float g = 0.0f, u = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kDnSlices; k++) { g += vg[k]; u += vu[k]; }
+        for (int s2 = p + kDnSlices * P; s2 < gu.ns; s2 += P) {
+            g += __ldcg(pg + (size_t)s2 * sstride);
+            u += __ldcg(pu + (size_t)s2 * sstride);
+        }
+        sg += g;
+        su += u;
+    }
+    const uint16_t *sc = reinterpret_cast<const uint16_t *>(expert_rec(bk, idx, a.K, t, j) +
+                                                           bk.scale_off);
+    const float gs = f16_keep(ld_pin_u16(sc + n)), us = f16_keep(ld_pin_u16(sc + inter + n));
+    a.ws.h[(size_t)pair * inter + n] = silu_ref(sg * gs) * (su * us);
 }
 
 /* ---- 4. combine --------------------------------------------------------------
@@ -1317,9 +1604,12 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         if (sh_here) y = __fadd_rn(y, shv);
         if (!a.ep.on) {
             a.out[(size_t)t * bk.lat + i] = y;
-        } else {                  /* straight into the token's rank, over NVLink */
+        } else if (!a.ep.rep) {   /* straight into the token's rank, over NVLink */
             const int owner = t / a.ep.T, tl = t % a.ep.T;
             ep_part(a.ep, owner)[((size_t)a.ep.rank * a.ep.T + tl) * a.ep.hidden + i] = y;
+        } else {                  /* every rank holds the token: to all of them */
+            for (int r = 0; r < a.ep.world; r++)
+                ep_part(a.ep, r)[((size_t)a.ep.rank * a.ep.T + t) * a.ep.hidden + i] = y;
         }
     }
     if (!a.ep.on) return;
@@ -1339,7 +1629,15 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         st_release_sys(ep_pflags(a.ep, threadIdx.x) + a.ep.rank, *ep_epoch(a.ep));
 }
 
-constexpr int kVsGateUp = WC_VS_GATEUP;
+/* Positions per gate/up tile: each slice's partial sums are written and
+ * summed again by the down tiles, so wide experts take longer slices. */
+extern "C" int wc_vs_gateup(int lat)
+{
+    /* 7168-wide experts: 224 slices of 4 positions would write and re-read
+     * 3.7 MB of partial sums per (token, expert); 8 positions halve that
+     * and the staged streams still fit (128 row blocks x 8 x 192 B) */
+    return lat >= 4096 ? 2 * WC_VS_GATEUP : WC_VS_GATEUP;
+}
 constexpr int kVsDown = WC_VS_DOWN;
 
 struct MoeGeom {
@@ -1378,10 +1676,14 @@ MoeGeom moe_geom(const wc_moe_args *a)
         /* one lane per quarter block: small tiles, many per SM, and the
          * empty ones retire right after the route */
         const int q = a->gu_eg * ((b.inter + kBlock - 1) / kBlock) * 4;
-        m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, kVsGateUp, b.stages, q), b.stages);
-        m.gu.groups = (a->K + m.gu.EG - 1) / m.gu.EG;
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, wc_vs_gateup(b.lat), b.stages, q), b.stages);
+        /* tiles for the expected local count; a tile takes further groups
+         * in rounds when a token has more (one lane: the table survives),
+         * else every group gets its own tile */
+        m.gu.groups = m.gu.nlanes == 1 ? (a->gu_eg + m.gu.EG - 1) / m.gu.EG
+                                       : (a->K + m.gu.EG - 1) / m.gu.EG;
     } else {
-        m.gu = with_stage(make_geom(b.inter, b.lat, a->K, kVsGateUp, b.stages, 512), b.stages);
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->K, wc_vs_gateup(b.lat), b.stages, 512), b.stages);
     }
     m.d = with_stage(make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448), b.stages);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
@@ -1455,7 +1757,20 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         /* programmatic launch: the router's weight copies overlap whatever
          * kernel precedes it in the stream (the previous layer's combine) */
         const bool rpdl = !P.on;
-        if (a->E <= 256)
+        if (a->T >= 2) {             /* several tokens: weights read once per group */
+            const RouterTGeom tg = router_t_geom(a->E, a->si, a->T, a->bank.lat);
+            const size_t tsm = 16 + (size_t)tg.TB * a->bank.lat * 4;
+            const dim3 tgrid(tg.rblocks + tg.sblocks, (a->T + tg.TB - 1) / tg.TB);
+            cudaFuncSetAttribute(router_tokens_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm);
+            cudaFuncSetAttribute(router_tokens_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm);
+            cudaFuncSetAttribute(router_tokens_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm);
+            if (a->E <= 256)
+                e = launch(router_tokens_kernel<8>, tgrid, dim3(kRouterBlock), tsm, s, rpdl, *a, tg);
+            else if (a->E <= 512)
+                e = launch(router_tokens_kernel<16>, tgrid, dim3(kRouterBlock), tsm, s, rpdl, *a, tg);
+            else
+                e = launch(router_tokens_kernel<32>, tgrid, dim3(kRouterBlock), tsm, s, rpdl, *a, tg);
+        } else if (a->E <= 256)
             e = launch(router_kernel<8>, rgrid, dim3(kRouterBlock), rsm, s, rpdl, *a, rg);
         else if (a->E <= 512)
             e = launch(router_kernel<16>, rgrid, dim3(kRouterBlock), rsm, s, rpdl, *a, rg);
@@ -1476,6 +1791,19 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
                pdl && !prof, *a, m.gu, idx);
     prof_end(pe, s);
     if (e != cudaSuccess) return (int)e;
+    /* batched calls: SiLU(g)*u once per (token, expert) instead of in
+     * every down tile, whose prologue would otherwise wait on ns_gu
+     * partial sums per input */
+    wc_moe_args da = *a;
+    da.act_pre = a->T * a->K >= 64;
+    if (da.act_pre) {
+        pe = prof_begin(WC_PH_ACT, s);
+        e = launch(act_kernel<ST>, dim3((a->bank.inter + 255) / 256, a->T * a->K), dim3(256), 0,
+                   s, !prof, da, m.gu, m.d, idx);
+        prof_end(pe, s);
+        g_launches += 1;
+        if (e != cudaSuccess) return (int)e;
+    }
     size_t dsm = m.d.smem;
     if (a->router && a->si > 0) {
         const size_t shm = shared_down_smem(m.d.threads, m.sh_rows_pw, a->si);
@@ -1484,7 +1812,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
     cudaFuncSetAttribute(down_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm);
     pe = prof_begin(WC_PH_DOWN, s);
     e = launch(down_kernel<ST>, dim3(m.d_tiles + (a->router ? m.sh_blocks : 0)),
-               dim3(m.d.threads), dsm, s, !prof, *a, m.gu, m.d, m.d_tiles, m.sh_rows_pw, idx);
+               dim3(m.d.threads), dsm, s, !prof, da, m.gu, m.d, m.d_tiles, m.sh_rows_pw, idx);
     prof_end(pe, s);
     if (e != cudaSuccess) return (int)e;
     wc_moe_args ca = *a;
@@ -1503,20 +1831,21 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
 extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
                                    int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
+    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat), stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     size_t n = 0;
     n += (size_t)T * 2 * gu.ns * K * inter;
     n += (size_t)T * K * d.ns * lat;
     n += (size_t)T * E;
     n += (size_t)T * si * 3 + (size_t)T * lat;
+    n += (size_t)T * K * inter;              /* h */
     return n + 256 + 64;                     /* + control words */
 }
 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
                                 int lat, int inter, int si, int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, K, kVsGateUp, stages, 512);
+    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat), stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     float *p = base;
     /* control words first (zeroed once at allocation, self-resetting):
@@ -1532,7 +1861,8 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     ws->sh_g = p; p += (size_t)T * si;
     ws->sh_u = p; p += (size_t)T * si;
     ws->sh_h = p; p += (size_t)T * si;
-    ws->sh_out = p;
+    ws->sh_out = p; p += (size_t)T * lat;
+    ws->h = p;
 }
 
 extern "C" int wc_moe_supported(const wc_moe_args *a)

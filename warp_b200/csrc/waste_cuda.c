@@ -513,8 +513,9 @@ static void bank_tensor_maps(wc_bank *kb)
     if (!enc) return;
     const int nv_gu = kb->lat / 8, nrb_gu = (kb->inter + 63) / 64;
     const int nv_d = kb->inter / 8, nrb_d = (kb->lat + 63) / 64;
-    if (nv_gu % WC_VS_GATEUP || nv_d % WC_VS_DOWN || nrb_gu % 2 || nrb_gu / 2 > 256 ||
-        nrb_d > 256 || WC_VS_DOWN * 24 > 256 || kb->stages != 3)
+    const int vs_gu = wc_vs_gateup(kb->lat);
+    if (nv_gu % vs_gu || nv_d % WC_VS_DOWN || nrb_gu % 2 || nrb_gu / 2 > 256 ||
+        nrb_d > 256 || WC_VS_DOWN * 24 > 256 || vs_gu * 24 > 256 || kb->stages != 3)
         return;
     const uint32_t off[3] = { kb->gate_off, kb->up_off, kb->down_off };
     for (int k = 0; k < 3; k++) {
@@ -522,7 +523,7 @@ static void bank_tensor_maps(wc_bank *kb)
         const cuuint64_t dims[3] = { (cuuint64_t)nv * 24, (cuuint64_t)nrb,
                                      (cuuint64_t)kb->n_experts };
         const cuuint64_t strides[2] = { (cuuint64_t)nv * 192, (cuuint64_t)kb->rec_bytes };
-        const cuuint32_t box[3] = { (cuuint32_t)(k < 2 ? WC_VS_GATEUP : WC_VS_DOWN) * 24,
+        const cuuint32_t box[3] = { (cuuint32_t)(k < 2 ? vs_gu : WC_VS_DOWN) * 24,
                                     (cuuint32_t)(k < 2 ? nrb / 2 : nrb), 1 };
         const cuuint32_t estr[3] = { 1, 1, 1 };
         void *base = (void *)(kb->base + off[k]);
@@ -1234,8 +1235,11 @@ void waste_cuda_ep_shutdown(void)
     pthread_mutex_unlock(&g_mu);
 }
 
-int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out, int *d_idx,
-                                float *d_w, void *stream)
+/* Both expert-parallel layer calls. rep = 0: each rank brings its own T
+ * tokens and receives their outputs. rep = 1: every rank brings the same T
+ * tokens and receives all of their outputs. */
+static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx, float *d_w,
+                    void *stream, int rep)
 {
     int rc = 0;
     wc_moe_args a;
@@ -1243,7 +1247,8 @@ int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out
     if (!d_x || !d_out || T <= 0) return fail(WASTE_CUDA_E_ARG, "ep_moe_layer: bad arguments");
     pthread_mutex_lock(&g_mu);
     if (!EP.active) { rc = fail(WASTE_CUDA_E_ARG, "ep_moe_layer before ep_init"); goto out; }
-    const int Ta = T * EP.world;
+    const int Ta = rep ? T : T * EP.world;
+    const int tr = rep ? 0 : EP.rank;            /* this rank's tokens in the routes */
     if ((rc = layer_args(layer, Ta, 1, &a, &L))) goto out;
     {
         int r0, rn;
@@ -1279,42 +1284,65 @@ int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out
         lk.world = EP.world;
         lk.T = T;
         lk.hidden = L->hidden;
+        lk.rep = rep;
         memcpy(lk.mail, EP.mail, sizeof lk.mail);
         CK((cudaError_t)wc_ep_publish_launch(&lk, d_x, a.ws.err, st), "ep publish");
-        a.x = (const float *)(EP.mail[EP.rank] + WC_EP_MAIL_HDR);
+        a.x = rep ? d_x : (const float *)(EP.mail[EP.rank] + WC_EP_MAIL_HDR);
         a.out = EP.d_outall;
         a.idx_out = S.d_idx;
         a.w_out = S.d_w;
-        a.sh_t0 = EP.rank * T;
-        a.sh_t1 = EP.rank * T + T;
         a.ep = lk;
-        if (a.gu_eg == 0) a.gu_eg = L->top_k;   /* route-first: x arrives with the route */
-        CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
-        CK((cudaError_t)wc_ep_finalize_launch(&lk, d_out, a.ws.err, st), "ep finalize");
-        if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)EP.rank * kb, kb * sizeof(int),
-                                      cudaMemcpyDeviceToDevice, st), "route copy");
-        if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)EP.rank * kb, kb * sizeof(float),
-                                    cudaMemcpyDeviceToDevice, st), "weight copy");
-        goto out;
+        if (a.gu_eg == 0)     /* route-first (x arrives with the route), tiles
+                                 for the expected local count */
+            a.gu_eg = (int)(((long)L->top_k * L->kb.n_experts + L->n_total - 1) / L->n_total);
+    } else if (!rep) {
+        const ncclResult_t r = EP.all_gather(d_x, EP.d_xall, per, ncclFloat32, EP.comm, st);
+        if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllGather"); goto out; }
+        a.x = EP.d_xall;
+        a.out = EP.d_outall;
+        a.idx_out = S.d_idx;
+        a.w_out = S.d_w;
+    } else {
+        a.x = d_x;
+        a.out = EP.d_outall;
+        a.idx_out = S.d_idx;
+        a.w_out = S.d_w;
     }
-    ncclResult_t r = EP.all_gather(d_x, EP.d_xall, per, ncclFloat32, EP.comm, st);
-    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllGather"); goto out; }
-    a.x = EP.d_xall;
-    a.out = EP.d_outall;
-    a.idx_out = S.d_idx;
-    a.w_out = S.d_w;
-    a.sh_t0 = EP.rank * T;            /* the shared expert once, on the token's rank */
-    a.sh_t1 = EP.rank * T + T;
+    /* the shared expert once per token: on the token's rank, or (rep) on
+     * one rank of a split of the tokens */
+    a.sh_t0 = rep ? EP.rank * T / EP.world : EP.rank * T;
+    a.sh_t1 = rep ? (EP.rank + 1) * T / EP.world : EP.rank * T + T;
     CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
-    r = EP.reduce_scatter(EP.d_outall, d_out, per, ncclFloat32, ncclSum, EP.comm, st);
-    if (r != ncclSuccess) { rc = nccl_fail(r, "ncclReduceScatter"); goto out; }
-    if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)EP.rank * kb, kb * sizeof(int),
+    if (a.ep.on) {
+        CK((cudaError_t)wc_ep_finalize_launch(&a.ep, d_out, a.ws.err, st), "ep finalize");
+    } else if (!rep) {
+        const ncclResult_t r = EP.reduce_scatter(EP.d_outall, d_out, per, ncclFloat32, ncclSum,
+                                                 EP.comm, st);
+        if (r != ncclSuccess) { rc = nccl_fail(r, "ncclReduceScatter"); goto out; }
+    } else {
+        const ncclResult_t r = EP.all_reduce(EP.d_outall, d_out, per, ncclFloat32, ncclSum,
+                                             EP.comm, st);
+        if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllReduce"); goto out; }
+    }
+    if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)tr * kb, kb * sizeof(int),
                                   cudaMemcpyDeviceToDevice, st), "route copy");
-    if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)EP.rank * kb, kb * sizeof(float),
+    if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)tr * kb, kb * sizeof(float),
                                 cudaMemcpyDeviceToDevice, st), "weight copy");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
+}
+
+int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out, int *d_idx,
+                                float *d_w, void *stream)
+{
+    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 0);
+}
+
+int waste_cuda_ep_moe_layer_rep_dev(int layer, int T, const float *d_x, float *d_out,
+                                    int *d_idx, float *d_w, void *stream)
+{
+    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 1);
 }
 
 /* The host-buffer layer call captured once: H2D of x, the kernel chain,

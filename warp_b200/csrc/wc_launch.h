@@ -14,9 +14,11 @@
 extern "C" {
 #endif
 
-/* Vector positions per gate/up and per down tile of the decode kernels. */
+/* Vector positions per gate/up and per down tile of the decode kernels.
+ * The gate/up count depends on the expert width (wc_vs_gateup). */
 #define WC_VS_GATEUP 4
 #define WC_VS_DOWN   8
+int wc_vs_gateup(int lat);
 
 /* One layer's bank as the kernels see it: E records of rec_bytes each,
  * all with the same payload offsets (checked at load). tmap: TMA tensor
@@ -42,6 +44,7 @@ typedef struct {
     float *p_d;        /* [T][K][ns_d][lat] partial down sums               */
     float *logits;     /* [T][E]                                            */
     float *sh_g, *sh_u, *sh_h, *sh_out;   /* shared expert [T][si] / [T][hid] */
+    float *h;          /* [T][K][inter] SiLU(g)*u, batched calls only        */
     unsigned int *tickets;  /* [T] router blocks done; zero between launches   */
     unsigned int *route_flag;  /* [T] 1 once routing is published            */
     unsigned int *route_pass;  /* [T] gate/up tiles that have seen the flag   */
@@ -65,11 +68,14 @@ typedef struct {
  *   +1024  x   [world][T][hidden]  : every rank's tokens
  *   then   part[world][T][hidden]  : every rank's partial sums of this
  *                                    rank's tokens
- * Flags only grow (epochs), so nothing is reset between calls. */
+ * Flags only grow (epochs), so nothing is reset between calls.
+ * With rep set, every rank holds the same T tokens: x is not copied (the x
+ * flags still order one call after the last), and each rank's partial sums
+ * go to every rank, so all of them finish with the full outputs. */
 #define WC_EP_MAX 8
 #define WC_EP_MAIL_HDR 1024
 typedef struct {
-    int on, rank, world, T, hidden;
+    int on, rank, world, T, hidden, rep;
     unsigned char *mail[WC_EP_MAX];   /* every rank's mailbox as mapped here */
 } wc_ep_link;
 
@@ -98,6 +104,8 @@ typedef struct {
                                  to the others are skipped, not computed      */
     int gu_eg;                /* gate/up experts per tile with a partial bank
                                  (0: all K of a token)                        */
+    int act_pre;              /* set by the launcher: SiLU(g)*u computed once
+                                 per (token, expert) before the down tiles    */
     wc_ep_link ep;            /* on: x comes from the mailbox, partial sums go
                                  to the tokens' ranks through peer memory    */
     const int8_t *shg, *shu, *shd;
@@ -185,7 +193,7 @@ uint64_t wc_launches(void);
 void     wc_count_launches(int n);
 
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
-enum { WC_PH_ROUTER, WC_PH_ROUTE, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
+enum { WC_PH_ROUTER, WC_PH_ACT, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
        WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_COUNT };
 int  wc_prof_enable(int on);
 int  wc_profiling(void);      /* 1 while the phase timers are on */

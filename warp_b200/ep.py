@@ -71,3 +71,11 @@ def moe_layer_dev(layer: int, T: int, d_x: int, d_out: int, d_idx: int = 0, d_w:
     _check(load_library().waste_cuda_ep_moe_layer_dev(layer, T, v(d_x), v(d_out), v(d_idx),
                                                       v(d_w), v(stream)))
 
+
+def moe_layer_rep_dev(layer: int, T: int, d_x: int, d_out: int, d_idx: int = 0, d_w: int = 0,
+                      stream: int = 0):
+    """T tokens that every rank holds (the same on every rank) through the
+    expert-parallel layer; every rank receives all T outputs."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_ep_moe_layer_rep_dev(layer, T, v(d_x), v(d_out),
+                                                          v(d_idx), v(d_w), v(stream)))

@@ -194,10 +194,11 @@ def random_bytes(rng: np.random.Generator, n: int) -> np.ndarray:
 
 
 def _finish_bank(bank: np.ndarray, rng: np.random.Generator, layer: int, cb_base: int,
-                 inter: int, lat: int, stages: int, scale_lo: float, scale_hi: float):
-    """Turns E rows of random bytes into E valid records in place: zero the
-    index padding rows, write the f16 row scales, zero the 4 KiB tail and
-    write each header with its crc32."""
+                 inter: int, lat: int, stages: int, scale_lo: float, scale_hi: float,
+                 eid0: int = 0):
+    """Turns E rows of random bytes into E valid records in place (expert ids
+    eid0, eid0+1, ...): zero the index padding rows, write the f16 row
+    scales, zero the 4 KiB tail and write each header with its crc32."""
     E, rb = bank.shape
     off = HDR_SIZE
     offs = []
@@ -218,7 +219,7 @@ def _finish_bank(bank: np.ndarray, rng: np.random.Generator, layer: int, cb_base
     for e in range(E):
         crc = zlib.crc32(memoryview(bank[e, HDR_SIZE:end])) & 0xFFFFFFFF
         bank[e, :HDR_SIZE] = np.frombuffer(
-            struct.pack(HDR_FMT, MAGIC_EXPERT, layer, e, fmt, 0, cb_base, 0, 0, blocks,
+            struct.pack(HDR_FMT, MAGIC_EXPERT, layer, eid0 + e, fmt, 0, cb_base, 0, 0, blocks,
                         offs[0], offs[1], offs[2], corr, crc, 0, 0), dtype=np.uint8)
 
 
@@ -229,6 +230,44 @@ def bank(rng: np.random.Generator, layer: int, n_experts: int, cb_base: int, int
     b = random_bytes(rng, n_experts * rb).reshape(n_experts, rb)
     _finish_bank(b, rng, layer, cb_base, inter, lat, stages, scale_lo, scale_hi)
     return b.reshape(-1)
+
+
+def bank_range(seed: int, layer: int, first: int, count: int, cb_base: int, inter: int,
+               lat: int, stages: int = 3, scale_lo: float = 0.5,
+               scale_hi: float = 1.5) -> np.ndarray:
+    """Records [first, first+count) of a layer's bank, each from its own
+    generator seeded by (seed, expert id): a rank that holds part of the
+    experts builds only those, and every split of the range gives the same
+    bytes. Returned as [count][rec_bytes] uint8."""
+    rb = record_bytes(inter, lat, stages)
+    out = np.empty((count, rb), dtype=np.uint8)
+    for k in range(count):
+        rng = np.random.default_rng((seed, first + k))
+        out[k] = random_bytes(rng, rb)
+        _finish_bank(out[k:k + 1], rng, layer, cb_base, inter, lat, stages, scale_lo, scale_hi,
+                     eid0=first + k)
+    return out
+
+
+def set_layer(records: np.ndarray, layer: int) -> None:
+    """Rewrites the layer field of [n][rec_bytes] records in place (the
+    crc32 covers the payload only), for benchmarks that load the same
+    payloads as several resident layers."""
+    records[:, 4:6] = np.frombuffer(struct.pack("<H", layer), dtype=np.uint8)
+
+
+def trunk(seed: int, hidden: int, n_experts: int, shared_inter: int):
+    """A seeded router [E][hidden] (rows N(0, 1/hidden), so logits are about
+    N(0, 1)) and Q8G shared expert {gate, up, down: (q, s)}."""
+    rng = np.random.default_rng(seed)
+    router = (rng.standard_normal((n_experts, hidden), dtype=np.float32)
+              / np.float32(np.sqrt(hidden))).astype(np.float32)
+    sh = {}
+    if shared_inter:
+        sh["gate"] = q8g(rng, shared_inter, hidden, 2e-4, 5e-4)
+        sh["up"] = q8g(rng, shared_inter, hidden, 2e-4, 5e-4)
+        sh["down"] = q8g(rng, hidden, shared_inter, 2e-4, 5e-4)
+    return router, sh
 
 
 def derive_layer(base: "MoELayer", layer: int, seed: int) -> "MoELayer":
