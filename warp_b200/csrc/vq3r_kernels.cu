@@ -862,7 +862,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     }
 }
 
-/* The router for several tokens (T >= 2): a block holds TB tokens' x in
+/* The router for many tokens (T >= 16): a block holds TB tokens' x in
  * shared memory and streams its weight rows once for all of them (the
  * single-token kernel re-reads every row per token). Router blocks take rw
  * rows per warp, shared blocks 2*rw Q8G rows per warp. Each dot product
@@ -871,6 +871,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
  * times the group's products), so both kernels give the same logits. The
  * last block of a token group routes its tokens, one warp each. */
 constexpr int kRouterTB = 8;           /* tokens per block, at most */
+constexpr int kRouterTokensMin = 16;   /* below: the single-token kernel per token
+                                          (more blocks, one round trip each) */
 constexpr int kRtChunk = 8;            /* router weight float4 loads in flight per lane */
 constexpr int kShChunk = 16;           /* shared-expert weight words in flight per lane */
 
@@ -1677,11 +1679,14 @@ MoeGeom moe_geom(const wc_moe_args *a)
          * empty ones retire right after the route */
         const int q = a->gu_eg * ((b.inter + kBlock - 1) / kBlock) * 4;
         m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, wc_vs_gateup(b.lat), b.stages, q), b.stages);
-        /* tiles for the expected local count; a tile takes further groups
-         * in rounds when a token has more (one lane: the table survives),
-         * else every group gets its own tile */
-        m.gu.groups = m.gu.nlanes == 1 ? (a->gu_eg + m.gu.EG - 1) / m.gu.EG
-                                       : (a->K + m.gu.EG - 1) / m.gu.EG;
+        /* every group its own tile while that keeps the grid within a few
+         * tiles per SM (decode: latency); beyond that, tiles for the
+         * expected local count, each taking further groups in rounds when
+         * a token has more (one lane: the table survives) */
+        const int full = (a->K + m.gu.EG - 1) / m.gu.EG;
+        const long full_tiles = (long)a->T * 2 * m.gu.ns * full;
+        m.gu.groups = (m.gu.nlanes == 1 && full_tiles > 8L * kSMs)
+                          ? (a->gu_eg + m.gu.EG - 1) / m.gu.EG : full;
     } else {
         m.gu = with_stage(make_geom(b.inter, b.lat, a->K, wc_vs_gateup(b.lat), b.stages, 512), b.stages);
     }
@@ -1757,7 +1762,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         /* programmatic launch: the router's weight copies overlap whatever
          * kernel precedes it in the stream (the previous layer's combine) */
         const bool rpdl = !P.on;
-        if (a->T >= 2) {             /* several tokens: weights read once per group */
+        if (a->T >= kRouterTokensMin) {   /* weights read once per token group */
             const RouterTGeom tg = router_t_geom(a->E, a->si, a->T, a->bank.lat);
             const size_t tsm = 16 + (size_t)tg.TB * a->bank.lat * 4;
             const dim3 tgrid(tg.rblocks + tg.sblocks, (a->T + tg.TB - 1) / tg.TB);
