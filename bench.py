@@ -22,10 +22,14 @@ metric and config.
 Multi-GPU (torchrun, --gpus N > 1): expert parallel — each rank holds a
 contiguous 1/N of every layer's experts (the router and shared expert are
 replicated) and contributes one token per step, so a step decodes N tokens;
-the routed tokens and partial sums cross NVLink inside the library (NCCL
-all-gather / reduce-scatter). Per-GPU work stays ~K expert-token pairs per
-layer (weak scaling). `--parallel replicas` instead runs N independent
-copies of the single-GPU decode.
+the routed tokens and partial sums cross NVLink inside the library's own
+kernels (peer-memory mailboxes; NCCL as the fallback). Per-GPU work stays
+~K expert-token pairs per layer (weak scaling). `--parallel replicas`
+instead runs N independent copies of the single-GPU decode.
+
+`--workload k3` measures config 4 instead: one K3-class MoE layer (hidden
+7168, 512 experts, top-16) at global batches 1/16/64, expert parallel over
+the N GPUs.
 """
 from __future__ import annotations
 
@@ -67,7 +71,7 @@ def layer_bytes():
 # dram__bytes_write.sum), from one ncu capture of this bench's workload
 # (profiles/gateup_kernel_kimi_linear_decode.txt): the algorithmic bytes plus
 # the deliberate L2 prefetch of the chosen experts' down streams.
-GATEUP_TRAFFIC_BYTES = 21_349_376
+GATEUP_TRAFFIC_BYTES = 21_357_184     # mean of the two captured launches
 
 
 def gateup_bytes():
