@@ -227,7 +227,11 @@ int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x,
  * (optional, [T][K]) receive its tokens' routes. Ordered on `stream`;
  * every rank must make the same calls in the same order. NCCL is loaded at
  * run time (libnccl.so.2); without it these return WASTE_CUDA_E_NODEV. No
- * counterpart in the reference, which runs on one host. */
+ * counterpart in the reference, which runs on one host.
+ * A wait on a peer's flag gives up after WASTE_CUDA_EP_WAIT_POLLS polls
+ * (environment, read by ep_init; default 2^24, several seconds) and sets
+ * WASTE_CUDA_DERR_PEER_WAIT, so a rank that never makes its call costs the
+ * others an error, not a hang. */
 int  waste_cuda_ep_range(int n_experts, int rank, int world, int *first,
                          int *count);
 int  waste_cuda_ep_unique_id(void *id, size_t bytes);   /* >= 128 bytes */
@@ -259,6 +263,9 @@ int  waste_cuda_ep_moe_layer_rep_dev(int layer, int T, const float *d_x,
 #define WASTE_CUDA_DERR_ROUTE_WAIT 1u
 #define WASTE_CUDA_DERR_TMA_WAIT   2u   /* also: a tensor-core commit that never came */
 #define WASTE_CUDA_DERR_BAD_EXPERT 4u   /* a device-side route named an expert not held */
+#define WASTE_CUDA_DERR_PEER_WAIT  8u   /* expert parallel: a peer's token or partial-sum
+                                           flag did not arrive (a rank that did not make
+                                           the call); the layer's outputs are not valid */
 unsigned waste_cuda_device_errors(void);
 
 /* ---- single VQ3R kernels ---------------------------------------------------

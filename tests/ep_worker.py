@@ -23,6 +23,33 @@ from warp_b200 import ep, synth
 TOL = 2e-5
 
 
+def skipped_call(rank, world, L, dev):
+    """A rank that does not make its layer call. With a short peer-wait
+    limit, rank 0's call gives up on rank 1's flags and reports
+    DERR_PEER_WAIT instead of hanging, and the device stays usable. Both
+    ranks first make one call together: the first call builds the
+    mailboxes, which takes a collective."""
+    os.environ["WASTE_CUDA_EP_WAIT_POLLS"] = str(1 << 20)
+    ep.setup(rank, world)
+    x = synth.activations(500, L.hidden, T=1)
+    dx = torch.from_numpy(x).to(dev)
+    out = torch.empty((1, L.hidden), device=dev)
+    dist.barrier()
+    ep.moe_layer_rep_dev(L.layer, 1, dx.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    assert wb.device_errors() == 0, "the joint call"
+    dist.barrier()
+    if rank == 0:                            # rank 1 sits this one out
+        ep.moe_layer_rep_dev(L.layer, 1, dx.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        errs = wb.device_errors()
+        assert errs & wb.DERR_PEER_WAIT, errs
+        assert wb.device_errors() == 0       # reading cleared the bits
+    dist.barrier()
+    ep.shutdown()
+    del os.environ["WASTE_CUDA_EP_WAIT_POLLS"]
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -81,6 +108,7 @@ def main():
     check("peer memory")                     # the default exchange
     dist.barrier()
     ep.shutdown()
+    skipped_call(rank, world, layers[0], dev)
     os.environ["WASTE_CUDA_EP_P2P"] = "0"    # the NCCL exchange, same banks
     ep.setup(rank, world)
     check("nccl")

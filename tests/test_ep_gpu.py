@@ -107,6 +107,9 @@ def test_two_ranks_over_nccl():
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
            "--master-port", str(port), os.path.join(ROOT, "tests", "ep_worker.py")]
-    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    # the worker includes a rank that skips a call: no NVLink multicast in
+    # any library while a rank may be out of step
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("ep_worker ok") == 2, r.stdout[-2000:]

@@ -38,6 +38,7 @@ EXPORTS = (
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
 
 OK, E_ARG, E_DEVICE, E_RECORD, E_NOBANK, E_NOMEM, E_NODEV = 0, -1, -2, -3, -4, -5, -6
+DERR_ROUTE_WAIT, DERR_TMA_WAIT, DERR_BAD_EXPERT, DERR_PEER_WAIT = 1, 2, 4, 8
 
 
 class WasteCudaError(RuntimeError):

@@ -501,12 +501,12 @@ __device__ __forceinline__ float *ep_part(const wc_ep_link &l, int r)
 
 /* Until every rank's flag (in this rank's mailbox) reaches epoch e. */
 __device__ __forceinline__ bool ep_wait_all(const unsigned int *flags, int world, unsigned int e,
-                                            unsigned int *err)
+                                            unsigned int *err, int polls)
 {
     for (int r = 0; r < world; r++) {
         long long i = 0;
         while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
-            if (++i >= kSpinLimit) {
+            if (++i >= polls) {
                 atomicOr(err, WC_ERR_PEER_WAIT);
                 return false;
             }
@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(256) ep_finalize_kernel(wc_ep_link l, float *o
 {
     __shared__ int ok;
     const unsigned int e = *ep_epoch(l);
-    if (threadIdx.x == 0) ok = ep_wait_all(ep_pflags(l, l.rank), l.world, e, err);
+    if (threadIdx.x == 0) ok = ep_wait_all(ep_pflags(l, l.rank), l.world, e, err, l.wait_polls);
     __syncthreads();
     if (!ok) return;
     for (int r = 0; r < l.world; r++) (void)ld_acquire_sys(ep_pflags(l, l.rank) + r);
@@ -779,7 +779,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     pdl_wait();
     if (threadIdx.x == 0) {
         if (a.ep.on) {            /* every rank's tokens are in this mailbox */
-            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err))
+            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err,
+                             a.ep.wait_polls))
                 ep_fail = 1;
             asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
         }
@@ -940,7 +941,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     pdl_wait();
     if (threadIdx.x == 0) {
         if (a.ep.on) {            /* every rank's tokens are in this mailbox */
-            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err))
+            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err,
+                             a.ep.wait_polls))
                 ep_fail = 1;
             asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
         }

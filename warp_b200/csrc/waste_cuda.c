@@ -131,6 +131,7 @@ static struct {
     int p2p;                      /* 1 once every rank mapped every mailbox */
     unsigned char *mail[WC_EP_MAX];
     int mail_T, mail_hidden;
+    int wait_polls;               /* peer-wait limit, WASTE_CUDA_EP_WAIT_POLLS */
 } EP;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
@@ -1125,6 +1126,11 @@ int waste_cuda_ep_init(int rank, int world, const void *id, size_t bytes)
     if (r != ncclSuccess) { rc = nccl_fail(r, "ncclCommInitRank"); goto out; }
     EP.rank = rank;
     EP.world = world;
+    {
+        const char *wp = getenv("WASTE_CUDA_EP_WAIT_POLLS");
+        const long v = (wp && *wp) ? strtol(wp, NULL, 10) : 0;
+        EP.wait_polls = (v > 0 && v <= (1L << 30)) ? (int)v : (1 << 24);
+    }
     EP.active = 1;
     g_epoch++;
 out:
@@ -1285,6 +1291,7 @@ static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx
         lk.T = T;
         lk.hidden = L->hidden;
         lk.rep = rep;
+        lk.wait_polls = EP.wait_polls;
         memcpy(lk.mail, EP.mail, sizeof lk.mail);
         CK((cudaError_t)wc_ep_publish_launch(&lk, d_x, a.ws.err, st), "ep publish");
         a.x = rep ? d_x : (const float *)(EP.mail[EP.rank] + WC_EP_MAIL_HDR);

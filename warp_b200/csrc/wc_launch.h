@@ -76,6 +76,7 @@ typedef struct {
 #define WC_EP_MAIL_HDR 1024
 typedef struct {
     int on, rank, world, T, hidden, rep;
+    int wait_polls;                   /* polls before a peer wait gives up  */
     unsigned char *mail[WC_EP_MAX];   /* every rank's mailbox as mapped here */
 } wc_ep_link;
 
