@@ -371,10 +371,21 @@ def run_warp(args):
                 o_pin.copy_(out[L], non_blocking=True)
             s.synchronize()
     else:
+        # the C entry point with caller-owned host buffers (what an engine
+        # in C passes): the library copies x to the device and the output,
+        # route and weights back on every call; addresses taken once
         x_host = [[np.ascontiguousarray(xs_h[t, L]) for L in range(nL)] for t in range(ntok)]
+        x_addr = [[a.ctypes.data for a in row] for row in x_host]
+        o_host = np.empty(HIDDEN, np.float32)
+        i_host = np.empty(TOPK, np.int32)
+        w_host = np.empty(TOPK, np.float32)
+        o_a, i_a, w_a = o_host.ctypes.data, i_host.ctypes.data, w_host.ctypes.data
+        layer_call = wb.load_library().waste_cuda_moe_layer
 
         def e2e_layer(t, L):
-            wb.moe_layer(L + 1, x_host[t][L], TOPK, HIDDEN)
+            rc = layer_call(L + 1, x_addr[t][L], o_a, i_a, w_a)
+            if rc:
+                wb._check(rc)
     for L in range(nL):
         e2e_layer(0, L)
     if dist:
@@ -694,9 +705,9 @@ def run_k3(args):
                                  T=ntok * nL * T).reshape(ntok, nL, T, K3_HIDDEN)
         xs = torch.from_numpy(xs_h).to(dev)
         out = torch.empty((nL, T, K3_HIDDEN), dtype=torch.float32, device=dev)
-        Tr = T if mode != "split" else T          # routes returned for this rank's tokens
-        idx = torch.empty((ntok, nL, Tr, K3_TOPK), dtype=torch.int32, device=dev)
-        w = torch.empty((ntok, nL, Tr, K3_TOPK), dtype=torch.float32, device=dev)
+        # routes returned for the tokens this rank passed
+        idx = torch.empty((ntok, nL, T, K3_TOPK), dtype=torch.int32, device=dev)
+        w = torch.empty((ntok, nL, T, K3_TOPK), dtype=torch.float32, device=dev)
 
         def call(t, L):
             xp, op = xs[t, L].data_ptr(), out[L].data_ptr()
