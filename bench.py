@@ -55,7 +55,9 @@ SEED = 1234
 
 
 def layer_bytes():
-    """Algorithmic bytes one token reads in one layer."""
+    """Algorithmic bytes one token reads in one layer: the 8 routed experts'
+    index streams and row scales, the Q8G shared expert, the F32 router,
+    the layer's codebooks and x in / y out."""
     from warp_b200 import synth
     idx = 2 * synth.index_bytes(INTER, HIDDEN, 3) + synth.index_bytes(HIDDEN, INTER, 3)
     scales = 2 * (2 * INTER + HIDDEN)
