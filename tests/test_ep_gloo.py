@@ -5,7 +5,8 @@ kernels:
   * the library's split gives every expert to exactly one rank;
   * rank 0's NCCL unique id reaches every rank unchanged (warp_b200.ep);
   * the per-rank partial sums (each rank's own experts, in router order) add
-    up over the ranks to the routed part of the layer, within 2e-5.
+    up over the ranks to the routed part of the layer, within 2e-5, both for
+    a batch split over the ranks and for one every rank holds.
 """
 import os
 import socket
@@ -71,13 +72,32 @@ def _worker(rank, world, port, q):
         # 3. partial sums over the ranks' experts add up to the routed part
         L = synth.moe_layer(41, hidden=128, inter=64, n_experts=E, top_k=6, shared_inter=64,
                             layer=3)
-        x = synth.activations(42, L.hidden, T=3)
-        part = torch.from_numpy(partial_reference(L, x, first, count))
+        # (a batch split over the ranks: every rank's tokens go to every
+        # rank, each computes its experts for all of them, and a rank's own
+        # rows of the summed partials are its tokens' routed outputs)
+        T = 3
+        x = synth.activations(42 + rank, L.hidden, T=T)       # this rank's tokens
+        xs = [torch.zeros((T, L.hidden)) for _ in range(world)]
+        dist.all_gather(xs, torch.from_numpy(x))
+        x_all = torch.cat(xs).numpy()
+        part = torch.from_numpy(partial_reference(L, x_all, first, count))
         dist.all_reduce(part)
-        for t in range(x.shape[0]):
+        mine = part[rank * T:(rank + 1) * T].numpy()
+        for t in range(T):
             _, idx, w = O.moe_layer(L, x[t], fma=1)
             full = O.moe_experts(L, idx, w, x[t], fma=1)
-            rel = float(np.linalg.norm(part[t].numpy() - full) / np.linalg.norm(full))
+            rel = float(np.linalg.norm(mine[t] - full) / np.linalg.norm(full))
+            assert rel < TOL, rel
+        # 4. a batch every rank holds (the replicated-token call): each rank
+        # its own experts for all tokens, the sum over ranks is every
+        # token's routed output on every rank
+        xr = synth.activations(43, L.hidden, T=2)             # the same seed everywhere
+        rp = torch.from_numpy(partial_reference(L, xr, first, count))
+        dist.all_reduce(rp)
+        for t in range(xr.shape[0]):
+            _, idx, w = O.moe_layer(L, xr[t], fma=1)
+            full = O.moe_experts(L, idx, w, xr[t], fma=1)
+            rel = float(np.linalg.norm(rp[t].numpy() - full) / np.linalg.norm(full))
             assert rel < TOL, rel
         dist.barrier()
         dist.destroy_process_group()
