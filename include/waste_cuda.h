@@ -203,13 +203,13 @@ int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
  * d_out[T][hidden] receives these partial sums; a token's output is the sum
  * of the partials over the devices, which hold disjoint ranges and add the
  * shared expert once. d_idx/d_w [T][K] receive the routes. For callers
- * that run their own exchange; waste_cuda_ep_moe_layer_dev wraps it with
- * NCCL. Ordered on `stream`. */
+ * that run their own exchange; waste_cuda_ep_moe_layer_dev and _rep_dev
+ * wrap it with the library's own. Ordered on `stream`. */
 int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x,
                                   float *d_out, int sh_t0, int sh_t1,
                                   int *d_idx, float *d_w, void *stream);
 
-/* ---- expert parallelism (one process per GPU, NCCL over NVLink) ----------
+/* ---- expert parallelism (one process per GPU, NVLink peer memory) --------
  * `world` processes share every MoE layer; rank r holds the contiguous
  * expert range [r*E/world, (r+1)*E/world) (waste_cuda_ep_range), and the
  * trunk (router, bias, shared expert) is replicated. Sequence per process:
@@ -220,12 +220,18 @@ int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x,
  * vq_bank_load after ep_init reserves the rank's range; a layer call
  * refuses a bank whose range is not the rank's) and trunks.
  * waste_cuda_ep_moe_layer_dev: every rank passes its own T tokens (the same
- * T everywhere, world*T <= 64). The library all-gathers them, routes all of
- * them, runs its own experts for every token routed there, adds the shared
- * expert for its own tokens, and reduce-scatters the partial sums so that
- * each rank receives its own tokens' outputs d_out[T][hidden]. d_idx/d_w
- * (optional, [T][K]) receive its tokens' routes. Ordered on `stream`;
- * every rank must make the same calls in the same order. NCCL is loaded at
+ * T everywhere, world*T <= 64). Every rank's tokens reach every rank, each
+ * routes all of them, runs its own experts for every token routed there,
+ * adds the shared expert for its own tokens, and sends each token's partial
+ * sum to the token's rank, which adds them in rank order: each rank
+ * receives its own tokens' outputs d_out[T][hidden]. d_idx/d_w (optional,
+ * [T][K]) receive its tokens' routes. The exchange runs inside the layer's
+ * kernels through every rank's mailbox, mapped into every other rank's
+ * address space over NVLink (CUDA IPC, set up by the first call, which is
+ * collective); where a mapping fails on any rank, every rank uses NCCL
+ * instead (all-gather, reduce-scatter), as it does with
+ * WASTE_CUDA_EP_P2P=0. Ordered on `stream`; every rank must make the same
+ * calls in the same order. NCCL (for set-up and the fallback) is loaded at
  * run time (libnccl.so.2); without it these return WASTE_CUDA_E_NODEV. No
  * counterpart in the reference, which runs on one host.
  * A wait on a peer's flag gives up after WASTE_CUDA_EP_WAIT_POLLS polls
