@@ -1635,12 +1635,13 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
 
 /* Positions per gate/up tile: each slice's partial sums are written and
  * summed again by the down tiles, so wide experts take longer slices. */
-extern "C" int wc_vs_gateup(int lat)
+extern "C" int wc_vs_gateup(int lat, int inter)
 {
     /* 7168-wide experts: 224 slices of 4 positions would write and re-read
      * 3.7 MB of partial sums per (token, expert); 8 positions halve that
-     * and the staged streams still fit (128 row blocks x 8 x 192 B) */
-    return lat >= 4096 ? 2 * WC_VS_GATEUP : WC_VS_GATEUP;
+     * and the staged streams still fit while a tile holds at most 128 row
+     * blocks (kMaxTileRows), i.e. while inter <= 8192 */
+    return (lat >= 4096 && inter <= kMaxTileRows) ? 2 * WC_VS_GATEUP : WC_VS_GATEUP;
 }
 constexpr int kVsDown = WC_VS_DOWN;
 
@@ -1680,7 +1681,7 @@ MoeGeom moe_geom(const wc_moe_args *a)
         /* one lane per quarter block: small tiles, many per SM, and the
          * empty ones retire right after the route */
         const int q = a->gu_eg * ((b.inter + kBlock - 1) / kBlock) * 4;
-        m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, wc_vs_gateup(b.lat), b.stages, q), b.stages);
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, wc_vs_gateup(b.lat, b.inter), b.stages, q), b.stages);
         /* every group its own tile while that keeps the grid within a few
          * tiles per SM (decode: latency); beyond that, tiles for the
          * expected local count, each taking further groups in rounds when
@@ -1690,7 +1691,7 @@ MoeGeom moe_geom(const wc_moe_args *a)
         m.gu.groups = (m.gu.nlanes == 1 && full_tiles > 8L * kSMs)
                           ? (a->gu_eg + m.gu.EG - 1) / m.gu.EG : full;
     } else {
-        m.gu = with_stage(make_geom(b.inter, b.lat, a->K, wc_vs_gateup(b.lat), b.stages, 512), b.stages);
+        m.gu = with_stage(make_geom(b.inter, b.lat, a->K, wc_vs_gateup(b.lat, b.inter), b.stages, 512), b.stages);
     }
     m.d = with_stage(make_geom(b.lat, b.inter, 1, kVsDown, b.stages, 448), b.stages);
     m.gu_tiles = a->T * 2 * m.gu.ns * m.gu.groups;
@@ -1838,7 +1839,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
 extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
                                    int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat), stages, 512);
+    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat, inter), stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     size_t n = 0;
     n += (size_t)T * 2 * gu.ns * K * inter;
@@ -1852,7 +1853,7 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
                                 int lat, int inter, int si, int stages)
 {
-    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat), stages, 512);
+    const TileGeom gu = make_geom(inter, lat, K, wc_vs_gateup(lat, inter), stages, 512);
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     float *p = base;
     /* control words first (zeroed once at allocation, self-resetting):

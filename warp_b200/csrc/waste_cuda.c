@@ -514,7 +514,7 @@ static void bank_tensor_maps(wc_bank *kb)
     if (!enc) return;
     const int nv_gu = kb->lat / 8, nrb_gu = (kb->inter + 63) / 64;
     const int nv_d = kb->inter / 8, nrb_d = (kb->lat + 63) / 64;
-    const int vs_gu = wc_vs_gateup(kb->lat);
+    const int vs_gu = wc_vs_gateup(kb->lat, kb->inter);
     if (nv_gu % vs_gu || nv_d % WC_VS_DOWN || nrb_gu % 2 || nrb_gu / 2 > 256 ||
         nrb_d > 256 || WC_VS_DOWN * 24 > 256 || vs_gu * 24 > 256 || kb->stages != 3)
         return;

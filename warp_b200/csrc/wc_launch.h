@@ -18,7 +18,7 @@ extern "C" {
  * The gate/up count depends on the expert width (wc_vs_gateup). */
 #define WC_VS_GATEUP 4
 #define WC_VS_DOWN   8
-int wc_vs_gateup(int lat);
+int wc_vs_gateup(int lat, int inter);
 
 /* One layer's bank as the kernels see it: E records of rec_bytes each,
  * all with the same payload offsets (checked at load). tmap: TMA tensor
