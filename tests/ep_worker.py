@@ -86,9 +86,10 @@ def main():
                     r = rel_l2(out[t], ro)
                     assert r < TOL, (mode, rank, L.layer, t, r)
                 # the same layer for tokens every rank holds (a batch of one;
-                # nine: 72 routes, the batched SiLU kernel; 25: the
-                # many-token router and gate/up tiles that take a token's
-                # local experts in rounds), interleaved with the calls above
+                # nine: the decode-sized forms over several tokens; 25: the
+                # batched forms — many-token router, gate/up tiles that take
+                # a token's local experts in rounds, the separate SiLU
+                # kernel), interleaved with the calls above
                 for Tr in (1, 9, 25):
                     xr = synth.activations(300 + L.layer + rep + Tr, L.hidden, T=Tr)
                     dx = torch.from_numpy(xr).to(dev)

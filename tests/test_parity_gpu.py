@@ -235,9 +235,10 @@ def test_moe_layer_k3_shape(cuda_lib):
     yo, route, rws = O.moe_chunk(L0, x, fma=1)
     y = wb.moe_chunk_experts(L.layer, route, rws, x, L.hidden, L.inter)
     assert rel_l2(y, yo) < TOL
-    # five tokens in one device call: the several-token router (groups of
-    # four at this width, then one) and the batched expert tiles
-    _batched_layer_check(wb, L, synth.activations(79, L.hidden, T=5))
+    # 17 tokens in one device call, the batched forms at this width: the
+    # many-token router (x of four tokens per block at hidden 7168: groups
+    # 4, 4, 4, 4, 1), 8-position gate/up slices, the separate SiLU kernel
+    _batched_layer_check(wb, L, synth.activations(79, L.hidden, T=17))
     wb.vq_bank_free(L.layer)
 
 
@@ -276,6 +277,8 @@ def test_moe_layer_512_experts_top16(cuda_lib):
         ro, ri, _ = O.moe_layer(L, x[t], fma=1)
         assert np.array_equal(idx, ri)
         assert rel_l2(out, ro) < TOL
-    # 17 tokens in one call: router token groups of eight, eight and one
+    # 17 tokens in one call: router token groups of eight, eight and one,
+    # the separate SiLU kernel; 9 tokens: the decode-sized forms
     _batched_layer_check(wb, L, synth.activations(93, L.hidden, T=17))
+    _batched_layer_check(wb, L, synth.activations(94, L.hidden, T=9))
     wb.vq_bank_free(L.layer)

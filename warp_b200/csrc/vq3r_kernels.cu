@@ -872,8 +872,11 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
  * times the group's products), so both kernels give the same logits. The
  * last block of a token group routes its tokens, one warp each. */
 constexpr int kRouterTB = 8;           /* tokens per block, at most */
-constexpr int kRouterTokensMin = 16;   /* below: the single-token kernel per token
-                                          (more blocks, one round trip each) */
+/* Calls of at least this many tokens take the batched forms (the many-token
+ * router, gate/up tiles that take further expert groups in rounds, the
+ * separate SiLU kernel); smaller ones keep the latency forms of decode. */
+constexpr int kBatchedT = 16;
+constexpr int kRouterTokensMin = kBatchedT;
 constexpr int kRtChunk = 8;            /* router weight float4 loads in flight per lane */
 constexpr int kShChunk = 16;           /* shared-expert weight words in flight per lane */
 
@@ -1682,13 +1685,12 @@ MoeGeom moe_geom(const wc_moe_args *a)
          * empty ones retire right after the route */
         const int q = a->gu_eg * ((b.inter + kBlock - 1) / kBlock) * 4;
         m.gu = with_stage(make_geom(b.inter, b.lat, a->gu_eg, wc_vs_gateup(b.lat, b.inter), b.stages, q), b.stages);
-        /* every group its own tile while that keeps the grid within a few
-         * tiles per SM (decode: latency); beyond that, tiles for the
-         * expected local count, each taking further groups in rounds when
-         * a token has more (one lane: the table survives) */
+        /* decode-sized calls: every group its own tile (latency); batched
+         * calls: tiles for the expected local count, each taking further
+         * groups in rounds when a token has more (one lane: the table
+         * survives) */
         const int full = (a->K + m.gu.EG - 1) / m.gu.EG;
-        const long full_tiles = (long)a->T * 2 * m.gu.ns * full;
-        m.gu.groups = (m.gu.nlanes == 1 && full_tiles > 8L * kSMs)
+        m.gu.groups = (m.gu.nlanes == 1 && a->T >= kBatchedT)
                           ? (a->gu_eg + m.gu.EG - 1) / m.gu.EG : full;
     } else {
         m.gu = with_stage(make_geom(b.inter, b.lat, a->K, wc_vs_gateup(b.lat, b.inter), b.stages, 512), b.stages);
@@ -1803,7 +1805,7 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
      * every down tile, whose prologue would otherwise wait on ns_gu
      * partial sums per input */
     wc_moe_args da = *a;
-    da.act_pre = a->T * a->K >= 64;
+    da.act_pre = a->T >= kBatchedT;
     if (da.act_pre) {
         pe = prof_begin(WC_PH_ACT, s);
         e = launch(act_kernel<ST>, dim3((a->bank.inter + 255) / 256, a->T * a->K), dim3(256), 0,
