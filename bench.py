@@ -3,14 +3,18 @@
 
 Workload (extended to a whole decode step's MoE work):
 one step is ONE token through the 26 MoE layers of a Kimi-Linear-48B-shaped
-model (27 layers, layer 0 dense), each layer = router (256 experts, F32) ->
+model (27 layers, layer 0 dense), chained the way the decode step chains
+them (src/model.c:3927-3945): each layer's MoE block takes the residual
+stream h the previous layer left, normalises it (rmsnorm with the layer's
+post-attention weight), runs the layer = router (256 experts, F32) ->
 sigmoid top-8 with renorm and routed scale 2.446 -> 8 routed experts whose
 gate/up/down weights are 3-bit residual VQ (3 x 256-entry codebooks over
-8-dim vectors) -> router-order reduce -> + one Q8G shared expert. hidden
-2304, expert intermediate 1024. All 26 layers' 256 experts are resident in
-HBM (26 x 683 MB); inputs are seeded synthetic activations (bf16-valued
-N(0,1)). A step touches ~803 MB, far more than the 126 MB L2, so no L2 flush
-is needed between steps.
+8-dim vectors) -> router-order reduce -> + one Q8G shared expert, and adds
+the result to h, which is the next layer's input. hidden 2304, expert
+intermediate 1024. All 26 layers' 256 experts are resident in HBM (26 x 683
+MB); the step's first h is seeded synthetic (bf16-valued N(0,1)). A step
+touches ~803 MB, far more than the 126 MB L2, so no L2 flush is needed
+between steps.
 
 Also measured: the config-1 VQ3R matvec (4096 x 4096) as a batched launch
 over 32 distinct matrices (203 MB of indices), in HBM GB/s.
@@ -47,7 +51,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "MoE decode tok/s (26 VQ3R MoE layers, Kimi-Linear-48B shape, batch 1)"
+METRIC = ("MoE decode tok/s (26 chained VQ3R MoE blocks: rmsnorm, MoE layer, residual; "
+          "Kimi-Linear-48B shape, batch 1)")
 UNIT = "tok/s"
 HIDDEN, INTER, EXPERTS, TOPK, SHARED = 2304, 1024, 256, 8, 1024
 MOE_LAYERS = 26
@@ -159,20 +164,25 @@ def run_reference(args):
     ncores = os.cpu_count() or 1
     base = synth.moe_layer(SEED)
     xs = synth.activations(SEED + 1, HIDDEN, T=64)
+    norms = [synth.norm_weight(SEED + 200 + L, HIDDEN) for L in range(1, MOE_LAYERS + 1)]
     if O.ref_available():
         layers = [O.RefMoe(base, max_tokens=1, threads=0),
                   O.RefMoe(synth.derive_layer(base, 2, SEED + 2), max_tokens=1, threads=0)]
         kind, cores = "reference", O.ref().refh_pool_threads()
         backend = layers[0].backend.decode()
-        step_layer = lambda L, x: layers[L % 2].layer(x)
+        rmsnorm = O.ref_rmsnorm
+        step_layer = lambda L, x: layers[L % 2].layer(x)[0]
     else:
         ders = [base, synth.derive_layer(base, 2, SEED + 2)]
         kind, cores, backend = "port", 1, "restatement"
-        step_layer = lambda L, x: O.moe_layer(ders[L % 2], x)
+        rmsnorm = O.rmsnorm
+        step_layer = lambda L, x: O.moe_layer(ders[L % 2], x)[0]
 
     def step(k):
+        # the decode step's chain (src/model.c:3927-3945): h += moe(rmsnorm(h))
+        h = xs[k % 64]
         for L in range(MOE_LAYERS):
-            step_layer(L, xs[(k * MOE_LAYERS + L) % 64])
+            h = h + step_layer(L, rmsnorm(h, norms[L], synth.NORM_EPS))
 
     for k in range(args.warmup):
         step(k)
@@ -181,9 +191,9 @@ def run_reference(args):
         step(args.warmup + k)
     dt = time.perf_counter() - t0
     v = args.steps / dt
-    sample = (f"{args.steps} tokens x {MOE_LAYERS} layers through the reference moe_layer "
-              f"({backend}, {cores} threads); banks alternate between 2 resident layers "
-              f"(683 MB each, larger than the host caches)")
+    sample = (f"{args.steps} tokens x {MOE_LAYERS} chained MoE blocks through the reference's "
+              f"waste_rmsnorm and moe_layer ({backend}, {cores} threads), h += output; banks "
+              f"alternate between 2 resident layers (683 MB each, larger than the host caches)")
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -264,22 +274,28 @@ def run_warp(args):
                         lay.bank[first * lay.rec_bytes:], lay.inter, lay.hidden, lay.stages)
         wb.moe_trunk_load(L, lay.n_experts, lay.hidden, lay.top_k, lay.renorm,
                           lay.routed_scale, lay.router, lay.bias, lay.shared_inter, lay.sh)
+        wb.moe_norm_load(L, synth.norm_weight(SEED + 200 + L, HIDDEN), synth.NORM_EPS)
         del lay
     ntok = 4
-    xs_h = synth.activations(SEED + 100 + rank, HIDDEN, T=ntok * nL).reshape(ntok, nL, HIDDEN)
+    # the step's first h per token slot; the layers' outputs alternate
+    # between two buffers, each layer reading the one the last layer wrote
+    xs_h = synth.activations(SEED + 100 + rank, HIDDEN, T=ntok)
     xs = torch.from_numpy(xs_h).to(dev)
-    out = torch.empty((nL, HIDDEN), dtype=torch.float32, device=dev)
+    hbuf = torch.empty((2, HIDDEN), dtype=torch.float32, device=dev)
     idx = torch.empty((nL, TOPK), dtype=torch.int32, device=dev)
     w = torch.empty((nL, TOPK), dtype=torch.float32, device=dev)
     s = torch.cuda.Stream(device=dev)
 
+    def h_in(t, L):
+        return xs[t].data_ptr() if L == 0 else hbuf[(L - 1) % 2].data_ptr()
+
     def step_direct(t):
         for L in range(nL):
             if ep_mode:
-                ep.moe_layer_dev(L + 1, 1, xs[t, L].data_ptr(), out[L].data_ptr(),
+                ep.moe_block_dev(L + 1, 1, h_in(t, L), hbuf[L % 2].data_ptr(),
                                  idx[L].data_ptr(), w[L].data_ptr(), s.cuda_stream)
             else:
-                wb.moe_layer_dev(L + 1, xs[t, L].data_ptr(), out[L].data_ptr(),
+                wb.moe_block_dev(L + 1, 1, h_in(t, L), hbuf[L % 2].data_ptr(),
                                  idx[L].data_ptr(), w[L].data_ptr(), s.cuda_stream)
 
     with torch.cuda.stream(s):
@@ -305,7 +321,7 @@ def run_warp(args):
     except Exception as e:  # direct launches still measure the same kernels
         print(f"graph capture unavailable: {e}", file=sys.stderr)
         graphs, use_graphs = [], False
-        launches_per_step = 5 * nL
+        launches_per_step = 4 * nL
 
     def step(k):
         if use_graphs:
@@ -359,33 +375,39 @@ def run_warp(args):
     value = world * args.steps / (ms / 1e3)
 
     # ---- end to end through the public entry points, host buffers: each
-    # layer's x copied in from pinned memory and its output copied back
+    # layer's h copied in from host memory and its h_out copied back, the
+    # next layer reading what the last one returned (an engine that runs
+    # attention on the host between the MoE blocks)
+    h_host = [np.ascontiguousarray(xs_h[t]) for t in range(ntok)]
+    hb_host = [np.empty(HIDDEN, np.float32), np.empty(HIDDEN, np.float32)]
     if ep_mode:
-        x_pin = torch.from_numpy(xs_h).pin_memory()
-        o_pin = torch.empty((HIDDEN,), dtype=torch.float32).pin_memory()
-        xd = torch.empty((HIDDEN,), dtype=torch.float32, device=dev)
+        h_pin = torch.empty((2, HIDDEN), dtype=torch.float32).pin_memory()
+        hd = torch.empty((2, HIDDEN), dtype=torch.float32, device=dev)
 
         def e2e_layer(t, L):
+            src = h_host[t] if L == 0 else hb_host[(L - 1) % 2]
             with torch.cuda.stream(s):
-                xd.copy_(x_pin[t, L], non_blocking=True)
-                ep.moe_layer_dev(L + 1, 1, xd.data_ptr(), out[L].data_ptr(), idx[L].data_ptr(),
+                h_pin[0].copy_(torch.from_numpy(src))
+                hd[0].copy_(h_pin[0], non_blocking=True)
+                ep.moe_block_dev(L + 1, 1, hd[0].data_ptr(), hd[1].data_ptr(), idx[L].data_ptr(),
                                  w[L].data_ptr(), s.cuda_stream)
-                o_pin.copy_(out[L], non_blocking=True)
+                h_pin[1].copy_(hd[1], non_blocking=True)
             s.synchronize()
+            hb_host[L % 2][:] = h_pin[1].numpy()
     else:
         # the C entry point with caller-owned host buffers (what an engine
-        # in C passes): the library copies x to the device and the output,
-        # route and weights back on every call; addresses taken once
-        x_host = [[np.ascontiguousarray(xs_h[t, L]) for L in range(nL)] for t in range(ntok)]
-        x_addr = [[a.ctypes.data for a in row] for row in x_host]
-        o_host = np.empty(HIDDEN, np.float32)
+        # in C passes): the library copies h to the device and h_out, the
+        # route and the weights back on every call; addresses taken once
+        h_addr = [a.ctypes.data for a in h_host]
+        hb_addr = [a.ctypes.data for a in hb_host]
         i_host = np.empty(TOPK, np.int32)
         w_host = np.empty(TOPK, np.float32)
-        o_a, i_a, w_a = o_host.ctypes.data, i_host.ctypes.data, w_host.ctypes.data
-        layer_call = wb.load_library().waste_cuda_moe_layer
+        i_a, w_a = i_host.ctypes.data, w_host.ctypes.data
+        block_call = wb.load_library().waste_cuda_moe_block
 
         def e2e_layer(t, L):
-            rc = layer_call(L + 1, x_addr[t][L], o_a, i_a, w_a)
+            rc = block_call(L + 1, h_addr[t] if L == 0 else hb_addr[(L - 1) % 2],
+                            hb_addr[L % 2], i_a, w_a)
             if rc:
                 wb._check(rc)
     for L in range(nL):
@@ -401,9 +423,12 @@ def run_warp(args):
         t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+    # per layer: h in; h_out, the route, the weights and the error word back
+    # (the library's result block: hidden + 2 x 64 + 4 words)
     e2e = {"value": world * args.steps / e2e_s, "unit": UNIT,
            "h2d_bytes_per_step": nL * HIDDEN * 4,
-           "d2h_bytes_per_step": nL * (HIDDEN * 4 + 2 * TOPK * 4)}
+           "d2h_bytes_per_step": nL * ((HIDDEN + 2 * 64 + 4) * 4 if not ep_mode
+                                       else HIDDEN * 4)}
 
     # ---- per-kernel times (phase timers): a GPU-side sleep holds the stream
     # while the host queues the launches, so each event pair brackets kernel
@@ -530,11 +555,14 @@ def run_warp(args):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; bf16-valued N(0,1) activations, N(0,0.02^2) codebooks, "
-                    "uniform indices, random-init router/shared expert)",
+            "data": "synthetic (seeded; bf16-valued N(0,1) first h, N(0,0.02^2) codebooks, "
+                    "uniform indices, random-init router/shared expert/norm weights)",
             "config": {"workload": "kimi_linear_48b_moe_decode", "hidden": HIDDEN,
                        "moe_inter": INTER, "experts": EXPERTS, "top_k": TOPK,
-                       "shared_experts": 1, "moe_layers": nL, "global_batch": world,
+                       "shared_experts": 1, "moe_layers": nL,
+                       "chained": "layer L+1's h is layer L's h_out (rmsnorm, MoE layer, "
+                                  "residual add per layer)",
+                       "global_batch": world,
                        "parallelism": (f"ep{world}" if ep_mode else f"replicas{world}")
                                       if world > 1 else "single",
                        "experts_per_gpu": count,

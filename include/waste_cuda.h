@@ -26,6 +26,9 @@
  *   waste_cuda_moe_layer(_dev)   src/model.c:2713-2939 moe_layer (router,
  *                                experts, shared expert) for a device-resident
  *                                hidden state
+ *   waste_cuda_moe_block(_dev)   src/model.c:3927-3945 the MoE half of a
+ *                                decoder layer: rmsnorm (:132-138), moe_layer,
+ *                                residual add
  */
 #ifndef WASTE_CUDA_H
 #define WASTE_CUDA_H
@@ -51,14 +54,21 @@ extern "C" {
  * src/backend.c:202-204 calls, once, under g_init_mu. Probes for an sm_100
  * device (WASTE_CUDA=0 declines; WASTE_CUDA_DEVICE picks one) and returns
  * the backend name, or NULL to decline so the previous backend stays
- * (src/waste_backend.h:116-120). It writes no slot of the reference's
- * waste_kernels table — the expert path has no slot there — so the table
- * pointer is taken as void* and left untouched. */
+ * (src/waste_backend.h:116-120). A translation unit that includes the
+ * engine's waste_backend.h first sees the engine's own prototype (a pointer
+ * to its waste_kernels table); anywhere else the table is an opaque
+ * pointer. It writes no slot of that table: the expert path's slots are
+ * waste_vq_slots below. */
+#ifdef WASTE_BACKEND_H
+const char *waste_register_cuda(waste_kernels *t);
+#else
 const char *waste_register_cuda(void *waste_kernels_table);
+#endif
 
-/* The expert-path slots the integration patch adds next to waste_kernels
- * (INTEGRATION.md). Filled by waste_register_cuda_vq; a NULL slot means the
- * engine keeps its CPU loop. */
+/* The expert-path slots an engine adds next to waste_kernels: its
+ * moe_layer and moe_chunk call them before their CPU expert loops, and its
+ * loader uploads the banks through them. Filled by waste_register_cuda_vq;
+ * a NULL slot means the engine keeps its CPU loop. */
 typedef struct waste_moe_call waste_moe_call;
 typedef struct waste_moe_chunk_call waste_moe_chunk_call;
 typedef struct {
@@ -196,6 +206,24 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed,
 int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out,
                              int *d_idx, float *d_w, void *stream);
 
+/* ---- the MoE block: the MoE half of a decoder layer ----------------------
+ * What the decode step does around moe_layer (src/model.c:3927-3945, a model
+ * without attention residuals): norm = rmsnorm(h) with the layer's
+ * post_attention_layernorm weight (src/model.c:132-138: r = 1/sqrtf(sum
+ * h*h / n + eps), norm = h*r*w), resid = moe_layer(norm), h_out = h + resid.
+ * The router normalises h on the device and every kernel of the layer
+ * works on that; the combine adds h. So the output of one layer's block is
+ * the next layer's input on the same stream, with no host step between.
+ * waste_cuda_moe_norm_load gives a layer (whose trunk is loaded) its norm
+ * weight [hidden] and eps. _dev: T (1..64) tokens, device pointers, every
+ * expert held here; d_h_out may equal d_h. Host form: one token, host
+ * buffers, like waste_cuda_moe_layer. */
+int waste_cuda_moe_norm_load(int layer, int hidden, const float *norm_w, float eps);
+int waste_cuda_moe_block(int layer, const float *h, float *h_out, int *routed,
+                         float *weights);
+int waste_cuda_moe_block_dev(int layer, int T, const float *d_h, float *d_h_out,
+                             int *d_idx, float *d_w, void *stream);
+
 /* The local part of a layer whose experts are spread over several devices:
  * T (1..64) tokens through the device router (the same routes on every
  * device), the routed experts THIS bank holds (all of its range loaded) in
@@ -237,7 +265,13 @@ int waste_cuda_moe_layer_part_dev(int layer, int T, const float *d_x,
  * A wait on a peer's flag gives up after WASTE_CUDA_EP_WAIT_POLLS polls
  * (environment, read by ep_init; default 2^24, several seconds) and sets
  * WASTE_CUDA_DERR_PEER_WAIT, so a rank that never makes its call costs the
- * others an error, not a hang. */
+ * others an error, not a hang. After that the ranks' exchange is out of
+ * step: the rank that gave up also marks every rank's mailbox, so every
+ * rank's later layer calls fail on the device (PEER_WAIT again, outputs not
+ * valid), and once waste_cuda_device_errors has reported the bit, the
+ * library refuses further ep layer calls with WASTE_CUDA_E_DEVICE. Recovery:
+ * every rank calls waste_cuda_ep_shutdown and then waste_cuda_ep_init with a
+ * new id, which builds new mailboxes. */
 int  waste_cuda_ep_range(int n_experts, int rank, int world, int *first,
                          int *count);
 int  waste_cuda_ep_unique_id(void *id, size_t bytes);   /* >= 128 bytes */
@@ -254,6 +288,16 @@ int  waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x,
  * split of the tokens. d_idx/d_w receive all T routes. */
 int  waste_cuda_ep_moe_layer_rep_dev(int layer, int T, const float *d_x,
                                      float *d_out, int *d_idx, float *d_w,
+                                     void *stream);
+/* The MoE block (see waste_cuda_moe_block) over the same exchange: every
+ * rank normalises the tokens it routes, and each token's h is added once,
+ * on the rank that receives its output. Same call rules as ep_moe_layer_dev
+ * and _rep_dev. */
+int  waste_cuda_ep_moe_block_dev(int layer, int T, const float *d_h,
+                                 float *d_h_out, int *d_idx, float *d_w,
+                                 void *stream);
+int  waste_cuda_ep_moe_block_rep_dev(int layer, int T, const float *d_h,
+                                     float *d_h_out, int *d_idx, float *d_w,
                                      void *stream);
 
 /* Sticky error bits raised on the device. Every wait inside a kernel is
@@ -308,9 +352,13 @@ int waste_cuda_vq_matvec_dev(int G, const uint8_t *const *idx,
  *  - Limit: G * ceil(N/64) * M * 4 bytes must fit the array (G = 32
  *    matrices of 4096 x 4096 fill it exactly); larger calls return
  *    WASTE_CUDA_E_ARG with the sizes in waste_cuda_last_error().
+ *  - The array is taken on the device when waste_cuda_init binds it (the
+ *    library's module is loaded there then, and the array's address looked
+ *    up), so every call after init allocates nothing, the first included.
+ *    Every GPU the library is bound to holds the 32 MiB until the process
+ *    exits. After waste_cuda_shutdown the next init looks the address up
+ *    again.
  *  - The calling thread's current device must be the library's device.
- *    The first call on a device looks up the array's address on it; make
- *    that first call before capturing a stream into a CUDA graph.
  *  - Nothing in the array has to start at zero: each call writes every
  *    partial sum it reads back.
  *  - There is one array per device: calls whose kernels overlap on the GPU

@@ -22,7 +22,19 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libwaste_ref.so")
-REF_TREE = os.environ.get("WARP_REFERENCE", "/root/reference")
+
+
+def reference_tree() -> str | None:
+    """The sqliteai/warp source tree the checker is built from: the
+    WARP_REFERENCE environment variable, else a checkout named `reference`
+    beside this repository. None when neither holds a `src/` directory
+    (machines that only run the prebuilt oracle/_ref)."""
+    cand = os.environ.get("WARP_REFERENCE") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(os.path.join(cand, "src")) else None
+
+
+REF_TREE = reference_tree()
 
 P = C.c_void_p
 
@@ -31,8 +43,10 @@ def build(ref: bool | None = None):
     """make -C oracle (and `ref` when the reference tree is present)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     if ref is None:
-        ref = os.path.isdir(os.path.join(REF_TREE, "src"))
+        ref = REF_TREE is not None
     if ref:
+        if REF_TREE is None:
+            raise FileNotFoundError("the reference tree is not present: set WARP_REFERENCE")
         subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
 
 
@@ -45,7 +59,8 @@ class OrcMoe(C.Structure):
                 ("n_books", C.c_int), ("bank", P), ("rec_bytes", C.c_size_t),
                 ("shared_inter", C.c_int), ("sh_gate", P), ("sh_up", P), ("sh_down", P),
                 ("sh_gate_s", P), ("sh_up_s", P), ("sh_down_s", P), ("sh_bits", C.c_int),
-                ("sh_group", C.c_int)]
+                ("sh_group", C.c_int), ("act_situ", C.c_int), ("situ_beta", C.c_float),
+                ("situ_lbeta", C.c_float)]
 
 
 _orc = None
@@ -78,6 +93,11 @@ def lib() -> C.CDLL:
         L.orc_mvq_rows.argtypes = [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_size_t]
         L.orc_record_check.argtypes = [C.POINTER(OrcMoe), C.c_int, C.c_int]
         L.orc_moe_layer.argtypes = [C.POINTER(OrcMoe), C.c_int, P, P, P, P, C.c_int]
+        L.orc_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
+        L.orc_situ_pair.restype = C.c_float
+        L.orc_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
+        L.orc_moe_block.argtypes = [C.POINTER(OrcMoe), C.c_int, P, P, C.c_float, P, P, P,
+                                    C.c_int]
         L.orc_moe_experts.argtypes = [C.POINTER(OrcMoe), P, P, C.c_int, P, P, C.c_int]
         L.orc_moe_chunk.argtypes = [C.POINTER(OrcMoe), C.c_int, P, C.c_int, P, P, P, C.c_int]
         _orc = L
@@ -121,6 +141,10 @@ def ref() -> C.CDLL | None:
         R.refh_codebooks.restype = C.POINTER(C.c_float)
         R.refh_codebooks.argtypes = [P, C.POINTER(C.c_int)]
         R.refh_free.argtypes = [P]
+        R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
+        R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
+        R.waste_situ_pair.restype = C.c_float
+        R.waste_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
         _ref = R
     return _ref
 
@@ -194,6 +218,9 @@ def _moe_struct(L, keep):
             setattr(s, "sh_" + k, _p(q))
             setattr(s, "sh_" + k + "_s", _p(sc))
         s.sh_bits, s.sh_group = 8, 128
+    s.act_situ = int(getattr(L, "act_situ", 0))
+    s.situ_beta = float(getattr(L, "situ_beta", 0.0))
+    s.situ_lbeta = float(getattr(L, "situ_lbeta", 0.0))
     return s
 
 
@@ -205,6 +232,40 @@ def moe_layer(L, x, fma=1):
     idx = np.empty(L.top_k, dtype=np.int32)
     w = np.empty(L.top_k, dtype=np.float32)
     rc = lib().orc_moe_layer(C.byref(s), L.layer, _p(xx), _p(out), _p(idx), _p(w), fma)
+    if rc:
+        raise RuntimeError("oracle: record check failed")
+    return out, idx, w
+
+
+def situ_pair(g, u, beta, lbeta):
+    """src/model.c:505-509, per element (restatement)."""
+    gg = np.ascontiguousarray(g, dtype=np.float32).ravel()
+    uu = np.ascontiguousarray(u, dtype=np.float32).ravel()
+    f = lib().orc_situ_pair
+    return np.array([f(C.c_float(a), C.c_float(b), C.c_float(beta), C.c_float(lbeta))
+                     for a, b in zip(gg, uu)], dtype=np.float32).reshape(np.shape(g))
+
+
+def rmsnorm(x, w, eps):
+    """src/model.c:132-138 (serial fp32 sum of squares)."""
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    ww = np.ascontiguousarray(w, dtype=np.float32)
+    o = np.empty_like(xx)
+    lib().orc_rmsnorm(_p(o), _p(xx), _p(ww), xx.size, C.c_float(eps))
+    return o
+
+
+def moe_block(L, h, norm_w, eps, fma=1):
+    """h + moe_layer(rmsnorm(h)): (h_out, idx, w)."""
+    keep = []
+    s = _moe_struct(L, keep)
+    hh = np.ascontiguousarray(h, dtype=np.float32)
+    nw = np.ascontiguousarray(norm_w, dtype=np.float32)
+    out = np.empty(L.hidden, dtype=np.float32)
+    idx = np.empty(L.top_k, dtype=np.int32)
+    w = np.empty(L.top_k, dtype=np.float32)
+    rc = lib().orc_moe_block(C.byref(s), L.layer, _p(hh), _p(nw), C.c_float(eps), _p(out),
+                             _p(idx), _p(w), fma)
     if rc:
         raise RuntimeError("oracle: record check failed")
     return out, idx, w
@@ -237,6 +298,30 @@ def moe_chunk(L, x, fma=1):
 
 # ---- the reference, compiled ---------------------------------------------
 
+def ref_rmsnorm(x, w, eps):
+    """The reference's own waste_rmsnorm (src/model.c:132-138), compiled."""
+    R = ref()
+    if R is None:
+        raise RuntimeError("oracle/_ref/libwaste_ref.so is not built")
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    ww = np.ascontiguousarray(w, dtype=np.float32)
+    o = np.empty_like(xx)
+    R.waste_rmsnorm(_p(o), _p(xx), _p(ww), xx.size, C.c_float(eps))
+    return o
+
+
+def ref_situ_pair(g, u, beta, lbeta):
+    """The reference's own waste_situ_pair (src/model.c:505-509), per element."""
+    R = ref()
+    if R is None:
+        raise RuntimeError("oracle/_ref/libwaste_ref.so is not built")
+    gg = np.ascontiguousarray(g, dtype=np.float32).ravel()
+    uu = np.ascontiguousarray(u, dtype=np.float32).ravel()
+    return np.array([R.waste_situ_pair(C.c_float(a), C.c_float(b), C.c_float(beta),
+                                       C.c_float(lbeta)) for a, b in zip(gg, uu)],
+                    dtype=np.float32).reshape(np.shape(g))
+
+
 class RefMoe:
     """One MoE layer inside the reference engine (ref_harness.c)."""
 
@@ -265,6 +350,8 @@ class RefMoe:
         if not self.h:
             raise RuntimeError("reference harness refused the layer "
                                "(the shared width must be a multiple of inter)")
+        if getattr(L, "act_situ", 0):
+            R.refh_moe_set_act(self.h, 1, C.c_float(L.situ_beta), C.c_float(L.situ_lbeta))
         self.L = L
 
     def layer(self, x):

@@ -288,6 +288,16 @@ void *refh_moe_open(int layer, int hidden, int inter, int n_experts, int top_k,
     return h;
 }
 
+/* The model's gated activation (src/model.c:987-990): act_situ selects
+ * waste_situ_pair (K3) in place of SiLU, with its two betas. */
+void refh_moe_set_act(void *p, int act_situ, float beta, float linear_beta)
+{
+    refh_moe *h = (refh_moe *)p;
+    h->m->cfg.act_situ = act_situ;
+    h->m->cfg.situ_beta = beta;
+    h->m->cfg.situ_linear_beta = linear_beta;
+}
+
 /* src/model.c:2713 moe_layer. Returns 0, or the sticky read error code. */
 int refh_moe_layer(void *p, const float *x, float *out, int *routed)
 {

@@ -9,7 +9,7 @@
  * written as explicit fmaf() calls.
  *
  * Parity is pinned: tests/golden/ holds vectors produced by the reference
- * compiled from its own sources (oracle/Makefile), and tests/test_oracle.py
+ * compiled from its own sources (oracle/Makefile), and tests/test_golden.py
  * checks this file against them bit for bit.
  */
 #include "vq3r_oracle.h"
@@ -153,6 +153,21 @@ float orc_dotf(const float *a, const float *b, int n)
 static float orc_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
 static float orc_silu(float v) { return v / (1.0f + expf(-v)); } /* src/model.c:501 */
 
+/* src/model.c:505-509 waste_situ_pair (K3's SiTU): beta*tanh(g/beta)*sigmoid(g),
+ * times lbeta*tanh(u/lbeta) (or u when lbeta <= 0). */
+float orc_situ_pair(float g, float u, float beta, float lbeta)
+{
+    const float a = beta * tanhf(g / beta) / (1.0f + expf(-g));
+    return a * (lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u);
+}
+
+/* The layer's gated activation: SiLU(g)*u, or SiTU when the model sets
+ * act_situ (src/model.c:2900-2904, :2658-2660, :3646-3650, :3687). */
+static float orc_act(const orc_moe *L, float g, float u)
+{
+    return L->act_situ ? orc_situ_pair(g, u, L->situ_beta, L->situ_lbeta) : orc_silu(g) * u;
+}
+
 /* src/model.c:2724-2747. */
 void orc_route(const float *sc, const float *bias, int E, int K, int renorm,
                float routed_scale, int *idx, float *w)
@@ -293,7 +308,7 @@ int orc_moe_experts(const orc_moe *L, const int *idx, const float *w, int K,
         }
         orc_vq_rows(ga, rec + h->gate_off, sc, lut_g, inter, lat / vd, st, en);
         orc_vq_rows(ub, rec + h->up_off, sc + inter, lut_u, inter, lat / vd, st, en);
-        for (int i = 0; i < inter; i++) ga[i] = orc_silu(ga[i]) * ub[i];
+        for (int i = 0; i < inter; i++) ga[i] = orc_act(L, ga[i], ub[i]);
         orc_vq_matvec(acc, rec + h->down_off, sc + 2 * inter, ga, lat, inter,
                       L->books, h->codebook_id + 2 * st, st, en, vd, lut_d, fma);
         const float wj = w[j];
@@ -314,7 +329,7 @@ static void orc_shared_ffn(const orc_moe *L, const float *x, float *out)
     const size_t rb_si = (size_t)((si + g - 1) / g) * g * (L->sh_bits == 4 ? 1 : 2) / 2;
     orc_mvq_rows(a, L->sh_gate, L->sh_gate_s, x, si, hid, g, L->sh_bits, rb_in);
     orc_mvq_rows(b, L->sh_up, L->sh_up_s, x, si, hid, g, L->sh_bits, rb_in);
-    for (int i = 0; i < si; i++) a[i] = orc_silu(a[i]) * b[i];
+    for (int i = 0; i < si; i++) a[i] = orc_act(L, a[i], b[i]);
     orc_mvq_rows(tmp, L->sh_down, L->sh_down_s, a, hid, si, g, L->sh_bits, rb_si);
     for (int i = 0; i < hid; i++) out[i] += tmp[i];
     free(a); free(b); free(tmp);
@@ -398,7 +413,7 @@ int orc_moe_chunk(const orc_moe *L, int layer, const float *x, int nT,
                         inter, lat / vd, st, en);
             orc_vq_rows(ub, rec + h->up_off, s16 + inter,
                         lut_gu + (size_t)(2 * t + 1) * lut_sz, inter, lat / vd, st, en);
-            for (int i = 0; i < inter; i++) ga[i] = orc_silu(ga[i]) * ub[i];
+            for (int i = 0; i < inter; i++) ga[i] = orc_act(L, ga[i], ub[i]);
             orc_vq_matvec(acc, rec + h->down_off, s16 + 2 * inter, ga, lat, inter,
                           L->books, h->codebook_id + 2 * st, st, en, vd, lut_d, fma);
             float *dst = ysum + (size_t)t * lat;
@@ -415,7 +430,7 @@ int orc_moe_chunk(const orc_moe *L, int layer, const float *x, int nT,
         const size_t rb_si = (size_t)((si + g - 1) / g) * g;
         orc_mmq_rows(sa, L->sh_gate, L->sh_gate_s, x, si, hid, nT, g, rb_in);
         orc_mmq_rows(sb, L->sh_up, L->sh_up_s, x, si, hid, nT, g, rb_in);
-        for (int i = 0; i < nT * si; i++) sa[i] = orc_silu(sa[i]) * sb[i];
+        for (int i = 0; i < nT * si; i++) sa[i] = orc_act(L, sa[i], sb[i]);
         orc_mmq_rows(sh, L->sh_down, L->sh_down_s, sa, hid, si, nT, g, rb_si);
         for (int i = 0; i < nT * hid; i++) out[i] += sh[i];
         free(sa); free(sb); free(sh);
@@ -424,5 +439,33 @@ int orc_moe_chunk(const orc_moe *L, int layer, const float *x, int nT,
     if (rw_out) memcpy(rw_out, rw, (size_t)nT * K * sizeof(float));
     free(route); free(rw); free(lut_gu); free(lut_d); free(ga); free(ub);
     free(acc); free(ysum);
+    return rc;
+}
+
+/* src/model.c:132-138 waste_rmsnorm: s accumulated serially in fp32, then
+ * r = 1 / sqrtf(s / n + eps), o[i] = (x[i] * r) * w[i]. */
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps)
+{
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s += x[i] * x[i];
+    const float r = 1.0f / sqrtf(s / (float)n + eps);
+    for (int i = 0; i < n; i++) o[i] = x[i] * r * w[i];
+}
+
+/* The MoE half of a decoder layer, src/model.c:3927-3945 (no attention
+ * residuals): norm = rmsnorm(h, post_attention_layernorm), resid =
+ * moe_layer(norm), h_out[i] = h[i] + resid[i]. */
+int orc_moe_block(const orc_moe *L, int layer, const float *h, const float *norm_w,
+                  float eps, float *h_out, int *idx_out, float *w_out, int fma)
+{
+    const int hid = L->hidden;
+    float *norm = (float *)malloc((size_t)hid * sizeof(float));
+    float *resid = (float *)malloc((size_t)hid * sizeof(float));
+    orc_rmsnorm(norm, h, norm_w, hid, eps);
+    const int rc = orc_moe_layer(L, layer, norm, resid, idx_out, w_out, fma);
+    if (!rc)
+        for (int i = 0; i < hid; i++) h_out[i] = h[i] + resid[i];
+    free(norm);
+    free(resid);
     return rc;
 }

@@ -27,6 +27,10 @@
  *                                              (router-order reduce) and shared FFN
  *   orc_moe_chunk      src/model.c:3512-3693   prefill chunk: ascending expert-id
  *                                              accumulation per token
+ *   orc_situ_pair      src/model.c:505-509     K3's SiTU activation (act_situ)
+ *   orc_rmsnorm        src/model.c:132-138     serial sum of squares, x*r*w
+ *   orc_moe_block      src/model.c:3927-3945   h + moe_layer(rmsnorm(h)): the MoE
+ *                                              half of a decoder layer
  *
  * Parity is pinned against the reference compiled from its own sources
  * (oracle/Makefile -> oracle/_ref/libwaste_ref.so); see tests/golden/.
@@ -86,7 +90,11 @@ typedef struct {
     const int8_t *sh_gate, *sh_up, *sh_down;       /* Q8G rows               */
     const uint16_t *sh_gate_s, *sh_up_s, *sh_down_s;
     int sh_bits, sh_group;
+    int act_situ;               /* 0: SiLU(g)*u; 1: SiTU (K3)               */
+    float situ_beta, situ_lbeta;
 } orc_moe;
+
+float orc_situ_pair(float g, float u, float beta, float lbeta);
 
 /* Returns 0, or -1 when a record header does not describe the record. */
 int orc_record_check(const orc_moe *L, int layer, int expert);
@@ -102,6 +110,12 @@ int orc_moe_experts(const orc_moe *L, const int *idx, const float *w, int K,
 /* nT tokens [nT][hidden] -> out [nT][hidden]; route/rw may be NULL. */
 int orc_moe_chunk(const orc_moe *L, int layer, const float *x, int nT,
                   float *out, int *route, float *rw, int fma);
+
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps);
+
+/* h_out[hidden] = h + moe_layer(rmsnorm(h, norm_w, eps)). */
+int orc_moe_block(const orc_moe *L, int layer, const float *h, const float *norm_w,
+                  float eps, float *h_out, int *idx_out, float *w_out, int fma);
 
 #ifdef __cplusplus
 }

@@ -28,7 +28,9 @@ def skipped_call(rank, world, L, dev):
     limit, rank 0's call gives up on rank 1's flags and reports
     DERR_PEER_WAIT instead of hanging, and the device stays usable. Both
     ranks first make one call together: the first call builds the
-    mailboxes, which takes a collective."""
+    mailboxes, which takes a collective. After the skipped call, both
+    ranks' next call fails (refused, or PEER_WAIT) until the exchange is
+    built again."""
     os.environ["WASTE_CUDA_EP_WAIT_POLLS"] = str(1 << 20)
     ep.setup(rank, world)
     x = synth.activations(500, L.hidden, T=1)
@@ -45,6 +47,27 @@ def skipped_call(rank, world, L, dev):
         errs = wb.device_errors()
         assert errs & wb.DERR_PEER_WAIT, errs
         assert wb.device_errors() == 0       # reading cleared the bits
+    dist.barrier()
+    # The ranks' epochs are now out of step. One more joint call: rank 0,
+    # which saw the bit, is refused on the host; rank 1 launches, and its
+    # waits fail at once on the poison word rank 0 left in its mailbox.
+    # Neither returns outputs as if they were valid.
+    if rank == 0:
+        try:
+            ep.moe_layer_rep_dev(L.layer, 1, dx.data_ptr(), out.data_ptr())
+            raise AssertionError("rank 0's call after a peer wait was not refused")
+        except wb.WasteCudaError as e:
+            assert e.rc == wb.E_DEVICE, e
+    else:
+        ep.moe_layer_rep_dev(L.layer, 1, dx.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        errs = wb.device_errors()
+        assert errs & wb.DERR_PEER_WAIT, errs
+        try:                                  # and now the host refuses too
+            ep.moe_layer_rep_dev(L.layer, 1, dx.data_ptr(), out.data_ptr())
+            raise AssertionError("rank 1's call after a peer wait was not refused")
+        except wb.WasteCudaError as e:
+            assert e.rc == wb.E_DEVICE, e
     dist.barrier()
     ep.shutdown()
     del os.environ["WASTE_CUDA_EP_WAIT_POLLS"]
@@ -67,6 +90,7 @@ def main():
                         L.bank[first * L.rec_bytes:], L.inter, L.hidden, L.stages)
         wb.moe_trunk_load(L.layer, L.n_experts, L.hidden, L.top_k, L.renorm, L.routed_scale,
                           L.router, L.bias, L.shared_inter, L.sh)
+        wb.moe_norm_load(L.layer, synth.norm_weight(80 + L.layer, L.hidden), synth.NORM_EPS)
     T = 3
     dev = torch.device("cuda", local)
 
@@ -104,6 +128,30 @@ def main():
                         assert np.array_equal(idx[t], ri), (mode, "rep", rank, L.layer, t)
                         r = rel_l2(out[t], ro)
                         assert r < TOL, (mode, "rep", rank, L.layer, t, r)
+        # the MoE block (rmsnorm, layer, residual) chained over both layers,
+        # split and replicated
+        for rep_mode in (False, True):
+            h0 = synth.activations(400 + rank * (not rep_mode) + 7 * rep_mode, 768, T=T)
+            h = torch.from_numpy(h0.copy()).to(dev)
+            hn = torch.empty_like(h)
+            ref = h0.copy()
+            for L in layers:
+                call = ep.moe_block_rep_dev if rep_mode else ep.moe_block_dev
+                call(L.layer, T, h.data_ptr(), hn.data_ptr())
+                torch.cuda.synchronize()
+                got = hn.cpu().numpy()
+                hin = h.cpu().numpy()
+                for t in range(T):
+                    ro, _, _ = O.moe_block(L, hin[t], synth.norm_weight(80 + L.layer, 768),
+                                           synth.NORM_EPS)
+                    r = rel_l2(got[t] - hin[t], ro - hin[t])
+                    assert r < TOL, (mode, "block", rep_mode, rank, L.layer, t, r)
+                    ref[t], _, _ = O.moe_block(L, ref[t], synth.norm_weight(80 + L.layer, 768),
+                                               synth.NORM_EPS)
+                h, hn = hn, h
+            fin = h.cpu().numpy()
+            for t in range(T):
+                assert rel_l2(fin[t], ref[t]) < TOL, (mode, "block chain", rep_mode, rank, t)
         assert wb.device_errors() == 0, mode
 
     check("peer memory")                     # the default exchange

@@ -1,6 +1,7 @@
 """Regenerates the golden fixtures in tests/golden/ from the REFERENCE.
 
-Run in a container that has the reference tree (default /root/reference) and
+Run on a machine that has the reference tree (WARP_REFERENCE, or a checkout
+named `reference` beside this repository) and
 oracle/_ref/libwaste_ref.so built from it (make -C oracle ref):
 
     python tests/golden/make_golden.py
@@ -41,7 +42,9 @@ import oracle as O  # noqa: E402
 from warp_b200 import synth  # noqa: E402
 
 OUT = os.path.dirname(os.path.abspath(__file__))
-REF_TREE = os.environ.get("WARP_REFERENCE", "/root/reference")
+REF_TREE = O.REF_TREE
+if REF_TREE is None:
+    raise SystemExit("make_golden.py needs the reference tree: set WARP_REFERENCE")
 
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 from golden_cases import MOE_CASES  # noqa: E402  (shared with the tests)
@@ -140,6 +143,23 @@ def moe_fixtures():
         print(name, "written")
 
 
+NORM_SIZES = (2304, 1024, 7168, 100)
+
+
+def norm_fixture():
+    """The reference's waste_rmsnorm (src/model.c:132-138) on seeded inputs:
+    the rmsnorm in front of every MoE block of a decode step."""
+    res = {}
+    for n in NORM_SIZES:
+        x = synth.activations(7000 + n, n)[0] * np.float32(3.0)
+        w = synth.norm_weight(7100 + n, n)
+        res[f"x{n}"], res[f"w{n}"] = x, w
+        res[f"out{n}"] = O.ref_rmsnorm(x, w, synth.NORM_EPS)
+    res["eps"] = np.float32(synth.NORM_EPS)
+    np.savez_compressed(os.path.join(OUT, "norm.npz"), **res)
+    print("norm.npz written")
+
+
 def main():
     R = O.ref()
     if R is None:
@@ -147,7 +167,11 @@ def main():
     f16_flush_fixture(R)
     lut_matvec_fixtures(R)
     moe_fixtures()
+    norm_fixture()
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["norm"]:
+        norm_fixture()
+    else:
+        main()

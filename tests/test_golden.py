@@ -105,3 +105,19 @@ def test_restatement_vs_reference_live(seed):
                          3, 256, 8)
         yo = O.vq_matvec(idx, sc, x, M, N, books, 3, fma=fma)
         assert np.array_equal(bits(y), bits(yo))
+
+
+def test_rmsnorm_golden():
+    """The MoE block's rmsnorm (src/model.c:132-138) bit for bit."""
+    from golden.make_golden import NORM_SIZES
+    g = load("norm")
+    for n in NORM_SIZES:
+        o = O.rmsnorm(g[f"x{n}"], g[f"w{n}"], float(g["eps"]))
+        assert np.array_equal(bits(o), bits(g[f"out{n}"])), n
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built here")
+def test_rmsnorm_vs_reference_live():
+    x = synth.activations(5, 4096)[0] * np.float32(0.01)
+    w = synth.norm_weight(6, 4096)
+    assert np.array_equal(bits(O.rmsnorm(x, w, 1e-5)), bits(O.ref_rmsnorm(x, w, 1e-5)))

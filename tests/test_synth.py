@@ -8,7 +8,7 @@ import pytest
 import oracle as O
 from warp_b200 import synth
 
-REF_TOOLS = os.path.join(os.environ.get("WARP_REFERENCE", "/root/reference"), "tools")
+REF_TOOLS = os.path.join(O.REF_TREE, "tools") if O.REF_TREE else ""
 
 
 def test_block_roundtrip():

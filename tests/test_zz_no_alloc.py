@@ -13,12 +13,20 @@ point on the same inputs. The checks:
     (2e-5 relative L2). The first call fills the array exactly
     (32 matrices of 4096 x 4096); the second has another shape, so its
     reads cannot lean on what the first left behind;
-  * the second call takes no device memory;
+  * neither call takes device memory;
   * a call one matrix past the limit is refused with WASTE_CUDA_E_ARG before
-    anything is launched.
+    anything is launched;
+  * in a fresh process, the FIRST call after init takes no device memory
+    either: init has already brought the array and the kernels onto the
+    device.
 The module is named to run last, and it also passes on its own in a fresh
 process.
 """
+import os
+import subprocess
+import sys
+import textwrap
+
 import numpy as np
 import pytest
 
@@ -70,8 +78,7 @@ def test_noalloc_matches_matvec_dev_two_calls(cuda_lib):
         torch.cuda.synchronize()
         free1 = torch.cuda.mem_get_info()[0]
         assert wb.launch_count() - n0 == 2          # the library's own kernels ran
-        if k == 1:                                  # set-up is behind us
-            assert free0 - free1 < (2 << 20), "the call took device memory"
+        assert free0 - free1 < (2 << 20), "the call took device memory"
         a, b = y_new.cpu().numpy(), y_ref.cpu().numpy()
         assert np.isfinite(a).all()
         for g in range(G):
@@ -97,3 +104,39 @@ def test_noalloc_refuses_past_the_limit(cuda_lib):
     assert ei.value.rc == wb.E_ARG
     assert "fixed" in str(ei.value)
     assert wb.launch_count() == n0
+
+
+def test_noalloc_first_call_after_init_fresh_process():
+    """A new process: device buffers first, then init, then free memory
+    around the very first call of the entry point."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = textwrap.dedent("""
+        import sys
+        sys.path.insert(0, %r)
+        import numpy as np, torch
+        import warp_b200 as wb
+        from warp_b200 import synth
+        rng = np.random.default_rng(7)
+        G, M, N = 4, 1024, 2304
+        mats = [synth.random_matrix(rng, M, N) for _ in range(G)]
+        d_idx = [torch.from_numpy(m[0]).cuda() for m in mats]
+        d_sc = [torch.from_numpy(m[1].view(np.int16)).cuda() for m in mats]
+        d_x = torch.from_numpy(synth.activations(8, N, T=G)).cuda()
+        y = torch.empty((G, M), dtype=torch.float32, device="cuda")
+        wb.init(0)
+        wb.codebooks_load_f16(synth.codebooks(rng, 3))
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        wb.vq_matvec_dev_noalloc([t.data_ptr() for t in d_idx], [t.data_ptr() for t in d_sc],
+                                 [d_x[g].data_ptr() for g in range(G)],
+                                 [y[g].data_ptr() for g in range(G)], M, N, 0, 3, 0)
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        assert wb.device_errors() == 0
+        assert np.isfinite(y.cpu().numpy()).all()
+        print("TAKEN", free0 - free1)
+    """ % root)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    taken = int(r.stdout.split("TAKEN")[-1].split()[0])
+    assert taken < (2 << 20), f"the first call after init took {taken} bytes of device memory"

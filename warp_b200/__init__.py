@@ -32,7 +32,8 @@ EXPORTS = (
     "waste_cuda_vq_bank_reserve", "waste_cuda_moe_layer_part_dev",
     "waste_cuda_ep_range", "waste_cuda_ep_unique_id", "waste_cuda_ep_init",
     "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev", "waste_cuda_moe_prefill_dev",
-    "waste_cuda_ep_moe_layer_rep_dev",
+    "waste_cuda_ep_moe_layer_rep_dev", "waste_cuda_moe_norm_load", "waste_cuda_moe_block",
+    "waste_cuda_moe_block_dev", "waste_cuda_ep_moe_block_dev", "waste_cuda_ep_moe_block_rep_dev",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -131,6 +132,11 @@ def load_library() -> C.CDLL:
         "waste_cuda_ep_moe_layer_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_layer_rep_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_moe_prefill_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_moe_norm_load": (C.c_int, [C.c_int, C.c_int, P, C.c_float]),
+        "waste_cuda_moe_block": (C.c_int, [C.c_int, P, P, P, P]),
+        "waste_cuda_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_ep_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_ep_moe_block_rep_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -306,6 +312,30 @@ def moe_layer_dev(layer: int, d_x: int, d_out: int, d_idx: int, d_w: int, stream
                                                    C.c_void_p(stream or None)))
 
 
+def moe_norm_load(layer: int, norm_w, eps: float):
+    """The layer's post-attention rmsnorm weight for the MoE block."""
+    w = _f32(norm_w)
+    _check(load_library().waste_cuda_moe_norm_load(layer, w.size, _ptr(w), C.c_float(eps)))
+
+
+def moe_block(layer: int, h, K: int, hidden: int):
+    """h + moe_layer(rmsnorm(h)) on host buffers: (h_out[hidden], idx[K], w[K])."""
+    hh = _f32(h)
+    out = np.empty(hidden, dtype=np.float32)
+    idx = np.empty(K, dtype=np.int32)
+    w = np.empty(K, dtype=np.float32)
+    _check(load_library().waste_cuda_moe_block(layer, _ptr(hh), _ptr(out), _ptr(idx), _ptr(w)))
+    return out, idx, w
+
+
+def moe_block_dev(layer: int, T: int, d_h: int, d_out: int, d_idx: int, d_w: int,
+                  stream: int = 0):
+    """T tokens' h + moe_layer(rmsnorm(h)), device pointers."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_moe_block_dev(layer, T, v(d_h), v(d_out), v(d_idx), v(d_w),
+                                                   v(stream)))
+
+
 def moe_layer_part_dev(layer: int, T: int, d_x: int, d_out: int, sh_t0: int, sh_t1: int,
                        d_idx: int, d_w: int, stream: int = 0):
     """The experts this device holds (+ the shared expert for tokens
@@ -368,8 +398,8 @@ def vq_matvec_dev_noalloc(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, 
     the device's memory up front, or cannot take cudaFree's device-wide
     synchronisation mid-run. Partial sums use a fixed 32 MiB array built
     into the library (G * ceil(N/64) * M * 4 bytes at most; larger calls
-    raise). Calls overlapping on the GPU race on that array; make the first
-    call on a device before any stream capture."""
+    raise). The array is taken when init binds the device, so no call after
+    init allocates; calls overlapping on the GPU race on that array."""
     G = len(idx_ptrs)
     arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
     _check(load_library().waste_cuda_vq_matvec_dev_noalloc(

@@ -499,15 +499,39 @@ __device__ __forceinline__ float *ep_part(const wc_ep_link &l, int r)
     return ep_x(l, r) + (size_t)l.world * l.T * l.hidden;
 }
 
-/* Until every rank's flag (in this rank's mailbox) reaches epoch e. */
-__device__ __forceinline__ bool ep_wait_all(const unsigned int *flags, int world, unsigned int e,
-                                            unsigned int *err, int polls)
+/* Rank r's poison word: set by any rank whose wait on a peer gave up. The
+ * ranks' epochs are out of step from then on (the rank that called alone is
+ * ahead), so a later wait could pass on a stale flag and read a mailbox that
+ * another rank is rewriting; every wait checks this word first and fails
+ * instead. Only new mailboxes (ep_init after ep_shutdown) clear it. */
+__device__ __forceinline__ unsigned int *ep_poison(const wc_ep_link &l, int r)
 {
-    for (int r = 0; r < world; r++) {
+    return reinterpret_cast<unsigned int *>(l.mail[r] + 768);
+}
+
+/* A wait that ran out: the error bit here, and the poison word in every
+ * rank's mailbox, so every rank's next exchange fails too. */
+__device__ __forceinline__ void ep_give_up(const wc_ep_link &l, unsigned int *err)
+{
+    atomicOr(err, WC_ERR_PEER_WAIT);
+    for (int r = 0; r < l.world; r++) st_release_sys(ep_poison(l, r), 1u);
+}
+
+/* Until every rank's flag (in this rank's mailbox) reaches epoch e, or the
+ * exchange is poisoned, or the poll limit runs out (false on either). */
+__device__ __forceinline__ bool ep_wait_all(const wc_ep_link &l, const unsigned int *flags,
+                                            unsigned int e, unsigned int *err)
+{
+    const unsigned int *poison = ep_poison(l, l.rank);
+    if (ld_acquire_sys(poison)) {
+        atomicOr(err, WC_ERR_PEER_WAIT);
+        return false;
+    }
+    for (int r = 0; r < l.world; r++) {
         long long i = 0;
         while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
-            if (++i >= polls) {
-                atomicOr(err, WC_ERR_PEER_WAIT);
+            if (++i >= l.wait_polls || ((i & 255) == 0 && ld_acquire_sys(poison))) {
+                ep_give_up(l, err);
                 return false;
             }
             __nanosleep(64);
@@ -538,11 +562,11 @@ __global__ void __launch_bounds__(256) ep_publish_kernel(wc_ep_link l, const flo
 /* Layer end: once every rank's partial sums of this rank's tokens are in,
  * out[t] = the sum over ranks in rank order. grid (ceil(hidden/256), T). */
 __global__ void __launch_bounds__(256) ep_finalize_kernel(wc_ep_link l, float *out,
-                                                         unsigned int *err)
+                                                         const float *resid, unsigned int *err)
 {
     __shared__ int ok;
     const unsigned int e = *ep_epoch(l);
-    if (threadIdx.x == 0) ok = ep_wait_all(ep_pflags(l, l.rank), l.world, e, err, l.wait_polls);
+    if (threadIdx.x == 0) ok = ep_wait_all(l, ep_pflags(l, l.rank), e, err);
     __syncthreads();
     if (!ok) return;
     for (int r = 0; r < l.world; r++) (void)ld_acquire_sys(ep_pflags(l, l.rank) + r);
@@ -552,6 +576,7 @@ __global__ void __launch_bounds__(256) ep_finalize_kernel(wc_ep_link l, float *o
     float y = 0.0f;
     for (int r = 0; r < l.world; r++)
         y = __fadd_rn(y, __ldcv(part + ((size_t)r * l.T + t) * l.hidden + i));
+    if (resid) y = __fadd_rn(resid[(size_t)t * l.hidden + i], y);   /* the block's h + moe */
     out[(size_t)t * l.hidden + i] = y;
 }
 
@@ -578,6 +603,31 @@ __device__ __forceinline__ float warp_sum(float v)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+/* The reference's rmsnorm (src/model.c:132-138) of x[0..n) in shared
+ * memory, in place: r = 1 / sqrtf(sum(x*x) / n + eps), x[i] = (x[i]*r)*w[i].
+ * The sum of squares is a fixed tree (thread strides, warp shuffles, warps
+ * in order), so every block that normalises the same x gets the same bits.
+ * red: blockDim/32 + 1 floats of shared memory. Every thread must call it. */
+__device__ __forceinline__ void block_rmsnorm(float *x, int n, const float *__restrict__ w,
+                                              float eps, float *red)
+{
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) t = __fadd_rn(t, red[k]);
+        red[32] = 1.0f / sqrtf(t / (float)n + eps);
+    }
+    __syncthreads();
+    const float r = red[32];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__fmul_rn(x[i], r), __ldg(w + i));
+    __syncthreads();
 }
 
 /* fp32 dot of w[0..n) with xs (shared memory), every load issued first.
@@ -728,6 +778,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     /* shared memory: barrier | x [lat] | staged weight rows | staged scales */
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ float part[kRouterBlock / 32];
+    __shared__ float nred[33];
     __shared__ unsigned int ticket;
     __shared__ int ep_fail;
     if (threadIdx.x == 0) ep_fail = 0;
@@ -779,16 +830,30 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     pdl_wait();
     if (threadIdx.x == 0) {
         if (a.ep.on) {            /* every rank's tokens are in this mailbox */
-            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err,
-                             a.ep.wait_polls))
+            if (!ep_wait_all(a.ep, ep_xflags(a.ep, a.ep.rank), *ep_epoch(a.ep), a.ws.err))
                 ep_fail = 1;
             asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
         }
+        /* x is complete: gate/up may build its tables (released even when a
+         * peer wait failed, so no tile waits for it in vain). With the
+         * rmsnorm in front, block 0 releases it once the normalised x is
+         * written (below). */
+        if (b == 0 && !a.norm_w) st_release(a.ws.x_flag + t, 1u);
         bulk_g2s(xs, a.x + (size_t)t * lat, (uint32_t)lat * 4, bar);
     }
     __syncthreads();
-    const bool ok = mbar_wait(bar, 0) && !ep_fail;   /* a missing peer: no dot products */
+    /* block-uniform (the rmsnorm below synchronises the block) */
+    const bool ok = __syncthreads_and(mbar_wait(bar, 0) && !ep_fail);   /* a missing peer: no dot products */
     if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    if (a.norm_w) {                  /* the MoE block: route and run on rmsnorm(x) */
+        if (ok) block_rmsnorm(xs, lat, a.norm_w, a.norm_eps, nred);
+        if (b == 0) {
+            for (int i = threadIdx.x; ok && i < lat; i += blockDim.x)
+                a.ws.xn[(size_t)t * lat + i] = xs[i];
+            __syncthreads();
+            if (threadIdx.x == 0) st_release(a.ws.x_flag + t, 1u);
+        }
+    }
     if (is_router) {
         const int lr = warp / kRouterSplit, qtr = warp % kRouterSplit;
         const int per = (n4 + kRouterSplit - 1) / kRouterSplit;
@@ -907,6 +972,7 @@ template <int NK>
 __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args a, RouterTGeom rg)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ float nred[33];
     __shared__ unsigned int ticket;
     __shared__ int ep_fail;
     if (threadIdx.x == 0) ep_fail = 0;
@@ -944,17 +1010,29 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     pdl_wait();
     if (threadIdx.x == 0) {
         if (a.ep.on) {            /* every rank's tokens are in this mailbox */
-            if (!ep_wait_all(ep_xflags(a.ep, a.ep.rank), a.ep.world, *ep_epoch(a.ep), a.ws.err,
-                             a.ep.wait_polls))
+            if (!ep_wait_all(a.ep, ep_xflags(a.ep, a.ep.rank), *ep_epoch(a.ep), a.ws.err))
                 ep_fail = 1;
             asm volatile("fence.proxy.async.global;" ::: "memory");   /* for the bulk copy */
         }
+        if (b == 0 && !a.norm_w)  /* the group's x is complete (see router_kernel) */
+            for (int k = 0; k < nt; k++) st_release(a.ws.x_flag + t0 + k, 1u);
         mbar_expect_tx(bar, (uint32_t)nt * lat * 4);
         bulk_g2s(xs, a.x + (size_t)t0 * lat, (uint32_t)nt * lat * 4, bar);
     }
     __syncthreads();
-    const bool ok = mbar_wait(bar, 0) && !ep_fail;
+    const bool ok = __syncthreads_and(mbar_wait(bar, 0) && !ep_fail);
     if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+    if (a.norm_w) {                  /* rmsnorm of each token, as in router_kernel */
+        for (int k = 0; k < nt && ok; k++) block_rmsnorm(xs + (size_t)k * lat, lat, a.norm_w,
+                                                         a.norm_eps, nred);
+        if (b == 0) {
+            for (int i = threadIdx.x; ok && i < nt * lat; i += blockDim.x)
+                a.ws.xn[(size_t)t0 * lat + i] = xs[i];
+            __syncthreads();
+            if (threadIdx.x == 0)
+                for (int k = 0; k < nt; k++) st_release(a.ws.x_flag + t0 + k, 1u);
+        }
+    }
     const float4 *x4 = reinterpret_cast<const float4 *>(xs);
     if (ok && is_router) {
         const int per = (n4 + kRouterSplit - 1) / kRouterSplit;
@@ -1122,24 +1200,39 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
     }
     /* routing-independent: x slice, codebook rows, the table — built while
      * the route is computed, unless this device holds so few of the experts
-     * (gu_eg > 0) that most tiles find no work: then the route comes first */
+     * (gu_eg > 0) that most tiles find no work: then the route comes first.
+     * With the router in the chain this grid starts while the router runs,
+     * and the router itself may still be waiting on whatever wrote x (the
+     * previous layer's combine, when layers are chained on one stream): x
+     * is read only after the router's x flag, which the router releases once
+     * its own grid-dependency wait has passed. The codebook rows are
+     * constants and come first. Without the router this grid is launched in
+     * stream order, after x is complete. */
     const bool route_first = a.partial_bank && a.gu_eg > 0;
+    const float *xsrc = a.norm_w ? a.ws.xn : a.x;   /* the block: the router's rmsnorm(x) */
     BookRows<ST, kGuBooks> books;
     if (!route_first) {
         books.load(a.books, bk.cb_base + kind * ST);
+        if (a.router) {
+            if (threadIdx.x == 0) go = wait_flag(a.ws.x_flag + t, a.ws.err);
+            __syncthreads();
+            if (!go) return;
+        }
         if ((int)threadIdx.x < nvs * kVecDim)
-            sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
+            sm.xs[threadIdx.x] = ld_pin_f32(xsrc + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
         __syncthreads();
         books.build(sm.lut, sm.xs, nvs);
     }
     if (a.router) {
         if (threadIdx.x == 0) {
             go = wait_flag(a.ws.route_flag + t, a.ws.err);
-            /* the last tile of this token to pass clears the flag */
+            /* the last tile of this token to pass clears both flags (every
+             * tile passed the x flag before the route flag) */
             const int per_t = 2 * g.ns * g.groups;
             if (atomicAdd(a.ws.route_pass + t, 1u) == (unsigned)per_t - 1) {
                 a.ws.route_pass[t] = 0;
                 a.ws.route_flag[t] = 0;
+                a.ws.x_flag[t] = 0;
             }
         }
         __syncthreads();
@@ -1172,7 +1265,7 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
         nm = min(g.EG, s_nloc - j0);
         books.load(a.books, bk.cb_base + kind * ST);
         if ((int)threadIdx.x < nvs * kVecDim)
-            sm.xs[threadIdx.x] = ld_pin_f32(a.x + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
+            sm.xs[threadIdx.x] = ld_pin_f32(xsrc + (size_t)t * bk.lat + (size_t)v0 * kVecDim + threadIdx.x);
         __syncthreads();
         books.build(sm.lut, sm.xs, nvs);
     } else {
@@ -1610,6 +1703,8 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         }
         if (sh_here) y = __fadd_rn(y, shv);
         if (!a.ep.on) {
+            /* the block's residual add, h + moe (src/model.c:3945) */
+            if (a.resid) y = __fadd_rn(__ldcg(a.resid + (size_t)t * bk.lat + i), y);
             a.out[(size_t)t * bk.lat + i] = y;
         } else if (!a.ep.rep) {   /* straight into the token's rank, over NVLink */
             const int owner = t / a.ep.T, tl = t % a.ep.T;
@@ -1849,7 +1944,8 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
     n += (size_t)T * E;
     n += (size_t)T * si * 3 + (size_t)T * lat;
     n += (size_t)T * K * inter;              /* h */
-    return n + 256 + 64;                     /* + control words */
+    n += (size_t)T * lat;                    /* xn */
+    return n + 512 + 64;                     /* + control words */
 }
 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
@@ -1859,12 +1955,14 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     const TileGeom d = make_geom(lat, inter, 1, kVsDown, stages, 448);
     float *p = base;
     /* control words first (zeroed once at allocation, self-resetting):
-     * tickets [0,64), route flags [64,128), pass counters [128,192), err */
+     * tickets [0,64), route flags [64,128), pass counters [128,192), err
+     * 192, x flags [256,320) */
     ws->tickets = reinterpret_cast<unsigned int *>(p);
     ws->route_flag = ws->tickets + 64;
     ws->route_pass = ws->tickets + 128;
     ws->err = ws->tickets + 192;
-    p += 256;
+    ws->x_flag = ws->tickets + 256;
+    p += 512;
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
     ws->p_d = p; p += (size_t)T * K * d.ns * lat;
     ws->logits = p; p += (size_t)T * E;
@@ -1872,7 +1970,8 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     ws->sh_u = p; p += (size_t)T * si;
     ws->sh_h = p; p += (size_t)T * si;
     ws->sh_out = p; p += (size_t)T * lat;
-    ws->h = p;
+    ws->h = p; p += (size_t)T * K * inter;
+    ws->xn = p;
 }
 
 extern "C" int wc_moe_supported(const wc_moe_args *a)
@@ -1905,6 +2004,33 @@ static __device__ __align__(256) float g_noalloc_part[WC_NOALLOC_PART_FLOATS];
 extern "C" int wc_noalloc_part(float **ptr)
 {
     return (int)cudaGetSymbolAddress((void **)ptr, g_noalloc_part);
+}
+
+/* Set-up of the allocation-free matvec on the current device: the array's
+ * address, and the kernels that entry point launches, loaded now. Under
+ * lazy module loading the module (and with it the 32 MiB array) and each
+ * kernel's code are otherwise brought onto the device at their first use,
+ * which would make that first call allocate. */
+extern "C" int wc_noalloc_setup(float **ptr)
+{
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaGetSymbolAddress((void **)ptr, g_noalloc_part);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_rows_kernel<3, 256, kVsMatvec>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_rows_kernel<3, 512, kVsMatvec>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_rows_kernel<2, 256, kVsMatvec>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_rows_kernel<2, 512, kVsMatvec>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_tiles_kernel<3, 512>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_tiles_kernel<2, 512>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, matvec_reduce_kernel);
+    return (int)e;
+}
+
+/* The architecture the loaded kernels were compiled for (100 = sm_100). */
+extern "C" int wc_binary_version(void)
+{
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, matvec_reduce_kernel) != cudaSuccess) return -1;
+    return fa.binaryVersion;
 }
 
 extern "C" void wc_count_launches(int n) { g_launches += (uint64_t)n; }
@@ -1979,6 +2105,23 @@ extern "C" int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *s
     return (int)cudaGetLastError();
 }
 
+/* out[i] = resid[i] + y[i] (the block's residual add where no kernel of
+ * the layer can do it: after an NCCL reduction). out may alias y. */
+__global__ void resid_add_kernel(float *out, const float *resid, const float *y, size_t n)
+{
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fadd_rn(resid[i], y[i]);
+}
+
+extern "C" int wc_resid_add_launch(float *out, const float *resid, const float *y, size_t n,
+                                   void *stream)
+{
+    resid_add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(out, resid,
+                                                                                 y, n);
+    g_launches += 1;
+    return (int)cudaGetLastError();
+}
+
 extern "C" int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigned int *err,
                                     void *stream)
 {
@@ -1988,11 +2131,11 @@ extern "C" int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigne
     return (int)cudaGetLastError();
 }
 
-extern "C" int wc_ep_finalize_launch(const wc_ep_link *l, float *out, unsigned int *err,
-                                     void *stream)
+extern "C" int wc_ep_finalize_launch(const wc_ep_link *l, float *out, const float *resid,
+                                     unsigned int *err, void *stream)
 {
     ep_finalize_kernel<<<dim3((l->hidden + 255) / 256, l->T), 256, 0, (cudaStream_t)stream>>>(
-        *l, out, err);
+        *l, out, resid, err);
     g_launches += 1;
     return (int)cudaGetLastError();
 }

@@ -62,10 +62,14 @@ typedef struct {
     int si;
     int8_t *d_shg, *d_shu, *d_shd;
     uint16_t *d_shg_s, *d_shu_s, *d_shd_s;
-    /* the host-buffer layer call as one CUDA graph (copies in, kernels,
-     * copies out), rebuilt when anything it points at may have moved */
-    cudaGraphExec_t gx;
-    unsigned gx_epoch;
+    /* the MoE block's rmsnorm (post_attention_layernorm) */
+    float *d_norm;
+    float norm_eps;
+    /* the host-buffer layer and block calls as one CUDA graph each (copies
+     * in, kernels, copies out), rebuilt when anything they point at may
+     * have moved */
+    cudaGraphExec_t gx, gxb;
+    unsigned gx_epoch, gxb_epoch;
 } wc_layer;
 
 static struct {
@@ -132,7 +136,15 @@ static struct {
     unsigned char *mail[WC_EP_MAX];
     int mail_T, mail_hidden;
     int wait_polls;               /* peer-wait limit, WASTE_CUDA_EP_WAIT_POLLS */
+    int poisoned;                 /* a peer wait gave up: layer calls refused until
+                                     ep_shutdown + ep_init build new mailboxes */
 } EP;
+
+/* The allocation-free matvec's fixed partial-sum array on the bound device
+ * (set by init, cleared by shutdown). */
+_Static_assert(WASTE_CUDA_NOALLOC_SCRATCH_BYTES == WC_NOALLOC_PART_FLOATS * sizeof(float),
+               "header and kernel disagree on the fixed scratch size");
+static float *g_noalloc_part;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
@@ -176,6 +188,7 @@ static unsigned read_device_errors(int clear)
     if (cudaStreamSynchronize(S.stream) != cudaSuccess) return ~0u;
     if (cudaMemcpy(&v, err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return ~0u;
     if (v && clear) cudaMemset(err, 0, sizeof v);
+    if ((v & WC_ERR_PEER_WAIT) && EP.active) EP.poisoned = 1;
     return v;
 }
 
@@ -276,6 +289,9 @@ static int init_locked(int device)
                                    p.major, p.minor);
     CK(cudaSetDevice(dev), "cudaSetDevice");
     CK(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    /* the allocation-free matvec's array and kernels, on the device now */
+    CK((cudaError_t)wc_noalloc_setup(&g_noalloc_part), "fixed scratch set-up");
+    if (!g_noalloc_part) return fail(WASTE_CUDA_E_DEVICE, "fixed scratch address: NULL");
     CK(cudaMalloc((void **)&S.d_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "idx");
     CK(cudaMalloc((void **)&S.d_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "w");
     CK(cudaMallocHost((void **)&S.h_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "h_idx");
@@ -306,6 +322,8 @@ const char *waste_cuda_backend_name(void) { return S.inited ? S.name : NULL; }
 static void free_layer(wc_layer *L)
 {
     if (L->gx) cudaGraphExecDestroy(L->gx);
+    if (L->gxb) cudaGraphExecDestroy(L->gxb);
+    cudaFree(L->d_norm);
     cudaFree(L->d_base);
     cudaFree(L->d_router); cudaFree(L->d_bias);
     cudaFree(L->d_shg); cudaFree(L->d_shu); cudaFree(L->d_shd);
@@ -329,6 +347,7 @@ void waste_cuda_shutdown(void)
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
         cudaStreamDestroy(S.stream);
         memset(&S, 0, sizeof S);
+        g_noalloc_part = NULL;
     }
     pthread_mutex_unlock(&g_mu);
 }
@@ -746,6 +765,31 @@ out:
     return rc;
 }
 
+int waste_cuda_moe_norm_load(int layer, int hidden, const float *norm_w, float eps)
+{
+    int rc = 0;
+    if (layer < 0 || layer >= WC_MAX_LAYERS || hidden <= 0 || !norm_w || !(eps >= 0.0f))
+        return fail(WASTE_CUDA_E_ARG, "moe_norm_load: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    wc_layer *L = &S.layer[layer];
+    if (!L->trunk || L->hidden != hidden) {
+        rc = fail(WASTE_CUDA_E_ARG, "moe_norm_load: layer %d's trunk (width %d) is not "
+                  "loaded, or its width is not %d", layer, L->hidden, hidden);
+        goto out;
+    }
+    g_epoch++;
+    cudaFree(L->d_norm);
+    L->d_norm = NULL;
+    CK(cudaMalloc((void **)&L->d_norm, (size_t)hidden * sizeof(float)), "norm weight");
+    CK(cudaMemcpy(L->d_norm, norm_w, (size_t)hidden * sizeof(float), cudaMemcpyHostToDevice),
+       "norm weight H2D");
+    L->norm_eps = eps;
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
 /* ---- expert loop ------------------------------------------------------- */
 
 static int layer_ready(int layer, int lat, int inter, wc_layer **out)
@@ -936,6 +980,38 @@ int waste_cuda_moe_layer_dev(int layer, const float *d_x, float *d_out, int *d_i
     a.idx_out = d_idx;
     a.w_out = d_w;
     CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "layer kernels");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* The block's extra arguments: the rmsnorm in front and the residual add. */
+static int block_args(wc_moe_args *a, const wc_layer *L, int layer, const float *d_h)
+{
+    if (!L->d_norm)
+        return fail(WASTE_CUDA_E_NOBANK, "layer %d: no norm weight (waste_cuda_moe_norm_load)",
+                    layer);
+    a->norm_w = L->d_norm;
+    a->norm_eps = L->norm_eps;
+    a->resid = d_h;
+    return 0;
+}
+
+int waste_cuda_moe_block_dev(int layer, int T, const float *d_h, float *d_h_out, int *d_idx,
+                             float *d_w, void *stream)
+{
+    int rc = 0;
+    wc_moe_args a;
+    wc_layer *L = NULL;
+    if (!d_h || !d_h_out || !d_idx || !d_w) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if ((rc = layer_args(layer, T, 0, &a, &L))) goto out;
+    if ((rc = block_args(&a, L, layer, d_h))) goto out;
+    a.x = d_h;
+    a.out = d_h_out;
+    a.idx_out = d_idx;
+    a.w_out = d_w;
+    CK((cudaError_t)wc_moe_launch(&a, stream ? stream : (void *)S.stream), "block kernels");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -1231,6 +1307,7 @@ static void ep_shutdown_locked(void)
     EP.d_xall = EP.d_outall = NULL;
     EP.all_floats = 0;
     EP.active = EP.rank = EP.world = 0;
+    EP.poisoned = 0;
     g_epoch++;
 }
 
@@ -1245,7 +1322,7 @@ void waste_cuda_ep_shutdown(void)
  * tokens and receives their outputs. rep = 1: every rank brings the same T
  * tokens and receives all of their outputs. */
 static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx, float *d_w,
-                    void *stream, int rep)
+                    void *stream, int rep, int block)
 {
     int rc = 0;
     wc_moe_args a;
@@ -1253,9 +1330,19 @@ static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx
     if (!d_x || !d_out || T <= 0) return fail(WASTE_CUDA_E_ARG, "ep_moe_layer: bad arguments");
     pthread_mutex_lock(&g_mu);
     if (!EP.active) { rc = fail(WASTE_CUDA_E_ARG, "ep_moe_layer before ep_init"); goto out; }
+    if (EP.poisoned) {
+        rc = fail(WASTE_CUDA_E_DEVICE, "ep_moe_layer: an earlier call gave up waiting on a "
+                  "peer; the ranks' exchange is out of step until waste_cuda_ep_shutdown and "
+                  "waste_cuda_ep_init");
+        goto out;
+    }
     const int Ta = rep ? T : T * EP.world;
     const int tr = rep ? 0 : EP.rank;            /* this rank's tokens in the routes */
     if ((rc = layer_args(layer, Ta, 1, &a, &L))) goto out;
+    /* the block: every rank normalises the tokens it routes; the residual
+     * is added once, where the token's output is finished (the finalize of
+     * the peer exchange, or after the NCCL reduction) */
+    if (block && (rc = block_args(&a, L, layer, NULL))) goto out;
     {
         int r0, rn;
         split_range(L->E, EP.rank, EP.world, &r0, &rn);
@@ -1321,7 +1408,8 @@ static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx
     a.sh_t1 = rep ? (EP.rank + 1) * T / EP.world : EP.rank * T + T;
     CK((cudaError_t)wc_moe_launch(&a, st), "layer kernels");
     if (a.ep.on) {
-        CK((cudaError_t)wc_ep_finalize_launch(&a.ep, d_out, a.ws.err, st), "ep finalize");
+        CK((cudaError_t)wc_ep_finalize_launch(&a.ep, d_out, block ? d_x : NULL, a.ws.err, st),
+           "ep finalize");
     } else if (!rep) {
         const ncclResult_t r = EP.reduce_scatter(EP.d_outall, d_out, per, ncclFloat32, ncclSum,
                                                  EP.comm, st);
@@ -1331,6 +1419,8 @@ static int ep_layer(int layer, int T, const float *d_x, float *d_out, int *d_idx
                                              EP.comm, st);
         if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllReduce"); goto out; }
     }
+    if (block && !a.ep.on)
+        CK((cudaError_t)wc_resid_add_launch(d_out, d_x, d_out, per, st), "residual add");
     if (d_idx) CK(cudaMemcpyAsync(d_idx, S.d_idx + (size_t)tr * kb, kb * sizeof(int),
                                   cudaMemcpyDeviceToDevice, st), "route copy");
     if (d_w) CK(cudaMemcpyAsync(d_w, S.d_w + (size_t)tr * kb, kb * sizeof(float),
@@ -1343,13 +1433,25 @@ out:
 int waste_cuda_ep_moe_layer_dev(int layer, int T, const float *d_x, float *d_out, int *d_idx,
                                 float *d_w, void *stream)
 {
-    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 0);
+    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 0, 0);
 }
 
 int waste_cuda_ep_moe_layer_rep_dev(int layer, int T, const float *d_x, float *d_out,
                                     int *d_idx, float *d_w, void *stream)
 {
-    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 1);
+    return ep_layer(layer, T, d_x, d_out, d_idx, d_w, stream, 1, 0);
+}
+
+int waste_cuda_ep_moe_block_dev(int layer, int T, const float *d_h, float *d_h_out, int *d_idx,
+                                float *d_w, void *stream)
+{
+    return ep_layer(layer, T, d_h, d_h_out, d_idx, d_w, stream, 0, 1);
+}
+
+int waste_cuda_ep_moe_block_rep_dev(int layer, int T, const float *d_h, float *d_h_out,
+                                    int *d_idx, float *d_w, void *stream)
+{
+    return ep_layer(layer, T, d_h, d_h_out, d_idx, d_w, stream, 1, 1);
 }
 
 /* The host-buffer layer call captured once: H2D of x, the kernel chain,
@@ -1373,11 +1475,12 @@ static int ensure_res(int lat)
     return 0;
 }
 
-static int layer_graph(wc_layer *L, const wc_moe_args *a, size_t xb)
+static int layer_graph(cudaGraphExec_t *gx, unsigned *gx_epoch, const wc_moe_args *a,
+                       size_t xb)
 {
     int rc = 0;
-    if (L->gx && L->gx_epoch == g_epoch) return 0;
-    if (L->gx) { cudaGraphExecDestroy(L->gx); L->gx = NULL; }
+    if (*gx && *gx_epoch == g_epoch) return 0;
+    if (*gx) { cudaGraphExecDestroy(*gx); *gx = NULL; }
     cudaGraph_t g = NULL;
     CK(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
     cudaError_t e = cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream);
@@ -1385,23 +1488,24 @@ static int layer_graph(wc_layer *L, const wc_moe_args *a, size_t xb)
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(S.h_res, S.d_res, res_floats(S.res_lat) * sizeof(float),
                             cudaMemcpyDeviceToHost, S.stream);
-    (void)L;
     const cudaError_t ee = cudaStreamEndCapture(S.stream, &g);   /* always end it */
     if (e == cudaSuccess) e = ee;
-    if (e == cudaSuccess) e = cudaGraphInstantiate(&L->gx, g, 0);
+    if (e == cudaSuccess) e = cudaGraphInstantiate(gx, g, 0);
     if (g) cudaGraphDestroy(g);
     if (e != cudaSuccess) {
-        L->gx = NULL;
+        *gx = NULL;
         cudaGetLastError();
         rc = cuda_fail(e, "layer graph");
         goto out;
     }
-    L->gx_epoch = g_epoch;
+    *gx_epoch = g_epoch;
 out:
     return rc;
 }
 
-int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, float *weights)
+/* The host-buffer layer call (block = 0) and block call (block = 1). */
+static int host_layer(int layer, const float *x, float *out, int *routed, float *weights,
+                      int block)
 {
     int rc = 0;
     wc_moe_args a;
@@ -1409,6 +1513,7 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
     if (!x || !out) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
     pthread_mutex_lock(&g_mu);
     if ((rc = layer_args(layer, 1, 0, &a, &L))) goto out;
+    if (block && (rc = block_args(&a, L, layer, S.d_x))) goto out;
     const size_t xb = (size_t)L->hidden * sizeof(float);
     a.x = S.d_x;
     a.out = S.d_out;
@@ -1424,8 +1529,9 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
         a.idx_out = (int *)(S.d_res + lat);
         a.w_out = S.d_res + lat + WC_MAX_TOPK;
         a.ws.err = (unsigned int *)(S.d_res + lat + 2 * WC_MAX_TOPK);
-        if ((rc = layer_graph(L, &a, xb))) goto out;
-        CK(cudaGraphLaunch(L->gx, S.stream), "layer graph");
+        if ((rc = block ? layer_graph(&L->gxb, &L->gxb_epoch, &a, xb)
+                        : layer_graph(&L->gx, &L->gx_epoch, &a, xb))) goto out;
+        CK(cudaGraphLaunch(block ? L->gxb : L->gx, S.stream), "layer graph");
         CK(cudaStreamSynchronize(S.stream), "moe layer");
         const unsigned int err = *(const unsigned int *)(S.h_res + lat + 2 * WC_MAX_TOPK);
         if (err) {
@@ -1457,6 +1563,16 @@ int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, flo
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
+}
+
+int waste_cuda_moe_layer(int layer, const float *x, float *out, int *routed, float *weights)
+{
+    return host_layer(layer, x, out, routed, weights, 0);
+}
+
+int waste_cuda_moe_block(int layer, const float *h, float *h_out, int *routed, float *weights)
+{
+    return host_layer(layer, h, h_out, routed, weights, 1);
 }
 
 /* ---- single kernels (host buffers) -------------------------------------- */
@@ -1571,19 +1687,14 @@ out:
 }
 
 /* Allocation-free form of vq_matvec_dev. The partial sums go to the fixed
- * device array behind wc_noalloc_part instead of the growable scratch, so
+ * device array behind wc_noalloc_setup instead of the growable scratch, so
  * no call makes cudaMalloc or cudaFree (whose implicit device-wide
  * synchronisation a running decode loop cannot afford, and which can fail
  * once the caller has reserved the device's memory). The array's address
- * is looked up once per device ordinal and kept here, outside S, so that
- * it survives shutdown/init: the module (and with it the array) stays
- * loaded while the device's primary context lives. Every partial a call
- * reads back is written earlier in the same call, so nothing has to start
- * at zero. */
-#define WC_NOALLOC_MAX_DEV 64
-_Static_assert(WASTE_CUDA_NOALLOC_SCRATCH_BYTES == WC_NOALLOC_PART_FLOATS * sizeof(float),
-               "header and kernel disagree on the fixed scratch size");
-static float *g_noalloc_part[WC_NOALLOC_MAX_DEV];
+ * is looked up, and its module and kernels loaded, when init binds the
+ * device; shutdown forgets it, and the next init looks it up again. Every
+ * partial a call reads back is written earlier in the same call, so
+ * nothing has to start at zero. */
 
 int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
                                      const uint16_t *const *scale, const float *const *x,
@@ -1609,19 +1720,11 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
     }
     int cur = -1;
     CK(cudaGetDevice(&cur), "cudaGetDevice");
-    if (cur != S.device || cur < 0 || cur >= WC_NOALLOC_MAX_DEV) {
+    if (!S.inited || cur != S.device || !g_noalloc_part) {
         rc = fail(WASTE_CUDA_E_ARG, "matvec_dev_noalloc: current device %d is not the "
-                  "library's device %d", cur, S.device);
+                  "library's device %d (waste_cuda_init binds it)", cur,
+                  S.inited ? S.device : -1);
         goto out;
-    }
-    if (!g_noalloc_part[cur]) {       /* once per device, with it current */
-        float *p = NULL;
-        CK((cudaError_t)wc_noalloc_part(&p), "fixed scratch address");
-        if (!p) {
-            rc = fail(WASTE_CUDA_E_DEVICE, "fixed scratch address: NULL");
-            goto out;
-        }
-        g_noalloc_part[cur] = p;
     }
     static wc_matvec_args a;
     memset(&a, 0, sizeof a);
@@ -1630,7 +1733,7 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
         a.idx[g] = idx[g]; a.scale[g] = scale[g]; a.x[g] = x[g]; a.y[g] = y[g];
     }
     a.books = S.d_books;
-    a.part = g_noalloc_part[cur];
+    a.part = g_noalloc_part;
     CK((cudaError_t)wc_matvec_launch(&a, stream ? stream : (void *)S.stream), "matvec");
 out:
     pthread_mutex_unlock(&g_mu);

@@ -45,9 +45,12 @@ typedef struct {
     float *logits;     /* [T][E]                                            */
     float *sh_g, *sh_u, *sh_h, *sh_out;   /* shared expert [T][si] / [T][hid] */
     float *h;          /* [T][K][inter] SiLU(g)*u, batched calls only        */
+    float *xn;         /* [T][lat] rmsnorm(x), the MoE block only            */
     unsigned int *tickets;  /* [T] router blocks done; zero between launches   */
     unsigned int *route_flag;  /* [T] 1 once routing is published            */
     unsigned int *route_pass;  /* [T] gate/up tiles that have seen the flag   */
+    unsigned int *x_flag;      /* [T] 1 once the router's dependency wait has
+                                  passed: x is complete                        */
     unsigned int *err;         /* sticky device error bits (WC_ERR_*)         */
 } wc_moe_ws;
 
@@ -65,6 +68,8 @@ typedef struct {
  *   +256   part flags  [WC_EP_MAX] : epoch of rank r's partial sums, set by r
  *   +512   combine ticket (local use)
  *   +640   epoch counter (local use: bumped once per layer call)
+ *   +768   poison word: set in every mailbox by a rank whose peer wait
+ *          gave up; every later wait fails at once (ep_init clears it)
  *   +1024  x   [world][T][hidden]  : every rank's tokens
  *   then   part[world][T][hidden]  : every rank's partial sums of this
  *                                    rank's tokens
@@ -81,7 +86,10 @@ typedef struct {
 } wc_ep_link;
 
 int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigned int *err, void *stream);
-int wc_ep_finalize_launch(const wc_ep_link *l, float *out, unsigned int *err, void *stream);
+int wc_ep_finalize_launch(const wc_ep_link *l, float *out, const float *resid,
+                          unsigned int *err, void *stream);
+/* out[i] = resid[i] + y[i], i < n (out may alias y). */
+int wc_resid_add_launch(float *out, const float *resid, const float *y, size_t n, void *stream);
 
 typedef struct {
     wc_bank bank;
@@ -112,6 +120,13 @@ typedef struct {
     const int8_t *shg, *shu, *shd;
     const uint16_t *shg_s, *shu_s, *shd_s;
     wc_moe_ws ws;
+    /* The MoE half of a decoder layer (src/model.c:3927-3945): with norm_w
+     * set, the router normalises x (rmsnorm, eps) and every kernel of the
+     * layer works on that; with resid set, out = resid + the layer's output
+     * (the residual add). */
+    const float *norm_w;
+    float norm_eps;
+    const float *resid;
     /* L2 prefetching: the routed experts' down streams during gate/up, and
      * up to four caller ranges (16-byte aligned) during combine */
     int prefetch_down;
@@ -154,6 +169,10 @@ int    wc_matvec_launch(const wc_matvec_args *a, void *stream);
  * return is a cudaError_t). */
 #define WC_NOALLOC_PART_FLOATS ((size_t)8 << 20)
 int    wc_noalloc_part(float **ptr);
+/* The same lookup plus loading the kernels the allocation-free matvec
+ * launches, so a later call needs nothing brought onto the device. */
+int    wc_noalloc_setup(float **ptr);
+int    wc_binary_version(void);
 
 int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
                    int nv, int stages, void *stream);

@@ -79,3 +79,20 @@ def moe_layer_rep_dev(layer: int, T: int, d_x: int, d_out: int, d_idx: int = 0, 
     v = lambda p: C.c_void_p(int(p) or None)
     _check(load_library().waste_cuda_ep_moe_layer_rep_dev(layer, T, v(d_x), v(d_out),
                                                           v(d_idx), v(d_w), v(stream)))
+
+
+def moe_block_dev(layer: int, T: int, d_h: int, d_out: int, d_idx: int = 0, d_w: int = 0,
+                  stream: int = 0):
+    """This rank's T tokens through the expert-parallel MoE block:
+    h + moe_layer(rmsnorm(h))."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_ep_moe_block_dev(layer, T, v(d_h), v(d_out), v(d_idx),
+                                                      v(d_w), v(stream)))
+
+
+def moe_block_rep_dev(layer: int, T: int, d_h: int, d_out: int, d_idx: int = 0, d_w: int = 0,
+                      stream: int = 0):
+    """T tokens every rank holds through the expert-parallel MoE block."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_ep_moe_block_rep_dev(layer, T, v(d_h), v(d_out),
+                                                          v(d_idx), v(d_w), v(stream)))

@@ -162,6 +162,9 @@ class MoELayer:
     rec_bytes: int
     shared_inter: int
     sh: dict = field(default_factory=dict)   # gate/up/down (q, s)
+    act_situ: int = 0                # 1: K3's SiTU in place of SiLU(g)*u
+    situ_beta: float = 0.0
+    situ_lbeta: float = 0.0
 
     @property
     def books(self) -> np.ndarray:
@@ -288,13 +291,15 @@ def derive_layer(base: "MoELayer", layer: int, seed: int) -> "MoELayer":
         sh["down"] = q8g(rng, base.hidden, base.shared_inter, 2e-4, 5e-4)
     return MoELayer(layer, base.hidden, base.inter, base.n_experts, base.top_k, base.renorm,
                     base.routed_scale, base.stages, base.cb_base, base.books_raw, router,
-                    base.bias, b.reshape(-1), base.rec_bytes, base.shared_inter, sh)
+                    base.bias, b.reshape(-1), base.rec_bytes, base.shared_inter, sh,
+                    base.act_situ, base.situ_beta, base.situ_lbeta)
 
 
 def moe_layer(seed: int, hidden: int = 2304, inter: int = 1024, n_experts: int = 256,
               top_k: int = 8, shared_inter: int = 1024, layer: int = 1,
               routed_scale: float = 2.446, renorm: int = 1, stages: int = 3,
-              with_bias: bool = False, cb_base: int | None = None) -> MoELayer:
+              with_bias: bool = False, cb_base: int | None = None, act_situ: int = 0,
+              situ_beta: float = 4.0, situ_lbeta: float = 25.0) -> MoELayer:
     """Seeded layer at the Kimi-Linear-48B shape by default (hidden 2304,
     expert inter 1024, 256 experts, top-8, one shared expert, routed scale
     2.446 with renorm)."""
@@ -314,7 +319,17 @@ def moe_layer(seed: int, hidden: int = 2304, inter: int = 1024, n_experts: int =
         sh["up"] = q8g(rng, shared_inter, hidden, 2e-4, 5e-4)
         sh["down"] = q8g(rng, hidden, shared_inter, 2e-4, 5e-4)
     return MoELayer(layer, hidden, inter, n_experts, top_k, renorm, routed_scale, stages,
-                    cb_base, books_raw, router, bias, bk, rb, shared_inter, sh)
+                    cb_base, books_raw, router, bias, bk, rb, shared_inter, sh, act_situ,
+                    situ_beta if act_situ else 0.0, situ_lbeta if act_situ else 0.0)
+
+
+NORM_EPS = 1e-6      # rms_norm_eps of the synthetic decoder layers
+
+
+def norm_weight(seed: int, hidden: int) -> np.ndarray:
+    """A post-attention rmsnorm weight: N(1, 0.1^2) per channel, seeded."""
+    rng = np.random.default_rng(seed)
+    return (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
 
 
 def activations(seed: int, n: int, T: int = 1) -> np.ndarray:
