@@ -143,13 +143,23 @@ int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
                               const uint16_t *sh_up_s, const int8_t *sh_down,
                               const uint16_t *sh_down_s);
 
+/* The gated activation the device-routed paths of a layer use (the whole
+ * layer, the block, expert parallel, prefill_dev) for its routed and shared
+ * experts: act 0 = SiLU(g)*u (the default), act 1 = SiTU with situ_beta > 0
+ * and situ_linear_beta (<= 0: u unsquashed) — the model's act_situ,
+ * activation_situ_beta and activation_situ_linear_beta
+ * (src/model.c:987-990). The expert-loop slots take it per call instead. */
+int waste_cuda_moe_activation(int layer, int act, float situ_beta,
+                              float situ_linear_beta);
+
 /* ---- the expert loop (decode) ------------------------------------------
  * What moe_layer's serial loop computes (src/model.c:2873-2911) for one
  * token: gate/up tables built once from x, then per routed expert j in
- * router order gate, up, SiLU(g)*u, down, and ysum = sum_j w[j]*acc_j
- * accumulated in j order. idx/w/x/ysum are host pointers owned by the
- * caller (m->... in the engine). act 0 = SiLU; SiTU (K3) returns
- * WASTE_CUDA_E_ARG so the engine keeps its CPU loop. */
+ * router order gate, up, the gated activation, down, and ysum = sum_j
+ * w[j]*acc_j accumulated in j order. idx/w/x/ysum are host pointers owned
+ * by the caller (m->... in the engine). act 0 = SiLU(g)*u (src/model.c:501);
+ * act 1 = K3's SiTU, waste_situ_pair(g, u, situ_beta, situ_linear_beta)
+ * (src/model.c:505-509, the model's act_situ). */
 struct waste_moe_call {
     int layer, K;
     const int *idx;

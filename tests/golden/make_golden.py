@@ -123,8 +123,10 @@ def lut_matvec_fixtures(R):
         print("lut/matvec fixtures for", name)
 
 
-def moe_fixtures():
+def moe_fixtures(only=None):
     for name, (seed, kw, xseed, T) in MOE_CASES.items():
+        if only and name not in only:
+            continue
         L = synth.moe_layer(seed, **kw)
         x = synth.activations(xseed, L.hidden, T=max(T, 2))
         res = {"sha": layer_sha(L), "seed": seed, "xseed": xseed}
@@ -173,5 +175,7 @@ def main():
 if __name__ == "__main__":
     if sys.argv[1:] == ["norm"]:
         norm_fixture()
+    elif sys.argv[1:2] == ["moe"]:
+        moe_fixtures(sys.argv[2:])
     else:
         main()

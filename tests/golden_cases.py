@@ -12,6 +12,9 @@ MOE_CASES = {
     "moe_ragged": (11, dict(hidden=192, inter=96, n_experts=12, top_k=3, shared_inter=192,
                             with_bias=False, renorm=0, routed_scale=1.0), 13, 5),
     "moe_kimi": (1234, dict(), 4321, 0),
+    # K3's activation (SiTU, beta 4, linear beta 25) at a small shape
+    "moe_situ": (17, dict(hidden=256, inter=128, n_experts=16, top_k=4, shared_inter=128,
+                          with_bias=True, routed_scale=2.827, act_situ=1), 19, 16),
 }
 
 MATVEC_CASES = ("matvec_ragged", "matvec_square", "matvec_vq2r")

@@ -121,3 +121,27 @@ def test_rmsnorm_vs_reference_live():
     x = synth.activations(5, 4096)[0] * np.float32(0.01)
     w = synth.norm_weight(6, 4096)
     assert np.array_equal(bits(O.rmsnorm(x, w, 1e-5)), bits(O.ref_rmsnorm(x, w, 1e-5)))
+
+
+def test_situ_golden_is_situ():
+    """The SiTU fixture really took the SiTU path: the SiLU restatement of
+    the same layer disagrees with it, the SiTU restatement matches."""
+    import copy
+    L, x, g, _ = _layer("moe_situ")
+    assert L.act_situ == 1
+    L0 = copy.copy(L)
+    L0.act_situ = 0
+    o_silu, _, _ = O.moe_layer(L0, x[0], fma=0)
+    o_situ, _, _ = O.moe_layer(L, x[0], fma=0)
+    assert rel_l2(o_silu, g["out0_cpu"]) > 1e-3
+    assert np.array_equal(bits(o_situ), bits(g["out0_cpu"]))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built here")
+def test_situ_pair_vs_reference_live():
+    rng = np.random.default_rng(3)
+    g = (rng.standard_normal(2000) * 6).astype(np.float32)
+    u = (rng.standard_normal(2000) * 40).astype(np.float32)
+    for beta, lbeta in ((4.0, 25.0), (1.0, 0.0), (2.5, -1.0)):
+        assert np.array_equal(bits(O.situ_pair(g, u, beta, lbeta)),
+                              bits(O.ref_situ_pair(g, u, beta, lbeta)))

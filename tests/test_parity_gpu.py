@@ -139,7 +139,8 @@ def test_moe_experts_parity(cuda_lib, name):
     wb.vq_bank_free(L.layer)
     wb.load_layer(L, trunk=False)
     _, idx, w = O.moe_layer(L, x[0], fma=1)
-    y = wb.moe_experts(L.layer, idx, w, x[0], L.hidden, L.inter)
+    y = wb.moe_experts(L.layer, idx, w, x[0], L.hidden, L.inter, L.act_situ, L.situ_beta,
+                       L.situ_lbeta)
     yo = O.moe_experts(L, idx, w, x[0], fma=1)
     assert rel_l2(y, yo) < TOL
 
@@ -153,7 +154,8 @@ def test_moe_chunk_parity(cuda_lib, name):
     wb.vq_bank_free(L.layer)
     wb.load_layer(L, trunk=False)
     route, rw = g["route_avx512"], g["rw_avx512"]
-    y = wb.moe_chunk_experts(L.layer, route, rw, x[:T], L.hidden, L.inter)
+    y = wb.moe_chunk_experts(L.layer, route, rw, x[:T], L.hidden, L.inter, L.act_situ,
+                             L.situ_beta, L.situ_lbeta)
     L0 = copy.copy(L)
     L0.shared_inter = 0          # the routed part alone
     yo, r2, _ = O.moe_chunk(L0, x[:T], fma=1)
@@ -214,14 +216,17 @@ def test_sharded_bank(cuda_lib):
     wb.vq_bank_free(L.layer)
 
 
-def test_moe_layer_k3_shape(cuda_lib):
+@pytest.mark.parametrize("act", [0, 1])
+def test_moe_layer_k3_shape(cuda_lib, act):
     """K3-class widths (hidden 7168, expert inter 2048, shared inter 2048,
     top-16) through the whole device layer and the prefill slot: the route
     bit-exact, outputs within 2e-5 of the oracle. 64 experts keep the bank
-    near 1 GB; the 512-expert router is covered below."""
+    near 1 GB; the 512-expert router is covered below. act 1: K3's own
+    activation, SiTU (beta 4, linear beta 25), in the routed and shared
+    experts."""
     wb = cuda_lib
     L = synth.moe_layer(77, hidden=7168, inter=2048, n_experts=64, top_k=16,
-                        shared_inter=2048, layer=11, routed_scale=2.827)
+                        shared_inter=2048, layer=11, routed_scale=2.827, act_situ=act)
     x = synth.activations(78, L.hidden, T=3)
     wb.vq_bank_free(L.layer)
     wb.load_layer(L)
@@ -233,7 +238,8 @@ def test_moe_layer_k3_shape(cuda_lib):
     L0 = copy.copy(L)
     L0.shared_inter = 0
     yo, route, rws = O.moe_chunk(L0, x, fma=1)
-    y = wb.moe_chunk_experts(L.layer, route, rws, x, L.hidden, L.inter)
+    y = wb.moe_chunk_experts(L.layer, route, rws, x, L.hidden, L.inter, act, L.situ_beta,
+                             L.situ_lbeta)
     assert rel_l2(y, yo) < TOL
     # 17 tokens in one device call, the batched forms at this width: the
     # many-token router (x of four tokens per block at hidden 7168: groups

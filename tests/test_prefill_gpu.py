@@ -22,11 +22,14 @@ def _ascending(L, idx, w, x):
     return O.moe_experts(L, idx[o].astype(np.int32), w[o].astype(np.float32), x, fma=1)
 
 
-@pytest.mark.parametrize("T", [128, 40])
-def test_prefill_tc_kimi_shape_zipf(cuda_lib, T):
+@pytest.mark.parametrize("T,act", [(128, 0), (40, 0), (512, 0), (128, 1)])
+def test_prefill_tc_kimi_shape_zipf(cuda_lib, T, act):
+    """T = 512 is config 3's size; act 1 is K3's SiTU in the gate/up -> down
+    hand-off."""
     import torch
     wb = cuda_lib
-    L = synth.moe_layer(1234)                       # hidden 2304, inter 1024, 256 experts, top-8
+    # hidden 2304, inter 1024, 256 experts, top-8
+    L = synth.moe_layer(1234, act_situ=act)
     wb.vq_bank_free(L.layer)
     wb.load_layer(L, trunk=False)
     route = synth.zipf_routes(77 + T, T, L.n_experts, L.top_k).astype(np.int32)
@@ -49,7 +52,8 @@ def test_prefill_tc_kimi_shape_zipf(cuda_lib, T):
     assert worst < TOL, worst
     # the host slot (the tensor cores for a full chunk, lookups below two
     # tokens per expert) agrees within the same tolerance
-    y = wb.moe_chunk_experts(L.layer, route[:64], rw[:64], x[:64], L.hidden, L.inter)
+    y = wb.moe_chunk_experts(L.layer, route[:64], rw[:64], x[:64], L.hidden, L.inter, act,
+                             L.situ_beta, L.situ_lbeta)
     assert max(rel_l2(y[t], out[t]) for t in range(min(T, 64))) < TOL
     wb.vq_bank_free(L.layer)
 

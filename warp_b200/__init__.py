@@ -34,6 +34,7 @@ EXPORTS = (
     "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev", "waste_cuda_moe_prefill_dev",
     "waste_cuda_ep_moe_layer_rep_dev", "waste_cuda_moe_norm_load", "waste_cuda_moe_block",
     "waste_cuda_moe_block_dev", "waste_cuda_ep_moe_block_dev", "waste_cuda_ep_moe_block_rep_dev",
+    "waste_cuda_moe_activation",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -133,6 +134,7 @@ def load_library() -> C.CDLL:
         "waste_cuda_ep_moe_layer_rep_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_moe_prefill_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_moe_norm_load": (C.c_int, [C.c_int, C.c_int, P, C.c_float]),
+        "waste_cuda_moe_activation": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_float]),
         "waste_cuda_moe_block": (C.c_int, [C.c_int, P, P, P, P]),
         "waste_cuda_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
@@ -259,16 +261,20 @@ def moe_trunk_load(layer: int, n_experts: int, hidden: int, top_k: int, renorm: 
 
 
 def load_layer(L, trunk: bool = True):
-    """Codebooks, the whole bank and (optionally) the trunk of a synth.MoELayer."""
+    """Codebooks, the whole bank and (optionally) the trunk of a synth.MoELayer,
+    with its activation."""
     codebooks_load_f16(L.books_raw)
     vq_bank_load(L.layer, L.n_experts, L.rec_bytes, 0, L.n_experts, L.bank, L.inter,
                  L.hidden, L.stages)
     if trunk:
         moe_trunk_load(L.layer, L.n_experts, L.hidden, L.top_k, L.renorm, L.routed_scale,
                        L.router, L.bias, L.shared_inter, L.sh)
+    moe_activation(L.layer, int(getattr(L, "act_situ", 0)), float(getattr(L, "situ_beta", 0.0)),
+                   float(getattr(L, "situ_lbeta", 0.0)))
 
 
-def moe_experts(layer: int, idx, w, x, lat: int, inter: int) -> np.ndarray:
+def moe_experts(layer: int, idx, w, x, lat: int, inter: int, act: int = 0,
+                situ_beta: float = 0.0, situ_lbeta: float = 0.0) -> np.ndarray:
     """The expert loop for one token (waste_moe_call): ysum[lat]."""
     i = np.ascontiguousarray(idx, dtype=np.int32)
     ww = _f32(w)
@@ -276,12 +282,13 @@ def moe_experts(layer: int, idx, w, x, lat: int, inter: int) -> np.ndarray:
     y = np.empty(lat, dtype=np.float32)
     c = MoeCall(layer, i.size, i.ctypes.data_as(C.POINTER(C.c_int)),
                 ww.ctypes.data_as(C.POINTER(C.c_float)), xx.ctypes.data_as(C.POINTER(C.c_float)),
-                y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, 0, 0.0, 0.0)
+                y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, act, situ_beta, situ_lbeta)
     _check(load_library().waste_cuda_moe_experts(C.byref(c)))
     return y
 
 
-def moe_chunk_experts(layer: int, route, rw, x, lat: int, inter: int) -> np.ndarray:
+def moe_chunk_experts(layer: int, route, rw, x, lat: int, inter: int, act: int = 0,
+                      situ_beta: float = 0.0, situ_lbeta: float = 0.0) -> np.ndarray:
     """The prefill expert loop (waste_moe_chunk_call): ysum[nT][lat]."""
     r = np.ascontiguousarray(route, dtype=np.int32)
     ww = _f32(rw)
@@ -291,7 +298,8 @@ def moe_chunk_experts(layer: int, route, rw, x, lat: int, inter: int) -> np.ndar
     c = MoeChunkCall(layer, nT, K, r.ctypes.data_as(C.POINTER(C.c_int)),
                      ww.ctypes.data_as(C.POINTER(C.c_float)),
                      xx.ctypes.data_as(C.POINTER(C.c_float)),
-                     y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, 0, 0.0, 0.0)
+                     y.ctypes.data_as(C.POINTER(C.c_float)), lat, inter, act, situ_beta,
+                     situ_lbeta)
     _check(load_library().waste_cuda_moe_chunk_experts(C.byref(c)))
     return y
 
@@ -310,6 +318,12 @@ def moe_layer_dev(layer: int, d_x: int, d_out: int, d_idx: int, d_w: int, stream
     _check(load_library().waste_cuda_moe_layer_dev(layer, C.c_void_p(d_x), C.c_void_p(d_out),
                                                    C.c_void_p(d_idx), C.c_void_p(d_w),
                                                    C.c_void_p(stream or None)))
+
+
+def moe_activation(layer: int, act: int, situ_beta: float = 0.0, situ_lbeta: float = 0.0):
+    """The layer's gated activation on the device-routed paths (0 SiLU, 1 SiTU)."""
+    _check(load_library().waste_cuda_moe_activation(layer, act, C.c_float(situ_beta),
+                                                    C.c_float(situ_lbeta)))
 
 
 def moe_norm_load(layer: int, norm_w, eps: float):

@@ -210,17 +210,20 @@ __global__ void __launch_bounds__(256) pf_split_x(wc_pf_args a)
     if (threadIdx.x == 0) a.xinv[t] = 1.0f / s;
 }
 
-/* h = SiLU(g) * u (src/model.c:501, 2898) for one routed pair */
+/* h = SiLU(g) * u (src/model.c:501, 2898), or SiTU (:505, :3646-3648), for
+ * one routed pair */
 __global__ void __launch_bounds__(256) pf_split_h(wc_pf_args a)
 {
     __shared__ float red[8];
     const int i = blockIdx.x, n = a.bank.inter;
     const float *g = a.gu + (size_t)i * 2 * n, *u = g + n;
     float m = 0.0f;
-    for (int k = threadIdx.x; k < n; k += blockDim.x) m = fmaxf(m, fabsf(silu_ref(g[k]) * u[k]));
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        m = fmaxf(m, fabsf(act_pair(a.act, g[k], u[k], a.situ_beta, a.situ_lbeta)));
     const float s = pow2_scale(block_max(m, red));
     for (int k = threadIdx.x; k < n; k += blockDim.x)
-        split_f16((silu_ref(g[k]) * u[k]) * s, a.hh[(size_t)i * n + k], a.hl[(size_t)i * n + k]);
+        split_f16(act_pair(a.act, g[k], u[k], a.situ_beta, a.situ_lbeta) * s,
+                  a.hh[(size_t)i * n + k], a.hl[(size_t)i * n + k]);
     if (threadIdx.x == 0) a.hinv[i] = 1.0f / s;
 }
 

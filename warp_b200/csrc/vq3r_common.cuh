@@ -385,4 +385,18 @@ __device__ __forceinline__ float silu_ref(float v)
     return v / (1.0f + expf(-v));
 }
 
+/* src/model.c:505-509 waste_situ_pair, K3's SiTU: beta*tanh(g/beta)*sigmoid(g)
+ * times lbeta*tanh(u/lbeta) (u itself when lbeta <= 0). */
+__device__ __forceinline__ float situ_ref(float g, float u, float beta, float lbeta)
+{
+    const float a = beta * tanhf(g / beta) / (1.0f + expf(-g));
+    return a * (lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u);
+}
+
+/* The gated activation of a layer: SiLU(g)*u (act 0) or SiTU (act 1). */
+__device__ __forceinline__ float act_pair(int act, float g, float u, float beta, float lbeta)
+{
+    return act ? situ_ref(g, u, beta, lbeta) : silu_ref(g) * u;
+}
+
 } /* namespace wc */

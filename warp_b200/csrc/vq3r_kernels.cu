@@ -914,12 +914,14 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
 #pragma unroll
         for (int k = 0; k < kSiluU; k++) {
             const int i = threadIdx.x - 32 + k * nt;
-            if (i < a.si) a.ws.sh_h[(size_t)t * a.si + i] = silu_ref(g[k]) * u[k];
+            if (i < a.si)
+                a.ws.sh_h[(size_t)t * a.si + i] = act_pair(a.act, g[k], u[k], a.situ_beta,
+                                                           a.situ_lbeta);
         }
         for (int i = threadIdx.x - 32 + kSiluU * nt; i < a.si; i += nt)   /* si > 1792 */
             a.ws.sh_h[(size_t)t * a.si + i] =
-                silu_ref(__ldcg(a.ws.sh_g + (size_t)t * a.si + i)) *
-                __ldcg(a.ws.sh_u + (size_t)t * a.si + i);
+                act_pair(a.act, __ldcg(a.ws.sh_g + (size_t)t * a.si + i),
+                         __ldcg(a.ws.sh_u + (size_t)t * a.si + i), a.situ_beta, a.situ_lbeta);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1141,7 +1143,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     for (int k = ts0; k < ts1; k++) {
         const size_t tb = (size_t)(t0 + k) * a.si;
         for (int i = threadIdx.x; i < a.si; i += blockDim.x)
-            a.ws.sh_h[tb + i] = silu_ref(__ldcg(a.ws.sh_g + tb + i)) * __ldcg(a.ws.sh_u + tb + i);
+            a.ws.sh_h[tb + i] = act_pair(a.act, __ldcg(a.ws.sh_g + tb + i),
+                                         __ldcg(a.ws.sh_u + tb + i), a.situ_beta, a.situ_lbeta);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1549,7 +1552,7 @@ down_kernel(const __grid_constant__ wc_moe_args a, TileGeom gu, TileGeom g, int 
             sg += red2[(p * 2 + 0) * nin + i];
             su += red2[(p * 2 + 1) * nin + i];
         }
-        xs[i] = silu_ref(sg * sg_scale) * (su * su_scale);
+        xs[i] = act_pair(a.act, sg * sg_scale, su * su_scale, a.situ_beta, a.situ_lbeta);
     }
     __syncthreads();
     books.build(lut, xs, nvs);
@@ -1602,7 +1605,8 @@ __global__ void __launch_bounds__(256) act_kernel(const __grid_constant__ wc_moe
     const uint16_t *sc = reinterpret_cast<const uint16_t *>(expert_rec(bk, idx, a.K, t, j) +
                                                            bk.scale_off);
     const float gs = f16_keep(ld_pin_u16(sc + n)), us = f16_keep(ld_pin_u16(sc + inter + n));
-    a.ws.h[(size_t)pair * inter + n] = silu_ref(sg * gs) * (su * us);
+    a.ws.h[(size_t)pair * inter + n] = act_pair(a.act, sg * gs, su * us, a.situ_beta,
+                                                a.situ_lbeta);
 }
 
 /* ---- 4. combine --------------------------------------------------------------

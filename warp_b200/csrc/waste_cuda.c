@@ -65,6 +65,9 @@ typedef struct {
     /* the MoE block's rmsnorm (post_attention_layernorm) */
     float *d_norm;
     float norm_eps;
+    /* the gated activation of the device-routed paths: 0 SiLU, 1 SiTU */
+    int act;
+    float situ_beta, situ_lbeta;
     /* the host-buffer layer and block calls as one CUDA graph each (copies
      * in, kernels, copies out), rebuilt when anything they point at may
      * have moved */
@@ -765,6 +768,22 @@ out:
     return rc;
 }
 
+int waste_cuda_moe_activation(int layer, int act, float situ_beta, float situ_linear_beta)
+{
+    if (layer < 0 || layer >= WC_MAX_LAYERS || (act != 0 && act != 1) ||
+        (act == 1 && !(situ_beta > 0.0f)))
+        return fail(WASTE_CUDA_E_ARG, "moe_activation: layer %d, act %d (0 SiLU, 1 SiTU with "
+                    "beta > 0)", layer, act);
+    pthread_mutex_lock(&g_mu);
+    wc_layer *L = &S.layer[layer];
+    g_epoch++;
+    L->act = act;
+    L->situ_beta = act ? situ_beta : 0.0f;
+    L->situ_lbeta = act ? situ_linear_beta : 0.0f;
+    pthread_mutex_unlock(&g_mu);
+    return 0;
+}
+
 int waste_cuda_moe_norm_load(int layer, int hidden, const float *norm_w, float eps)
 {
     int rc = 0;
@@ -840,13 +859,14 @@ static void fill_args(wc_moe_args *a, const wc_layer *L, int T, int K, int E, in
 
 static int run_experts(int layer, int T, int K, const int *idx, const float *w,
                        const float *x, float *ysum, int lat, int inter, int act,
-                       int order_by_id)
+                       float situ_beta, float situ_lbeta, int order_by_id)
 {
     int rc = 0;
     wc_layer *L = NULL;
     if (T <= 0 || T > WC_CHUNK_MAX || K <= 0 || K > WC_MAX_TOPK || !idx || !w || !x || !ysum)
         return fail(WASTE_CUDA_E_ARG, "moe call: bad arguments");
-    if (act != 0) return fail(WASTE_CUDA_E_ARG, "SiTU is not implemented on the device");
+    if (act != 0 && act != 1)
+        return fail(WASTE_CUDA_E_ARG, "moe call: act %d (0 SiLU, 1 SiTU)", act);
     pthread_mutex_lock(&g_mu);
     if ((rc = layer_ready(layer, lat, inter, &L))) goto out;
     if ((rc = check_route(L, idx, T * K))) goto out;
@@ -864,6 +884,9 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
         /* a chunk with enough tokens per expert: dense tiles on the tensor cores */
         wc_pf_args pa;
         if ((rc = pf_args(L, T, K, &pa))) goto out;
+        pa.act = act;
+        pa.situ_beta = situ_beta;
+        pa.situ_lbeta = situ_lbeta;
         pa.route = S.d_idx;
         pa.rw = S.d_w;
         pa.x = S.d_x;
@@ -877,6 +900,9 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
         a.w = S.d_w;
         a.out = S.d_out;
         a.order_by_id = order_by_id;
+        a.act = act;
+        a.situ_beta = situ_beta;
+        a.situ_lbeta = situ_lbeta;
         a.prefetch_down = 1;
         if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
         CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
@@ -897,14 +923,14 @@ int waste_cuda_moe_experts(const waste_moe_call *c)
 {
     if (!c) return fail(WASTE_CUDA_E_ARG, "NULL call");
     return run_experts(c->layer, 1, c->K, c->idx, c->w, c->x, c->ysum, c->lat, c->inter,
-                       c->act, 0);
+                       c->act, c->situ_beta, c->situ_linear_beta, 0);
 }
 
 int waste_cuda_moe_chunk_experts(const waste_moe_chunk_call *c)
 {
     if (!c) return fail(WASTE_CUDA_E_ARG, "NULL call");
     return run_experts(c->layer, c->nT, c->K, c->route, c->rw, c->x, c->ysum, c->lat,
-                       c->inter, c->act, 1);
+                       c->inter, c->act, c->situ_beta, c->situ_linear_beta, 1);
 }
 
 /* ---- whole layer ----------------------------------------------------------- */
@@ -940,6 +966,9 @@ static int layer_args(int layer, int T, int part, wc_moe_args *a, wc_layer **Lp)
     a->routed_scale = L->routed_scale;
     a->shg = L->d_shg; a->shu = L->d_shu; a->shd = L->d_shd;
     a->shg_s = L->d_shg_s; a->shu_s = L->d_shu_s; a->shd_s = L->d_shd_s;
+    a->act = L->act;
+    a->situ_beta = L->situ_beta;
+    a->situ_lbeta = L->situ_lbeta;
     a->prefetch_down = 1;
     if (S.prefetch_next && layer + 1 < WC_MAX_LAYERS && S.layer[layer + 1].trunk) {
         /* the next layer's router and shared expert, fetched into L2 while
@@ -1129,6 +1158,9 @@ int waste_cuda_moe_prefill_dev(int layer, int T, int K, const int *d_route, cons
     }
     if ((rc = ensure_ws(1, K, 1, L->kb.lat, L->kb.inter, 0, L->kb.stages))) goto out;
     if ((rc = pf_args(L, T, K, &a))) goto out;
+    a.act = L->act;
+    a.situ_beta = L->situ_beta;
+    a.situ_lbeta = L->situ_lbeta;
     a.route = d_route;
     a.rw = d_rw;
     a.x = d_x;

@@ -127,6 +127,10 @@ typedef struct {
     const float *norm_w;
     float norm_eps;
     const float *resid;
+    /* the gated activation: 0 SiLU(g)*u, 1 SiTU with its two betas
+     * (src/model.c:505-509) */
+    int act;
+    float situ_beta, situ_lbeta;
     /* L2 prefetching: the routed experts' down streams during gate/up, and
      * up to four caller ranges (16-byte aligned) during combine */
     int prefetch_down;
@@ -202,6 +206,8 @@ typedef struct {
     float *hinv;              /* [pairs]                                         */
     float *y;                 /* [T*K][lat] per pair, unweighted                 */
     unsigned int *err;
+    int act;                  /* 0 SiLU(g)*u, 1 SiTU                             */
+    float situ_beta, situ_lbeta;
 } wc_pf_args;
 
 int    wc_pf_supported(const wc_bank *b, int T, int K);
