@@ -238,6 +238,54 @@ def cpu_baseline(budget_s=10.0):
                       f"Kimi-Linear shape, scaled to {MOE_LAYERS} layers per token"}
 
 
+def engine_slot_path(base, budget_s=3.0):
+    """The drop-in as an engine binds it: the reference engine patched with
+    this backend (integration/), its own moe_layer at the Kimi-Linear shape
+    through the oracle's harness. Per layer: the engine's CPU router, the
+    routed experts through the moe_experts slot (host buffers: x, route and
+    weights in, ysum out, one synchronisation), the shared expert on the
+    CPU. Returns tok/s for 26 such layers, the per-layer time, and the time
+    of the slot call alone (waste_cuda_moe_experts) on the same layer."""
+    import oracle as O
+    import warp_b200 as wb
+    from warp_b200 import synth
+    R = O.engine_cuda()
+    if R is None:
+        return {"unavailable": "integration/_build/libwaste_engine_cuda.so is not built"}
+    backend = R.refh_backend_auto().decode()
+    L = synth.derive_layer(base, 100, SEED + 300)
+    rm = O.RefMoe(L, max_tokens=1, lib=R)
+    try:
+        if not R.refh_moe_upload(rm.h):
+            return {"unavailable": "the CUDA backend declined the bank"}
+        xs = synth.activations(SEED + 301, HIDDEN, T=16)
+        for i in range(3):
+            rm.layer(xs[i])
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            rm.layer(xs[n % 16])
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        routes = [O.moe_layer(L, xs[i])[1:] for i in range(4)]
+        for i in range(4):
+            wb.moe_experts(100, routes[i][0], routes[i][1], xs[i], HIDDEN, INTER)
+        m, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s / 2:
+            i = m % 4
+            wb.moe_experts(100, routes[i][0], routes[i][1], xs[i], HIDDEN, INTER)
+            m += 1
+        slot = (time.perf_counter() - t0) / m
+    finally:
+        rm.close()
+    return {"value": 1.0 / (per * MOE_LAYERS), "unit": UNIT, "ms_per_layer": per * 1e3,
+            "slot_ms_per_layer": slot * 1e3, "layer_calls": n, "engine_backend": backend,
+            "cpu_threads": int(R.refh_pool_threads()),
+            "h2d_bytes_per_step": MOE_LAYERS * (HIDDEN + 2 * TOPK) * 4,
+            "d2h_bytes_per_step": MOE_LAYERS * (HIDDEN + 1) * 4,
+            "path": "the reference engine's moe_layer with integration/warp_cuda.patch: CPU "
+                    "router and shared expert, routed experts through the moe_experts slot"}
+
+
 # ---------------------------------------------------------------- this repo
 
 def run_warp(args):
@@ -451,53 +499,55 @@ def run_warp(args):
                    "share": v[0] / tot if tot else None} for k, v in ph.items() if v[1]}
 
     # ---- config 1: VQ3R matvec 4096 x 4096, 32 distinct matrices per launch
-    G, M, N = 32, 4096, 4096
-    rng = np.random.default_rng(SEED + 7)
-    raw = synth.codebooks(rng, 3)
-    wb.codebooks_load_f16(raw)
-    mats = [synth.random_matrix(rng, M, N) for _ in range(G)]
-    d_idx = torch.from_numpy(np.stack([m[0] for m in mats])).to(dev)
-    d_sc = torch.from_numpy(np.stack([m[1].view(np.int16) for m in mats])).to(dev)
-    d_x = torch.from_numpy(synth.activations(SEED + 8, N, T=G)).to(dev)
-    d_y = torch.empty((G, M), dtype=torch.float32, device=dev)
-    ptrs = ([d_idx[g].data_ptr() for g in range(G)], [d_sc[g].data_ptr() for g in range(G)],
-            [d_x[g].data_ptr() for g in range(G)], [d_y[g].data_ptr() for g in range(G)])
-    mv_iters = max(args.steps, 10)
-    for _ in range(3):
-        wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
-    torch.cuda.synchronize()
-    # The launches are queued behind a GPU-side sleep that outlasts the host's
-    # enqueue time (the Python wrapper builds its pointer tables per call), so
-    # the events bracket back-to-back device work only.
-    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):
-        torch.cuda._sleep(int(2e8))                  # ~0.1 s at 2 GHz
-        m0.record(s)
-        for _ in range(mv_iters):
+    matvec = None
+    if not args.decode_only:
+        G, M, N = 32, 4096, 4096
+        rng = np.random.default_rng(SEED + 7)
+        raw = synth.codebooks(rng, 3)
+        wb.codebooks_load_f16(raw)
+        mats = [synth.random_matrix(rng, M, N) for _ in range(G)]
+        d_idx = torch.from_numpy(np.stack([m[0] for m in mats])).to(dev)
+        d_sc = torch.from_numpy(np.stack([m[1].view(np.int16) for m in mats])).to(dev)
+        d_x = torch.from_numpy(synth.activations(SEED + 8, N, T=G)).to(dev)
+        d_y = torch.empty((G, M), dtype=torch.float32, device=dev)
+        ptrs = ([d_idx[g].data_ptr() for g in range(G)], [d_sc[g].data_ptr() for g in range(G)],
+                [d_x[g].data_ptr() for g in range(G)], [d_y[g].data_ptr() for g in range(G)])
+        mv_iters = max(args.steps, 10)
+        for _ in range(3):
             wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
-        m1.record(s)
-    torch.cuda.synchronize()
-    wb.profile(True)
-    with torch.cuda.stream(s):
-        torch.cuda._sleep(int(1e8))
-        for _ in range(10):
-            wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
-    torch.cuda.synchronize()
-    mph = wb.profile_read()
-    wb.profile(False)
-    mv_ms = m0.elapsed_time(m1) / mv_iters
-    mv_bytes = G * (synth.index_bytes(M, N, 3) + 2 * M + 4 * N + 4 * M) + 3 * 256 * 8 * 4
-    mv_tiles_avg = mph["matvec"][0] / max(mph["matvec"][1], 1)
-    matvec = {"workload": "vq3r_matvec_4096x4096_x32", "GBps": mv_bytes / (mv_ms / 1e3) / 1e9,
-              "frac": mv_bytes / (mv_ms / 1e3) / 1e9 / peak, "ms_per_launch": mv_ms,
-              "gather_kernel_GBps": G * synth.index_bytes(M, N, 3) / (mv_tiles_avg / 1e3) / 1e9,
-              "bytes_per_launch": mv_bytes}
+        torch.cuda.synchronize()
+        # The launches are queued behind a GPU-side sleep that outlasts the host's
+        # enqueue time (the Python wrapper builds its pointer tables per call), so
+        # the events bracket back-to-back device work only.
+        m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(2e8))                  # ~0.1 s at 2 GHz
+            m0.record(s)
+            for _ in range(mv_iters):
+                wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
+            m1.record(s)
+        torch.cuda.synchronize()
+        wb.profile(True)
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(1e8))
+            for _ in range(10):
+                wb.vq_matvec_dev(*ptrs, M, N, 0, 3, s.cuda_stream)
+        torch.cuda.synchronize()
+        mph = wb.profile_read()
+        wb.profile(False)
+        mv_ms = m0.elapsed_time(m1) / mv_iters
+        mv_bytes = G * (synth.index_bytes(M, N, 3) + 2 * M + 4 * N + 4 * M) + 3 * 256 * 8 * 4
+        mv_tiles_avg = mph["matvec"][0] / max(mph["matvec"][1], 1)
+        matvec = {"workload": "vq3r_matvec_4096x4096_x32", "GBps": mv_bytes / (mv_ms / 1e3) / 1e9,
+                  "frac": mv_bytes / (mv_ms / 1e3) / 1e9 / peak, "ms_per_launch": mv_ms,
+                  "gather_kernel_GBps": G * synth.index_bytes(M, N, 3) / (mv_tiles_avg / 1e3) / 1e9,
+                  "bytes_per_launch": mv_bytes}
 
     # ---- config 3: prefill, 512 tokens with Zipf(1.1) routes, one layer (layer
     # 1's bank), on the tensor cores; the lookup path (8 host-slot chunks of 64
     # tokens, copies included) timed beside it
     prefill = None
-    if not ep_mode:
+    if not ep_mode and not args.decode_only:
         PT = 512
         route = synth.zipf_routes(SEED + 9, PT, EXPERTS, TOPK).astype(np.int32)
         rw = np.random.default_rng(SEED + 10).uniform(0.05, 0.6, size=route.shape).astype(np.float32)
@@ -549,6 +599,7 @@ def run_warp(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_budget)
+    engine = engine_slot_path(base) if world == 1 and not args.decode_only else None
 
     if rank == 0:
         line = {
@@ -571,6 +622,7 @@ def run_warp(args):
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": ck,
             "e2e": e2e,
+            "e2e_engine_slot": engine,
             "roofline": {"bound": "hbm", "kernel": "gateup_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
@@ -897,6 +949,9 @@ def main():
     ap.add_argument("--impl", choices=("warp", "reference"), default="warp")
     ap.add_argument("--layers", type=int, default=MOE_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the decode chain (no matvec, prefill or engine-slot legs): "
+                         "for profiling runs")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--parallel", choices=("ep", "replicas"), default="ep",
                     help="with --gpus N > 1: expert parallel (default) or N replicas")

@@ -113,40 +113,67 @@ def ref() -> C.CDLL | None:
     if _ref is None:
         if not os.path.exists(REF_SO):
             return None
-        R = C.CDLL(REF_SO)
-        R.refh_set_backend.restype = C.c_char_p
-        R.refh_set_backend.argtypes = [C.c_int]
-        R.refh_best_backend.restype = C.c_int
-        R.refh_pool_init.argtypes = [C.c_int]
-        R.refh_pool_threads.restype = C.c_int
-        R.refh_version.restype = C.c_char_p
-        R.refh_lutb.argtypes = [P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int]
-        R.refh_vq_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int,
-                                     C.c_int, C.c_int, C.c_int]
-        R.refh_mv_open.restype = P
-        R.refh_mv_open.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
-        R.refh_mv_run.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int]
-        R.refh_mv_close.argtypes = [P]
-        R.refh_moe_open.restype = P
-        R.refh_moe_open.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
-                                    C.c_float, P, P, P, C.c_int, C.c_int, P, C.c_size_t,
-                                    C.c_int, P, P, P, P, P, P, C.c_int]
-        R.refh_moe_layer.restype = C.c_int
-        R.refh_moe_layer.argtypes = [P, P, P, P]
-        R.refh_moe_chunk.restype = C.c_int
-        R.refh_moe_chunk.argtypes = [P, P, C.c_int, P, P, P]
-        R.refh_moe_close.argtypes = [P]
-        R.refh_load.restype = P
-        R.refh_load.argtypes = [C.c_char_p]
-        R.refh_codebooks.restype = C.POINTER(C.c_float)
-        R.refh_codebooks.argtypes = [P, C.POINTER(C.c_int)]
-        R.refh_free.argtypes = [P]
-        R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
-        R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
-        R.waste_situ_pair.restype = C.c_float
-        R.waste_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
-        _ref = R
+        _ref = _bind_refh(C.CDLL(REF_SO))
     return _ref
+
+
+ENGINE_CUDA_SO = os.path.join(os.path.dirname(HERE), "integration", "_build",
+                              "libwaste_engine_cuda.so")
+_engine_cuda = None
+
+
+def engine_cuda() -> C.CDLL | None:
+    """The reference engine patched with the CUDA backend (integration/),
+    with the same harness entry points as ref() plus refh_backend_auto and
+    refh_moe_upload. Loads libwaste_cuda.so as its dependency (the same
+    instance warp_b200 binds)."""
+    global _engine_cuda
+    if _engine_cuda is None:
+        if not os.path.exists(ENGINE_CUDA_SO):
+            return None
+        R = _bind_refh(C.CDLL(ENGINE_CUDA_SO))
+        R.refh_backend_auto.restype = C.c_char_p
+        R.refh_moe_upload.restype = C.c_int
+        R.refh_moe_upload.argtypes = [P]
+        _engine_cuda = R
+    return _engine_cuda
+
+
+def _bind_refh(R: C.CDLL) -> C.CDLL:
+    """ctypes signatures of the harness (ref_harness.c) and of the engine
+    functions the checker calls."""
+    R.refh_set_backend.restype = C.c_char_p
+    R.refh_set_backend.argtypes = [C.c_int]
+    R.refh_best_backend.restype = C.c_int
+    R.refh_pool_init.argtypes = [C.c_int]
+    R.refh_pool_threads.restype = C.c_int
+    R.refh_version.restype = C.c_char_p
+    R.refh_lutb.argtypes = [P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int]
+    R.refh_vq_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int,
+                                 C.c_int, C.c_int, C.c_int]
+    R.refh_mv_open.restype = P
+    R.refh_mv_open.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+    R.refh_mv_run.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int]
+    R.refh_mv_close.argtypes = [P]
+    R.refh_moe_open.restype = P
+    R.refh_moe_open.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                C.c_float, P, P, P, C.c_int, C.c_int, P, C.c_size_t,
+                                C.c_int, P, P, P, P, P, P, C.c_int]
+    R.refh_moe_layer.restype = C.c_int
+    R.refh_moe_layer.argtypes = [P, P, P, P]
+    R.refh_moe_chunk.restype = C.c_int
+    R.refh_moe_chunk.argtypes = [P, P, C.c_int, P, P, P]
+    R.refh_moe_close.argtypes = [P]
+    R.refh_load.restype = P
+    R.refh_load.argtypes = [C.c_char_p]
+    R.refh_codebooks.restype = C.POINTER(C.c_float)
+    R.refh_codebooks.argtypes = [P, C.POINTER(C.c_int)]
+    R.refh_free.argtypes = [P]
+    R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
+    R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
+    R.waste_situ_pair.restype = C.c_float
+    R.waste_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
+    return R
 
 
 # ---- restatement ----------------------------------------------------------
@@ -325,8 +352,8 @@ def ref_situ_pair(g, u, beta, lbeta):
 class RefMoe:
     """One MoE layer inside the reference engine (ref_harness.c)."""
 
-    def __init__(self, L, max_tokens=64, backend=None, threads=0):
-        R = ref()
+    def __init__(self, L, max_tokens=64, backend=None, threads=0, lib=None):
+        R = lib if lib is not None else ref()
         if R is None:
             raise RuntimeError("oracle/_ref/libwaste_ref.so is not built")
         self.R = R

@@ -321,10 +321,36 @@ int refh_moe_chunk(void *p, const float *x, int nT, float *out, int *route,
     return h->m->read_error;
 }
 
+#if defined(WASTE_ENABLE_CUDA)
+/* Built against the engine patched with this repository's CUDA backend
+ * (integration/): the engine's own backend choice (src/backend.c:168-212)
+ * with the CUDA backend compiled in, which registers it when an sm_100
+ * device is present and fills the expert-path slots. */
+const char *refh_backend_auto(void)
+{
+    waste_backend_init(WASTE_BE_AUTO);
+    return waste_backend_name();
+}
+
+/* The patched loader's upload (wcu_upload) for a layer built here: the
+ * codebooks and the bank go to HBM. Returns 1 when the expert-path slots
+ * are live afterwards (moe_layer / moe_chunk run their experts on the
+ * device), 0 when the backend declined. */
+int refh_moe_upload(void *p)
+{
+    refh_moe *h = (refh_moe *)p;
+    wcu_upload(h->m);
+    return waste_vq.moe_experts != NULL;
+}
+#endif
+
 void refh_moe_close(void *p)
 {
     refh_moe *h = (refh_moe *)p;
     waste_model *m = h->m;
+#if defined(WASTE_ENABLE_CUDA)
+    wcu_release(m);
+#endif
     close(m->bank[h->layer].fd);
     free(m->t); free(m->miss_buf); free(m->att); free(m->ff); free(m->e_gate);
     free(m->h); free(m->ares); free(m->lut); free(m->croute); free(m->crw);

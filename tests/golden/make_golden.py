@@ -28,6 +28,7 @@ from __future__ import annotations
 import hashlib
 import os
 import shutil
+import subprocess
 import struct
 import sys
 import tempfile
@@ -145,6 +146,18 @@ def moe_fixtures(only=None):
         print(name, "written")
 
 
+def tiny_container():
+    """tests/golden/tiny_container/: the reference's own test container
+    (tools/make_test_container.py, seed 0: a Kimi-Linear at 1/18 scale, 4
+    layers, 8 VQ3R experts top-2, 0.8 MB), for driving the engine through
+    its public API with and without the CUDA backend."""
+    out = os.path.join(OUT, "tiny_container")
+    shutil.rmtree(out, ignore_errors=True)
+    subprocess.run([sys.executable, os.path.join(REF_TREE, "tools", "make_test_container.py"),
+                    out, "--seed", "0"], check=True)
+    print("tiny_container written")
+
+
 NORM_SIZES = (2304, 1024, 7168, 100)
 
 
@@ -170,6 +183,7 @@ def main():
     lut_matvec_fixtures(R)
     moe_fixtures()
     norm_fixture()
+    tiny_container()
 
 
 if __name__ == "__main__":
@@ -177,5 +191,7 @@ if __name__ == "__main__":
         norm_fixture()
     elif sys.argv[1:2] == ["moe"]:
         moe_fixtures(sys.argv[2:])
+    elif sys.argv[1:] == ["container"]:
+        tiny_container()
     else:
         main()

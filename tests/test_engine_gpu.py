@@ -1,0 +1,73 @@
+"""The reference engine with the CUDA backend wired in (integration/), on a
+B200, against the unmodified reference engine (oracle/_ref).
+
+Two levels:
+  * the public API (waste_open / waste_eval) on the reference's own test
+    container: the patched engine registers the CUDA backend, its expert
+    loops run on the device (the backend's launch count grows), and the
+    greedy tokens match the reference's while the logits stay within 1e-4
+    relative L2 (four decoder layers of fp32 arithmetic in between, so this
+    is looser than the per-layer bound);
+  * the engine's own moe_layer and moe_chunk at the Kimi-Linear-48B shape,
+    reached through the oracle's harness compiled against the patched
+    model.c: the route comes from the engine's CPU router in both engines
+    (identical bits), and the layer outputs — routed experts through the
+    moe_experts / moe_chunk_experts slots, the shared expert on the CPU —
+    are within 2e-5 relative L2 of the reference's. 64-token chunks take
+    the tensor-core path, 5-token chunks the lookup path; SiTU too.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from golden_cases import rel_l2
+from test_engine import CUDA_ENGINE, REF_ENGINE, needs_engines, run_engine
+from warp_b200 import synth
+
+pytestmark = [pytest.mark.gpu, needs_engines]
+TOL = 2e-5
+
+
+def test_engine_public_api_on_device(tmp_path):
+    b_ref, _, tok_ref, lg_ref = run_engine(REF_ENGINE, tmp_path, "ref")
+    b_cu, launches, tok_cu, lg_cu = run_engine(CUDA_ENGINE, tmp_path, "cuda")
+    assert "CUDA sm_100a" in b_cu, b_cu
+    assert launches and launches > 0
+    assert np.array_equal(tok_ref, tok_cu)
+    worst = max(rel_l2(lg_cu[e], lg_ref[e]) for e in range(len(tok_ref)))
+    assert worst < 1e-4, worst
+
+
+def _pair(L, R):
+    ref = O.RefMoe(L, max_tokens=64)
+    cu = O.RefMoe(L, max_tokens=64, lib=R)
+    assert R.refh_moe_upload(cu.h) == 1, "the backend declined the bank"
+    return ref, cu
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_engine_moe_layer_and_chunk_through_slots(cuda_lib, act):
+    wb = cuda_lib
+    R = O.engine_cuda()
+    assert b"CUDA" in R.refh_backend_auto()
+    L = synth.moe_layer(1234, layer=90, cb_base=0, act_situ=act)
+    x = synth.activations(90 + act, L.hidden, T=64)
+    ref, cu = _pair(L, R)
+    try:
+        n0 = wb.launch_count()
+        for t in range(3):                       # decode: moe_layer
+            o_r, i_r = ref.layer(x[t])
+            o_c, i_c = cu.layer(x[t])
+            assert np.array_equal(i_r, i_c)
+            assert rel_l2(o_c, o_r) < TOL, t
+        assert wb.launch_count() > n0
+        for T in (64, 5):                        # prefill: moe_chunk
+            c_r, r_r, w_r = ref.chunk(x[:T])
+            c_c, r_c, w_c = cu.chunk(x[:T])
+            assert np.array_equal(r_r, r_c)
+            worst = max(rel_l2(c_c[t], c_r[t]) for t in range(T))
+            assert worst < TOL, (T, worst)
+        assert wb.device_errors() == 0
+    finally:
+        cu.close()
+        ref.close()
