@@ -478,6 +478,40 @@ def run_warp(args):
            "d2h_bytes_per_step": nL * ((HIDDEN + 2 * 64 + 4) * 4 if not ep_mode
                                        else HIDDEN * 4)}
 
+    # ---- parity, outside the timed region: this rank's own token through
+    # layer 1's MoE block against the oracle (routes bit-exact, the MoE part
+    # within 2e-5 relative L2), so a multi-GPU run carries its own evidence
+    parity = None
+    if not args.no_parity:
+        import oracle as O
+        nw1 = synth.norm_weight(SEED + 201, HIDDEN)
+        hout = torch.empty((1, HIDDEN), dtype=torch.float32, device=dev)
+        pi = torch.empty((1, TOPK), dtype=torch.int32, device=dev)
+        pw = torch.empty((1, TOPK), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        if ep_mode:
+            ep.moe_block_dev(1, 1, xs[0].data_ptr(), hout.data_ptr(), pi.data_ptr(),
+                             pw.data_ptr(), s.cuda_stream)
+        else:
+            wb.moe_block_dev(1, 1, xs[0].data_ptr(), hout.data_ptr(), pi.data_ptr(),
+                             pw.data_ptr(), s.cuda_stream)
+        torch.cuda.synchronize()
+        derr = wb.device_errors()
+        h0 = xs_h[0]
+        ro, ri, _ = O.moe_block(base, h0, nw1, synth.NORM_EPS)
+        got = hout.cpu().numpy()[0]
+        d, r = (got - h0).astype(np.float64), (ro - h0).astype(np.float64)
+        rel = float(np.linalg.norm(d - r) / max(np.linalg.norm(r), 1e-30))
+        same = bool(np.array_equal(pi.cpu().numpy()[0], ri)) and derr == 0
+        if dist:
+            t = torch.tensor([rel, 0.0 if same else 1.0], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rel, same = float(t[0].item()), t[1].item() == 0.0
+        parity = {"ok": bool(same and rel < 2e-5), "worst_rel_l2": rel, "tolerance": 2e-5,
+                  "routes_bit_exact": same,
+                  "checked": f"layer 1 MoE block (rmsnorm, layer, residual) of one token per "
+                             f"rank on {world} rank(s), against the oracle (max over ranks)"}
+
     # ---- per-kernel times (phase timers): a GPU-side sleep holds the stream
     # while the host queues the launches, so each event pair brackets kernel
     # time rather than host launch gaps. Kept under the launch-queue depth.
@@ -596,6 +630,54 @@ def run_warp(args):
                    "lookup_path_ms_per_layer": lookup_ms,
                    "speedup_vs_lookup": lookup_ms / p_ms}
 
+    # ---- the trunk matvec (the mvq_rows_f32 slot) at the Kimi-Linear
+    # lm_head shape: 163840 x 2304 Q8G, 383 MB read once per token
+    trunk = None
+    if not args.decode_only:
+        VOCAB = 163840
+        rng = np.random.default_rng(SEED + 12)
+        raw, sc, rb = synth.trunk_tensor(rng, VOCAB, HIDDEN, 8)
+        dW = torch.from_numpy(raw).to(dev)
+        ds = torch.from_numpy(sc.view(np.int16)).to(dev)
+        del raw, sc
+        dx = torch.from_numpy(synth.activations(SEED + 13, HIDDEN)[0]).to(dev)
+        dy = torch.empty((VOCAB,), dtype=torch.float32, device=dev)
+        call = lambda: wb.mvq_rows_dev(dy.data_ptr(), dW.data_ptr(), ds.data_ptr(), dx.data_ptr(),
+                                       0, VOCAB, HIDDEN, 128, 8, rb, s.cuda_stream)
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        t_iters = 20
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(2e7))
+            q0.record(s)
+            for _ in range(t_iters):
+                call()
+            q1.record(s)
+        torch.cuda.synchronize()
+        t_ms = q0.elapsed_time(q1) / t_iters
+        ng = (HIDDEN + 127) // 128
+        tb = VOCAB * rb + VOCAB * ng * 2 + HIDDEN * 4 + VOCAB * 4
+        trunk = {"workload": "kimi_linear_lm_head_q8g_163840x2304", "ms_per_call": t_ms,
+                 "bytes_per_call": tb, "GBps": tb / (t_ms / 1e3) / 1e9,
+                 "frac": tb / (t_ms / 1e3) / 1e9 / peaks()[0],
+                 "l2": "383 MB per call, larger than L2"}
+        del dW, ds
+
+    # ---- config 4 (the K3-class layer, batches 1/16/64) at this N: layers
+    # 101.., codebooks appended to layer 1's
+    k3 = None
+    if (world == 1 or ep_mode) and not args.decode_only and not args.no_k3:
+        k3_res, k3_facts = k3_workload(args, rank, world, dev, dist, cb_books=base.books_raw,
+                                       layer0=100)
+        peak_k3 = peaks()[0]
+        k3 = {"metric": K3_METRIC, "unit": UNIT, "batches": k3_res,
+              "tok_per_s": {b: r["tok_per_s"] for b, r in k3_res.items()},
+              "rank0_frac_of_hbm": {b: (r["rank0_GBps"] or 0) / peak_k3 for b, r in k3_res.items()},
+              "config": dict(k3_facts, hidden=K3_HIDDEN, moe_inter=K3_INTER, top_k=K3_TOPK,
+                             parallelism=f"ep{world}" if world > 1 else "single")}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_budget)
@@ -633,6 +715,9 @@ def run_warp(args):
             "kernels": kernels,
             "matvec": matvec,
             "prefill": prefill,
+            "trunk_mvq": trunk,
+            "parity": parity,
+            "k3": k3,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -725,56 +810,52 @@ def run_k3_reference(args):
     return 0
 
 
-def run_k3(args):
-    """Config 4: one K3-class MoE layer per step, batches 1/16/64 tokens.
-    N = 1: the whole layer on one GPU (the batched layer call). N > 1:
-    expert parallel, 512/N experts per rank; batch 1 is held by every rank
-    (replicated trunk: routes agree, partial sums all-reduced through peer
-    memory), larger batches are split B/N tokens per rank (tokens out to
-    every rank, partial sums back to the tokens' ranks)."""
+def k3_workload(args, rank, world, dev, dist, cb_books=None, layer0=0):
+    """Config 4: one K3-class MoE layer per step, batches 1/16/64 tokens, on
+    a device (and, with world > 1, an expert-parallel exchange) that is
+    already set up. N = 1: the whole layer on one GPU (the batched layer
+    call). N > 1: expert parallel, 512/N experts per rank; batch 1 is held
+    by every rank (replicated trunk: routes agree, partial sums all-reduced
+    through peer memory), larger batches are split B/N tokens per rank
+    (tokens out to every rank, partial sums back to the tokens' ranks).
+    Layers are numbered from layer0 + 1; cb_books, when given, are codebooks
+    already loaded that the K3 books are appended to (the K3 records then
+    name their own books after them). Returns the results and setup facts."""
     import torch
     import warp_b200 as wb
     from warp_b200 import synth
-
-    rank, world, local = dist_setup(args.gpus)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
+    ep = None
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
-    wb.init(local)
+        from warp_b200 import ep
     E = args.k3_experts
     first, count = 0, E
     if world > 1:
-        from warp_b200 import ep
-        ep.setup(rank, world)
         first, count = ep.ep_range(E, rank, world)
     nL = args.k3_layers
     books = synth.codebooks(np.random.default_rng(SEED + 20), 9)
+    cb0 = 0
+    if cb_books is not None:
+        cb0 = cb_books.shape[0]
+        books = np.concatenate([cb_books, books])
     wb.codebooks_load_f16(books)
     rb = synth.record_bytes(K3_INTER, K3_HIDDEN, 3)
     t_gen = time.perf_counter()
     chunk = 16
     for c0 in range(first, first + count, chunk):
         n = min(chunk, first + count - c0)
-        recs = synth.bank_range(SEED + 30, 1, c0, n, 0, K3_INTER, K3_HIDDEN)
+        recs = synth.bank_range(SEED + 30, 1, c0, n, cb0, K3_INTER, K3_HIDDEN)
         for L in range(1, nL + 1):
-            synth.set_layer(recs, L)
-            wb.vq_bank_load(L, E, rb, c0, n, recs.reshape(-1), K3_INTER, K3_HIDDEN, 3)
+            synth.set_layer(recs, layer0 + L)
+            wb.vq_bank_load(layer0 + L, E, rb, c0, n, recs.reshape(-1), K3_INTER, K3_HIDDEN, 3)
         del recs
     for L in range(1, nL + 1):
         router, sh = synth.trunk(SEED + 40 + L, K3_HIDDEN, E, K3_SHARED)
-        wb.moe_trunk_load(L, E, K3_HIDDEN, K3_TOPK, 1, K3_SCALE, router, None,
+        wb.moe_trunk_load(layer0 + L, E, K3_HIDDEN, K3_TOPK, 1, K3_SCALE, router, None,
                           K3_SHARED, sh)
     t_gen = time.perf_counter() - t_gen
     s = torch.cuda.Stream(device=dev)
     ntok = 4
     results, graphs = {}, []
-    clocks = Clocks(local)
-    clocks.start()
     expert_b = k3_expert_bytes()
     router_b, shared_b = k3_trunk_bytes()
     router_b = router_b * E // K3_EXPERTS
@@ -796,13 +877,13 @@ def run_k3(args):
             ip, wp = idx[t, L].data_ptr(), w[t, L].data_ptr()
             if mode == "single":
                 if T == 1:
-                    wb.moe_layer_dev(L + 1, xp, op, ip, wp, s.cuda_stream)
+                    wb.moe_layer_dev(layer0 + L + 1, xp, op, ip, wp, s.cuda_stream)
                 else:
-                    wb.moe_layer_part_dev(L + 1, T, xp, op, 0, T, ip, wp, s.cuda_stream)
+                    wb.moe_layer_part_dev(layer0 + L + 1, T, xp, op, 0, T, ip, wp, s.cuda_stream)
             elif mode == "rep":
-                ep.moe_layer_rep_dev(L + 1, T, xp, op, ip, wp, s.cuda_stream)
+                ep.moe_layer_rep_dev(layer0 + L + 1, T, xp, op, ip, wp, s.cuda_stream)
             else:
-                ep.moe_layer_dev(L + 1, T, xp, op, ip, wp, s.cuda_stream)
+                ep.moe_layer_dev(layer0 + L + 1, T, xp, op, ip, wp, s.cuda_stream)
 
         def step_direct(t):
             for L in range(nL):
@@ -896,6 +977,37 @@ def run_k3(args):
             results[B]["rank0_bytes_per_call"] = call_bytes
             results[B]["rank0_GBps"] = per_rank_GBps
         assert wb.device_errors() == 0
+    torch.cuda.synchronize()
+    graphs.clear()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    return results, {"experts": E, "experts_per_gpu": count, "resident_layers": nL,
+                     "setup_s": t_gen}
+
+
+def run_k3(args):
+    """Config 4 on its own (--workload k3): the K3-class layer at batches
+    1/16/64 over N GPUs (k3_workload)."""
+    import torch
+    import warp_b200 as wb
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    wb.init(local)
+    if world > 1:
+        from warp_b200 import ep
+        ep.setup(rank, world)
+    clocks = Clocks(local)
+    clocks.start()
+    results, facts = k3_workload(args, rank, world, dev, dist)
     ck = clocks.stop()
     peak, peak_src = peaks()
     cpu = None
@@ -912,14 +1024,14 @@ def run_k3(args):
             "data": "synthetic (seeded per expert; uniform indices, N(0,0.02^2) codebooks, "
                     "router rows N(0,1/hidden), bf16-valued N(0,1) tokens)",
             "config": {"workload": "k3_class_moe_layer_decode", "hidden": K3_HIDDEN,
-                       "moe_inter": K3_INTER, "experts": E, "top_k": K3_TOPK,
-                       "shared_experts": 1, "resident_layers": nL,
-                       "global_batch": max(results), "experts_per_gpu": count,
+                       "moe_inter": K3_INTER, "experts": facts["experts"], "top_k": K3_TOPK,
+                       "shared_experts": 1, "resident_layers": facts["resident_layers"],
+                       "global_batch": max(results), "experts_per_gpu": facts["experts_per_gpu"],
                        "parallelism": f"ep{world}" if world > 1 else "single",
-                       "l2": f"steps cycle over {nL} resident layers and 4 token slots "
-                             "(> 126 MB of distinct weights between repeats at the "
+                       "l2": f"steps cycle over {facts['resident_layers']} resident layers and 4 "
+                             "token slots (> 126 MB of distinct weights between repeats at the "
                              "default 4 layers x 512 experts)",
-                       "cuda_graphs": bool(graphs), "setup_s": t_gen},
+                       "cuda_graphs": True, "setup_s": facts["setup_s"]},
             "batches": results,
             "roofline": {"bound": "hbm", "peak": peak, "peak_source": peak_src,
                          "unit": "GB/s",
@@ -929,11 +1041,6 @@ def run_k3(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    torch.cuda.synchronize()
-    graphs.clear()
-    import gc
-    gc.collect()
-    torch.cuda.synchronize()
     if dist:
         dist.barrier()
         ep.shutdown()
@@ -949,6 +1056,9 @@ def main():
     ap.add_argument("--impl", choices=("warp", "reference"), default="warp")
     ap.add_argument("--layers", type=int, default=MOE_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check")
+    ap.add_argument("--no-k3", action="store_true",
+                    help="skip the config-4 (K3-class) leg of the default workload")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the decode chain (no matvec, prefill or engine-slot legs): "
                          "for profiling runs")

@@ -57,8 +57,10 @@ extern "C" {
  * (src/waste_backend.h:116-120). A translation unit that includes the
  * engine's waste_backend.h first sees the engine's own prototype (a pointer
  * to its waste_kernels table); anywhere else the table is an opaque
- * pointer. It writes no slot of that table: the expert path's slots are
- * waste_vq_slots below. */
+ * pointer. Of that table it fills mvq_rows_f32 (the trunk matvec, see
+ * waste_cuda_mvq_rows_dev; WASTE_CUDA_TRUNK=0 leaves it alone) and sets
+ * on_device, so the engine hands it whole row ranges on the calling
+ * thread. The expert path's slots are waste_vq_slots below. */
 #ifdef WASTE_BACKEND_H
 const char *waste_register_cuda(waste_kernels *t);
 #else
@@ -381,6 +383,26 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
                                      const float *const *x, float *const *y,
                                      int M, int N, int cb_base, int stages,
                                      void *stream);
+
+/* ---- the trunk matvec (the mvq_rows_f32 slot) ---------------------------
+ * src/model.c:265-320 waste_mvq_rows_f32 on the device: y[r] for r in
+ * [r0, r1) = sum over groups k of f16(ws[r][k]) * (sum over the group's
+ * weights w*x), for Q8G (bits 8), Q4G (bits 4: two signed nibbles per byte,
+ * low first, minus 8) and Q3G (bits 3: a 3-bit bitstream, minus 4) rows of
+ * `rowbytes` bytes with `group` weights per f16 scale. Device pointers,
+ * ordered on `stream`; within 2e-5 of the CPU kernel (sum order).
+ * The slot waste_register_cuda installs does the same from the engine's
+ * host tensors: it keeps an HBM copy of each tensor it sees (keyed by the
+ * host address of its weights, made at first use), copies x in and y out,
+ * and runs tensors below WASTE_CUDA_TRUNK_MIN bytes (default 1 MiB) — and
+ * anything the device path cannot take — on the CPU kernel the slot held
+ * before. waste_cuda_release_host_buffers drops those copies (the engine
+ * calls it before freeing a model: src/backend.c:223-229,
+ * waste_backend_release_host_buffers). */
+int  waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws,
+                             const float *d_x, int r0, int r1, int in, int group,
+                             int bits, size_t rowbytes, void *stream);
+void waste_cuda_release_host_buffers(void);
 
 /* Kernels this library launched since load (a running count, for
  * benchmarks that report how many of their launches were this library's). */

@@ -170,6 +170,7 @@ def _bind_refh(R: C.CDLL) -> C.CDLL:
     R.refh_codebooks.argtypes = [P, C.POINTER(C.c_int)]
     R.refh_free.argtypes = [P]
     R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
+    R.waste_mvq_rows_f32.argtypes = [C.c_int, C.c_int, P]
     R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
     R.waste_situ_pair.restype = C.c_float
     R.waste_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
@@ -271,6 +272,37 @@ def situ_pair(g, u, beta, lbeta):
     f = lib().orc_situ_pair
     return np.array([f(C.c_float(a), C.c_float(b), C.c_float(beta), C.c_float(lbeta))
                      for a, b in zip(gg, uu)], dtype=np.float32).reshape(np.shape(g))
+
+
+def mvq_rows(raw, scales, x, inp, group, bits, rowbytes):
+    """src/model.c:265-320 waste_mvq_rows_f32 (restatement): y[rows]."""
+    r = np.ascontiguousarray(raw, dtype=np.uint8)
+    s = np.ascontiguousarray(scales, dtype=np.uint16)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(r.shape[0], dtype=np.float32)
+    lib().orc_mvq_rows(_p(y), _p(r), _p(s), _p(xx), r.shape[0], inp, group, bits, rowbytes)
+    return y
+
+
+class MvqArg(C.Structure):
+    """mvq_arg (src/simd.h:35-39): the engine's argument of mvq_rows_f32."""
+    _fields_ = [("y", P), ("W", P), ("ws", P), ("xq", P), ("xs", P), ("in_", C.c_int),
+                ("ng", C.c_int), ("group", C.c_int), ("bits", C.c_int), ("rowbytes", C.c_size_t)]
+
+
+def ref_mvq_rows(raw, scales, x, inp, group, bits, rowbytes):
+    """The reference's own portable waste_mvq_rows_f32, compiled."""
+    R = ref()
+    if R is None:
+        raise RuntimeError("oracle/_ref/libwaste_ref.so is not built")
+    r = np.ascontiguousarray(raw, dtype=np.uint8)
+    s = np.ascontiguousarray(scales, dtype=np.uint16)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(r.shape[0], dtype=np.float32)
+    a = MvqArg(_p(y), _p(r), _p(s), None, _p(xx), inp, (inp + group - 1) // group, group, bits,
+               rowbytes)
+    R.waste_mvq_rows_f32(0, r.shape[0], C.byref(a))
+    return y
 
 
 def rmsnorm(x, w, eps):

@@ -210,7 +210,16 @@ void orc_mvq_rows(float *y, const int8_t *W, const uint16_t *ws, const float *x,
         float acc = 0;
         for (int k = 0; k < ng; k++) {
             const int8_t *w;
-            if (bits == 4) {
+            if (bits == 3) {
+                /* src/simd.h:69-74 waste_q3_at over the row's bitstream */
+                const uint8_t *p3 = (const uint8_t *)row;
+                for (int i = 0; i < g; i++) {
+                    const long off = ((long)k * g + i) * 3;
+                    const int v = (p3[off >> 3] >> (off & 7)) | (p3[(off >> 3) + 1] << (8 - (off & 7)));
+                    unp[i] = (int8_t)((v & 7) - 4);
+                }
+                w = unp;
+            } else if (bits == 4) {
                 const uint8_t *p4 = (const uint8_t *)row + (size_t)k * g / 2;
                 for (int i = 0; i < g / 2; i++) {
                     unp[2 * i] = (int8_t)((p4[i] & 0x0F) - 8);

@@ -22,7 +22,7 @@
  *   orc_dotf           src/model.c:155-160     x86 dot product (serial)
  *   orc_route          src/model.c:2720-2747   sigmoid + bias, iterative argmax,
  *                                              renorm (+1e-20), routed scale
- *   orc_mvq_rows       src/model.c:265-320     Q8G/Q4G matvec, portable order
+ *   orc_mvq_rows       src/model.c:265-320     Q8G/Q4G/Q3G matvec, portable order
  *   orc_moe_layer      src/model.c:2713-2939   one token through router, K experts
  *                                              (router-order reduce) and shared FFN
  *   orc_moe_chunk      src/model.c:3512-3693   prefill chunk: ascending expert-id
@@ -70,7 +70,8 @@ float orc_dotf(const float *a, const float *b, int n);
 void orc_route(const float *logits, const float *bias, int E, int K, int renorm,
                float routed_scale, int *idx, float *w);
 
-/* Q8G (bits=8) or Q4G (bits=4) row matvec, group `group`, rowbytes stride. */
+/* Q8G (bits=8), Q4G (bits=4) or Q3G (bits=3) row matvec, group `group`,
+ * rowbytes stride. */
 void orc_mvq_rows(float *y, const int8_t *W, const uint16_t *ws, const float *x,
                   int rows, int in, int group, int bits, size_t rowbytes);
 

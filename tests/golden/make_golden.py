@@ -48,7 +48,7 @@ if REF_TREE is None:
     raise SystemExit("make_golden.py needs the reference tree: set WARP_REFERENCE")
 
 sys.path.insert(0, os.path.join(ROOT, "tests"))
-from golden_cases import MOE_CASES  # noqa: E402  (shared with the tests)
+from golden_cases import MOE_CASES, MVQ_CASES, NORM_SIZES  # noqa: E402  (shared with the tests)
 
 
 def layer_sha(L) -> str:
@@ -158,7 +158,19 @@ def tiny_container():
     print("tiny_container written")
 
 
-NORM_SIZES = (2304, 1024, 7168, 100)
+def mvq_fixture():
+    """The reference's waste_mvq_rows_f32 (src/model.c:265-320, the trunk
+    matvec the mvq_rows_f32 slot replaces) on seeded Q8G/Q4G/Q3G tensors."""
+    res = {}
+    for name, (rows, inp, bits) in MVQ_CASES.items():
+        rng = np.random.default_rng(zlib.crc32(name.encode()))
+        raw, s, rb = synth.trunk_tensor(rng, rows, inp, bits)
+        x = synth.activations(len(name) + rows, inp)[0]
+        res[f"{name}_raw"], res[f"{name}_s"], res[f"{name}_x"] = raw, s, x
+        res[f"{name}_rowbytes"] = np.int64(rb)
+        res[f"{name}_y"] = O.ref_mvq_rows(raw, s, x, inp, 128, bits, rb)
+    np.savez_compressed(os.path.join(OUT, "mvq.npz"), **res)
+    print("mvq.npz written")
 
 
 def norm_fixture():
@@ -184,6 +196,7 @@ def main():
     moe_fixtures()
     norm_fixture()
     tiny_container()
+    mvq_fixture()
 
 
 if __name__ == "__main__":
@@ -193,5 +206,7 @@ if __name__ == "__main__":
         moe_fixtures(sys.argv[2:])
     elif sys.argv[1:] == ["container"]:
         tiny_container()
+    elif sys.argv[1:] == ["mvq"]:
+        mvq_fixture()
     else:
         main()

@@ -19,6 +19,15 @@ MOE_CASES = {
 
 MATVEC_CASES = ("matvec_ragged", "matvec_square", "matvec_vq2r")
 
+# the trunk matvec fixtures (mvq.npz): name -> (rows, in, bits)
+MVQ_CASES = {
+    "q8g": (96, 2304, 8), "q8g_ragged": (70, 1000, 8), "q4g": (96, 2304, 4),
+    "q4g_ragged": (50, 520, 4), "q3g": (64, 2304, 3), "q3g_ragged": (33, 300, 3),
+}
+
+# the rmsnorm fixtures (norm.npz): widths
+NORM_SIZES = (2304, 1024, 7168, 100)
+
 
 def load(name):
     return np.load(os.path.join(GOLDEN, name + ".npz"))

@@ -8,6 +8,7 @@ Two levels:
     greedy tokens match the reference's while the logits stay within 1e-4
     relative L2 (four decoder layers of fp32 arithmetic in between, so this
     is looser than the per-layer bound);
+  * the same with every trunk matvec (the mvq_rows_f32 slot) on the device;
   * the engine's own moe_layer and moe_chunk at the Kimi-Linear-48B shape,
     reached through the oracle's harness compiled against the patched
     model.c: the route comes from the engine's CPU router in both engines
@@ -33,6 +34,21 @@ def test_engine_public_api_on_device(tmp_path):
     b_cu, launches, tok_cu, lg_cu = run_engine(CUDA_ENGINE, tmp_path, "cuda")
     assert "CUDA sm_100a" in b_cu, b_cu
     assert launches and launches > 0
+    assert np.array_equal(tok_ref, tok_cu)
+    worst = max(rel_l2(lg_cu[e], lg_ref[e]) for e in range(len(tok_ref)))
+    assert worst < 1e-4, worst
+
+
+def test_engine_trunk_on_device(tmp_path):
+    """Every trunk matvec of the engine through the mvq_rows_f32 slot on the
+    device (WASTE_CUDA_TRUNK_MIN=0 takes even the small ones): more of the
+    backend's kernels run, and the tokens and logits still match."""
+    _, _, tok_ref, lg_ref = run_engine(REF_ENGINE, tmp_path, "ref")
+    _, l_exp, _, _ = run_engine(CUDA_ENGINE, tmp_path, "experts")
+    b_cu, launches, tok_cu, lg_cu = run_engine(CUDA_ENGINE, tmp_path, "trunk",
+                                               env={"WASTE_CUDA_TRUNK_MIN": "0"})
+    assert "CUDA sm_100a" in b_cu
+    assert launches > l_exp
     assert np.array_equal(tok_ref, tok_cu)
     worst = max(rel_l2(lg_cu[e], lg_ref[e]) for e in range(len(tok_ref)))
     assert worst < 1e-4, worst

@@ -109,7 +109,7 @@ def test_restatement_vs_reference_live(seed):
 
 def test_rmsnorm_golden():
     """The MoE block's rmsnorm (src/model.c:132-138) bit for bit."""
-    from golden.make_golden import NORM_SIZES
+    from golden_cases import NORM_SIZES
     g = load("norm")
     for n in NORM_SIZES:
         o = O.rmsnorm(g[f"x{n}"], g[f"w{n}"], float(g["eps"]))
@@ -145,3 +145,23 @@ def test_situ_pair_vs_reference_live():
     for beta, lbeta in ((4.0, 25.0), (1.0, 0.0), (2.5, -1.0)):
         assert np.array_equal(bits(O.situ_pair(g, u, beta, lbeta)),
                               bits(O.ref_situ_pair(g, u, beta, lbeta)))
+
+
+def test_mvq_golden():
+    """The trunk matvec (src/model.c:265-320, Q8G/Q4G/Q3G) bit for bit."""
+    from golden_cases import MVQ_CASES
+    g = load("mvq")
+    for name, (rows, inp, nb) in MVQ_CASES.items():
+        y = O.mvq_rows(g[f"{name}_raw"], g[f"{name}_s"], g[f"{name}_x"], inp, 128, nb,
+                       int(g[f"{name}_rowbytes"]))
+        assert np.array_equal(bits(y), bits(g[f"{name}_y"])), name
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built here")
+def test_mvq_vs_reference_live():
+    rng = np.random.default_rng(11)
+    for nb in (8, 4, 3):
+        raw, s, rb = synth.trunk_tensor(rng, 40, 777, nb)
+        x = synth.activations(12 + nb, 777)[0]
+        assert np.array_equal(bits(O.mvq_rows(raw, s, x, 777, 128, nb, rb)),
+                              bits(O.ref_mvq_rows(raw, s, x, 777, 128, nb, rb)))

@@ -34,7 +34,7 @@ EXPORTS = (
     "waste_cuda_ep_shutdown", "waste_cuda_ep_moe_layer_dev", "waste_cuda_moe_prefill_dev",
     "waste_cuda_ep_moe_layer_rep_dev", "waste_cuda_moe_norm_load", "waste_cuda_moe_block",
     "waste_cuda_moe_block_dev", "waste_cuda_ep_moe_block_dev", "waste_cuda_ep_moe_block_rep_dev",
-    "waste_cuda_moe_activation",
+    "waste_cuda_moe_activation", "waste_cuda_mvq_rows_dev", "waste_cuda_release_host_buffers",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -135,6 +135,9 @@ def load_library() -> C.CDLL:
         "waste_cuda_moe_prefill_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_moe_norm_load": (C.c_int, [C.c_int, C.c_int, P, C.c_float]),
         "waste_cuda_moe_activation": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_float]),
+        "waste_cuda_mvq_rows_dev": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              C.c_int, C.c_size_t, P]),
+        "waste_cuda_release_host_buffers": (None, []),
         "waste_cuda_moe_block": (C.c_int, [C.c_int, P, P, P, P]),
         "waste_cuda_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
@@ -365,6 +368,14 @@ def moe_prefill_dev(layer: int, T: int, K: int, d_route: int, d_rw: int, d_x: in
     v = lambda p: C.c_void_p(int(p) or None)
     _check(load_library().waste_cuda_moe_prefill_dev(layer, T, K, v(d_route), v(d_rw), v(d_x),
                                                      v(d_out), v(stream)))
+
+
+def mvq_rows_dev(d_y: int, d_W: int, d_ws: int, d_x: int, r0: int, r1: int, inp: int,
+                 group: int, bits: int, rowbytes: int, stream: int = 0):
+    """The trunk matvec (mvq_rows_f32) on device pointers."""
+    v = lambda p: C.c_void_p(int(p) or None)
+    _check(load_library().waste_cuda_mvq_rows_dev(v(d_y), v(d_W), v(d_ws), v(d_x), r0, r1, inp,
+                                                  group, bits, rowbytes, v(stream)))
 
 
 def lutb(x, cb_base: int, stages: int = 3) -> np.ndarray:

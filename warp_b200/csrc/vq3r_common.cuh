@@ -32,6 +32,32 @@ __device__ __forceinline__ float f16_keep(uint16_t h)
     return __uint_as_float(sign | ((e + 112u) << 23) | (mn << 13));
 }
 
+/* The four signed bytes of w (byte 0 first) as exact floats, without
+ * integer-to-float conversions, whose issue rate is a small fraction of the
+ * FMA pipe's: each byte, offset by 128, becomes the low mantissa bits of
+ * 2^23 (a byte permute), and 2^23 + 128 is subtracted in float — exact, so
+ * the values are those of (float)(int8_t)byte. */
+__device__ __forceinline__ float4 s8x4_to_f32(uint32_t w)
+{
+    const uint32_t u = w ^ 0x80808080u;
+    const float bias = 8388736.0f;                       /* 2^23 + 128 */
+    return make_float4(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - bias,
+                       __int_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - bias,
+                       __int_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - bias,
+                       __int_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - bias);
+}
+
+/* The four 4-bit codes of the low 16 bits of w (low nibble first) minus 8,
+ * as exact floats, the same way (2^23 + code - (2^23 + 8)). */
+__device__ __forceinline__ float4 u4x4_to_f32(uint32_t w)
+{
+    const float bias = 8388616.0f;                       /* 2^23 + 8 */
+    return make_float4(__int_as_float(0x4B000000u | (w & 0xfu)) - bias,
+                       __int_as_float(0x4B000000u | ((w >> 4) & 0xfu)) - bias,
+                       __int_as_float(0x4B000000u | ((w >> 8) & 0xfu)) - bias,
+                       __int_as_float(0x4B000000u | ((w >> 12) & 0xfu)) - bias);
+}
+
 /* Byte `p` (compile-time) of a little-endian run of 32-bit words. */
 template <int P>
 __device__ __forceinline__ uint32_t byte_at(const uint32_t *w)

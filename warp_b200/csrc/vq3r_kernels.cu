@@ -442,9 +442,11 @@ constexpr long long kSpinLimit = 1ll << 24;
 
 __device__ __forceinline__ bool wait_flag(const unsigned int *flag, unsigned int *err)
 {
+    /* the first polls back to back (the flag is usually a few hundred
+     * nanoseconds away), then with a pause between them */
     for (long long i = 0; i < kSpinLimit; i++) {
         if (ld_acquire(flag)) return true;
-        __nanosleep(64);
+        if (i >= 64) __nanosleep(64);
     }
     atomicOr(err, WC_ERR_ROUTE_WAIT);
     return false;
@@ -609,9 +611,11 @@ __device__ __forceinline__ float warp_sum(float v)
  * memory, in place: r = 1 / sqrtf(sum(x*x) / n + eps), x[i] = (x[i]*r)*w[i].
  * The sum of squares is a fixed tree (thread strides, warp shuffles, warps
  * in order), so every block that normalises the same x gets the same bits.
- * red: blockDim/32 + 1 floats of shared memory. Every thread must call it. */
-__device__ __forceinline__ void block_rmsnorm(float *x, int n, const float *__restrict__ w,
-                                              float eps, float *red)
+ * w: the weights, staged in shared memory with x (a global read per element
+ * here would be a dependent round trip per loop step). red: blockDim/32 + 1
+ * floats of shared memory. Every thread must call it. */
+__device__ __forceinline__ void block_rmsnorm(float *x, int n, const float *w, float eps,
+                                              float *red)
 {
     float s = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
@@ -626,7 +630,7 @@ __device__ __forceinline__ void block_rmsnorm(float *x, int n, const float *__re
     }
     __syncthreads();
     const float r = red[32];
-    for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__fmul_rn(x[i], r), __ldg(w + i));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
     __syncthreads();
 }
 
@@ -672,12 +676,12 @@ __device__ __forceinline__ float dot_q8g_smem(const uint8_t *row, const float *g
     for (int s = 0; s < ng; s++) {
         const int i = s * 128 + lane * 4;
         if (i < n) {
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+            const float4 wf = s8x4_to_f32(*reinterpret_cast<const uint32_t *>(row + i));
             const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
-            float part = (float)(int8_t)(w & 0xff) * xv.x;
-            part = fmaf((float)(int8_t)((w >> 8) & 0xff), xv.y, part);
-            part = fmaf((float)(int8_t)((w >> 16) & 0xff), xv.z, part);
-            part = fmaf((float)(int8_t)(w >> 24), xv.w, part);
+            float part = wf.x * xv.x;
+            part = fmaf(wf.y, xv.y, part);
+            part = fmaf(wf.z, xv.z, part);
+            part = fmaf(wf.w, xv.w, part);
             acc = fmaf(gsc[s], part, acc);
         }
     }
@@ -722,6 +726,15 @@ __host__ __device__ inline RouterGeom router_geom(int E, int si)
  * lowest id wins a tie and a NaN never wins, exactly as the sequential scan
  * from -1e30f does. w = score[best]; renorm by (sum + 1e-20f) accumulated in
  * j order; times routed_scale. */
+/* A float as an unsigned key with the same order (-0 taken as +0): larger
+ * float, larger key. Only finite values above -1e30 are keyed here (the
+ * candidates the reference's scan can select), and their keys are nonzero. */
+__device__ __forceinline__ uint32_t order_key(float f)
+{
+    const uint32_t u = __float_as_uint(f + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 template <int NK>
 __device__ void route_warp(const wc_moe_args &a, int t, int lane)
 {
@@ -745,24 +758,27 @@ __device__ void route_warp(const wc_moe_args &a, int t, int lane)
     float wsel = 0.0f, wsum = 0.0f;
     int mine = -1;                      /* lane j keeps the j-th choice */
     for (int j = 0; j < K; j++) {
+        /* this lane's best: ids ascend within a lane, strict > from -1e30 */
         float bv = -1e30f, bsc = 0.0f;
         int bk = -1;
 #pragma unroll
         for (int k = 0; k < NK; k++)
             if (((live >> k) & 1) && v[k] > bv) { bv = v[k]; bsc = sc[k]; bk = k; }
-        int best = bk >= 0 ? lane + 32 * bk : -1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const float os = __shfl_xor_sync(0xffffffffu, bsc, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, best, o);
-            if (oi >= 0 && (best < 0 || ov > bv || (ov == bv && oi < best))) {
-                bv = ov; bsc = os; best = oi;
-            }
+        /* the warp's largest value, then the lowest id holding it: the
+         * reference's ascending scan with a strict > picks exactly that */
+        const uint32_t key = bk >= 0 ? order_key(bv) : 0u;
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+        int best = -1;
+        float wb = 0.0f;
+        if (kmax != 0u) {                                    /* warp-uniform */
+            const uint32_t cand = (bk >= 0 && key == kmax) ? (uint32_t)(lane + 32 * bk)
+                                                           : 0xffffffffu;
+            best = (int)__reduce_min_sync(0xffffffffu, cand);
+            wb = __shfl_sync(0xffffffffu, bsc, best & 31);
+            if ((best & 31) == lane) live &= ~(1u << (best >> 5));
         }
-        if (best >= 0 && (best & 31) == lane) live &= ~(1u << (best >> 5));
-        if (lane == j) { mine = best; wsel = best >= 0 ? bsc : 0.0f; }
-        wsum += best >= 0 ? bsc : 0.0f;   /* the same j-order sum in every lane */
+        if (lane == j) { mine = best; wsel = wb; }
+        wsum += wb;                     /* the same j-order sum in every lane */
     }
     if (lane < K) {
         float w = wsel;
@@ -812,20 +828,23 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
         wbytes = (uint32_t)nr * ng * 128;
     }
     uint16_t *sst = reinterpret_cast<uint16_t *>(wst + (size_t)(kRouterBlock / 32) * ng * 128);
-    /* The weight rows depend on nothing earlier in the stream: their copies
-     * are issued before the grid-dependency wait, so they overlap the end
-     * of the previous kernel. x, and every write this kernel makes, come
-     * after it. */
+    float *nws = reinterpret_cast<float *>(sst + (size_t)(kRouterBlock / 32) * ng);
+    /* The weight rows (and the block's rmsnorm weights) depend on nothing
+     * earlier in the stream: their copies are issued before the
+     * grid-dependency wait, so they overlap the end of the previous kernel.
+     * x, and every write this kernel makes, come after it. */
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         mbar_fence_init();
         uint32_t tx = (uint32_t)lat * 4 + wbytes;
         const uint32_t sbytes = is_router ? 0u : (uint32_t)nr * ng * 2;
-        tx += sbytes;
+        const uint32_t nbytes = a.norm_w ? (uint32_t)lat * 4 : 0u;
+        tx += sbytes + nbytes;
         mbar_expect_tx(bar, tx);
         if (wbytes) bulk_g2s(wst, wsrc, wbytes, bar);
         if (sbytes)
             bulk_g2s(sst, (kind ? a.shu_s : a.shg_s) + (size_t)o0 * ng, sbytes, bar);
+        if (nbytes) bulk_g2s(nws, a.norm_w, nbytes, bar);
     }
     pdl_wait();
     if (threadIdx.x == 0) {
@@ -846,7 +865,7 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     const bool ok = __syncthreads_and(mbar_wait(bar, 0) && !ep_fail);   /* a missing peer: no dot products */
     if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
     if (a.norm_w) {                  /* the MoE block: route and run on rmsnorm(x) */
-        if (ok) block_rmsnorm(xs, lat, a.norm_w, a.norm_eps, nred);
+        if (ok) block_rmsnorm(xs, lat, nws, a.norm_eps, nred);
         if (b == 0) {
             for (int i = threadIdx.x; ok && i < lat; i += blockDim.x)
                 a.ws.xn[(size_t)t * lat + i] = xs[i];
@@ -881,12 +900,12 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
         for (int gi = 0; gi < ng; gi++) {
             const int i = gi * 128 + lane * 4;
             if (i < lat) {
-                const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+                const float4 wf = s8x4_to_f32(*reinterpret_cast<const uint32_t *>(row + i));
                 const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
-                float part = (float)(int8_t)(w & 0xff) * xv.x;
-                part = fmaf((float)(int8_t)((w >> 8) & 0xff), xv.y, part);
-                part = fmaf((float)(int8_t)((w >> 16) & 0xff), xv.z, part);
-                part = fmaf((float)(int8_t)(w >> 24), xv.w, part);
+                float part = wf.x * xv.x;
+                part = fmaf(wf.y, xv.y, part);
+                part = fmaf(wf.z, xv.z, part);
+                part = fmaf(wf.w, xv.w, part);
                 acc = fmaf(f16_keep(srow[gi]), part, acc);
             }
         }
@@ -896,37 +915,53 @@ __global__ void __launch_bounds__(kRouterBlock) router_kernel(wc_moe_args a, Rou
     /* the last block of this token routes it: the block's writes are
      * ordered before thread 0's release; its acquire orders the other
      * blocks' writes before the routing reads (all through L2) */
+    /* Two tickets: the route waits only for the router blocks; the shared
+     * expert's activation only for the shared blocks (its consumer, the
+     * down kernel's shared blocks, waits on the shared flag). */
+    unsigned int *tk = is_router ? a.ws.tickets + t : a.ws.sh_ticket + t;
+    const unsigned int nblk = is_router ? (unsigned)rg.rblocks : (unsigned)rg.sblocks;
     __syncthreads();
-    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(a.ws.tickets + t, 1u);
+    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(tk, 1u);
     __syncthreads();
-    if (ticket != gridDim.x - 1) return;
-    if (warp == 0) {
-        route_warp<NK>(a, t, lane);
-    } else if (sh_here) {
+    if (ticket != nblk - 1) return;
+    if (is_router) {
+        if (warp == 0) route_warp<NK>(a, t, lane);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            *tk = 0;                                   /* ready for the next launch */
+            st_release(a.ws.route_flag + t, 1u);       /* gate/up may go */
+        }
+        return;
+    }
+    if (!sh_here) {
+        if (threadIdx.x == 0) *tk = 0;
+        return;
+    }
+    {
         float g[kSiluU], u[kSiluU];
-        const int nt = blockDim.x - 32;
+        const int nt = blockDim.x;
 #pragma unroll
         for (int k = 0; k < kSiluU; k++) {
-            const int i = threadIdx.x - 32 + k * nt;
+            const int i = threadIdx.x + k * nt;
             g[k] = i < a.si ? __ldcg(a.ws.sh_g + (size_t)t * a.si + i) : 0.0f;
             u[k] = i < a.si ? __ldcg(a.ws.sh_u + (size_t)t * a.si + i) : 0.0f;
         }
 #pragma unroll
         for (int k = 0; k < kSiluU; k++) {
-            const int i = threadIdx.x - 32 + k * nt;
+            const int i = threadIdx.x + k * nt;
             if (i < a.si)
                 a.ws.sh_h[(size_t)t * a.si + i] = act_pair(a.act, g[k], u[k], a.situ_beta,
                                                            a.situ_lbeta);
         }
-        for (int i = threadIdx.x - 32 + kSiluU * nt; i < a.si; i += nt)   /* si > 1792 */
+        for (int i = threadIdx.x + kSiluU * nt; i < a.si; i += nt)   /* si > 2048 */
             a.ws.sh_h[(size_t)t * a.si + i] =
                 act_pair(a.act, __ldcg(a.ws.sh_g + (size_t)t * a.si + i),
                          __ldcg(a.ws.sh_u + (size_t)t * a.si + i), a.situ_beta, a.situ_lbeta);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        a.ws.tickets[t] = 0;                           /* ready for the next launch */
-        st_release(a.ws.route_flag + t, 1u);           /* gate/up may go */
+        *tk = 0;
+        st_release(a.ws.sh_flag + t, 1u);              /* the shared down rows may go */
     }
 }
 
@@ -995,9 +1030,15 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     const int r0 = min(nrows, rb0 + warp * rpw), r1 = min(nrows, r0 + rpw);
     /* tokens of the group that get the shared expert here */
     const int ts0 = max(0, a.sh_t0 - t0), ts1 = min(nt, a.sh_t1 - t0);
+    float *nws = xs + (size_t)rg.TB * lat;          /* rmsnorm weights */
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         mbar_fence_init();
+        /* one arrival for every byte this block stages: the group's x (its
+         * copy is issued after the dependency wait) and the rmsnorm
+         * weights (constants: copied now) */
+        mbar_expect_tx(bar, (uint32_t)(nt + (a.norm_w ? 1 : 0)) * lat * 4);
+        if (a.norm_w) bulk_g2s(nws, a.norm_w, (uint32_t)lat * 4, bar);
     }
     /* the block's weight rows into L2 while the previous kernel finishes */
     if (lane == 0 && r1 > r0) {
@@ -1018,14 +1059,13 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
         }
         if (b == 0 && !a.norm_w)  /* the group's x is complete (see router_kernel) */
             for (int k = 0; k < nt; k++) st_release(a.ws.x_flag + t0 + k, 1u);
-        mbar_expect_tx(bar, (uint32_t)nt * lat * 4);
         bulk_g2s(xs, a.x + (size_t)t0 * lat, (uint32_t)nt * lat * 4, bar);
     }
     __syncthreads();
     const bool ok = __syncthreads_and(mbar_wait(bar, 0) && !ep_fail);
     if (!ok && !ep_fail && threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
     if (a.norm_w) {                  /* rmsnorm of each token, as in router_kernel */
-        for (int k = 0; k < nt && ok; k++) block_rmsnorm(xs + (size_t)k * lat, lat, a.norm_w,
+        for (int k = 0; k < nt && ok; k++) block_rmsnorm(xs + (size_t)k * lat, lat, nws,
                                                          a.norm_eps, nred);
         if (b == 0) {
             for (int i = threadIdx.x; ok && i < nt * lat; i += blockDim.x)
@@ -1107,10 +1147,9 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
                     const int gi = gb + c, i = gi * 128 + lane * 4;
                     if (gi >= ng) break;
                     if (i >= lat) continue;
-                    const uint32_t w = wv[c];
                     const float sc = f16_keep(sv[c]);
-                    const float w0 = (float)(int8_t)(w & 0xff), w1 = (float)(int8_t)((w >> 8) & 0xff);
-                    const float w2 = (float)(int8_t)((w >> 16) & 0xff), w3 = (float)(int8_t)(w >> 24);
+                    const float4 wf = s8x4_to_f32(wv[c]);
+                    const float w0 = wf.x, w1 = wf.y, w2 = wf.z, w3 = wf.w;
 #pragma unroll
                     for (int k = 0; k < kRouterTB; k++) {
                         if (k >= ts0 && k < ts1) {
@@ -1135,11 +1174,23 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     }
     /* the last block of this token group routes it (ordering as in the
      * single-token kernel: writes, barrier, acq_rel ticket) */
+    /* two tickets, as in router_kernel: the group's route after its router
+     * blocks, the shared activation after its shared blocks */
+    unsigned int *tk = is_router ? a.ws.tickets + t0 : a.ws.sh_ticket + t0;
+    const unsigned int nblk = is_router ? (unsigned)rg.rblocks : (unsigned)rg.sblocks;
     __syncthreads();
-    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(a.ws.tickets + t0, 1u);
+    if (threadIdx.x == 0) ticket = atomic_add_acq_rel(tk, 1u);
     __syncthreads();
-    if (ticket != gridDim.x - 1) return;
-    if (warp < nt) route_warp<NK>(a, t0 + warp, lane);
+    if (ticket != nblk - 1) return;
+    if (is_router) {
+        if (warp < nt) route_warp<NK>(a, t0 + warp, lane);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            *tk = 0;                                   /* ready for the next launch */
+            for (int k = 0; k < nt; k++) st_release(a.ws.route_flag + t0 + k, 1u);
+        }
+        return;
+    }
     for (int k = ts0; k < ts1; k++) {
         const size_t tb = (size_t)(t0 + k) * a.si;
         for (int i = threadIdx.x; i < a.si; i += blockDim.x)
@@ -1148,8 +1199,8 @@ __global__ void __launch_bounds__(kRouterBlock) router_tokens_kernel(wc_moe_args
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        a.ws.tickets[t0] = 0;                          /* ready for the next launch */
-        for (int k = 0; k < nt; k++) st_release(a.ws.route_flag + t0 + k, 1u);
+        *tk = 0;
+        for (int k = ts0; k < ts1; k++) st_release(a.ws.sh_flag + t0 + k, 1u);
     }
 }
 
@@ -1325,7 +1376,14 @@ gateup_kernel(const __grid_constant__ wc_moe_args a, TileGeom g, const int *idx)
     }
     if (threadIdx.x == 0 && t == 0 && round == 0 && a.prefetch_down) {
         /* this block's share of the routed experts' down index streams:
-         * L2 fetches them while the gathers below keep HBM idle */
+         * L2 fetches them while the gathers below keep HBM idle. Issued
+         * once this tile's own streams have landed, so the prefetch does
+         * not compete with them for HBM (bounded waits; a failure shows
+         * again, and is reported, in the gather's own wait) */
+        if (nhere) {
+            mbar_wait(&sm.bars[0], round & 1u);
+            if (use_map || nvs > h) mbar_wait(&sm.bars[1], round & 1u);
+        }
         const size_t per = bk.scale_off - bk.down_off;
         const size_t total = per * (size_t)a.K * a.T;
         const int nb = gridDim.x;
@@ -1402,7 +1460,7 @@ constexpr int kDnSlices = 12;          /* gate/up slices summed per thread  */
 constexpr int kShRowsMax = 12;         /* shared down rows per warp (shared memory) */
 
 __device__ __forceinline__ void shared_down_block(const wc_moe_args &a, unsigned char *raw,
-                                                  int sb, int rows_pw)
+                                                  int sb, int rows_pw, int d_tiles)
 {
     const wc_bank &bk = a.bank;
     const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -1442,10 +1500,25 @@ __device__ __forceinline__ void shared_down_block(const wc_moe_args &a, unsigned
     }
     pdl_trigger();
     pdl_wait();
+    /* the shared activation of each token: the router's last shared block
+     * raises its flag (every block of the router grid has started before
+     * this grid launched, so the wait ends); the last of these blocks to
+     * pass a token's flag clears it */
+    __shared__ int sgo;
+    if (threadIdx.x == 0) {
+        sgo = 1;
+        for (int tt = a.sh_t0; tt < a.sh_t1; tt++) {
+            if (!wait_flag(a.ws.sh_flag + tt, a.ws.err)) { sgo = 0; break; }
+            if (atomicAdd(a.ws.sh_pass + tt, 1u) == gridDim.x - (unsigned)d_tiles - 1) {
+                a.ws.sh_pass[tt] = 0;
+                a.ws.sh_flag[tt] = 0;
+            }
+        }
+    }
     __syncthreads();
-    const bool ok = nrows == 0 || mbar_wait(bar, 0);
+    const bool ok = sgo && (nrows == 0 || mbar_wait(bar, 0));
     if (!ok) {
-        if (threadIdx.x == 0) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
+        if (threadIdx.x == 0 && sgo) atomicOr(a.ws.err, WC_ERR_TMA_WAIT);
         return;
     }
     for (int tt = a.sh_t0; tt < a.sh_t1; tt++) {
@@ -1470,7 +1543,7 @@ down_kernel(const __grid_constant__ wc_moe_args a, TileGeom gu, TileGeom g, int 
     extern __shared__ __align__(16) unsigned char smraw[];
     const wc_bank &bk = a.bank;
     if ((int)blockIdx.x >= d_tiles) {
-        shared_down_block(a, smraw, blockIdx.x - d_tiles, sh_rows_pw);
+        shared_down_block(a, smraw, blockIdx.x - d_tiles, sh_rows_pw, d_tiles);
         return;
     }
     TileSmem sm(smraw, g);
@@ -1654,9 +1727,14 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
                                     (min(n, lo + share) - lo) & ~(size_t)15);
         }
     }
+    /* the route weights and the residual input are complete before this
+     * layer's first kernel ran its own wait (the router wrote the weights;
+     * the residual is the layer's input): read them before the wait */
+    if (threadIdx.x < K) wsm[threadIdx.x] = __ldcg(w + (size_t)t * K + threadIdx.x);
+    const float hres = (a.resid && !a.ep.on && jl == 0 && ok)
+                           ? __ldcg(a.resid + (size_t)t * bk.lat + i) : 0.0f;
     pdl_wait();
     pdl_trigger();         /* down is done: the next layer's router may prefetch its rows */
-    if (threadIdx.x < K) wsm[threadIdx.x] = __ldcg(w + (size_t)t * K + threadIdx.x);
     const bool sh_here = a.si > 0 && t >= a.sh_t0 && t < a.sh_t1;
     const float shv = (sh_here && jl == 0 && ok) ? __ldcg(a.ws.sh_out + (size_t)t * bk.lat + i)
                                                  : 0.0f;
@@ -1708,7 +1786,7 @@ __global__ void __launch_bounds__(256) combine_kernel(wc_moe_args a, TileGeom g,
         if (sh_here) y = __fadd_rn(y, shv);
         if (!a.ep.on) {
             /* the block's residual add, h + moe (src/model.c:3945) */
-            if (a.resid) y = __fadd_rn(__ldcg(a.resid + (size_t)t * bk.lat + i), y);
+            if (a.resid) y = __fadd_rn(hres, y);
             a.out[(size_t)t * bk.lat + i] = y;
         } else if (!a.ep.rep) {   /* straight into the token's rank, over NVLink */
             const int owner = t / a.ep.T, tl = t % a.ep.T;
@@ -1762,7 +1840,8 @@ size_t router_smem(int lat)
     size_t wmax = (size_t)((kRouterBlock / 32) / kRouterSplit) * lat * 4;
     const size_t wsh = (size_t)(kRouterBlock / 32) * ngr * 128;
     if (wsh > wmax) wmax = wsh;
-    return 16 + (size_t)lat * 4 + wmax + (size_t)(kRouterBlock / 32) * ngr * 2 + 16;
+    /* barrier | x | rows | scales | rmsnorm weights */
+    return 16 + (size_t)lat * 4 + wmax + (size_t)(kRouterBlock / 32) * ngr * 2 + (size_t)lat * 4 + 16;
 }
 
 /* dynamic shared memory of a shared-down block: barrier | h | scales | rows */
@@ -1868,7 +1947,8 @@ int moe_launch_st(const wc_moe_args *a, cudaStream_t s)
         const bool rpdl = !P.on;
         if (a->T >= kRouterTokensMin) {   /* weights read once per token group */
             const RouterTGeom tg = router_t_geom(a->E, a->si, a->T, a->bank.lat);
-            const size_t tsm = 16 + (size_t)tg.TB * a->bank.lat * 4;
+            /* barrier | x of the group | rmsnorm weights */
+            const size_t tsm = 16 + (size_t)(tg.TB + 1) * a->bank.lat * 4;
             const dim3 tgrid(tg.rblocks + tg.sblocks, (a->T + tg.TB - 1) / tg.TB);
             cudaFuncSetAttribute(router_tokens_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm);
             cudaFuncSetAttribute(router_tokens_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm);
@@ -1949,7 +2029,7 @@ extern "C" size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int 
     n += (size_t)T * si * 3 + (size_t)T * lat;
     n += (size_t)T * K * inter;              /* h */
     n += (size_t)T * lat;                    /* xn */
-    return n + 512 + 64;                     /* + control words */
+    return n + WC_WS_CONTROL_WORDS + 64;     /* + control words */
 }
 
 extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
@@ -1960,13 +2040,17 @@ extern "C" void wc_moe_ws_carve(wc_moe_ws *ws, float *base, int T, int K, int E,
     float *p = base;
     /* control words first (zeroed once at allocation, self-resetting):
      * tickets [0,64), route flags [64,128), pass counters [128,192), err
-     * 192, x flags [256,320) */
+     * 192, x flags [256,320), shared tickets [320,384), shared flags
+     * [384,448), shared pass counters [448,512) */
     ws->tickets = reinterpret_cast<unsigned int *>(p);
     ws->route_flag = ws->tickets + 64;
     ws->route_pass = ws->tickets + 128;
     ws->err = ws->tickets + 192;
     ws->x_flag = ws->tickets + 256;
-    p += 512;
+    ws->sh_ticket = ws->tickets + 320;
+    ws->sh_flag = ws->tickets + 384;
+    ws->sh_pass = ws->tickets + 448;
+    p += WC_WS_CONTROL_WORDS;
     ws->p_gu = p; p += (size_t)T * 2 * gu.ns * K * inter;
     ws->p_d = p; p += (size_t)T * K * d.ns * lat;
     ws->logits = p; p += (size_t)T * E;

@@ -151,6 +151,7 @@ static float *g_noalloc_part;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
+static void mirrors_free(void);
 static int pf_wanted(const wc_layer *L, int T, int K);
 static int pf_args(const wc_layer *L, int T, int K, wc_pf_args *a);
 static _Thread_local char g_err[256];
@@ -190,7 +191,10 @@ static unsigned read_device_errors(int clear)
     unsigned int *err = (unsigned int *)S.d_ws + 192, v = 0;
     if (cudaStreamSynchronize(S.stream) != cudaSuccess) return ~0u;
     if (cudaMemcpy(&v, err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return ~0u;
-    if (v && clear) cudaMemset(err, 0, sizeof v);
+    /* a wait that gave up leaves tickets, flags and pass counters of that
+     * launch half-set: the whole control block (the error word included)
+     * starts again from zero */
+    if (v && clear) cudaMemset(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
     if ((v & WC_ERR_PEER_WAIT) && EP.active) EP.poisoned = 1;
     return v;
 }
@@ -348,6 +352,7 @@ void waste_cuda_shutdown(void)
         cudaFreeHost(S.h_x); cudaFreeHost(S.h_out); cudaFreeHost(S.h_idx);
         cudaFreeHost(S.h_w);
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
+        mirrors_free();
         cudaStreamDestroy(S.stream);
         memset(&S, 0, sizeof S);
         g_noalloc_part = NULL;
@@ -357,13 +362,209 @@ void waste_cuda_shutdown(void)
 
 /* ---- registration ---------------------------------------------------- */
 
+/* ---- the trunk matvec slot ---------------------------------------------
+ * The engine's dispatch table (src/waste_backend.h:67-90) and the argument
+ * of its mvq_rows_f32 slot (src/simd.h:35-39), restated field for field:
+ * the slot is called with a pointer to the table at registration and with
+ * a pointer to the argument on every trunk matvec. */
+typedef struct {
+    void (*kda_step)(void);
+    void (*short_conv_step)(void);
+    void (*rmsnorm_gated)(void);
+    void (*mvq_rows_f32)(int b, int e, void *arg);
+    void (*lutb_range)(int lo, int hi, void *arg);
+    int on_device;
+} wc_kernels_table;
+
+typedef struct {
+    float *y;
+    const int8_t *W;
+    const uint16_t *ws;
+    const int8_t *xq;
+    const float *xs;
+    int in, ng, group, bits;
+    size_t rowbytes;
+} wc_mvq_arg;
+
+/* Device copies of the engine's trunk tensors, keyed by the host address
+ * of their weights (the engine keeps them resident and passes the same
+ * pointers on every call), open addressing. */
+#define WC_MIRRORS 4096
+static struct {
+    const void *key;
+    uint8_t *d_W;
+    uint16_t *d_ws;
+    size_t rows, rowbytes;
+    int ng;
+} g_mirror[WC_MIRRORS];
+static float *g_mvq_x, *g_mvq_y;
+static size_t g_mvq_xcap, g_mvq_ycap;
+static void (*g_mvq_cpu)(int b, int e, void *arg);   /* the slot's previous occupant */
+static size_t g_trunk_min = (size_t)1 << 20;         /* WASTE_CUDA_TRUNK_MIN bytes */
+
+static size_t mirror_hash(const void *p)
+{
+    uint64_t x = (uint64_t)(uintptr_t)p;
+    x ^= x >> 33; x *= 0xff51afd7ed558ccdULL; x ^= x >> 33;
+    return (size_t)(x & (WC_MIRRORS - 1));
+}
+
+/* The tensor's device copy holding at least `rows` rows, made (or grown)
+ * now when it is not there yet. NULL when it cannot be. Under g_mu. */
+static int mirror_get(const wc_mvq_arg *a, size_t rows, uint8_t **dW, uint16_t **dws)
+{
+    size_t i = mirror_hash(a->W);
+    for (int probe = 0; probe < WC_MIRRORS; probe++, i = (i + 1) & (WC_MIRRORS - 1)) {
+        if (g_mirror[i].key == a->W) {
+            if (g_mirror[i].rows >= rows && g_mirror[i].rowbytes == a->rowbytes &&
+                g_mirror[i].ng == a->ng) {
+                *dW = g_mirror[i].d_W;
+                *dws = g_mirror[i].d_ws;
+                return 0;
+            }
+            cudaFree(g_mirror[i].d_W);
+            cudaFree(g_mirror[i].d_ws);
+            break;
+        }
+        if (!g_mirror[i].key) break;
+    }
+    if (g_mirror[i].key && g_mirror[i].key != a->W) return -1;   /* table full */
+    const size_t wb = rows * a->rowbytes, sb = rows * (size_t)a->ng * sizeof(uint16_t);
+    uint8_t *w = NULL;
+    uint16_t *s = NULL;
+    if (cudaMalloc((void **)&w, wb) != cudaSuccess || cudaMalloc((void **)&s, sb) != cudaSuccess ||
+        cudaMemcpy(w, a->W, wb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(s, a->ws, sb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(w);
+        cudaFree(s);
+        cudaGetLastError();
+        memset(&g_mirror[i], 0, sizeof g_mirror[i]);
+        return -1;
+    }
+    g_mirror[i].key = a->W;
+    g_mirror[i].d_W = w;
+    g_mirror[i].d_ws = s;
+    g_mirror[i].rows = rows;
+    g_mirror[i].rowbytes = a->rowbytes;
+    g_mirror[i].ng = a->ng;
+    *dW = w;
+    *dws = s;
+    return 0;
+}
+
+static void mirrors_free(void)
+{
+    for (int i = 0; i < WC_MIRRORS; i++) {
+        if (!g_mirror[i].key) continue;
+        cudaFree(g_mirror[i].d_W);
+        cudaFree(g_mirror[i].d_ws);
+    }
+    memset(g_mirror, 0, sizeof g_mirror);
+    cudaFree(g_mvq_x);
+    cudaFree(g_mvq_y);
+    g_mvq_x = g_mvq_y = NULL;
+    g_mvq_xcap = g_mvq_ycap = 0;
+}
+
+/* The device side of one slot call, under g_mu: 0, or -1 (the caller
+ * computes the rows on the CPU instead). */
+static int mvq_device(int b, int e, const wc_mvq_arg *a)
+{
+    uint8_t *dW;
+    uint16_t *dws;
+    if (!S.inited || mirror_get(a, (size_t)e, &dW, &dws)) return -1;
+    const size_t xb = (size_t)a->in * sizeof(float), yb = (size_t)e * sizeof(float);
+    if (xb > g_mvq_xcap) {
+        cudaFree(g_mvq_x);
+        g_mvq_x = NULL;
+        g_mvq_xcap = 0;
+        if (cudaMalloc((void **)&g_mvq_x, xb) != cudaSuccess) return -1;
+        g_mvq_xcap = xb;
+    }
+    if (yb > g_mvq_ycap) {
+        cudaFree(g_mvq_y);
+        g_mvq_y = NULL;
+        g_mvq_ycap = 0;
+        if (cudaMalloc((void **)&g_mvq_y, yb) != cudaSuccess) return -1;
+        g_mvq_ycap = yb;
+    }
+    wc_mvq_args k = { g_mvq_y, dW, dws, g_mvq_x, b, e, a->in, a->ng, a->group, a->bits,
+                      a->rowbytes };
+    if (cudaMemcpyAsync(g_mvq_x, a->xs, xb, cudaMemcpyHostToDevice, S.stream) != cudaSuccess ||
+        wc_mvq_launch(&k, S.stream) != 0 ||
+        cudaMemcpyAsync(a->y + b, g_mvq_y + b, (size_t)(e - b) * sizeof(float),
+                        cudaMemcpyDeviceToHost, S.stream) != cudaSuccess ||
+        cudaStreamSynchronize(S.stream) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return 0;
+}
+
+/* The engine's mvq_rows_f32 slot (src/model.c:397, run on the calling
+ * thread with the whole row range: on_device). Tensors of at least
+ * WASTE_CUDA_TRUNK_MIN bytes (default 1 MiB) run on the device from their
+ * HBM copy; smaller ones, the quantised-activation form (xq set) and any
+ * device failure run on the CPU kernel the slot held before (the slot has
+ * no error channel, as the Metal backend does it). */
+static void mvq_slot(int b, int e, void *arg)
+{
+    const wc_mvq_arg *a = (const wc_mvq_arg *)arg;
+    int done = -1;
+    if (!a->xq && a->xs && (a->bits == 8 || a->bits == 4 || a->bits == 3) && e > b &&
+        (size_t)e * a->rowbytes >= g_trunk_min) {
+        pthread_mutex_lock(&g_mu);
+        done = mvq_device(b, e, a);
+        pthread_mutex_unlock(&g_mu);
+    }
+    if (done != 0 && g_mvq_cpu) g_mvq_cpu(b, e, arg);
+}
+
 const char *waste_register_cuda(void *table)
 {
-    (void)table;
     const char *e = getenv("WASTE_CUDA");
     if (e && *e == '0') return NULL;
     if (waste_cuda_init(-1) != 0) return NULL;
+    wc_kernels_table *t = (wc_kernels_table *)table;
+    if (t && t->mvq_rows_f32 && getenv_flag("WASTE_CUDA_TRUNK", 1)) {
+        const char *m = getenv("WASTE_CUDA_TRUNK_MIN");
+        if (m && *m) g_trunk_min = (size_t)strtoull(m, NULL, 10);
+        if (t->mvq_rows_f32 != mvq_slot) g_mvq_cpu = t->mvq_rows_f32;
+        t->mvq_rows_f32 = mvq_slot;
+        t->on_device = 1;
+    }
     return S.name;
+}
+
+void waste_cuda_release_host_buffers(void)
+{
+    pthread_mutex_lock(&g_mu);
+    if (S.inited) {
+        cudaStreamSynchronize(S.stream);
+        mirrors_free();
+    }
+    pthread_mutex_unlock(&g_mu);
+}
+
+int waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws, const float *d_x,
+                            int r0, int r1, int in, int group, int bits, size_t rowbytes,
+                            void *stream)
+{
+    if (!d_y || !d_W || !d_ws || !d_x || r0 < 0 || r1 <= r0 || in <= 0 || group <= 0 ||
+        (bits != 8 && bits != 4 && bits != 3) || rowbytes == 0)
+        return fail(WASTE_CUDA_E_ARG, "mvq_rows_dev: bad arguments");
+    int rc = 0;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "mvq_rows_dev before waste_cuda_init"); goto out; }
+    {
+        const int ng = (in + group - 1) / group;
+        wc_mvq_args k = { d_y, (const uint8_t *)d_W, d_ws, d_x, r0, r1, in, ng, group, bits,
+                          rowbytes };
+        CK((cudaError_t)wc_mvq_launch(&k, stream ? stream : (void *)S.stream), "trunk matvec");
+    }
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
 }
 
 static int slot_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
@@ -1568,6 +1769,7 @@ static int host_layer(int layer, const float *x, float *out, int *routed, float 
         const unsigned int err = *(const unsigned int *)(S.h_res + lat + 2 * WC_MAX_TOPK);
         if (err) {
             cudaMemset(S.d_res + lat + 2 * WC_MAX_TOPK, 0, sizeof(unsigned int));
+            cudaMemset(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
             rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
             goto out;
         }

@@ -51,6 +51,9 @@ typedef struct {
     unsigned int *route_pass;  /* [T] gate/up tiles that have seen the flag   */
     unsigned int *x_flag;      /* [T] 1 once the router's dependency wait has
                                   passed: x is complete                        */
+    unsigned int *sh_ticket;   /* [T] router blocks of the shared expert done */
+    unsigned int *sh_flag;     /* [T] 1 once the shared activation is written */
+    unsigned int *sh_pass;     /* [T] shared down blocks that have seen it     */
     unsigned int *err;         /* sticky device error bits (WC_ERR_*)         */
 } wc_moe_ws;
 
@@ -138,6 +141,10 @@ typedef struct {
     size_t pf_bytes[4];
 } wc_moe_args;
 
+/* The workspace starts with this many control words (tickets, flags, pass
+ * counters, the error word at 192), then the float arrays. */
+#define WC_WS_CONTROL_WORDS 512
+
 /* Floats of workspace for T tokens. The region must be zeroed once when it
  * is allocated (the ticket counters reset themselves after every launch). */
 size_t wc_moe_ws_floats(int T, int K, int E, int lat, int inter, int si,
@@ -213,6 +220,21 @@ typedef struct {
 int    wc_pf_supported(const wc_bank *b, int T, int K);
 size_t wc_pf_max_tiles(int T, int K, int n_experts);
 int    wc_pf_launch(const wc_pf_args *a, void *stream);
+
+/* The trunk matvec (trunk_mvq.cu): rows [r0, r1) of a Q8G / Q4G / Q3G
+ * tensor (bits 8 / 4 / 3), `rowbytes` bytes per row, one f16 scale per
+ * group of `group` weights (ng groups per row), against x[in] fp32; all
+ * device pointers. y[r] for r in [r0, r1). */
+typedef struct {
+    float *y;
+    const uint8_t *W;
+    const uint16_t *ws;
+    const float *x;
+    int r0, r1, in, ng, group, bits;
+    size_t rowbytes;
+} wc_mvq_args;
+
+int wc_mvq_launch(const wc_mvq_args *a, void *stream);
 
 /* Kernels launched by this library since load. */
 uint64_t wc_launches(void);

@@ -143,6 +143,23 @@ def q8g(rng: np.random.Generator, rows: int, cols: int, s_lo: float, s_hi: float
     return q, s
 
 
+def trunk_tensor(rng: np.random.Generator, rows: int, cols: int, bits: int, group: int = GROUP):
+    """A quantised trunk tensor in the engine's layout (src/model.c:601-610):
+    (raw row bytes [rows][rowbytes] uint8, f16 group scales [rows][ng],
+    rowbytes). Q8G/Q4G rows are ng*group*bits/8 bytes, Q3G rows a 3-bit
+    bitstream plus one guard byte. Padding past `cols` is zero."""
+    ng = (cols + group - 1) // group
+    if bits == 3:
+        rowbytes = (ng * group * 3 + 7) // 8 + 1
+    else:
+        rowbytes = ng * group * bits // 8
+    raw = rng.integers(0, 256, size=(rows, rowbytes), dtype=np.uint8)
+    if bits == 8 and cols % group:
+        raw[:, cols:] = 0
+    s = f16_bits(rng.uniform(2e-4, 2e-3, size=(rows, ng)))
+    return raw, s, rowbytes
+
+
 @dataclass
 class MoELayer:
     """One Kimi-Linear-shaped MoE layer, as the engine holds it after load."""
