@@ -81,6 +81,9 @@ typedef struct {
     void (*vq_bank_free)(int layer);
     int  (*moe_experts)(const waste_moe_call *c);
     int  (*moe_chunk_experts)(const waste_moe_chunk_call *c);
+    int  (*vq_bank_load_file)(int layer, int fd, int64_t offset, int n_experts,
+                              size_t rec_bytes, int first, int count, int inter,
+                              int lat, int stages);
 } waste_vq_slots;
 
 /* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */
@@ -121,6 +124,19 @@ int  waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes,
                              int first, int count, const void *records,
                              int inter, int lat, int stages);
 void waste_cuda_vq_bank_free(int layer);
+
+/* The same records read straight from a bank file: record e of the layer
+ * at byte offset + e * rec_bytes of `fd` (src/model.c:1767-1795 bank_fetch
+ * reads them there, offset 0). Ranges of whole records (up to 64 MB) are
+ * read with pread into two pinned staging buffers, and each range's upload
+ * overlaps the read of the next; every header is checked before its range
+ * is copied. The buffers are page aligned, so a file opened for direct I/O
+ * (O_DIRECT) reads too. Replaces, for a bank resident in HBM, the engine's
+ * expert cache (src/ecache.c) and its per-record reads. Returns once the
+ * records are in HBM. */
+int  waste_cuda_vq_bank_load_file(int layer, int fd, int64_t offset, int n_experts,
+                                  size_t rec_bytes, int first, int count, int inter,
+                                  int lat, int stages);
 
 /* Reserves HBM for records [first, first+count) of a layer of n_experts
  * ahead of loading, for a caller that holds only part of the experts. Later
@@ -403,6 +419,25 @@ int  waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws,
                              const float *d_x, int r0, int r1, int in, int group,
                              int bits, size_t rowbytes, void *stream);
 void waste_cuda_release_host_buffers(void);
+
+/* ---- the matvec with interleaved table copies ----------------------------
+ * vq_matvec_dev with fewer shared-memory bank conflicts: every table entry
+ * is held `copies` (2 or 4) times side by side, and each lookup reads the
+ * copy a per-matrix copy-select stream names, chosen once so that the 32
+ * lookups of a warp instruction spread over the banks. The sums are the
+ * ones vq_matvec_dev computes, bit for bit (same order, same table values).
+ * vq_sel_bytes: the stream's size for an M x N matrix (0 for shapes outside
+ * 2048 < M <= 8192, N a multiple of 8, 3 stages). vq_sel_build_dev writes
+ * the stream of one matrix from its index stream (device pointers, 16-byte
+ * aligned; once per matrix, e.g. at load). No counterpart in the reference
+ * (a CPU has no bank conflicts to avoid). */
+size_t waste_cuda_vq_sel_bytes(int M, int N, int stages, int copies);
+int    waste_cuda_vq_sel_build_dev(const uint8_t *d_idx, void *d_sel, int M, int N,
+                                   int stages, int copies, void *stream);
+int    waste_cuda_vq_matvec_sel_dev(int G, const uint8_t *const *idx,
+                                    const void *const *sel, const uint16_t *const *scale,
+                                    const float *const *x, float *const *y, int M, int N,
+                                    int cb_base, int stages, int copies, void *stream);
 
 /* Kernels this library launched since load (a running count, for
  * benchmarks that report how many of their launches were this library's). */

@@ -35,6 +35,8 @@ EXPORTS = (
     "waste_cuda_ep_moe_layer_rep_dev", "waste_cuda_moe_norm_load", "waste_cuda_moe_block",
     "waste_cuda_moe_block_dev", "waste_cuda_ep_moe_block_dev", "waste_cuda_ep_moe_block_rep_dev",
     "waste_cuda_moe_activation", "waste_cuda_mvq_rows_dev", "waste_cuda_release_host_buffers",
+    "waste_cuda_vq_sel_bytes", "waste_cuda_vq_sel_build_dev", "waste_cuda_vq_matvec_sel_dev",
+    "waste_cuda_vq_bank_load_file",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -71,7 +73,7 @@ class VqSlots(C.Structure):
     """waste_vq_slots: the expert-path slots next to waste_kernels."""
     _fields_ = [("codebooks_load", C.c_void_p), ("vq_bank_load", C.c_void_p),
                 ("vq_bank_free", C.c_void_p), ("moe_experts", C.c_void_p),
-                ("moe_chunk_experts", C.c_void_p)]
+                ("moe_chunk_experts", C.c_void_p), ("vq_bank_load_file", C.c_void_p)]
 
 
 _lib = None
@@ -138,6 +140,13 @@ def load_library() -> C.CDLL:
         "waste_cuda_mvq_rows_dev": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int,
                                               C.c_int, C.c_size_t, P]),
         "waste_cuda_release_host_buffers": (None, []),
+        "waste_cuda_vq_sel_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq_bank_load_file": (C.c_int, [C.c_int, C.c_int, C.c_int64, C.c_int,
+                                                   C.c_size_t, C.c_int, C.c_int, C.c_int,
+                                                   C.c_int, C.c_int]),
+        "waste_cuda_vq_sel_build_dev": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.c_int, P]),
+        "waste_cuda_vq_matvec_sel_dev": (C.c_int, [C.c_int, P, P, P, P, P, C.c_int, C.c_int,
+                                                   C.c_int, C.c_int, C.c_int, P]),
         "waste_cuda_moe_block": (C.c_int, [C.c_int, P, P, P, P]),
         "waste_cuda_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
@@ -229,6 +238,18 @@ def vq_bank_load(layer: int, n_experts: int, rec_bytes: int, first: int, count: 
         raise ValueError("records buffer shorter than count * rec_bytes")
     _check(load_library().waste_cuda_vq_bank_load(layer, n_experts, rec_bytes, first, count,
                                                   _ptr(r), inter, lat, stages))
+
+
+def vq_bank_load_file(layer: int, path: str, n_experts: int, rec_bytes: int, first: int,
+                      count: int, inter: int, lat: int, stages: int = 3, offset: int = 0):
+    """Records [first, first+count) of a layer straight from a bank file."""
+    fd = os.open(path, os.O_RDONLY)
+    try:
+        _check(load_library().waste_cuda_vq_bank_load_file(layer, fd, offset, n_experts,
+                                                           rec_bytes, first, count, inter, lat,
+                                                           stages))
+    finally:
+        os.close(fd)
 
 
 def vq_bank_free(layer: int):
@@ -412,6 +433,27 @@ def vq_matvec_dev(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base:
     _check(load_library().waste_cuda_vq_matvec_dev(
         G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base, stages,
         C.c_void_p(stream or None)))
+
+
+def vq_sel_bytes(M: int, N: int, stages: int = 3, copies: int = 2) -> int:
+    return int(load_library().waste_cuda_vq_sel_bytes(M, N, stages, copies))
+
+
+def vq_sel_build_dev(d_idx: int, d_sel: int, M: int, N: int, stages: int = 3, copies: int = 2,
+                     stream: int = 0):
+    """Writes a matrix's copy-select stream (device pointers)."""
+    _check(load_library().waste_cuda_vq_sel_build_dev(C.c_void_p(d_idx), C.c_void_p(d_sel), M, N,
+                                                      stages, copies, C.c_void_p(stream or None)))
+
+
+def vq_matvec_sel_dev(idx_ptrs, sel_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int,
+                      cb_base: int, stages: int = 3, copies: int = 2, stream: int = 0):
+    """vq_matvec_dev with interleaved table copies and copy-select streams."""
+    G = len(idx_ptrs)
+    arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
+    _check(load_library().waste_cuda_vq_matvec_sel_dev(
+        G, arr(idx_ptrs), arr(sel_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base,
+        stages, copies, C.c_void_p(stream or None)))
 
 
 NOALLOC_SCRATCH_BYTES = 32 << 20

@@ -2158,6 +2158,16 @@ static int matvec_launch_st(const wc_matvec_args *a, cudaStream_t s)
     return (int)cudaGetLastError();
 }
 
+extern "C" int wc_matvec_reduce_launch(const wc_matvec_args *a, int ns, void *stream)
+{
+    const int n = a->G * a->M;
+    const int pe = prof_begin(WC_PH_MATVEC_REDUCE, (cudaStream_t)stream);
+    matvec_reduce_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(ns, *a);
+    prof_end(pe, (cudaStream_t)stream);
+    g_launches += 1;
+    return (int)cudaGetLastError();
+}
+
 extern "C" int wc_matvec_launch(const wc_matvec_args *a, void *stream)
 {
     cudaStream_t s = (cudaStream_t)stream;

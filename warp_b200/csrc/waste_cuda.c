@@ -23,6 +23,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #define WC_MAX_LAYERS 128          /* WASTE_MAX_LAYERS, src/model.h:44 */
 #define WC_MAX_TOPK 64             /* src/model.c:814-815 bounds top_k */
@@ -148,6 +149,16 @@ static struct {
 _Static_assert(WASTE_CUDA_NOALLOC_SCRATCH_BYTES == WC_NOALLOC_PART_FLOATS * sizeof(float),
                "header and kernel disagree on the fixed scratch size");
 static float *g_noalloc_part;
+
+/* Two pinned staging buffers for loading banks from files: while one is
+ * copied to HBM, the next range is read into the other. */
+#define WC_STAGE_BYTES ((size_t)64 << 20)
+static struct {
+    uint8_t *buf[2];
+    size_t bytes;
+    cudaEvent_t done[2];
+    int ev;
+} g_stage;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
@@ -353,6 +364,11 @@ void waste_cuda_shutdown(void)
         cudaFreeHost(S.h_w);
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
         mirrors_free();
+        for (int b = 0; b < 2; b++) {
+            cudaFreeHost(g_stage.buf[b]);
+            if (g_stage.ev) cudaEventDestroy(g_stage.done[b]);
+        }
+        memset(&g_stage, 0, sizeof g_stage);
         cudaStreamDestroy(S.stream);
         memset(&S, 0, sizeof S);
         g_noalloc_part = NULL;
@@ -585,6 +601,7 @@ int waste_register_cuda_vq(waste_vq_slots *s)
     s->vq_bank_free = waste_cuda_vq_bank_free;
     s->moe_experts = waste_cuda_moe_experts;
     s->moe_chunk_experts = waste_cuda_moe_chunk_experts;
+    s->vq_bank_load_file = waste_cuda_vq_bank_load_file;
     return 0;
 }
 
@@ -817,14 +834,15 @@ out:
     return rc;
 }
 
-int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
-                            int count, const void *records, int inter, int lat,
-                            int stages)
+/* Records [first, first+count) of a layer from host memory: every header
+ * checked, the layer's bank reserved at its first load, then one copy —
+ * synchronous, or (copy_stream set: records in pinned memory) ordered on
+ * copy_stream. Under g_mu. */
+static int bank_load_locked(int layer, int n_experts, size_t rec_bytes, int first, int count,
+                            const void *records, int inter, int lat, int stages,
+                            cudaStream_t copy_stream)
 {
     int rc = 0;
-    if (!records || !bank_args_ok(layer, n_experts, rec_bytes, first, count, inter, lat, stages))
-        return fail(WASTE_CUDA_E_ARG, "vq_bank_load: bad arguments");
-    pthread_mutex_lock(&g_mu);
     if (!S.inited && (rc = init_locked(-1))) goto out;
     if (!S.d_books) { rc = fail(WASTE_CUDA_E_ARG, "load codebooks before banks"); goto out; }
     wc_layer *L = &S.layer[layer];
@@ -877,13 +895,88 @@ int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int firs
         bank_tensor_maps(&L->kb);
     }
     const int at = first - L->kb.first;
-    CK(cudaMemcpy(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
-                  cudaMemcpyHostToDevice), "bank H2D");
+    if (copy_stream)
+        CK(cudaMemcpyAsync(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
+                           cudaMemcpyHostToDevice, copy_stream), "bank H2D");
+    else
+        CK(cudaMemcpy(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
+                      cudaMemcpyHostToDevice), "bank H2D");
     for (int i = at; i < at + count; i++) {
         L->n_present += !L->present[i];
         L->present[i] = 1;
     }
     L->loaded = 1;
+out:
+    return rc;
+}
+
+int waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes, int first,
+                            int count, const void *records, int inter, int lat,
+                            int stages)
+{
+    if (!records || !bank_args_ok(layer, n_experts, rec_bytes, first, count, inter, lat, stages))
+        return fail(WASTE_CUDA_E_ARG, "vq_bank_load: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    const int rc = bank_load_locked(layer, n_experts, rec_bytes, first, count, records, inter,
+                                    lat, stages, NULL);
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_bank_load_file(int layer, int fd, int64_t offset, int n_experts,
+                                 size_t rec_bytes, int first, int count, int inter, int lat,
+                                 int stages)
+{
+    int rc = 0;
+    if (fd < 0 || offset < 0 || !bank_args_ok(layer, n_experts, rec_bytes, first, count, inter,
+                                                lat, stages))
+        return fail(WASTE_CUDA_E_ARG, "vq_bank_load_file: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    /* whole records per range, at least one; the buffers are page aligned
+     * (pinned allocations), so files opened for direct I/O read too */
+    size_t per = WC_STAGE_BYTES / rec_bytes;
+    if (per < 1) per = 1;
+    const size_t need = per * rec_bytes;
+    if (need > g_stage.bytes) {
+        for (int b = 0; b < 2; b++) {
+            if (g_stage.ev) cudaEventSynchronize(g_stage.done[b]);
+            cudaFreeHost(g_stage.buf[b]);
+            g_stage.buf[b] = NULL;
+        }
+        g_stage.bytes = 0;
+        for (int b = 0; b < 2; b++)
+            CK(cudaMallocHost((void **)&g_stage.buf[b], need), "bank staging");
+        g_stage.bytes = need;
+    }
+    if (!g_stage.ev) {
+        for (int b = 0; b < 2; b++)
+            CK(cudaEventCreateWithFlags(&g_stage.done[b], cudaEventDisableTiming), "staging event");
+        g_stage.ev = 1;
+    }
+    for (int e0 = 0, k = 0; e0 < count; e0 += (int)per, k++) {
+        const int n = count - e0 < (int)per ? count - e0 : (int)per;
+        const int b = k & 1;
+        CK(cudaEventSynchronize(g_stage.done[b]), "staging reuse");   /* its last copy is done */
+        size_t got = 0;
+        const size_t want = (size_t)n * rec_bytes;
+        const int64_t at = offset + (int64_t)(first + e0) * (int64_t)rec_bytes;
+        while (got < want) {
+            const ssize_t r = pread(fd, g_stage.buf[b] + got, want - got, (off_t)(at + (int64_t)got));
+            if (r <= 0) {
+                rc = fail(WASTE_CUDA_E_ARG, "vq_bank_load_file: layer %d: short read at byte %lld",
+                          layer, (long long)(at + (int64_t)got));
+                goto drain;
+            }
+            got += (size_t)r;
+        }
+        if ((rc = bank_load_locked(layer, n_experts, rec_bytes, first + e0, n, g_stage.buf[b],
+                                   inter, lat, stages, S.stream)))
+            goto drain;
+        CK(cudaEventRecord(g_stage.done[b], S.stream), "staging event");
+    }
+drain:
+    cudaStreamSynchronize(S.stream);
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -1969,6 +2062,70 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
     a.books = S.d_books;
     a.part = g_noalloc_part;
     CK((cudaError_t)wc_matvec_launch(&a, stream ? stream : (void *)S.stream), "matvec");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- the matvec with interleaved table copies (matvec_sel.cu) ------------ */
+
+static int sel_shape_ok(int M, int N, int stages, int copies)
+{
+    if ((copies != 2 && copies != 4) || stages != 3 || N <= 0 || N % 8 || M <= 2048 || M > 8192)
+        return fail(WASTE_CUDA_E_ARG, "vq_sel: copies 2 or 4, 3 stages, 2048 < M <= 8192, "
+                    "N a multiple of 8 (got copies %d, stages %d, %dx%d)", copies, stages, M, N);
+    return 0;
+}
+
+size_t waste_cuda_vq_sel_bytes(int M, int N, int stages, int copies)
+{
+    if (sel_shape_ok(M, N, stages, copies)) return 0;
+    return wc_sel_words(M, N, copies) * sizeof(uint32_t);
+}
+
+int waste_cuda_vq_sel_build_dev(const uint8_t *d_idx, void *d_sel, int M, int N, int stages,
+                                int copies, void *stream)
+{
+    int rc = 0;
+    if (!d_idx || !d_sel || ((uintptr_t)d_sel & 15))
+        return fail(WASTE_CUDA_E_ARG, "vq_sel_build: NULL or unaligned (16 bytes) pointer");
+    if ((rc = sel_shape_ok(M, N, stages, copies))) return rc;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "vq_sel_build before waste_cuda_init"); goto out; }
+    CK((cudaError_t)wc_sel_build_launch(d_idx, (uint32_t *)d_sel, M, N, stages, copies,
+                                        stream ? stream : (void *)S.stream), "copy-select build");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_matvec_sel_dev(int G, const uint8_t *const *idx, const void *const *sel,
+                                 const uint16_t *const *scale, const float *const *x,
+                                 float *const *y, int M, int N, int cb_base, int stages,
+                                 int copies, void *stream)
+{
+    int rc = 0;
+    if (G <= 0 || G > WC_MAX_G || !idx || !sel || !scale || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "matvec_sel_dev: G must be 1..%d, pointers non-NULL", WC_MAX_G);
+    if ((rc = sel_shape_ok(M, N, stages, copies))) return rc;
+    for (int g = 0; g < G; g++)
+        if (((uintptr_t)idx[g] & 15) || ((uintptr_t)x[g] & 15) || ((uintptr_t)sel[g] & 15))
+            return fail(WASTE_CUDA_E_ARG, "matrix %d: index, select or x pointer not 16-byte "
+                        "aligned", g);
+    pthread_mutex_lock(&g_mu);
+    if ((rc = check_mat(M, N, cb_base, stages))) goto out;
+    if ((rc = tmp_reserve(wc_matvec_part_floats(G, M, N) * 4))) goto out;
+    static wc_matvec_args a;
+    memset(&a, 0, sizeof a);
+    a.G = G; a.M = M; a.N = N; a.stages = stages; a.cb_base = cb_base;
+    for (int g = 0; g < G; g++) {
+        a.idx[g] = idx[g]; a.scale[g] = scale[g]; a.x[g] = x[g]; a.y[g] = y[g];
+        a.sel[g] = (const uint32_t *)sel[g];
+    }
+    a.books = S.d_books;
+    a.part = (float *)S.d_tmp;
+    CK((cudaError_t)wc_matvec_sel_launch(&a, copies, stream ? stream : (void *)S.stream),
+       "matvec_sel");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;

@@ -169,10 +169,22 @@ typedef struct {
     float *y[WC_MAX_G];
     const float *books;
     float *part;              /* [G][ns][M] workspace                         */
+    const uint32_t *sel[WC_MAX_G];   /* copy-select streams (matvec_sel.cu)   */
 } wc_matvec_args;
 
 size_t wc_matvec_part_floats(int G, int M, int N);
 int    wc_matvec_launch(const wc_matvec_args *a, void *stream);
+/* The reduce step alone: y[g][r] = f16(scale) * sum of the ns partials. */
+int    wc_matvec_reduce_launch(const wc_matvec_args *a, int ns, void *stream);
+
+/* The matvec with interleaved table copies (matvec_sel.cu): copies 2 or 4,
+ * stages 3, rows 2049..8192 (one lane of quarter blocks per tile). The
+ * copy-select stream of a matrix has wc_sel_words(M, N, copies) 32-bit
+ * words and is written once by wc_sel_build_launch from its index stream. */
+size_t wc_sel_words(int M, int N, int copies);
+int    wc_sel_build_launch(const uint8_t *idx, uint32_t *sel, int M, int N, int stages,
+                           int copies, void *stream);
+int    wc_matvec_sel_launch(const wc_matvec_args *a, int copies, void *stream);
 
 /* Fixed partial-sum scratch of the allocation-free matvec: a module-scope
  * device array of WC_NOALLOC_PART_FLOATS floats (32 MiB). wc_noalloc_part
