@@ -610,6 +610,44 @@ def run_warp(args):
             matvec.update(GBps=sel_res[best]["GBps"], frac=sel_res[best]["frac"],
                           ms_per_launch=sel_res[best]["ms_per_launch"],
                           kernel=f"{best} interleaved table copies (copy-select stream)")
+        # the same shape in the VQ4P format (four 64-entry stages, 6-bit indices
+        # packed four to three bytes: the same index bytes), bit-exact to the
+        # reference; a separate line, since it is another container format
+        del d_idx
+        raw4 = synth.codebooks(rng, 4, entries=synth.ENTRIES_VQ4P)
+        wb.codebooks_load_f16(raw4)
+        mats4 = [synth.random_matrix(rng, M, N, stages=4) for _ in range(G)]
+        d_idx4 = torch.from_numpy(np.stack([m[0] for m in mats4])).to(dev)
+        d_sc4 = torch.from_numpy(np.stack([m[1].view(np.int16) for m in mats4])).to(dev)
+        p4 = ([d_idx4[g].data_ptr() for g in range(G)], [d_sc4[g].data_ptr() for g in range(G)],
+              ptrs[2], ptrs[3])
+        pcall = lambda: wb.vq4p_matvec_dev(*p4, M, N, 0, s.cuda_stream)
+        for _ in range(3):
+            pcall()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(int(2e8))
+            m0.record(s)
+            for _ in range(mv_iters):
+                pcall()
+            m1.record(s)
+        torch.cuda.synchronize()
+        p_ms = m0.elapsed_time(m1) / mv_iters
+        p_bytes = G * (synth.index_bytes(M, N, 4) + 2 * M + 4 * N + 4 * M) + 4 * 64 * 8 * 4
+        exact = None
+        if not args.no_parity:       # matrix 0 against the oracle, outside the timing
+            import oracle as O
+            y4 = d_y[0].cpu().numpy()
+            y4o = O.vq4p_matvec(mats4[0][0], mats4[0][1],
+                                synth.activations(SEED + 8, N, T=G)[0], M, N,
+                                synth.flush_f16(raw4), 0, fma=1)
+            exact = bool(np.array_equal(y4.view(np.uint32), y4o.view(np.uint32)))
+        matvec["vq4p"] = {"workload": "vq4p_matvec_4096x4096_x32", "ms_per_launch": p_ms,
+                          "GBps": p_bytes / (p_ms / 1e3) / 1e9,
+                          "frac": p_bytes / (p_ms / 1e3) / 1e9 / peak,
+                          "bytes_per_launch": p_bytes, "launches_per_call": 2,
+                          "bit_exact_vs_oracle": exact}
+        del d_idx4, d_sc4
 
     # ---- config 3: prefill, 512 tokens with Zipf(1.1) routes, one layer (layer
     # 1's bank), on the tensor cores; the lookup path (8 host-slot chunks of 64

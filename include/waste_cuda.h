@@ -21,6 +21,8 @@
  *                                (slot lutb_range, src/waste_backend.h:82)
  *   waste_cuda_vq_matvec(_dev)   src/model.c:2282-2289 vq_matvec
  *   waste_cuda_vq_dequant        tools/verify_container.py:73-84 (dequantised W)
+ *   waste_cuda_vq4p_*            src/model.c:2026-2229 vq_quant_range / vq_rows_p6
+ *                                (the WQ_VQ4P format, src/waste_format.h:57)
  *   waste_cuda_moe_experts       src/model.c:2873-2911 moe_layer's expert loop
  *   waste_cuda_moe_chunk_experts src/model.c:3585-3659 moe_chunk's expert loop
  *   waste_cuda_moe_layer(_dev)   src/model.c:2713-2939 moe_layer (router,
@@ -104,7 +106,8 @@ const char *waste_cuda_backend_name(void);
  * load (m->codebooks, src/model.c:1275-1288 — subnormals already flushed).
  * The _f16 form takes the raw codebooks.bin entries and decodes them the
  * way the engine's loader does (src/model.c:1278-1287: f16 -> f32 with
- * subnormals flushed to signed zero). Only entries == 256, vec_dim == 8. */
+ * subnormals flushed to signed zero). entries 256 (VQ3R, VQ2R) or 64
+ * (VQ4P); vec_dim 8. */
 int waste_cuda_codebooks_load(const float *books, int n_books, int entries,
                               int vec_dim);
 int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries,
@@ -117,9 +120,11 @@ int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries,
  * record_check does (magic, identity, size, fmt, lowrank, codebook range,
  * offset order, room for the scales) before anything is copied. The first
  * call for a layer sizes its bank for n_experts records; the shapes are
- * gate/up [inter][lat] and down [lat][inter]. A caller that shards the
- * experts loads only the records it owns (first/count); the others stay
- * absent and a call that names one fails with WASTE_CUDA_E_ARG. */
+ * gate/up [inter][lat] and down [lat][inter]. stages 2 or 3: VQ2R/VQ3R
+ * records (256-entry codebooks); stages 4: VQ4P records (64-entry
+ * codebooks, see below). A caller that shards the experts loads only the
+ * records it owns (first/count); the others stay absent and a call that
+ * names one fails with WASTE_CUDA_E_ARG. */
 int  waste_cuda_vq_bank_load(int layer, int n_experts, size_t rec_bytes,
                              int first, int count, const void *records,
                              int inter, int lat, int stages);
@@ -359,6 +364,34 @@ int waste_cuda_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
                          const float *x, int M, int N, int cb_base, int stages);
 int waste_cuda_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale,
                           int M, int N, int cb_base, int stages);
+
+/* ---- VQ4P ----------------------------------------------------------------
+ * The engine's other 3-bit expert format (WQ_VQ4P, src/waste_format.h:57):
+ * four residual stages of 64-entry codebooks, the four 6-bit indices of a
+ * row and position packed little-endian into three bytes
+ * (tools/convert.py:315-337), in the same blocked layout [M/64][N/8][64][3].
+ * The fp32 table is quantised to int8 with one scale per 32 positions and
+ * the sums stay integers until a per-block fold (src/model.c:2026-2229
+ * vq_quant_range / vq_rows_p6), so results are bit-identical to the CPU's.
+ * Needs codebooks loaded with entries = 64. A bank loaded with stages = 4
+ * holds VQ4P records (fmt 8); moe_experts and moe_chunk_experts run it, and
+ * the device-routed layer, block, prefill and expert-parallel entry points
+ * (VQ3R only) return WASTE_CUDA_E_ARG for it. Its gated activation uses
+ * correctly rounded exp and tanh (libm's float versions miss the correct
+ * rounding on a few inputs, which the int8 re-quantisation of the down
+ * table can turn into a whole table step).
+ * vq4p_matvec(_dev): y = VQ4P(idx, scale) . x, any M, N a multiple of 8;
+ * the _dev form runs G (1..120) matrices of one shape, idx[g] 8-byte
+ * aligned. vq4p_table: the int8 tables q[N/8][4][64] and scales
+ * qs[ceil(N/256)] of x against books cb_base..cb_base+3 (vq_build_lut then
+ * vq_quant_lut). */
+int waste_cuda_vq4p_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
+                           const float *x, int M, int N, int cb_base);
+int waste_cuda_vq4p_matvec_dev(int G, const uint8_t *const *idx,
+                               const uint16_t *const *scale,
+                               const float *const *x, float *const *y, int M,
+                               int N, int cb_base, void *stream);
+int waste_cuda_vq4p_table(int8_t *q, float *qs, const float *x, int N, int cb_base);
 
 /* Batched independent matvecs on device pointers: for g < G (1..120),
  * y[g][M] = VQ(idx[g], scale[g]) . x[g][N]. idx/scale/x/y are arrays of G

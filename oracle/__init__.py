@@ -60,7 +60,7 @@ class OrcMoe(C.Structure):
                 ("shared_inter", C.c_int), ("sh_gate", P), ("sh_up", P), ("sh_down", P),
                 ("sh_gate_s", P), ("sh_up_s", P), ("sh_down_s", P), ("sh_bits", C.c_int),
                 ("sh_group", C.c_int), ("act_situ", C.c_int), ("situ_beta", C.c_float),
-                ("situ_lbeta", C.c_float)]
+                ("situ_lbeta", C.c_float), ("index_bits", C.c_int)]
 
 
 _orc = None
@@ -87,6 +87,11 @@ def lib() -> C.CDLL:
                                     C.c_int, P, C.c_int]
         L.orc_dequant.argtypes = [P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                   C.c_int, C.c_int]
+        L.orc_vq4p_quant.argtypes = [P, C.c_int, P, P]
+        L.orc_vq4p_rows.argtypes = [P, P, P, P, P, C.c_int, C.c_int]
+        L.orc_vq4p_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P, P,
+                                      C.c_int]
+        L.orc_set_exact_math.argtypes = [C.c_int]
         L.orc_dotf.restype = C.c_float
         L.orc_dotf.argtypes = [P, P, C.c_int]
         L.orc_route.argtypes = [P, P, C.c_int, C.c_int, C.c_int, C.c_float, P, P]
@@ -158,7 +163,9 @@ def _bind_refh(R: C.CDLL) -> C.CDLL:
     R.refh_moe_open.restype = P
     R.refh_moe_open.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_float, P, P, P, C.c_int, C.c_int, P, C.c_size_t,
-                                C.c_int, P, P, P, P, P, P, C.c_int]
+                                C.c_int, P, P, P, P, P, P, C.c_int, C.c_int]
+    R.refh_vq4p_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, C.c_int]
+    R.refh_vq4p_table.argtypes = [P, P, P, C.c_int, P, C.c_int, C.c_int]
     R.refh_moe_layer.restype = C.c_int
     R.refh_moe_layer.argtypes = [P, P, P, P]
     R.refh_moe_chunk.restype = C.c_int
@@ -206,6 +213,67 @@ def vq_matvec(idx, scale, x, M, N, books, cb_base, stages=3, fma=1):
     return y
 
 
+def vq4p_matvec(idx, scale, x, M, N, books, cb_base, fma=1):
+    """A VQ4P matrix (books [n][64][8], flushed) times x."""
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    nv = N // 8
+    y = np.empty(M, dtype=np.float32)
+    lut = np.empty(nv * 256, dtype=np.float32)
+    q = np.empty(nv * 256, dtype=np.int8)
+    qs = np.empty(nv // 32 + 2, dtype=np.float32)
+    lib().orc_vq4p_matvec(_p(y), _p(i), _p(s), _p(xx), M, N, _p(b), cb_base, _p(lut), _p(q),
+                          _p(qs), fma)
+    return y
+
+
+def lut_build_en(books, cb_base, x, stages, entries, fma=1):
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    nv = xx.size // 8
+    lut = np.empty((nv, stages, entries), dtype=np.float32)
+    lib().orc_lut_build(_p(lut), _p(b), cb_base, _p(xx), nv, stages, entries, 8, fma)
+    return lut
+
+
+def vq4p_table(books, cb_base, x, fma=1):
+    """The int8 VQ4P tables of x: q [N/8][4][64], qs [ceil(N/256)]."""
+    nv = np.size(x) // 8
+    lut = lut_build_en(books, cb_base, x, 4, 64, fma)
+    q = np.empty((nv, 4, 64), dtype=np.int8)
+    qs = np.empty((nv + 31) // 32, dtype=np.float32)
+    lib().orc_vq4p_quant(_p(lut), nv, _p(q), _p(qs))
+    return q, qs
+
+
+def ref_vq4p_matvec(idx, scale, x, M, N, books, cb_base):
+    """The compiled reference's vq_matvec on a VQ4P matrix (LUT backend:
+    the best this host has), through the harness."""
+    R = ref()
+    R.refh_set_backend(R.refh_best_backend())
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    y = np.empty(M, dtype=np.float32)
+    R.refh_vq4p_matvec(_p(y), _p(i), _p(s), _p(xx), M, N, _p(b), b.shape[0], cb_base)
+    return y
+
+
+def ref_vq4p_table(books, cb_base, x):
+    R = ref()
+    R.refh_set_backend(R.refh_best_backend())
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    b = np.ascontiguousarray(books, dtype=np.float32)
+    nv = xx.size // 8
+    q = np.empty((nv, 4, 64), dtype=np.int8)
+    qs = np.empty(nv // 32 + 2, dtype=np.float32)
+    R.refh_vq4p_table(_p(q), _p(qs), _p(xx), xx.size, _p(b), b.shape[0], cb_base)
+    return q, qs[: (nv + 31) // 32]
+
+
 def dequant(idx, scale, M, N, books, cb_base, stages=3):
     i = np.ascontiguousarray(idx, dtype=np.uint8)
     s = np.ascontiguousarray(scale, dtype=np.uint16)
@@ -231,7 +299,9 @@ def _moe_struct(L, keep):
     s = OrcMoe()
     s.hidden, s.inter, s.n_experts, s.top_k = L.hidden, L.inter, L.n_experts, L.top_k
     s.renorm, s.routed_scale = L.renorm, L.routed_scale
-    s.stages, s.entries, s.vec_dim, s.index_block = L.stages, 256, 8, 64
+    p6 = L.stages == 4               # VQ4P: four stages of 64, packed indices
+    s.stages, s.entries, s.vec_dim, s.index_block = L.stages, 64 if p6 else 256, 8, 64
+    s.index_bits = 6 if p6 else 8
     s.router, s.books, s.n_books = _p(router), _p(books), books.shape[0]
     if L.bias is not None:
         b = np.ascontiguousarray(L.bias, dtype=np.float32)
@@ -405,7 +475,8 @@ class RefMoe:
         self.h = R.refh_moe_open(L.layer, L.hidden, L.inter, L.n_experts, L.top_k, L.renorm,
                                  C.c_float(L.routed_scale), _p(self.keep[0]), _p(bias),
                                  _p(self.keep[1]), self.keep[1].shape[0], L.cb_base,
-                                 _p(L.bank), L.rec_bytes, L.shared_inter, *sh, max_tokens)
+                                 _p(L.bank), L.rec_bytes, L.shared_inter, *sh, max_tokens,
+                                 6 if L.stages == 4 else 8)
         if not self.h:
             raise RuntimeError("reference harness refused the layer "
                                "(the shared width must be a multiple of inter)")
@@ -437,3 +508,17 @@ class RefMoe:
         if self.h:
             self.R.refh_moe_close(self.h)
             self.h = None
+
+
+class exact_math:
+    """Within this context the restatement's activation (and KDA) exp/tanh
+    are correctly rounded (the device's arithmetic where it rounds them
+    correctly) rather than libm's: `with O.exact_math(): ...`."""
+
+    def __enter__(self):
+        lib().orc_set_exact_math(1)
+        return self
+
+    def __exit__(self, *exc):
+        lib().orc_set_exact_math(0)
+        return False

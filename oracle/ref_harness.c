@@ -137,6 +137,36 @@ void refh_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
     free(m->codebooks); free(m->codebooksT); free(m);
 }
 
+/* src/model.c:2282 vq_matvec on a VQ4P matrix (index_bits 6: four stages of
+ * 64 entries, packed indices): books [n_books][64][8]. */
+void refh_vq4p_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
+                      const float *x, int M, int N, const float *books,
+                      int n_books, int cb_base)
+{
+    waste_model *m = mk_model(books, n_books, 4, 64, 8);
+    m->index_bits = 6;
+    const int nv = N / 8;
+    float *lut = (float *)malloc((size_t)nv * 4 * 64 * sizeof(float));
+    int8_t *q = (int8_t *)malloc((size_t)nv * 4 * 64);
+    float *qs = (float *)malloc((size_t)(nv / WASTE_VQ_LUT_BLK + 2) * sizeof(float));
+    vq_matvec(m, y, idx, scale, x, M, N, cb_base, lut, q, qs);
+    free(lut); free(q); free(qs);
+    free(m->codebooks); free(m->codebooksT); free(m);
+}
+
+/* src/model.c:1911-1923 vq_build_lut with the int8 shadow (vq_quant_lut):
+ * q [N/8][4][64], qs [ceil(N/256)]. */
+void refh_vq4p_table(int8_t *q, float *qs, const float *x, int N, const float *books,
+                     int n_books, int cb_base)
+{
+    waste_model *m = mk_model(books, n_books, 4, 64, 8);
+    m->index_bits = 6;
+    float *lut = (float *)malloc((size_t)(N / 8) * 4 * 64 * sizeof(float));
+    vq_build_lut(m, lut, cb_base, x, N, 4, 64, 8, q, qs);
+    free(lut);
+    free(m->codebooks); free(m->codebooksT); free(m);
+}
+
 /* A reusable handle for repeated matvec timing: same as refh_vq_matvec but
  * with the model and table allocated once. */
 typedef struct { waste_model *m; float *lut; int N; } refh_mv;
@@ -189,10 +219,13 @@ void *refh_moe_open(int layer, int hidden, int inter, int n_experts, int top_k,
                     int cb_base, const void *bank, size_t rec_bytes,
                     int sh_inter, const int8_t *shg, const uint16_t *shg_s,
                     const int8_t *shu, const uint16_t *shu_s,
-                    const int8_t *shd, const uint16_t *shd_s, int max_tokens)
+                    const int8_t *shd, const uint16_t *shd_s, int max_tokens,
+                    int index_bits)
 {
-    const int st = 3, en = 256, vd = 8, g = 128;
+    /* index_bits 6: a VQ4P bank (four stages of 64-entry books) */
+    const int st = index_bits == 6 ? 4 : 3, en = index_bits == 6 ? 64 : 256, vd = 8, g = 128;
     waste_model *m = mk_model(books, n_books, st, en, vd);
+    m->index_bits = index_bits == 6 ? 6 : 8;
     waste_config *c = &m->cfg;
     c->n_layers = layer + 1;
     c->hidden = hidden;
@@ -278,6 +311,14 @@ void *refh_moe_open(int layer, int hidden, int inter, int n_experts, int top_k,
     m->cused = (int *)calloc((size_t)T * 64 + n_experts, sizeof(int));
     m->cq = (float *)malloc((size_t)(2 * T + 1) * lut_sz * sizeof(float));
     m->cff = (float *)calloc((size_t)2 * inter + hidden, sizeof(float));
+    if (m->index_bits == 6) {
+        /* the int8 shadows of m->lut and m->cq, region for region */
+        const size_t nsc = (size_t)(nmax / vd + 1) / WASTE_VQ_LUT_BLK + 2;
+        m->lut8 = (int8_t *)malloc(3 * lut_sz);
+        m->lut8_scale = (float *)malloc(3 * nsc * sizeof(float));
+        m->cq8 = (int8_t *)malloc((size_t)(2 * T + 1) * lut_sz);
+        m->cq8_scale = (float *)malloc((size_t)(2 * T + 1) * nsc * sizeof(float));
+    }
     m->clat = (float *)calloc((size_t)2 * T * hidden, sizeof(float));
     m->ckv = (float *)calloc((size_t)T * (2 * si + hidden), sizeof(float));
     m->chunk_cap = T;
@@ -356,6 +397,7 @@ void refh_moe_close(void *p)
     free(m->h); free(m->ares); free(m->lut); free(m->croute); free(m->crw);
     free(m->cused); free(m->cq); free(m->cff); free(m->clat); free(m->ckv);
     free(m->codebooks); free(m->codebooksT);
+    free(m->lut8); free(m->lut8_scale); free(m->cq8); free(m->cq8_scale);
     pthread_mutex_destroy(&m->fetch_mu);
     free(m); free(h);
 }

@@ -35,6 +35,8 @@ typedef struct {
 #define ORC_MAGIC_EXPERT 0x50584557u /* src/waste_format.h:33 */
 #define ORC_WQ_VQ3R 4                /* src/waste_format.h:51 */
 #define ORC_WQ_VQ2R 5                /* src/waste_format.h:52 */
+#define ORC_WQ_VQ4P 8                /* src/waste_format.h:57 */
+#define ORC_LUT_BLK 32               /* WASTE_VQ_LUT_BLK, src/model.h:60 */
 #define ORC_ALIGN 4096u              /* src/waste_format.h:42 */
 
 /* src/model.c:1278-1287: sign kept, exponent 0 (zero or subnormal) -> 0.
@@ -120,6 +122,73 @@ void orc_vq_matvec(float *y, const uint8_t *idx, const uint16_t *scale,
     orc_vq_rows(y, idx, scale, lut, M, N / vd, stages, entries);
 }
 
+/* src/model.c:2049-2114 vq_quant_range, the portable loop: per block of 32
+ * positions (4 stages x 64 entries each), mx = max |lut| by a strict >
+ * scan, scale mx / 127, and q = clamp(lrintf(lut * (127 / mx)), -127, 127)
+ * (inv = 0 when mx is 0). */
+void orc_vq4p_quant(const float *lut, int nv, int8_t *q, float *qs)
+{
+    const int per = 4 * 64;
+    for (int blk = 0; blk * ORC_LUT_BLK < nv; blk++) {
+        const int v0 = blk * ORC_LUT_BLK;
+        const int v1 = v0 + ORC_LUT_BLK < nv ? v0 + ORC_LUT_BLK : nv;
+        const size_t n = (size_t)(v1 - v0) * per;
+        const float *src = lut + (size_t)v0 * per;
+        float mx = 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            const float f = fabsf(src[i]);
+            if (f > mx) mx = f;
+        }
+        qs[blk] = mx / 127.0f;
+        const float inv = mx > 0 ? 127.0f / mx : 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            int t = (int)lrintf(src[i] * inv);
+            if (t > 127) t = 127;
+            else if (t < -127) t = -127;
+            q[(size_t)v0 * per + i] = (int8_t)t;
+        }
+    }
+}
+
+/* src/model.c:2129-2229 vq_rows_p6, the portable loop: per row and block of
+ * 32 positions an int16 sum of the four stages' table bytes (indices
+ * unpacked from three little-endian bytes, 6 bits each), folded into
+ * acc += scale_blk * (float)sum; y = acc * f16(row scale). */
+void orc_vq4p_rows(float *y, const uint8_t *idx, const uint16_t *scale, const int8_t *q,
+                   const float *qs, int M, int nv)
+{
+    const int B = 64, en = 64;
+    for (int r = 0; r < M; r++) {
+        const int rb = r / B, ri = r % B;
+        float acc = 0.0f;
+        for (int v0 = 0; v0 < nv; v0 += ORC_LUT_BLK) {
+            const int v1 = v0 + ORC_LUT_BLK < nv ? v0 + ORC_LUT_BLK : nv;
+            int16_t sum = 0;
+            for (int v = v0; v < v1; v++) {
+                const int8_t *T = q + (size_t)v * 4 * en;
+                const uint8_t *ix = idx + (((size_t)rb * nv + v) * B + ri) * 3;
+                const unsigned b0 = ix[0], b1 = ix[1], b2 = ix[2];
+                const unsigned j0 = b0 & 0x3f, j1 = ((b0 >> 6) | (b1 << 2)) & 0x3f;
+                const unsigned j2 = ((b1 >> 4) | (b2 << 4)) & 0x3f, j3 = (b2 >> 2) & 0x3f;
+                sum = (int16_t)(sum + T[j0] + T[en + j1] + T[2 * en + j2] + T[3 * en + j3]);
+            }
+            acc += qs[v0 / ORC_LUT_BLK] * (float)sum;
+        }
+        y[r] = acc * orc_f16(scale[r]);
+    }
+}
+
+/* src/model.c:2282-2289 vq_matvec for a VQ4P matrix: the fp32 table (books
+ * [n][64][8]), its int8 quantisation, then the packed-index gather. */
+void orc_vq4p_matvec(float *y, const uint8_t *idx, const uint16_t *scale, const float *x,
+                     int M, int N, const float *books, int cb_base, float *lut, int8_t *q,
+                     float *qs, int fma)
+{
+    orc_lut_build(lut, books, cb_base, x, N / 8, 4, 64, 8, fma);
+    orc_vq4p_quant(lut, N / 8, q, qs);
+    orc_vq4p_rows(y, idx, scale, q, qs, M, N / 8);
+}
+
 /* tools/verify_container.py:73-84 (un-block, recon = sum_s C_s[idx_s] from a
  * zero vector, times the row scale), with the codebooks decoded the way the
  * engine decodes them (flushed, src/model.c:1278-1287). W is [M][N]. */
@@ -150,15 +219,26 @@ float orc_dotf(const float *a, const float *b, int n)
     return acc;
 }
 
+/* exp and tanh of the activations (and of KDA): libm's expf / tanhf (what
+ * the reference calls), or — with orc_set_exact_math(1) — the correctly
+ * rounded values, computed in double and rounded once. The second mode is
+ * the device's arithmetic where its exp and tanh are correctly rounded, so
+ * the two differ only where libm's float functions are not. The router's
+ * sigmoid always uses expf. */
+static int orc_exact_math;
+void orc_set_exact_math(int on) { orc_exact_math = on; }
+static float orc_expf(float x) { return orc_exact_math ? (float)exp((double)x) : expf(x); }
+static float orc_tanhf(float x) { return orc_exact_math ? (float)tanh((double)x) : tanhf(x); }
+
 static float orc_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
-static float orc_silu(float v) { return v / (1.0f + expf(-v)); } /* src/model.c:501 */
+static float orc_silu(float v) { return v / (1.0f + orc_expf(-v)); } /* src/model.c:501 */
 
 /* src/model.c:505-509 waste_situ_pair (K3's SiTU): beta*tanh(g/beta)*sigmoid(g),
  * times lbeta*tanh(u/lbeta) (or u when lbeta <= 0). */
 float orc_situ_pair(float g, float u, float beta, float lbeta)
 {
-    const float a = beta * tanhf(g / beta) / (1.0f + expf(-g));
-    return a * (lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u);
+    const float a = beta * orc_tanhf(g / beta) / (1.0f + orc_expf(-g));
+    return a * (lbeta > 0.0f ? lbeta * orc_tanhf(u / lbeta) : u);
 }
 
 /* The layer's gated activation: SiLU(g)*u, or SiTU when the model sets
@@ -275,7 +355,9 @@ int orc_record_check(const orc_moe *L, int layer, int expert)
     if (rb < sizeof *h || h->magic != ORC_MAGIC_EXPERT) return -1;
     if (h->layer != (uint16_t)layer || h->expert_id != (uint16_t)expert) return -1;
     if ((size_t)h->rec_4k_blocks * ORC_ALIGN != rb) return -1;
-    if (h->fmt != ORC_WQ_VQ3R && h->fmt != ORC_WQ_VQ2R) return -1;
+    if (L->index_bits == 6 ? h->fmt != ORC_WQ_VQ4P
+                           : (h->fmt != ORC_WQ_VQ3R && h->fmt != ORC_WQ_VQ2R))
+        return -1;
     if (h->lowrank_id != 0) return -1;
     if ((long)h->codebook_id + 3L * L->stages > L->n_books) return -1;
     if (!(h->gate_off == sizeof *h && h->gate_off < h->up_off &&
@@ -285,6 +367,24 @@ int orc_record_check(const orc_moe *L, int layer, int expert)
     const size_t scales = 2u * (size_t)(2 * L->inter + L->hidden);
     if (scales > rb - h->chan_corr_off) return -1;
     return 0;
+}
+
+/* src/model.c:2264-2280 vq_apply in the layer's format. For VQ4P the table
+ * is quantised here; the engine quantises once when it builds the table
+ * (vq_build_lut), which gives the same bytes. */
+static void orc_apply(const orc_moe *L, float *y, const uint8_t *idx, const uint16_t *sc,
+                      const float *lut, int M, int nv)
+{
+    if (L->index_bits == 6) {
+        int8_t *q = (int8_t *)malloc((size_t)nv * 4 * 64);
+        float *qs = (float *)malloc((size_t)(nv / ORC_LUT_BLK + 2) * sizeof(float));
+        orc_vq4p_quant(lut, nv, q, qs);
+        orc_vq4p_rows(y, idx, sc, q, qs, M, nv);
+        free(q);
+        free(qs);
+    } else {
+        orc_vq_rows(y, idx, sc, lut, M, nv, L->stages, L->entries);
+    }
 }
 
 /* The serial expert loop of src/model.c:2873-2911: gate/up tables built
@@ -315,11 +415,12 @@ int orc_moe_experts(const orc_moe *L, const int *idx, const float *w, int K,
                           st, en, vd, fma);
             lut_ready = 1;
         }
-        orc_vq_rows(ga, rec + h->gate_off, sc, lut_g, inter, lat / vd, st, en);
-        orc_vq_rows(ub, rec + h->up_off, sc + inter, lut_u, inter, lat / vd, st, en);
+        orc_apply(L, ga, rec + h->gate_off, sc, lut_g, inter, lat / vd);
+        orc_apply(L, ub, rec + h->up_off, sc + inter, lut_u, inter, lat / vd);
         for (int i = 0; i < inter; i++) ga[i] = orc_act(L, ga[i], ub[i]);
-        orc_vq_matvec(acc, rec + h->down_off, sc + 2 * inter, ga, lat, inter,
-                      L->books, h->codebook_id + 2 * st, st, en, vd, lut_d, fma);
+        orc_lut_build(lut_d, L->books, h->codebook_id + 2 * st, ga, inter / vd, st, en, vd,
+                      fma);
+        orc_apply(L, acc, rec + h->down_off, sc + 2 * inter, lut_d, lat, inter / vd);
         const float wj = w[j];
         for (int i = 0; i < lat; i++) ysum[i] += wj * acc[i];
     }
@@ -418,13 +519,14 @@ int orc_moe_chunk(const orc_moe *L, int layer, const float *x, int nT,
             for (int j = 0; j < K; j++)
                 if (route[(size_t)t * K + j] == e) { wj = rw[(size_t)t * K + j]; break; }
             if (wj == 0.0f) continue;
-            orc_vq_rows(ga, rec + h->gate_off, s16, lut_gu + (size_t)(2 * t) * lut_sz,
-                        inter, lat / vd, st, en);
-            orc_vq_rows(ub, rec + h->up_off, s16 + inter,
-                        lut_gu + (size_t)(2 * t + 1) * lut_sz, inter, lat / vd, st, en);
+            orc_apply(L, ga, rec + h->gate_off, s16, lut_gu + (size_t)(2 * t) * lut_sz, inter,
+                      lat / vd);
+            orc_apply(L, ub, rec + h->up_off, s16 + inter,
+                      lut_gu + (size_t)(2 * t + 1) * lut_sz, inter, lat / vd);
             for (int i = 0; i < inter; i++) ga[i] = orc_act(L, ga[i], ub[i]);
-            orc_vq_matvec(acc, rec + h->down_off, s16 + 2 * inter, ga, lat, inter,
-                          L->books, h->codebook_id + 2 * st, st, en, vd, lut_d, fma);
+            orc_lut_build(lut_d, L->books, h->codebook_id + 2 * st, ga, inter / vd, st, en,
+                          vd, fma);
+            orc_apply(L, acc, rec + h->down_off, s16 + 2 * inter, lut_d, lat, inter / vd);
             float *dst = ysum + (size_t)t * lat;
             for (int i = 0; i < lat; i++) dst[i] += wj * acc[i];
         }

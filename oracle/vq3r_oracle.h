@@ -18,6 +18,9 @@
  *                      the portable src/model.c:1862-1901 (mul then add)
  *   orc_vq_rows        src/model.c:1956-2024   blocked-index gather, t=(L0+L1)+L2
  *   orc_vq_matvec      src/model.c:2282-2289   lut build + gather
+ *   orc_vq4p_quant     src/model.c:2049-2114   VQ4P: int8 table, one scale per 32 positions
+ *   orc_vq4p_rows      src/model.c:2129-2229   VQ4P: 6-bit unpack, int16 block sums, fp32 fold
+ *   orc_vq4p_matvec    src/model.c:2282-2289   VQ4P table + quantise + gather
  *   orc_dequant        tools/verify_container.py:51-88 with the loader's flush
  *   orc_dotf           src/model.c:155-160     x86 dot product (serial)
  *   orc_route          src/model.c:2720-2747   sigmoid + bias, iterative argmax,
@@ -65,6 +68,14 @@ void orc_dequant(float *W, const uint8_t *idx, const uint16_t *scale, int M,
                  int entries, int vec_dim, int index_block);
 
 float orc_dotf(const float *a, const float *b, int n);
+/* VQ4P: lut [nv][4][64] -> q [nv][4][64], qs [ceil(nv/32)]; rows over the
+ * packed blocked layout [M/64][nv][64][3]; books [n_books][64][8]. */
+void orc_vq4p_quant(const float *lut, int nv, int8_t *q, float *qs);
+void orc_vq4p_rows(float *y, const uint8_t *idx, const uint16_t *scale, const int8_t *q,
+                   const float *qs, int M, int nv);
+void orc_vq4p_matvec(float *y, const uint8_t *idx, const uint16_t *scale, const float *x,
+                     int M, int N, const float *books, int cb_base, float *lut, int8_t *q,
+                     float *qs, int fma);
 
 /* logits: [E]; writes idx[K], w[K]. bias may be NULL. */
 void orc_route(const float *logits, const float *bias, int E, int K, int renorm,
@@ -93,9 +104,13 @@ typedef struct {
     int sh_bits, sh_group;
     int act_situ;               /* 0: SiLU(g)*u; 1: SiTU (K3)               */
     float situ_beta, situ_lbeta;
+    int index_bits;             /* 8: VQ3R/VQ2R; 6: VQ4P (4 stages of 64)    */
 } orc_moe;
 
 float orc_situ_pair(float g, float u, float beta, float lbeta);
+/* 1: the activations' (and KDA's) exp/tanh correctly rounded (the device's
+ * arithmetic) instead of libm's expf/tanhf (the reference's); 0 (default). */
+void orc_set_exact_math(int on);
 
 /* Returns 0, or -1 when a record header does not describe the record. */
 int orc_record_check(const orc_moe *L, int layer, int expert);

@@ -15,6 +15,8 @@ Every output here is produced by the reference's own code:
   tree, seed 0), and its codebooks.bin is then replaced.
 * lut_*.npz, matvec_*.npz — vq_build_lut / vq_matvec (src/model.c:1911,
   2282) through the reference's AVX-512 slot and its portable (CPU) slot.
+* vq4p.npz, moe_vq4p*.npz — the VQ4P format (src/model.c:2026-2229): the
+  matvec, its int8 tables, and VQ4P MoE layers.
 * moe_*.npz — moe_layer / moe_chunk (src/model.c:2713, 3512) on seeded
   layers built by warp_b200.synth; the inputs are regenerated from the seed
   (numpy PCG64, which is stable across numpy versions) and pinned by a
@@ -48,7 +50,8 @@ if REF_TREE is None:
     raise SystemExit("make_golden.py needs the reference tree: set WARP_REFERENCE")
 
 sys.path.insert(0, os.path.join(ROOT, "tests"))
-from golden_cases import MOE_CASES, MVQ_CASES, NORM_SIZES  # noqa: E402  (shared with the tests)
+from golden_cases import (MOE_CASES, MVQ_CASES, NORM_SIZES, VQ4P_CASES,  # noqa: E402
+                          VQ4P_MOE_CASES, sha, vq4p_books, vq4p_case)  # shared with the tests
 
 
 def layer_sha(L) -> str:
@@ -124,8 +127,8 @@ def lut_matvec_fixtures(R):
         print("lut/matvec fixtures for", name)
 
 
-def moe_fixtures(only=None):
-    for name, (seed, kw, xseed, T) in MOE_CASES.items():
+def moe_fixtures(only=None, cases=MOE_CASES):
+    for name, (seed, kw, xseed, T) in cases.items():
         if only and name not in only:
             continue
         L = synth.moe_layer(seed, **kw)
@@ -144,6 +147,27 @@ def moe_fixtures(only=None):
             rm.close()
         np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **res)
         print(name, "written")
+
+
+def vq4p_fixtures():
+    """VQ4P (src/model.c:2026-2229): vq_matvec and vq_build_lut's int8
+    shadow through the reference with its best LUT backend (AVX-512 here),
+    on seeded packed matrices (regenerated by golden_cases.vq4p_case and
+    pinned by a sha256); then moe_layer / moe_chunk on VQ4P layers."""
+    raw = vq4p_books()
+    books = synth.flush_f16(raw)
+    res = {"books_sha": sha(raw), "cb_base": np.int64(4)}
+    for name in VQ4P_CASES:
+        idx, sc, x, M, N = vq4p_case(name)
+        res[f"{name}_sha"] = sha(idx, sc, x)
+        res[f"{name}_y"] = O.ref_vq4p_matvec(idx, sc, x, M, N, books, 4)
+        q, qs = O.ref_vq4p_table(books, 4, x)
+        res[f"{name}_q"], res[f"{name}_qs"] = q, qs
+    R = O.ref()
+    res["backend"] = R.refh_set_backend(R.refh_best_backend())
+    np.savez_compressed(os.path.join(OUT, "vq4p.npz"), **res)
+    print("vq4p.npz written")
+    moe_fixtures(cases=VQ4P_MOE_CASES)
 
 
 def tiny_container():
@@ -197,6 +221,7 @@ def main():
     norm_fixture()
     tiny_container()
     mvq_fixture()
+    vq4p_fixtures()
 
 
 if __name__ == "__main__":
@@ -208,5 +233,7 @@ if __name__ == "__main__":
         tiny_container()
     elif sys.argv[1:] == ["mvq"]:
         mvq_fixture()
+    elif sys.argv[1:] == ["vq4p"]:
+        vq4p_fixtures()
     else:
         main()

@@ -19,6 +19,49 @@ MOE_CASES = {
 
 MATVEC_CASES = ("matvec_ragged", "matvec_square", "matvec_vq2r")
 
+# VQ4P (four stages of 64-entry books, 6-bit indices packed four to three
+# bytes): matvec fixtures in vq4p.npz, name -> (M, N). Books 4..7 of 12;
+# x is zero on positions [32, 64) where N allows, so one table block has
+# scale 0.
+VQ4P_CASES = {"p6_square": (256, 2304), "p6_ragged": (70, 1000), "p6_down": (2304, 1024),
+              "p6_small": (64, 256)}
+
+# VQ4P MoE layers (moe_vq4p*.npz), in the form of MOE_CASES
+VQ4P_MOE_CASES = {
+    "moe_vq4p": (31, dict(hidden=256, inter=128, n_experts=16, top_k=4, shared_inter=128,
+                          with_bias=True, routed_scale=2.0, stages=4), 33, 16),
+    "moe_vq4p_situ": (37, dict(hidden=256, inter=128, n_experts=16, top_k=4, shared_inter=128,
+                               with_bias=True, routed_scale=2.827, act_situ=1, stages=4), 39, 16),
+}
+
+
+def vq4p_books():
+    """The raw f16 books of the VQ4P matvec fixtures: 12 books of 64."""
+    from warp_b200 import synth
+    return synth.codebooks(np.random.default_rng(4040), 12, entries=synth.ENTRIES_VQ4P)
+
+
+def vq4p_case(name):
+    """(idx, scale, x, M, N) of a VQ4P matvec fixture, regenerated from its
+    seed (the fixture pins them by a sha256)."""
+    import zlib
+    from warp_b200 import synth
+    M, N = VQ4P_CASES[name]
+    idx, sc = synth.random_matrix(np.random.default_rng(zlib.crc32(name.encode())), M, N,
+                                  stages=4)
+    x = synth.activations(len(name) + M, N)[0]
+    if N >= 512:
+        x[256:512] = 0
+    return idx, sc, x, M, N
+
+
+def sha(*arrays) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
 # the trunk matvec fixtures (mvq.npz): name -> (rows, in, bits)
 MVQ_CASES = {
     "q8g": (96, 2304, 8), "q8g_ragged": (70, 1000, 8), "q4g": (96, 2304, 4),

@@ -36,7 +36,8 @@ EXPORTS = (
     "waste_cuda_moe_block_dev", "waste_cuda_ep_moe_block_dev", "waste_cuda_ep_moe_block_rep_dev",
     "waste_cuda_moe_activation", "waste_cuda_mvq_rows_dev", "waste_cuda_release_host_buffers",
     "waste_cuda_vq_sel_bytes", "waste_cuda_vq_sel_build_dev", "waste_cuda_vq_matvec_sel_dev",
-    "waste_cuda_vq_bank_load_file",
+    "waste_cuda_vq_bank_load_file", "waste_cuda_vq4p_matvec", "waste_cuda_vq4p_matvec_dev",
+    "waste_cuda_vq4p_table",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -151,6 +152,10 @@ def load_library() -> C.CDLL:
         "waste_cuda_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_block_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
         "waste_cuda_ep_moe_block_rep_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_vq4p_matvec": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int]),
+        "waste_cuda_vq4p_matvec_dev": (C.c_int, [C.c_int, P, P, P, P, C.c_int, C.c_int,
+                                                 C.c_int, P]),
+        "waste_cuda_vq4p_table": (C.c_int, [P, P, P, C.c_int, C.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -472,3 +477,35 @@ def vq_matvec_dev_noalloc(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, 
     _check(load_library().waste_cuda_vq_matvec_dev_noalloc(
         G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base, stages,
         C.c_void_p(stream or None)))
+
+
+def vq4p_matvec(idx, scale, x, M: int, N: int, cb_base: int) -> np.ndarray:
+    """y = VQ4P(idx, scale) . x (64-entry codebooks loaded; host buffers)."""
+    i = np.ascontiguousarray(idx, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint16)
+    xx = _f32(x)
+    y = np.empty(M, dtype=np.float32)
+    _check(load_library().waste_cuda_vq4p_matvec(_ptr(y), _ptr(i), _ptr(s), _ptr(xx), M, N,
+                                                 cb_base))
+    return y
+
+
+def vq4p_matvec_dev(idx_ptrs, scale_ptrs, x_ptrs, y_ptrs, M: int, N: int, cb_base: int,
+                    stream: int = 0):
+    """G VQ4P matvecs of one shape on device pointers."""
+    G = len(idx_ptrs)
+    arr = lambda v: (C.c_void_p * G)(*[C.c_void_p(int(p)) for p in v])
+    _check(load_library().waste_cuda_vq4p_matvec_dev(
+        G, arr(idx_ptrs), arr(scale_ptrs), arr(x_ptrs), arr(y_ptrs), M, N, cb_base,
+        C.c_void_p(stream or None)))
+
+
+def vq4p_table(x, cb_base: int):
+    """The int8 tables of x (q [N/8][4][64]) and their scales (one per 32
+    positions)."""
+    xx = _f32(x)
+    nv = xx.size // 8
+    q = np.empty((nv, 4, 64), dtype=np.int8)
+    qs = np.empty((nv + 31) // 32, dtype=np.float32)
+    _check(load_library().waste_cuda_vq4p_table(_ptr(q), _ptr(qs), _ptr(xx), xx.size, cb_base))
+    return q, qs

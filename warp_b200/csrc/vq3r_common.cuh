@@ -419,6 +419,60 @@ __device__ __forceinline__ float situ_ref(float g, float u, float beta, float lb
     return a * (lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u);
 }
 
+/* exp(x) rounded once to float, for the VQ4P expert loop (whose int8
+ * re-quantisation of the down table turns a one-ulp difference in an
+ * activation into a whole table step, about 1e-4 relative on a layer) and
+ * for KDA. Method: Cody and Waite's reduction x = k*ln2 + r with
+ * k = rint(x/ln2) (two fused multiply-adds against ln2 split into a double
+ * and its remainder), exp(r) by its Taylor series to r^13 in double
+ * (|r| <= 0.347, truncation below 1e-17), scaled by 2^k and converted to
+ * float in one rounding. The result is the correctly rounded exp(x) except
+ * within about 1e-16 relative of a rounding midpoint; glibc's expf (within
+ * 0.502 ulp) returns the same float for all but a few inputs in 10^4. */
+__host__ __device__ __forceinline__ float expf_cr(float x)
+{
+    if (x != x) return x;
+    if (x < -104.0f) return 0.0f;                        /* below half the least subnormal */
+    if (x > 89.0f) return (float)(1e300 * 1e300);        /* above FLT_MAX: +inf */
+    const double xd = (double)x;
+    const double k = rint(xd * 1.4426950408889634);
+    double r = fma(-k, 0.6931471805599453, xd);
+    r = fma(-k, 2.3190468138462996e-17, r);
+    double p = 1.0 / 6227020800.0;                       /* 1/13! */
+    p = fma(p, r, 1.0 / 479001600.0);
+    p = fma(p, r, 1.0 / 39916800.0);
+    p = fma(p, r, 1.0 / 3628800.0);
+    p = fma(p, r, 1.0 / 362880.0);
+    p = fma(p, r, 1.0 / 40320.0);
+    p = fma(p, r, 1.0 / 5040.0);
+    p = fma(p, r, 1.0 / 720.0);
+    p = fma(p, r, 1.0 / 120.0);
+    p = fma(p, r, 1.0 / 24.0);
+    p = fma(p, r, 1.0 / 6.0);
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    return (float)scalbn(p, (int)k);
+}
+
+/* tanh(x) rounded once to float: CUDA's double tanh (an error of a few
+ * double ulps) converted in one rounding, so correctly rounded except
+ * within about 1e-15 relative of a rounding midpoint. */
+__device__ __forceinline__ float tanhf_cr(float x)
+{
+    return (float)tanh((double)x);
+}
+
+/* The activations of the VQ4P loop with those functions: SiLU as
+ * src/model.c:501 (v / (1 + expf(-v)), IEEE division), SiTU as :505-509. */
+__device__ __forceinline__ float act_pair_cr(int act, float g, float u, float beta, float lbeta)
+{
+    const float sg = __fadd_rn(1.0f, expf_cr(-g));
+    if (!act) return __fmul_rn(__fdiv_rn(g, sg), u);
+    const float a = __fdiv_rn(__fmul_rn(beta, tanhf_cr(__fdiv_rn(g, beta))), sg);
+    return __fmul_rn(a, lbeta > 0.0f ? __fmul_rn(lbeta, tanhf_cr(__fdiv_rn(u, lbeta))) : u);
+}
+
 /* The gated activation of a layer: SiLU(g)*u (act 0) or SiTU (act 1). */
 __device__ __forceinline__ float act_pair(int act, float g, float u, float beta, float lbeta)
 {

@@ -45,6 +45,7 @@ typedef struct {
 #define WC_MAGIC_EXPERT 0x50584557u   /* src/waste_format.h:33 */
 #define WC_WQ_VQ3R 4                  /* src/waste_format.h:51 */
 #define WC_WQ_VQ2R 5                  /* src/waste_format.h:52 */
+#define WC_WQ_VQ4P 8                  /* src/waste_format.h:57: 4 stages of 64, 6-bit indices packed 4-in-3 */
 #define WC_ALIGN 4096u                /* src/waste_format.h:42 */
 
 typedef struct {
@@ -82,6 +83,7 @@ static struct {
     char name[300];
     float *d_books;
     int n_books;
+    int cb_entries;              /* 256 (VQ3R/VQ2R) or 64 (VQ4P); books sit 256 entries apart */
     float *book_absmax;          /* host: max |entry| of each book               */
     int books_f16;               /* every entry an fp16 normal or zero (exact in fp16) */
     /* batched (prefill) path on the tensor cores */
@@ -108,6 +110,9 @@ static struct {
      * back: out [res_lat] | route [WC_MAX_TOPK] | weights [WC_MAX_TOPK] | err */
     float *d_res, *h_res;
     int res_lat;
+    /* VQ4P scratch: integer block sums, table scales, activations */
+    void *d_p6;
+    size_t p6_bytes;
 } S;
 
 /* Bumped by every call that allocates, frees or reloads what a cached
@@ -164,6 +169,8 @@ static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
 static void mirrors_free(void);
 static int pf_wanted(const wc_layer *L, int T, int K);
+static int p6_experts(const wc_layer *L, int T, int K, int act, float situ_beta,
+                      float situ_lbeta, int order_by_id);
 static int pf_args(const wc_layer *L, int T, int K, wc_pf_args *a);
 static _Thread_local char g_err[256];
 static char g_err_global[256];
@@ -363,6 +370,7 @@ void waste_cuda_shutdown(void)
         cudaFreeHost(S.h_x); cudaFreeHost(S.h_out); cudaFreeHost(S.h_idx);
         cudaFreeHost(S.h_w);
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
+        cudaFree(S.d_p6);
         mirrors_free();
         for (int b = 0; b < 2; b++) {
             cudaFreeHost(g_stage.buf[b]);
@@ -607,15 +615,26 @@ int waste_register_cuda_vq(waste_vq_slots *s)
 
 /* ---- codebooks --------------------------------------------------------- */
 
-static int books_upload(const float *books, int n_books)
+static int books_upload(const float *books, int n_books, int entries)
 {
     int rc = 0;
+    float *pad = NULL;
     g_epoch++;
     const size_t bytes = (size_t)n_books * 256 * 8 * sizeof(float);
     if (S.d_books) { cudaFree(S.d_books); S.d_books = NULL; S.n_books = 0; }
+    if (entries != 256) {
+        /* every book keeps a 256-entry slot; a 64-entry book fills the
+         * first 64 and the rest stays zero */
+        pad = (float *)calloc((size_t)n_books * 256 * 8, sizeof(float));
+        if (!pad) return fail(WASTE_CUDA_E_NOMEM, "codebook staging");
+        for (int b = 0; b < n_books; b++)
+            memcpy(pad + (size_t)b * 256 * 8, books + (size_t)b * entries * 8,
+                   (size_t)entries * 8 * sizeof(float));
+        books = pad;
+    }
     free(S.book_absmax);
     S.book_absmax = (float *)calloc((size_t)n_books, sizeof(float));
-    if (!S.book_absmax) return fail(WASTE_CUDA_E_NOMEM, "codebook maxima");
+    if (!S.book_absmax) { rc = fail(WASTE_CUDA_E_NOMEM, "codebook maxima"); goto out; }
     /* per-book maxima (the tensor-core path's weight pre-scale), and whether
      * every entry is exact in fp16 (normal or zero), which that path needs */
     S.books_f16 = 1;
@@ -632,17 +651,20 @@ static int books_upload(const float *books, int n_books)
     CK(cudaMalloc((void **)&S.d_books, bytes), "codebooks");
     CK(cudaMemcpy(S.d_books, books, bytes, cudaMemcpyHostToDevice), "codebooks H2D");
     S.n_books = n_books;
+    S.cb_entries = entries;
 out:
+    free(pad);
     return rc;
 }
 
 int waste_cuda_codebooks_load(const float *books, int n_books, int entries, int vec_dim)
 {
-    if (!books || n_books <= 0 || entries != 256 || vec_dim != 8)
-        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256, vec_dim 8");
+    if (!books || n_books <= 0 || (entries != 256 && entries != 64) || vec_dim != 8)
+        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256 (VQ3R) or 64 (VQ4P), "
+                    "vec_dim 8");
     pthread_mutex_lock(&g_mu);
     int rc = S.inited ? 0 : init_locked(-1);
-    if (!rc) rc = books_upload(books, n_books);
+    if (!rc) rc = books_upload(books, n_books, entries);
     pthread_mutex_unlock(&g_mu);
     return rc;
 }
@@ -661,8 +683,9 @@ static float f16_flush(uint16_t v)
 
 int waste_cuda_codebooks_load_f16(const uint16_t *raw, int n_books, int entries, int vec_dim)
 {
-    if (!raw || n_books <= 0 || entries != 256 || vec_dim != 8)
-        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256, vec_dim 8");
+    if (!raw || n_books <= 0 || (entries != 256 && entries != 64) || vec_dim != 8)
+        return fail(WASTE_CUDA_E_ARG, "codebooks: need entries 256 (VQ3R) or 64 (VQ4P), "
+                    "vec_dim 8");
     const size_t n = (size_t)n_books * entries * vec_dim;
     float *f = (float *)malloc(n * sizeof(float));
     if (!f) return fail(WASTE_CUDA_E_NOMEM, "codebook staging");
@@ -681,7 +704,11 @@ static int check_record(const wc_hdr *h, int layer, int expert, size_t rec_bytes
     if (rec_bytes < sizeof *h || h->magic != WC_MAGIC_EXPERT) return -1;
     if (h->layer != (uint16_t)layer || h->expert_id != (uint16_t)expert) return -1;
     if ((size_t)h->rec_4k_blocks * WC_ALIGN != rec_bytes) return -1;
-    if (h->fmt != WC_WQ_VQ3R && h->fmt != WC_WQ_VQ2R) return -1;
+    /* the fmt byte and the layer's format agree (src/model.c:1713-1719):
+     * VQ4P with four stages of 64-entry books, else VQ3R/VQ2R with 256 */
+    if (stages == 4 ? (h->fmt != WC_WQ_VQ4P || S.cb_entries != 64)
+                    : ((h->fmt != WC_WQ_VQ3R && h->fmt != WC_WQ_VQ2R) || S.cb_entries != 256))
+        return -1;
     if (h->lowrank_id != 0) return -1;
     if ((long)h->codebook_id + 3L * stages > S.n_books) return -1;
     if (!(h->gate_off == sizeof *h && h->gate_off < h->up_off &&
@@ -692,8 +719,9 @@ static int check_record(const wc_hdr *h, int layer, int expert, size_t rec_bytes
     if (scales > rec_bytes - h->chan_corr_off) return -1;
     /* the index streams must fit before the next section */
     const size_t nrb_i = (size_t)(inter + 63) / 64, nrb_l = (size_t)(lat + 63) / 64;
-    const size_t gate_b = nrb_i * 64 * (lat / 8) * stages;
-    const size_t down_b = nrb_l * 64 * (inter / 8) * stages;
+    const size_t per = stages == 4 ? 3 : (size_t)stages;   /* index bytes per row and position */
+    const size_t gate_b = nrb_i * 64 * (lat / 8) * per;
+    const size_t down_b = nrb_l * 64 * (inter / 8) * per;
     if (h->up_off - h->gate_off < gate_b || h->down_off - h->up_off < gate_b ||
         h->chan_corr_off - h->down_off < down_b)
         return -1;
@@ -817,7 +845,7 @@ static int bank_args_ok(int layer, int n_experts, size_t rec_bytes, int first, i
     return layer >= 0 && layer < WC_MAX_LAYERS && n_experts > 0 && first >= 0 && count > 0 &&
            first + count <= n_experts && rec_bytes > 0 && rec_bytes % WC_ALIGN == 0 &&
            inter > 0 && lat > 0 && inter % 8 == 0 && lat % 8 == 0 &&
-           (stages == 2 || stages == 3);
+           (stages == 2 || stages == 3 || stages == 4);
 }
 
 int waste_cuda_vq_bank_reserve(int layer, int n_experts, size_t rec_bytes, int first,
@@ -1164,7 +1192,9 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
     pthread_mutex_lock(&g_mu);
     if ((rc = layer_ready(layer, lat, inter, &L))) goto out;
     if ((rc = check_route(L, idx, T * K))) goto out;
-    if ((rc = ensure_ws(T, K, 1, lat, inter, 0, L->kb.stages))) goto out;
+    /* a VQ4P bank uses the io buffers and the error word, not the fused
+     * kernels' workspace layout, which is sized here as for VQ3R */
+    if ((rc = ensure_ws(T, K, 1, lat, inter, 0, L->kb.stages == 4 ? 3 : L->kb.stages))) goto out;
     const size_t xb = (size_t)T * lat * sizeof(float);
     memcpy(S.h_x, x, xb);
     memcpy(S.h_idx, idx, (size_t)T * K * sizeof(int));
@@ -1174,7 +1204,9 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
                        S.stream), "idx H2D");
     CK(cudaMemcpyAsync(S.d_w, S.h_w, (size_t)T * K * sizeof(float), cudaMemcpyHostToDevice,
                        S.stream), "w H2D");
-    if (order_by_id && pf_wanted(L, T, K)) {
+    if (L->kb.stages == 4) {
+        if ((rc = p6_experts(L, T, K, act, situ_beta, situ_lbeta, order_by_id))) goto out;
+    } else if (order_by_id && pf_wanted(L, T, K)) {
         /* a chunk with enough tokens per expert: dense tiles on the tensor cores */
         wc_pf_args pa;
         if ((rc = pf_args(L, T, K, &pa))) goto out;
@@ -1238,6 +1270,9 @@ static int layer_args(int layer, int T, int part, wc_moe_args *a, wc_layer **Lp)
     if (layer < 0 || layer >= WC_MAX_LAYERS || !S.layer[layer].loaded || !S.layer[layer].trunk)
         return fail(WASTE_CUDA_E_NOBANK, "layer %d: bank or trunk not loaded", layer);
     wc_layer *L = &S.layer[layer];
+    if (L->kb.stages == 4)
+        return fail(WASTE_CUDA_E_ARG, "layer %d: a VQ4P bank runs through moe_experts / "
+                    "moe_chunk_experts only", layer);
     if (T <= 0 || T > WC_CHUNK_MAX)
         return fail(WASTE_CUDA_E_ARG, "layer %d: %d tokens, 1..%d per call", layer, T,
                     WC_CHUNK_MAX);
@@ -1422,7 +1457,7 @@ static int pf_args(const wc_layer *L, int T, int K, wc_pf_args *a)
  * codebooks, and enough pairs per expert for dense tiles to beat lookups. */
 static int pf_wanted(const wc_layer *L, int T, int K)
 {
-    return S.books_f16 && wc_pf_supported(&L->kb, T, K) == 0 &&
+    return S.books_f16 && L->kb.stages == 3 && wc_pf_supported(&L->kb, T, K) == 0 &&
            (long)T * K >= 2L * L->kb.n_experts && getenv_flag("WASTE_CUDA_PREFILL_TC", 1);
 }
 
@@ -1444,7 +1479,7 @@ int waste_cuda_moe_prefill_dev(int layer, int T, int K, const int *d_route, cons
         rc = fail(WASTE_CUDA_E_ARG, "layer %d: not every record of the bank is loaded", layer);
         goto out;
     }
-    if (!S.books_f16 || wc_pf_supported(&L->kb, T, K)) {
+    if (!S.books_f16 || L->kb.stages != 3 || wc_pf_supported(&L->kb, T, K)) {
         rc = fail(WASTE_CUDA_E_ARG, "layer %d: outside the tensor-core path's bounds (3 stages, "
                   "rows multiples of 128, T*K <= %d, K <= 64, fp16-exact codebooks)", layer,
                   WC_PF_MAX_PAIRS);
@@ -1917,6 +1952,177 @@ static int tmp_reserve(size_t bytes)
 }
 
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+/* ---- VQ4P ------------------------------------------------------------------ */
+
+/* Scratch for a VQ4P launch: integer block sums and table scales for the
+ * larger of two phases (G problems of [M][N] each), then `h_floats` floats
+ * of activations. */
+static int p6_reserve(int G0, int M0, int N0, int G1, int M1, int N1, size_t h_floats,
+                      int **part, float **ls, float **h)
+{
+    size_t pi = wc_p6_part_ints(G0, M0, N0), lf = wc_p6_ls_floats(G0, N0);
+    if (G1 > 0) {
+        const size_t pi1 = wc_p6_part_ints(G1, M1, N1), lf1 = wc_p6_ls_floats(G1, N1);
+        if (pi1 > pi) pi = pi1;
+        if (lf1 > lf) lf = lf1;
+    }
+    const size_t need = al256(pi * sizeof(int)) + al256(lf * sizeof(float)) +
+                        al256(h_floats * sizeof(float));
+    if (need > S.p6_bytes) {
+        g_epoch++;
+        cudaFree(S.d_p6);
+        S.d_p6 = NULL;
+        S.p6_bytes = 0;
+        const cudaError_t e = cudaMalloc(&S.d_p6, need);
+        if (e != cudaSuccess) return cuda_fail(e, "VQ4P scratch");
+        S.p6_bytes = need;
+    }
+    char *b = (char *)S.d_p6;
+    *part = (int *)b;
+    *ls = (float *)(b + al256(pi * sizeof(int)));
+    if (h) *h = (float *)(b + al256(pi * sizeof(int)) + al256(lf * sizeof(float)));
+    return 0;
+}
+
+/* The expert loop over a VQ4P bank for the T tokens staged in S.d_x /
+ * S.d_idx / S.d_w; ysum into S.d_out. The caller holds g_mu. */
+static int p6_experts(const wc_layer *L, int T, int K, int act, float situ_beta,
+                      float situ_lbeta, int order_by_id)
+{
+    int rc = 0;
+    const int pairs = T * K, lat = L->kb.lat, inter = L->kb.inter;
+    wc_p6_args *a = (wc_p6_args *)calloc(1, sizeof *a);
+    if (!a) return fail(WASTE_CUDA_E_NOMEM, "VQ4P arguments");
+    if ((rc = p6_reserve(2 * pairs, inter, lat, pairs, lat, inter, (size_t)pairs * inter,
+                         &a->part, &a->ls, &a->h)))
+        goto out;
+    a->books = S.d_books;
+    a->bank = L->kb;
+    a->T = T;
+    a->K = K;
+    a->order_by_id = order_by_id;
+    a->act = act;
+    a->situ_beta = situ_beta;
+    a->situ_lbeta = situ_lbeta;
+    a->route = S.d_idx;
+    a->rw = S.d_w;
+    a->x_in = S.d_x;
+    a->ysum = S.d_out;
+    a->err = (unsigned int *)S.d_ws + 192;
+    CK((cudaError_t)wc_p6_moe_launch(a, S.stream), "VQ4P expert kernels");
+out:
+    free(a);
+    return rc;
+}
+
+static int check_p6(int M, int N, int cb_base)
+{
+    if (M <= 0 || N <= 0 || N % 8 || cb_base < 0)
+        return fail(WASTE_CUDA_E_ARG, "VQ4P matrix: bad shape");
+    if (!S.d_books || S.cb_entries != 64 || cb_base + 4 > S.n_books)
+        return fail(WASTE_CUDA_E_ARG, "VQ4P: 64-entry codebooks not loaded or cb_base out of "
+                    "range");
+    return 0;
+}
+
+int waste_cuda_vq4p_matvec_dev(int G, const uint8_t *const *idx, const uint16_t *const *scale,
+                               const float *const *x, float *const *y, int M, int N,
+                               int cb_base, void *stream)
+{
+    int rc = 0;
+    wc_p6_args *a = NULL;
+    if (G <= 0 || G > WC_MAX_G || !idx || !scale || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "vq4p_matvec_dev: bad arguments");
+    for (int g = 0; g < G; g++)
+        if (!idx[g] || !scale[g] || !x[g] || !y[g] || ((uintptr_t)idx[g] & 7))
+            return fail(WASTE_CUDA_E_ARG, "vq4p_matvec_dev: matrix %d: NULL or idx not "
+                        "8-byte aligned", g);
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    if ((rc = check_p6(M, N, cb_base))) goto out;
+    a = (wc_p6_args *)calloc(1, sizeof *a);
+    if (!a) { rc = fail(WASTE_CUDA_E_NOMEM, "VQ4P arguments"); goto out; }
+    if ((rc = p6_reserve(G, M, N, 0, 0, 0, 0, &a->part, &a->ls, NULL))) goto out;
+    a->G = G;
+    a->M = M;
+    a->N = N;
+    a->books = S.d_books;
+    for (int g = 0; g < G; g++) {
+        a->idx[g] = idx[g];
+        a->scale[g] = scale[g];
+        a->x[g] = x[g];
+        a->y[g] = y[g];
+        a->cb[g] = cb_base;
+    }
+    CK((cudaError_t)wc_p6_matvec_launch(a, stream ? stream : (void *)S.stream), "VQ4P matvec");
+out:
+    free(a);
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq4p_matvec(float *y, const uint8_t *idx, const uint16_t *scale, const float *x,
+                           int M, int N, int cb_base)
+{
+    int rc = 0;
+    wc_p6_args *a = NULL;
+    if (!y || !idx || !scale || !x) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    if ((rc = check_p6(M, N, cb_base))) goto out;
+    const size_t ib = (size_t)((M + 63) / 64) * 64 * (N / 8) * 3;
+    const size_t o_sc = al256(ib), o_x = o_sc + al256((size_t)M * 2),
+                 o_y = o_x + al256((size_t)N * 4), tot = o_y + (size_t)M * 4;
+    if ((rc = tmp_reserve(tot))) goto out;
+    char *t = (char *)S.d_tmp;
+    CK(cudaMemcpyAsync(t, idx, ib, cudaMemcpyHostToDevice, S.stream), "idx H2D");
+    CK(cudaMemcpyAsync(t + o_sc, scale, (size_t)M * 2, cudaMemcpyHostToDevice, S.stream),
+       "scale H2D");
+    CK(cudaMemcpyAsync(t + o_x, x, (size_t)N * 4, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    a = (wc_p6_args *)calloc(1, sizeof *a);
+    if (!a) { rc = fail(WASTE_CUDA_E_NOMEM, "VQ4P arguments"); goto out; }
+    if ((rc = p6_reserve(1, M, N, 0, 0, 0, 0, &a->part, &a->ls, NULL))) goto out;
+    a->G = 1;
+    a->M = M;
+    a->N = N;
+    a->books = S.d_books;
+    a->idx[0] = (const uint8_t *)t;
+    a->scale[0] = (const uint16_t *)(t + o_sc);
+    a->x[0] = (const float *)(t + o_x);
+    a->y[0] = (float *)(t + o_y);
+    a->cb[0] = cb_base;
+    CK((cudaError_t)wc_p6_matvec_launch(a, S.stream), "VQ4P matvec");
+    CK(cudaMemcpyAsync(y, t + o_y, (size_t)M * 4, cudaMemcpyDeviceToHost, S.stream), "y D2H");
+    CK(cudaStreamSynchronize(S.stream), "VQ4P matvec");
+out:
+    free(a);
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq4p_table(int8_t *q, float *qs, const float *x, int N, int cb_base)
+{
+    int rc = 0;
+    if (!q || !qs || !x) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    if ((rc = check_p6(1, N, cb_base))) goto out;
+    const int nv = N / 8, nb = (nv + 31) / 32;
+    const size_t qb = (size_t)nv * 256, o_qs = al256(qb), o_x = o_qs + al256((size_t)nb * 4);
+    if ((rc = tmp_reserve(o_x + (size_t)N * 4))) goto out;
+    char *t = (char *)S.d_tmp;
+    CK(cudaMemcpyAsync(t + o_x, x, (size_t)N * 4, cudaMemcpyHostToDevice, S.stream), "x H2D");
+    CK((cudaError_t)wc_p6_table_launch((int8_t *)t, (float *)(t + o_qs), (const float *)(t + o_x),
+                                       S.d_books, cb_base, nv, S.stream), "VQ4P table");
+    CK(cudaMemcpyAsync(q, t, qb, cudaMemcpyDeviceToHost, S.stream), "table D2H");
+    CK(cudaMemcpyAsync(qs, t + o_qs, (size_t)nb * 4, cudaMemcpyDeviceToHost, S.stream),
+       "scales D2H");
+    CK(cudaStreamSynchronize(S.stream), "VQ4P table");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
 
 int waste_cuda_lutb(float *lut, const float *x, int cb_base, int nv, int stages)
 {

@@ -197,6 +197,44 @@ int    wc_noalloc_part(float **ptr);
 int    wc_noalloc_setup(float **ptr);
 int    wc_binary_version(void);
 
+/* VQ4P (vq4p.cu): four 64-entry stages, 6-bit indices packed four to three
+ * bytes, int8 tables with one scale per 32 positions. The list form runs
+ * G <= WC_MAX_G independent matvecs y[g] = VQ4P(idx[g], scale[g]) . x[g]
+ * (book base cb[g]); the expert form runs the expert loop of T tokens over
+ * a VQ4P bank: gate/up of every (token, slot) pair, the gated activation
+ * into h, down, and the weighted reduce into ysum (router order, or
+ * ascending expert id when order_by_id). part/ls are scratch of
+ * wc_p6_part_ints / wc_p6_ls_floats elements for the larger of the two
+ * phases (G = 2*T*K pairs of [inter][lat], or T*K of [lat][inter]). */
+typedef struct {
+    int G, M, N;
+    const uint8_t *idx[WC_MAX_G];
+    const uint16_t *scale[WC_MAX_G];
+    const float *x[WC_MAX_G];
+    float *y[WC_MAX_G];
+    int cb[WC_MAX_G];
+    const float *books;        /* [n_books][256][8] f32; a VQ4P book fills entries 0..63 */
+    int *part;                 /* [problem][block][M] integer block sums             */
+    float *ls;                 /* [problem][block] table scales                      */
+    wc_bank bank;
+    int T, K, order_by_id, act;
+    float situ_beta, situ_lbeta;
+    const int *route;          /* [T][K] global expert ids                           */
+    const float *rw;           /* [T][K]                                             */
+    const float *x_in;         /* [T][lat]                                           */
+    float *h;                  /* [T*K][inter] activations                           */
+    float *ysum;               /* [T][lat]                                           */
+    unsigned int *err;
+} wc_p6_args;
+
+size_t wc_p6_part_ints(int G, int M, int N);
+size_t wc_p6_ls_floats(int G, int N);
+int    wc_p6_matvec_launch(const wc_p6_args *a, void *stream);
+int    wc_p6_moe_launch(const wc_p6_args *a, void *stream);
+/* The int8 tables of x against books cb..cb+3: q [nv][4][64], qs [blocks]. */
+int    wc_p6_table_launch(int8_t *q, float *qs, const float *x, const float *books, int cb,
+                          int nv, void *stream);
+
 int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
                    int nv, int stages, void *stream);
 int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *scale,

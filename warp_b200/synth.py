@@ -11,6 +11,11 @@ the reference CPU engine and to this backend:
   tools/convert.py:457 write_expert_record);
 * codebooks — ``n_books`` books of 256 entries x 8 f16 (codebooks.bin
   payload, src/waste_format.h:139-150);
+* VQ4P records (``stages=4``; src/waste_format.h:57) — four stages of
+  64-entry books, the four 6-bit indices of a row and position packed
+  little-endian into three bytes (tools/convert.py:315-337), so the index
+  streams have the same size as VQ3R's; any three bytes are a valid
+  packing, so uniform random bytes are uniform indices;
 * Q8G trunk rows — int8 rows padded to whole groups of 128 plus one f16
   scale per group (src/model.c:265-320 layout).
 
@@ -27,11 +32,12 @@ from dataclasses import dataclass, field
 import numpy as np
 
 MAGIC_EXPERT = 0x50584557
-FMT_VQ3R, FMT_VQ2R = 4, 5
+FMT_VQ3R, FMT_VQ2R, FMT_VQ4P = 4, 5, 8
 ALIGN = 4096
 HDR_SIZE = 48
 HDR_FMT = "<IHHBBHHHIIIIIIII"      # waste_expert_hdr, src/waste_format.h:98-132
 VEC_DIM, ENTRIES, BLOCK = 8, 256, 64
+ENTRIES_VQ4P = 64
 GROUP = 128
 
 
@@ -57,9 +63,27 @@ def flush_f16(raw: np.ndarray) -> np.ndarray:
     return bits.astype(np.uint32).view(np.float32)
 
 
-def codebooks(rng: np.random.Generator, n_books: int, std: float = 0.02) -> np.ndarray:
-    """Raw f16 codebook entries [n_books][256][8] as uint16."""
-    return f16_bits(rng.normal(0.0, std, size=(n_books, ENTRIES, VEC_DIM)))
+def codebooks(rng: np.random.Generator, n_books: int, std: float = 0.02,
+              entries: int = ENTRIES) -> np.ndarray:
+    """Raw f16 codebook entries [n_books][entries][8] as uint16."""
+    return f16_bits(rng.normal(0.0, std, size=(n_books, entries, VEC_DIM)))
+
+
+def row_bytes(stages: int) -> int:
+    """Index bytes per row and vector position: one per stage, or three
+    for VQ4P's four packed 6-bit indices."""
+    return 3 if stages == 4 else stages
+
+
+def fmt_of(stages: int) -> int:
+    return {2: FMT_VQ2R, 3: FMT_VQ3R, 4: FMT_VQ4P}[stages]
+
+
+def unpack_p6(b: np.ndarray) -> np.ndarray:
+    """[..., 3] packed VQ4P bytes -> [..., 4] 6-bit indices."""
+    b = np.asarray(b, dtype=np.uint32)
+    p = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)
+    return np.stack([(p >> (6 * s)) & 63 for s in range(4)], axis=-1).astype(np.uint8)
 
 
 def block_indices(idx: np.ndarray) -> np.ndarray:
@@ -74,20 +98,22 @@ def block_indices(idx: np.ndarray) -> np.ndarray:
 def unblock_indices(blob: np.ndarray, M: int, N: int, stages: int) -> np.ndarray:
     nv = N // VEC_DIM
     nb = (M + BLOCK - 1) // BLOCK
-    a = np.asarray(blob, dtype=np.uint8)[: nb * nv * BLOCK * stages]
-    return a.reshape(nb, nv, BLOCK, stages).transpose(0, 2, 1, 3).reshape(nb * BLOCK, nv, stages)[:M]
+    rb = row_bytes(stages)
+    a = np.asarray(blob, dtype=np.uint8)[: nb * nv * BLOCK * rb]
+    return a.reshape(nb, nv, BLOCK, rb).transpose(0, 2, 1, 3).reshape(nb * BLOCK, nv, rb)[:M]
 
 
 def random_matrix(rng: np.random.Generator, M: int, N: int, stages: int = 3,
                   scale_lo: float = 0.5, scale_hi: float = 1.5):
     """One VQ matrix: blocked index bytes and f16 row scales (uint16)."""
-    idx = random_bytes(rng, M * (N // VEC_DIM) * stages).reshape(M, N // VEC_DIM, stages)
+    rb = row_bytes(stages)
+    idx = random_bytes(rng, M * (N // VEC_DIM) * rb).reshape(M, N // VEC_DIM, rb)
     scales = f16_bits(rng.uniform(scale_lo, scale_hi, size=M))
     return block_indices(idx), scales
 
 
 def index_bytes(M: int, N: int, stages: int) -> int:
-    return ((M + BLOCK - 1) // BLOCK) * (N // VEC_DIM) * BLOCK * stages
+    return ((M + BLOCK - 1) // BLOCK) * (N // VEC_DIM) * BLOCK * row_bytes(stages)
 
 
 def record_bytes(inter: int, lat: int, stages: int) -> int:
@@ -104,7 +130,7 @@ def expert_record(rng: np.random.Generator, layer: int, eid: int, cb_base: int,
     for (M, N) in ((inter, lat), (inter, lat), (lat, inter)):
         b = random_bytes(rng, index_bytes(M, N, stages))
         if M % BLOCK:      # padding rows stay zero, as block_indices writes them
-            b = b.reshape((M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK, stages)
+            b = b.reshape((M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK, row_bytes(stages))
             b[-1, :, M % BLOCK:, :] = 0
             b = b.reshape(-1)
         offsets.append(off)
@@ -118,7 +144,7 @@ def expert_record(rng: np.random.Generator, layer: int, eid: int, cb_base: int,
     body = b"".join(parts)
     total = HDR_SIZE + len(body)
     blocks = (total + ALIGN - 1) // ALIGN
-    fmt = FMT_VQ3R if stages == 3 else FMT_VQ2R
+    fmt = fmt_of(stages)
     hdr = struct.pack(HDR_FMT, MAGIC_EXPERT, layer, eid, fmt, 0, cb_base, 0, 0, blocks,
                       offsets[0], offsets[1], offsets[2], corr_off,
                       zlib.crc32(body) & 0xFFFFFFFF, 0, 0)
@@ -172,7 +198,7 @@ class MoELayer:
     routed_scale: float
     stages: int
     cb_base: int
-    books_raw: np.ndarray            # [n_books][256][8] uint16
+    books_raw: np.ndarray            # [n_books][256 (64 for VQ4P)][8] uint16
     router: np.ndarray               # [E][hidden] f32
     bias: np.ndarray | None          # [E] f32
     bank: np.ndarray                 # E * rec_bytes uint8
@@ -226,7 +252,8 @@ def _finish_bank(bank: np.ndarray, rng: np.random.Generator, layer: int, cb_base
         n = index_bytes(M, N, stages)
         offs.append(off)
         if M % BLOCK:
-            v = bank[:, off:off + n].reshape(E, (M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK, stages)
+            v = bank[:, off:off + n].reshape(E, (M + BLOCK - 1) // BLOCK, N // VEC_DIM, BLOCK,
+                                             row_bytes(stages))
             v[:, -1, :, M % BLOCK:, :] = 0
         off += n
     corr = off
@@ -234,7 +261,7 @@ def _finish_bank(bank: np.ndarray, rng: np.random.Generator, layer: int, cb_base
     bank[:, corr:corr + 2 * ns] = f16_bits(rng.uniform(scale_lo, scale_hi, size=(E, ns))).view(np.uint8)
     end = corr + 2 * ns
     bank[:, end:] = 0
-    fmt = FMT_VQ3R if stages == 3 else FMT_VQ2R
+    fmt = fmt_of(stages)
     blocks = rb // ALIGN
     for e in range(E):
         crc = zlib.crc32(memoryview(bank[e, HDR_SIZE:end])) & 0xFFFFFFFF
@@ -319,12 +346,12 @@ def moe_layer(seed: int, hidden: int = 2304, inter: int = 1024, n_experts: int =
               situ_beta: float = 4.0, situ_lbeta: float = 25.0) -> MoELayer:
     """Seeded layer at the Kimi-Linear-48B shape by default (hidden 2304,
     expert inter 1024, 256 experts, top-8, one shared expert, routed scale
-    2.446 with renorm)."""
+    2.446 with renorm). stages 4 is a VQ4P layer (64-entry books)."""
     rng = np.random.default_rng(seed)
     if cb_base is None:
         cb_base = 3 * stages * (layer - 1) if layer >= 1 else 0
     n_books = cb_base + 3 * stages
-    books_raw = codebooks(rng, n_books)
+    books_raw = codebooks(rng, n_books, entries=ENTRIES_VQ4P if stages == 4 else ENTRIES)
     router = (rng.standard_normal((n_experts, hidden), dtype=np.float32)
               / np.float32(np.sqrt(hidden))).astype(np.float32)
     bias = (rng.normal(0, 0.05, size=n_experts).astype(np.float32) if with_bias else None)
