@@ -28,6 +28,10 @@
  *   waste_cuda_moe_layer(_dev)   src/model.c:2713-2939 moe_layer (router,
  *                                experts, shared expert) for a device-resident
  *                                hidden state
+ *   waste_cuda_kda_step(_dev)    src/kda.c:26-68 waste_kda_step (slot kda_step,
+ *                                src/waste_backend.h:69-72)
+ *   waste_cuda_short_conv_*      src/kda.c:84-99 (slot short_conv_step)
+ *   waste_cuda_rmsnorm_gated_*   src/kda.c:101-111 (slot rmsnorm_gated)
  *   waste_cuda_moe_block(_dev)   src/model.c:3927-3945 the MoE half of a
  *                                decoder layer: rmsnorm (:132-138), moe_layer,
  *                                residual add
@@ -60,9 +64,13 @@ extern "C" {
  * engine's waste_backend.h first sees the engine's own prototype (a pointer
  * to its waste_kernels table); anywhere else the table is an opaque
  * pointer. Of that table it fills mvq_rows_f32 (the trunk matvec, see
- * waste_cuda_mvq_rows_dev; WASTE_CUDA_TRUNK=0 leaves it alone) and sets
- * on_device, so the engine hands it whole row ranges on the calling
- * thread. The expert path's slots are waste_vq_slots below. */
+ * waste_cuda_mvq_rows_dev; WASTE_CUDA_TRUNK=0 leaves it alone), kda_step
+ * (WASTE_CUDA_KDA=0 leaves it), short_conv_step and rmsnorm_gated (only
+ * with WASTE_CUDA_KDA_CONV=1 / WASTE_CUDA_KDA_NORM=1: their calls carry a
+ * few KB each, and the host round trip costs more than the CPU's work),
+ * and sets on_device, so the engine hands it whole row ranges — and the
+ * whole head range of a KDA step — on the calling thread. The expert
+ * path's slots are waste_vq_slots below. */
 #ifdef WASTE_BACKEND_H
 const char *waste_register_cuda(waste_kernels *t);
 #else
@@ -86,6 +94,16 @@ typedef struct {
     int  (*vq_bank_load_file)(int layer, int fd, int64_t offset, int n_experts,
                               size_t rec_bytes, int first, int count, int inter,
                               int lat, int stages);
+    /* KDA recurrent state held in HBM (see waste_cuda_state_push/pull): the
+     * engine pushes a state range after writing it on the host (reset,
+     * snapshot load) and pulls it before reading it (snapshot save). */
+    void (*state_push)(const void *host, size_t bytes);
+    void (*state_pull)(void *host, size_t bytes);
+    /* rmsnorm_gated over nh heads of C channels with one weight vector, in
+     * one call (NULL unless WASTE_CUDA_KDA_NORM=1; the engine then loops
+     * over heads through waste_kernels.rmsnorm_gated). */
+    void (*rmsnorm_gated_heads)(int nh, int C, const float *x, const float *gate,
+                                const float *weight, float eps, float *y);
 } waste_vq_slots;
 
 /* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */
@@ -433,6 +451,40 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
                                      int M, int N, int cb_base, int stages,
                                      void *stream);
 
+/* ---- KDA (Kimi Delta Attention) decode step -----------------------------
+ * src/kda.c:19-111 on the device, bit for bit except where glibc's expf is
+ * not correctly rounded (the device's exp is; a few inputs in 10^4).
+ * kda_step: q, k, g_log [H][K]; v, o [H][V]; beta [H]; S [H][K][V] updated
+ * in place; K 32, 64 or 128. short_conv_step: C channels, kernel KS, w
+ * [C][KS], bias [C] or NULL, ring [C][KS-1] (oldest first) updated,
+ * y = SiLU(conv) (y may be x). rmsnorm_gated_heads: nh heads of C
+ * channels, one weight vector, y = x * r * w * sigmoid(gate) per head (y
+ * may be x).
+ * Host-pointer forms (the slots): the state (S, ring) and the weights are
+ * kept in HBM from the first call that names them, keyed by host address:
+ * the host copy of a state is stale from then on — waste_cuda_state_pull
+ * copies a range back, waste_cuda_state_push reloads it after the caller
+ * wrote it (both cover every held copy that overlaps the range; ranges
+ * nothing holds are left alone). A call whose state range partly overlaps
+ * a held one fails with WASTE_CUDA_E_NOMEM. waste_cuda_release_host_buffers
+ * drops every held copy. _dev forms: device pointers, ordered on `stream`. */
+int waste_cuda_kda_step(int H, int K, int V, const float *q, const float *k,
+                        const float *v, const float *g_log, const float *beta,
+                        float *S, float *o);
+int waste_cuda_short_conv_step(int C, int KS, const float *w, const float *bias,
+                               float *ring, const float *x, float *y);
+int waste_cuda_rmsnorm_gated_heads(int nh, int C, const float *x, const float *gate,
+                                   const float *weight, float eps, float *y);
+int waste_cuda_state_push(const void *host, size_t bytes);
+int waste_cuda_state_pull(void *host, size_t bytes);
+int waste_cuda_kda_step_dev(int H, int K, int V, const float *q, const float *k,
+                            const float *v, const float *g_log, const float *beta,
+                            float *S, float *o, void *stream);
+int waste_cuda_short_conv_dev(int C, int KS, const float *w, const float *bias,
+                              float *ring, const float *x, float *y, void *stream);
+int waste_cuda_rmsnorm_gated_dev(int nh, int C, const float *x, const float *gate,
+                                 const float *weight, float eps, float *y, void *stream);
+
 /* ---- the trunk matvec (the mvq_rows_f32 slot) ---------------------------
  * src/model.c:265-320 waste_mvq_rows_f32 on the device: y[r] for r in
  * [r0, r1) = sum over groups k of f16(ws[r][k]) * (sum over the group's
@@ -445,9 +497,9 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
  * host address of its weights, made at first use), copies x in and y out,
  * and runs tensors below WASTE_CUDA_TRUNK_MIN bytes (default 1 MiB) — and
  * anything the device path cannot take — on the CPU kernel the slot held
- * before. waste_cuda_release_host_buffers drops those copies (the engine
- * calls it before freeing a model: src/backend.c:223-229,
- * waste_backend_release_host_buffers). */
+ * before. waste_cuda_release_host_buffers drops those copies, and the KDA
+ * state copies below (the engine calls it before freeing a model:
+ * src/backend.c:223-229, waste_backend_release_host_buffers). */
 int  waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws,
                              const float *d_x, int r0, int r1, int in, int group,
                              int bits, size_t rowbytes, void *stream);

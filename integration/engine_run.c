@@ -12,6 +12,13 @@
  * Makefile with the CUDA backend. out.bin: int32 evals, int32 vocab, then
  * per eval int32 argmax and vocab floats. The engine's build info (which
  * names the backend it selected) is printed on stdout.
+ *
+ * With ENGINE_RUN_STATE=<path> the conversation state goes through a
+ * snapshot half way: after the prompt and steps/2 decode steps the state is
+ * saved (waste_state_save), the context reset (waste_state_reset) and the
+ * prompt evaluated again (one extra eval, which must repeat eval 0), then
+ * the snapshot loaded (waste_state_load) and the remaining steps decoded
+ * from where the save left off.
  */
 #include "waste.h"
 
@@ -26,6 +33,8 @@ typedef waste_status (*eval_fn)(waste_ctx *, const int32_t *, size_t, const floa
 typedef void (*close_fn)(waste_ctx *);
 typedef const char *(*str_fn)(void);
 typedef const char *(*detail_fn)(const waste_ctx *);
+typedef waste_status (*state_fn)(waste_ctx *, const char *);
+typedef void (*reset_fn)(waste_ctx *);
 
 static int argmax(const float *v, size_t n)
 {
@@ -69,16 +78,35 @@ int main(int argc, char **argv)
 
     FILE *out = fopen(argv[3], "wb");
     if (!out) { perror("out"); return 1; }
-    const int32_t nev = 1 + steps;
+    const char *snap = getenv("ENGINE_RUN_STATE");
+    state_fn ssave = (state_fn)dlsym(h, "waste_state_save");
+    state_fn sload = (state_fn)dlsym(h, "waste_state_load");
+    reset_fn sreset = (reset_fn)dlsym(h, "waste_state_reset");
+    if (snap && (!ssave || !sload || !sreset)) {
+        fprintf(stderr, "engine library lacks the state entry points\n");
+        return 2;
+    }
+    const int half = snap ? steps / 2 : -1;     /* decode steps before the snapshot */
+    const int32_t nev = 1 + steps + (snap ? 1 : 0);
     int32_t vocab32 = 0;
     fwrite(&nev, 4, 1, out);
     fwrite(&vocab32, 4, 1, out);           /* patched below */
     const float *lg = NULL;
     size_t vocab = 0;
-    int32_t tok = 0;
+    int32_t tok = 0, tok_saved = 0;
     for (int e = 0; e < nev; e++) {
-        st = e == 0 ? weval(ctx, prompt, (size_t)np, &lg, &vocab)
-                    : weval(ctx, &tok, 1, &lg, &vocab);
+        const int again = snap && e == 1 + half;   /* the prompt after the reset */
+        if (again) {
+            tok_saved = tok;
+            if (ssave(ctx, snap) != WASTE_OK) { fprintf(stderr, "state save failed\n"); return 1; }
+            sreset(ctx);
+        }
+        if (snap && e == 2 + half) {
+            if (sload(ctx, snap) != WASTE_OK) { fprintf(stderr, "state load failed\n"); return 1; }
+            tok = tok_saved;
+        }
+        st = (e == 0 || again) ? weval(ctx, prompt, (size_t)np, &lg, &vocab)
+                               : weval(ctx, &tok, 1, &lg, &vocab);
         if (st != WASTE_OK) {
             fprintf(stderr, "waste_eval %d: %d (%s)\n", e, (int)st,
                     detail && detail(ctx) ? detail(ctx) : "");

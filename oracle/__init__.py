@@ -92,6 +92,9 @@ def lib() -> C.CDLL:
         L.orc_vq4p_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P, P,
                                       C.c_int]
         L.orc_set_exact_math.argtypes = [C.c_int]
+        L.orc_kda_step.argtypes = [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]
+        L.orc_short_conv_step.argtypes = [C.c_int, C.c_int, P, P, P, P, P]
+        L.orc_rmsnorm_gated.argtypes = [C.c_int, P, P, P, C.c_float, P]
         L.orc_dotf.restype = C.c_float
         L.orc_dotf.argtypes = [P, P, C.c_int]
         L.orc_route.argtypes = [P, P, C.c_int, C.c_int, C.c_int, C.c_float, P, P]
@@ -179,6 +182,9 @@ def _bind_refh(R: C.CDLL) -> C.CDLL:
     R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
     R.waste_mvq_rows_f32.argtypes = [C.c_int, C.c_int, P]
     R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
+    R.waste_kda_step.argtypes = [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]
+    R.waste_short_conv_step.argtypes = [C.c_int, C.c_int, P, P, P, P, P]
+    R.waste_rmsnorm_gated.argtypes = [C.c_int, P, P, P, C.c_float, P]
     R.waste_situ_pair.restype = C.c_float
     R.waste_situ_pair.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
     return R
@@ -522,3 +528,58 @@ class exact_math:
     def __exit__(self, *exc):
         lib().orc_set_exact_math(0)
         return False
+
+
+# ---- KDA (src/kda.c) --------------------------------------------------------
+
+def _kda(fn, H, K, V, q, k, v, g, beta, S):
+    a = [np.ascontiguousarray(t, dtype=np.float32) for t in (q, k, v, g, beta)]
+    S2 = np.array(S, dtype=np.float32, copy=True, order="C")
+    o = np.empty(H * V, dtype=np.float32)
+    u = np.empty(V, dtype=np.float32)
+    fn(H, K, V, *[_p(t) for t in a], _p(S2), _p(o), _p(u))
+    return S2, o
+
+
+def kda_step(H, K, V, q, k, v, g, beta, S):
+    """One KDA decode step: returns (new state, o); S is not modified."""
+    return _kda(lib().orc_kda_step, H, K, V, q, k, v, g, beta, S)
+
+
+def ref_kda_step(H, K, V, q, k, v, g, beta, S):
+    """The compiled reference's waste_kda_step (src/kda.c:26-68)."""
+    return _kda(ref().waste_kda_step, H, K, V, q, k, v, g, beta, S)
+
+
+def _conv(fn, C_, KS, w, bias, ring, x):
+    ww = np.ascontiguousarray(w, dtype=np.float32)
+    bb = np.ascontiguousarray(bias, dtype=np.float32) if bias is not None else None
+    r2 = np.array(ring, dtype=np.float32, copy=True, order="C")
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(C_, dtype=np.float32)
+    fn(C_, KS, _p(ww), _p(bb), _p(r2), _p(xx), _p(y))
+    return r2, y
+
+
+def short_conv_step(C_, KS, w, bias, ring, x):
+    """Returns (new ring, y); ring is not modified."""
+    return _conv(lib().orc_short_conv_step, C_, KS, w, bias, ring, x)
+
+
+def ref_short_conv_step(C_, KS, w, bias, ring, x):
+    return _conv(ref().waste_short_conv_step, C_, KS, w, bias, ring, x)
+
+
+def _rg(fn, C_, x, gate, w, eps):
+    a = [np.ascontiguousarray(t, dtype=np.float32) for t in (x, gate, w)]
+    y = np.empty(C_, dtype=np.float32)
+    fn(C_, _p(a[0]), _p(a[1]), _p(a[2]), C.c_float(eps), _p(y))
+    return y
+
+
+def rmsnorm_gated(C_, x, gate, w, eps):
+    return _rg(lib().orc_rmsnorm_gated, C_, x, gate, w, eps)
+
+
+def ref_rmsnorm_gated(C_, x, gate, w, eps):
+    return _rg(ref().waste_rmsnorm_gated, C_, x, gate, w, eps)

@@ -580,3 +580,85 @@ int orc_moe_block(const orc_moe *L, int layer, const float *h, const float *norm
     free(resid);
     return rc;
 }
+
+/* ---- KDA (src/kda.c, the x86 scalar kernels; -ffp-contract=off keeps
+ * every a += b * c a rounded multiply then a rounded add) ---------------- */
+
+/* src/kda.c:19-24 l2_rnorm */
+static float orc_l2_rnorm(const float *x, int n)
+{
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s += x[i] * x[i];
+    return 1.0f / sqrtf(s + 1e-12f);
+}
+
+/* src/kda.c:26-68 waste_kda_step: per head, q and k L2-normalised (q also
+ * by K^-0.5); pass A decays the rows by exp(g) and forms u = S'^T k; the
+ * delta d = beta (v - u); pass B adds k d^T and forms o = S^T q. */
+void orc_kda_step(int H, int K, int V, const float *q, const float *k, const float *v,
+                  const float *g_log, const float *beta, float *S, float *o, float *u)
+{
+    const float qscale = 1.0f / sqrtf((float)K);
+    for (int h = 0; h < H; h++) {
+        const float *qh = q + (size_t)h * K, *kh = k + (size_t)h * K;
+        const float *vh = v + (size_t)h * V, *gh = g_log + (size_t)h * K;
+        float *Sh = S + (size_t)h * K * V, *oh = o + (size_t)h * V;
+        const float b = beta[h];
+        const float qn = orc_l2_rnorm(qh, K) * qscale;
+        const float kn = orc_l2_rnorm(kh, K);
+        memset(u, 0, (size_t)V * sizeof(float));
+        for (int kk = 0; kk < K; kk++) {
+            float *row = Sh + (size_t)kk * V;
+            const float d = orc_expf(gh[kk]);
+            const float kv = kh[kk] * kn;
+            for (int i = 0; i < V; i++) {
+                row[i] *= d;
+                u[i] += row[i] * kv;
+            }
+        }
+        for (int i = 0; i < V; i++) u[i] = b * (vh[i] - u[i]);
+        memset(oh, 0, (size_t)V * sizeof(float));
+        for (int kk = 0; kk < K; kk++) {
+            float *row = Sh + (size_t)kk * V;
+            const float kv = kh[kk] * kn;
+            const float qv = qh[kk] * qn;
+            for (int i = 0; i < V; i++) {
+                row[i] += u[i] * kv;
+                oh[i] += row[i] * qv;
+            }
+        }
+    }
+}
+
+/* src/kda.c:84-99 waste_short_conv_step: a causal depthwise conv over the
+ * ring of the previous KS-1 inputs (oldest first) and this one, the ring
+ * shifted, then SiLU. */
+void orc_short_conv_step(int C, int KS, const float *w, const float *bias, float *ring,
+                         const float *x, float *y)
+{
+    const int R = KS - 1;
+    for (int c = 0; c < C; c++) {
+        const float *wc = w + (size_t)c * KS;
+        float *rc = ring + (size_t)c * R;
+        float acc = bias ? bias[c] : 0.0f;
+        for (int j = 0; j < R; j++) acc += rc[j] * wc[j];
+        acc += x[c] * wc[R];
+        for (int j = 0; j + 1 < R; j++) rc[j] = rc[j + 1];
+        if (R > 0) rc[R - 1] = x[c];
+        y[c] = acc / (1.0f + orc_expf(-acc));
+    }
+}
+
+/* src/kda.c:101-111 waste_rmsnorm_gated: y = x * r * w * sigmoid(gate),
+ * r = 1 / sqrt(mean(x^2) + eps), the sum serial. */
+void orc_rmsnorm_gated(int C, const float *x, const float *gate, const float *weight, float eps,
+                       float *y)
+{
+    float s = 0.0f;
+    for (int i = 0; i < C; i++) s += x[i] * x[i];
+    const float r = 1.0f / sqrtf(s / (float)C + eps);
+    for (int i = 0; i < C; i++) {
+        const float g = 1.0f / (1.0f + orc_expf(-gate[i]));
+        y[i] = x[i] * r * weight[i] * g;
+    }
+}

@@ -34,6 +34,9 @@
  *   orc_rmsnorm        src/model.c:132-138     serial sum of squares, x*r*w
  *   orc_moe_block      src/model.c:3927-3945   h + moe_layer(rmsnorm(h)): the MoE
  *                                              half of a decoder layer
+ *   orc_kda_step       src/kda.c:26-68         Kimi Delta Attention decode step
+ *   orc_short_conv_step src/kda.c:84-99        causal depthwise conv + SiLU
+ *   orc_rmsnorm_gated  src/kda.c:101-111       rmsnorm times sigmoid(gate)
  *
  * Parity is pinned against the reference compiled from its own sources
  * (oracle/Makefile -> oracle/_ref/libwaste_ref.so); see tests/golden/.
@@ -133,6 +136,14 @@ void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps);
 int orc_moe_block(const orc_moe *L, int layer, const float *h, const float *norm_w,
                   float eps, float *h_out, int *idx_out, float *w_out, int fma);
 
+/* KDA: q, k, g_log [H][K]; v, o [H][V]; beta [H]; S [H][K][V] updated in
+ * place; u scratch of V floats. */
+void orc_kda_step(int H, int K, int V, const float *q, const float *k, const float *v,
+                  const float *g_log, const float *beta, float *S, float *o, float *u);
+void orc_short_conv_step(int C, int KS, const float *w, const float *bias, float *ring,
+                         const float *x, float *y);
+void orc_rmsnorm_gated(int C, const float *x, const float *gate, const float *weight,
+                       float eps, float *y);
 #ifdef __cplusplus
 }
 #endif

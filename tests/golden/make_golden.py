@@ -17,6 +17,7 @@ Every output here is produced by the reference's own code:
   2282) through the reference's AVX-512 slot and its portable (CPU) slot.
 * vq4p.npz, moe_vq4p*.npz — the VQ4P format (src/model.c:2026-2229): the
   matvec, its int8 tables, and VQ4P MoE layers.
+* kda.npz — the KDA kernels (src/kda.c:26-111) on seeded inputs.
 * moe_*.npz — moe_layer / moe_chunk (src/model.c:2713, 3512) on seeded
   layers built by warp_b200.synth; the inputs are regenerated from the seed
   (numpy PCG64, which is stable across numpy versions) and pinned by a
@@ -50,8 +51,10 @@ if REF_TREE is None:
     raise SystemExit("make_golden.py needs the reference tree: set WARP_REFERENCE")
 
 sys.path.insert(0, os.path.join(ROOT, "tests"))
-from golden_cases import (MOE_CASES, MVQ_CASES, NORM_SIZES, VQ4P_CASES,  # noqa: E402
-                          VQ4P_MOE_CASES, sha, vq4p_books, vq4p_case)  # shared with the tests
+from golden_cases import (CONV_C, CONV_KS, KDA_CASES, MOE_CASES, MVQ_CASES,  # noqa: E402
+                          NORM_DIM, NORM_HEADS, NORM_SIZES, VQ4P_CASES, VQ4P_MOE_CASES,
+                          conv_inputs, kda_inputs, norm_inputs, sha, vq4p_books,
+                          vq4p_case)  # shared with the tests
 
 
 def layer_sha(L) -> str:
@@ -170,6 +173,33 @@ def vq4p_fixtures():
     moe_fixtures(cases=VQ4P_MOE_CASES)
 
 
+def kda_fixture():
+    """The reference's KDA kernels (src/kda.c:26-111: waste_kda_step,
+    waste_short_conv_step, waste_rmsnorm_gated) on seeded inputs: the state
+    (by a sha256) and output after every step of each case, three conv steps
+    from a zero ring, and the gated norm of every head."""
+    res = {}
+    for name, (H, K, V, T) in KDA_CASES.items():
+        S = np.zeros((H, K, V), np.float32)
+        for t, (q, k, v, g, beta) in enumerate(kda_inputs(name)):
+            S, o = O.ref_kda_step(H, K, V, q, k, v, g, beta, S)
+            res[f"{name}_o{t}"] = o
+        res[f"{name}_S_sha"] = sha(S)      # the final state, pinned by its bytes
+    w, xs = conv_inputs()
+    ring = np.zeros((CONV_C, CONV_KS - 1), np.float32)
+    for t in range(xs.shape[0]):
+        ring, y = O.ref_short_conv_step(CONV_C, CONV_KS, w, None, ring, xs[t])
+        res[f"conv_y{t}"] = y
+    res["conv_ring"] = ring
+    x, gate, wn, eps = norm_inputs()
+    res["norm_y"] = np.concatenate([
+        O.ref_rmsnorm_gated(NORM_DIM, x[h * NORM_DIM:(h + 1) * NORM_DIM],
+                            gate[h * NORM_DIM:(h + 1) * NORM_DIM], wn, float(eps))
+        for h in range(NORM_HEADS)])
+    np.savez_compressed(os.path.join(OUT, "kda.npz"), **res)
+    print("kda.npz written")
+
+
 def tiny_container():
     """tests/golden/tiny_container/: the reference's own test container
     (tools/make_test_container.py, seed 0: a Kimi-Linear at 1/18 scale, 4
@@ -222,6 +252,7 @@ def main():
     tiny_container()
     mvq_fixture()
     vq4p_fixtures()
+    kda_fixture()
 
 
 if __name__ == "__main__":
@@ -235,5 +266,7 @@ if __name__ == "__main__":
         mvq_fixture()
     elif sys.argv[1:] == ["vq4p"]:
         vq4p_fixtures()
+    elif sys.argv[1:] == ["kda"]:
+        kda_fixture()
     else:
         main()

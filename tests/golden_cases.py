@@ -84,3 +84,42 @@ def rel_l2(a, b):
 
 def bits(a):
     return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+# KDA decode-step fixtures (kda.npz): name -> (H, K, V, steps); the state
+# starts at zero and runs `steps` tokens.
+KDA_CASES = {"kda_kimi": (32, 128, 128, 4), "kda_small": (4, 64, 64, 3)}
+CONV_C, CONV_KS = 4096, 4                     # one of q/k/v's short convs
+NORM_HEADS, NORM_DIM = 32, 128                # the gated o-norm, per head
+
+
+def kda_inputs(name):
+    """Seeded per-step inputs (q, k, v, g_log, beta) of a KDA fixture:
+    q, k, v N(0, 1); log decays -|N(0, 0.5)| (g <= 0, as the decay gate
+    gives); beta uniform (0, 1)."""
+    H, K, V, T = KDA_CASES[name]
+    rng = np.random.default_rng(len(name) * 131 + H)
+    steps = []
+    for _ in range(T):
+        q = rng.standard_normal(H * K, dtype=np.float32)
+        k = rng.standard_normal(H * K, dtype=np.float32)
+        v = rng.standard_normal(H * V, dtype=np.float32)
+        g = (-np.abs(rng.normal(0.0, 0.5, H * K))).astype(np.float32)
+        beta = rng.uniform(0.0, 1.0, H).astype(np.float32)
+        steps.append((q, k, v, g, beta))
+    return steps
+
+
+def conv_inputs():
+    rng = np.random.default_rng(808)
+    w = rng.normal(0.0, 0.5, (CONV_C, CONV_KS)).astype(np.float32)
+    xs = rng.standard_normal((3, CONV_C), dtype=np.float32)
+    return w, xs
+
+
+def norm_inputs():
+    rng = np.random.default_rng(809)
+    x = rng.standard_normal(NORM_HEADS * NORM_DIM, dtype=np.float32)
+    gate = rng.standard_normal(NORM_HEADS * NORM_DIM, dtype=np.float32)
+    w = rng.normal(1.0, 0.1, NORM_DIM).astype(np.float32)
+    return x, gate, w, np.float32(1e-6)

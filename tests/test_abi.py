@@ -85,3 +85,14 @@ def test_argument_checks_need_no_device(lib_path):
     assert lib.waste_cuda_codebooks_load(None, 1, 256, 8) == wb.E_ARG
     assert lib.waste_cuda_codebooks_load_f16(None, 1, 128, 8) == wb.E_ARG
     assert lib.waste_cuda_moe_experts(None) == wb.E_ARG
+
+
+def test_slot_table_layout_matches_header():
+    """The ctypes mirror of waste_vq_slots has the header's fields in order
+    (a shorter mirror would be overrun by waste_register_cuda_vq)."""
+    src = open(HEADER).read()
+    body = src[src.index("typedef struct {\n    int  (*codebooks_load)"):]
+    body = body[:body.index("} waste_vq_slots;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = re.findall(r"\(\*(\w+)\)", body)
+    assert [f[0] for f in wb.VqSlots._fields_] == fields

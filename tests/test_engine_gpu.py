@@ -87,3 +87,43 @@ def test_engine_moe_layer_and_chunk_through_slots(cuda_lib, act):
     finally:
         cu.close()
         ref.close()
+
+
+def test_engine_kda_on_device(tmp_path):
+    """The reference's test container has KDA layers (4 heads of 32): with
+    the kda_step slot (on by default) and the conv and gated-norm slots
+    switched on, the decoder's linear attention runs on the device — its
+    recurrent state and conv rings held in HBM across tokens — and the
+    tokens and logits still match the reference's."""
+    _, _, tok_ref, lg_ref = run_engine(REF_ENGINE, tmp_path, "ref")
+    _, l_off, tok_off, _ = run_engine(CUDA_ENGINE, tmp_path, "kda_off", env={"WASTE_CUDA_KDA": "0"})
+    b_cu, launches, tok_cu, lg_cu = run_engine(
+        CUDA_ENGINE, tmp_path, "kda_all",
+        env={"WASTE_CUDA_KDA_CONV": "1", "WASTE_CUDA_KDA_NORM": "1"})
+    assert "CUDA sm_100a" in b_cu
+    # 3 KDA layers x (1 step + 3 convs + 1 norm) launches per decode step, at least
+    assert launches >= l_off + 3 * 5 * (len(tok_ref) - 1)
+    assert np.array_equal(tok_ref, tok_off)
+    assert np.array_equal(tok_ref, tok_cu)
+    worst = max(rel_l2(lg_cu[e], lg_ref[e]) for e in range(len(tok_ref)))
+    assert worst < 1e-4, worst
+
+
+def test_engine_snapshot_with_state_on_device(tmp_path):
+    """waste_state_save / waste_state_reset / waste_state_load with the KDA
+    state and conv rings in HBM: the patched engine pulls them before the
+    save and pushes them after the reset and the load, so the prompt after
+    the reset repeats eval 0 bit for bit, and the decode after the load
+    repeats the uninterrupted run's, in both engines."""
+    env = {"WASTE_CUDA_KDA_CONV": "1", "WASTE_CUDA_KDA_NORM": "1"}
+    from test_engine import STEPS
+    half = STEPS // 2
+    for lib, tag in ((REF_ENGINE, "ref"), (CUDA_ENGINE, "cuda")):
+        _, _, tok_u, lg_u = run_engine(lib, tmp_path, tag + "_u", env=env)
+        _, _, tok_s, lg_s = run_engine(
+            lib, tmp_path, tag + "_s",
+            env=dict(env, ENGINE_RUN_STATE=str(tmp_path / f"{tag}.state")))
+        assert len(tok_s) == len(tok_u) + 1
+        assert np.array_equal(lg_s[1 + half].view(np.uint32), lg_u[0].view(np.uint32))
+        assert np.array_equal(lg_s[2 + half:].view(np.uint32), lg_u[1 + half:].view(np.uint32))
+        assert np.array_equal(lg_s[:1 + half].view(np.uint32), lg_u[:1 + half].view(np.uint32))

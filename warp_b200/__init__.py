@@ -37,7 +37,9 @@ EXPORTS = (
     "waste_cuda_moe_activation", "waste_cuda_mvq_rows_dev", "waste_cuda_release_host_buffers",
     "waste_cuda_vq_sel_bytes", "waste_cuda_vq_sel_build_dev", "waste_cuda_vq_matvec_sel_dev",
     "waste_cuda_vq_bank_load_file", "waste_cuda_vq4p_matvec", "waste_cuda_vq4p_matvec_dev",
-    "waste_cuda_vq4p_table",
+    "waste_cuda_vq4p_table", "waste_cuda_kda_step", "waste_cuda_short_conv_step",
+    "waste_cuda_rmsnorm_gated_heads", "waste_cuda_state_push", "waste_cuda_state_pull",
+    "waste_cuda_kda_step_dev", "waste_cuda_short_conv_dev", "waste_cuda_rmsnorm_gated_dev",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -74,7 +76,9 @@ class VqSlots(C.Structure):
     """waste_vq_slots: the expert-path slots next to waste_kernels."""
     _fields_ = [("codebooks_load", C.c_void_p), ("vq_bank_load", C.c_void_p),
                 ("vq_bank_free", C.c_void_p), ("moe_experts", C.c_void_p),
-                ("moe_chunk_experts", C.c_void_p), ("vq_bank_load_file", C.c_void_p)]
+                ("moe_chunk_experts", C.c_void_p), ("vq_bank_load_file", C.c_void_p),
+                ("state_push", C.c_void_p), ("state_pull", C.c_void_p),
+                ("rmsnorm_gated_heads", C.c_void_p)]
 
 
 _lib = None
@@ -156,6 +160,14 @@ def load_library() -> C.CDLL:
         "waste_cuda_vq4p_matvec_dev": (C.c_int, [C.c_int, P, P, P, P, C.c_int, C.c_int,
                                                  C.c_int, P]),
         "waste_cuda_vq4p_table": (C.c_int, [P, P, P, C.c_int, C.c_int]),
+        "waste_cuda_kda_step": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P]),
+        "waste_cuda_short_conv_step": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P]),
+        "waste_cuda_rmsnorm_gated_heads": (C.c_int, [C.c_int, C.c_int, P, P, P, C.c_float, P]),
+        "waste_cuda_state_push": (C.c_int, [P, C.c_size_t]),
+        "waste_cuda_state_pull": (C.c_int, [P, C.c_size_t]),
+        "waste_cuda_kda_step_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]),
+        "waste_cuda_short_conv_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P, P]),
+        "waste_cuda_rmsnorm_gated_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, C.c_float, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -509,3 +521,67 @@ def vq4p_table(x, cb_base: int):
     qs = np.empty((nv + 31) // 32, dtype=np.float32)
     _check(load_library().waste_cuda_vq4p_table(_ptr(q), _ptr(qs), _ptr(xx), xx.size, cb_base))
     return q, qs
+
+# ---- KDA ----------------------------------------------------------------------
+
+def kda_step(H: int, K: int, V: int, q, k, v, g_log, beta, S: np.ndarray) -> np.ndarray:
+    """One decode step (the kda_step slot): S, a float32 array the caller
+    keeps, is held in HBM from the first call on (its host bytes are stale
+    until state_pull). Returns o [H*V]."""
+    a = [_f32(t) for t in (q, k, v, g_log, beta)]
+    assert S.dtype == np.float32 and S.flags.c_contiguous
+    o = np.empty(H * V, dtype=np.float32)
+    _check(load_library().waste_cuda_kda_step(H, K, V, *[_ptr(t) for t in a], _ptr(S), _ptr(o)))
+    return o
+
+
+def short_conv_step(C_: int, KS: int, w, bias, ring: np.ndarray, x) -> np.ndarray:
+    """The short_conv_step slot: ring (float32, caller-kept) held in HBM."""
+    ww = _f32(w)
+    assert ring.dtype == np.float32 and ring.flags.c_contiguous
+    bb = _f32(bias) if bias is not None else None
+    xx = _f32(x)
+    y = np.empty(C_, dtype=np.float32)
+    _check(load_library().waste_cuda_short_conv_step(C_, KS, _ptr(ww), _ptr(bb) if bb is not None
+                                                     else None, _ptr(ring), _ptr(xx), _ptr(y)))
+    return y
+
+
+def rmsnorm_gated_heads(nh: int, C_: int, x, gate, w, eps: float) -> np.ndarray:
+    xx, gg, ww = _f32(x), _f32(gate), _f32(w)
+    y = np.empty(nh * C_, dtype=np.float32)
+    _check(load_library().waste_cuda_rmsnorm_gated_heads(nh, C_, _ptr(xx), _ptr(gg), _ptr(ww),
+                                                         C.c_float(eps), _ptr(y)))
+    return y
+
+
+def state_pull(a: np.ndarray):
+    _check(load_library().waste_cuda_state_pull(_ptr(a), a.nbytes))
+
+
+def state_push(a: np.ndarray):
+    _check(load_library().waste_cuda_state_push(_ptr(a), a.nbytes))
+
+
+def kda_step_dev(H, K, V, d_q, d_k, d_v, d_g, d_beta, d_S, d_o, stream: int = 0):
+    v = lambda p: C.c_void_p(int(p)) if p else None
+    _check(load_library().waste_cuda_kda_step_dev(H, K, V, v(d_q), v(d_k), v(d_v), v(d_g),
+                                                  v(d_beta), v(d_S), v(d_o), v(stream)))
+
+
+def short_conv_dev(C_, KS, d_w, d_bias, d_ring, d_x, d_y, stream: int = 0):
+    v = lambda p: C.c_void_p(int(p)) if p else None
+    _check(load_library().waste_cuda_short_conv_dev(C_, KS, v(d_w), v(d_bias), v(d_ring), v(d_x),
+                                                    v(d_y), v(stream)))
+
+
+def rmsnorm_gated_dev(nh, C_, d_x, d_gate, d_w, eps, d_y, stream: int = 0):
+    v = lambda p: C.c_void_p(int(p)) if p else None
+    _check(load_library().waste_cuda_rmsnorm_gated_dev(nh, C_, v(d_x), v(d_gate), v(d_w),
+                                                       C.c_float(eps), v(d_y), v(stream)))
+
+
+def release_host_buffers():
+    """Drop every device copy keyed by a host address (trunk mirrors, KDA
+    state and weights): what the engine calls before freeing a model."""
+    load_library().waste_cuda_release_host_buffers()

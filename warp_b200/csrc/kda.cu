@@ -1,0 +1,180 @@
+/*
+ * kda.cu — Kimi Delta Attention's decode-time kernels on sm_100a: the
+ * kda_step, short_conv_step and rmsnorm_gated slots of the reference's
+ * dispatch table (src/waste_backend.h:69-76; arithmetic src/kda.c:19-111).
+ *
+ *   kda_step       per head: q, k L2-normalised (q also by K^-0.5); the state
+ *                  rows decayed by exp(g) and u = S'^T k (pass A); the delta
+ *                  d = beta (v - u); S += k d^T and o = S^T q (pass B)
+ *   short_conv     per channel: a causal depthwise conv over a ring of the
+ *                  previous KS-1 inputs, the ring shifted, then SiLU
+ *   rmsnorm_gated  per head: x * r * w * sigmoid(gate), r = 1/sqrt(mean x^2 + eps)
+ *
+ * B200 mapping. The recurrent state (K x V floats a head, 64 KB at 128 x 128)
+ * stays in HBM between tokens. One warp per (head, 32 columns), lane l
+ * owning one column of the head's state: the column is read once, decayed
+ * and reduced into u (pass A) while it is staged in shared memory, then
+ * updated, reduced into o and written once (pass B) — the state crosses
+ * HBM twice a token (a read and a write, 128-byte row segments), where the
+ * CPU streams it through cache four times. kv = k*kn and qv = q*qn are
+ * recomputed per use, which gives the same floats as the CPU's.
+ *
+ * Arithmetic follows the reference's x86 build term for term (rounded
+ * multiply, then rounded add: no contraction), the serial sums in the same
+ * order, sqrtf and the divisions IEEE, and exp rounded once (expf_cr), so
+ * the device matches the CPU bit for bit except where glibc's expf is not
+ * correctly rounded (a few inputs in 10^4).
+ */
+#include "vq3r_common.cuh"
+#include "wc_launch.h"
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+using namespace wc;
+
+namespace {
+
+/* src/kda.c:19-24: serial sum of squares, 1 / sqrtf(s + 1e-12). */
+__device__ __forceinline__ float l2_rnorm_serial(const float *x, int n)
+{
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s, 1e-12f)));
+}
+
+/* grid (H, ceil(V/32)), one warp: lane l owns column c = 32*blockIdx.y + l
+ * of head blockIdx.x, staged in shared memory between the two passes. */
+template <int K>
+__global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__restrict__ q,
+                                                      const float *__restrict__ k,
+                                                      const float *__restrict__ v,
+                                                      const float *__restrict__ g_log,
+                                                      const float *__restrict__ beta, float *S,
+                                                      float *__restrict__ o)
+{
+    __shared__ float qs[K], ks[K], dec[K];
+    __shared__ float col[K][32];
+    __shared__ float norms[2];
+    const int h = blockIdx.x, lane = threadIdx.x;
+    const int c = blockIdx.y * 32 + lane;
+    for (int i = lane; i < K; i += 32) {
+        qs[i] = q[(size_t)h * K + i];
+        ks[i] = k[(size_t)h * K + i];
+        dec[i] = expf_cr(g_log[(size_t)h * K + i]);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)K));
+        norms[0] = __fmul_rn(l2_rnorm_serial(qs, K), qscale);
+    } else if (lane == 16) {
+        norms[1] = l2_rnorm_serial(ks, K);
+    }
+    __syncwarp();
+    const float qn = norms[0], kn = norms[1];
+    if (c >= V) return;
+    float *Sc = S + (size_t)h * K * V + c;
+    float u = 0.0f;
+#pragma unroll 8
+    for (int kk = 0; kk < K; kk++) {
+        const float r = __fmul_rn(Sc[(size_t)kk * V], dec[kk]);
+        col[kk][lane] = r;
+        u = __fadd_rn(u, __fmul_rn(r, __fmul_rn(ks[kk], kn)));
+    }
+    const float d = __fmul_rn(beta[h], __fsub_rn(v[(size_t)h * V + c], u));
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int kk = 0; kk < K; kk++) {
+        const float r = __fadd_rn(col[kk][lane], __fmul_rn(d, __fmul_rn(ks[kk], kn)));
+        acc = __fadd_rn(acc, __fmul_rn(r, __fmul_rn(qs[kk], qn)));
+        Sc[(size_t)kk * V] = r;
+    }
+    o[(size_t)h * V + c] = acc;
+}
+
+__global__ void __launch_bounds__(256) short_conv_kernel(int C, int KS, const float *__restrict__ w,
+                                                         const float *__restrict__ bias,
+                                                         float *ring, const float *x, float *y)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const int R = KS - 1;
+    const float *wc = w + (size_t)c * KS;
+    float *rc = ring + (size_t)c * R;
+    const float xc = x[c];
+    float acc = bias ? bias[c] : 0.0f;
+    for (int j = 0; j < R; j++) acc = __fadd_rn(acc, __fmul_rn(rc[j], wc[j]));
+    acc = __fadd_rn(acc, __fmul_rn(xc, wc[R]));
+    for (int j = 0; j + 1 < R; j++) rc[j] = rc[j + 1];
+    if (R > 0) rc[R - 1] = xc;
+    y[c] = __fdiv_rn(acc, __fadd_rn(1.0f, expf_cr(-acc)));
+}
+
+/* nh heads of C channels, one CTA each (one weight vector for all). */
+__global__ void __launch_bounds__(128) rmsnorm_gated_kernel(int C, const float *x, const float *gate,
+                                                            const float *__restrict__ weight,
+                                                            float eps, float *y)
+{
+    extern __shared__ float xs[];
+    __shared__ float rr;
+    const size_t base = (size_t)blockIdx.x * C;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) xs[i] = x[base + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < C; i++) s = __fadd_rn(s, __fmul_rn(xs[i], xs[i]));
+        rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)C), eps)));
+    }
+    __syncthreads();
+    const float r = rr;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+        const float g = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-gate[base + i])));
+        y[base + i] = __fmul_rn(__fmul_rn(__fmul_rn(xs[i], r), weight[i]), g);
+    }
+}
+
+} /* namespace */
+
+extern "C" {
+
+int wc_kda_supported(int K, int V)
+{
+    return (K == 128 || K == 64 || K == 32) && V > 0 ? 0 : -1;
+}
+
+int wc_kda_step_launch(int H, int K, int V, const float *q, const float *k, const float *v,
+                       const float *g_log, const float *beta, float *S, float *o, void *stream)
+{
+    cudaStream_t st = (cudaStream_t)stream;
+    const dim3 grid(H, (V + 31) / 32);
+    if (K == 128)
+        kda_step_kernel<128><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+    else if (K == 64)
+        kda_step_kernel<64><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+    else if (K == 32)
+        kda_step_kernel<32><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+    else
+        return (int)cudaErrorInvalidValue;
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float *ring,
+                         const float *x, float *y, void *stream)
+{
+    short_conv_kernel<<<(C + 255) / 256, 256, 0, (cudaStream_t)stream>>>(C, KS, w, bias, ring, x,
+                                                                          y);
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
+                            float eps, float *y, void *stream)
+{
+    rmsnorm_gated_kernel<<<nh, 128, (size_t)C * sizeof(float), (cudaStream_t)stream>>>(
+        C, x, gate, weight, eps, y);
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+} /* extern "C" */

@@ -168,6 +168,24 @@ static struct {
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static void ep_shutdown_locked(void);
 static void mirrors_free(void);
+/* the engine's KDA slot signatures (src/waste_backend.h:69-76) */
+typedef void (*wc_kda_fn)(int H, int K, int V, const float *q, const float *k, const float *v,
+                          const float *g_log, const float *beta, float *S, float *o,
+                          float *scratch);
+typedef void (*wc_conv_fn)(int C, int KS, const float *w, const float *bias, float *ring,
+                           const float *x, float *y);
+typedef void (*wc_rmsg_fn)(int C, const float *x, const float *gate, const float *weight,
+                           float eps, float *y);
+static void states_free(void);
+static void kda_slot(int H, int K, int V, const float *q, const float *k, const float *v,
+                     const float *g_log, const float *beta, float *S, float *o, float *scratch);
+static void conv_slot(int C, int KS, const float *w, const float *bias, float *ring,
+                      const float *x, float *y);
+static void rmsg_slot(int C, const float *x, const float *gate, const float *weight, float eps,
+                      float *y);
+static wc_kda_fn g_kda_cpu;
+static wc_conv_fn g_conv_cpu;
+static wc_rmsg_fn g_rmsg_cpu;
 static int pf_wanted(const wc_layer *L, int T, int K);
 static int p6_experts(const wc_layer *L, int T, int K, int act, float situ_beta,
                       float situ_lbeta, int order_by_id);
@@ -372,6 +390,7 @@ void waste_cuda_shutdown(void)
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
         cudaFree(S.d_p6);
         mirrors_free();
+        states_free();
         for (int b = 0; b < 2; b++) {
             cudaFreeHost(g_stage.buf[b]);
             if (g_stage.ev) cudaEventDestroy(g_stage.done[b]);
@@ -392,9 +411,9 @@ void waste_cuda_shutdown(void)
  * the slot is called with a pointer to the table at registration and with
  * a pointer to the argument on every trunk matvec. */
 typedef struct {
-    void (*kda_step)(void);
-    void (*short_conv_step)(void);
-    void (*rmsnorm_gated)(void);
+    wc_kda_fn kda_step;
+    wc_conv_fn short_conv_step;
+    wc_rmsg_fn rmsnorm_gated;
     void (*mvq_rows_f32)(int b, int e, void *arg);
     void (*lutb_range)(int lo, int hi, void *arg);
     int on_device;
@@ -557,6 +576,22 @@ const char *waste_register_cuda(void *table)
         t->mvq_rows_f32 = mvq_slot;
         t->on_device = 1;
     }
+    /* KDA: the decode step (recurrent state kept in HBM) by default; the
+     * conv and the gated norm on request, since each of their calls is a
+     * few KB whose host round trip costs more than the CPU's arithmetic */
+    if (t && t->kda_step && getenv_flag("WASTE_CUDA_KDA", 1)) {
+        if (t->kda_step != kda_slot) g_kda_cpu = t->kda_step;
+        t->kda_step = kda_slot;
+        t->on_device = 1;
+    }
+    if (t && t->short_conv_step && getenv_flag("WASTE_CUDA_KDA_CONV", 0)) {
+        if (t->short_conv_step != conv_slot) g_conv_cpu = t->short_conv_step;
+        t->short_conv_step = conv_slot;
+    }
+    if (t && t->rmsnorm_gated && getenv_flag("WASTE_CUDA_KDA_NORM", 0)) {
+        if (t->rmsnorm_gated != rmsg_slot) g_rmsg_cpu = t->rmsnorm_gated;
+        t->rmsnorm_gated = rmsg_slot;
+    }
     return S.name;
 }
 
@@ -566,9 +601,304 @@ void waste_cuda_release_host_buffers(void)
     if (S.inited) {
         cudaStreamSynchronize(S.stream);
         mirrors_free();
+        states_free();
     }
     pthread_mutex_unlock(&g_mu);
 }
+
+/* ---- KDA: recurrent state resident in HBM -----------------------------
+ * The engine's KDA state (m->S[L], [H][K][V]) and conv rings (m->conv[L])
+ * move to HBM the first time a slot sees them, keyed by host address, as
+ * do the conv and norm weights; from then on the device copy is the state
+ * and the host copy is stale. waste_cuda_state_pull brings a range back to
+ * the host (before the engine reads it: a snapshot save) and
+ * waste_cuda_state_push reloads it from the host (after the engine writes
+ * it: a reset, a snapshot load). */
+#define WC_STATES 1024
+static struct {
+    const uint8_t *host;
+    size_t bytes;
+    uint8_t *dev;
+} g_rs[WC_STATES];
+static int g_nrs;
+static float *g_kda_pin, *g_kda_dev;     /* pinned and device staging, floats */
+static size_t g_kda_cap;
+
+/* The device address of host range [h, h + bytes): inside a held copy, or
+ * a copy made now from the host bytes. NULL when it partly overlaps a held
+ * copy or cannot be made. Under g_mu. */
+static void *rs_get(const void *h, size_t bytes)
+{
+    const uint8_t *p = (const uint8_t *)h;
+    for (int i = 0; i < g_nrs; i++)
+        if (p >= g_rs[i].host && p + bytes <= g_rs[i].host + g_rs[i].bytes)
+            return g_rs[i].dev + (p - g_rs[i].host);
+    for (int i = 0; i < g_nrs; i++)
+        if (p < g_rs[i].host + g_rs[i].bytes && g_rs[i].host < p + bytes) return NULL;
+    if (g_nrs == WC_STATES) return NULL;
+    uint8_t *d = NULL;
+    if (cudaMalloc((void **)&d, bytes) != cudaSuccess ||
+        cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(d);
+        cudaGetLastError();
+        return NULL;
+    }
+    g_rs[g_nrs].host = p;
+    g_rs[g_nrs].bytes = bytes;
+    g_rs[g_nrs].dev = d;
+    g_nrs++;
+    return d;
+}
+
+static void states_free(void)
+{
+    for (int i = 0; i < g_nrs; i++) cudaFree(g_rs[i].dev);
+    memset(g_rs, 0, sizeof g_rs);
+    g_nrs = 0;
+    cudaFreeHost(g_kda_pin);
+    cudaFree(g_kda_dev);
+    g_kda_pin = g_kda_dev = NULL;
+    g_kda_cap = 0;
+}
+
+/* Copies the parts of [h, h + bytes) held in HBM one way or the other. */
+static int rs_sync(const void *h, size_t bytes, int to_host)
+{
+    int rc = 0;
+    const uint8_t *p = (const uint8_t *)h;
+    for (int i = 0; i < g_nrs; i++) {
+        const uint8_t *lo = p > g_rs[i].host ? p : g_rs[i].host;
+        const uint8_t *e0 = p + bytes, *e1 = g_rs[i].host + g_rs[i].bytes;
+        const uint8_t *hi = e0 < e1 ? e0 : e1;
+        if (lo >= hi) continue;
+        uint8_t *d = g_rs[i].dev + (lo - g_rs[i].host);
+        if (to_host)
+            CK(cudaMemcpy((void *)lo, d, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "state D2H");
+        else
+            CK(cudaMemcpy(d, lo, (size_t)(hi - lo), cudaMemcpyHostToDevice), "state H2D");
+    }
+out:
+    return rc;
+}
+
+int waste_cuda_state_pull(void *host, size_t bytes)
+{
+    if (!host) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    int rc = 0;
+    if (S.inited) {
+        cudaStreamSynchronize(S.stream);
+        rc = rs_sync(host, bytes, 1);
+    }
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_state_push(const void *host, size_t bytes)
+{
+    if (!host) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    pthread_mutex_lock(&g_mu);
+    int rc = 0;
+    if (S.inited) {
+        cudaStreamSynchronize(S.stream);
+        rc = rs_sync(host, bytes, 0);
+    }
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+static int kda_stage(size_t floats)
+{
+    if (floats <= g_kda_cap) return 0;
+    cudaFreeHost(g_kda_pin);
+    cudaFree(g_kda_dev);
+    g_kda_pin = g_kda_dev = NULL;
+    g_kda_cap = 0;
+    if (cudaMallocHost((void **)&g_kda_pin, floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc((void **)&g_kda_dev, floats * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(WASTE_CUDA_E_NOMEM, "KDA staging");
+    }
+    g_kda_cap = floats;
+    return 0;
+}
+
+int waste_cuda_kda_step(int H, int K, int V, const float *q, const float *k, const float *v,
+                        const float *g_log, const float *beta, float *S_, float *o)
+{
+    int rc = 0;
+    if (H <= 0 || !q || !k || !v || !g_log || !beta || !S_ || !o || wc_kda_supported(K, V))
+        return fail(WASTE_CUDA_E_ARG, "kda_step: bad arguments (K 32, 64 or 128)");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    float *dS = (float *)rs_get(S_, (size_t)H * K * V * sizeof(float));
+    if (!dS) { rc = fail(WASTE_CUDA_E_NOMEM, "kda_step: state copy"); goto out; }
+    const size_t hk = (size_t)H * K, hv = (size_t)H * V, n_in = 3 * hk + hv + H;
+    if ((rc = kda_stage(n_in + hv))) goto out;
+    float *p = g_kda_pin;
+    memcpy(p, q, hk * 4);
+    memcpy(p + hk, k, hk * 4);
+    memcpy(p + 2 * hk, g_log, hk * 4);
+    memcpy(p + 3 * hk, v, hv * 4);
+    memcpy(p + 3 * hk + hv, beta, (size_t)H * 4);
+    float *d = g_kda_dev;
+    CK(cudaMemcpyAsync(d, p, n_in * 4, cudaMemcpyHostToDevice, S.stream), "KDA inputs H2D");
+    CK((cudaError_t)wc_kda_step_launch(H, K, V, d, d + hk, d + 3 * hk, d + 2 * hk,
+                                       d + 3 * hk + hv, dS, d + n_in, S.stream), "KDA step");
+    CK(cudaMemcpyAsync(p + n_in, d + n_in, hv * 4, cudaMemcpyDeviceToHost, S.stream), "o D2H");
+    CK(cudaStreamSynchronize(S.stream), "KDA step");
+    memcpy(o, p + n_in, hv * 4);
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_short_conv_step(int C, int KS, const float *w, const float *bias, float *ring,
+                               const float *x, float *y)
+{
+    int rc = 0;
+    if (C <= 0 || KS < 1 || !w || !ring || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "short_conv_step: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    float *dr = KS > 1 ? (float *)rs_get(ring, (size_t)C * (KS - 1) * sizeof(float)) : NULL;
+    float *dw = (float *)rs_get(w, (size_t)C * KS * sizeof(float));
+    float *db = bias ? (float *)rs_get(bias, (size_t)C * sizeof(float)) : NULL;
+    if ((KS > 1 && !dr) || !dw || (bias && !db)) {
+        rc = fail(WASTE_CUDA_E_NOMEM, "short_conv_step: device copies");
+        goto out;
+    }
+    if ((rc = kda_stage(2 * (size_t)C))) goto out;
+    memcpy(g_kda_pin, x, (size_t)C * 4);
+    CK(cudaMemcpyAsync(g_kda_dev, g_kda_pin, (size_t)C * 4, cudaMemcpyHostToDevice, S.stream),
+       "conv x H2D");
+    CK((cudaError_t)wc_short_conv_launch(C, KS, dw, db, dr, g_kda_dev, g_kda_dev + C, S.stream),
+       "short conv");
+    CK(cudaMemcpyAsync(g_kda_pin + C, g_kda_dev + C, (size_t)C * 4, cudaMemcpyDeviceToHost,
+                       S.stream), "conv y D2H");
+    CK(cudaStreamSynchronize(S.stream), "short conv");
+    memcpy(y, g_kda_pin + C, (size_t)C * 4);
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_rmsnorm_gated_heads(int nh, int C, const float *x, const float *gate,
+                                   const float *weight, float eps, float *y)
+{
+    int rc = 0;
+    if (nh <= 0 || C <= 0 || C > 8192 || !x || !gate || !weight || !y)
+        return fail(WASTE_CUDA_E_ARG, "rmsnorm_gated: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    float *dw = (float *)rs_get(weight, (size_t)C * sizeof(float));
+    if (!dw) { rc = fail(WASTE_CUDA_E_NOMEM, "rmsnorm_gated: weight copy"); goto out; }
+    const size_t n = (size_t)nh * C;
+    if ((rc = kda_stage(3 * n))) goto out;
+    memcpy(g_kda_pin, x, n * 4);
+    memcpy(g_kda_pin + n, gate, n * 4);
+    CK(cudaMemcpyAsync(g_kda_dev, g_kda_pin, 2 * n * 4, cudaMemcpyHostToDevice, S.stream),
+       "norm inputs H2D");
+    CK((cudaError_t)wc_rmsnorm_gated_launch(nh, C, g_kda_dev, g_kda_dev + n, dw, eps,
+                                            g_kda_dev + 2 * n, S.stream), "gated norm");
+    CK(cudaMemcpyAsync(g_kda_pin + 2 * n, g_kda_dev + 2 * n, n * 4, cudaMemcpyDeviceToHost,
+                       S.stream), "norm y D2H");
+    CK(cudaStreamSynchronize(S.stream), "gated norm");
+    memcpy(y, g_kda_pin + 2 * n, n * 4);
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_kda_step_dev(int H, int K, int V, const float *q, const float *k, const float *v,
+                            const float *g_log, const float *beta, float *S_, float *o,
+                            void *stream)
+{
+    int rc = 0;
+    if (H <= 0 || !q || !k || !v || !g_log || !beta || !S_ || !o || wc_kda_supported(K, V))
+        return fail(WASTE_CUDA_E_ARG, "kda_step_dev: bad arguments (K 32, 64 or 128)");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "kda_step_dev before waste_cuda_init"); goto out; }
+    CK((cudaError_t)wc_kda_step_launch(H, K, V, q, k, v, g_log, beta, S_, o,
+                                       stream ? stream : (void *)S.stream), "KDA step");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_short_conv_dev(int C, int KS, const float *w, const float *bias, float *ring,
+                              const float *x, float *y, void *stream)
+{
+    int rc = 0;
+    if (C <= 0 || KS < 1 || !w || (KS > 1 && !ring) || !x || !y)
+        return fail(WASTE_CUDA_E_ARG, "short_conv_dev: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "short_conv_dev before waste_cuda_init"); goto out; }
+    CK((cudaError_t)wc_short_conv_launch(C, KS, w, bias, ring, x, y,
+                                         stream ? stream : (void *)S.stream), "short conv");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_rmsnorm_gated_dev(int nh, int C, const float *x, const float *gate,
+                                 const float *weight, float eps, float *y, void *stream)
+{
+    int rc = 0;
+    if (nh <= 0 || C <= 0 || C > 8192 || !x || !gate || !weight || !y)
+        return fail(WASTE_CUDA_E_ARG, "rmsnorm_gated_dev: bad arguments");
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "rmsnorm_gated_dev before waste_cuda_init"); goto out; }
+    CK((cudaError_t)wc_rmsnorm_gated_launch(nh, C, x, gate, weight, eps, y,
+                                            stream ? stream : (void *)S.stream), "gated norm");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* The slots: the device, or — when it cannot take the call — the CPU
+ * kernel the slot held before, on the host copy brought up to date first
+ * and pushed back after. */
+static void kda_slot(int H, int K, int V, const float *q, const float *k, const float *v,
+                     const float *g_log, const float *beta, float *S_, float *o, float *scratch)
+{
+    if (waste_cuda_kda_step(H, K, V, q, k, v, g_log, beta, S_, o) == 0) return;
+    const size_t b = (size_t)H * K * V * sizeof(float);
+    waste_cuda_state_pull(S_, b);
+    g_kda_cpu(H, K, V, q, k, v, g_log, beta, S_, o, scratch);
+    waste_cuda_state_push(S_, b);
+}
+
+static void conv_slot(int C, int KS, const float *w, const float *bias, float *ring,
+                      const float *x, float *y)
+{
+    if (waste_cuda_short_conv_step(C, KS, w, bias, ring, x, y) == 0) return;
+    const size_t b = (size_t)C * (KS > 1 ? KS - 1 : 0) * sizeof(float);
+    if (b) waste_cuda_state_pull(ring, b);
+    g_conv_cpu(C, KS, w, bias, ring, x, y);
+    if (b) waste_cuda_state_push(ring, b);
+}
+
+static void rmsg_slot(int C, const float *x, const float *gate, const float *weight, float eps,
+                      float *y)
+{
+    if (waste_cuda_rmsnorm_gated_heads(1, C, x, gate, weight, eps, y) == 0) return;
+    g_rmsg_cpu(C, x, gate, weight, eps, y);
+}
+
+/* The engine's per-layer loop of rmsnorm_gated over its heads as one call
+ * (a slot of waste_vq_slots, used when WASTE_CUDA_KDA_NORM is set). */
+static void rmsg_heads_slot(int nh, int C, const float *x, const float *gate,
+                            const float *weight, float eps, float *y)
+{
+    if (waste_cuda_rmsnorm_gated_heads(nh, C, x, gate, weight, eps, y) == 0) return;
+    for (int h = 0; h < nh; h++)
+        g_rmsg_cpu(C, x + (size_t)h * C, gate + (size_t)h * C, weight, eps, y + (size_t)h * C);
+}
+
+static void state_push_slot(const void *host, size_t bytes) { waste_cuda_state_push(host, bytes); }
+static void state_pull_slot(void *host, size_t bytes) { waste_cuda_state_pull(host, bytes); }
+
 
 int waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws, const float *d_x,
                             int r0, int r1, int in, int group, int bits, size_t rowbytes,
@@ -610,6 +940,9 @@ int waste_register_cuda_vq(waste_vq_slots *s)
     s->moe_experts = waste_cuda_moe_experts;
     s->moe_chunk_experts = waste_cuda_moe_chunk_experts;
     s->vq_bank_load_file = waste_cuda_vq_bank_load_file;
+    s->state_push = state_push_slot;
+    s->state_pull = state_pull_slot;
+    if (g_rmsg_cpu && getenv_flag("WASTE_CUDA_KDA_NORM", 0)) s->rmsnorm_gated_heads = rmsg_heads_slot;
     return 0;
 }
 

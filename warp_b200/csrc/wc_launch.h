@@ -235,6 +235,15 @@ int    wc_p6_moe_launch(const wc_p6_args *a, void *stream);
 int    wc_p6_table_launch(int8_t *q, float *qs, const float *x, const float *books, int cb,
                           int nv, void *stream);
 
+/* KDA (kda.cu): decode step, causal conv, gated rmsnorm (src/kda.c). */
+int wc_kda_supported(int K, int V);
+int wc_kda_step_launch(int H, int K, int V, const float *q, const float *k, const float *v,
+                       const float *g_log, const float *beta, float *S, float *o, void *stream);
+int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float *ring,
+                         const float *x, float *y, void *stream);
+int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
+                            float eps, float *y, void *stream);
+
 int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
                    int nv, int stages, void *stream);
 int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *scale,
