@@ -32,6 +32,9 @@
  *                                src/waste_backend.h:69-72)
  *   waste_cuda_short_conv_*      src/kda.c:84-99 (slot short_conv_step)
  *   waste_cuda_rmsnorm_gated_*   src/kda.c:101-111 (slot rmsnorm_gated)
+ *   waste_cuda_vq_encode(_dev)   src/vq.c:50-105 waste_vq_encode (the converter's
+ *                                RVQ encoder, tools/convert.py:349-363)
+ *   waste_cuda_vq_lloyd(_dev)    src/vq.c:107-136 waste_vq_lloyd
  *   waste_cuda_moe_block(_dev)   src/model.c:3927-3945 the MoE half of a
  *                                decoder layer: rmsnorm (:132-138), moe_layer,
  *                                residual add
@@ -484,6 +487,27 @@ int waste_cuda_short_conv_dev(int C, int KS, const float *w, const float *bias,
                               float *ring, const float *x, float *y, void *stream);
 int waste_cuda_rmsnorm_gated_dev(int nh, int C, const float *x, const float *gate,
                                  const float *weight, float eps, float *y, void *stream);
+
+/* ---- the converter's residual-VQ encoder ----------------------------------
+ * vq_encode: for each of n vectors X[n][dim] and each stage s, the index of
+ * the entry of books[s] ([stages][entries][dim]) nearest to the residual
+ * (squared Euclidean distance summed in dim order; the first index wins a
+ * tie), written to out[n][stages], then subtracted — src/vq.c:50-105,
+ * bit for bit. vq_lloyd: one Lloyd iteration of C [entries][dim] over X:
+ * assign, then each non-empty cluster's centroid becomes the double sum of
+ * its members in vector order over their count, rounded to float (empty
+ * clusters keep theirs) — src/vq.c:107-136, bit for bit; returns the number
+ * of non-empty clusters (host form) or writes it to *d_live (device form).
+ * entries 1..256, dim 1..64, stages * entries * dim * 4 bytes <= 227 KB.
+ * The host forms take the converter's buffers (its nthreads argument has
+ * no counterpart); the _dev forms take device pointers and `stream`. */
+int waste_cuda_vq_encode(const float *X, int n, const float *books, int stages,
+                         int entries, int dim, uint8_t *out);
+int waste_cuda_vq_encode_dev(const float *X, int n, const float *books, int stages,
+                             int entries, int dim, uint8_t *out, void *stream);
+int waste_cuda_vq_lloyd(const float *X, int n, float *C, int entries, int dim);
+int waste_cuda_vq_lloyd_dev(const float *X, int n, float *C, int entries, int dim,
+                            int *d_live, void *stream);
 
 /* ---- the trunk matvec (the mvq_rows_f32 slot) ---------------------------
  * src/model.c:265-320 waste_mvq_rows_f32 on the device: y[r] for r in

@@ -92,6 +92,9 @@ def lib() -> C.CDLL:
         L.orc_vq4p_matvec.argtypes = [P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P, P,
                                       C.c_int]
         L.orc_set_exact_math.argtypes = [C.c_int]
+        L.orc_vq_encode.argtypes = [P, C.c_int, P, C.c_int, C.c_int, C.c_int, P]
+        L.orc_vq_lloyd.restype = C.c_int
+        L.orc_vq_lloyd.argtypes = [P, C.c_int, P, C.c_int, C.c_int]
         L.orc_kda_step.argtypes = [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]
         L.orc_short_conv_step.argtypes = [C.c_int, C.c_int, P, P, P, P, P]
         L.orc_rmsnorm_gated.argtypes = [C.c_int, P, P, P, C.c_float, P]
@@ -182,6 +185,9 @@ def _bind_refh(R: C.CDLL) -> C.CDLL:
     R.waste_rmsnorm.argtypes = [P, P, P, C.c_int, C.c_float]
     R.waste_mvq_rows_f32.argtypes = [C.c_int, C.c_int, P]
     R.refh_moe_set_act.argtypes = [P, C.c_int, C.c_float, C.c_float]
+    R.waste_vq_encode.argtypes = [P, C.c_int, P, C.c_int, C.c_int, C.c_int, P, C.c_int]
+    R.waste_vq_lloyd.restype = C.c_int
+    R.waste_vq_lloyd.argtypes = [P, C.c_int, P, C.c_int, C.c_int, C.c_int]
     R.waste_kda_step.argtypes = [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]
     R.waste_short_conv_step.argtypes = [C.c_int, C.c_int, P, P, P, P, P]
     R.waste_rmsnorm_gated.argtypes = [C.c_int, P, P, P, C.c_float, P]
@@ -583,3 +589,40 @@ def rmsnorm_gated(C_, x, gate, w, eps):
 
 def ref_rmsnorm_gated(C_, x, gate, w, eps):
     return _rg(ref().waste_rmsnorm_gated, C_, x, gate, w, eps)
+
+
+# ---- the converter's RVQ encoder (src/vq.c) --------------------------------------
+
+def vq_encode(X, books):
+    """X [n][dim], books [stages][entries][dim] -> codes [n][stages]."""
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    bb = np.ascontiguousarray(books, dtype=np.float32)
+    out = np.empty((xx.shape[0], bb.shape[0]), dtype=np.uint8)
+    lib().orc_vq_encode(_p(xx), xx.shape[0], _p(bb), bb.shape[0], bb.shape[1], xx.shape[1],
+                        _p(out))
+    return out
+
+
+def ref_vq_encode(X, books, threads=0):
+    """The compiled reference's waste_vq_encode (its thread pool)."""
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    bb = np.ascontiguousarray(books, dtype=np.float32)
+    out = np.empty((xx.shape[0], bb.shape[0]), dtype=np.uint8)
+    ref().waste_vq_encode(_p(xx), xx.shape[0], _p(bb), bb.shape[0], bb.shape[1], xx.shape[1],
+                          _p(out), threads)
+    return out
+
+
+def vq_lloyd(X, C):
+    """(new centroids, non-empty clusters)."""
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    cc = np.array(C, dtype=np.float32, copy=True, order="C")
+    live = lib().orc_vq_lloyd(_p(xx), xx.shape[0], _p(cc), cc.shape[0], cc.shape[1])
+    return cc, live
+
+
+def ref_vq_lloyd(X, C, threads=0):
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    cc = np.array(C, dtype=np.float32, copy=True, order="C")
+    live = ref().waste_vq_lloyd(_p(xx), xx.shape[0], _p(cc), cc.shape[0], cc.shape[1], threads)
+    return cc, live

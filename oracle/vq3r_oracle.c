@@ -662,3 +662,68 @@ void orc_rmsnorm_gated(int C, const float *x, const float *gate, const float *we
         y[i] = x[i] * r * weight[i] * g;
     }
 }
+
+/* ---- the converter's RVQ encoder (src/vq.c, the portable loops) ---------- */
+
+/* src/vq.c:51-82 vq_step: the nearest entry (d = sum (v_j - e_j)^2 in j
+ * order, strict <, first index wins), and the residual. */
+static int orc_vq_step(const float *v, const float *C, int entries, int dim, float *resid)
+{
+    int best = 0;
+    float bestd = INFINITY;
+    for (int c = 0; c < entries; c++) {
+        const float *e = C + (size_t)c * dim;
+        float d = 0;
+        for (int j = 0; j < dim; j++) {
+            const float t = v[j] - e[j];
+            d += t * t;
+        }
+        if (d < bestd) {
+            bestd = d;
+            best = c;
+        }
+    }
+    for (int j = 0; j < dim; j++) resid[j] = v[j] - C[(size_t)best * dim + j];
+    return best;
+}
+
+/* src/vq.c:84-105 vq_range / waste_vq_encode: every stage of every vector. */
+void orc_vq_encode(const float *X, int n, const float *books, int stages, int entries, int dim,
+                   uint8_t *out)
+{
+    float cur[64], nxt[64];
+    for (int i = 0; i < n; i++) {
+        for (int d = 0; d < dim; d++) cur[d] = X[(size_t)i * dim + d];
+        for (int s = 0; s < stages; s++) {
+            out[(size_t)i * stages + s] = (uint8_t)orc_vq_step(
+                cur, books + (size_t)s * entries * dim, entries, dim, nxt);
+            for (int d = 0; d < dim; d++) cur[d] = nxt[d];
+        }
+    }
+}
+
+/* src/vq.c:107-136 waste_vq_lloyd: assign, then double sums in vector
+ * order and centroid = (float)(sum / count) for the non-empty clusters.
+ * Returns their number (or -1 when out of memory). */
+int orc_vq_lloyd(const float *X, int n, float *C, int entries, int dim)
+{
+    uint8_t *asg = (uint8_t *)malloc((size_t)n);
+    double *sum = (double *)calloc((size_t)entries * dim, sizeof(double));
+    long *cnt = (long *)calloc((size_t)entries, sizeof(long));
+    if (!asg || !sum || !cnt) { free(asg); free(sum); free(cnt); return -1; }
+    orc_vq_encode(X, n, C, 1, entries, dim, asg);
+    for (int i = 0; i < n; i++) {
+        const int a = asg[i];
+        cnt[a]++;
+        for (int d = 0; d < dim; d++) sum[(size_t)a * dim + d] += X[(size_t)i * dim + d];
+    }
+    int live = 0;
+    for (int c = 0; c < entries; c++)
+        if (cnt[c]) {
+            live++;
+            for (int d = 0; d < dim; d++)
+                C[(size_t)c * dim + d] = (float)(sum[(size_t)c * dim + d] / (double)cnt[c]);
+        }
+    free(asg); free(sum); free(cnt);
+    return live;
+}

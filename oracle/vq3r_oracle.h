@@ -35,6 +35,8 @@
  *   orc_moe_block      src/model.c:3927-3945   h + moe_layer(rmsnorm(h)): the MoE
  *                                              half of a decoder layer
  *   orc_kda_step       src/kda.c:26-68         Kimi Delta Attention decode step
+ *   orc_vq_encode      src/vq.c:50-105         the converter's RVQ encoder
+ *   orc_vq_lloyd       src/vq.c:107-136        one Lloyd iteration
  *   orc_short_conv_step src/kda.c:84-99        causal depthwise conv + SiLU
  *   orc_rmsnorm_gated  src/kda.c:101-111       rmsnorm times sigmoid(gate)
  *
@@ -144,6 +146,12 @@ void orc_short_conv_step(int C, int KS, const float *w, const float *bias, float
                          const float *x, float *y);
 void orc_rmsnorm_gated(int C, const float *x, const float *gate, const float *weight,
                        float eps, float *y);
+/* The converter's encoder: X [n][dim], books [stages][entries][dim],
+ * out [n][stages]; Lloyd updates C [entries][dim] and returns the number of
+ * non-empty clusters. */
+void orc_vq_encode(const float *X, int n, const float *books, int stages, int entries, int dim,
+                   uint8_t *out);
+int orc_vq_lloyd(const float *X, int n, float *C, int entries, int dim);
 #ifdef __cplusplus
 }
 #endif

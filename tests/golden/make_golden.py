@@ -18,6 +18,7 @@ Every output here is produced by the reference's own code:
 * vq4p.npz, moe_vq4p*.npz — the VQ4P format (src/model.c:2026-2229): the
   matvec, its int8 tables, and VQ4P MoE layers.
 * kda.npz — the KDA kernels (src/kda.c:26-111) on seeded inputs.
+* enc.npz — the converter's encoder and Lloyd step (src/vq.c:50-136).
 * moe_*.npz — moe_layer / moe_chunk (src/model.c:2713, 3512) on seeded
   layers built by warp_b200.synth; the inputs are regenerated from the seed
   (numpy PCG64, which is stable across numpy versions) and pinned by a
@@ -54,7 +55,8 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 from golden_cases import (CONV_C, CONV_KS, KDA_CASES, MOE_CASES, MVQ_CASES,  # noqa: E402
                           NORM_DIM, NORM_HEADS, NORM_SIZES, VQ4P_CASES, VQ4P_MOE_CASES,
                           conv_inputs, kda_inputs, norm_inputs, sha, vq4p_books,
-                          vq4p_case)  # shared with the tests
+                          vq4p_case, ENC_CASES, LLOYD_CASES, enc_inputs,
+                          lloyd_inputs)  # shared with the tests
 
 
 def layer_sha(L) -> str:
@@ -200,6 +202,24 @@ def kda_fixture():
     print("kda.npz written")
 
 
+def enc_fixture():
+    """The reference's waste_vq_encode and waste_vq_lloyd (src/vq.c:50-136)
+    on seeded inputs (regenerated by golden_cases and pinned by a sha256):
+    the codes of every encoder case, and the centroids and live count after
+    one Lloyd iteration."""
+    res = {}
+    for name in ENC_CASES:
+        X, books = enc_inputs(name)
+        res[f"{name}_sha"] = sha(X, books)
+        res[f"{name}_codes"] = O.ref_vq_encode(X, books)
+    for name in LLOYD_CASES:
+        X, C0 = lloyd_inputs(name)
+        res[f"{name}_sha"] = sha(X, C0)
+        res[f"{name}_C"], res[f"{name}_live"] = O.ref_vq_lloyd(X, C0)
+    np.savez_compressed(os.path.join(OUT, "enc.npz"), **res)
+    print("enc.npz written")
+
+
 def tiny_container():
     """tests/golden/tiny_container/: the reference's own test container
     (tools/make_test_container.py, seed 0: a Kimi-Linear at 1/18 scale, 4
@@ -253,6 +273,7 @@ def main():
     mvq_fixture()
     vq4p_fixtures()
     kda_fixture()
+    enc_fixture()
 
 
 if __name__ == "__main__":
@@ -268,5 +289,7 @@ if __name__ == "__main__":
         vq4p_fixtures()
     elif sys.argv[1:] == ["kda"]:
         kda_fixture()
+    elif sys.argv[1:] == ["enc"]:
+        enc_fixture()
     else:
         main()

@@ -123,3 +123,34 @@ def norm_inputs():
     gate = rng.standard_normal(NORM_HEADS * NORM_DIM, dtype=np.float32)
     w = rng.normal(1.0, 0.1, NORM_DIM).astype(np.float32)
     return x, gate, w, np.float32(1e-6)
+
+
+# The converter's encoder (enc.npz): name -> (n vectors, stages, entries,
+# dim). "enc_ties" repeats entries inside each book (the first index must
+# win); "enc_dim12" is a dimension other than 8.
+ENC_CASES = {"enc_kimi": (20000, 3, 256, 8), "enc_ties": (3000, 2, 64, 8),
+             "enc_dim12": (2000, 2, 32, 12)}
+# Lloyd iterations: name -> (n, entries, dim); "lloyd_sparse" has fewer
+# vectors than clusters, so most clusters stay empty.
+LLOYD_CASES = {"lloyd_kimi": (50000, 256, 8), "lloyd_sparse": (100, 256, 8)}
+
+
+def enc_inputs(name):
+    """Seeded (X, books) of an encoder case: X like the converter's W/scale
+    rows (|x| <= 1), books N(0, 0.3^2) per stage (shrinking by stage)."""
+    n, st, en, dim = ENC_CASES[name]
+    rng = np.random.default_rng(len(name) * 977 + n)
+    X = np.clip(rng.normal(0.0, 0.4, (n, dim)), -1, 1).astype(np.float32)
+    books = np.stack([rng.normal(0.0, 0.3 / (s + 1), (en, dim)) for s in range(st)]
+                     ).astype(np.float32)
+    if name == "enc_ties":
+        books[:, en // 2:] = books[:, :en // 2]       # every entry twice
+    return X, books
+
+
+def lloyd_inputs(name):
+    n, en, dim = LLOYD_CASES[name]
+    rng = np.random.default_rng(len(name) * 313 + n)
+    X = rng.normal(0.0, 0.4, (n, dim)).astype(np.float32)
+    C0 = X[rng.choice(n, size=en, replace=n < en)].copy()
+    return X, C0

@@ -40,6 +40,8 @@ EXPORTS = (
     "waste_cuda_vq4p_table", "waste_cuda_kda_step", "waste_cuda_short_conv_step",
     "waste_cuda_rmsnorm_gated_heads", "waste_cuda_state_push", "waste_cuda_state_pull",
     "waste_cuda_kda_step_dev", "waste_cuda_short_conv_dev", "waste_cuda_rmsnorm_gated_dev",
+    "waste_cuda_vq_encode", "waste_cuda_vq_encode_dev", "waste_cuda_vq_lloyd",
+    "waste_cuda_vq_lloyd_dev",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
@@ -168,6 +170,10 @@ def load_library() -> C.CDLL:
         "waste_cuda_kda_step_dev": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P]),
         "waste_cuda_short_conv_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, P, P, P]),
         "waste_cuda_rmsnorm_gated_dev": (C.c_int, [C.c_int, C.c_int, P, P, P, C.c_float, P, P]),
+        "waste_cuda_vq_encode": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int, P]),
+        "waste_cuda_vq_encode_dev": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int, P, P]),
+        "waste_cuda_vq_lloyd": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int]),
+        "waste_cuda_vq_lloyd_dev": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -585,3 +591,40 @@ def release_host_buffers():
     """Drop every device copy keyed by a host address (trunk mirrors, KDA
     state and weights): what the engine calls before freeing a model."""
     load_library().waste_cuda_release_host_buffers()
+
+
+# ---- the converter's RVQ encoder ------------------------------------------------
+
+def vq_encode(X, books) -> np.ndarray:
+    """X [n][dim], books [stages][entries][dim] -> codes [n][stages] uint8."""
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    bb = np.ascontiguousarray(books, dtype=np.float32)
+    n, dim = xx.shape
+    stages, entries = bb.shape[0], bb.shape[1]
+    out = np.empty((n, stages), dtype=np.uint8)
+    _check(load_library().waste_cuda_vq_encode(_ptr(xx), n, _ptr(bb), stages, entries, dim,
+                                               _ptr(out)))
+    return out
+
+
+def vq_lloyd(X, C):
+    """One Lloyd iteration: returns (new centroids, non-empty clusters)."""
+    xx = np.ascontiguousarray(X, dtype=np.float32)
+    cc = np.array(C, dtype=np.float32, copy=True, order="C")
+    rc = load_library().waste_cuda_vq_lloyd(_ptr(xx), xx.shape[0], _ptr(cc), cc.shape[0],
+                                            cc.shape[1])
+    if rc < 0:
+        _check(rc)
+    return cc, rc
+
+
+def vq_encode_dev(d_X, n, d_books, stages, entries, dim, d_out, stream: int = 0):
+    v = lambda p: C.c_void_p(int(p)) if p else None
+    _check(load_library().waste_cuda_vq_encode_dev(v(d_X), n, v(d_books), stages, entries, dim,
+                                                   v(d_out), v(stream)))
+
+
+def vq_lloyd_dev(d_X, n, d_C, entries, dim, d_live, stream: int = 0):
+    v = lambda p: C.c_void_p(int(p)) if p else None
+    _check(load_library().waste_cuda_vq_lloyd_dev(v(d_X), n, v(d_C), entries, dim, v(d_live),
+                                                  v(stream)))

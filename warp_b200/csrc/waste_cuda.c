@@ -113,6 +113,9 @@ static struct {
     /* VQ4P scratch: integer block sums, table scales, activations */
     void *d_p6;
     size_t p6_bytes;
+    /* the encoder's buffers (host-pointer forms) and the Lloyd scratch */
+    void *d_enc;
+    size_t enc_bytes;
 } S;
 
 /* Bumped by every call that allocates, frees or reloads what a cached
@@ -389,6 +392,7 @@ void waste_cuda_shutdown(void)
         cudaFreeHost(S.h_w);
         cudaFree(S.d_res); cudaFreeHost(S.h_res);
         cudaFree(S.d_p6);
+        cudaFree(S.d_enc);
         mirrors_free();
         states_free();
         for (int b = 0; b < 2; b++) {
@@ -2452,6 +2456,120 @@ int waste_cuda_vq4p_table(int8_t *q, float *qs, const float *x, int N, int cb_ba
     CK(cudaMemcpyAsync(qs, t + o_qs, (size_t)nb * 4, cudaMemcpyDeviceToHost, S.stream),
        "scales D2H");
     CK(cudaStreamSynchronize(S.stream), "VQ4P table");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+/* ---- the converter's RVQ encoder --------------------------------------------- */
+
+#define WC_ENC_SMEM_MAX 232448      /* 227 KB of shared memory a block */
+
+static int enc_args(int n, int stages, int entries, int dim)
+{
+    if (n <= 0 || stages <= 0 || entries <= 0 || entries > 256 || dim <= 0 || dim > 64)
+        return fail(WASTE_CUDA_E_ARG, "vq_encode: n > 0, stages > 0, entries 1..256, dim 1..64");
+    if (wc_vq_encode_smem(stages, entries, dim) > WC_ENC_SMEM_MAX)
+        return fail(WASTE_CUDA_E_ARG, "vq_encode: %d stages x %d entries x %d dims of codebook "
+                    "exceed 227 KB of shared memory", stages, entries, dim);
+    return 0;
+}
+
+static int enc_reserve(size_t bytes)
+{
+    if (bytes <= S.enc_bytes) return 0;
+    cudaFree(S.d_enc);
+    S.d_enc = NULL;
+    S.enc_bytes = 0;
+    const cudaError_t e = cudaMalloc(&S.d_enc, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "encoder buffers");
+    S.enc_bytes = bytes;
+    return 0;
+}
+
+int waste_cuda_vq_encode_dev(const float *d_X, int n, const float *d_books, int stages,
+                             int entries, int dim, uint8_t *d_out, void *stream)
+{
+    int rc;
+    if (!d_X || !d_books || !d_out) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    if ((rc = enc_args(n, stages, entries, dim))) return rc;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "vq_encode_dev before waste_cuda_init"); goto out; }
+    CK((cudaError_t)wc_vq_encode_launch(d_X, n, d_books, stages, entries, dim, d_out,
+                                        stream ? stream : (void *)S.stream), "vq encode");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_encode(const float *X, int n, const float *books, int stages, int entries,
+                         int dim, uint8_t *out)
+{
+    int rc;
+    if (!X || !books || !out) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    if ((rc = enc_args(n, stages, entries, dim))) return rc;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    {
+        const size_t xb = (size_t)n * dim * sizeof(float);
+        const size_t bb = (size_t)stages * entries * dim * sizeof(float);
+        const size_t ob = (size_t)n * stages;
+        const size_t o_b = al256(xb), o_o = o_b + al256(bb);
+        if ((rc = enc_reserve(o_o + ob))) goto out;
+        char *d = (char *)S.d_enc;
+        CK(cudaMemcpyAsync(d, X, xb, cudaMemcpyHostToDevice, S.stream), "X H2D");
+        CK(cudaMemcpyAsync(d + o_b, books, bb, cudaMemcpyHostToDevice, S.stream), "books H2D");
+        CK((cudaError_t)wc_vq_encode_launch((const float *)d, n, (const float *)(d + o_b), stages,
+                                            entries, dim, (uint8_t *)(d + o_o), S.stream),
+           "vq encode");
+        CK(cudaMemcpyAsync(out, d + o_o, ob, cudaMemcpyDeviceToHost, S.stream), "codes D2H");
+        CK(cudaStreamSynchronize(S.stream), "vq encode");
+    }
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_lloyd_dev(const float *d_X, int n, float *d_C, int entries, int dim,
+                            int *d_live, void *stream)
+{
+    int rc;
+    if (!d_X || !d_C || !d_live) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    if ((rc = enc_args(n, 1, entries, dim))) return rc;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "vq_lloyd_dev before waste_cuda_init"); goto out; }
+    if ((rc = enc_reserve(wc_vq_lloyd_scratch(n, entries, dim)))) goto out;
+    CK((cudaError_t)wc_vq_lloyd_launch(d_X, n, d_C, entries, dim, S.d_enc, d_live,
+                                       stream ? stream : (void *)S.stream), "lloyd");
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
+int waste_cuda_vq_lloyd(const float *X, int n, float *C, int entries, int dim)
+{
+    int rc;
+    if (!X || !C) return fail(WASTE_CUDA_E_ARG, "NULL pointer");
+    if ((rc = enc_args(n, 1, entries, dim))) return rc;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    {
+        const size_t xb = (size_t)n * dim * sizeof(float);
+        const size_t cb = (size_t)entries * dim * sizeof(float);
+        const size_t o_c = al256(xb), o_l = o_c + al256(cb), o_s = o_l + 256;
+        if ((rc = enc_reserve(o_s + wc_vq_lloyd_scratch(n, entries, dim)))) goto out;
+        char *d = (char *)S.d_enc;
+        int live = 0;
+        CK(cudaMemcpyAsync(d, X, xb, cudaMemcpyHostToDevice, S.stream), "X H2D");
+        CK(cudaMemcpyAsync(d + o_c, C, cb, cudaMemcpyHostToDevice, S.stream), "C H2D");
+        CK((cudaError_t)wc_vq_lloyd_launch((const float *)d, n, (float *)(d + o_c), entries, dim,
+                                           d + o_s, (int *)(d + o_l), S.stream), "lloyd");
+        CK(cudaMemcpyAsync(C, d + o_c, cb, cudaMemcpyDeviceToHost, S.stream), "C D2H");
+        CK(cudaMemcpyAsync(&live, d + o_l, sizeof live, cudaMemcpyDeviceToHost, S.stream),
+           "live D2H");
+        CK(cudaStreamSynchronize(S.stream), "lloyd");
+        rc = live;
+    }
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;

@@ -244,6 +244,18 @@ int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float
 int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
                             float eps, float *y, void *stream);
 
+/* The converter's residual-VQ encoder (vq_encode.cu, src/vq.c:50-136):
+ * encode n vectors of dim against `stages` books of `entries` each (the
+ * books in shared memory: wc_vq_encode_smem bytes); one Lloyd iteration
+ * over n vectors with scratch of wc_vq_lloyd_scratch bytes, C updated in
+ * place and the number of non-empty clusters written to d_live. */
+size_t wc_vq_encode_smem(int stages, int entries, int dim);
+int    wc_vq_encode_launch(const float *X, int n, const float *books, int stages, int entries,
+                           int dim, uint8_t *out, void *stream);
+size_t wc_vq_lloyd_scratch(int n, int entries, int dim);
+int    wc_vq_lloyd_launch(const float *X, int n, float *C, int entries, int dim, void *scratch,
+                          int *d_live, void *stream);
+
 int wc_lutb_launch(float *lut, const float *x, const float *books, int cb_base,
                    int nv, int stages, void *stream);
 int wc_dequant_launch(float *W, const uint8_t *idx, const uint16_t *scale,
