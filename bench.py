@@ -34,6 +34,18 @@ instead runs N independent copies of the single-GPU decode.
 `--workload k3` measures config 4 instead: one K3-class MoE layer (hidden
 7168, 512 experts, top-16) at global batches 1/16/64, expert parallel over
 the N GPUs.
+
+`--workload engine` measures config 5: the whole decode step through the
+reference engine's public API (waste_open / waste_eval), built with this
+backend wired in (integration/), on a synthetic Kimi-Linear-48B-shaped
+container (27 layers: a dense layer, 21 KDA and 6 MLA layers, 26 MoE
+layers of 256 experts; ~19 GB, written once by warp_b200.synth into
+--container, default /dev/shm/warp_c5). Every slot is live: the trunk
+matvecs, the KDA steps and the expert loops run on the device, MLA and
+the router on the host. Tokens/s is the wall clock of waste_eval per
+decode step (host API, copies included, so value and e2e coincide); the
+unmodified reference engine on the same container is the CPU baseline.
+Single GPU (the engine is one process).
 """
 from __future__ import annotations
 
@@ -1120,6 +1132,134 @@ def run_k3(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 5
+
+ENGINE_RUN = os.path.join(ROOT, "integration", "_build", "engine_run")
+CUDA_ENGINE = os.path.join(ROOT, "integration", "_build", "libwaste_engine_cuda.so")
+REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "libwaste_ref.so")
+C5_PROMPT = [1, 17, 4242, 99, 12345, 7, 808, 3]
+
+
+def _engine(lib, cdir, steps, env=None, timeout=3600):
+    """Runs integration/_build/engine_run: per eval (ms, next token), the
+    logits, open time and the backend's launch count."""
+    out = tempfile.mktemp(suffix=".bin")
+    r = subprocess.run([ENGINE_RUN, lib, cdir, out, str(steps)] + [str(t) for t in C5_PROMPT],
+                       capture_output=True, text=True, timeout=timeout,
+                       env=dict(os.environ, **(env or {})))
+    if r.returncode != 0:
+        raise RuntimeError(f"engine_run failed: {r.stdout[-2000:]} {r.stderr[-2000:]}")
+    res = {"ms": [], "tok": [], "launches": None, "open_ms": None, "build": ""}
+    for line in r.stdout.splitlines():
+        if line.startswith("build:"):
+            res["build"] = line[7:]
+        elif line.startswith("open:"):
+            res["open_ms"] = float(line.split()[1])
+        elif line.startswith("eval "):
+            res["tok"].append(int(line.split("next token ")[1].split()[0]))
+            res["ms"].append(float(line.split("(")[1].split()[0]))
+        elif line.startswith("cuda launches:"):
+            res["launches"] = int(line.split(":")[1])
+    raw = np.fromfile(out, dtype=np.int32)
+    os.unlink(out)
+    nev, vocab = int(raw[0]), int(raw[1])
+    res["logits"] = raw[2:].reshape(nev, 1 + vocab)[:, 1:].copy().view(np.float32)
+    return res
+
+
+def _container(args):
+    from warp_b200 import synth
+    import shutil
+    cdir = args.container
+    if not cdir:                     # the first place with room for ~19 GB (tmpfs first)
+        for base in ("/dev/shm", tempfile.gettempdir(), ROOT):
+            try:
+                if os.access(base, os.W_OK) and shutil.disk_usage(base).free > (24 << 30):
+                    cdir = os.path.join(base, "warp_c5")
+                    break
+            except OSError:
+                continue
+        if not cdir:
+            raise SystemExit("no file system with 24 GB free for the config-5 container")
+    t0 = time.time()
+    if not os.path.exists(os.path.join(cdir, "manifest.json")):
+        synth.write_container(cdir, seed=SEED)
+    return cdir, time.time() - t0
+
+
+def run_engine_reference(args):
+    """The unmodified reference engine on config 5's container (CPU)."""
+    cdir, wt = _container(args)
+    steps = max(3, min(args.steps, 8))
+    ref = _engine(REF_ENGINE, cdir, args.warmup + steps)
+    dec = ref["ms"][1 + args.warmup:]
+    v = 1e3 / statistics.mean(dec)
+    print(json.dumps({"impl": "reference", "metric": ENGINE_METRIC, "value": v, "unit": UNIT,
+                      "n_gpus": 1, "steps": len(dec), "warmup": args.warmup,
+                      "ms_per_step": statistics.mean(dec), "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic (seeded container)",
+                      "config": {"workload": "kimi_linear_48b_full_decode_step", "layers": 27},
+                      "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(),
+                                       "kind": "reference",
+                                       "sample": f"{len(dec)} decode steps through waste_eval"},
+                      "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
+ENGINE_METRIC = ("decode tok/s through the engine's waste.h (full Kimi-Linear-48B-shaped decode "
+                 "step: 27 layers, KDA + MLA attention, 26 VQ3R MoE layers, batch 1)")
+
+
+def run_engine_workload(args):
+    def rel_l2(a, b):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+    cdir, wt = _container(args)
+    n = args.warmup + args.steps
+    clk = ClockSampler(0)
+    clk.start()
+    cu = _engine(CUDA_ENGINE, cdir, n)
+    clocks = clk.stop()
+    dec = cu["ms"][1 + args.warmup:]
+    v = 1e3 / statistics.mean(dec)
+    # the unmodified engine on the same container: a bounded sample
+    rs = max(3, min(args.steps, 8))
+    ref = _engine(REF_ENGINE, cdir, args.warmup + rs)
+    rdec = ref["ms"][1 + args.warmup:]
+    cpu = 1e3 / statistics.mean(rdec)
+    m = min(len(cu["tok"]), len(ref["tok"]))
+    worst = max(rel_l2(cu["logits"][e], ref["logits"][e]) for e in range(m))
+    launches = cu["launches"] or 0
+    per_step = launches / max(len(cu["ms"]), 1)
+    hid, vocab = 2304, 163840
+    line = {"metric": ENGINE_METRIC, "value": v, "unit": UNIT, "n_gpus": 1, "steps": len(dec),
+            "warmup": args.warmup, "ms_per_step": statistics.mean(dec),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Kimi-Linear-48B-shaped container written by "
+                    "warp_b200.synth: random trunk in its Q8G/Q4G/F32 formats, N(0, 0.02^2) "
+                    "codebooks, uniform expert indices)",
+            "config": {"workload": "kimi_linear_48b_full_decode_step", "layers": 27,
+                       "kda_layers": 21, "mla_layers": 6, "moe_layers": 26, "experts": 256,
+                       "top_k": 8, "hidden": hid, "vocab": vocab, "prompt_tokens": len(C5_PROMPT),
+                       "timing": "wall clock of each decode step's waste_eval (host API)",
+                       "container_write_s": wt, "engine_open_ms": cu["open_ms"],
+                       "backend": cu["build"]},
+            "gpu_launches": int(per_step * len(dec)), "clocks": clocks,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": hid * 4,
+                    "d2h_bytes_per_step": vocab * 4},
+            "parity": {"tokens_equal": cu["tok"][:m] == ref["tok"][:m],
+                       "worst_logits_rel_l2": worst, "evals_compared": m,
+                       "against": "the unmodified reference engine, same container and prompt"},
+            "cpu_baseline": {"value": cpu, "unit": UNIT, "cores": os.cpu_count(),
+                             "kind": "reference",
+                             "sample": f"{len(rdec)} decode steps of the unmodified engine "
+                                       "through waste_eval on the same container"}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1137,9 +1277,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--parallel", choices=("ep", "replicas"), default="ep",
                     help="with --gpus N > 1: expert parallel (default) or N replicas")
-    ap.add_argument("--workload", choices=("kimi", "k3"), default="kimi",
+    ap.add_argument("--workload", choices=("kimi", "k3", "engine"), default="kimi",
                     help="kimi: the Kimi-Linear decode step (default); k3: one K3-class "
-                         "MoE layer at batches 1/16/64")
+                         "MoE layer at batches 1/16/64; engine: config 5 through waste.h")
+    ap.add_argument("--container", default=None,
+                    help="engine: where the synthetic container is (written if missing)")
     ap.add_argument("--batches", default="1,16,64", help="k3: global batches")
     ap.add_argument("--k3-experts", type=int, default=K3_EXPERTS,
                     help="k3: experts per layer (fewer only for small profiling cases)")
@@ -1149,6 +1291,12 @@ def main():
         args.warmup = 3
     if args.workload == "k3":
         return run_k3_reference(args) if args.impl == "reference" else run_k3(args)
+    if args.workload == "engine":
+        if args.gpus != 1:
+            raise SystemExit("--workload engine runs one engine process on one GPU")
+        if args.impl == "reference":
+            return run_engine_reference(args)
+        return run_engine_workload(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_warp(args)

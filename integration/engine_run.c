@@ -19,6 +19,9 @@
  * prompt evaluated again (one extra eval, which must repeat eval 0), then
  * the snapshot loaded (waste_state_load) and the remaining steps decoded
  * from where the save left off.
+ *
+ * Each eval's wall-clock time is printed ("eval <e>: next token <t> (<ms>
+ * ms)"), and the time to open the container ("open: <ms> ms").
  */
 #include "waste.h"
 
@@ -26,6 +29,14 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <time.h>
+
+static double now_ms(void)
+{
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec * 1e-6;
+}
 
 typedef void (*cfg_init_fn)(waste_cfg *);
 typedef waste_status (*open_fn)(const char *, const waste_cfg *, waste_ctx **);
@@ -72,9 +83,11 @@ int main(int argc, char **argv)
     cfg.ctx_tokens = 256;
     cfg.n_threads = 0;
     waste_ctx *ctx = NULL;
+    const double t_open = now_ms();
     waste_status st = wopen(argv[2], &cfg, &ctx);
     if (st != WASTE_OK) { fprintf(stderr, "waste_open: %d\n", (int)st); return 1; }
     printf("build: %s\n", info());
+    printf("open: %.1f ms\n", now_ms() - t_open);
 
     FILE *out = fopen(argv[3], "wb");
     if (!out) { perror("out"); return 1; }
@@ -105,8 +118,10 @@ int main(int argc, char **argv)
             if (sload(ctx, snap) != WASTE_OK) { fprintf(stderr, "state load failed\n"); return 1; }
             tok = tok_saved;
         }
+        const double t0 = now_ms();
         st = (e == 0 || again) ? weval(ctx, prompt, (size_t)np, &lg, &vocab)
                                : weval(ctx, &tok, 1, &lg, &vocab);
+        const double dt = now_ms() - t0;
         if (st != WASTE_OK) {
             fprintf(stderr, "waste_eval %d: %d (%s)\n", e, (int)st,
                     detail && detail(ctx) ? detail(ctx) : "");
@@ -115,7 +130,7 @@ int main(int argc, char **argv)
         tok = argmax(lg, vocab);
         fwrite(&tok, 4, 1, out);
         fwrite(lg, sizeof(float), vocab, out);
-        printf("eval %d: next token %d\n", e, tok);
+        printf("eval %d: next token %d (%.3f ms)\n", e, tok, dt);
     }
     /* the CUDA backend's own count of its kernel launches, when the engine
      * links it (a dependency of the patched engine library) */

@@ -393,3 +393,165 @@ def zipf_routes(seed: int, T: int, E: int, K: int, s: float = 1.1) -> np.ndarray
     for t in range(T):
         out[t] = perm[rng.choice(E, size=K, replace=False, p=p)]
     return out
+
+
+# ---- a whole container ---------------------------------------------------------
+
+#: Kimi-Linear-48B's shape for a full decode step: 27
+#: layers, layer 0 dense (its intermediate width is not recorded in the
+#: reference; 9216 is used), KDA layers of 32 heads x 128 and an MLA layer
+#: every fourth (NoPE, latent 512), 256 experts top-8 of 1024, one shared
+#: expert, vocab 163840. The trunk is Q4G but for the embedding, lm_head and
+#: shared experts (Q8G) and the router, norms and small parameters (F32).
+KIMI_LINEAR_48B = dict(hidden=2304, layers=27, first_dense=1, dense_inter=9216, moe_inter=1024,
+                       experts=256, top_k=8, n_shared=1, routed_scale=2.446, kda_heads=32,
+                       kda_dim=128, conv_k=4, mla_heads=32, qk_nope=128, qk_rope=64, v_head=128,
+                       kv_lora=512, vocab=163840, full_attn=(4, 8, 12, 16, 20, 24), eps=1e-6)
+
+FMT_F32, FMT_Q8G, FMT_Q4G = 0, 2, 3           # waste_fmt, src/waste_format.h:46-49
+MAGIC_CODEBOOK = 0x4B424357                   # 'WCBK', src/waste_format.h
+
+
+class _TrunkWriter:
+    """trunk.bin written as it grows, with the manifest's tensor index:
+    F32 tensors raw; Q8G/Q4G rows padded to whole groups of 128 (Q4G: two
+    signed nibbles per byte, low first, biased by 8), then one f16 scale per
+    (row, group) — the layout src/model.c reads (:265-320)."""
+
+    def __init__(self, path, rng):
+        self.f = open(path, "wb")
+        self.rng = rng
+        self.off = 0
+        self.index = []
+
+    def _put(self, b):
+        self.f.write(b)
+        self.off += len(b)
+
+    def f32(self, name, a):
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        off = self.off
+        self._put(a.tobytes())
+        self.index.append({"name": name, "fmt": FMT_F32, "off": off, "shape": list(a.shape),
+                           "bytes": self.off - off})
+
+    def quant(self, name, shape, bits):
+        rows, n_in = int(np.prod(shape[:-1])), shape[-1]
+        ng = (n_in + GROUP - 1) // GROUP
+        off = self.off
+        rb = ng * GROUP if bits == 8 else ng * GROUP // 2
+        self._put(random_bytes(self.rng, rows * rb).tobytes())
+        soff = self.off
+        # weights uniform over the code range; scales that keep y = W x at
+        # about the size of x (variance of a code: 127^2/3 or 21.25)
+        var = 127.0 ** 2 / 3.0 if bits == 8 else 21.25
+        s = self.rng.uniform(0.8, 1.2, size=(rows, ng)) / np.sqrt(n_in * var)
+        self._put(f16_bits(s).tobytes())
+        self.index.append({"name": name, "fmt": FMT_Q8G if bits == 8 else FMT_Q4G, "off": off,
+                           "shape": list(shape), "group": GROUP, "scale_off": soff,
+                           "bytes": self.off - off})
+
+    def close(self):
+        self.f.close()
+
+
+def write_container(out: str, seed: int = 0, **over) -> dict:
+    """A synthetic container the reference engine loads (manifest.json,
+    trunk.bin, codebooks.bin, experts-L<n>.bin; the format of
+    docs/FORMAT.md, src/waste_format.h), Kimi-Linear-48B-shaped by default
+    (KIMI_LINEAR_48B; keyword arguments override). Seeded; weights random
+    in their formats' code ranges, codebooks N(0, 0.02^2). Returns the
+    config used. The record checksums are left 0 (the engine checks them
+    only with WASTE_VERIFY)."""
+    import json
+    import os
+    c = dict(KIMI_LINEAR_48B, **over)
+    os.makedirs(out, exist_ok=True)
+    rng = np.random.default_rng(seed)
+    hid, H, D = c["hidden"], c["kda_heads"], c["kda_dim"]
+    C = H * D
+    full = set(c["full_attn"])
+    kda_layers = [L + 1 for L in range(c["layers"]) if L + 1 not in full]
+    t = _TrunkWriter(os.path.join(out, "trunk.bin"), rng)
+    t.quant("model.embed_tokens.weight", [c["vocab"], hid], 8)
+    ones = lambda n: (1.0 + rng.normal(0.0, 0.02, n)).astype(np.float32)
+    for L in range(c["layers"]):
+        p = f"model.layers.{L}."
+        t.f32(p + "input_layernorm.weight", ones(hid))
+        t.f32(p + "post_attention_layernorm.weight", ones(hid))
+        a = p + "self_attn."
+        if L + 1 in full:                               # MLA (NoPE)
+            nh = c["mla_heads"]
+            t.quant(a + "q_proj.weight", [nh * (c["qk_nope"] + c["qk_rope"]), hid], 4)
+            t.quant(a + "kv_a_proj_with_mqa.weight", [c["kv_lora"] + c["qk_rope"], hid], 4)
+            t.f32(a + "kv_a_layernorm.weight", ones(c["kv_lora"]))
+            t.quant(a + "kv_b_proj.weight", [nh * (c["qk_nope"] + c["v_head"]), c["kv_lora"]], 4)
+            t.quant(a + "o_proj.weight", [hid, nh * c["v_head"]], 4)
+        else:                                           # KDA
+            for w in ("q_proj", "k_proj", "v_proj"):
+                t.quant(a + w + ".weight", [C, hid], 4)
+            t.quant(a + "b_proj.weight", [H, hid], 4)
+            t.quant(a + "f_a_proj.weight", [D, hid], 4)
+            t.quant(a + "f_b_proj.weight", [C, D], 4)
+            t.quant(a + "g_a_proj.weight", [D, hid], 4)
+            t.quant(a + "g_b_proj.weight", [C, D], 4)
+            t.quant(a + "o_proj.weight", [hid, C], 4)
+            for w in ("q_conv1d", "k_conv1d", "v_conv1d"):
+                t.f32(a + w + ".weight", rng.normal(0.0, 0.3, (C, 1, c["conv_k"])))
+            t.f32(a + "A_log", np.log(rng.uniform(1.0, 16.0, (1, 1, H, 1))))
+            t.f32(a + "dt_bias", rng.normal(0.0, 0.1, C))
+            t.f32(a + "o_norm.weight", ones(D))
+        if L < c["first_dense"]:
+            m = p + "mlp."
+            t.quant(m + "gate_proj.weight", [c["dense_inter"], hid], 4)
+            t.quant(m + "up_proj.weight", [c["dense_inter"], hid], 4)
+            t.quant(m + "down_proj.weight", [hid, c["dense_inter"]], 4)
+        else:
+            m = p + "block_sparse_moe."
+            t.f32(m + "gate.weight", rng.standard_normal((c["experts"], hid), dtype=np.float32)
+                  / np.float32(np.sqrt(hid)))
+            t.f32(m + "gate.e_score_correction_bias", rng.normal(0.0, 0.05, c["experts"]))
+            si = c["moe_inter"] * c["n_shared"]
+            t.quant(m + "shared_experts.gate_proj.weight", [si, hid], 8)
+            t.quant(m + "shared_experts.up_proj.weight", [si, hid], 8)
+            t.quant(m + "shared_experts.down_proj.weight", [hid, si], 8)
+    t.f32("model.norm.weight", ones(hid))
+    t.quant("lm_head.weight", [c["vocab"], hid], 8)
+    t.close()
+
+    layers, cb_base = {}, 0
+    with open(os.path.join(out, "codebooks.bin"), "wb") as cf:
+        for L in range(c["first_dense"], c["layers"]):
+            books = codebooks(rng, 3 * 3)
+            for k in range(9):
+                cf.write(struct.pack("<IHBBII", MAGIC_CODEBOOK, (cb_base + k) & 0xFFFF,
+                                     FMT_VQ3R, VEC_DIM, ENTRIES, 0))
+                cf.write(books[k].tobytes())
+            name = f"experts-L{L}.bin"
+            bk = bank(rng, L, c["experts"], cb_base, c["moe_inter"], hid)
+            bk.tofile(os.path.join(out, name))
+            layers[str(L)] = {"file": name, "experts": c["experts"], "bytes": int(bk.size),
+                              "codebook_base": cb_base}
+            cb_base += 9
+    cfg = {"model_type": "kimi_linear", "architectures": ["KimiLinearForCausalLM"],
+           "hidden_size": hid, "num_hidden_layers": c["layers"],
+           "first_k_dense_replace": c["first_dense"], "intermediate_size": c["dense_inter"],
+           "moe_intermediate_size": c["moe_inter"], "num_experts": c["experts"],
+           "num_experts_per_token": c["top_k"], "num_shared_experts": c["n_shared"],
+           "moe_renormalize": True, "moe_router_activation_func": "sigmoid",
+           "routed_scaling_factor": c["routed_scale"], "num_attention_heads": c["mla_heads"],
+           "qk_nope_head_dim": c["qk_nope"], "qk_rope_head_dim": c["qk_rope"],
+           "v_head_dim": c["v_head"], "kv_lora_rank": c["kv_lora"], "q_lora_rank": None,
+           "mla_use_nope": True, "rms_norm_eps": c["eps"], "vocab_size": c["vocab"],
+           "tie_word_embeddings": False, "bos_token_id": 1, "eos_token_id": 2,
+           "linear_attn_config": {"head_dim": D, "num_heads": H,
+                                  "short_conv_kernel_size": c["conv_k"],
+                                  "kda_layers": kda_layers,
+                                  "full_attn_layers": sorted(full)}}
+    manifest = {"format_version": 0, "arch": "kimi_linear", "tensor_prefix": "", "config": cfg,
+                "expert_quant": {"fmt": "VQ3R", "stages": 3, "vec_dim": VEC_DIM,
+                                 "entries": ENTRIES, "index_block": BLOCK, "bits_per_weight": 3},
+                "layers": layers, "trunk": t.index}
+    with open(os.path.join(out, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=1)
+    return c
