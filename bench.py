@@ -1218,7 +1218,7 @@ def run_engine_workload(args):
         return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
     cdir, wt = _container(args)
     n = args.warmup + args.steps
-    clk = ClockSampler(0)
+    clk = Clocks(0)
     clk.start()
     cu = _engine(CUDA_ENGINE, cdir, n)
     clocks = clk.stop()

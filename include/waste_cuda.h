@@ -107,6 +107,19 @@ typedef struct {
      * over heads through waste_kernels.rmsnorm_gated). */
     void (*rmsnorm_gated_heads)(int nh, int C, const float *x, const float *gate,
                                 const float *weight, float eps, float *y);
+    /* A whole moe_layer on the device for a layer whose trunk (F32 router,
+     * optional bias, Q8G shared expert of group 128) the engine handed over
+     * with moe_trunk_load and moe_activation: one token, out[hidden] =
+     * routed experts (router order) + shared expert, routed[K] the chosen
+     * ids (NULL allowed). A negative return leaves the engine's own path.
+     * WASTE_CUDA_MOE_LAYER=0 leaves moe_layer NULL. */
+    int  (*moe_trunk_load)(int layer, int n_experts, int hidden, int top_k, int renorm,
+                           float routed_scale, const float *router, const float *bias,
+                           int sh_inter, const int8_t *sh_gate, const uint16_t *sh_gate_s,
+                           const int8_t *sh_up, const uint16_t *sh_up_s,
+                           const int8_t *sh_down, const uint16_t *sh_down_s);
+    int  (*moe_activation)(int layer, int act, float situ_beta, float situ_linear_beta);
+    int  (*moe_layer)(int layer, const float *x, float *out, int *routed);
 } waste_vq_slots;
 
 /* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */

@@ -21,7 +21,9 @@
  * from where the save left off.
  *
  * Each eval's wall-clock time is printed ("eval <e>: next token <t> (<ms>
- * ms)"), and the time to open the container ("open: <ms> ms").
+ * ms)"), the time to open the container ("open: <ms> ms") and, with
+ * WASTE_PROFILE=1, the engine's own phase times per eval over the evals
+ * after the first three ("prof <phase>: ...").
  */
 #include "waste.h"
 
@@ -107,7 +109,15 @@ int main(int argc, char **argv)
     const float *lg = NULL;
     size_t vocab = 0;
     int32_t tok = 0, tok_saved = 0;
+    /* the profile is reported over the decode evals after the first two */
+    const double *prof = (const double *)dlsym(h, "waste_prof");
+    const uint64_t *prof_n = (const uint64_t *)dlsym(h, "waste_prof_n");
+    double prof0[16] = {0};
+    uint64_t prof0_n[16] = {0};
+    const int prof_from = nev > 4 ? 3 : 0;
     for (int e = 0; e < nev; e++) {
+        if (prof && prof_n && e == prof_from)
+            for (int i = 0; i < 16; i++) { prof0[i] = prof[i]; prof0_n[i] = prof_n[i]; }
         const int again = snap && e == 1 + half;   /* the prompt after the reset */
         if (again) {
             tok_saved = tok;
@@ -136,6 +146,18 @@ int main(int argc, char **argv)
      * links it (a dependency of the patched engine library) */
     uint64_t (*launches)(void) = (uint64_t (*)(void))dlsym(h, "waste_cuda_launch_count");
     if (launches) printf("cuda launches: %llu\n", (unsigned long long)launches());
+    /* the engine's own phase timers (WASTE_PROFILE=1), per eval over the
+     * evals from prof_from on */
+    if (prof && prof_n && getenv("WASTE_PROFILE")) {
+        static const char *names[] = { "lutb", "kda", "mla", "moe", "expert_read",
+                                       "expert_mm", "head", "lut_apply", "matmul" };
+        const int ne = nev - prof_from;
+        for (int i = 0; i < 9; i++)
+            if (prof_n[i] > prof0_n[i])
+                printf("prof %s: %.3f ms per eval in %llu calls (evals %d..%d)\n", names[i],
+                       (prof[i] - prof0[i]) * 1e3 / ne,
+                       (unsigned long long)(prof_n[i] - prof0_n[i]), prof_from, nev - 1);
+    }
     vocab32 = (int32_t)vocab;
     fseek(out, 4, SEEK_SET);
     fwrite(&vocab32, 4, 1, out);

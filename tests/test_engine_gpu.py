@@ -127,3 +127,38 @@ def test_engine_snapshot_with_state_on_device(tmp_path):
         assert np.array_equal(lg_s[1 + half].view(np.uint32), lg_u[0].view(np.uint32))
         assert np.array_equal(lg_s[2 + half:].view(np.uint32), lg_u[1 + half:].view(np.uint32))
         assert np.array_equal(lg_s[:1 + half].view(np.uint32), lg_u[:1 + half].view(np.uint32))
+
+
+def test_engine_whole_moe_layer_on_device(tmp_path):
+    """A container from warp_b200.synth.write_container (F32 router, Q8G
+    shared expert, KDA and MLA layers) at a small width: the patched engine
+    hands each MoE layer's router and shared expert to the backend and runs
+    the whole moe_layer in one call (the moe_layer slot); tokens match the
+    unmodified engine's and logits stay within 1e-4, as they do with that
+    slot switched off."""
+    import os
+    import subprocess
+    from test_engine import ENGINE_RUN
+    cdir = str(tmp_path / "c")
+    synth.write_container(cdir, seed=3, hidden=256, layers=5, dense_inter=512, moe_inter=128,
+                          experts=16, top_k=4, kda_heads=4, kda_dim=64, mla_heads=4, qk_nope=32,
+                          qk_rope=16, v_head=32, kv_lora=64, vocab=1024, full_attn=(3,))
+
+    def run(lib, tag, env=None):
+        out = str(tmp_path / f"{tag}.bin")
+        r = subprocess.run([ENGINE_RUN, lib, cdir, out, "6", "1", "17", "42", "99"],
+                           capture_output=True, text=True, timeout=600,
+                           env=dict(os.environ, **(env or {})))
+        assert r.returncode == 0, r.stdout + r.stderr
+        n = [int(l.split(":")[1]) for l in r.stdout.splitlines() if l.startswith("cuda launches")]
+        raw = np.fromfile(out, dtype=np.int32)
+        rows = raw[2:].reshape(int(raw[0]), 1 + int(raw[1]))
+        return (n[0] if n else None), rows[:, 0].copy(), rows[:, 1:].copy().view(np.float32)
+
+    _, tok_ref, lg_ref = run(REF_ENGINE, "ref")
+    l_whole, tok_w, lg_w = run(CUDA_ENGINE, "whole")
+    l_split, tok_s, lg_s = run(CUDA_ENGINE, "split", {"WASTE_CUDA_MOE_LAYER": "0"})
+    assert np.array_equal(tok_ref, tok_w) and np.array_equal(tok_ref, tok_s)
+    for lg in (lg_w, lg_s):
+        assert max(rel_l2(lg[e], lg_ref[e]) for e in range(len(tok_ref))) < 1e-4
+    assert l_whole != l_split                      # the two paths launch different kernels

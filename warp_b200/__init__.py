@@ -80,7 +80,8 @@ class VqSlots(C.Structure):
                 ("vq_bank_free", C.c_void_p), ("moe_experts", C.c_void_p),
                 ("moe_chunk_experts", C.c_void_p), ("vq_bank_load_file", C.c_void_p),
                 ("state_push", C.c_void_p), ("state_pull", C.c_void_p),
-                ("rmsnorm_gated_heads", C.c_void_p)]
+                ("rmsnorm_gated_heads", C.c_void_p), ("moe_trunk_load", C.c_void_p),
+                ("moe_activation", C.c_void_p), ("moe_layer", C.c_void_p)]
 
 
 _lib = None

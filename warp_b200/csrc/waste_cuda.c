@@ -901,6 +901,12 @@ static void rmsg_heads_slot(int nh, int C, const float *x, const float *gate,
 }
 
 static void state_push_slot(const void *host, size_t bytes) { waste_cuda_state_push(host, bytes); }
+
+/* The whole-layer slot: moe_layer on the device for one token. */
+static int moe_layer_slot(int layer, const float *x, float *out, int *routed)
+{
+    return waste_cuda_moe_layer(layer, x, out, routed, NULL);
+}
 static void state_pull_slot(void *host, size_t bytes) { waste_cuda_state_pull(host, bytes); }
 
 
@@ -946,6 +952,9 @@ int waste_register_cuda_vq(waste_vq_slots *s)
     s->vq_bank_load_file = waste_cuda_vq_bank_load_file;
     s->state_push = state_push_slot;
     s->state_pull = state_pull_slot;
+    s->moe_trunk_load = waste_cuda_moe_trunk_load;
+    s->moe_activation = waste_cuda_moe_activation;
+    if (getenv_flag("WASTE_CUDA_MOE_LAYER", 1)) s->moe_layer = moe_layer_slot;
     if (g_rmsg_cpu && getenv_flag("WASTE_CUDA_KDA_NORM", 0)) s->rmsnorm_gated_heads = rmsg_heads_slot;
     return 0;
 }
