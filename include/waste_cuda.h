@@ -31,6 +31,7 @@
  *   waste_cuda_kda_step(_dev)    src/kda.c:26-68 waste_kda_step (slot kda_step,
  *                                src/waste_backend.h:69-72)
  *   waste_cuda_short_conv_*      src/kda.c:84-99 (slot short_conv_step)
+ *   waste_cuda_kda_layer         src/model.c:2417-2472 kda_layer (whole layer)
  *   waste_cuda_rmsnorm_gated_*   src/kda.c:101-111 (slot rmsnorm_gated)
  *   waste_cuda_vq_encode(_dev)   src/vq.c:50-105 waste_vq_encode (the converter's
  *                                RVQ encoder, tools/convert.py:349-363)
@@ -86,6 +87,7 @@ const char *waste_register_cuda(void *waste_kernels_table);
  * a NULL slot means the engine keeps its CPU loop. */
 typedef struct waste_moe_call waste_moe_call;
 typedef struct waste_moe_chunk_call waste_moe_chunk_call;
+typedef struct waste_cuda_kda_layer_desc waste_cuda_kda_layer_desc;
 typedef struct {
     int  (*codebooks_load)(const float *books, int n_books, int entries, int vec_dim);
     int  (*vq_bank_load)(int layer, int n_experts, size_t rec_bytes, int first,
@@ -120,6 +122,10 @@ typedef struct {
                            const int8_t *sh_down, const uint16_t *sh_down_s);
     int  (*moe_activation)(int layer, int act, float situ_beta, float situ_linear_beta);
     int  (*moe_layer)(int layer, const float *x, float *out, int *routed);
+    /* A whole KDA attention layer on the device (see waste_cuda_kda_layer);
+     * a negative return leaves the engine's own path. WASTE_CUDA_KDA_LAYER=0
+     * or WASTE_CUDA_KDA=0 leaves it NULL. */
+    int  (*kda_layer)(const waste_cuda_kda_layer_desc *d, const float *in, float *out);
 } waste_vq_slots;
 
 /* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */
@@ -484,6 +490,34 @@ int waste_cuda_vq_matvec_dev_noalloc(int G, const uint8_t *const *idx,
  * nothing holds are left alone). A call whose state range partly overlaps
  * a held one fails with WASTE_CUDA_E_NOMEM. waste_cuda_release_host_buffers
  * drops every held copy. _dev forms: device pointers, ordered on `stream`. */
+/* A whole KDA attention layer for one token (src/model.c:2417-2472
+ * kda_layer): q/k/v projections each through its short conv, the f
+ * low-rank path and the decay gate, beta = sigmoid(b_proj x), the KDA step
+ * on the layer's state, the g path (low-rank, or full when g_full.W is
+ * set), the gated rmsnorm per head and o_proj: out[hidden] from in[hidden]
+ * in one call. Trunk tensors as the engine holds them (Q8G or Q4G rows of
+ * `rowbytes`, f16 group scales), copied to HBM at first use and keyed by
+ * host address like the trunk slot's; S and the three conv rings are the
+ * engine's state, held in HBM like the kda_step slot's (state_push /
+ * state_pull keep them coherent). */
+typedef struct {
+    const void *W;             /* rows x rowbytes quantised weights        */
+    const uint16_t *ws;        /* rows x ceil(cols/group) f16 scales       */
+    int rows, cols, bits, group;
+    size_t rowbytes;
+} waste_cuda_qtensor;
+struct waste_cuda_kda_layer_desc {
+    int H, D, conv_k, hidden;                   /* C = H * D channels      */
+    waste_cuda_qtensor q, k, v, o, f_a, f_b, g_a, g_b, b, g_full;
+    const float *conv_w[3];                     /* [C][conv_k] each        */
+    const float *A_log;                         /* [H]                     */
+    const float *dt_bias;                       /* [C] or NULL             */
+    const float *o_norm;                        /* [D]                     */
+    float lower_bound, eps;
+    float *S;                                   /* [H][D][D]               */
+    float *conv_ring[3];                        /* [C][conv_k - 1] each    */
+};
+int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, float *out);
 int waste_cuda_kda_step(int H, int K, int V, const float *q, const float *k,
                         const float *v, const float *g_log, const float *beta,
                         float *S, float *o);

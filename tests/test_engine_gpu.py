@@ -129,13 +129,13 @@ def test_engine_snapshot_with_state_on_device(tmp_path):
         assert np.array_equal(lg_s[:1 + half].view(np.uint32), lg_u[:1 + half].view(np.uint32))
 
 
-def test_engine_whole_moe_layer_on_device(tmp_path):
+def test_engine_whole_layers_on_device(tmp_path):
     """A container from warp_b200.synth.write_container (F32 router, Q8G
     shared expert, KDA and MLA layers) at a small width: the patched engine
-    hands each MoE layer's router and shared expert to the backend and runs
-    the whole moe_layer in one call (the moe_layer slot); tokens match the
-    unmodified engine's and logits stay within 1e-4, as they do with that
-    slot switched off."""
+    runs each MoE layer whole in one call (router, experts, shared expert:
+    the moe_layer slot) and each KDA attention layer whole in one call (the
+    kda_layer slot); tokens match the unmodified engine's and logits stay
+    within 1e-4, as they do with either slot switched off."""
     import os
     import subprocess
     from test_engine import ENGINE_RUN
@@ -157,8 +157,10 @@ def test_engine_whole_moe_layer_on_device(tmp_path):
 
     _, tok_ref, lg_ref = run(REF_ENGINE, "ref")
     l_whole, tok_w, lg_w = run(CUDA_ENGINE, "whole")
-    l_split, tok_s, lg_s = run(CUDA_ENGINE, "split", {"WASTE_CUDA_MOE_LAYER": "0"})
-    assert np.array_equal(tok_ref, tok_w) and np.array_equal(tok_ref, tok_s)
-    for lg in (lg_w, lg_s):
+    l_split, tok_s, lg_s = run(CUDA_ENGINE, "split", {"WASTE_CUDA_MOE_LAYER": "0",
+                                                      "WASTE_CUDA_KDA_LAYER": "0"})
+    _, tok_k, lg_k = run(CUDA_ENGINE, "kda_only", {"WASTE_CUDA_MOE_LAYER": "0"})
+    for tok, lg in ((tok_w, lg_w), (tok_s, lg_s), (tok_k, lg_k)):
+        assert np.array_equal(tok_ref, tok)
         assert max(rel_l2(lg[e], lg_ref[e]) for e in range(len(tok_ref))) < 1e-4
-    assert l_whole != l_split                      # the two paths launch different kernels
+    assert l_whole != l_split                      # the paths launch different kernels

@@ -133,9 +133,39 @@ __global__ void __launch_bounds__(128) rmsnorm_gated_kernel(int C, const float *
     }
 }
 
+/* The decay gate in place (src/model.c:2374-2391, per head): with
+ * lower_bound < 0, g = lb / (1 + exp(-ea * z)); else g = -ea * softplus(z)
+ * (z itself above 20), z = g + dt_bias, ea = exp(A_log[h]); and beta =
+ * sigmoid(beta) (src/model.c:2447). exp and log1p rounded once. */
+__global__ void __launch_bounds__(256) kda_gate_kernel(float *g, const float *A_log,
+                                                       const float *dt_bias, int H, int D,
+                                                       float lower_bound, float *beta)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < H) beta[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-beta[i])));
+    if (i >= H * D) return;
+    const float ea = expf_cr(A_log[i / D]);
+    const float z = __fadd_rn(g[i], dt_bias ? dt_bias[i] : 0.0f);
+    if (lower_bound < 0.0f) {
+        g[i] = __fdiv_rn(lower_bound, __fadd_rn(1.0f, expf_cr(-__fmul_rn(ea, z))));
+    } else {
+        const float sp = z > 20.0f ? z : (float)log1p((double)expf_cr(z));
+        g[i] = __fmul_rn(-ea, sp);
+    }
+}
+
 } /* namespace */
 
 extern "C" {
+
+int wc_kda_gate_launch(float *g, const float *A_log, const float *dt_bias, int H, int D,
+                       float lower_bound, float *beta, void *stream)
+{
+    kda_gate_kernel<<<(H * D + 255) / 256, 256, 0, (cudaStream_t)stream>>>(g, A_log, dt_bias, H,
+                                                                            D, lower_bound, beta);
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
 
 int wc_kda_supported(int K, int V)
 {

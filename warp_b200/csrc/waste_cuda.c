@@ -860,6 +860,90 @@ out:
     return rc;
 }
 
+/* The device copy of a trunk tensor (a mirror, made at first use). */
+static int qt_dev(const waste_cuda_qtensor *t, uint8_t **dW, uint16_t **dws, int *ng)
+{
+    if (!t->W || !t->ws || t->rows <= 0 || t->cols <= 0 || t->group <= 0 ||
+        (t->bits != 8 && t->bits != 4 && t->bits != 3) || t->rowbytes == 0)
+        return -1;
+    *ng = (t->cols + t->group - 1) / t->group;
+    const wc_mvq_arg a = { NULL, (const int8_t *)t->W, t->ws, NULL, NULL, t->cols, *ng, t->group,
+                           t->bits, t->rowbytes };
+    return mirror_get(&a, (size_t)t->rows, dW, dws);
+}
+
+static int qt_launch(const waste_cuda_qtensor *t, const float *x, float *y)
+{
+    uint8_t *dW;
+    uint16_t *dws;
+    int ng;
+    if (qt_dev(t, &dW, &dws, &ng)) return -1;
+    wc_mvq_args k = { y, dW, dws, x, 0, t->rows, t->cols, ng, t->group, t->bits, t->rowbytes };
+    return wc_mvq_launch(&k, S.stream);
+}
+
+int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, float *out)
+{
+    int rc = 0;
+    if (!d || !in || !out || d->H <= 0 || d->hidden <= 0 || d->conv_k < 1 ||
+        wc_kda_supported(d->D, d->D) || !d->S || !d->A_log || !d->o_norm)
+        return fail(WASTE_CUDA_E_ARG, "kda_layer: bad descriptor (D 32, 64 or 128)");
+    const int H = d->H, D = d->D, C = H * D, hid = d->hidden, KS = d->conv_k;
+    const int full_gate = d->g_full.W != NULL;
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    {
+        float *dS = (float *)rs_get(d->S, (size_t)H * D * D * sizeof(float));
+        float *dA = (float *)rs_get(d->A_log, (size_t)H * sizeof(float));
+        float *dB = d->dt_bias ? (float *)rs_get(d->dt_bias, (size_t)C * sizeof(float)) : NULL;
+        float *dN = (float *)rs_get(d->o_norm, (size_t)D * sizeof(float));
+        float *dw[3], *dr[3];
+        int ok = dS && dA && dN && (!d->dt_bias || dB);
+        for (int i = 0; i < 3 && ok; i++) {
+            dw[i] = d->conv_w[i] ? (float *)rs_get(d->conv_w[i], (size_t)C * KS * sizeof(float))
+                                 : NULL;
+            dr[i] = KS > 1 && d->conv_ring[i]
+                        ? (float *)rs_get(d->conv_ring[i], (size_t)C * (KS - 1) * sizeof(float))
+                        : NULL;
+            ok = dw[i] && (KS == 1 || dr[i]);
+        }
+        if (!ok) { rc = fail(WASTE_CUDA_E_NOMEM, "kda_layer: device copies"); goto out; }
+        /* staging: in | q k v g o gate | beta | lo_f lo_g | out */
+        const size_t n = (size_t)hid + 6 * (size_t)C + H + 2 * (size_t)D + hid;
+        if ((rc = kda_stage(n))) goto out;
+        float *x = g_kda_dev, *q = x + hid, *k = q + C, *v = k + C, *g = v + C, *o = g + C;
+        float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
+        memcpy(g_kda_pin, in, (size_t)hid * 4);
+        CK(cudaMemcpyAsync(x, g_kda_pin, (size_t)hid * 4, cudaMemcpyHostToDevice, S.stream),
+           "kda_layer in H2D");
+        const waste_cuda_qtensor *qkv[3] = { &d->q, &d->k, &d->v };
+        float *dst[3] = { q, k, v };
+        int lrc = 0;
+        for (int i = 0; i < 3 && !lrc; i++) {
+            lrc = qt_launch(qkv[i], x, dst[i]);
+            if (!lrc) lrc = wc_short_conv_launch(C, KS, dw[i], NULL, dr[i], dst[i], dst[i], S.stream);
+        }
+        if (!lrc) lrc = qt_launch(&d->f_a, x, lf);
+        if (!lrc) lrc = qt_launch(&d->f_b, lf, g);
+        if (!lrc) lrc = qt_launch(&d->b, x, beta);
+        if (!lrc) lrc = wc_kda_gate_launch(g, dA, dB, H, D, d->lower_bound, beta, S.stream);
+        if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, k, v, g, beta, dS, o, S.stream);
+        if (!lrc && full_gate) lrc = qt_launch(&d->g_full, x, gate);
+        if (!lrc && !full_gate) lrc = qt_launch(&d->g_a, x, lg);
+        if (!lrc && !full_gate) lrc = qt_launch(&d->g_b, lg, gate);
+        if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, dN, d->eps, o, S.stream);
+        if (!lrc) lrc = qt_launch(&d->o, o, y);
+        if (lrc) { rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: a launch or a tensor copy failed"); goto out; }
+        CK(cudaMemcpyAsync(g_kda_pin, y, (size_t)hid * 4, cudaMemcpyDeviceToHost, S.stream),
+           "kda_layer out D2H");
+        CK(cudaStreamSynchronize(S.stream), "kda_layer");
+        memcpy(out, g_kda_pin, (size_t)hid * 4);
+    }
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
 /* The slots: the device, or — when it cannot take the call — the CPU
  * kernel the slot held before, on the host copy brought up to date first
  * and pushed back after. */
@@ -955,6 +1039,8 @@ int waste_register_cuda_vq(waste_vq_slots *s)
     s->moe_trunk_load = waste_cuda_moe_trunk_load;
     s->moe_activation = waste_cuda_moe_activation;
     if (getenv_flag("WASTE_CUDA_MOE_LAYER", 1)) s->moe_layer = moe_layer_slot;
+    if (getenv_flag("WASTE_CUDA_KDA", 1) && getenv_flag("WASTE_CUDA_KDA_LAYER", 1))
+        s->kda_layer = waste_cuda_kda_layer;
     if (g_rmsg_cpu && getenv_flag("WASTE_CUDA_KDA_NORM", 0)) s->rmsnorm_gated_heads = rmsg_heads_slot;
     return 0;
 }

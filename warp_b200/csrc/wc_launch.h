@@ -243,6 +243,9 @@ int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float
                          const float *x, float *y, void *stream);
 int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
                             float eps, float *y, void *stream);
+/* The decay gate of H*D channels in place and beta = sigmoid(beta) [H]. */
+int wc_kda_gate_launch(float *g, const float *A_log, const float *dt_bias, int H, int D,
+                       float lower_bound, float *beta, void *stream);
 
 /* The converter's residual-VQ encoder (vq_encode.cu, src/vq.c:50-136):
  * encode n vectors of dim against `stages` books of `entries` each (the
