@@ -17,7 +17,9 @@ touches ~803 MB, far more than the 126 MB L2, so no L2 flush is needed
 between steps.
 
 Also measured: the config-1 VQ3R matvec (4096 x 4096) as a batched launch
-over 32 distinct matrices (203 MB of indices), in HBM GB/s.
+over 32 distinct matrices (203 MB of indices), in HBM GB/s; and, at one GPU,
+config 5 (`engine_step`, see `--workload engine` below) — the whole decode
+step through the reference engine's waste.h with this backend wired in.
 
 `--impl reference` times the reference engine's own moe_layer (compiled
 from the reference sources into oracle/_ref) on this host's cores, same
@@ -766,6 +768,9 @@ def run_warp(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_budget)
     engine = engine_slot_path(base) if world == 1 and not args.decode_only else None
+    engine_step = None
+    if rank == 0 and world == 1 and not args.decode_only and not args.no_engine_step:
+        engine_step = engine_step_leg(args)
 
     if rank == 0:
         line = {
@@ -789,6 +794,7 @@ def run_warp(args):
             "clocks": ck,
             "e2e": e2e,
             "e2e_engine_slot": engine,
+            "engine_step": engine_step,
             "roofline": {"bound": "hbm", "kernel": "gateup_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
@@ -1212,25 +1218,56 @@ ENGINE_METRIC = ("decode tok/s through the engine's waste.h (full Kimi-Linear-48
                  "step: 27 layers, KDA + MLA attention, 26 VQ3R MoE layers, batch 1)")
 
 
-def run_engine_workload(args):
+def engine_step_measure(args, steps=10, warmup=3):
+    """Config 5 measured: the patched engine's decode steps on the synthetic
+    container (clocks sampled meanwhile), then a bounded sample of the
+    unmodified engine on it, and their agreement."""
     def rel_l2(a, b):
         a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
         return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
     cdir, wt = _container(args)
-    n = args.warmup + args.steps
     clk = Clocks(0)
     clk.start()
-    cu = _engine(CUDA_ENGINE, cdir, n)
+    cu = _engine(CUDA_ENGINE, cdir, warmup + steps)
     clocks = clk.stop()
-    dec = cu["ms"][1 + args.warmup:]
-    v = 1e3 / statistics.mean(dec)
-    # the unmodified engine on the same container: a bounded sample
-    rs = max(3, min(args.steps, 8))
-    ref = _engine(REF_ENGINE, cdir, args.warmup + rs)
-    rdec = ref["ms"][1 + args.warmup:]
-    cpu = 1e3 / statistics.mean(rdec)
+    dec = cu["ms"][1 + warmup:]
+    rs = max(3, min(steps, 8))
+    ref = _engine(REF_ENGINE, cdir, warmup + rs)
+    rdec = ref["ms"][1 + warmup:]
     m = min(len(cu["tok"]), len(ref["tok"]))
-    worst = max(rel_l2(cu["logits"][e], ref["logits"][e]) for e in range(m))
+    return {"cu": cu, "dec": dec, "ref": ref, "rdec": rdec, "clocks": clocks, "write_s": wt,
+            "tokens_equal": cu["tok"][:m] == ref["tok"][:m], "evals_compared": m,
+            "worst": max(rel_l2(cu["logits"][e], ref["logits"][e]) for e in range(m))}
+
+
+def engine_step_leg(args):
+    """The default line's config-5 object (one GPU), or None when the engine
+    builds are missing."""
+    if not (os.path.exists(ENGINE_RUN) and os.path.exists(CUDA_ENGINE) and
+            os.path.exists(REF_ENGINE)):
+        return None
+    r = engine_step_measure(args)
+    v = 1e3 / statistics.mean(r["dec"])
+    cpu = 1e3 / statistics.mean(r["rdec"])
+    return {"metric": ENGINE_METRIC, "value": v, "unit": UNIT, "steps": len(r["dec"]),
+            "ms_per_step": statistics.mean(r["dec"]),
+            "timing": "wall clock of each decode step's waste_eval (host API, copies included)",
+            "config": {"workload": "kimi_linear_48b_full_decode_step", "layers": 27,
+                       "kda_layers": 21, "mla_layers": 6, "moe_layers": 26,
+                       "container_write_s": r["write_s"], "engine_open_ms": r["cu"]["open_ms"]},
+            "clocks": r["clocks"],
+            "parity": {"tokens_equal": r["tokens_equal"], "worst_logits_rel_l2": r["worst"],
+                       "evals_compared": r["evals_compared"]},
+            "cpu_baseline": {"value": cpu, "unit": UNIT, "cores": os.cpu_count(),
+                             "kind": "reference",
+                             "sample": f"{len(r['rdec'])} decode steps of the unmodified engine"}}
+
+
+def run_engine_workload(args):
+    r = engine_step_measure(args, steps=args.steps, warmup=args.warmup)
+    cu, dec = r["cu"], r["dec"]
+    v = 1e3 / statistics.mean(dec)
+    cpu = 1e3 / statistics.mean(r["rdec"])
     launches = cu["launches"] or 0
     per_step = launches / max(len(cu["ms"]), 1)
     hid, vocab = 2304, 163840
@@ -1244,17 +1281,17 @@ def run_engine_workload(args):
                        "kda_layers": 21, "mla_layers": 6, "moe_layers": 26, "experts": 256,
                        "top_k": 8, "hidden": hid, "vocab": vocab, "prompt_tokens": len(C5_PROMPT),
                        "timing": "wall clock of each decode step's waste_eval (host API)",
-                       "container_write_s": wt, "engine_open_ms": cu["open_ms"],
+                       "container_write_s": r["write_s"], "engine_open_ms": cu["open_ms"],
                        "backend": cu["build"]},
-            "gpu_launches": int(per_step * len(dec)), "clocks": clocks,
+            "gpu_launches": int(per_step * len(dec)), "clocks": r["clocks"],
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": hid * 4,
                     "d2h_bytes_per_step": vocab * 4},
-            "parity": {"tokens_equal": cu["tok"][:m] == ref["tok"][:m],
-                       "worst_logits_rel_l2": worst, "evals_compared": m,
+            "parity": {"tokens_equal": r["tokens_equal"], "worst_logits_rel_l2": r["worst"],
+                       "evals_compared": r["evals_compared"],
                        "against": "the unmodified reference engine, same container and prompt"},
             "cpu_baseline": {"value": cpu, "unit": UNIT, "cores": os.cpu_count(),
                              "kind": "reference",
-                             "sample": f"{len(rdec)} decode steps of the unmodified engine "
+                             "sample": f"{len(r['rdec'])} decode steps of the unmodified engine "
                                        "through waste_eval on the same container"}}
     print(json.dumps(line), flush=True)
     return 0
@@ -1280,6 +1317,8 @@ def main():
     ap.add_argument("--workload", choices=("kimi", "k3", "engine"), default="kimi",
                     help="kimi: the Kimi-Linear decode step (default); k3: one K3-class "
                          "MoE layer at batches 1/16/64; engine: config 5 through waste.h")
+    ap.add_argument("--no-engine-step", action="store_true",
+                    help="skip the config-5 leg (the whole decode step through the engine)")
     ap.add_argument("--container", default=None,
                     help="engine: where the synthetic container is (written if missing)")
     ap.add_argument("--batches", default="1,16,64", help="k3: global batches")
