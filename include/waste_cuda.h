@@ -613,6 +613,8 @@ enum {
     WASTE_CUDA_PH_COMBINE,      /* router-order reduce (+ shared)       */
     WASTE_CUDA_PH_MATVEC,       /* batched matvec gathers               */
     WASTE_CUDA_PH_MATVEC_REDUCE,
+    WASTE_CUDA_PH_EP_PUBLISH,   /* expert parallel: tokens into the mailboxes */
+    WASTE_CUDA_PH_EP_FINALIZE,  /* expert parallel: partial sums in rank order */
     WASTE_CUDA_PH_COUNT
 };
 int waste_cuda_profile(int on);

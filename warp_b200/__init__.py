@@ -44,7 +44,8 @@ EXPORTS = (
     "waste_cuda_vq_lloyd_dev", "waste_cuda_kda_layer",
 )
 
-PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce")
+PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce", "ep_publish",
+          "ep_finalize")
 
 OK, E_ARG, E_DEVICE, E_RECORD, E_NOBANK, E_NOMEM, E_NODEV = 0, -1, -2, -3, -4, -5, -6
 DERR_ROUTE_WAIT, DERR_TMA_WAIT, DERR_BAD_EXPERT, DERR_PEER_WAIT = 1, 2, 4, 8

@@ -548,6 +548,8 @@ __device__ __forceinline__ bool ep_wait_all(const wc_ep_link &l, const unsigned 
 __global__ void __launch_bounds__(256) ep_publish_kernel(wc_ep_link l, const float *x)
 {
     __shared__ unsigned int e;
+    pdl_trigger();                   /* the router may start staging its rows */
+    pdl_wait();                      /* x: the previous kernel's output */
     if (threadIdx.x == 0) e = *ep_epoch(l) + 1;
     __syncthreads();
     const size_t n4 = (size_t)l.T * l.hidden / 4, off = (size_t)l.rank * l.T * l.hidden;
@@ -567,6 +569,12 @@ __global__ void __launch_bounds__(256) ep_finalize_kernel(wc_ep_link l, float *o
                                                          const float *resid, unsigned int *err)
 {
     __shared__ int ok;
+    /* launched programmatically behind the combine: nothing here reads what
+     * the combine writes before the partial-sum flags say it is in (the
+     * combine's last block releases this rank's flag after every block's
+     * stores), so the grid-dependency wait is not needed; the next kernel
+     * may start its own prologue at once */
+    pdl_trigger();
     const unsigned int e = *ep_epoch(l);
     if (threadIdx.x == 0) ok = ep_wait_all(l, ep_pflags(l, l.rank), e, err);
     __syncthreads();
@@ -2224,7 +2232,11 @@ extern "C" int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigne
                                     void *stream)
 {
     (void)err;
-    ep_publish_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(*l, x);
+    const int pe = prof_begin(WC_PH_EP_PUBLISH, (cudaStream_t)stream);
+    const cudaError_t e = launch(ep_publish_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream,
+                                 !P.on, *l, x);
+    prof_end(pe, (cudaStream_t)stream);
+    if (e != cudaSuccess) return (int)e;
     g_launches += 1;
     return (int)cudaGetLastError();
 }
@@ -2232,8 +2244,11 @@ extern "C" int wc_ep_publish_launch(const wc_ep_link *l, const float *x, unsigne
 extern "C" int wc_ep_finalize_launch(const wc_ep_link *l, float *out, const float *resid,
                                      unsigned int *err, void *stream)
 {
-    ep_finalize_kernel<<<dim3((l->hidden + 255) / 256, l->T), 256, 0, (cudaStream_t)stream>>>(
-        *l, out, resid, err);
+    const int pe = prof_begin(WC_PH_EP_FINALIZE, (cudaStream_t)stream);
+    const cudaError_t e = launch(ep_finalize_kernel, dim3((l->hidden + 255) / 256, l->T),
+                                 dim3(256), 0, (cudaStream_t)stream, !P.on, *l, out, resid, err);
+    prof_end(pe, (cudaStream_t)stream);
+    if (e != cudaSuccess) return (int)e;
     g_launches += 1;
     return (int)cudaGetLastError();
 }

@@ -316,7 +316,7 @@ void     wc_count_launches(int n);
 
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
 enum { WC_PH_ROUTER, WC_PH_ACT, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
-       WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_COUNT };
+       WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_EP_PUBLISH, WC_PH_EP_FINALIZE, WC_PH_COUNT };
 int  wc_prof_enable(int on);
 int  wc_profiling(void);      /* 1 while the phase timers are on */
 void wc_prof_read(double *ms, unsigned long long *cnt, int nphase);
