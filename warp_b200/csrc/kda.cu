@@ -12,11 +12,12 @@
  *
  * B200 mapping. The recurrent state (K x V floats a head, 64 KB at 128 x 128)
  * stays in HBM between tokens. One warp per (head, 32 columns), lane l
- * owning one column of the head's state: the column is read once, decayed
- * and reduced into u (pass A) while it is staged in shared memory, then
- * updated, reduced into o and written once (pass B) — the state crosses
- * HBM twice a token (a read and a write, 128-byte row segments), where the
- * CPU streams it through cache four times. kv = k*kn and qv = q*qn are
+ * owning one column of the head's state: the column is copied into shared
+ * memory with all its rows in flight at once (cp.async), decayed and
+ * reduced into u (pass A), then updated, reduced into o and written once
+ * (pass B) — the state crosses HBM twice a token (a read and a write,
+ * 128-byte row segments), where the CPU streams it through cache four
+ * times. kv = k*kn and qv = q*qn are
  * recomputed per use, which gives the same floats as the CPU's.
  *
  * Arithmetic follows the reference's x86 build term for term (rounded
@@ -35,16 +36,30 @@ using namespace wc;
 
 namespace {
 
-/* src/kda.c:19-24: serial sum of squares, 1 / sqrtf(s + 1e-12). */
-__device__ __forceinline__ float l2_rnorm_serial(const float *x, int n)
+/* src/kda.c:19-24: serial sum of squares, 1 / sqrtf(s + 1e-12). N is a
+ * compile-time length, so the loads are issued well ahead of the (serial)
+ * adds. */
+template <int N>
+__device__ __forceinline__ float l2_rnorm_serial(const float *x)
 {
     float s = 0.0f;
-    for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+#pragma unroll 32
+    for (int i = 0; i < N; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s, 1e-12f)));
 }
 
+/* 4-byte asynchronous copy global -> shared (cp.async), so that all K rows
+ * of a lane's column are in flight at once. */
+__device__ __forceinline__ void cp_async4(float *dst, const float *src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;"
+                 ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
+}
+
 /* grid (H, ceil(V/32)), one warp: lane l owns column c = 32*blockIdx.y + l
- * of head blockIdx.x, staged in shared memory between the two passes. */
+ * of head blockIdx.x. The column is copied into shared memory first, all
+ * K rows at once (one memory round trip instead of one per few rows), and
+ * both passes work on it there. */
 template <int K>
 __global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__restrict__ q,
                                                       const float *__restrict__ k,
@@ -58,6 +73,12 @@ __global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__rest
     __shared__ float norms[2];
     const int h = blockIdx.x, lane = threadIdx.x;
     const int c = blockIdx.y * 32 + lane;
+    float *Sc = S + (size_t)h * K * V + c;
+    if (c < V) {
+#pragma unroll 16
+        for (int kk = 0; kk < K; kk++) cp_async4(&col[kk][lane], Sc + (size_t)kk * V);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     for (int i = lane; i < K; i += 32) {
         qs[i] = q[(size_t)h * K + i];
         ks[i] = k[(size_t)h * K + i];
@@ -66,24 +87,24 @@ __global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__rest
     __syncwarp();
     if (lane == 0) {
         const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)K));
-        norms[0] = __fmul_rn(l2_rnorm_serial(qs, K), qscale);
+        norms[0] = __fmul_rn(l2_rnorm_serial<K>(qs), qscale);
     } else if (lane == 16) {
-        norms[1] = l2_rnorm_serial(ks, K);
+        norms[1] = l2_rnorm_serial<K>(ks);
     }
     __syncwarp();
     const float qn = norms[0], kn = norms[1];
+    asm volatile("cp.async.wait_group 0;" ::: "memory");   /* this lane's own column */
     if (c >= V) return;
-    float *Sc = S + (size_t)h * K * V + c;
     float u = 0.0f;
-#pragma unroll 8
+#pragma unroll 32
     for (int kk = 0; kk < K; kk++) {
-        const float r = __fmul_rn(Sc[(size_t)kk * V], dec[kk]);
+        const float r = __fmul_rn(col[kk][lane], dec[kk]);
         col[kk][lane] = r;
         u = __fadd_rn(u, __fmul_rn(r, __fmul_rn(ks[kk], kn)));
     }
     const float d = __fmul_rn(beta[h], __fsub_rn(v[(size_t)h * V + c], u));
     float acc = 0.0f;
-#pragma unroll 8
+#pragma unroll 32
     for (int kk = 0; kk < K; kk++) {
         const float r = __fadd_rn(col[kk][lane], __fmul_rn(d, __fmul_rn(ks[kk], kn)));
         acc = __fadd_rn(acc, __fmul_rn(r, __fmul_rn(qs[kk], qn)));
