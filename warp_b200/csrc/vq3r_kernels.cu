@@ -2219,6 +2219,44 @@ __global__ void resid_add_kernel(float *out, const float *resid, const float *y,
     if (i < n) out[i] = __fadd_rn(resid[i], y[i]);
 }
 
+/* blockIdx.y = copy; every thread's loads issued before its stores. */
+__global__ void __launch_bounds__(256) copy_words_kernel(const wc_copy_args c)
+{
+    const int k = blockIdx.y;
+    if (k >= c.n) return;
+    const uint32_t *src = static_cast<const uint32_t *>(c.src[k]);
+    uint32_t *dst = static_cast<uint32_t *>(c.dst[k]);
+    const size_t n = c.bytes[k] / 4, stride = (size_t)gridDim.x * blockDim.x;
+    constexpr int U = 8;
+    for (size_t base = (size_t)blockIdx.x * blockDim.x + threadIdx.x; base < n; base += U * stride) {
+        uint32_t v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const size_t i = base + u * stride;
+            v[u] = i < n ? __ldcv(src + i) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const size_t i = base + u * stride;
+            if (i < n) __stcs(dst + i, v[u]);
+        }
+    }
+}
+
+extern "C" int wc_copy_launch(const wc_copy_args *c, void *stream)
+{
+    size_t most = 0;
+    for (int k = 0; k < c->n && k < WC_COPY_MAX; k++)
+        if (c->bytes[k] > most) most = c->bytes[k];
+    if (c->n <= 0 || c->n > WC_COPY_MAX || most == 0) return (int)cudaErrorInvalidValue;
+    const size_t words = most / 4;
+    unsigned blocks = (unsigned)((words + 256 * 8 - 1) / (256 * 8));
+    if (blocks > 64) blocks = 64;
+    copy_words_kernel<<<dim3(blocks, c->n), 256, 0, (cudaStream_t)stream>>>(*c);
+    g_launches += 1;
+    return (int)cudaGetLastError();
+}
+
 extern "C" int wc_resid_add_launch(float *out, const float *resid, const float *y, size_t n,
                                    void *stream)
 {

@@ -106,6 +106,9 @@ static struct {
     size_t tmp_bytes;
     /* fetch layer+1's router and shared expert into L2 during layer */
     int prefetch_next;
+    /* pinned host buffers are mapped at their own addresses: the host
+     * calls move their small inputs and results with one copy kernel */
+    int host_direct;
     /* the host layer call's results in one block, so one copy brings them
      * back: out [res_lat] | route [WC_MAX_TOPK] | weights [WC_MAX_TOPK] | err */
     float *d_res, *h_res;
@@ -283,6 +286,23 @@ static int pick_device(int requested)
 }
 
 /* Workspace for T tokens at the largest shapes loaded so far. */
+/* The small copies of one host call between pinned host buffers and device
+ * buffers (at most WC_COPY_MAX, 256 KB in all): one copy kernel, whose
+ * loads and stores cross the bus in one round trip, when the pinned
+ * buffers are mapped at their own addresses; else one copy-engine transfer
+ * each (the copy engine pays a setup of several microseconds per transfer). */
+static cudaError_t small_copies(const wc_copy_args *c, enum cudaMemcpyKind kind)
+{
+    size_t total = 0;
+    for (int k = 0; k < c->n; k++) total += c->bytes[k];
+    if (S.host_direct && total <= (256u << 10)) return (cudaError_t)wc_copy_launch(c, S.stream);
+    for (int k = 0; k < c->n; k++) {
+        const cudaError_t e = cudaMemcpyAsync(c->dst[k], c->src[k], c->bytes[k], kind, S.stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages)
 {
     const size_t need = wc_moe_ws_floats(T, K, E, lat, inter, si, stages);
@@ -342,6 +362,13 @@ static int init_locked(int device)
     CK(cudaMalloc((void **)&S.d_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "w");
     CK(cudaMallocHost((void **)&S.h_idx, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(int)), "h_idx");
     CK(cudaMallocHost((void **)&S.h_w, (size_t)WC_CHUNK_MAX * WC_MAX_TOPK * sizeof(float)), "h_w");
+    {
+        void *dp = NULL;
+        S.host_direct = getenv_flag("WASTE_CUDA_HOST_COPY_KERNEL", 1) &&
+                        cudaHostGetDevicePointer(&dp, S.h_idx, 0) == cudaSuccess &&
+                        dp == (void *)S.h_idx;
+        cudaGetLastError();
+    }
     snprintf(S.name, sizeof S.name, "CUDA sm_100a (%s)", p.name);
     {
         const char *pe = getenv("WASTE_CUDA_PREFETCH");
@@ -1631,11 +1658,12 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
     memcpy(S.h_x, x, xb);
     memcpy(S.h_idx, idx, (size_t)T * K * sizeof(int));
     memcpy(S.h_w, w, (size_t)T * K * sizeof(float));
-    CK(cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream), "x H2D");
-    CK(cudaMemcpyAsync(S.d_idx, S.h_idx, (size_t)T * K * sizeof(int), cudaMemcpyHostToDevice,
-                       S.stream), "idx H2D");
-    CK(cudaMemcpyAsync(S.d_w, S.h_w, (size_t)T * K * sizeof(float), cudaMemcpyHostToDevice,
-                       S.stream), "w H2D");
+    {
+        const wc_copy_args cin = { { S.d_x, S.d_idx, S.d_w, NULL }, { S.h_x, S.h_idx, S.h_w, NULL },
+                                   { xb, (size_t)T * K * sizeof(int), (size_t)T * K * sizeof(float), 0 },
+                                   3 };
+        CK(small_copies(&cin, cudaMemcpyHostToDevice), "x, route, weights in");
+    }
     if (L->kb.stages == 4) {
         if ((rc = p6_experts(L, T, K, act, situ_beta, situ_lbeta, order_by_id))) goto out;
     } else if (order_by_id && pf_wanted(L, T, K)) {
@@ -1665,7 +1693,10 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
         if (wc_moe_supported(&a)) { rc = fail(WASTE_CUDA_E_ARG, "expert shape outside the kernels' bounds"); goto out; }
         CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
     }
-    CK(cudaMemcpyAsync(S.h_out, S.d_out, xb, cudaMemcpyDeviceToHost, S.stream), "ysum D2H");
+    {
+        const wc_copy_args cout = { { S.h_out }, { S.d_out }, { xb }, 1 };
+        CK(small_copies(&cout, cudaMemcpyDeviceToHost), "ysum out");
+    }
     CK(cudaStreamSynchronize(S.stream), "expert loop");
     if (read_device_errors(1)) {
         rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
@@ -2276,11 +2307,12 @@ static int layer_graph(cudaGraphExec_t *gx, unsigned *gx_epoch, const wc_moe_arg
     if (*gx) { cudaGraphExecDestroy(*gx); *gx = NULL; }
     cudaGraph_t g = NULL;
     CK(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
-    cudaError_t e = cudaMemcpyAsync(S.d_x, S.h_x, xb, cudaMemcpyHostToDevice, S.stream);
+    const wc_copy_args cin = { { S.d_x }, { S.h_x }, { xb }, 1 };
+    const wc_copy_args cout = { { S.h_res }, { S.d_res },
+                                { res_floats(S.res_lat) * sizeof(float) }, 1 };
+    cudaError_t e = small_copies(&cin, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = (cudaError_t)wc_moe_launch(a, S.stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(S.h_res, S.d_res, res_floats(S.res_lat) * sizeof(float),
-                            cudaMemcpyDeviceToHost, S.stream);
+    if (e == cudaSuccess) e = small_copies(&cout, cudaMemcpyDeviceToHost);
     const cudaError_t ee = cudaStreamEndCapture(S.stream, &g);   /* always end it */
     if (e == cudaSuccess) e = ee;
     if (e == cudaSuccess) e = cudaGraphInstantiate(gx, g, 0);

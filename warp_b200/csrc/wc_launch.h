@@ -94,6 +94,20 @@ int wc_ep_finalize_launch(const wc_ep_link *l, float *out, const float *resid,
 /* out[i] = resid[i] + y[i], i < n (out may alias y). */
 int wc_resid_add_launch(float *out, const float *resid, const float *y, size_t n, void *stream);
 
+/* Up to four copies of 4-byte words in one launch, for the small per-call
+ * transfers between pinned host memory (mapped into the device's address
+ * space) and device buffers: a kernel's loads and stores cross the bus in
+ * one round trip, where each copy-engine transfer costs its own setup.
+ * Pointers 4-byte aligned, sizes multiples of 4. */
+#define WC_COPY_MAX 4
+typedef struct {
+    void *dst[WC_COPY_MAX];
+    const void *src[WC_COPY_MAX];
+    size_t bytes[WC_COPY_MAX];
+    int n;
+} wc_copy_args;
+int wc_copy_launch(const wc_copy_args *c, void *stream);
+
 typedef struct {
     wc_bank bank;
     const float *books;       /* [n_books][256][8] fp32                      */
