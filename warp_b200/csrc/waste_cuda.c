@@ -473,6 +473,8 @@ static struct {
 } g_mirror[WC_MIRRORS];
 static float *g_mvq_x, *g_mvq_y;
 static size_t g_mvq_xcap, g_mvq_ycap;
+static float *g_mvq_hx, *g_mvq_hy;                  /* pinned staging of x and y */
+static size_t g_mvq_hxcap, g_mvq_hycap;
 static void (*g_mvq_cpu)(int b, int e, void *arg);   /* the slot's previous occupant */
 static size_t g_trunk_min = (size_t)1 << 20;         /* WASTE_CUDA_TRUNK_MIN bytes */
 
@@ -538,6 +540,25 @@ static void mirrors_free(void)
     cudaFree(g_mvq_y);
     g_mvq_x = g_mvq_y = NULL;
     g_mvq_xcap = g_mvq_ycap = 0;
+    cudaFreeHost(g_mvq_hx);
+    cudaFreeHost(g_mvq_hy);
+    g_mvq_hx = g_mvq_hy = NULL;
+    g_mvq_hxcap = g_mvq_hycap = 0;
+}
+
+/* A pinned host buffer of at least `bytes` (grown, never shrunk). */
+static int pinned_at_least(float **p, size_t *cap, size_t bytes)
+{
+    if (bytes <= *cap) return 0;
+    cudaFreeHost(*p);
+    *p = NULL;
+    *cap = 0;
+    if (cudaMallocHost((void **)p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    *cap = bytes;
+    return 0;
 }
 
 /* The device side of one slot call, under g_mu: 0, or -1 (the caller
@@ -564,14 +585,25 @@ static int mvq_device(int b, int e, const wc_mvq_arg *a)
     }
     wc_mvq_args k = { g_mvq_y, dW, dws, g_mvq_x, b, e, a->in, a->ng, a->group, a->bits,
                       a->rowbytes };
-    if (cudaMemcpyAsync(g_mvq_x, a->xs, xb, cudaMemcpyHostToDevice, S.stream) != cudaSuccess ||
+    /* x and (up to 256 KB of) y through pinned staging and the copy
+     * kernel; a longer y range (lm_head) straight into the caller's memory */
+    const size_t yr = (size_t)(e - b) * sizeof(float);
+    const int stage_y = S.host_direct && yr <= (256u << 10) &&
+                        !pinned_at_least(&g_mvq_hy, &g_mvq_hycap, yr);
+    if (pinned_at_least(&g_mvq_hx, &g_mvq_hxcap, xb)) return -1;
+    memcpy(g_mvq_hx, a->xs, xb);
+    const wc_copy_args cin = { { g_mvq_x }, { g_mvq_hx }, { xb }, 1 };
+    const wc_copy_args cout = { { g_mvq_hy }, { g_mvq_y + b }, { yr }, 1 };
+    if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess ||
         wc_mvq_launch(&k, S.stream) != 0 ||
-        cudaMemcpyAsync(a->y + b, g_mvq_y + b, (size_t)(e - b) * sizeof(float),
-                        cudaMemcpyDeviceToHost, S.stream) != cudaSuccess ||
+        (stage_y ? small_copies(&cout, cudaMemcpyDeviceToHost)
+                 : cudaMemcpyAsync(a->y + b, g_mvq_y + b, yr, cudaMemcpyDeviceToHost,
+                                   S.stream)) != cudaSuccess ||
         cudaStreamSynchronize(S.stream) != cudaSuccess) {
         cudaGetLastError();
         return -1;
     }
+    if (stage_y) memcpy(a->y + b, g_mvq_hy, yr);
     return 0;
 }
 
@@ -941,8 +973,8 @@ int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, fl
         float *x = g_kda_dev, *q = x + hid, *k = q + C, *v = k + C, *g = v + C, *o = g + C;
         float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
         memcpy(g_kda_pin, in, (size_t)hid * 4);
-        CK(cudaMemcpyAsync(x, g_kda_pin, (size_t)hid * 4, cudaMemcpyHostToDevice, S.stream),
-           "kda_layer in H2D");
+        const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1 };
+        CK(small_copies(&cin, cudaMemcpyHostToDevice), "kda_layer in");
         const waste_cuda_qtensor *qkv[3] = { &d->q, &d->k, &d->v };
         float *dst[3] = { q, k, v };
         int lrc = 0;
@@ -961,8 +993,8 @@ int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, fl
         if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, dN, d->eps, o, S.stream);
         if (!lrc) lrc = qt_launch(&d->o, o, y);
         if (lrc) { rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: a launch or a tensor copy failed"); goto out; }
-        CK(cudaMemcpyAsync(g_kda_pin, y, (size_t)hid * 4, cudaMemcpyDeviceToHost, S.stream),
-           "kda_layer out D2H");
+        const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1 };
+        CK(small_copies(&cout, cudaMemcpyDeviceToHost), "kda_layer out");
         CK(cudaStreamSynchronize(S.stream), "kda_layer");
         memcpy(out, g_kda_pin, (size_t)hid * 4);
     }
