@@ -32,6 +32,8 @@
  *                                src/waste_backend.h:69-72)
  *   waste_cuda_short_conv_*      src/kda.c:84-99 (slot short_conv_step)
  *   waste_cuda_kda_layer         src/model.c:2417-2472 kda_layer (whole layer)
+ *   waste_cuda_mla_layer         src/model.c:2577-2649 mla_layer with its absorbed
+ *                                head loop mla_head_range (:2530-2575)
  *   waste_cuda_rmsnorm_gated_*   src/kda.c:101-111 (slot rmsnorm_gated)
  *   waste_cuda_vq_encode(_dev)   src/vq.c:50-105 waste_vq_encode (the converter's
  *                                RVQ encoder, tools/convert.py:349-363)
@@ -88,6 +90,7 @@ const char *waste_register_cuda(void *waste_kernels_table);
 typedef struct waste_moe_call waste_moe_call;
 typedef struct waste_moe_chunk_call waste_moe_chunk_call;
 typedef struct waste_cuda_kda_layer_desc waste_cuda_kda_layer_desc;
+typedef struct waste_cuda_mla_layer_desc waste_cuda_mla_layer_desc;
 typedef struct {
     int  (*codebooks_load)(const float *books, int n_books, int entries, int vec_dim);
     int  (*vq_bank_load)(int layer, int n_experts, size_t rec_bytes, int first,
@@ -126,6 +129,10 @@ typedef struct {
      * a negative return leaves the engine's own path. WASTE_CUDA_KDA_LAYER=0
      * or WASTE_CUDA_KDA=0 leaves it NULL. */
     int  (*kda_layer)(const waste_cuda_kda_layer_desc *d, const float *in, float *out);
+    /* A whole MLA attention layer on the device (see waste_cuda_mla_layer);
+     * a negative return leaves the engine's own path. WASTE_CUDA_MLA_LAYER=0
+     * leaves it NULL. */
+    int  (*mla_layer)(const waste_cuda_mla_layer_desc *d, int pos, const float *in, float *out);
 } waste_vq_slots;
 
 /* Fills `s` and returns 0, or returns WASTE_CUDA_E_NODEV (slots left NULL). */
@@ -518,6 +525,34 @@ struct waste_cuda_kda_layer_desc {
     float *conv_ring[3];                        /* [C][conv_k - 1] each    */
 };
 int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, float *out);
+
+/* A whole MLA attention layer for one token at position `pos`
+ * (src/model.c:2577-2649 mla_layer): the query (q_proj, or q_a_proj ->
+ * rmsnorm -> q_b_proj when q_lora > 0), the latent kv_a_proj_with_mqa(in)
+ * with kv_a_layernorm over its first kv_lora values, the rotary pairs
+ * (skipped when nope is set), the latent stored at row pos of the layer's
+ * cache, the absorbed attention of every head over rows 0..pos (q~ =
+ * W_kb^T q_nope, scores times `scale`, softmax, context, W_vb), the optional
+ * sigmoid output gate (g.W set), and o_proj: out[hidden] in one call. The
+ * cache is the engine's latcache[L] ([kv_cap][kv_lora + qk_rope] floats):
+ * held in HBM from the first call, keyed by host address; every call also
+ * writes its new row into the host copy, so the engine's own reads of the
+ * cache (a snapshot save) see it, and state_push after the engine writes
+ * rows (a snapshot load) updates the HBM copy. kv_b_proj in 8- or 4-bit
+ * groups; pos < kv_cap. Sums in the reference's order where it fixes one
+ * (q~, the context, the softmax sum); the dot products lane-strided. */
+struct waste_cuda_mla_layer_desc {
+    int heads, qk_nope, qk_rope, v_head, kv_lora, q_lora, hidden, kv_cap;
+    int nope;                                   /* 1: no rotary pairs      */
+    waste_cuda_qtensor q, q_a, q_b, kv_a, kv_b, o, g;
+    const float *q_a_norm;                      /* [q_lora], with q_lora   */
+    const float *kv_a_norm;                     /* [kv_lora]               */
+    const float *rope_inv_freq;                 /* [qk_rope / 2]           */
+    float eps, scale;
+    float *latcache;                            /* [kv_cap][kv_lora + qk_rope] */
+};
+int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const float *in,
+                         float *out);
 int waste_cuda_kda_step(int H, int K, int V, const float *q, const float *k,
                         const float *v, const float *g_log, const float *beta,
                         float *S, float *o);

@@ -41,7 +41,7 @@ EXPORTS = (
     "waste_cuda_rmsnorm_gated_heads", "waste_cuda_state_push", "waste_cuda_state_pull",
     "waste_cuda_kda_step_dev", "waste_cuda_short_conv_dev", "waste_cuda_rmsnorm_gated_dev",
     "waste_cuda_vq_encode", "waste_cuda_vq_encode_dev", "waste_cuda_vq_lloyd",
-    "waste_cuda_vq_lloyd_dev", "waste_cuda_kda_layer",
+    "waste_cuda_vq_lloyd_dev", "waste_cuda_kda_layer", "waste_cuda_mla_layer",
 )
 
 PHASES = ("router", "act", "gateup", "down", "combine", "matvec", "matvec_reduce", "ep_publish",
@@ -83,7 +83,7 @@ class VqSlots(C.Structure):
                 ("state_push", C.c_void_p), ("state_pull", C.c_void_p),
                 ("rmsnorm_gated_heads", C.c_void_p), ("moe_trunk_load", C.c_void_p),
                 ("moe_activation", C.c_void_p), ("moe_layer", C.c_void_p),
-                ("kda_layer", C.c_void_p)]
+                ("kda_layer", C.c_void_p), ("mla_layer", C.c_void_p)]
 
 
 _lib = None
@@ -178,6 +178,7 @@ def load_library() -> C.CDLL:
         "waste_cuda_vq_lloyd": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int]),
         "waste_cuda_vq_lloyd_dev": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, P, P]),
         "waste_cuda_kda_layer": (C.c_int, [P, P, P]),
+        "waste_cuda_mla_layer": (C.c_int, [P, C.c_int, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

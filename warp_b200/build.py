@@ -23,7 +23,8 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["vq3r_kernels.cu", "prefill_tc.cu", "trunk_mvq.cu", "matvec_sel.cu", "vq4p.cu", "kda.cu", "vq_encode.cu"]
+CU_SOURCES = ["vq3r_kernels.cu", "prefill_tc.cu", "trunk_mvq.cu", "matvec_sel.cu", "vq4p.cu", "kda.cu",
+              "vq_encode.cu", "mla.cu"]
 C_SOURCES = ["waste_cuda.c"]
 HEADERS = ["vq3r_common.cuh", "wc_launch.h"]
 

@@ -1,0 +1,258 @@
+/*
+ * mla.cu — the MLA attention layer's decode-time kernels on sm_100a, for the
+ * whole-layer slot (the reference's mla_layer, src/model.c:2577-2649, with
+ * the absorbed head loop mla_head_range, :2530-2575).
+ *
+ *   mla_prep_kernel  the latent c = kv_a_proj(x) normalised (rmsnorm with
+ *                    kv_a_layernorm over its first kv_lora values), the
+ *                    rotary pairs applied to it and to every head's query
+ *                    (unless the model is NoPE), the latent stored at its
+ *                    position in the cache and in the result block; or, for
+ *                    the LoRA'd query, the plain rmsnorm of q_a
+ *   mla_head_kernel  per head: q~ = W_kb^T q_nope (rows of kv_b_proj scaled
+ *                    by the query and summed, the reference's order), the
+ *                    scores against every cached latent (times the scale),
+ *                    softmax, the context c~ = sum_s p_s c_s, and o = W_vb c~
+ *   mla_gate_kernel  the optional sigmoid output gate
+ *
+ * B200 mapping. Decode attention over a short latent cache is latency work:
+ * one CTA per head (512 threads, one per latent dimension), the query, the
+ * absorbed query, the scores and the context in shared memory; kv_b_proj's
+ * rows are read once per token with coalesced byte loads (8- or 4-bit
+ * groups of 128, the engine's layout) and the latents once per phase. The
+ * projections around it run through the trunk matvec (trunk_mvq.cu).
+ * Sums keep the reference's orders where it has one (q~ over the query's
+ * dimensions ascending, the context over positions ascending, the softmax
+ * sum ascending); the dot products are lane-strided with warp reductions.
+ */
+#include "vq3r_common.cuh"
+#include "wc_launch.h"
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+using namespace wc;
+
+namespace {
+
+constexpr int kMlaThreads = 512;
+
+/* Value j of row r of a quantised trunk tensor (groups of `group`, one f16
+ * scale per group): 8-bit signed bytes, or 4-bit codes minus 8 (low nibble
+ * first), times the group's scale — src/model.c:407-440. */
+template <int BITS>
+__device__ __forceinline__ float deq_at(const uint8_t *W, const uint16_t *ws, size_t rowbytes,
+                                        int ng, int group, int r, int j)
+{
+    const float s = f16_keep(__ldg(ws + (size_t)r * ng + j / group));
+    const uint8_t *row = W + (size_t)r * rowbytes;
+    if (BITS == 8) return s * (float)(int8_t)__ldg(row + j);
+    const int base = (j / group) * group, i = j - base;
+    const uint8_t byte = __ldg(row + base / 2 + (i >> 1));
+    const int v = (i & 1) ? (byte >> 4) - 8 : (byte & 0x0F) - 8;
+    return s * (float)v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int k = 0; k < nw; k++) t += red[k];
+    return t;
+}
+
+/* One block. x[0..n) normalised in place by weight w (rmsnorm; n <= 8 *
+ * blockDim). With rope (cs/sn, half pairs) the pairs of rot[0..2*half) are
+ * rotated; with q (nh heads of qd, rope part at qk_nope) every head's rope
+ * pairs too. lat_dst / lat_out: where the latent (x then rot, latd values)
+ * is stored (the cache row and the result block). */
+__global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
+    float *x, int n, const float *w, float eps, float *rot, const float *cs, const float *sn,
+    int half, float *q, int nh, int qd, int qk_nope, float *lat_dst, float *lat_out, int latd)
+{
+    __shared__ float red[32];
+    float v[8];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        v[k] = i < n ? x[i] : 0.0f;
+        s = __fadd_rn(s, __fmul_rn(v[k], v[k]));
+    }
+    s = block_sum(s, red);
+    const float r = 1.0f / sqrtf(s / (float)n + eps);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = threadIdx.x + k * blockDim.x;
+        if (i < n) x[i] = __fmul_rn(__fmul_rn(v[k], r), w[i]);
+    }
+    if (half > 0) {                  /* src/model.c:2512-2519 */
+        for (int j = threadIdx.x; j < half; j += blockDim.x) {
+            const float e = rot[2 * j], o = rot[2 * j + 1];
+            rot[2 * j] = __fsub_rn(__fmul_rn(e, cs[j]), __fmul_rn(o, sn[j]));
+            rot[2 * j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, cs[j]));
+        }
+        for (int t = threadIdx.x; t < nh * half; t += blockDim.x) {
+            const int h = t / half, j = t % half;
+            float *qr = q + (size_t)h * qd + qk_nope;
+            const float e = qr[2 * j], o = qr[2 * j + 1];
+            qr[2 * j] = __fsub_rn(__fmul_rn(e, cs[j]), __fmul_rn(o, sn[j]));
+            qr[2 * j + 1] = __fadd_rn(__fmul_rn(e, sn[j]), __fmul_rn(o, cs[j]));
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; lat_dst && i < latd; i += blockDim.x) {
+        lat_dst[i] = x[i];
+        if (lat_out) lat_out[i] = x[i];
+    }
+}
+
+/* grid nh: head h. Shared memory: q (qd) | q~ (kl) | c~ (kl) | scores (S). */
+template <int BITS>
+__global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
+    const float *__restrict__ q, const float *__restrict__ lat, int S, int latd, int kl,
+    int qd, int nope, int rope, int vh, const uint8_t *__restrict__ W,
+    const uint16_t *__restrict__ ws, size_t rowbytes, int ng, int group, float scale,
+    float *__restrict__ o)
+{
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float red[32];
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = blockDim.x >> 5, wrows = nope + vh;
+    float *qs = sm, *qa = qs + ((qd + 3) & ~3), *ca = qa + ((kl + 3) & ~3), *sc = ca + ((kl + 3) & ~3);
+    for (int i = tid; i < qd; i += blockDim.x) qs[i] = q[(size_t)h * qd + i];
+    __syncthreads();
+    /* q~[j] = sum over i ascending of q_i * W_kb[h*wrows + i][j] (exact
+     * zeros skipped, as the reference does) */
+    for (int j = tid; j < kl; j += blockDim.x) {
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < nope; i++) {
+            const float qi = qs[i];
+            if (qi == 0.0f) continue;
+            acc = __fadd_rn(acc, __fmul_rn(qi, deq_at<BITS>(W, ws, rowbytes, ng, group,
+                                                            h * wrows + i, j)));
+        }
+        qa[j] = acc;
+    }
+    __syncthreads();
+    /* scores: one warp per position */
+    for (int s = warp; s < S; s += nw) {
+        const float *cs = lat + (size_t)s * latd;
+        float a = 0.0f, b = 0.0f;
+        for (int j = lane; j < kl; j += 32) a = fmaf(qa[j], __ldg(cs + j), a);
+        for (int j = lane; j < rope; j += 32) b = fmaf(qs[nope + j], __ldg(cs + kl + j), b);
+#pragma unroll
+        for (int k = 16; k > 0; k >>= 1) {
+            a += __shfl_xor_sync(0xffffffffu, a, k);
+            b += __shfl_xor_sync(0xffffffffu, b, k);
+        }
+        if (lane == 0) sc[s] = __fmul_rn(__fadd_rn(a, b), scale);
+    }
+    __syncthreads();
+    /* softmax (src/model.c:511-518): max, exp(x - max), sum, divide */
+    float mx = -3.402823466e38f;
+    for (int s = tid; s < S; s += blockDim.x) mx = fmaxf(mx, sc[s]);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, k));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k = 1; k < nw; k++) mx = fmaxf(mx, red[k]);
+    __syncthreads();
+    for (int s = tid; s < S; s += blockDim.x) sc[s] = expf_cr(__fsub_rn(sc[s], mx));
+    __syncthreads();
+    if (tid == 0) {                  /* the sum in position order */
+        float t = 0.0f;
+        for (int s = 0; s < S; s++) t = __fadd_rn(t, sc[s]);
+        red[0] = t;
+    }
+    __syncthreads();
+    const float sum = red[0];
+    __syncthreads();
+    for (int s = tid; s < S; s += blockDim.x) sc[s] = __fdiv_rn(sc[s], sum);
+    __syncthreads();
+    /* c~[j] = sum over positions ascending of p_s * c_s[j] */
+    for (int j = tid; j < kl; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int s = 0; s < S; s++) acc = __fadd_rn(acc, __fmul_rn(sc[s], __ldg(lat + (size_t)s * latd + j)));
+        ca[j] = acc;
+    }
+    __syncthreads();
+    /* o[i] = W_vb[h*wrows + nope + i] . c~, one warp per row */
+    for (int i = warp; i < vh; i += nw) {
+        const int r = h * wrows + nope + i;
+        float a = 0.0f;
+        for (int j = lane; j < kl; j += 32)
+            a = fmaf(deq_at<BITS>(W, ws, rowbytes, ng, group, r, j), ca[j], a);
+#pragma unroll
+        for (int k = 16; k > 0; k >>= 1) a += __shfl_xor_sync(0xffffffffu, a, k);
+        if (lane == 0) o[(size_t)h * vh + i] = a;
+    }
+}
+
+__global__ void __launch_bounds__(256) mla_gate_kernel(float *o, const float *g, int n)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) o[i] = __fmul_rn(o[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-g[i]))));
+}
+
+} /* namespace */
+
+extern "C" {
+
+size_t wc_mla_head_smem(int qd, int kl, int S)
+{
+    return (size_t)(((qd + 3) & ~3) + 2 * ((kl + 3) & ~3) + S) * sizeof(float);
+}
+
+int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, const float *cs,
+                       const float *sn, int half, float *q, int nh, int qd, int qk_nope,
+                       float *lat_dst, float *lat_out, int latd, void *stream)
+{
+    if (n > 8 * kMlaThreads) return (int)cudaErrorInvalidValue;
+    mla_prep_kernel<<<1, kMlaThreads, 0, (cudaStream_t)stream>>>(
+        x, n, w, eps, rot, cs, sn, half, q, nh, qd, qk_nope, lat_dst, lat_out, latd);
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+int wc_mla_head_launch(const float *q, const float *lat, int S, int latd, int kl, int qd,
+                       int nope, int rope, int vh, int nh, const uint8_t *W, const uint16_t *ws,
+                       size_t rowbytes, int ng, int group, int bits, float scale, float *o,
+                       void *stream)
+{
+    const size_t smem = wc_mla_head_smem(qd, kl, S);
+    cudaError_t e;
+    if (bits == 8) {
+        e = cudaFuncSetAttribute(mla_head_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        mla_head_kernel<8><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
+            q, lat, S, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+    } else if (bits == 4) {
+        e = cudaFuncSetAttribute(mla_head_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        mla_head_kernel<4><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
+            q, lat, S, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+    } else {
+        return (int)cudaErrorInvalidValue;
+    }
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+int wc_mla_gate_launch(float *o, const float *g, int n, void *stream)
+{
+    mla_gate_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(o, g, n);
+    wc_count_launches(1);
+    return (int)cudaGetLastError();
+}
+
+} /* extern "C" */

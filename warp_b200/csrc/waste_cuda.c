@@ -686,6 +686,8 @@ static struct {
 static int g_nrs;
 static float *g_kda_pin, *g_kda_dev;     /* pinned and device staging, floats */
 static size_t g_kda_cap;
+static float *g_mla_pin, *g_mla_dev;     /* the MLA layer's staging */
+static size_t g_mla_cap;
 
 /* The device address of host range [h, h + bytes): inside a held copy, or
  * a copy made now from the host bytes. NULL when it partly overlaps a held
@@ -722,6 +724,10 @@ static void states_free(void)
     cudaFree(g_kda_dev);
     g_kda_pin = g_kda_dev = NULL;
     g_kda_cap = 0;
+    cudaFreeHost(g_mla_pin);
+    cudaFree(g_mla_dev);
+    g_mla_pin = g_mla_dev = NULL;
+    g_mla_cap = 0;
 }
 
 /* Copies the parts of [h, h + bytes) held in HBM one way or the other. */
@@ -1003,6 +1009,102 @@ out:
     return rc;
 }
 
+/* ---- MLA: the whole attention layer, its latent cache in HBM ------------- */
+
+static int mla_stage(size_t floats)
+{
+    if (floats <= g_mla_cap) return 0;
+    cudaFreeHost(g_mla_pin);
+    cudaFree(g_mla_dev);
+    g_mla_pin = g_mla_dev = NULL;
+    g_mla_cap = 0;
+    if (cudaMallocHost((void **)&g_mla_pin, floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc((void **)&g_mla_dev, floats * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(WASTE_CUDA_E_NOMEM, "MLA staging");
+    }
+    g_mla_cap = floats;
+    return 0;
+}
+
+int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const float *in, float *out)
+{
+    int rc = 0;
+    if (!d || !in || !out || d->heads <= 0 || d->hidden <= 0 || d->kv_lora <= 0 ||
+        d->kv_lora > 4096 || d->qk_nope <= 0 || d->qk_rope < 0 || (d->qk_rope & 1) ||
+        d->v_head <= 0 || !d->latcache || !d->kv_a_norm || pos < 0 || pos >= d->kv_cap ||
+        !d->kv_b.W || (d->kv_b.bits != 8 && d->kv_b.bits != 4) || d->kv_b.cols != d->kv_lora ||
+        d->kv_b.rows != d->heads * (d->qk_nope + d->v_head) || !d->kv_a.W || !d->o.W ||
+        (d->q_lora > 0 ? (!d->q_a.W || !d->q_b.W || !d->q_a_norm || d->q_lora > 4096) : !d->q.W) ||
+        (!d->nope && d->qk_rope > 0 && !d->rope_inv_freq))
+        return fail(WASTE_CUDA_E_ARG, "mla_layer: bad descriptor or position");
+    const int nh = d->heads, qd = d->qk_nope + d->qk_rope, vh = d->v_head, kl = d->kv_lora;
+    const int latd = kl + d->qk_rope, hid = d->hidden, half = d->nope ? 0 : d->qk_rope / 2;
+    const int S_ = pos + 1;
+    if (wc_mla_head_smem(qd, kl, S_) > 200u * 1024)
+        return fail(WASTE_CUDA_E_ARG, "mla_layer: %d positions exceed the head kernel's "
+                    "shared memory", S_);
+    pthread_mutex_lock(&g_mu);
+    if (!S.inited && (rc = init_locked(-1))) goto out;
+    {
+        float *dlat = (float *)rs_get(d->latcache, (size_t)d->kv_cap * latd * sizeof(float));
+        float *dkvn = (float *)rs_get(d->kv_a_norm, (size_t)kl * sizeof(float));
+        float *dqan = d->q_lora > 0 ? (float *)rs_get(d->q_a_norm, (size_t)d->q_lora * 4) : NULL;
+        uint8_t *kW;
+        uint16_t *kws;
+        int kng;
+        if (!dlat || !dkvn || (d->q_lora > 0 && !dqan) || qt_dev(&d->kv_b, &kW, &kws, &kng)) {
+            rc = fail(WASTE_CUDA_E_NOMEM, "mla_layer: device copies");
+            goto out;
+        }
+        /* staging: in x | cs | sn ; out y | latent row ; work q | c | q_a | o | g */
+        const size_t n_in = (size_t)hid + 2 * (size_t)half, n_out = (size_t)hid + latd;
+        const size_t n = n_in + n_out + (size_t)nh * qd + latd + (size_t)d->q_lora +
+                         2 * (size_t)nh * vh;
+        if ((rc = mla_stage(n))) goto out;
+        float *x = g_mla_dev, *cs = x + hid, *sn = cs + half, *y = sn + half, *lrow = y + hid;
+        float *q = lrow + latd, *ckv = q + (size_t)nh * qd, *qa = ckv + latd;
+        float *o = qa + d->q_lora, *g = o + (size_t)nh * vh;
+        memcpy(g_mla_pin, in, (size_t)hid * 4);
+        for (int j = 0; j < half; j++) {        /* src/model.c:2502-2510, on the host's libm */
+            const float a = (float)pos * d->rope_inv_freq[j];
+            g_mla_pin[hid + j] = cosf(a);
+            g_mla_pin[hid + half + j] = sinf(a);
+        }
+        const wc_copy_args cin = { { x }, { g_mla_pin }, { n_in * 4 }, 1 };
+        CK(small_copies(&cin, cudaMemcpyHostToDevice), "mla_layer in");
+        int lrc = 0;
+        if (d->q_lora > 0) {
+            lrc = qt_launch(&d->q_a, x, qa);
+            if (!lrc) lrc = wc_mla_prep_launch(qa, d->q_lora, dqan, d->eps, NULL, NULL, NULL, 0,
+                                               NULL, 0, 0, 0, NULL, NULL, 0, S.stream);
+            if (!lrc) lrc = qt_launch(&d->q_b, qa, q);
+        } else {
+            lrc = qt_launch(&d->q, x, q);
+        }
+        if (!lrc) lrc = qt_launch(&d->kv_a, x, ckv);
+        if (!lrc) lrc = wc_mla_prep_launch(ckv, kl, dkvn, d->eps, ckv + kl, cs, sn, half, q, nh, qd,
+                                           d->qk_nope, dlat + (size_t)pos * latd, lrow, latd,
+                                           S.stream);
+        if (!lrc) lrc = wc_mla_head_launch(q, dlat, S_, latd, kl, qd, d->qk_nope, d->qk_rope, vh, nh,
+                                           kW, kws, d->kv_b.rowbytes, kng, d->kv_b.group,
+                                           d->kv_b.bits, d->scale, o, S.stream);
+        if (!lrc && d->g.W) lrc = qt_launch(&d->g, x, g);
+        if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
+        if (!lrc) lrc = qt_launch(&d->o, o, y);
+        if (lrc) { rc = fail(WASTE_CUDA_E_DEVICE, "mla_layer: a launch or a tensor copy failed"); goto out; }
+        const wc_copy_args cout = { { g_mla_pin + n_in }, { y }, { n_out * 4 }, 1 };
+        CK(small_copies(&cout, cudaMemcpyDeviceToHost), "mla_layer out");
+        CK(cudaStreamSynchronize(S.stream), "mla_layer");
+        memcpy(out, g_mla_pin + n_in, (size_t)hid * 4);
+        /* the engine's own copy of the cache row (its snapshot save reads it) */
+        memcpy(d->latcache + (size_t)pos * latd, g_mla_pin + n_in + hid, (size_t)latd * 4);
+    }
+out:
+    pthread_mutex_unlock(&g_mu);
+    return rc;
+}
+
 /* The slots: the device, or — when it cannot take the call — the CPU
  * kernel the slot held before, on the host copy brought up to date first
  * and pushed back after. */
@@ -1100,6 +1202,7 @@ int waste_register_cuda_vq(waste_vq_slots *s)
     if (getenv_flag("WASTE_CUDA_MOE_LAYER", 1)) s->moe_layer = moe_layer_slot;
     if (getenv_flag("WASTE_CUDA_KDA", 1) && getenv_flag("WASTE_CUDA_KDA_LAYER", 1))
         s->kda_layer = waste_cuda_kda_layer;
+    if (getenv_flag("WASTE_CUDA_MLA_LAYER", 1)) s->mla_layer = waste_cuda_mla_layer;
     if (g_rmsg_cpu && getenv_flag("WASTE_CUDA_KDA_NORM", 0)) s->rmsnorm_gated_heads = rmsg_heads_slot;
     return 0;
 }

@@ -328,6 +328,17 @@ int wc_mvq_launch(const wc_mvq_args *a, void *stream);
 uint64_t wc_launches(void);
 void     wc_count_launches(int n);
 
+/* MLA attention (mla.cu). */
+size_t wc_mla_head_smem(int qd, int kl, int S);
+int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, const float *cs,
+                       const float *sn, int half, float *q, int nh, int qd, int qk_nope,
+                       float *lat_dst, float *lat_out, int latd, void *stream);
+int wc_mla_head_launch(const float *q, const float *lat, int S, int latd, int kl, int qd,
+                       int nope, int rope, int vh, int nh, const uint8_t *W, const uint16_t *ws,
+                       size_t rowbytes, int ng, int group, int bits, float scale, float *o,
+                       void *stream);
+int wc_mla_gate_launch(float *o, const float *g, int n, void *stream);
+
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
 enum { WC_PH_ROUTER, WC_PH_ACT, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
        WC_PH_MATVEC, WC_PH_MATVEC_REDUCE, WC_PH_EP_PUBLISH, WC_PH_EP_FINALIZE, WC_PH_COUNT };
