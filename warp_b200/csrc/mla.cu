@@ -73,8 +73,12 @@ __device__ __forceinline__ float block_sum(float v, float *red)
  * is stored (the cache row and the result block). */
 __global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
     float *x, int n, const float *w, float eps, float *rot, const float *cs, const float *sn,
-    int half, float *q, int nh, int qd, int qk_nope, float *lat_dst, float *lat_out, int latd)
+    int half, float *q, int nh, int qd, int qk_nope, float *lat, const int *pos_p,
+    float *lat_out, int latd)
 {
+    /* the cache row of this token's position (read from device memory, so
+     * one launch serves every position) */
+    float *lat_dst = lat && pos_p ? lat + (size_t)(*pos_p) * latd : nullptr;
     __shared__ float red[32];
     float v[8];
     float s = 0.0f;
@@ -112,10 +116,11 @@ __global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
     }
 }
 
-/* grid nh: head h. Shared memory: q (qd) | q~ (kl) | c~ (kl) | scores (S). */
+/* grid nh: head h, over cache rows 0..*pos_p. Shared memory: q (qd) | q~
+ * (kl) | c~ (kl) | scores (up to the cache's rows). */
 template <int BITS>
 __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
-    const float *__restrict__ q, const float *__restrict__ lat, int S, int latd, int kl,
+    const float *__restrict__ q, const float *__restrict__ lat, const int *pos_p, int latd, int kl,
     int qd, int nope, int rope, int vh, const uint8_t *__restrict__ W,
     const uint16_t *__restrict__ ws, size_t rowbytes, int ng, int group, float scale,
     float *__restrict__ o)
@@ -124,6 +129,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
     __shared__ float red[32];
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nw = blockDim.x >> 5, wrows = nope + vh;
+    const int S = *pos_p + 1;
     float *qs = sm, *qa = qs + ((qd + 3) & ~3), *ca = qa + ((kl + 3) & ~3), *sc = ca + ((kl + 3) & ~3);
     for (int i = tid; i < qd; i += blockDim.x) qs[i] = q[(size_t)h * qd + i];
     __syncthreads();
@@ -213,34 +219,34 @@ size_t wc_mla_head_smem(int qd, int kl, int S)
 
 int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, const float *cs,
                        const float *sn, int half, float *q, int nh, int qd, int qk_nope,
-                       float *lat_dst, float *lat_out, int latd, void *stream)
+                       float *lat, const int *pos_p, float *lat_out, int latd, void *stream)
 {
     if (n > 8 * kMlaThreads) return (int)cudaErrorInvalidValue;
     mla_prep_kernel<<<1, kMlaThreads, 0, (cudaStream_t)stream>>>(
-        x, n, w, eps, rot, cs, sn, half, q, nh, qd, qk_nope, lat_dst, lat_out, latd);
+        x, n, w, eps, rot, cs, sn, half, q, nh, qd, qk_nope, lat, pos_p, lat_out, latd);
     wc_count_launches(1);
     return (int)cudaGetLastError();
 }
 
-int wc_mla_head_launch(const float *q, const float *lat, int S, int latd, int kl, int qd,
-                       int nope, int rope, int vh, int nh, const uint8_t *W, const uint16_t *ws,
-                       size_t rowbytes, int ng, int group, int bits, float scale, float *o,
-                       void *stream)
+int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S_max, int latd,
+                       int kl, int qd, int nope, int rope, int vh, int nh, const uint8_t *W,
+                       const uint16_t *ws, size_t rowbytes, int ng, int group, int bits,
+                       float scale, float *o, void *stream)
 {
-    const size_t smem = wc_mla_head_smem(qd, kl, S);
+    const size_t smem = wc_mla_head_smem(qd, kl, S_max);
     cudaError_t e;
     if (bits == 8) {
         e = cudaFuncSetAttribute(mla_head_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return (int)e;
         mla_head_kernel<8><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
-            q, lat, S, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+            q, lat, pos_p, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
     } else if (bits == 4) {
         e = cudaFuncSetAttribute(mla_head_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return (int)e;
         mla_head_kernel<4><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
-            q, lat, S, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+            q, lat, pos_p, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
     } else {
         return (int)cudaErrorInvalidValue;
     }

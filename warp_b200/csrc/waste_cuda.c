@@ -500,6 +500,7 @@ static int mirror_get(const wc_mvq_arg *a, size_t rows, uint8_t **dW, uint16_t *
             }
             cudaFree(g_mirror[i].d_W);
             cudaFree(g_mirror[i].d_ws);
+            g_epoch++;                  /* graphs holding the old copy are stale */
             break;
         }
         if (!g_mirror[i].key) break;
@@ -530,6 +531,7 @@ static int mirror_get(const wc_mvq_arg *a, size_t rows, uint8_t **dW, uint16_t *
 
 static void mirrors_free(void)
 {
+    g_epoch++;
     for (int i = 0; i < WC_MIRRORS; i++) {
         if (!g_mirror[i].key) continue;
         cudaFree(g_mirror[i].d_W);
@@ -715,8 +717,11 @@ static void *rs_get(const void *h, size_t bytes)
     return d;
 }
 
+static void layer_graphs_free(void);
 static void states_free(void)
 {
+    g_epoch++;
+    layer_graphs_free();
     for (int i = 0; i < g_nrs; i++) cudaFree(g_rs[i].dev);
     memset(g_rs, 0, sizeof g_rs);
     g_nrs = 0;
@@ -779,6 +784,7 @@ int waste_cuda_state_push(const void *host, size_t bytes)
 static int kda_stage(size_t floats)
 {
     if (floats <= g_kda_cap) return 0;
+    g_epoch++;
     cudaFreeHost(g_kda_pin);
     cudaFree(g_kda_dev);
     g_kda_pin = g_kda_dev = NULL;
@@ -947,6 +953,108 @@ static int qt_launch(const waste_cuda_qtensor *t, const float *x, float *y)
     return wc_mvq_launch(&k, S.stream);
 }
 
+/* ---- per-layer CUDA graphs of the whole-layer slots ---------------------
+ * A whole-layer call is a dozen kernels (projections, convolutions, the
+ * step, norms) plus the copies in and out; launched one by one from the
+ * host, the launches cost more than the kernels. Each layer's sequence is
+ * captured once into a graph, keyed by the caller's descriptor (the engine
+ * keeps one per layer), at the descriptor's second call: its first call
+ * makes the device copies of the layer's tensors and state, which a capture
+ * cannot. A graph is rebuilt when g_epoch has moved (staging, mirrors or
+ * states reallocated or freed). WASTE_CUDA_LAYER_GRAPHS=0 launches directly. */
+#define WC_LGRAPHS 256
+static struct {
+    const void *key;
+    int seen;
+    unsigned epoch;
+    cudaGraphExec_t gx;
+} g_lg[WC_LGRAPHS];
+static int g_nlg;
+static int g_lg_on = -1;
+
+static void layer_graphs_free(void)
+{
+    for (int i = 0; i < g_nlg; i++)
+        if (g_lg[i].gx) cudaGraphExecDestroy(g_lg[i].gx);
+    memset(g_lg, 0, sizeof g_lg);
+    g_nlg = 0;
+}
+
+/* Runs fn(ctx) on S.stream: from the key's graph, or captured into one, or
+ * directly. 0 or -1. Under g_mu. */
+static int run_layer(const void *key, int (*fn)(void *), void *ctx)
+{
+    if (g_lg_on < 0) g_lg_on = getenv_flag("WASTE_CUDA_LAYER_GRAPHS", 1);
+    int e = -1;
+    for (int i = 0; i < g_nlg; i++)
+        if (g_lg[i].key == key) { e = i; break; }
+    if (e < 0 && g_nlg < WC_LGRAPHS && g_lg_on) {
+        e = g_nlg++;
+        g_lg[e].key = key;
+    }
+    if (e >= 0 && g_lg[e].gx && g_lg[e].epoch == g_epoch)
+        return cudaGraphLaunch(g_lg[e].gx, S.stream) == cudaSuccess ? 0 : -1;
+    if (e >= 0 && g_lg[e].seen) {
+        if (g_lg[e].gx) { cudaGraphExecDestroy(g_lg[e].gx); g_lg[e].gx = NULL; }
+        cudaGraph_t g = NULL;
+        if (cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int r = fn(ctx);
+            const cudaError_t ee = cudaStreamEndCapture(S.stream, &g);   /* always end it */
+            if (!r && ee == cudaSuccess && g &&
+                cudaGraphInstantiate(&g_lg[e].gx, g, 0) == cudaSuccess) {
+                cudaGraphDestroy(g);
+                g_lg[e].epoch = g_epoch;
+                return cudaGraphLaunch(g_lg[e].gx, S.stream) == cudaSuccess ? 0 : -1;
+            }
+            if (g) cudaGraphDestroy(g);
+            g_lg[e].gx = NULL;
+        }
+        cudaGetLastError();             /* a failed capture: launch directly */
+    }
+    if (e >= 0) g_lg[e].seen = 1;
+    return fn(ctx);
+}
+
+struct kda_ctx {
+    const waste_cuda_kda_layer_desc *d;
+    float *dS, *dA, *dB, *dN, *dw[3], *dr[3];
+};
+
+/* The layer's device work on S.stream: x in from the pinned staging, the
+ * kernels, y out to it. */
+static int kda_enqueue(void *p)
+{
+    const struct kda_ctx *k = (const struct kda_ctx *)p;
+    const waste_cuda_kda_layer_desc *d = k->d;
+    const int H = d->H, D = d->D, C = H * D, hid = d->hidden, KS = d->conv_k;
+    const int full_gate = d->g_full.W != NULL;
+    /* staging: in | q k v g o gate | beta | lo_f lo_g | out */
+    float *x = g_kda_dev, *q = x + hid, *kk = q + C, *v = kk + C, *g = v + C, *o = g + C;
+    float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
+    const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1 };
+    if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    const waste_cuda_qtensor *qkv[3] = { &d->q, &d->k, &d->v };
+    float *dst[3] = { q, kk, v };
+    int lrc = 0;
+    for (int i = 0; i < 3 && !lrc; i++) {
+        lrc = qt_launch(qkv[i], x, dst[i]);
+        if (!lrc) lrc = wc_short_conv_launch(C, KS, k->dw[i], NULL, k->dr[i], dst[i], dst[i], S.stream);
+    }
+    if (!lrc) lrc = qt_launch(&d->f_a, x, lf);
+    if (!lrc) lrc = qt_launch(&d->f_b, lf, g);
+    if (!lrc) lrc = qt_launch(&d->b, x, beta);
+    if (!lrc) lrc = wc_kda_gate_launch(g, k->dA, k->dB, H, D, d->lower_bound, beta, S.stream);
+    if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, kk, v, g, beta, k->dS, o, S.stream);
+    if (!lrc && full_gate) lrc = qt_launch(&d->g_full, x, gate);
+    if (!lrc && !full_gate) lrc = qt_launch(&d->g_a, x, lg);
+    if (!lrc && !full_gate) lrc = qt_launch(&d->g_b, lg, gate);
+    if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, k->dN, d->eps, o, S.stream);
+    if (!lrc) lrc = qt_launch(&d->o, o, y);
+    if (lrc) return -1;
+    const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1 };
+    return small_copies(&cout, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
 int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, float *out)
 {
     int rc = 0;
@@ -954,53 +1062,32 @@ int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, fl
         wc_kda_supported(d->D, d->D) || !d->S || !d->A_log || !d->o_norm)
         return fail(WASTE_CUDA_E_ARG, "kda_layer: bad descriptor (D 32, 64 or 128)");
     const int H = d->H, D = d->D, C = H * D, hid = d->hidden, KS = d->conv_k;
-    const int full_gate = d->g_full.W != NULL;
     pthread_mutex_lock(&g_mu);
     if (!S.inited && (rc = init_locked(-1))) goto out;
     {
-        float *dS = (float *)rs_get(d->S, (size_t)H * D * D * sizeof(float));
-        float *dA = (float *)rs_get(d->A_log, (size_t)H * sizeof(float));
-        float *dB = d->dt_bias ? (float *)rs_get(d->dt_bias, (size_t)C * sizeof(float)) : NULL;
-        float *dN = (float *)rs_get(d->o_norm, (size_t)D * sizeof(float));
-        float *dw[3], *dr[3];
-        int ok = dS && dA && dN && (!d->dt_bias || dB);
+        struct kda_ctx k;
+        k.d = d;
+        k.dS = (float *)rs_get(d->S, (size_t)H * D * D * sizeof(float));
+        k.dA = (float *)rs_get(d->A_log, (size_t)H * sizeof(float));
+        k.dB = d->dt_bias ? (float *)rs_get(d->dt_bias, (size_t)C * sizeof(float)) : NULL;
+        k.dN = (float *)rs_get(d->o_norm, (size_t)D * sizeof(float));
+        int ok = k.dS && k.dA && k.dN && (!d->dt_bias || k.dB);
         for (int i = 0; i < 3 && ok; i++) {
-            dw[i] = d->conv_w[i] ? (float *)rs_get(d->conv_w[i], (size_t)C * KS * sizeof(float))
-                                 : NULL;
-            dr[i] = KS > 1 && d->conv_ring[i]
-                        ? (float *)rs_get(d->conv_ring[i], (size_t)C * (KS - 1) * sizeof(float))
-                        : NULL;
-            ok = dw[i] && (KS == 1 || dr[i]);
+            k.dw[i] = d->conv_w[i] ? (float *)rs_get(d->conv_w[i], (size_t)C * KS * sizeof(float))
+                                   : NULL;
+            k.dr[i] = KS > 1 && d->conv_ring[i]
+                          ? (float *)rs_get(d->conv_ring[i], (size_t)C * (KS - 1) * sizeof(float))
+                          : NULL;
+            ok = k.dw[i] && (KS == 1 || k.dr[i]);
         }
         if (!ok) { rc = fail(WASTE_CUDA_E_NOMEM, "kda_layer: device copies"); goto out; }
-        /* staging: in | q k v g o gate | beta | lo_f lo_g | out */
         const size_t n = (size_t)hid + 6 * (size_t)C + H + 2 * (size_t)D + hid;
         if ((rc = kda_stage(n))) goto out;
-        float *x = g_kda_dev, *q = x + hid, *k = q + C, *v = k + C, *g = v + C, *o = g + C;
-        float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
         memcpy(g_kda_pin, in, (size_t)hid * 4);
-        const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1 };
-        CK(small_copies(&cin, cudaMemcpyHostToDevice), "kda_layer in");
-        const waste_cuda_qtensor *qkv[3] = { &d->q, &d->k, &d->v };
-        float *dst[3] = { q, k, v };
-        int lrc = 0;
-        for (int i = 0; i < 3 && !lrc; i++) {
-            lrc = qt_launch(qkv[i], x, dst[i]);
-            if (!lrc) lrc = wc_short_conv_launch(C, KS, dw[i], NULL, dr[i], dst[i], dst[i], S.stream);
+        if (run_layer(d, kda_enqueue, &k)) {
+            rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: a launch or a tensor copy failed");
+            goto out;
         }
-        if (!lrc) lrc = qt_launch(&d->f_a, x, lf);
-        if (!lrc) lrc = qt_launch(&d->f_b, lf, g);
-        if (!lrc) lrc = qt_launch(&d->b, x, beta);
-        if (!lrc) lrc = wc_kda_gate_launch(g, dA, dB, H, D, d->lower_bound, beta, S.stream);
-        if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, k, v, g, beta, dS, o, S.stream);
-        if (!lrc && full_gate) lrc = qt_launch(&d->g_full, x, gate);
-        if (!lrc && !full_gate) lrc = qt_launch(&d->g_a, x, lg);
-        if (!lrc && !full_gate) lrc = qt_launch(&d->g_b, lg, gate);
-        if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, dN, d->eps, o, S.stream);
-        if (!lrc) lrc = qt_launch(&d->o, o, y);
-        if (lrc) { rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: a launch or a tensor copy failed"); goto out; }
-        const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1 };
-        CK(small_copies(&cout, cudaMemcpyDeviceToHost), "kda_layer out");
         CK(cudaStreamSynchronize(S.stream), "kda_layer");
         memcpy(out, g_kda_pin, (size_t)hid * 4);
     }
@@ -1014,6 +1101,7 @@ out:
 static int mla_stage(size_t floats)
 {
     if (floats <= g_mla_cap) return 0;
+    g_epoch++;
     cudaFreeHost(g_mla_pin);
     cudaFree(g_mla_dev);
     g_mla_pin = g_mla_dev = NULL;
@@ -1025,6 +1113,56 @@ static int mla_stage(size_t floats)
     }
     g_mla_cap = floats;
     return 0;
+}
+
+struct mla_ctx {
+    const waste_cuda_mla_layer_desc *d;
+    float *dlat, *dkvn, *dqan;
+    uint8_t *kW;
+    uint16_t *kws;
+    int kng, S_max;
+    size_t n_in, n_out;
+};
+
+/* The layer's device work on S.stream: x, the rope tables and the
+ * position in from the pinned staging, the kernels, y and the new latent
+ * row out to it. Nothing here depends on the position except through the
+ * staged word, so one graph serves every position. */
+static int mla_enqueue(void *p)
+{
+    const struct mla_ctx *k = (const struct mla_ctx *)p;
+    const waste_cuda_mla_layer_desc *d = k->d;
+    const int nh = d->heads, qd = d->qk_nope + d->qk_rope, vh = d->v_head, kl = d->kv_lora;
+    const int latd = kl + d->qk_rope, hid = d->hidden, half = d->nope ? 0 : d->qk_rope / 2;
+    /* staging: in x | cs | sn | pos ; out y | latent row ; work q | c | q_a | o | g */
+    float *x = g_mla_dev, *cs = x + hid, *sn = cs + half;
+    const int *pos_d = (const int *)(sn + half);
+    float *y = x + k->n_in, *lrow = y + hid;
+    float *q = lrow + latd, *ckv = q + (size_t)nh * qd, *qa = ckv + latd;
+    float *o = qa + d->q_lora, *g = o + (size_t)nh * vh;
+    const wc_copy_args cin = { { x }, { g_mla_pin }, { k->n_in * 4 }, 1 };
+    if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    int lrc = 0;
+    if (d->q_lora > 0) {
+        lrc = qt_launch(&d->q_a, x, qa);
+        if (!lrc) lrc = wc_mla_prep_launch(qa, d->q_lora, k->dqan, d->eps, NULL, NULL, NULL, 0,
+                                           NULL, 0, 0, 0, NULL, NULL, NULL, 0, S.stream);
+        if (!lrc) lrc = qt_launch(&d->q_b, qa, q);
+    } else {
+        lrc = qt_launch(&d->q, x, q);
+    }
+    if (!lrc) lrc = qt_launch(&d->kv_a, x, ckv);
+    if (!lrc) lrc = wc_mla_prep_launch(ckv, kl, k->dkvn, d->eps, ckv + kl, cs, sn, half, q, nh, qd,
+                                       d->qk_nope, k->dlat, pos_d, lrow, latd, S.stream);
+    if (!lrc) lrc = wc_mla_head_launch(q, k->dlat, pos_d, k->S_max, latd, kl, qd, d->qk_nope,
+                                       d->qk_rope, vh, nh, k->kW, k->kws, d->kv_b.rowbytes, k->kng,
+                                       d->kv_b.group, d->kv_b.bits, d->scale, o, S.stream);
+    if (!lrc && d->g.W) lrc = qt_launch(&d->g, x, g);
+    if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
+    if (!lrc) lrc = qt_launch(&d->o, o, y);
+    if (lrc) return -1;
+    const wc_copy_args cout = { { g_mla_pin + k->n_in }, { y }, { k->n_out * 4 }, 1 };
+    return small_copies(&cout, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
 int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const float *in, float *out)
@@ -1040,65 +1178,47 @@ int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const floa
         return fail(WASTE_CUDA_E_ARG, "mla_layer: bad descriptor or position");
     const int nh = d->heads, qd = d->qk_nope + d->qk_rope, vh = d->v_head, kl = d->kv_lora;
     const int latd = kl + d->qk_rope, hid = d->hidden, half = d->nope ? 0 : d->qk_rope / 2;
-    const int S_ = pos + 1;
-    if (wc_mla_head_smem(qd, kl, S_) > 200u * 1024)
+    /* the head kernel's shared memory sized for the whole cache (one graph
+     * for every position), or else for this call's rows (launched directly) */
+    const int whole = wc_mla_head_smem(qd, kl, d->kv_cap) <= 200u * 1024;
+    const int S_max = whole ? d->kv_cap : pos + 1;
+    if (wc_mla_head_smem(qd, kl, S_max) > 200u * 1024)
         return fail(WASTE_CUDA_E_ARG, "mla_layer: %d positions exceed the head kernel's "
-                    "shared memory", S_);
+                    "shared memory", pos + 1);
     pthread_mutex_lock(&g_mu);
     if (!S.inited && (rc = init_locked(-1))) goto out;
     {
-        float *dlat = (float *)rs_get(d->latcache, (size_t)d->kv_cap * latd * sizeof(float));
-        float *dkvn = (float *)rs_get(d->kv_a_norm, (size_t)kl * sizeof(float));
-        float *dqan = d->q_lora > 0 ? (float *)rs_get(d->q_a_norm, (size_t)d->q_lora * 4) : NULL;
-        uint8_t *kW;
-        uint16_t *kws;
-        int kng;
-        if (!dlat || !dkvn || (d->q_lora > 0 && !dqan) || qt_dev(&d->kv_b, &kW, &kws, &kng)) {
+        struct mla_ctx k;
+        k.d = d;
+        k.S_max = S_max;
+        k.dlat = (float *)rs_get(d->latcache, (size_t)d->kv_cap * latd * sizeof(float));
+        k.dkvn = (float *)rs_get(d->kv_a_norm, (size_t)kl * sizeof(float));
+        k.dqan = d->q_lora > 0 ? (float *)rs_get(d->q_a_norm, (size_t)d->q_lora * 4) : NULL;
+        if (!k.dlat || !k.dkvn || (d->q_lora > 0 && !k.dqan) ||
+            qt_dev(&d->kv_b, &k.kW, &k.kws, &k.kng)) {
             rc = fail(WASTE_CUDA_E_NOMEM, "mla_layer: device copies");
             goto out;
         }
-        /* staging: in x | cs | sn ; out y | latent row ; work q | c | q_a | o | g */
-        const size_t n_in = (size_t)hid + 2 * (size_t)half, n_out = (size_t)hid + latd;
-        const size_t n = n_in + n_out + (size_t)nh * qd + latd + (size_t)d->q_lora +
+        k.n_in = (size_t)hid + 2 * (size_t)half + 1;
+        k.n_out = (size_t)hid + latd;
+        const size_t n = k.n_in + k.n_out + (size_t)nh * qd + latd + (size_t)d->q_lora +
                          2 * (size_t)nh * vh;
         if ((rc = mla_stage(n))) goto out;
-        float *x = g_mla_dev, *cs = x + hid, *sn = cs + half, *y = sn + half, *lrow = y + hid;
-        float *q = lrow + latd, *ckv = q + (size_t)nh * qd, *qa = ckv + latd;
-        float *o = qa + d->q_lora, *g = o + (size_t)nh * vh;
         memcpy(g_mla_pin, in, (size_t)hid * 4);
         for (int j = 0; j < half; j++) {        /* src/model.c:2502-2510, on the host's libm */
             const float a = (float)pos * d->rope_inv_freq[j];
             g_mla_pin[hid + j] = cosf(a);
             g_mla_pin[hid + half + j] = sinf(a);
         }
-        const wc_copy_args cin = { { x }, { g_mla_pin }, { n_in * 4 }, 1 };
-        CK(small_copies(&cin, cudaMemcpyHostToDevice), "mla_layer in");
-        int lrc = 0;
-        if (d->q_lora > 0) {
-            lrc = qt_launch(&d->q_a, x, qa);
-            if (!lrc) lrc = wc_mla_prep_launch(qa, d->q_lora, dqan, d->eps, NULL, NULL, NULL, 0,
-                                               NULL, 0, 0, 0, NULL, NULL, 0, S.stream);
-            if (!lrc) lrc = qt_launch(&d->q_b, qa, q);
-        } else {
-            lrc = qt_launch(&d->q, x, q);
+        memcpy(g_mla_pin + hid + 2 * half, &pos, sizeof(int));
+        if (whole ? run_layer(d, mla_enqueue, &k) : mla_enqueue(&k)) {
+            rc = fail(WASTE_CUDA_E_DEVICE, "mla_layer: a launch or a tensor copy failed");
+            goto out;
         }
-        if (!lrc) lrc = qt_launch(&d->kv_a, x, ckv);
-        if (!lrc) lrc = wc_mla_prep_launch(ckv, kl, dkvn, d->eps, ckv + kl, cs, sn, half, q, nh, qd,
-                                           d->qk_nope, dlat + (size_t)pos * latd, lrow, latd,
-                                           S.stream);
-        if (!lrc) lrc = wc_mla_head_launch(q, dlat, S_, latd, kl, qd, d->qk_nope, d->qk_rope, vh, nh,
-                                           kW, kws, d->kv_b.rowbytes, kng, d->kv_b.group,
-                                           d->kv_b.bits, d->scale, o, S.stream);
-        if (!lrc && d->g.W) lrc = qt_launch(&d->g, x, g);
-        if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
-        if (!lrc) lrc = qt_launch(&d->o, o, y);
-        if (lrc) { rc = fail(WASTE_CUDA_E_DEVICE, "mla_layer: a launch or a tensor copy failed"); goto out; }
-        const wc_copy_args cout = { { g_mla_pin + n_in }, { y }, { n_out * 4 }, 1 };
-        CK(small_copies(&cout, cudaMemcpyDeviceToHost), "mla_layer out");
         CK(cudaStreamSynchronize(S.stream), "mla_layer");
-        memcpy(out, g_mla_pin + n_in, (size_t)hid * 4);
+        memcpy(out, g_mla_pin + k.n_in, (size_t)hid * 4);
         /* the engine's own copy of the cache row (its snapshot save reads it) */
-        memcpy(d->latcache + (size_t)pos * latd, g_mla_pin + n_in + hid, (size_t)latd * 4);
+        memcpy(d->latcache + (size_t)pos * latd, g_mla_pin + k.n_in + hid, (size_t)latd * 4);
     }
 out:
     pthread_mutex_unlock(&g_mu);

@@ -330,13 +330,16 @@ void     wc_count_launches(int n);
 
 /* MLA attention (mla.cu). */
 size_t wc_mla_head_smem(int qd, int kl, int S);
+/* pos_p: the token's position in device memory (the cache row written,
+ * rows 0..pos attended); S_max: the rows the head kernel's shared memory
+ * is sized for (> pos). */
 int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, const float *cs,
                        const float *sn, int half, float *q, int nh, int qd, int qk_nope,
-                       float *lat_dst, float *lat_out, int latd, void *stream);
-int wc_mla_head_launch(const float *q, const float *lat, int S, int latd, int kl, int qd,
-                       int nope, int rope, int vh, int nh, const uint8_t *W, const uint16_t *ws,
-                       size_t rowbytes, int ng, int group, int bits, float scale, float *o,
-                       void *stream);
+                       float *lat, const int *pos_p, float *lat_out, int latd, void *stream);
+int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S_max, int latd,
+                       int kl, int qd, int nope, int rope, int vh, int nh, const uint8_t *W,
+                       const uint16_t *ws, size_t rowbytes, int ng, int group, int bits,
+                       float scale, float *o, void *stream);
 int wc_mla_gate_launch(float *o, const float *g, int n, void *stream);
 
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
