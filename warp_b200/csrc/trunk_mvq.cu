@@ -26,6 +26,29 @@ using namespace wc;
 namespace {
 
 constexpr int kMvqThreads = 256;
+
+/* Programmatic dependent launch (a no-op for a kernel launched without it):
+ * the next kernel may start its prologue; and the wait for the previous
+ * kernel's results. */
+__device__ __forceinline__ void pdl_trigger_m() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void pdl_wait_m() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_m(void (*kern)(KArgs...), unsigned blocks, size_t smem, cudaStream_t s, bool pdl,
+                     Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(kMvqThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 constexpr int kMvqStages = 2;            /* bulk-copy ring depth of the tile kernel */
 
 __device__ __forceinline__ float warp_sum_f(float v)
@@ -51,6 +74,8 @@ mvq_kernel(float *__restrict__ y, const uint8_t *__restrict__ W, const uint16_t 
 {
     extern __shared__ __align__(16) float xs[];
     const int n = ng * g;
+    pdl_trigger_m();
+    pdl_wait_m();                            /* x: the previous kernel's output */
     for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = i < in ? x[i] : 0.0f;
     __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -127,6 +152,8 @@ mvq_tma_kernel(float *__restrict__ y, const uint8_t *__restrict__ W,
         for (int q = 0; q < kMvqStages; q++)
             if ((int)(blockIdx.x + q * gridDim.x) < ntiles) issue(blockIdx.x + q * gridDim.x, q);
     }
+    pdl_trigger_m();
+    pdl_wait_m();                            /* the weights are constants: only x waits */
     for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = i < in ? x[i] : 0.0f;
     __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -201,10 +228,10 @@ int mvq_go(const wc_mvq_args *a, cudaStream_t s)
     const int cap = 148 * 8;                 /* 8 resident blocks per SM */
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    k<<<blocks, kMvqThreads, smem, s>>>(a->y, a->W, a->ws, a->x, a->r0, a->r1, a->in, a->ng,
-                                         a->group, a->rowbytes);
+    const cudaError_t e = launch_m(k, (unsigned)blocks, smem, s, a->pdl != 0, a->y, a->W, a->ws,
+                                   a->x, a->r0, a->r1, a->in, a->ng, a->group, a->rowbytes);
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 template <int BITS>
@@ -232,10 +259,10 @@ int mvq_tma_go(const wc_mvq_args *a, cudaStream_t s)
     const int ntiles = (a->r1 - a->r0 + tl.R - 1) / tl.R;
     int blocks = 148 * 2;
     if (blocks > ntiles) blocks = ntiles;
-    k<<<blocks, kMvqThreads, smem, s>>>(a->y, a->W, a->ws, a->x, a->r0, a->r1, a->in, a->ng,
-                                         a->rowbytes, tl);
+    const cudaError_t e = launch_m(k, (unsigned)blocks, smem, s, a->pdl != 0, a->y, a->W, a->ws,
+                                   a->x, a->r0, a->r1, a->in, a->ng, a->rowbytes, tl);
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 } /* namespace */

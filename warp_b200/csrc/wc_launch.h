@@ -320,6 +320,9 @@ typedef struct {
     const float *x;
     int r0, r1, in, ng, group, bits;
     size_t rowbytes;
+    int pdl;           /* 1: launched programmatically behind the previous
+                          kernel; the weight copies start before its end
+                          and x is read only after the dependency wait   */
 } wc_mvq_args;
 
 int wc_mvq_launch(const wc_mvq_args *a, void *stream);
