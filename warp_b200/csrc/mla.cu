@@ -39,16 +39,17 @@ constexpr int kMlaThreads = 512;
 
 /* Value j of row r of a quantised trunk tensor (groups of `group`, one f16
  * scale per group): 8-bit signed bytes, or 4-bit codes minus 8 (low nibble
- * first), times the group's scale — src/model.c:407-440. */
+ * first), times the group's scale — src/model.c:407-440. W and ws are the
+ * head's rows staged in shared memory (r counted from the head's first). */
 template <int BITS>
 __device__ __forceinline__ float deq_at(const uint8_t *W, const uint16_t *ws, size_t rowbytes,
                                         int ng, int group, int r, int j)
 {
-    const float s = f16_keep(__ldg(ws + (size_t)r * ng + j / group));
+    const float s = f16_keep(ws[(size_t)r * ng + j / group]);
     const uint8_t *row = W + (size_t)r * rowbytes;
-    if (BITS == 8) return s * (float)(int8_t)__ldg(row + j);
+    if (BITS == 8) return s * (float)(int8_t)row[j];
     const int base = (j / group) * group, i = j - base;
-    const uint8_t byte = __ldg(row + base / 2 + (i >> 1));
+    const uint8_t byte = row[base / 2 + (i >> 1)];
     const int v = (i & 1) ? (byte >> 4) - 8 : (byte & 0x0F) - 8;
     return s * (float)v;
 }
@@ -116,8 +117,10 @@ __global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
     }
 }
 
-/* grid nh: head h, over cache rows 0..*pos_p. Shared memory: q (qd) | q~
- * (kl) | c~ (kl) | scores (up to the cache's rows). */
+/* grid nh: head h, over cache rows 0..*pos_p. Shared memory: the head's
+ * kv_b_proj rows (nope + vh rows, staged by one bulk copy at the start) and
+ * their scales | q (qd) | q~ (kl) | c~ (kl) | scores (up to the cache's
+ * rows). */
 template <int BITS>
 __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
     const float *__restrict__ q, const float *__restrict__ lat, const int *pos_p, int latd, int kl,
@@ -125,14 +128,32 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
     const uint16_t *__restrict__ ws, size_t rowbytes, int ng, int group, float scale,
     float *__restrict__ o)
 {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(16) unsigned char smb[];
     __shared__ float red[32];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int okw;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nw = blockDim.x >> 5, wrows = nope + vh;
+    const uint32_t wb = (uint32_t)((size_t)wrows * rowbytes), sb = (uint32_t)wrows * ng * 2;
+    uint8_t *Ws = smb;
+    uint16_t *wss = reinterpret_cast<uint16_t *>(smb + wb);
+    float *qs = reinterpret_cast<float *>(smb + wb + ((sb + 15) & ~15u));
+    float *qa = qs + ((qd + 3) & ~3), *ca = qa + ((kl + 3) & ~3), *sc = ca + ((kl + 3) & ~3);
+    if (tid == 0) {                  /* the head's rows: constants, before the wait */
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        mbar_expect_tx(&bar, wb + sb);
+        bulk_g2s(Ws, W + (size_t)h * wrows * rowbytes, wb, &bar);
+        bulk_g2s(wss, ws + (size_t)h * wrows * ng, sb, &bar);
+    }
     const int S = *pos_p + 1;
-    float *qs = sm, *qa = qs + ((qd + 3) & ~3), *ca = qa + ((kl + 3) & ~3), *sc = ca + ((kl + 3) & ~3);
     for (int i = tid; i < qd; i += blockDim.x) qs[i] = q[(size_t)h * qd + i];
+    if (tid == 0) okw = mbar_wait(&bar, 0);
     __syncthreads();
+    if (!okw) {                      /* the copy never landed: the head's output is NaN */
+        for (int i = tid; i < vh; i += blockDim.x) o[(size_t)h * vh + i] = __int_as_float(0x7fc00000);
+        return;
+    }
     /* q~[j] = sum over i ascending of q_i * W_kb[h*wrows + i][j] (exact
      * zeros skipped, as the reference does) */
     for (int j = tid; j < kl; j += blockDim.x) {
@@ -141,8 +162,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
         for (int i = 0; i < nope; i++) {
             const float qi = qs[i];
             if (qi == 0.0f) continue;
-            acc = __fadd_rn(acc, __fmul_rn(qi, deq_at<BITS>(W, ws, rowbytes, ng, group,
-                                                            h * wrows + i, j)));
+            acc = __fadd_rn(acc, __fmul_rn(qi, deq_at<BITS>(Ws, wss, rowbytes, ng, group, i, j)));
         }
         qa[j] = acc;
     }
@@ -192,10 +212,10 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
     __syncthreads();
     /* o[i] = W_vb[h*wrows + nope + i] . c~, one warp per row */
     for (int i = warp; i < vh; i += nw) {
-        const int r = h * wrows + nope + i;
+        const int r = nope + i;
         float a = 0.0f;
         for (int j = lane; j < kl; j += 32)
-            a = fmaf(deq_at<BITS>(W, ws, rowbytes, ng, group, r, j), ca[j], a);
+            a = fmaf(deq_at<BITS>(Ws, wss, rowbytes, ng, group, r, j), ca[j], a);
 #pragma unroll
         for (int k = 16; k > 0; k >>= 1) a += __shfl_xor_sync(0xffffffffu, a, k);
         if (lane == 0) o[(size_t)h * vh + i] = a;
@@ -212,9 +232,10 @@ __global__ void __launch_bounds__(256) mla_gate_kernel(float *o, const float *g,
 
 extern "C" {
 
-size_t wc_mla_head_smem(int qd, int kl, int S)
+size_t wc_mla_head_smem(int qd, int kl, int S, int wrows, size_t rowbytes, int ng)
 {
-    return (size_t)(((qd + 3) & ~3) + 2 * ((kl + 3) & ~3) + S) * sizeof(float);
+    const size_t wb = (size_t)wrows * rowbytes, sb = ((size_t)wrows * ng * 2 + 15) & ~(size_t)15;
+    return wb + sb + (size_t)(((qd + 3) & ~3) + 2 * ((kl + 3) & ~3) + S) * sizeof(float);
 }
 
 int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, const float *cs,
@@ -233,7 +254,11 @@ int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S
                        const uint16_t *ws, size_t rowbytes, int ng, int group, int bits,
                        float scale, float *o, void *stream)
 {
-    const size_t smem = wc_mla_head_smem(qd, kl, S_max);
+    /* the bulk copies want 16-byte sizes and addresses */
+    if ((((size_t)(nope + vh) * rowbytes) & 15) || (((size_t)(nope + vh) * ng * 2) & 15) ||
+        ((uintptr_t)W & 15) || ((uintptr_t)ws & 15))
+        return (int)cudaErrorInvalidValue;
+    const size_t smem = wc_mla_head_smem(qd, kl, S_max, nope + vh, rowbytes, ng);
     cudaError_t e;
     if (bits == 8) {
         e = cudaFuncSetAttribute(mla_head_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -1183,9 +1183,10 @@ int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const floa
     const int latd = kl + d->qk_rope, hid = d->hidden, half = d->nope ? 0 : d->qk_rope / 2;
     /* the head kernel's shared memory sized for the whole cache (one graph
      * for every position), or else for this call's rows (launched directly) */
-    const int whole = wc_mla_head_smem(qd, kl, d->kv_cap) <= 200u * 1024;
+    const int wrows = d->qk_nope + vh, kng_ = (kl + d->kv_b.group - 1) / d->kv_b.group;
+    const int whole = wc_mla_head_smem(qd, kl, d->kv_cap, wrows, d->kv_b.rowbytes, kng_) <= 200u * 1024;
     const int S_max = whole ? d->kv_cap : pos + 1;
-    if (wc_mla_head_smem(qd, kl, S_max) > 200u * 1024)
+    if (wc_mla_head_smem(qd, kl, S_max, wrows, d->kv_b.rowbytes, kng_) > 200u * 1024)
         return fail(WASTE_CUDA_E_ARG, "mla_layer: %d positions exceed the head kernel's "
                     "shared memory", pos + 1);
     pthread_mutex_lock(&g_mu);

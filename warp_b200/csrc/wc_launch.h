@@ -332,7 +332,7 @@ uint64_t wc_launches(void);
 void     wc_count_launches(int n);
 
 /* MLA attention (mla.cu). */
-size_t wc_mla_head_smem(int qd, int kl, int S);
+size_t wc_mla_head_smem(int qd, int kl, int S, int wrows, size_t rowbytes, int ng);
 /* pos_p: the token's position in device memory (the cache row written,
  * rows 0..pos attended); S_max: the rows the head kernel's shared memory
  * is sized for (> pos). */
