@@ -183,6 +183,7 @@ typedef void (*wc_conv_fn)(int C, int KS, const float *w, const float *bias, flo
 typedef void (*wc_rmsg_fn)(int C, const float *x, const float *gate, const float *weight,
                            float eps, float *y);
 static void states_free(void);
+static void branches_free(void);
 static void kda_slot(int H, int K, int V, const float *q, const float *k, const float *v,
                      const float *g_log, const float *beta, float *S, float *o, float *scratch);
 static void conv_slot(int C, int KS, const float *w, const float *bias, float *ring,
@@ -427,6 +428,7 @@ void waste_cuda_shutdown(void)
             if (g_stage.ev) cudaEventDestroy(g_stage.done[b]);
         }
         memset(&g_stage, 0, sizeof g_stage);
+        branches_free();
         cudaStreamDestroy(S.stream);
         memset(&S, 0, sizeof S);
         g_noalloc_part = NULL;
@@ -943,17 +945,73 @@ static int qt_dev(const waste_cuda_qtensor *t, uint8_t **dW, uint16_t **dws, int
     return mirror_get(&a, (size_t)t->rows, dW, dws);
 }
 
-static int qt_launch(const waste_cuda_qtensor *t, const float *x, float *y)
+static int qt_launch_on(const waste_cuda_qtensor *t, const float *x, float *y, cudaStream_t st,
+                        int pdl)
 {
     uint8_t *dW;
     uint16_t *dws;
     int ng;
     if (qt_dev(t, &dW, &dws, &ng)) return -1;
-    /* programmatic: the weight copies overlap the kernel before (not while
-     * the phase timers put events between kernels) */
     wc_mvq_args k = { y, dW, dws, x, 0, t->rows, t->cols, ng, t->group, t->bits, t->rowbytes,
-                      !wc_profiling() };
-    return wc_mvq_launch(&k, S.stream);
+                      pdl };
+    return wc_mvq_launch(&k, st);
+}
+
+/* On the library's stream, launched programmatically: the weight copies
+ * overlap the kernel before (not while the phase timers put events between
+ * kernels). */
+static int qt_launch(const waste_cuda_qtensor *t, const float *x, float *y)
+{
+    return qt_launch_on(t, x, y, S.stream, !wc_profiling());
+}
+
+/* Side streams and events for the independent branches of a layer (its
+ * projections of the same input): forked from the library's stream and
+ * joined back, so they run side by side — and become parallel branches of
+ * a layer's graph when captured. Created outside any capture. */
+#define WC_BRANCHES 6
+static cudaStream_t g_side[WC_BRANCHES];
+static cudaEvent_t g_fork, g_join[WC_BRANCHES];
+static int g_branches_ok;
+
+static int branches_ready(void)
+{
+    if (g_branches_ok) return 0;
+    if (cudaEventCreateWithFlags(&g_fork, cudaEventDisableTiming) != cudaSuccess) return -1;
+    for (int i = 0; i < WC_BRANCHES; i++)
+        if (cudaStreamCreateWithFlags(&g_side[i], cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&g_join[i], cudaEventDisableTiming) != cudaSuccess)
+            return -1;
+    g_branches_ok = 1;
+    return 0;
+}
+
+static void branches_free(void)
+{
+    if (!g_branches_ok) return;
+    for (int i = 0; i < WC_BRANCHES; i++) {
+        cudaStreamDestroy(g_side[i]);
+        cudaEventDestroy(g_join[i]);
+    }
+    cudaEventDestroy(g_fork);
+    g_branches_ok = 0;
+}
+
+static int fork_branches(int n)
+{
+    if (cudaEventRecord(g_fork, S.stream) != cudaSuccess) return -1;
+    for (int i = 0; i < n; i++)
+        if (cudaStreamWaitEvent(g_side[i], g_fork, 0) != cudaSuccess) return -1;
+    return 0;
+}
+
+static int join_branches(int n)
+{
+    for (int i = 0; i < n; i++)
+        if (cudaEventRecord(g_join[i], g_side[i]) != cudaSuccess ||
+            cudaStreamWaitEvent(S.stream, g_join[i], 0) != cudaSuccess)
+            return -1;
+    return 0;
 }
 
 /* ---- per-layer CUDA graphs of the whole-layer slots ---------------------
@@ -1036,21 +1094,25 @@ static int kda_enqueue(void *p)
     float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
     const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1 };
     if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    /* the branches that read only x, side by side: q, k and v each through
+     * its short conv; the f path (f_a, f_b); beta's projection; the g path */
     const waste_cuda_qtensor *qkv[3] = { &d->q, &d->k, &d->v };
     float *dst[3] = { q, kk, v };
-    int lrc = 0;
+    int lrc = fork_branches(WC_BRANCHES);
     for (int i = 0; i < 3 && !lrc; i++) {
-        lrc = qt_launch(qkv[i], x, dst[i]);
-        if (!lrc) lrc = wc_short_conv_launch(C, KS, k->dw[i], NULL, k->dr[i], dst[i], dst[i], S.stream);
+        lrc = qt_launch_on(qkv[i], x, dst[i], g_side[i], 0);
+        if (!lrc) lrc = wc_short_conv_launch(C, KS, k->dw[i], NULL, k->dr[i], dst[i], dst[i],
+                                             g_side[i]);
     }
-    if (!lrc) lrc = qt_launch(&d->f_a, x, lf);
-    if (!lrc) lrc = qt_launch(&d->f_b, lf, g);
-    if (!lrc) lrc = qt_launch(&d->b, x, beta);
+    if (!lrc) lrc = qt_launch_on(&d->f_a, x, lf, g_side[3], 0);
+    if (!lrc) lrc = qt_launch_on(&d->f_b, lf, g, g_side[3], 0);
+    if (!lrc) lrc = qt_launch_on(&d->b, x, beta, g_side[4], 0);
+    if (!lrc && full_gate) lrc = qt_launch_on(&d->g_full, x, gate, g_side[5], 0);
+    if (!lrc && !full_gate) lrc = qt_launch_on(&d->g_a, x, lg, g_side[5], 0);
+    if (!lrc && !full_gate) lrc = qt_launch_on(&d->g_b, lg, gate, g_side[5], 0);
+    if (!lrc) lrc = join_branches(WC_BRANCHES);
     if (!lrc) lrc = wc_kda_gate_launch(g, k->dA, k->dB, H, D, d->lower_bound, beta, S.stream);
     if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, kk, v, g, beta, k->dS, o, S.stream);
-    if (!lrc && full_gate) lrc = qt_launch(&d->g_full, x, gate);
-    if (!lrc && !full_gate) lrc = qt_launch(&d->g_a, x, lg);
-    if (!lrc && !full_gate) lrc = qt_launch(&d->g_b, lg, gate);
     if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, k->dN, d->eps, o, S.stream);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
@@ -1086,6 +1148,7 @@ int waste_cuda_kda_layer(const waste_cuda_kda_layer_desc *d, const float *in, fl
         if (!ok) { rc = fail(WASTE_CUDA_E_NOMEM, "kda_layer: device copies"); goto out; }
         const size_t n = (size_t)hid + 6 * (size_t)C + H + 2 * (size_t)D + hid;
         if ((rc = kda_stage(n))) goto out;
+        if (branches_ready()) { rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: side streams"); goto out; }
         memcpy(g_kda_pin, in, (size_t)hid * 4);
         if (run_layer(d, kda_enqueue, &k)) {
             rc = fail(WASTE_CUDA_E_DEVICE, "kda_layer: a launch or a tensor copy failed");
@@ -1145,22 +1208,24 @@ static int mla_enqueue(void *p)
     float *o = qa + d->q_lora, *g = o + (size_t)nh * vh;
     const wc_copy_args cin = { { x }, { g_mla_pin }, { k->n_in * 4 }, 1 };
     if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
-    int lrc = 0;
-    if (d->q_lora > 0) {
-        lrc = qt_launch(&d->q_a, x, qa);
+    /* the query, the latent and the gate read only x: side by side */
+    int lrc = fork_branches(3);
+    if (!lrc && d->q_lora > 0) {
+        lrc = qt_launch_on(&d->q_a, x, qa, g_side[0], 0);
         if (!lrc) lrc = wc_mla_prep_launch(qa, d->q_lora, k->dqan, d->eps, NULL, NULL, NULL, 0,
-                                           NULL, 0, 0, 0, NULL, NULL, NULL, 0, S.stream);
-        if (!lrc) lrc = qt_launch(&d->q_b, qa, q);
-    } else {
-        lrc = qt_launch(&d->q, x, q);
+                                           NULL, 0, 0, 0, NULL, NULL, NULL, 0, g_side[0]);
+        if (!lrc) lrc = qt_launch_on(&d->q_b, qa, q, g_side[0], 0);
+    } else if (!lrc) {
+        lrc = qt_launch_on(&d->q, x, q, g_side[0], 0);
     }
-    if (!lrc) lrc = qt_launch(&d->kv_a, x, ckv);
+    if (!lrc) lrc = qt_launch_on(&d->kv_a, x, ckv, g_side[1], 0);
+    if (!lrc && d->g.W) lrc = qt_launch_on(&d->g, x, g, g_side[2], 0);
+    if (!lrc) lrc = join_branches(3);
     if (!lrc) lrc = wc_mla_prep_launch(ckv, kl, k->dkvn, d->eps, ckv + kl, cs, sn, half, q, nh, qd,
                                        d->qk_nope, k->dlat, pos_d, lrow, latd, S.stream);
     if (!lrc) lrc = wc_mla_head_launch(q, k->dlat, pos_d, k->S_max, latd, kl, qd, d->qk_nope,
                                        d->qk_rope, vh, nh, k->kW, k->kws, d->kv_b.rowbytes, k->kng,
                                        d->kv_b.group, d->kv_b.bits, d->scale, o, S.stream);
-    if (!lrc && d->g.W) lrc = qt_launch(&d->g, x, g);
     if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
@@ -1208,6 +1273,7 @@ int waste_cuda_mla_layer(const waste_cuda_mla_layer_desc *d, int pos, const floa
         const size_t n = k.n_in + k.n_out + (size_t)nh * qd + latd + (size_t)d->q_lora +
                          2 * (size_t)nh * vh;
         if ((rc = mla_stage(n))) goto out;
+        if (branches_ready()) { rc = fail(WASTE_CUDA_E_DEVICE, "mla_layer: side streams"); goto out; }
         memcpy(g_mla_pin, in, (size_t)hid * 4);
         for (int j = 0; j < half; j++) {        /* src/model.c:2502-2510, on the host's libm */
             const float a = (float)pos * d->rope_inv_freq[j];
