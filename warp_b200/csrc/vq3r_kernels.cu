@@ -2222,6 +2222,8 @@ __global__ void resid_add_kernel(float *out, const float *resid, const float *y,
 /* blockIdx.y = copy; every thread's loads issued before its stores. */
 __global__ void __launch_bounds__(256) copy_words_kernel(const wc_copy_args c)
 {
+    pdl_trigger();                   /* the next kernel may stage its constants */
+    pdl_wait();                      /* src: complete */
     const int k = blockIdx.y;
     if (k >= c.n) return;
     const uint32_t *src = static_cast<const uint32_t *>(c.src[k]);
@@ -2252,9 +2254,10 @@ extern "C" int wc_copy_launch(const wc_copy_args *c, void *stream)
     const size_t words = most / 4;
     unsigned blocks = (unsigned)((words + 256 * 8 - 1) / (256 * 8));
     if (blocks > 64) blocks = 64;
-    copy_words_kernel<<<dim3(blocks, c->n), 256, 0, (cudaStream_t)stream>>>(*c);
+    const cudaError_t e = launch(copy_words_kernel, dim3(blocks, c->n), dim3(256), 0,
+                                 (cudaStream_t)stream, c->pdl && !P.on, *c);
     g_launches += 1;
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 extern "C" int wc_resid_add_launch(float *out, const float *resid, const float *y, size_t n,

@@ -1116,7 +1116,7 @@ static int kda_enqueue(void *p)
     if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, k->dN, d->eps, o, S.stream);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
-    const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1 };
+    const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1, 1 };
     return small_copies(&cout, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
@@ -1229,7 +1229,7 @@ static int mla_enqueue(void *p)
     if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
-    const wc_copy_args cout = { { g_mla_pin + k->n_in }, { y }, { k->n_out * 4 }, 1 };
+    const wc_copy_args cout = { { g_mla_pin + k->n_in }, { y }, { k->n_out * 4 }, 1, 1 };
     return small_copies(&cout, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
@@ -2634,7 +2634,7 @@ static int layer_graph(cudaGraphExec_t *gx, unsigned *gx_epoch, const wc_moe_arg
     CK(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
     const wc_copy_args cin = { { S.d_x }, { S.h_x }, { xb }, 1 };
     const wc_copy_args cout = { { S.h_res }, { S.d_res },
-                                { res_floats(S.res_lat) * sizeof(float) }, 1 };
+                                { res_floats(S.res_lat) * sizeof(float) }, 1, 1 };
     cudaError_t e = small_copies(&cin, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = (cudaError_t)wc_moe_launch(a, S.stream);
     if (e == cudaSuccess) e = small_copies(&cout, cudaMemcpyDeviceToHost);

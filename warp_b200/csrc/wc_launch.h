@@ -105,6 +105,9 @@ typedef struct {
     const void *src[WC_COPY_MAX];
     size_t bytes[WC_COPY_MAX];
     int n;
+    int pdl;           /* 1: launched programmatically behind the kernel that
+                          wrote src (it waits for that kernel, not for the
+                          launch boundary) */
 } wc_copy_args;
 int wc_copy_launch(const wc_copy_args *c, void *stream);
 
