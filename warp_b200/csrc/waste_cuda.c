@@ -172,6 +172,23 @@ static struct {
 } g_stage;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
+
+/* Uploads and clears issued outside the library's streams. Those streams
+ * are non-blocking, so nothing orders them after the default stream, and a
+ * cudaMemcpy from pageable memory (or a cudaMemset) may return before the
+ * device holds the bytes: each of these returns only once it does, so a
+ * kernel on any stream launched afterwards reads them. */
+static cudaError_t h2d_now(void *d, const void *h, size_t n)
+{
+    const cudaError_t e = cudaMemcpy(d, h, n, cudaMemcpyHostToDevice);
+    return e != cudaSuccess ? e : cudaStreamSynchronize(0);
+}
+
+static cudaError_t memset_now(void *d, int v, size_t n)
+{
+    const cudaError_t e = cudaMemset(d, v, n);
+    return e != cudaSuccess ? e : cudaStreamSynchronize(0);
+}
 static void ep_shutdown_locked(void);
 static void mirrors_free(void);
 /* the engine's KDA slot signatures (src/waste_backend.h:69-76) */
@@ -237,7 +254,7 @@ static unsigned read_device_errors(int clear)
     /* a wait that gave up leaves tickets, flags and pass counters of that
      * launch half-set: the whole control block (the error word included)
      * starts again from zero */
-    if (v && clear) cudaMemset(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
+    if (v && clear) memset_now(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
     if ((v & WC_ERR_PEER_WAIT) && EP.active) EP.poisoned = 1;
     return v;
 }
@@ -316,7 +333,7 @@ static int ensure_ws(int T, int K, int E, int lat, int inter, int si, int stages
         cudaError_t e = cudaMalloc((void **)&S.d_ws, need * sizeof(float));
         if (e != cudaSuccess) return cuda_fail(e, "workspace");
         /* the router's ticket counters live here and must start at zero */
-        e = cudaMemset(S.d_ws, 0, need * sizeof(float));
+        e = memset_now(S.d_ws, 0, need * sizeof(float));
         if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
         S.ws_floats = need;
     }
@@ -512,8 +529,7 @@ static int mirror_get(const wc_mvq_arg *a, size_t rows, uint8_t **dW, uint16_t *
     uint8_t *w = NULL;
     uint16_t *s = NULL;
     if (cudaMalloc((void **)&w, wb) != cudaSuccess || cudaMalloc((void **)&s, sb) != cudaSuccess ||
-        cudaMemcpy(w, a->W, wb, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(s, a->ws, sb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        h2d_now(w, a->W, wb) != cudaSuccess || h2d_now(s, a->ws, sb) != cudaSuccess) {
         cudaFree(w);
         cudaFree(s);
         cudaGetLastError();
@@ -588,7 +604,7 @@ static int mvq_device(int b, int e, const wc_mvq_arg *a)
         g_mvq_ycap = yb;
     }
     wc_mvq_args k = { g_mvq_y, dW, dws, g_mvq_x, b, e, a->in, a->ng, a->group, a->bits,
-                      a->rowbytes };
+                      a->rowbytes, 0 };
     /* x and (up to 256 KB of) y through pinned staging and the copy
      * kernel; a longer y range (lm_head) straight into the caller's memory */
     const size_t yr = (size_t)(e - b) * sizeof(float);
@@ -596,8 +612,8 @@ static int mvq_device(int b, int e, const wc_mvq_arg *a)
                         !pinned_at_least(&g_mvq_hy, &g_mvq_hycap, yr);
     if (pinned_at_least(&g_mvq_hx, &g_mvq_hxcap, xb)) return -1;
     memcpy(g_mvq_hx, a->xs, xb);
-    const wc_copy_args cin = { { g_mvq_x }, { g_mvq_hx }, { xb }, 1 };
-    const wc_copy_args cout = { { g_mvq_hy }, { g_mvq_y + b }, { yr }, 1 };
+    const wc_copy_args cin = { { g_mvq_x }, { g_mvq_hx }, { xb }, 1, 0 };
+    const wc_copy_args cout = { { g_mvq_hy }, { g_mvq_y + b }, { yr }, 1, 0 };
     if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess ||
         wc_mvq_launch(&k, S.stream) != 0 ||
         (stage_y ? small_copies(&cout, cudaMemcpyDeviceToHost)
@@ -707,7 +723,7 @@ static void *rs_get(const void *h, size_t bytes)
     if (g_nrs == WC_STATES) return NULL;
     uint8_t *d = NULL;
     if (cudaMalloc((void **)&d, bytes) != cudaSuccess ||
-        cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        h2d_now(d, h, bytes) != cudaSuccess) {
         cudaFree(d);
         cudaGetLastError();
         return NULL;
@@ -751,7 +767,7 @@ static int rs_sync(const void *h, size_t bytes, int to_host)
         if (to_host)
             CK(cudaMemcpy((void *)lo, d, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "state D2H");
         else
-            CK(cudaMemcpy(d, lo, (size_t)(hi - lo), cudaMemcpyHostToDevice), "state H2D");
+            CK(h2d_now(d, lo, (size_t)(hi - lo)), "state H2D");
     }
 out:
     return rc;
@@ -1092,7 +1108,7 @@ static int kda_enqueue(void *p)
     /* staging: in | q k v g o gate | beta | lo_f lo_g | out */
     float *x = g_kda_dev, *q = x + hid, *kk = q + C, *v = kk + C, *g = v + C, *o = g + C;
     float *gate = o + C, *beta = gate + C, *lf = beta + H, *lg = lf + D, *y = lg + D;
-    const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1 };
+    const wc_copy_args cin = { { x }, { g_kda_pin }, { (size_t)hid * 4 }, 1, 0 };
     if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
     /* the branches that read only x, side by side: q, k and v each through
      * its short conv; the f path (f_a, f_b); beta's projection; the g path */
@@ -1206,7 +1222,7 @@ static int mla_enqueue(void *p)
     float *y = x + k->n_in, *lrow = y + hid;
     float *q = lrow + latd, *ckv = q + (size_t)nh * qd, *qa = ckv + latd;
     float *o = qa + d->q_lora, *g = o + (size_t)nh * vh;
-    const wc_copy_args cin = { { x }, { g_mla_pin }, { k->n_in * 4 }, 1 };
+    const wc_copy_args cin = { { x }, { g_mla_pin }, { k->n_in * 4 }, 1, 0 };
     if (small_copies(&cin, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
     /* the query, the latent and the gate read only x: side by side */
     int lrc = fork_branches(3);
@@ -1358,7 +1374,7 @@ int waste_cuda_mvq_rows_dev(float *d_y, const void *d_W, const uint16_t *d_ws, c
     {
         const int ng = (in + group - 1) / group;
         wc_mvq_args k = { d_y, (const uint8_t *)d_W, d_ws, d_x, r0, r1, in, ng, group, bits,
-                          rowbytes };
+                          rowbytes, 0 };
         CK((cudaError_t)wc_mvq_launch(&k, stream ? stream : (void *)S.stream), "trunk matvec");
     }
 out:
@@ -1433,7 +1449,7 @@ static int books_upload(const float *books, int n_books, int entries)
             if (m > S.book_absmax[b]) S.book_absmax[b] = m;
         }
     CK(cudaMalloc((void **)&S.d_books, bytes), "codebooks");
-    CK(cudaMemcpy(S.d_books, books, bytes, cudaMemcpyHostToDevice), "codebooks H2D");
+    CK(h2d_now(S.d_books, books, bytes), "codebooks H2D");
     S.n_books = n_books;
     S.cb_entries = entries;
 out:
@@ -1711,8 +1727,8 @@ static int bank_load_locked(int layer, int n_experts, size_t rec_bytes, int firs
         CK(cudaMemcpyAsync(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
                            cudaMemcpyHostToDevice, copy_stream), "bank H2D");
     else
-        CK(cudaMemcpy(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count,
-                      cudaMemcpyHostToDevice), "bank H2D");
+        CK(h2d_now(L->d_base + (size_t)at * rec_bytes, records, rec_bytes * (size_t)count),
+           "bank H2D");
     for (int i = at; i < at + count; i++) {
         L->n_present += !L->present[i];
         L->present[i] = 1;
@@ -1838,11 +1854,10 @@ int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
     L->d_shg_s = L->d_shu_s = L->d_shd_s = NULL;
     const size_t rb = (size_t)n_experts * hidden * sizeof(float);
     CK(cudaMalloc((void **)&L->d_router, rb), "router");
-    CK(cudaMemcpy(L->d_router, router, rb, cudaMemcpyHostToDevice), "router H2D");
+    CK(h2d_now(L->d_router, router, rb), "router H2D");
     if (bias) {
         CK(cudaMalloc((void **)&L->d_bias, (size_t)n_experts * sizeof(float)), "bias");
-        CK(cudaMemcpy(L->d_bias, bias, (size_t)n_experts * sizeof(float),
-                      cudaMemcpyHostToDevice), "bias H2D");
+        CK(h2d_now(L->d_bias, bias, (size_t)n_experts * sizeof(float)), "bias H2D");
     }
     if (sh_inter > 0) {
         const int g = 128;
@@ -1855,12 +1870,12 @@ int waste_cuda_moe_trunk_load(int layer, int n_experts, int hidden, int top_k,
         CK(cudaMalloc((void **)&L->d_shg_s, gs), "shared gate scales");
         CK(cudaMalloc((void **)&L->d_shu_s, gs), "shared up scales");
         CK(cudaMalloc((void **)&L->d_shd_s, ds), "shared down scales");
-        CK(cudaMemcpy(L->d_shg, sh_gate, gb, cudaMemcpyHostToDevice), "H2D");
-        CK(cudaMemcpy(L->d_shu, sh_up, gb, cudaMemcpyHostToDevice), "H2D");
-        CK(cudaMemcpy(L->d_shd, sh_down, db, cudaMemcpyHostToDevice), "H2D");
-        CK(cudaMemcpy(L->d_shg_s, sh_gate_s, gs, cudaMemcpyHostToDevice), "H2D");
-        CK(cudaMemcpy(L->d_shu_s, sh_up_s, gs, cudaMemcpyHostToDevice), "H2D");
-        CK(cudaMemcpy(L->d_shd_s, sh_down_s, ds, cudaMemcpyHostToDevice), "H2D");
+        CK(h2d_now(L->d_shg, sh_gate, gb), "H2D");
+        CK(h2d_now(L->d_shu, sh_up, gb), "H2D");
+        CK(h2d_now(L->d_shd, sh_down, db), "H2D");
+        CK(h2d_now(L->d_shg_s, sh_gate_s, gs), "H2D");
+        CK(h2d_now(L->d_shu_s, sh_up_s, gs), "H2D");
+        CK(h2d_now(L->d_shd_s, sh_down_s, ds), "H2D");
     }
     L->trunk = 1;
     L->E = n_experts;
@@ -1907,8 +1922,7 @@ int waste_cuda_moe_norm_load(int layer, int hidden, const float *norm_w, float e
     cudaFree(L->d_norm);
     L->d_norm = NULL;
     CK(cudaMalloc((void **)&L->d_norm, (size_t)hidden * sizeof(float)), "norm weight");
-    CK(cudaMemcpy(L->d_norm, norm_w, (size_t)hidden * sizeof(float), cudaMemcpyHostToDevice),
-       "norm weight H2D");
+    CK(h2d_now(L->d_norm, norm_w, (size_t)hidden * sizeof(float)), "norm weight H2D");
     L->norm_eps = eps;
 out:
     pthread_mutex_unlock(&g_mu);
@@ -1986,7 +2000,7 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
     {
         const wc_copy_args cin = { { S.d_x, S.d_idx, S.d_w, NULL }, { S.h_x, S.h_idx, S.h_w, NULL },
                                    { xb, (size_t)T * K * sizeof(int), (size_t)T * K * sizeof(float), 0 },
-                                   3 };
+                                   3, 0 };
         CK(small_copies(&cin, cudaMemcpyHostToDevice), "x, route, weights in");
     }
     if (L->kb.stages == 4) {
@@ -2019,7 +2033,7 @@ static int run_experts(int layer, int T, int K, const int *idx, const float *w,
         CK((cudaError_t)wc_moe_launch(&a, S.stream), "expert kernels");
     }
     {
-        const wc_copy_args cout = { { S.h_out }, { S.d_out }, { xb }, 1 };
+        const wc_copy_args cout = { { S.h_out }, { S.d_out }, { xb }, 1, 0 };
         CK(small_copies(&cout, cudaMemcpyDeviceToHost), "ysum out");
     }
     CK(cudaStreamSynchronize(S.stream), "expert loop");
@@ -2369,7 +2383,7 @@ static int ep_agree_min(int v, int *out)
     int rc = 0;
     int *d = NULL;
     CK(cudaMalloc((void **)&d, sizeof(int)), "agreement word");
-    CK(cudaMemcpy(d, &v, sizeof(int), cudaMemcpyHostToDevice), "agreement H2D");
+    CK(h2d_now(d, &v, sizeof(int)), "agreement H2D");
     const ncclResult_t r = EP.all_reduce(d, d, 1, ncclInt32, ncclMin, EP.comm, S.stream);
     if (r != ncclSuccess) { rc = nccl_fail(r, "ncclAllReduce"); goto out; }
     CK(cudaStreamSynchronize(S.stream), "agreement");
@@ -2407,12 +2421,12 @@ static int ep_mail_setup(int T, int hidden)
     cudaIpcMemHandle_t hs[WC_EP_MAX];
     int ok = 1;
     CK(cudaMalloc((void **)&mine, bytes), "mailbox");
-    CK(cudaMemset(mine, 0, bytes), "mailbox clear");
+    CK(memset_now(mine, 0, bytes), "mailbox clear");
     CK(cudaDeviceSynchronize(), "mailbox clear");
     if (cudaIpcGetMemHandle(&hs[EP.rank], mine) != cudaSuccess) ok = 0;
     CK(cudaMalloc((void **)&dh, sizeof hs), "handle exchange");
-    CK(cudaMemcpy(dh + EP.rank * sizeof(cudaIpcMemHandle_t), &hs[EP.rank],
-                  sizeof(cudaIpcMemHandle_t), cudaMemcpyHostToDevice), "handle H2D");
+    CK(h2d_now(dh + EP.rank * sizeof(cudaIpcMemHandle_t), &hs[EP.rank],
+               sizeof(cudaIpcMemHandle_t)), "handle H2D");
     {
         const ncclResult_t r = EP.all_gather(dh + EP.rank * sizeof(cudaIpcMemHandle_t), dh,
                                              sizeof(cudaIpcMemHandle_t), ncclUint8, EP.comm,
@@ -2618,7 +2632,7 @@ static int ensure_res(int lat)
     S.res_lat = 0;
     if (cudaMalloc((void **)&S.d_res, res_floats(lat) * sizeof(float)) != cudaSuccess ||
         cudaMallocHost((void **)&S.h_res, res_floats(lat) * sizeof(float)) != cudaSuccess ||
-        cudaMemset(S.d_res, 0, res_floats(lat) * sizeof(float)) != cudaSuccess)
+        memset_now(S.d_res, 0, res_floats(lat) * sizeof(float)) != cudaSuccess)
         return fail(WASTE_CUDA_E_NOMEM, "layer result block");
     S.res_lat = lat;
     return 0;
@@ -2632,7 +2646,7 @@ static int layer_graph(cudaGraphExec_t *gx, unsigned *gx_epoch, const wc_moe_arg
     if (*gx) { cudaGraphExecDestroy(*gx); *gx = NULL; }
     cudaGraph_t g = NULL;
     CK(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
-    const wc_copy_args cin = { { S.d_x }, { S.h_x }, { xb }, 1 };
+    const wc_copy_args cin = { { S.d_x }, { S.h_x }, { xb }, 1, 0 };
     const wc_copy_args cout = { { S.h_res }, { S.d_res },
                                 { res_floats(S.res_lat) * sizeof(float) }, 1, 1 };
     cudaError_t e = small_copies(&cin, cudaMemcpyHostToDevice);
@@ -2685,8 +2699,8 @@ static int host_layer(int layer, const float *x, float *out, int *routed, float 
         CK(cudaStreamSynchronize(S.stream), "moe layer");
         const unsigned int err = *(const unsigned int *)(S.h_res + lat + 2 * WC_MAX_TOPK);
         if (err) {
-            cudaMemset(S.d_res + lat + 2 * WC_MAX_TOPK, 0, sizeof(unsigned int));
-            cudaMemset(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
+            memset_now(S.d_res + lat + 2 * WC_MAX_TOPK, 0, sizeof(unsigned int));
+            memset_now(S.d_ws, 0, WC_WS_CONTROL_WORDS * sizeof(unsigned int));
             rc = fail(WASTE_CUDA_E_DEVICE, "layer %d: a bounded device wait gave up", layer);
             goto out;
         }
