@@ -26,7 +26,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["vq3r_kernels.cu", "prefill_tc.cu", "trunk_mvq.cu", "matvec_sel.cu", "vq4p.cu", "kda.cu",
               "vq_encode.cu", "mla.cu"]
 C_SOURCES = ["waste_cuda.c"]
-HEADERS = ["vq3r_common.cuh", "wc_launch.h"]
+HEADERS = ["vq3r_common.cuh", "wc_launch.h", "pdl.cuh"]
 
 
 def _run(cmd, verbose):

@@ -28,6 +28,7 @@
  */
 #include "vq3r_common.cuh"
 #include "wc_launch.h"
+#include "pdl.cuh"
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -59,7 +60,9 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src)
 /* grid (H, ceil(V/32)), one warp: lane l owns column c = 32*blockIdx.y + l
  * of head blockIdx.x. The column is copied into shared memory first, all
  * K rows at once (one memory round trip instead of one per few rows), and
- * both passes work on it there. */
+ * both passes work on it there. The state is the previous token's, final
+ * before this layer began, so its copies are issued before the wait on the
+ * kernel that produced q, k, v, g and beta. */
 template <int K>
 __global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__restrict__ q,
                                                       const float *__restrict__ k,
@@ -79,6 +82,8 @@ __global__ void __launch_bounds__(32) kda_step_kernel(int V, const float *__rest
         for (int kk = 0; kk < K; kk++) cp_async4(&col[kk][lane], Sc + (size_t)kk * V);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    wc_pdl::trigger();
+    wc_pdl::wait();
     for (int i = lane; i < K; i += 32) {
         qs[i] = q[(size_t)h * K + i];
         ks[i] = k[(size_t)h * K + i];
@@ -139,6 +144,8 @@ __global__ void __launch_bounds__(128) rmsnorm_gated_kernel(int C, const float *
     extern __shared__ float xs[];
     __shared__ float rr;
     const size_t base = (size_t)blockIdx.x * C;
+    wc_pdl::trigger();          /* the projection behind may stage its weights */
+    wc_pdl::wait();             /* x: the step's output */
     for (int i = threadIdx.x; i < C; i += blockDim.x) xs[i] = x[base + i];
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -163,6 +170,7 @@ __global__ void __launch_bounds__(256) kda_gate_kernel(float *g, const float *A_
                                                        float lower_bound, float *beta)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    wc_pdl::trigger();          /* the step behind may fetch its state meanwhile */
     if (i < H) beta[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-beta[i])));
     if (i >= H * D) return;
     const float ea = expf_cr(A_log[i / D]);
@@ -194,20 +202,25 @@ int wc_kda_supported(int K, int V)
 }
 
 int wc_kda_step_launch(int H, int K, int V, const float *q, const float *k, const float *v,
-                       const float *g_log, const float *beta, float *S, float *o, void *stream)
+                       const float *g_log, const float *beta, float *S, float *o, void *stream,
+                       int pdl)
 {
     cudaStream_t st = (cudaStream_t)stream;
     const dim3 grid(H, (V + 31) / 32);
+    cudaError_t e;
     if (K == 128)
-        kda_step_kernel<128><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+        e = wc_pdl::launch(kda_step_kernel<128>, grid, dim3(32), 0, st, pdl != 0, V, q, k, v,
+                           g_log, beta, S, o);
     else if (K == 64)
-        kda_step_kernel<64><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+        e = wc_pdl::launch(kda_step_kernel<64>, grid, dim3(32), 0, st, pdl != 0, V, q, k, v,
+                           g_log, beta, S, o);
     else if (K == 32)
-        kda_step_kernel<32><<<grid, 32, 0, st>>>(V, q, k, v, g_log, beta, S, o);
+        e = wc_pdl::launch(kda_step_kernel<32>, grid, dim3(32), 0, st, pdl != 0, V, q, k, v,
+                           g_log, beta, S, o);
     else
         return (int)cudaErrorInvalidValue;
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float *ring,
@@ -220,12 +233,13 @@ int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float
 }
 
 int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
-                            float eps, float *y, void *stream)
+                            float eps, float *y, void *stream, int pdl)
 {
-    rmsnorm_gated_kernel<<<nh, 128, (size_t)C * sizeof(float), (cudaStream_t)stream>>>(
-        C, x, gate, weight, eps, y);
+    const cudaError_t e = wc_pdl::launch(rmsnorm_gated_kernel, dim3(nh), dim3(128),
+                                         (size_t)C * sizeof(float), (cudaStream_t)stream,
+                                         pdl != 0, C, x, gate, weight, eps, y);
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 } /* extern "C" */

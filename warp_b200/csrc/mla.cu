@@ -27,6 +27,7 @@
  */
 #include "vq3r_common.cuh"
 #include "wc_launch.h"
+#include "pdl.cuh"
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
     /* the cache row of this token's position (read from device memory, so
      * one launch serves every position) */
     float *lat_dst = lat && pos_p ? lat + (size_t)(*pos_p) * latd : nullptr;
+    wc_pdl::trigger();               /* the head kernel behind may stage its rows */
     __shared__ float red[32];
     float v[8];
     float s = 0.0f;
@@ -146,6 +148,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
         bulk_g2s(Ws, W + (size_t)h * wrows * rowbytes, wb, &bar);
         bulk_g2s(wss, ws + (size_t)h * wrows * ng, sb, &bar);
     }
+    wc_pdl::trigger();
+    wc_pdl::wait();                  /* q, the cache row and the position: the prep's */
     const int S = *pos_p + 1;
     for (int i = tid; i < qd; i += blockDim.x) qs[i] = q[(size_t)h * qd + i];
     if (tid == 0) okw = mbar_wait(&bar, 0);
@@ -225,6 +229,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
 __global__ void __launch_bounds__(256) mla_gate_kernel(float *o, const float *g, int n)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    wc_pdl::trigger();               /* the output projection may stage its weights */
+    wc_pdl::wait();                  /* o: the head kernel's */
     if (i < n) o[i] = __fmul_rn(o[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-g[i]))));
 }
 
@@ -252,7 +258,7 @@ int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, c
 int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S_max, int latd,
                        int kl, int qd, int nope, int rope, int vh, int nh, const uint8_t *W,
                        const uint16_t *ws, size_t rowbytes, int ng, int group, int bits,
-                       float scale, float *o, void *stream)
+                       float scale, float *o, void *stream, int pdl)
 {
     /* the bulk copies want 16-byte sizes and addresses */
     if ((((size_t)(nope + vh) * rowbytes) & 15) || (((size_t)(nope + vh) * ng * 2) & 15) ||
@@ -264,26 +270,29 @@ int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S
         e = cudaFuncSetAttribute(mla_head_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return (int)e;
-        mla_head_kernel<8><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
-            q, lat, pos_p, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+        e = wc_pdl::launch(mla_head_kernel<8>, dim3(nh), dim3(kMlaThreads), smem,
+                           (cudaStream_t)stream, pdl != 0, q, lat, pos_p, latd, kl, qd, nope,
+                           rope, vh, W, ws, rowbytes, ng, group, scale, o);
     } else if (bits == 4) {
         e = cudaFuncSetAttribute(mla_head_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return (int)e;
-        mla_head_kernel<4><<<nh, kMlaThreads, smem, (cudaStream_t)stream>>>(
-            q, lat, pos_p, latd, kl, qd, nope, rope, vh, W, ws, rowbytes, ng, group, scale, o);
+        e = wc_pdl::launch(mla_head_kernel<4>, dim3(nh), dim3(kMlaThreads), smem,
+                           (cudaStream_t)stream, pdl != 0, q, lat, pos_p, latd, kl, qd, nope,
+                           rope, vh, W, ws, rowbytes, ng, group, scale, o);
     } else {
         return (int)cudaErrorInvalidValue;
     }
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-int wc_mla_gate_launch(float *o, const float *g, int n, void *stream)
+int wc_mla_gate_launch(float *o, const float *g, int n, void *stream, int pdl)
 {
-    mla_gate_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(o, g, n);
+    const cudaError_t e = wc_pdl::launch(mla_gate_kernel, dim3((n + 255) / 256), dim3(256), 0,
+                                         (cudaStream_t)stream, pdl != 0, o, g, n);
     wc_count_launches(1);
-    return (int)cudaGetLastError();
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 } /* extern "C" */

@@ -837,7 +837,7 @@ int waste_cuda_kda_step(int H, int K, int V, const float *q, const float *k, con
     float *d = g_kda_dev;
     CK(cudaMemcpyAsync(d, p, n_in * 4, cudaMemcpyHostToDevice, S.stream), "KDA inputs H2D");
     CK((cudaError_t)wc_kda_step_launch(H, K, V, d, d + hk, d + 3 * hk, d + 2 * hk,
-                                       d + 3 * hk + hv, dS, d + n_in, S.stream), "KDA step");
+                                       d + 3 * hk + hv, dS, d + n_in, S.stream, 0), "KDA step");
     CK(cudaMemcpyAsync(p + n_in, d + n_in, hv * 4, cudaMemcpyDeviceToHost, S.stream), "o D2H");
     CK(cudaStreamSynchronize(S.stream), "KDA step");
     memcpy(o, p + n_in, hv * 4);
@@ -893,7 +893,7 @@ int waste_cuda_rmsnorm_gated_heads(int nh, int C, const float *x, const float *g
     CK(cudaMemcpyAsync(g_kda_dev, g_kda_pin, 2 * n * 4, cudaMemcpyHostToDevice, S.stream),
        "norm inputs H2D");
     CK((cudaError_t)wc_rmsnorm_gated_launch(nh, C, g_kda_dev, g_kda_dev + n, dw, eps,
-                                            g_kda_dev + 2 * n, S.stream), "gated norm");
+                                            g_kda_dev + 2 * n, S.stream, 0), "gated norm");
     CK(cudaMemcpyAsync(g_kda_pin + 2 * n, g_kda_dev + 2 * n, n * 4, cudaMemcpyDeviceToHost,
                        S.stream), "norm y D2H");
     CK(cudaStreamSynchronize(S.stream), "gated norm");
@@ -913,7 +913,7 @@ int waste_cuda_kda_step_dev(int H, int K, int V, const float *q, const float *k,
     pthread_mutex_lock(&g_mu);
     if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "kda_step_dev before waste_cuda_init"); goto out; }
     CK((cudaError_t)wc_kda_step_launch(H, K, V, q, k, v, g_log, beta, S_, o,
-                                       stream ? stream : (void *)S.stream), "KDA step");
+                                       stream ? stream : (void *)S.stream, 0), "KDA step");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -943,7 +943,7 @@ int waste_cuda_rmsnorm_gated_dev(int nh, int C, const float *x, const float *gat
     pthread_mutex_lock(&g_mu);
     if (!S.inited) { rc = fail(WASTE_CUDA_E_NODEV, "rmsnorm_gated_dev before waste_cuda_init"); goto out; }
     CK((cudaError_t)wc_rmsnorm_gated_launch(nh, C, x, gate, weight, eps, y,
-                                            stream ? stream : (void *)S.stream), "gated norm");
+                                            stream ? stream : (void *)S.stream, 0), "gated norm");
 out:
     pthread_mutex_unlock(&g_mu);
     return rc;
@@ -1128,8 +1128,12 @@ static int kda_enqueue(void *p)
     if (!lrc && !full_gate) lrc = qt_launch_on(&d->g_b, lg, gate, g_side[5], 0);
     if (!lrc) lrc = join_branches(WC_BRANCHES);
     if (!lrc) lrc = wc_kda_gate_launch(g, k->dA, k->dB, H, D, d->lower_bound, beta, S.stream);
-    if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, kk, v, g, beta, k->dS, o, S.stream);
-    if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, k->dN, d->eps, o, S.stream);
+    /* gate → step → norm → o_proj programmatically (not while the phase
+     * timers put events between kernels): the step's state fetch and the
+     * projection's weight copies overlap the kernel before each */
+    const int pdl = !wc_profiling();
+    if (!lrc) lrc = wc_kda_step_launch(H, D, D, q, kk, v, g, beta, k->dS, o, S.stream, pdl);
+    if (!lrc) lrc = wc_rmsnorm_gated_launch(H, D, o, gate, k->dN, d->eps, o, S.stream, pdl);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
     const wc_copy_args cout = { { g_kda_pin }, { y }, { (size_t)hid * 4 }, 1, 1 };
@@ -1239,10 +1243,14 @@ static int mla_enqueue(void *p)
     if (!lrc) lrc = join_branches(3);
     if (!lrc) lrc = wc_mla_prep_launch(ckv, kl, k->dkvn, d->eps, ckv + kl, cs, sn, half, q, nh, qd,
                                        d->qk_nope, k->dlat, pos_d, lrow, latd, S.stream);
+    /* prep → head → gate → o_proj programmatically (not under the phase
+     * timers): the head's row staging and the projection's weight copies
+     * overlap the kernel before each */
+    const int pdl = !wc_profiling();
     if (!lrc) lrc = wc_mla_head_launch(q, k->dlat, pos_d, k->S_max, latd, kl, qd, d->qk_nope,
                                        d->qk_rope, vh, nh, k->kW, k->kws, d->kv_b.rowbytes, k->kng,
-                                       d->kv_b.group, d->kv_b.bits, d->scale, o, S.stream);
-    if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream);
+                                       d->kv_b.group, d->kv_b.bits, d->scale, o, S.stream, pdl);
+    if (!lrc && d->g.W) lrc = wc_mla_gate_launch(o, g, nh * vh, S.stream, pdl);
     if (!lrc) lrc = qt_launch(&d->o, o, y);
     if (lrc) return -1;
     const wc_copy_args cout = { { g_mla_pin + k->n_in }, { y }, { k->n_out * 4 }, 1, 1 };

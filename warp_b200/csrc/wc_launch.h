@@ -252,14 +252,18 @@ int    wc_p6_moe_launch(const wc_p6_args *a, void *stream);
 int    wc_p6_table_launch(int8_t *q, float *qs, const float *x, const float *books, int cb,
                           int nv, void *stream);
 
-/* KDA (kda.cu): decode step, causal conv, gated rmsnorm (src/kda.c). */
+/* KDA (kda.cu): decode step, causal conv, gated rmsnorm (src/kda.c). With
+ * pdl set, the step and the norm launch programmatically behind the kernel
+ * before them on the stream: the step fetches its state before waiting on
+ * that kernel; the norm lets the kernel behind it start at once. */
 int wc_kda_supported(int K, int V);
 int wc_kda_step_launch(int H, int K, int V, const float *q, const float *k, const float *v,
-                       const float *g_log, const float *beta, float *S, float *o, void *stream);
+                       const float *g_log, const float *beta, float *S, float *o, void *stream,
+                       int pdl);
 int wc_short_conv_launch(int C, int KS, const float *w, const float *bias, float *ring,
                          const float *x, float *y, void *stream);
 int wc_rmsnorm_gated_launch(int nh, int C, const float *x, const float *gate, const float *weight,
-                            float eps, float *y, void *stream);
+                            float eps, float *y, void *stream, int pdl);
 /* The decay gate of H*D channels in place and beta = sigmoid(beta) [H]. */
 int wc_kda_gate_launch(float *g, const float *A_log, const float *dt_bias, int H, int D,
                        float lower_bound, float *beta, void *stream);
@@ -345,8 +349,11 @@ int wc_mla_prep_launch(float *x, int n, const float *w, float eps, float *rot, c
 int wc_mla_head_launch(const float *q, const float *lat, const int *pos_p, int S_max, int latd,
                        int kl, int qd, int nope, int rope, int vh, int nh, const uint8_t *W,
                        const uint16_t *ws, size_t rowbytes, int ng, int group, int bits,
-                       float scale, float *o, void *stream);
-int wc_mla_gate_launch(float *o, const float *g, int n, void *stream);
+                       float scale, float *o, void *stream, int pdl);
+int wc_mla_gate_launch(float *o, const float *g, int n, void *stream, int pdl);
+/* With pdl set, the head and the gate launch programmatically behind the
+ * kernel before them: the head stages its kv_b_proj rows (constants) while
+ * the prep runs. */
 
 /* Phase timers (see waste_cuda_profile in include/waste_cuda.h). */
 enum { WC_PH_ROUTER, WC_PH_ACT, WC_PH_GATEUP, WC_PH_DOWN, WC_PH_COMBINE,
