@@ -58,6 +58,28 @@ __device__ __forceinline__ float warp_sum_f(float v)
     return v;
 }
 
+/* xs[0..n) = x[0..in), zero past in. Each thread issues up to kXBatch of
+ * its loads before storing any, so the copy costs one memory round trip per
+ * kXBatch * blockDim values instead of one per blockDim. */
+constexpr int kXBatch = 16;
+
+__device__ __forceinline__ void stage_x(float *xs, const float *__restrict__ x, int in, int n)
+{
+    for (int base = threadIdx.x; base < n; base += kXBatch * blockDim.x) {
+        float v[kXBatch];
+#pragma unroll
+        for (int j = 0; j < kXBatch; j++) {
+            const int i = base + j * blockDim.x;
+            v[j] = i < in ? x[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kXBatch; j++) {
+            const int i = base + j * blockDim.x;
+            if (i < n) xs[i] = v[j];
+        }
+    }
+}
+
 /* src/simd.h:69-74 waste_q3_at: signed 3-bit code i of a packed row. */
 __device__ __forceinline__ int q3_at(const uint8_t *p, long i)
 {
@@ -76,7 +98,7 @@ mvq_kernel(float *__restrict__ y, const uint8_t *__restrict__ W, const uint16_t 
     const int n = ng * g;
     pdl_trigger_m();
     pdl_wait_m();                            /* x: the previous kernel's output */
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = i < in ? x[i] : 0.0f;
+    stage_x(xs, x, in, n);
     __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int wpb = blockDim.x / 32;
@@ -154,7 +176,7 @@ mvq_tma_kernel(float *__restrict__ y, const uint8_t *__restrict__ W,
     }
     pdl_trigger_m();
     pdl_wait_m();                            /* the weights are constants: only x waits */
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = i < in ? x[i] : 0.0f;
+    stage_x(xs, x, in, n);
     __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     int it = 0;
