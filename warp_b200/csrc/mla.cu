@@ -37,6 +37,7 @@ using namespace wc;
 namespace {
 
 constexpr int kMlaThreads = 512;
+constexpr int kLatBatch = 16;        /* cached-latent loads a thread has in flight */
 
 /* Value j of row r of a quantised trunk tensor (groups of `group`, one f16
  * scale per group): 8-bit signed bytes, or 4-bit codes minus 8 (low nibble
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_prep_kernel(
  * their scales | q (qd) | q~ (kl) | c~ (kl) | scores (up to the cache's
  * rows). */
 template <int BITS>
-__global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
+__global__ void __launch_bounds__(kMlaThreads, 1) mla_head_kernel(
     const float *__restrict__ q, const float *__restrict__ lat, const int *pos_p, int latd, int kl,
     int qd, int nope, int rope, int vh, const uint8_t *__restrict__ W,
     const uint16_t *__restrict__ ws, size_t rowbytes, int ng, int group, float scale,
@@ -171,12 +172,29 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
         qa[j] = acc;
     }
     __syncthreads();
-    /* scores: one warp per position */
+    /* scores: one warp per position. The cached latents are read through L2
+     * (the prep kernel ahead wrote this token's row), each lane's loads
+     * batched ahead of its sums, which keep their order. */
     for (int s = warp; s < S; s += nw) {
         const float *cs = lat + (size_t)s * latd;
         float a = 0.0f, b = 0.0f;
-        for (int j = lane; j < kl; j += 32) a = fmaf(qa[j], __ldg(cs + j), a);
-        for (int j = lane; j < rope; j += 32) b = fmaf(qs[nope + j], __ldg(cs + kl + j), b);
+        float rv[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+            rv[u] = lane + 32 * u < rope ? __ldcg(cs + kl + lane + 32 * u) : 0.0f;
+        for (int j0 = lane; j0 < kl; j0 += 32 * kLatBatch) {
+            float v[kLatBatch];
+#pragma unroll
+            for (int u = 0; u < kLatBatch; u++)
+                v[u] = j0 + 32 * u < kl ? __ldcg(cs + j0 + 32 * u) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kLatBatch; u++)
+                if (j0 + 32 * u < kl) a = fmaf(qa[j0 + 32 * u], v[u], a);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+            if (lane + 32 * u < rope) b = fmaf(qs[nope + lane + 32 * u], rv[u], b);
+        for (int j = lane + 64; j < rope; j += 32) b = fmaf(qs[nope + j], __ldcg(cs + kl + j), b);
 #pragma unroll
         for (int k = 16; k > 0; k >>= 1) {
             a += __shfl_xor_sync(0xffffffffu, a, k);
@@ -210,7 +228,15 @@ __global__ void __launch_bounds__(kMlaThreads) mla_head_kernel(
     /* c~[j] = sum over positions ascending of p_s * c_s[j] */
     for (int j = tid; j < kl; j += blockDim.x) {
         float acc = 0.0f;
-        for (int s = 0; s < S; s++) acc = __fadd_rn(acc, __fmul_rn(sc[s], __ldg(lat + (size_t)s * latd + j)));
+        for (int s0 = 0; s0 < S; s0 += kLatBatch) {
+            float v[kLatBatch];
+#pragma unroll
+            for (int u = 0; u < kLatBatch; u++)
+                v[u] = s0 + u < S ? __ldcg(lat + (size_t)(s0 + u) * latd + j) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kLatBatch; u++)
+                if (s0 + u < S) acc = __fadd_rn(acc, __fmul_rn(sc[s0 + u], v[u]));
+        }
         ca[j] = acc;
     }
     __syncthreads();
