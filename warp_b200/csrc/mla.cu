@@ -42,17 +42,29 @@ constexpr int kLatBatch = 16;        /* cached-latent loads a thread has in flig
 /* Value j of row r of a quantised trunk tensor (groups of `group`, one f16
  * scale per group): 8-bit signed bytes, or 4-bit codes minus 8 (low nibble
  * first), times the group's scale — src/model.c:407-440. W and ws are the
- * head's rows staged in shared memory (r counted from the head's first). */
+ * head's rows staged in shared memory (r counted from the head's first).
+ * Column j's place in a row is the same for every row (its group gj, the
+ * byte holding it and, at 4 bits, which nibble), so DeqCol computes it once
+ * and steps it along a lane's columns without a division. */
+struct DeqCol {
+    int gj, jin;                     /* group, index inside it */
+    __device__ __forceinline__ DeqCol(int j, int group) : gj(j / group), jin(j - gj * group) {}
+    __device__ __forceinline__ void advance(int step, int group)
+    {
+        jin += step;
+        while (jin >= group) { jin -= group; gj++; }
+    }
+};
+
 template <int BITS>
-__device__ __forceinline__ float deq_at(const uint8_t *W, const uint16_t *ws, size_t rowbytes,
-                                        int ng, int group, int r, int j)
+__device__ __forceinline__ float deq_col(const uint8_t *W, const uint16_t *ws, size_t rowbytes,
+                                         int ng, int group, int r, const DeqCol &c)
 {
-    const float s = f16_keep(ws[(size_t)r * ng + j / group]);
+    const float s = f16_keep(ws[(size_t)r * ng + c.gj]);
     const uint8_t *row = W + (size_t)r * rowbytes;
-    if (BITS == 8) return s * (float)(int8_t)row[j];
-    const int base = (j / group) * group, i = j - base;
-    const uint8_t byte = row[base / 2 + (i >> 1)];
-    const int v = (i & 1) ? (byte >> 4) - 8 : (byte & 0x0F) - 8;
+    if (BITS == 8) return s * (float)(int8_t)row[c.gj * group + c.jin];
+    const uint8_t byte = row[(c.gj * group) / 2 + (c.jin >> 1)];
+    const int v = (c.jin & 1) ? (byte >> 4) - 8 : (byte & 0x0F) - 8;
     return s * (float)v;
 }
 
@@ -162,12 +174,13 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_head_kernel(
     /* q~[j] = sum over i ascending of q_i * W_kb[h*wrows + i][j] (exact
      * zeros skipped, as the reference does) */
     for (int j = tid; j < kl; j += blockDim.x) {
+        const DeqCol col(j, group);
         float acc = 0.0f;
 #pragma unroll 8
         for (int i = 0; i < nope; i++) {
             const float qi = qs[i];
             if (qi == 0.0f) continue;
-            acc = __fadd_rn(acc, __fmul_rn(qi, deq_at<BITS>(Ws, wss, rowbytes, ng, group, i, j)));
+            acc = __fadd_rn(acc, __fmul_rn(qi, deq_col<BITS>(Ws, wss, rowbytes, ng, group, i, col)));
         }
         qa[j] = acc;
     }
@@ -244,8 +257,9 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_head_kernel(
     for (int i = warp; i < vh; i += nw) {
         const int r = nope + i;
         float a = 0.0f;
-        for (int j = lane; j < kl; j += 32)
-            a = fmaf(deq_at<BITS>(Ws, wss, rowbytes, ng, group, r, j), ca[j], a);
+        DeqCol col(lane, group);
+        for (int j = lane; j < kl; j += 32, col.advance(32, group))
+            a = fmaf(deq_col<BITS>(Ws, wss, rowbytes, ng, group, r, col), ca[j], a);
 #pragma unroll
         for (int k = 16; k > 0; k >>= 1) a += __shfl_xor_sync(0xffffffffu, a, k);
         if (lane == 0) o[(size_t)h * vh + i] = a;
